@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fisheye tracer: fisheye Mpix/s forward + backward.
+
+Workload (default ``single_view``): 1,000,000 Gaussians with SH degree 3, a
+Kannala-Brandt 200 deg fisheye at 1600x1600, k-buffer 16, L1 loss against a
+U[0,1] target.  One step = trace forward, L1 loss gradient, trace backward
+(and, with N > 1 ranks, the NCCL all-reduce of the per-Gaussian gradients);
+every rank renders its own view of the same scene (weak scaling).
+
+``--impl reference`` times the CPU restatement of the reference's equations
+(oracle/) on the host cores: the reference renders only on the GPU and its
+extension cannot be built here, so the scalar C++ port is the reference arm.
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fisheye Mpix/s fwd+bwd"
+UNIT = "Mpix/s"
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
+    p.add_argument("--workload", choices=["single_view", "cpu_scale"], default="single_view")
+    p.add_argument("--num-gaussians", type=int, default=None, help="override the workload's Gaussian count")
+    p.add_argument("--size", type=int, default=None, help="override the raster size")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- workload
+def build_workload(args, rank: int):
+    from gofish_b200 import scene as sc
+    from gofish_b200.camera import random_kb_coefficients  # noqa: F401
+
+    if args.workload == "cpu_scale":
+        w = sc.workload_cpu_scale()
+    else:
+        kw = {}
+        if args.num_gaussians:
+            kw["n"] = args.num_gaussians
+        if args.size:
+            kw["size"] = args.size
+        w = sc.workload_single_view(**kw)
+    pose = w.poses[0]
+    if rank > 0:
+        # weak scaling: every further rank renders its own random view of the same scene
+        rng = np.random.default_rng(5000 + rank)
+        c = rng.standard_normal(3)
+        c = c / np.linalg.norm(c) * 0.5 * np.cbrt(rng.random())
+        pose = sc.pose_world_to_sensor(c, sc.random_rotation_quaternion_xyzw(rng))
+    return w, pose
+
+
+def workload_config(w, args, world: int) -> dict:
+    cam = w.camera
+    return {
+        "workload": w.name,
+        "gaussians": w.scene.num,
+        "sh_degree": w.scene.sh_degree,
+        "camera": f"OPENCV_FISHEYE (Kannala-Brandt) 200deg {cam.width}x{cam.height}",
+        "k_buffer": w.k_buffer,
+        "sort_key": "per-tile max-response depth",
+        "views_per_step": world,
+        "loss": "L1 vs U[0,1] target",
+        "l2_policy": "inputs larger than L2 (packed particles + SH + rays > 126 MB)",
+        "parallelism": f"dp{world} (views sharded, NCCL all-reduce of particle gradients)" if world > 1 else "single GPU",
+    }
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(smax)), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- peaks
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# Algorithmic bytes (fixed byte model): per intersection and per pixel.
+FWD_RENDER_BYTES_PER_INTERSECTION = 4 + 88 + 12     # id, particle fetch (pos, B^-1, density), rgb
+FWD_RENDER_BYTES_PER_PIXEL = 48                     # rays 24, rgba 16, hit distance 4, hit count 4
+BWD_RENDER_BYTES_PER_INTERSECTION = 144             # id 4 + particle record 128 + rgb 12
+BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output gradients
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from gofish_b200.splat_raster import SplatRaster
+    from gofish_b200.scene import pack_particles
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    w, pose = build_workload(args, rank)
+    cam = w.camera
+    ray_o_np, ray_d_np, valid_np = cam.rays()
+    particles_host = torch.from_numpy(pack_particles(w.scene)).pin_memory()
+    features_host = torch.from_numpy(np.ascontiguousarray(w.scene.features)).pin_memory()
+    rng = np.random.default_rng(777 + rank)
+    target_host = torch.from_numpy(rng.random((cam.height, cam.width, 3), dtype=np.float32)).pin_memory()
+
+    particles = particles_host.to(device)
+    features = features_host.to(device)
+    target = target_host.to(device)
+    ray_o = torch.from_numpy(ray_o_np).to(device)
+    ray_d = torch.from_numpy(ray_d_np).to(device)
+    valid = torch.from_numpy(valid_np[0]).to(device)  # [H,W,1] bool
+    valid_f = valid.float()
+    n_valid = max(1.0, float(valid_np.sum()))
+    from gofish_b200.physical_tile_mask import build_physical_tile_binding
+
+    class _Batch:
+        physical_fov_mask = valid[None]
+
+    binding = build_physical_tile_binding(_Batch, ray_d, "bench")
+    conf = {"render": {"splat": {"k_buffer_size": w.k_buffer}, "enable_hitcounts": True}}
+    raster = SplatRaster(conf)
+    raster.register_physical_tile_mask(binding.mask, binding.token)
+    sensor = cam.model()
+    pose_t = torch.from_numpy(np.asarray(pose, dtype=np.float32))
+    zeros14 = [torch.zeros(1, device=device)] * 14
+    scale = 1.0 / (3.0 * n_valid)
+    zero_hit = torch.zeros((cam.height, cam.width, 1), device=device)
+
+    def step(p, f, tgt, want_loss=False):
+        out = raster.trace(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
+                           binding.token)
+        rgba = out[0]
+        diff = rgba[..., :3] - tgt
+        grad = torch.zeros_like(rgba)
+        grad[..., :3] = torch.sign(diff) * (valid_f * scale)
+        gp, gs = raster.trace_bwd(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
+                                  rgba, grad, out[1], zero_hit, *zeros14, binding.token)
+        if world > 1:
+            dist.all_reduce(gp)
+            dist.all_reduce(gs)
+        if want_loss:
+            return (diff.abs() * valid_f).sum() * scale
+        return None
+
+    for _ in range(args.warmup):
+        step(particles, features, target)
+    torch.cuda.synchronize(device)
+    intersections = int(raster.stats().num_intersections)
+
+    # --- device-timed region: inputs resident in HBM
+    raster.collect_stage_times()
+    raster.enable_stage_timing(True)
+    launches_before = int(raster.stats().total_kernel_launches)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(particles, features, target)
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    clock_info = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    raster.enable_stage_timing(False)
+    stages = raster.collect_stage_times()
+    launches = int(raster.stats().total_kernel_launches) - launches_before
+    ms_max = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(ms_max.item())
+    pixels = cam.width * cam.height
+    value = world * pixels * args.steps / (elapsed_ms / 1000.0) / 1e6
+
+    # --- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        h2d = particles_host.numel() * 4 + features_host.numel() * 4 + target_host.numel() * 4
+        p_dev = torch.empty_like(particles)
+        f_dev = torch.empty_like(features)
+        t_dev = torch.empty_like(target)
+        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            p_dev.copy_(particles_host, non_blocking=True)
+            f_dev.copy_(features_host, non_blocking=True)
+            t_dev.copy_(target_host, non_blocking=True)
+            loss = step(p_dev, f_dev, t_dev, want_loss=True)
+            loss_host.copy_(loss, non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * pixels * args.steps / (float(ems.item()) / 1000.0) / 1e6, "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4}
+
+    # --- roofline of the dominant kernel (average launch duration from stage events)
+    peak, peak_kind = measured_peaks()
+    dominant = max(("render_fwd", "render_bwd"), key=lambda s: stages[s][0])
+    dom_ms, dom_launches = stages[dominant]
+    avg_s = dom_ms / max(1, dom_launches) / 1000.0
+    if dominant == "render_bwd":
+        alg = intersections * BWD_RENDER_BYTES_PER_INTERSECTION + pixels * BWD_RENDER_BYTES_PER_PIXEL
+    else:
+        alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
+    achieved = alg / avg_s / 1e9
+    roofline = {"kernel": f"k_render_{dominant.split('_')[1]}<{w.k_buffer}>", "bound": "hbm",
+                "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5),
+                "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "alg_bytes_per_launch": int(alg), "avg_launch_ms": round(avg_s * 1000.0, 4)}
+
+    result = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
+        "config": workload_config(w, args, world), "e2e": e2e, "roofline": roofline,
+        "gpu_launches": int(launches),
+        "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
+        "intersections_per_view": intersections,
+    }
+    if clock_info is not None:
+        result["clocks"] = clock_info
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(w, pose, ray_o_np, ray_d_np, valid_np, budget_s=20.0)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ----------------------------------------------------------------------------- CPU (oracle) arm
+def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
+    """Times the oracle (scalar C++ restatement of the reference equations) on
+    a bounded sample: projection, binning and sort of every Gaussian, then
+    forward + backward compositing of a band of tile rows through the image
+    centre; the full-frame time is the projection/sort time plus the band time
+    scaled by the retained-tile ratio."""
+    import oracle
+    from gofish_b200.scene import pack_particles
+
+    cam = w.camera
+    ocam = oracle.camera(1, cam.width, cam.height, cam.principal, cam.focal, cam.coefficients, cam.max_angle)
+    parts = pack_particles(w.scene)
+    valid2 = valid[0, :, :, 0]
+    h, wd = valid2.shape
+    ty, tx = (h + 15) // 16, (wd + 15) // 16
+    pad = np.zeros((ty * 16, tx * 16), dtype=bool)
+    pad[:h, :wd] = valid2
+    tmask = pad.reshape(ty, 16, tx, 16).any(axis=(1, 3)).astype(np.uint8)
+    o, d = ray_o[0], ray_d[0]
+    t0 = time.perf_counter()
+    pose_o = oracle.prepare_pose(pose)
+    proj, rgb, counts = oracle.project(ocam, pose_o, parts, w.scene.features, w.scene.sh_degree, tmask)
+    tr = oracle.tile_rays(ocam, pose_o, o, d)
+    keys, ids, ranges = oracle.bin(ocam, pose_o, parts, proj, counts, tmask, tr, 0)
+    t_pb = time.perf_counter() - t0
+    # band of tile rows around the centre, grown until the budget is used
+    rows = 1
+    centre = ty // 2
+    spent = 0.0
+    rendered_tiles = 0
+    t_render = 0.0
+    while True:
+        r0 = max(0, centre - rows // 2)
+        r1 = min(ty, r0 + rows)
+        tiles = (r0 * tx, r1 * tx)
+        t1 = time.perf_counter()
+        rgba, hit_t, _ = oracle.render_forward(ocam, pose_o, parts, rgb, o, d, tmask, ranges, ids, w.k_buffer, tiles)
+        grad = np.sign(rgba)
+        grad[..., 3] = 0.0
+        oracle.render_backward(ocam, pose_o, parts, rgb, o, d, tmask, ranges, ids, w.k_buffer, rgba, hit_t,
+                               grad.astype(np.float32), np.zeros_like(hit_t), tiles)
+        t_render = time.perf_counter() - t1
+        rendered_tiles = int(tmask.reshape(-1)[tiles[0]:tiles[1]].sum())
+        spent = t_pb + t_render
+        if spent > budget_s / 2 or r1 - r0 >= ty:
+            break
+        rows *= 2
+    retained = int(tmask.sum())
+    full = t_pb + t_render * retained / max(1, rendered_tiles)
+    pixels = cam.width * cam.height
+    return {"value": round(pixels / full / 1e6, 5), "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": (f"projection+sort of all {w.scene.num} Gaussians ({t_pb:.2f} s), fwd+bwd of {rendered_tiles} "
+                       f"of {retained} retained tiles ({t_render:.2f} s), scaled to the full {cam.width}x{cam.height} "
+                       "frame")}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w, pose = build_workload(args, 0)
+    cam = w.camera
+    ray_o, ray_d, valid = cam.rays()
+    values = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        base = cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s=6.0)
+        if i >= args.warmup:
+            values.append(base["value"])
+    value = float(np.median(values))
+    result = {
+        "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)", "impl": "reference",
+        "config": workload_config(w, args, 1),
+        "cpu_baseline": {**base, "value": round(value, 5)},
+        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,152 @@
+"""ctypes binding of the C ABI declared in include/gofish_b200.h.
+
+Loading fails loudly: there is no CPU fallback for any entry point.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+from .build import LIBRARY
+
+GF_OK = 0
+GF_CAMERA_OPENCV_PINHOLE = 0
+GF_CAMERA_OPENCV_FISHEYE = 1
+GF_KEY_PER_TILE_DEPTH = 0
+GF_KEY_GLOBAL_DEPTH = 1
+STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
+
+
+class GfCamera(ctypes.Structure):
+    _fields_ = [
+        ("model", ctypes.c_int32),
+        ("width", ctypes.c_int32),
+        ("height", ctypes.c_int32),
+        ("shutter", ctypes.c_int32),
+        ("principal_point", ctypes.c_float * 2),
+        ("focal_length", ctypes.c_float * 2),
+        ("radial", ctypes.c_float * 6),
+        ("tangential", ctypes.c_float * 2),
+        ("thin_prism", ctypes.c_float * 4),
+        ("max_angle", ctypes.c_float),
+        ("reserved", ctypes.c_float),
+    ]
+
+
+class GfTracerConfig(ctypes.Structure):
+    _fields_ = [
+        ("k_buffer_size", ctypes.c_int32),
+        ("sort_key", ctypes.c_int32),
+        ("enable_hit_counts", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class GfTraceInputs(ctypes.Structure):
+    _fields_ = [
+        ("frame", ctypes.c_uint32),
+        ("sh_degree", ctypes.c_int32),
+        ("num_particles", ctypes.c_uint32),
+        ("sh_coeffs", ctypes.c_uint32),
+        ("particles", ctypes.c_void_p),
+        ("features", ctypes.c_void_p),
+        ("ray_origin", ctypes.c_void_p),
+        ("ray_direction", ctypes.c_void_p),
+        ("camera", GfCamera),
+        ("pose_start", ctypes.c_float * 7),
+        ("pose_end", ctypes.c_float * 7),
+        ("timestamp_start", ctypes.c_int64),
+        ("timestamp_end", ctypes.c_int64),
+        ("tile_token", ctypes.c_char_p),
+    ]
+
+
+class GfTraceOutputs(ctypes.Structure):
+    _fields_ = [
+        ("rgba", ctypes.c_void_p),
+        ("hit_distance", ctypes.c_void_p),
+        ("hit_count", ctypes.c_void_p),
+        ("visibility", ctypes.c_void_p),
+    ]
+
+
+class GfTraceGrads(ctypes.Structure):
+    _fields_ = [
+        ("rgba", ctypes.c_void_p),
+        ("hit_distance", ctypes.c_void_p),
+        ("grad_rgba", ctypes.c_void_p),
+        ("grad_hit_distance", ctypes.c_void_p),
+        ("grad_particles", ctypes.c_void_p),
+        ("grad_features", ctypes.c_void_p),
+    ]
+
+
+class GfTraceStats(ctypes.Structure):
+    _fields_ = [
+        ("num_intersections", ctypes.c_uint64),
+        ("num_tiles", ctypes.c_uint32),
+        ("num_particles", ctypes.c_uint32),
+        ("kernel_launches", ctypes.c_uint32),
+        ("reserved", ctypes.c_uint32),
+        ("total_kernel_launches", ctypes.c_uint64),
+    ]
+
+
+# (name, restype, argtypes) of every exported symbol of include/gofish_b200.h.
+_SIGNATURES = [
+    ("gf_abi_version", ctypes.c_int, []),
+    ("gf_last_error", ctypes.c_char_p, []),
+    ("gf_tracer_create", ctypes.c_void_p, [ctypes.POINTER(GfTracerConfig)]),
+    ("gf_tracer_destroy", None, [ctypes.c_void_p]),
+    ("gf_tracer_register_tile_mask", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_char_p, ctypes.c_void_p]),
+    ("gf_tracer_trace", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(GfTraceInputs), ctypes.POINTER(GfTraceOutputs), ctypes.c_void_p]),
+    ("gf_tracer_trace_bwd", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(GfTraceInputs), ctypes.POINTER(GfTraceGrads), ctypes.c_void_p]),
+    ("gf_tracer_trace_inference", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(GfTraceInputs), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    ("gf_tracer_enable_timing", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    ("gf_tracer_collect_times", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    ("gf_tracer_stats", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(GfTraceStats)]),
+    ("gf_tracer_copy_intermediates", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),
+]
+
+EXPORTED_SYMBOLS = [name for name, _, _ in _SIGNATURES]
+
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A gofish_b200 entry point returned an error code."""
+
+
+def load(path: Path | None = None):
+    """Load libgofish_b200.so (raises if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    target = Path(path) if path is not None else LIBRARY
+    if not target.exists():
+        raise RuntimeError(
+            f"gofish_b200 native library not found at {target}; build it with `python -m gofish_b200.build` "
+            "(the tracer has no CPU fallback)")
+    lib = ctypes.CDLL(str(target))
+    for name, restype, argtypes in _SIGNATURES:
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.gf_abi_version() != 1:
+        raise RuntimeError("gofish_b200 native library ABI version mismatch")
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(code: int, what: str) -> None:
+    if code != GF_OK:
+        message = load().gf_last_error().decode(errors="replace")
+        raise NativeError(f"{what} failed ({code}): {message}")

@@ -1,0 +1,615 @@
+// Host orchestration and C ABI of the B200 fisheye tracer.
+//
+// One gf_tracer owns the device buffers of one renderer instance (the
+// reference's GutRenderForwardContext, gutRenderer.cu:229-671): projected
+// particle state, render records, tile counts and offsets, the (tile|depth)
+// keys and particle ids with their sort ping-pong buffers, per-tile ranges
+// and the backward gradient records.  Buffers grow geometrically and are
+// stream-ordered (cudaMallocAsync), so steady-state frames allocate nothing.
+//
+// Host synchronization: exactly one per forward pass, to read the number of
+// tile intersections after the count scan (the reference synchronizes about
+// eight times, gutRenderer.cu:843-1599).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/gofish_b200.h"
+#include "gf_sort.cuh"
+#include "gf_tracer_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_lastError;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_lastError = buf;
+    return code;
+}
+
+#define GF_CUDA(call)                                                                                     \
+    do {                                                                                                  \
+        const cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+#define GF_LAUNCH_CHECK()                                                                                  \
+    do {                                                                                                   \
+        const cudaError_t e_ = cudaGetLastError();                                                         \
+        if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
+    } while (0)
+
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t need, cudaStream_t stream) {
+        if (need <= bytes) return GF_OK;
+        if (ptr != nullptr) {
+            GF_CUDA(cudaFreeAsync(ptr, stream));
+            ptr = nullptr;
+            bytes = 0;
+        }
+        const size_t grown = need + need / 4 + 256;
+        GF_CUDA(cudaMallocAsync(&ptr, grown, stream));
+        bytes = grown;
+        return GF_OK;
+    }
+    void release() {
+        if (ptr != nullptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    template <typename T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+struct TileMask {
+    DeviceBuffer buf;
+    uint32_t ty = 0, tx = 0;
+};
+
+uint32_t bit_length(uint32_t n) {
+    uint32_t b = 0;
+    while (n != 0u) {
+        ++b;
+        n >>= 1;
+    }
+    return b;
+}
+
+bool valid_k(int k) { return k == 0 || k == 4 || k == 8 || k == 12 || k == 16 || k == 24 || k == 32; }
+
+}  // namespace
+
+struct gf_tracer {
+    gf_tracer_config cfg{};
+    int device = -1;
+    std::map<std::string, TileMask> masks;
+
+    // Forward context.
+    DeviceBuffer proj, records, counts, offsets, scanTiles, total, tileRays, ranges;
+    DeviceBuffer keys[2], ids[2], hist;
+    DeviceBuffer gradRecords;
+    uint64_t* hostTotal = nullptr;
+    int finalBuf = 0;
+    bool haveForward = false;
+    gf::FrameArgs frame{};
+    const uint8_t* frameMask = nullptr;
+    const float* frameRayO = nullptr;
+    const float* frameRayD = nullptr;
+    uint64_t numIntersections = 0;
+    uint32_t launches = 0;
+    uint64_t totalLaunches = 0;
+
+    // Per-stage event timing (enabled by gf_tracer_enable_timing).
+    bool timing = false;
+    struct StageEvent {
+        int stage;
+        cudaEvent_t start, end;
+    };
+    std::vector<StageEvent> pending;
+    std::vector<cudaEvent_t> eventPool;
+};
+
+namespace {
+
+cudaEvent_t take_event(gf_tracer* t) {
+    if (!t->eventPool.empty()) {
+        cudaEvent_t e = t->eventPool.back();
+        t->eventPool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    return e;
+}
+
+// Brackets one stage with events when timing is enabled.
+struct StageTimer {
+    gf_tracer* t;
+    int stage;
+    cudaStream_t stream;
+    cudaEvent_t start = nullptr;
+    StageTimer(gf_tracer* t_, int stage_, cudaStream_t s) : t(t_), stage(stage_), stream(s) {
+        if (t->timing) {
+            start = take_event(t);
+            if (start != nullptr) cudaEventRecord(start, stream);
+        }
+    }
+    ~StageTimer() {
+        if (start == nullptr) return;
+        cudaEvent_t end = take_event(t);
+        if (end == nullptr) return;
+        cudaEventRecord(end, stream);
+        t->pending.push_back({stage, start, end});
+    }
+};
+
+void prepare_pose(const float* pose7, gf::Pose& out) {
+    // Same double-precision construction as the oracle's oracle_prepare_pose:
+    // world->sensor rotation of quaternion (x, y, z, w), its transpose, and the
+    // sensor centre c = -R^T t.
+    const double tx = pose7[0], ty = pose7[1], tz = pose7[2];
+    const double x = pose7[3], y = pose7[4], z = pose7[5], w = pose7[6];
+    double R[9];
+    R[0] = 1.0 - 2.0 * (y * y + z * z);
+    R[1] = 2.0 * (x * y - w * z);
+    R[2] = 2.0 * (x * z + w * y);
+    R[3] = 2.0 * (x * y + w * z);
+    R[4] = 1.0 - 2.0 * (x * x + z * z);
+    R[5] = 2.0 * (y * z - w * x);
+    R[6] = 2.0 * (x * z - w * y);
+    R[7] = 2.0 * (y * z + w * x);
+    R[8] = 1.0 - 2.0 * (x * x + y * y);
+    for (int i = 0; i < 9; ++i) out.R[i] = float(R[i]);
+    out.t[0] = float(tx);
+    out.t[1] = float(ty);
+    out.t[2] = float(tz);
+    for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < 3; ++c) out.Rinv[3 * r + c] = out.R[3 * c + r];
+    for (int r = 0; r < 3; ++r) out.c[r] = float(-(R[0 * 3 + r] * tx + R[1 * 3 + r] * ty + R[2 * 3 + r] * tz));
+}
+
+int bind_device(gf_tracer* t) {
+    int dev = -1;
+    GF_CUDA(cudaGetDevice(&dev));
+    if (t->device < 0) {
+        t->device = dev;
+        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), sizeof(uint64_t), cudaHostAllocDefault));
+    } else if (t->device != dev) {
+        return fail(GF_ERR_STATE, "tracer bound to device %d, called on device %d", t->device, dev);
+    }
+    return GF_OK;
+}
+
+int validate_inputs(const gf_tracer* t, const gf_trace_inputs* in, const TileMask** maskOut) {
+    if (in == nullptr) return fail(GF_ERR_BAD_INPUT, "inputs is NULL");
+    const gf_camera& cam = in->camera;
+    if (cam.width <= 0 || cam.height <= 0) return fail(GF_ERR_BAD_INPUT, "camera resolution must be positive");
+    if (cam.model != GF_CAMERA_OPENCV_FISHEYE && cam.model != GF_CAMERA_OPENCV_PINHOLE)
+        return fail(GF_ERR_BAD_INPUT, "only OPENCV_FISHEYE and PINHOLE cameras are supported");
+    if (cam.shutter != GF_SHUTTER_GLOBAL)
+        return fail(GF_ERR_BAD_INPUT, "unconditional support union requires global shutter");
+    for (int k = 0; k < 7; ++k) {
+        if (in->pose_start[k] != in->pose_end[k])
+            return fail(GF_ERR_BAD_INPUT, "conservative opacity bound requires exact global-shutter poses");
+    }
+    if (in->sh_coeffs != 1 && in->sh_coeffs != 4 && in->sh_coeffs != 9 && in->sh_coeffs != 16)
+        return fail(GF_ERR_BAD_INPUT, "sh_coeffs must be 1, 4, 9 or 16 (got %u)", in->sh_coeffs);
+    if (in->sh_degree < 0 || in->sh_degree > 3) return fail(GF_ERR_BAD_INPUT, "sh_degree must be in [0,3]");
+    if (in->num_particles > 0 && (in->particles == nullptr || in->features == nullptr))
+        return fail(GF_ERR_BAD_INPUT, "particle buffers are NULL");
+    if (in->ray_origin == nullptr || in->ray_direction == nullptr) return fail(GF_ERR_BAD_INPUT, "ray buffers are NULL");
+    if ((reinterpret_cast<uintptr_t>(in->particles) & 15u) != 0u)
+        return fail(GF_ERR_BAD_INPUT, "particle rows must be 16-byte aligned");
+    if (in->tile_token == nullptr) return fail(GF_ERR_BAD_INPUT, "tile token is NULL");
+    const auto it = t->masks.find(in->tile_token);
+    if (it == t->masks.end()) return fail(GF_ERR_NOT_REGISTERED, "physical tile token is not registered on this tracer");
+    const uint32_t gx = uint32_t((cam.width + 15) / 16), gy = uint32_t((cam.height + 15) / 16);
+    if (it->second.tx != gx || it->second.ty != gy)
+        return fail(GF_ERR_BAD_INPUT, "physical tile token does not match current raster");
+    *maskOut = &it->second;
+    return GF_OK;
+}
+
+template <typename In, typename Out>
+int exclusive_scan(gf_tracer* t, const In* in, uint64_t n, Out* out, Out* grandTotal, cudaStream_t stream) {
+    const uint32_t tiles = uint32_t((n + gf::kScanTile - 1) / gf::kScanTile);
+    if (tiles == 0) {
+        GF_CUDA(cudaMemsetAsync(grandTotal, 0, sizeof(Out), stream));
+        return GF_OK;
+    }
+    if (int e = t->scanTiles.ensure(sizeof(Out) * tiles, stream)) return e;
+    Out* ts = t->scanTiles.as<Out>();
+    gf::k_scan_reduce<In, Out><<<tiles, gf::kScanThreads, 0, stream>>>(in, n, ts);
+    gf::k_scan_tiles<Out><<<1, gf::kScanThreads, 0, stream>>>(ts, tiles, grandTotal);
+    gf::k_scan_downsweep<In, Out><<<tiles, gf::kScanThreads, 0, stream>>>(in, n, ts, out);
+    t->launches += 3;
+    GF_LAUNCH_CHECK();
+    return GF_OK;
+}
+
+int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream) {
+    t->finalBuf = 0;
+    if (n == 0) return GF_OK;
+    const uint32_t blocks = (n + gf::kSortTile - 1) / gf::kSortTile;
+    if (int e = t->hist.ensure(sizeof(uint32_t) * (size_t(blocks) * gf::kRadixBins + 1), stream)) return e;
+    uint32_t* hist = t->hist.as<uint32_t>();
+    const int smem = int(sizeof(gf::SortScatterSmem));
+    GF_CUDA(cudaFuncSetAttribute(gf::k_radix_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int src = 0;
+    for (int shift = 0; shift < endBit; shift += 8) {
+        gf::k_radix_histogram<<<blocks, gf::kSortThreads, 0, stream>>>(t->keys[src].as<uint64_t>(), n, shift, blocks,
+                                                                      hist);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+        if (int e = exclusive_scan<uint32_t, uint32_t>(t, hist, uint64_t(blocks) * gf::kRadixBins, hist,
+                                                        hist + size_t(blocks) * gf::kRadixBins, stream))
+            return e;
+        gf::k_radix_scatter<<<blocks, gf::kSortThreads, smem, stream>>>(
+            t->keys[src].as<uint64_t>(), t->ids[src].as<uint32_t>(), t->keys[src ^ 1].as<uint64_t>(),
+            t->ids[src ^ 1].as<uint32_t>(), n, shift, blocks, hist);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+        src ^= 1;
+    }
+    t->finalBuf = src;
+    return GF_OK;
+}
+
+template <int K>
+void launch_render_fwd(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
+                       cudaStream_t stream) {
+    gf::k_render_fwd<K><<<tiles, gf::kTileThreads, 0, stream>>>(a, rgba, hd, hc);
+}
+
+template <int K>
+void launch_render_bwd(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
+    gf::k_render_bwd<K><<<tiles, gf::kTileThreads, 0, stream>>>(a);
+}
+
+int dispatch_fwd(int K, const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
+                 cudaStream_t s) {
+    switch (K) {
+        case 0: launch_render_fwd<0>(a, tiles, rgba, hd, hc, s); break;
+        case 4: launch_render_fwd<4>(a, tiles, rgba, hd, hc, s); break;
+        case 8: launch_render_fwd<8>(a, tiles, rgba, hd, hc, s); break;
+        case 12: launch_render_fwd<12>(a, tiles, rgba, hd, hc, s); break;
+        case 16: launch_render_fwd<16>(a, tiles, rgba, hd, hc, s); break;
+        case 24: launch_render_fwd<24>(a, tiles, rgba, hd, hc, s); break;
+        case 32: launch_render_fwd<32>(a, tiles, rgba, hd, hc, s); break;
+        default: return fail(GF_ERR_BAD_INPUT, "unsupported k-buffer size %d", K);
+    }
+    return GF_OK;
+}
+
+int dispatch_bwd(int K, const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t s) {
+    switch (K) {
+        case 0: launch_render_bwd<0>(a, tiles, s); break;
+        case 4: launch_render_bwd<4>(a, tiles, s); break;
+        case 8: launch_render_bwd<8>(a, tiles, s); break;
+        case 12: launch_render_bwd<12>(a, tiles, s); break;
+        case 16: launch_render_bwd<16>(a, tiles, s); break;
+        case 24: launch_render_bwd<24>(a, tiles, s); break;
+        case 32: launch_render_bwd<32>(a, tiles, s); break;
+        default: return fail(GF_ERR_BAD_INPUT, "unsupported k-buffer size %d", K);
+    }
+    return GF_OK;
+}
+
+// Projection, binning, sort and forward composite.
+int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, float* hc, float* vis,
+            cudaStream_t stream) {
+    if (int e = bind_device(t)) return e;
+    const TileMask* mask = nullptr;
+    if (int e = validate_inputs(t, in, &mask)) return e;
+    if (rgba == nullptr || hd == nullptr) return fail(GF_ERR_BAD_INPUT, "output buffers are NULL");
+    t->launches = 0;
+    t->haveForward = false;
+
+    gf::FrameArgs& f = t->frame;
+    f.cam = in->camera;
+    prepare_pose(in->pose_start, f.pose);
+    f.W = in->camera.width;
+    f.H = in->camera.height;
+    f.gx = (f.W + gf::kTile - 1) / gf::kTile;
+    f.gy = (f.H + gf::kTile - 1) / gf::kTile;
+    f.N = in->num_particles;
+    f.shDegree = in->sh_degree;
+    f.shCoeffs = in->sh_coeffs;
+    f.keyMode = t->cfg.sort_key;
+    const uint32_t T = uint32_t(f.gx * f.gy);
+    const uint32_t N = f.N;
+
+    if (int e = t->proj.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
+    if (int e = t->records.ensure(sizeof(float4) * 4 * size_t(N) + 16, stream)) return e;
+    if (int e = t->counts.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
+    if (int e = t->offsets.ensure(sizeof(uint64_t) * size_t(N) + 16, stream)) return e;
+    if (int e = t->total.ensure(sizeof(uint64_t) * 2, stream)) return e;
+    if (int e = t->tileRays.ensure(sizeof(float4) * 2 * size_t(T), stream)) return e;
+    if (int e = t->ranges.ensure(sizeof(uint2) * size_t(T), stream)) return e;
+
+    if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
+        StageTimer st(t, GF_STAGE_TILE_RAYS, stream);
+        gf::k_tile_rays<<<(T + 127) / 128, 128, 0, stream>>>(f, in->ray_origin, in->ray_direction,
+                                                              t->tileRays.as<float4>());
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    if (N > 0) {
+        StageTimer st(t, GF_STAGE_PROJECT, stream);
+        gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
+                                                          t->proj.as<float4>(), t->records.as<float4>(),
+                                                          t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis));
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    {
+        StageTimer st(t, GF_STAGE_SCAN, stream);
+        if (int e = exclusive_scan<uint32_t, uint64_t>(t, t->counts.as<uint32_t>(), N, t->offsets.as<uint64_t>(),
+                                                        t->total.as<uint64_t>(), stream))
+            return e;
+    }
+    GF_CUDA(cudaMemcpyAsync(t->hostTotal, t->total.ptr, sizeof(uint64_t), cudaMemcpyDeviceToHost, stream));
+    GF_CUDA(cudaStreamSynchronize(stream));
+    const uint64_t I = *t->hostTotal;
+    if (I > 0xffffffffull - gf::kSortTile)
+        return fail(GF_ERR_CAPACITY, "%llu tile intersections exceed the 32-bit index range",
+                    static_cast<unsigned long long>(I));
+    t->numIntersections = I;
+    for (int b = 0; b < 2; ++b) {
+        if (int e = t->keys[b].ensure(sizeof(uint64_t) * (I + 1), stream)) return e;
+        if (int e = t->ids[b].ensure(sizeof(uint32_t) * (I + 1), stream)) return e;
+    }
+    if (I > 0) {
+        StageTimer st(t, GF_STAGE_EMIT, stream);
+        gf::k_emit<<<(N + 255) / 256, 256, 0, stream>>>(f, t->proj.as<float4>(), t->records.as<float4>(),
+                                                        mask->buf.as<uint8_t>(), t->tileRays.as<float4>(),
+                                                        t->offsets.as<uint64_t>(), t->counts.as<uint32_t>(),
+                                                        t->keys[0].as<uint64_t>(), t->ids[0].as<uint32_t>());
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    const int endBit = 32 + int(bit_length(T));
+    {
+        StageTimer st(t, GF_STAGE_SORT, stream);
+        if (int e = radix_sort(t, uint32_t(I), endBit, stream)) return e;
+    }
+    {
+        StageTimer st(t, GF_STAGE_RANGES, stream);
+        GF_CUDA(cudaMemsetAsync(t->ranges.ptr, 0, sizeof(uint2) * T, stream));
+        if (I > 0) {
+            gf::k_tile_ranges<<<uint32_t((I + 255) / 256), 256, 0, stream>>>(t->keys[t->finalBuf].as<uint64_t>(),
+                                                                            uint32_t(I), t->ranges.as<uint2>());
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
+    }
+    gf::RenderArgs a;
+    a.f = f;
+    a.mask = mask->buf.as<uint8_t>();
+    a.ranges = t->ranges.as<uint2>();
+    a.sortedIds = t->ids[t->finalBuf].as<uint32_t>();
+    a.records = t->records.as<float4>();
+    a.rayO = in->ray_origin;
+    a.rayD = in->ray_direction;
+    {
+        StageTimer st(t, GF_STAGE_RENDER_FWD, stream);
+        if (int e = dispatch_fwd(t->cfg.k_buffer_size, a, T, rgba, hd, hc, stream)) return e;
+    }
+    t->launches += 1;
+    GF_LAUNCH_CHECK();
+    t->frameMask = a.mask;
+    t->frameRayO = in->ray_origin;
+    t->frameRayD = in->ray_direction;
+    t->haveForward = true;
+    t->totalLaunches += t->launches;
+    return GF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gf_abi_version(void) { return GF_ABI_VERSION; }
+
+const char* gf_last_error(void) { return g_lastError.c_str(); }
+
+gf_tracer* gf_tracer_create(const gf_tracer_config* config) {
+    if (config == nullptr) {
+        fail(GF_ERR_BAD_INPUT, "config is NULL");
+        return nullptr;
+    }
+    if (!valid_k(config->k_buffer_size)) {
+        fail(GF_ERR_BAD_INPUT, "k_buffer_size must be one of 0, 4, 8, 12, 16, 24, 32 (got %d)",
+             config->k_buffer_size);
+        return nullptr;
+    }
+    if (config->sort_key != GF_KEY_PER_TILE_DEPTH && config->sort_key != GF_KEY_GLOBAL_DEPTH) {
+        fail(GF_ERR_BAD_INPUT, "unknown sort key %d", config->sort_key);
+        return nullptr;
+    }
+    gf_tracer* t = new gf_tracer();
+    t->cfg = *config;
+    return t;
+}
+
+void gf_tracer_destroy(gf_tracer* t) {
+    if (t == nullptr) return;
+    if (t->device >= 0) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(t->device);
+        cudaDeviceSynchronize();
+        DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->counts, &t->offsets, &t->scanTiles, &t->total,
+                                &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
+                                &t->hist,    &t->gradRecords};
+        for (DeviceBuffer* b : bufs) b->release();
+        for (auto& kv : t->masks) kv.second.buf.release();
+        for (auto& ev : t->pending) {
+            cudaEventDestroy(ev.start);
+            cudaEventDestroy(ev.end);
+        }
+        for (cudaEvent_t e : t->eventPool) cudaEventDestroy(e);
+        if (t->hostTotal != nullptr) cudaFreeHost(t->hostTotal);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    delete t;
+}
+
+int gf_tracer_register_tile_mask(gf_tracer* t, const uint8_t* mask, uint32_t tiles_y, uint32_t tiles_x,
+                                 const char* token, void* stream) {
+    if (t == nullptr || mask == nullptr || token == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    if (tiles_y == 0 || tiles_x == 0) return fail(GF_ERR_BAD_INPUT, "empty tile mask");
+    if (int e = bind_device(t)) return e;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    TileMask& m = t->masks[token];
+    const size_t bytes = size_t(tiles_y) * tiles_x;
+    if (int e = m.buf.ensure(bytes, s)) return e;
+    GF_CUDA(cudaMemcpyAsync(m.buf.ptr, mask, bytes, cudaMemcpyDeviceToDevice, s));
+    m.ty = tiles_y;
+    m.tx = tiles_x;
+    return GF_OK;
+}
+
+int gf_tracer_trace(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_outputs* out, void* stream) {
+    if (t == nullptr || out == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    return forward(t, in, out->rgba, out->hit_distance, t->cfg.enable_hit_counts ? out->hit_count : nullptr,
+                   out->visibility, static_cast<cudaStream_t>(stream));
+}
+
+int gf_tracer_trace_inference(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hit_distance,
+                              void* stream) {
+    if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    return forward(t, in, rgba, hit_distance, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_grads* g, void* stream) {
+    if (t == nullptr || in == nullptr || g == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    if (!t->haveForward) return fail(GF_ERR_STATE, "trace_bwd requires a preceding trace");
+    if (int e = bind_device(t)) return e;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    gf::FrameArgs& f = t->frame;
+    if (in->num_particles != f.N || in->camera.width != f.W || in->camera.height != f.H ||
+        in->sh_coeffs != f.shCoeffs || in->ray_origin != t->frameRayO || in->ray_direction != t->frameRayD)
+        return fail(GF_ERR_STATE, "trace_bwd inputs differ from the preceding trace");
+    if (g->rgba == nullptr || g->hit_distance == nullptr || g->grad_rgba == nullptr || g->grad_hit_distance == nullptr ||
+        g->grad_particles == nullptr || g->grad_features == nullptr)
+        return fail(GF_ERR_BAD_INPUT, "backward buffers are NULL");
+    t->launches = 0;
+    const uint32_t N = f.N;
+    const uint32_t T = uint32_t(f.gx * f.gy);
+    if (int e = t->gradRecords.ensure(sizeof(float4) * 4 * size_t(N) + 16, s)) return e;
+    GF_CUDA(cudaMemsetAsync(t->gradRecords.ptr, 0, sizeof(float4) * 4 * size_t(N), s));
+    gf::RenderBwdArgs a;
+    a.r.f = f;
+    a.r.mask = t->frameMask;
+    a.r.ranges = t->ranges.as<uint2>();
+    a.r.sortedIds = t->ids[t->finalBuf].as<uint32_t>();
+    a.r.records = t->records.as<float4>();
+    a.r.rayO = t->frameRayO;
+    a.r.rayD = t->frameRayD;
+    a.rgba = g->rgba;
+    a.hitDistance = g->hit_distance;
+    a.gradRgba = g->grad_rgba;
+    a.gradHitDistance = g->grad_hit_distance;
+    a.gradRecords = t->gradRecords.as<float4>();
+    {
+        StageTimer st(t, GF_STAGE_RENDER_BWD, s);
+        if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, T, s)) return e;
+    }
+    t->launches += 1;
+    GF_LAUNCH_CHECK();
+    if (N > 0) {
+        StageTimer st(t, GF_STAGE_PROJECT_BWD, s);
+        gf::k_project_bwd<<<(N + 255) / 256, 256, 0, s>>>(f, in->particles, in->features, t->counts.as<uint32_t>(),
+                                                          t->gradRecords.as<float4>(), g->grad_particles,
+                                                          g->grad_features);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    t->totalLaunches += t->launches;
+    return GF_OK;
+}
+
+int gf_tracer_enable_timing(gf_tracer* t, int enable) {
+    if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    t->timing = enable != 0;
+    return GF_OK;
+}
+
+int gf_tracer_collect_times(gf_tracer* t, float* ms, uint32_t* launches) {
+    if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    float acc[GF_NUM_STAGES] = {};
+    uint32_t cnt[GF_NUM_STAGES] = {};
+    for (auto& ev : t->pending) {
+        GF_CUDA(cudaEventSynchronize(ev.end));
+        float v = 0.0f;
+        GF_CUDA(cudaEventElapsedTime(&v, ev.start, ev.end));
+        acc[ev.stage] += v;
+        cnt[ev.stage] += 1;
+        t->eventPool.push_back(ev.start);
+        t->eventPool.push_back(ev.end);
+    }
+    t->pending.clear();
+    for (int i = 0; i < GF_NUM_STAGES; ++i) {
+        if (ms != nullptr) ms[i] = acc[i];
+        if (launches != nullptr) launches[i] = cnt[i];
+    }
+    return GF_OK;
+}
+
+int gf_tracer_stats(const gf_tracer* t, gf_trace_stats* st) {
+    if (t == nullptr || st == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    st->num_intersections = t->numIntersections;
+    st->num_tiles = uint32_t(t->frame.gx * t->frame.gy);
+    st->num_particles = t->frame.N;
+    st->kernel_launches = t->launches;
+    st->reserved = 0;
+    st->total_kernel_launches = t->totalLaunches;
+    return GF_OK;
+}
+
+int gf_tracer_copy_intermediates(const gf_tracer* t, float* projected, float* radiance, uint32_t* counts,
+                                 uint64_t* sorted_keys, uint32_t* sorted_ids, uint64_t capacity, uint32_t* ranges,
+                                 void* stream) {
+    if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    if (!t->haveForward) return fail(GF_ERR_STATE, "no forward pass to copy");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t N = t->frame.N;
+    const size_t T = size_t(t->frame.gx) * t->frame.gy;
+    if (projected != nullptr && N > 0)
+        GF_CUDA(cudaMemcpyAsync(projected, t->proj.ptr, sizeof(float4) * 2 * N, cudaMemcpyDeviceToDevice, s));
+    if (radiance != nullptr && N > 0)
+        GF_CUDA(cudaMemcpy2DAsync(radiance, 3 * sizeof(float), static_cast<const char*>(t->records.ptr) + 52,
+                                  sizeof(float4) * 4, 3 * sizeof(float), N, cudaMemcpyDeviceToDevice, s));
+    if (counts != nullptr && N > 0)
+        GF_CUDA(cudaMemcpyAsync(counts, t->counts.ptr, sizeof(uint32_t) * N, cudaMemcpyDeviceToDevice, s));
+    const uint64_t I = t->numIntersections;
+    if ((sorted_keys != nullptr || sorted_ids != nullptr) && capacity < I)
+        return fail(GF_ERR_CAPACITY, "capacity %llu < %llu intersections", static_cast<unsigned long long>(capacity),
+                    static_cast<unsigned long long>(I));
+    if (sorted_keys != nullptr && I > 0)
+        GF_CUDA(cudaMemcpyAsync(sorted_keys, t->keys[t->finalBuf].ptr, sizeof(uint64_t) * I, cudaMemcpyDeviceToDevice, s));
+    if (sorted_ids != nullptr && I > 0)
+        GF_CUDA(cudaMemcpyAsync(sorted_ids, t->ids[t->finalBuf].ptr, sizeof(uint32_t) * I, cudaMemcpyDeviceToDevice, s));
+    if (ranges != nullptr)
+        GF_CUDA(cudaMemcpyAsync(ranges, t->ranges.ptr, sizeof(uint2) * T, cudaMemcpyDeviceToDevice, s));
+    return GF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,50 @@
+"""16x16 tile mask of the calibrated camera domain (reference
+threedgut_tracer/physical_tile_mask.py:1-65, same token and semantics).
+
+Tiles without a single valid pixel are skipped by the renderer.  The mask is
+built once per camera domain and registered under a 64-hex token.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from dataclasses import dataclass
+
+TILE = 16
+
+
+@dataclass(frozen=True)
+class PhysicalTileBinding:
+    mask: object
+    token: str
+
+
+def _token(*, domain: str, height: int, width: int, device: str, tile: int = TILE) -> str:
+    payload = {"domain": domain, "device": device, "height": height, "tile": tile, "width": width}
+    return hashlib.sha256(json.dumps(payload, sort_keys=True, separators=(",", ":")).encode()).hexdigest()
+
+
+def build_physical_tile_binding(batch, rays, domain: str = "full-raster", tile: int = TILE) -> PhysicalTileBinding:
+    """Tile mask of ``batch.physical_fov_mask`` (all tiles if absent)."""
+    import torch
+    import torch.nn.functional as functional
+
+    t = int(tile)
+    if rays.ndim != 4 or rays.shape[0] != 1 or rays.shape[-1] != 3 or rays.device.type != "cuda":
+        raise RuntimeError("physical tile pruning requires CUDA [1,H,W,3] rays")
+    height, width = int(rays.shape[1]), int(rays.shape[2])
+    physical = getattr(batch, "physical_fov_mask", None)
+    if physical is None:
+        tiles = torch.ones(((height + t - 1) // t, (width + t - 1) // t), dtype=torch.uint8, device=rays.device)
+    else:
+        if (not torch.is_tensor(physical) or physical.dtype != torch.bool or physical.ndim != 4
+                or tuple(physical.shape) != (1, height, width, 1) or physical.device != rays.device):
+            raise RuntimeError("physical_fov_mask must be a bool [1,H,W,1] tensor on the ray device")
+        mask = physical[0, ..., 0]
+        ph = ((height + t - 1) // t) * t
+        pw = ((width + t - 1) // t) * t
+        padded = functional.pad(mask, (0, pw - width, 0, ph - height), mode="constant", value=False)
+        tiles = padded.reshape(ph // t, t, pw // t, t).any(dim=3).any(dim=1).to(dtype=torch.uint8).contiguous()
+    return PhysicalTileBinding(mask=tiles,
+                               token=_token(domain=domain, height=height, width=width, device=str(rays.device), tile=t))

@@ -1,0 +1,214 @@
+"""Seeded synthetic scenes and cameras of the five benchmark workloads.
+
+The reference measures on public datasets (FIORD, FullCircle, ScanNet++,
+Tanks and Temples) that are not available here; these generators stand in
+for them with the workload shapes and value distributions:
+
+* means uniform in the spherical shell 1-5 m around the origin,
+* log-scales N(ln 0.02, 0.5^2) per axis, uniform unit quaternions,
+* opacity sigmoid(N(0, 1.5^2)),
+* SH DC chosen so the base colour is U[0,1] (c0 = (rgb - 0.5) / 0.2820948),
+  higher SH coefficients N(0, 0.1^2).
+
+``pack_particles`` builds the reference's packed [N,32] particle rows
+(threedgut_tracer/tracer.py:171-179): position, density, rotation (w,x,y,z),
+scale, intrinsic density, factor B = R diag(s) and its inverse, padding.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+from .camera import EQUISOLID_KB4, FisheyeCamera, fisheye_camera, random_kb_coefficients
+
+SH_C0 = 0.28209479177387814
+PACKED_WIDTH = 32
+SLOTS = {"position": (0, 3), "density": (3, 4), "rotation": (4, 8), "scale": (8, 11),
+         "intrinsic_density": (11, 12), "factor": (12, 21), "inverse_factor": (21, 30), "padding": (30, 32)}
+
+
+@dataclasses.dataclass
+class Scene:
+    positions: np.ndarray   # [N,3] float32
+    rotations: np.ndarray   # [N,4] float32 unit quaternions (w, x, y, z)
+    scales: np.ndarray      # [N,3] float32
+    density: np.ndarray     # [N,1] float32 opacity in (0, 1)
+    features: np.ndarray    # [N, 3*C] float32, coefficient k of channel c at [3k + c]
+    sh_degree: int
+
+    @property
+    def num(self) -> int:
+        return int(self.positions.shape[0])
+
+    @property
+    def sh_coeffs(self) -> int:
+        return int(self.features.shape[1] // 3)
+
+
+def quaternion_to_matrix(q: np.ndarray) -> np.ndarray:
+    """Rotation matrices [N,3,3] of unit quaternions (w, x, y, z)."""
+    q = np.asarray(q, dtype=np.float64)
+    w, x, y, z = q[:, 0], q[:, 1], q[:, 2], q[:, 3]
+    R = np.empty((q.shape[0], 3, 3), dtype=np.float64)
+    R[:, 0, 0] = 1 - 2 * (y * y + z * z)
+    R[:, 0, 1] = 2 * (x * y - w * z)
+    R[:, 0, 2] = 2 * (x * z + w * y)
+    R[:, 1, 0] = 2 * (x * y + w * z)
+    R[:, 1, 1] = 1 - 2 * (x * x + z * z)
+    R[:, 1, 2] = 2 * (y * z - w * x)
+    R[:, 2, 0] = 2 * (x * z - w * y)
+    R[:, 2, 1] = 2 * (y * z + w * x)
+    R[:, 2, 2] = 1 - 2 * (x * x + y * y)
+    return R
+
+
+def pack_particles(scene: Scene, chunk: int = 1 << 20) -> np.ndarray:
+    """[N,32] float32 packed rows with B = R diag(s), B^-1 = diag(1/s) R^T."""
+    n = scene.num
+    out = np.zeros((n, PACKED_WIDTH), dtype=np.float32)
+    for b in range(0, n, chunk):
+        e = min(n, b + chunk)
+        R = quaternion_to_matrix(scene.rotations[b:e])
+        s = scene.scales[b:e].astype(np.float64)
+        B = R * s[:, None, :]
+        Binv = np.transpose(R, (0, 2, 1)) / s[:, :, None]
+        rows = out[b:e]
+        rows[:, 0:3] = scene.positions[b:e]
+        rows[:, 3:4] = scene.density[b:e]
+        rows[:, 4:8] = scene.rotations[b:e]
+        rows[:, 8:11] = scene.scales[b:e]
+        rows[:, 11:12] = scene.density[b:e]
+        rows[:, 12:21] = B.reshape(-1, 9).astype(np.float32)
+        rows[:, 21:30] = Binv.reshape(-1, 9).astype(np.float32)
+    return out
+
+
+def _uniform_directions(rng: np.random.Generator, n: int) -> np.ndarray:
+    v = rng.standard_normal((n, 3))
+    return v / np.linalg.norm(v, axis=1, keepdims=True)
+
+
+def random_scene(n: int, sh_degree: int, seed: int, r_min: float = 1.0, r_max: float = 5.0) -> Scene:
+    rng = np.random.default_rng(seed)
+    u = rng.random(n)
+    radius = np.cbrt(u * (r_max ** 3 - r_min ** 3) + r_min ** 3)
+    positions = (_uniform_directions(rng, n) * radius[:, None]).astype(np.float32)
+    scales = np.exp(rng.normal(math.log(0.02), 0.5, size=(n, 3))).astype(np.float32)
+    q = rng.standard_normal((n, 4))
+    rotations = (q / np.linalg.norm(q, axis=1, keepdims=True)).astype(np.float32)
+    density = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.5, size=(n, 1))))).astype(np.float32)
+    coeffs = (sh_degree + 1) ** 2
+    features = np.empty((n, 3 * coeffs), dtype=np.float32)
+    rgb = rng.random((n, 3))
+    features[:, 0:3] = ((rgb - 0.5) / SH_C0).astype(np.float32)
+    if coeffs > 1:
+        features[:, 3:] = rng.normal(0.0, 0.1, size=(n, 3 * (coeffs - 1))).astype(np.float32)
+    return Scene(positions, rotations, scales, density, features, sh_degree)
+
+
+def random_rotation_quaternion_xyzw(rng: np.random.Generator) -> np.ndarray:
+    q = rng.standard_normal(4)
+    q /= np.linalg.norm(q)
+    return q.astype(np.float64)  # (x, y, z, w)
+
+
+def pose_world_to_sensor(center: np.ndarray, quat_xyzw: np.ndarray) -> np.ndarray:
+    """7-float world->sensor pose [t, q(x,y,z,w)] of a camera at ``center``
+    whose world->sensor rotation is ``quat_xyzw`` (t = -R c)."""
+    x, y, z, w = (float(v) for v in quat_xyzw)
+    R = quaternion_to_matrix(np.array([[w, x, y, z]]))[0]
+    t = -R @ np.asarray(center, dtype=np.float64)
+    return np.concatenate([t, [x, y, z, w]]).astype(np.float32)
+
+
+def look_outward_pose(center: np.ndarray, yaw: float) -> np.ndarray:
+    """World->sensor pose of a camera at ``center`` whose optical axis (+z)
+    points horizontally outward at azimuth ``yaw`` (world z up)."""
+    forward = np.array([math.cos(yaw), math.sin(yaw), 0.0])
+    up = np.array([0.0, 0.0, 1.0])
+    right = np.cross(forward, up)
+    right /= np.linalg.norm(right)
+    down = np.cross(forward, right)
+    # Sensor axes (x right, y down, z forward) expressed in world coordinates are
+    # the rows of the world->sensor rotation.
+    R = np.stack([right, down, forward], axis=0)
+    # quaternion (x, y, z, w) of R
+    tr = np.trace(R)
+    if tr > 0:
+        s = math.sqrt(tr + 1.0) * 2
+        w = 0.25 * s
+        x = (R[2, 1] - R[1, 2]) / s
+        y = (R[0, 2] - R[2, 0]) / s
+        z = (R[1, 0] - R[0, 1]) / s
+    elif R[0, 0] > R[1, 1] and R[0, 0] > R[2, 2]:
+        s = math.sqrt(1.0 + R[0, 0] - R[1, 1] - R[2, 2]) * 2
+        w = (R[2, 1] - R[1, 2]) / s
+        x = 0.25 * s
+        y = (R[0, 1] + R[1, 0]) / s
+        z = (R[0, 2] + R[2, 0]) / s
+    elif R[1, 1] > R[2, 2]:
+        s = math.sqrt(1.0 + R[1, 1] - R[0, 0] - R[2, 2]) * 2
+        w = (R[0, 2] - R[2, 0]) / s
+        x = (R[0, 1] + R[1, 0]) / s
+        y = 0.25 * s
+        z = (R[1, 2] + R[2, 1]) / s
+    else:
+        s = math.sqrt(1.0 + R[2, 2] - R[0, 0] - R[1, 1]) * 2
+        w = (R[1, 0] - R[0, 1]) / s
+        x = (R[0, 2] + R[2, 0]) / s
+        y = (R[1, 2] + R[2, 1]) / s
+        z = 0.25 * s
+    q = np.array([x, y, z, w])
+    q /= np.linalg.norm(q)
+    return pose_world_to_sensor(center, q)
+
+
+IDENTITY_POSE = np.array([0, 0, 0, 0, 0, 0, 1], dtype=np.float32)
+
+
+@dataclasses.dataclass
+class Workload:
+    name: str
+    scene: Scene
+    camera: FisheyeCamera
+    poses: list          # list of 7-float world->sensor poses
+    k_buffer: int
+    description: str
+
+
+def workload_cpu_scale(seed: int = 1234) -> Workload:
+    """10,000 Gaussians, SH degree 0, equidistant 200 deg 320x320, identity pose, k = 16."""
+    scene = random_scene(10_000, 0, seed)
+    cam = fisheye_camera(320, 320, 200.0)
+    return Workload("cpu_scale_fwd", scene, cam, [IDENTITY_POSE.copy()], 16,
+                    "10k Gaussians SH0, equidistant 200deg 320x320, identity pose, K=16")
+
+
+def workload_single_view(seed: int = 1235, n: int = 1_000_000, size: int = 1600) -> Workload:
+    """1M Gaussians SH3, Kannala-Brandt 200 deg 1600x1600, random pose in r < 0.5 m, k = 16."""
+    scene = random_scene(n, 3, seed)
+    rng = np.random.default_rng(seed + 1000)
+    k = random_kb_coefficients(rng, 200.0)
+    cam = fisheye_camera(size, size, 200.0, k)
+    center = _uniform_directions(rng, 1)[0] * 0.5 * np.cbrt(rng.random())
+    pose = pose_world_to_sensor(center, random_rotation_quaternion_xyzw(rng))
+    return Workload("single_view_fwd_bwd", scene, cam, [pose], 16,
+                    f"{n} Gaussians SH3, KB 200deg {size}x{size}, random pose, K=16, L1 vs U[0,1] target")
+
+
+def workload_multi_view(seed: int = 1236, n: int = 3_000_000, views: int = 64, size: int = 1600) -> Workload:
+    """3M Gaussians SH3, 64 KB 200 deg 1600x1600 views on a 2 m ring."""
+    scene = random_scene(n, 3, seed)
+    rng = np.random.default_rng(seed + 1000)
+    k = random_kb_coefficients(rng, 200.0)
+    cam = fisheye_camera(size, size, 200.0, k)
+    poses = []
+    for v in range(views):
+        yaw = rng.uniform(0.0, 2.0 * math.pi)
+        center = np.array([2.0 * math.cos(yaw), 2.0 * math.sin(yaw), 0.0])
+        poses.append(look_outward_pose(center, yaw))
+    return Workload("multi_view_fwd_bwd", scene, cam, poses, 16,
+                    f"{n} Gaussians SH3, {views} KB 200deg {size}x{size} views on a 2 m ring, K=16")

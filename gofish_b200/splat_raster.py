@@ -1,0 +1,254 @@
+"""``SplatRaster``: the reference's native renderer object, over the C ABI.
+
+Method names, argument order and outputs follow the reference's pybind module
+(threedgut_tracer/bindings.cpp:106-124, src/splatRaster.cpp): ``trace``,
+``trace_bwd``, ``trace_inference``, ``register_physical_tile_mask`` and
+``collect_times``.  Tensors stay on the device of the rays; every call is
+enqueued on the current CUDA stream of that device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Mapping
+
+import torch
+
+from . import _native
+from ._native import (GfTraceGrads, GfTraceInputs, GfTraceOutputs, GfTracerConfig, GfTraceStats, check)
+from .camera import CameraModelParameters
+
+# Channels of the reference's trace() outputs that are produced by the SOF
+# geometric losses of training (normals, distortion moments, quantile and
+# exact-crossing depth, extent, opacity field, inverse-depth moments).
+QUANT_CHANNELS = 10
+
+
+def _select(conf: Mapping[str, Any] | None, path: str, default):
+    node: Any = conf
+    for part in path.split("."):
+        if not isinstance(node, Mapping) or part not in node:
+            return default
+        node = node[part]
+    return default if node is None else node
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _pose7(pose) -> list[float]:
+    values = torch.as_tensor(pose, dtype=torch.float32).reshape(-1).cpu().tolist()
+    if len(values) != 7:
+        raise ValueError("sensor pose must have 7 values [tx, ty, tz, qx, qy, qz, qw]")
+    return values
+
+
+class SplatRaster:
+    """Renderer state of one scene/configuration (reference SplatRaster)."""
+
+    def __init__(self, conf: Mapping[str, Any] | None = None):
+        self._lib = _native.load()
+        cfg = GfTracerConfig()
+        cfg.k_buffer_size = int(_select(conf, "render.splat.k_buffer_size", 16))
+        cfg.sort_key = (_native.GF_KEY_GLOBAL_DEPTH if bool(_select(conf, "render.gofish.fast_global_depth_key", False))
+                        else _native.GF_KEY_PER_TILE_DEPTH)
+        cfg.enable_hit_counts = 1 if bool(_select(conf, "render.enable_hitcounts", True)) else 0
+        handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
+        if not handle:
+            raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())
+        self._handle = ctypes.c_void_p(handle)
+        self.config = cfg
+        self._masks: dict[str, torch.Tensor] = {}
+        self._times: dict[str, float] = {}
+        self._events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+        self.enable_kernel_timings = bool(_select(conf, "render.enable_kernel_timings", False))
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and handle.value:
+            self._lib.gf_tracer_destroy(handle)
+            self._handle = None
+
+    # ------------------------------------------------------------------ registry
+    def register_physical_tile_mask(self, mask: torch.Tensor, token: str) -> None:
+        """splatRaster.cpp:229-248: keep the uint8 [Ty,Tx] tile mask under ``token``."""
+        if mask.dtype != torch.uint8 or mask.ndim != 2 or not mask.is_cuda:
+            raise RuntimeError("physical tile mask must be a CUDA uint8 [Ty,Tx] tensor")
+        mask = mask.contiguous()
+        with torch.cuda.device(mask.device):
+            check(self._lib.gf_tracer_register_tile_mask(self._handle, mask.data_ptr(), mask.shape[0], mask.shape[1],
+                                                         token.encode(), _stream(mask.device)),
+                  "register_physical_tile_mask")
+        self._masks[token] = mask
+
+    # ------------------------------------------------------------------ helpers
+    def _inputs(self, frame, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir,
+                sensor: CameraModelParameters, t0, t1, pose0, pose1, token) -> GfTraceInputs:
+        for name, t in (("particle_density", particle_density), ("particle_radiance", particle_radiance),
+                        ("ray_ori", ray_ori), ("ray_dir", ray_dir)):
+            if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+                raise RuntimeError(f"{name} must be a contiguous CUDA float32 tensor")
+        if particle_density.ndim != 2 or particle_density.shape[1] != 32:
+            raise RuntimeError("particle_density must be [N,32]")
+        n = particle_density.shape[0]
+        if particle_radiance.shape[0] != n or particle_radiance.numel() % (3 * max(n, 1)) != 0:
+            raise RuntimeError("particle_radiance must be [N, 3*C]")
+        if ray_ori.ndim != 4 or ray_ori.shape[0] != 1 or ray_ori.shape[-1] != 3 or ray_dir.shape != ray_ori.shape:
+            raise RuntimeError("rays must be [1,H,W,3]")
+        height, width = int(ray_ori.shape[1]), int(ray_ori.shape[2])
+        inp = GfTraceInputs()
+        inp.frame = int(frame)
+        inp.sh_degree = int(n_active_features)
+        inp.num_particles = n
+        inp.sh_coeffs = particle_radiance.numel() // (3 * n) if n > 0 else 1
+        inp.particles = particle_density.data_ptr()
+        inp.features = particle_radiance.data_ptr()
+        inp.ray_origin = ray_ori.data_ptr()
+        inp.ray_direction = ray_dir.data_ptr()
+        inp.camera = sensor.native(width, height)
+        inp.pose_start[:] = _pose7(pose0)
+        inp.pose_end[:] = _pose7(pose1)
+        inp.timestamp_start = int(t0)
+        inp.timestamp_end = int(t1)
+        inp.tile_token = token.encode()
+        return inp
+
+    def _timed(self, name: str, device):
+        if not self.enable_kernel_timings:
+            return None
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(torch.cuda.current_stream(device))
+        self._events.append((name, start, end))
+        return end
+
+    # ------------------------------------------------------------------ trace
+    def trace(self, frame_id, sof_exact_opacity_active, n_active_features, particle_density, particle_radiance,
+              ray_ori, ray_dir, ray_time, sensor, t0, t1, pose0, pose1, token):
+        """splatRaster.cpp:259-380.  Returns the reference's 11 tensors:
+        radiance+opacity [H,W,4], hit distance [H,W,1], hit count [H,W,1],
+        visibility [N,1], and the seven training geometric channels."""
+        if sof_exact_opacity_active:
+            raise NotImplementedError("the SOF opacity-field channel is not implemented by this tracer")
+        device = ray_ori.device
+        height, width = int(ray_ori.shape[1]), int(ray_ori.shape[2])
+        n = particle_density.shape[0]
+        f32 = dict(dtype=torch.float32, device=device)
+        rgba = torch.empty((height, width, 4), **f32)
+        hit_distance = torch.empty((height, width, 1), **f32)
+        hit_count = torch.zeros((height, width, 1), **f32)
+        visibility = torch.zeros((n, 1), **f32)
+        inp = self._inputs(frame_id, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir,
+                           sensor, t0, t1, pose0, pose1, token)
+        out = GfTraceOutputs()
+        out.rgba = rgba.data_ptr()
+        out.hit_distance = hit_distance.data_ptr()
+        out.hit_count = hit_count.data_ptr()
+        out.visibility = visibility.data_ptr() if n > 0 else None
+        with torch.cuda.device(device):
+            end = self._timed("forward_render", device)
+            check(self._lib.gf_tracer_trace(self._handle, ctypes.byref(inp), ctypes.byref(out), _stream(device)),
+                  "trace")
+            if end is not None:
+                end.record(torch.cuda.current_stream(device))
+        zeros = lambda c: torch.zeros((height, width, c), **f32)  # noqa: E731
+        return (rgba, hit_distance, hit_count, visibility, zeros(3), zeros(1), zeros(QUANT_CHANNELS), zeros(1),
+                zeros(1), zeros(1), zeros(1))
+
+    def trace_inference(self, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir, sensor, t0,
+                        t1, pose0, pose1, token):
+        """splatRaster.cpp:383-466: radiance+opacity [H,W,4], hit distance [H,W,1]."""
+        device = ray_ori.device
+        height, width = int(ray_ori.shape[1]), int(ray_ori.shape[2])
+        f32 = dict(dtype=torch.float32, device=device)
+        rgba = torch.empty((height, width, 4), **f32)
+        hit_distance = torch.empty((height, width, 1), **f32)
+        inp = self._inputs(0, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir, sensor, t0,
+                           t1, pose0, pose1, token)
+        with torch.cuda.device(device):
+            check(self._lib.gf_tracer_trace_inference(self._handle, ctypes.byref(inp), rgba.data_ptr(),
+                                                      hit_distance.data_ptr(), _stream(device)), "trace_inference")
+        return rgba, hit_distance
+
+    def trace_bwd(self, frame_id, sof_exact_opacity_active, n_active_features, particle_density, particle_radiance,
+                  ray_ori, ray_dir, ray_time, sensor, t0, t1, pose0, pose1, ray_features_density,
+                  ray_features_density_grd, ray_hit_distance, ray_hit_distance_grd, *geometry_and_token):
+        """splatRaster.cpp:469-640.  ``geometry_and_token`` holds the seven
+        (value, gradient) pairs of the geometric channels followed by the tile
+        token, as in the reference's argument list.  Returns the [N,32]
+        particle gradient and the [N, 3*C] SH gradient."""
+        *geometry, token = geometry_and_token
+        if len(geometry) not in (0, 14):
+            raise TypeError("trace_bwd expects the seven (value, gradient) geometric channel pairs and the token")
+        # The geometric channels are outputs of zeros here; their gradients do
+        # not reach the particles (Tracer refuses a loss that uses them).
+        device = ray_ori.device
+        n = particle_density.shape[0]
+        grad_particles = torch.empty((n, 32), dtype=torch.float32, device=device)
+        grad_features = torch.empty_like(particle_radiance)
+        inp = self._inputs(frame_id, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir,
+                           sensor, t0, t1, pose0, pose1, token)
+        g = GfTraceGrads()
+        rgba = ray_features_density.float().contiguous()
+        grad_rgba = ray_features_density_grd.float().contiguous()
+        hd = ray_hit_distance.contiguous()
+        ghd = (ray_hit_distance_grd if ray_hit_distance_grd is not None else torch.zeros_like(hd)).contiguous()
+        g.rgba = rgba.data_ptr()
+        g.hit_distance = hd.data_ptr()
+        g.grad_rgba = grad_rgba.data_ptr()
+        g.grad_hit_distance = ghd.data_ptr()
+        g.grad_particles = grad_particles.data_ptr()
+        g.grad_features = grad_features.data_ptr()
+        with torch.cuda.device(device):
+            end = self._timed("backward_render", device)
+            check(self._lib.gf_tracer_trace_bwd(self._handle, ctypes.byref(inp), ctypes.byref(g), _stream(device)),
+                  "trace_bwd")
+            if end is not None:
+                end.record(torch.cuda.current_stream(device))
+        return grad_particles, grad_features
+
+    # ------------------------------------------------------------------ introspection
+    def collect_times(self) -> dict[str, float]:
+        """splatRaster.cpp:702-732: milliseconds of the timed calls since the last collection."""
+        times: dict[str, float] = {}
+        for name, start, end in self._events:
+            end.synchronize()
+            times[name] = times.get(name, 0.0) + start.elapsed_time(end)
+        self._events.clear()
+        return times
+
+    def enable_stage_timing(self, enable: bool = True) -> None:
+        check(self._lib.gf_tracer_enable_timing(self._handle, 1 if enable else 0), "enable_timing")
+
+    def collect_stage_times(self) -> dict[str, tuple[float, int]]:
+        """Milliseconds and launch count per native stage since the last collection."""
+        ms = (ctypes.c_float * len(_native.STAGES))()
+        launches = (ctypes.c_uint32 * len(_native.STAGES))()
+        check(self._lib.gf_tracer_collect_times(self._handle, ms, launches), "collect_times")
+        return {name: (float(ms[i]), int(launches[i])) for i, name in enumerate(_native.STAGES)}
+
+    def stats(self) -> GfTraceStats:
+        st = GfTraceStats()
+        check(self._lib.gf_tracer_stats(self._handle, ctypes.byref(st)), "stats")
+        return st
+
+    def copy_intermediates(self, device) -> dict[str, torch.Tensor]:
+        """Projected state, radiance, counts, sorted keys/ids and tile ranges of the last forward."""
+        st = self.stats()
+        n, t, i = st.num_particles, st.num_tiles, st.num_intersections
+        dev = torch.device(device)
+        proj = torch.empty((n, 8), dtype=torch.float32, device=dev)
+        rgb = torch.empty((n, 3), dtype=torch.float32, device=dev)
+        counts = torch.empty((n,), dtype=torch.int32, device=dev)
+        keys = torch.empty((max(i, 1),), dtype=torch.int64, device=dev)
+        ids = torch.empty((max(i, 1),), dtype=torch.int32, device=dev)
+        ranges = torch.empty((t, 2), dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            check(self._lib.gf_tracer_copy_intermediates(self._handle, proj.data_ptr(), rgb.data_ptr(),
+                                                         counts.data_ptr(), keys.data_ptr(), ids.data_ptr(), max(i, 1),
+                                                         ranges.data_ptr(), _stream(dev)), "copy_intermediates")
+        return dict(proj=proj, rgb=rgb, counts=counts, keys=keys[:i], ids=ids[:i], ranges=ranges)

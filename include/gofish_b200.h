@@ -1,0 +1,199 @@
+/*
+ * gofish_b200: C ABI of the B200 (sm_100a) fisheye Gaussian tracer.
+ *
+ * Plain pointers and sizes only.  Every device pointer is CUDA global memory
+ * on the device that is current when the call is made; `stream` is a
+ * cudaStream_t passed as void*.  All work is enqueued on that stream.  Calls
+ * return 0 on success and a negative GF_ERR_* code on failure, in which case
+ * gf_last_error() describes the failure (thread-local string).
+ *
+ * Each entry point replaces one method of the reference's pybind module
+ * (tuallen/GOFish, threedgut_tracer/bindings.cpp:106-165 and
+ * src/splatRaster.cpp); the binding a maintainer adds on the reference side
+ * is shown in INTEGRATION.md.
+ */
+#ifndef GOFISH_B200_H
+#define GOFISH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GF_ABI_VERSION 1
+
+#define GF_OK 0
+#define GF_ERR_BAD_INPUT (-1)
+#define GF_ERR_CUDA (-2)
+#define GF_ERR_NOT_REGISTERED (-3)
+#define GF_ERR_STATE (-4)
+#define GF_ERR_CAPACITY (-5)
+
+/* Camera model types (cameraModels.h ModelType) and shutter types
+ * (cameraModels.h:51-57 ShutterType; only GLOBAL is rendered, as in the
+ * reference, gutRenderer.cu:704-706). */
+#define GF_CAMERA_OPENCV_PINHOLE 0
+#define GF_CAMERA_OPENCV_FISHEYE 1
+#define GF_SHUTTER_ROLLING_TOP_TO_BOTTOM 0
+#define GF_SHUTTER_ROLLING_LEFT_TO_RIGHT 1
+#define GF_SHUTTER_ROLLING_BOTTOM_TO_TOP 2
+#define GF_SHUTTER_ROLLING_RIGHT_TO_LEFT 3
+#define GF_SHUTTER_GLOBAL 4
+
+/* Camera model parameters.  Replaces the TSensorModel built by
+ * fromOpenCVFisheyeCameraModelParameters / fromOpenCVPinholeCameraModelParameters
+ * (threedgut_tracer/bindings.cpp:36-79).  Fisheye uses radial[0..3] = k1..k4
+ * and max_angle; pinhole uses radial[0..5], tangential and thin_prism. */
+typedef struct gf_camera {
+    int32_t model;
+    int32_t width;
+    int32_t height;
+    int32_t shutter;
+    float principal_point[2];
+    float focal_length[2];
+    float radial[6];
+    float tangential[2];
+    float thin_prism[4];
+    float max_angle;
+    float reserved;
+} gf_camera;
+
+/* Sort key of the (tile | depth) radix sort. */
+#define GF_KEY_PER_TILE_DEPTH 0  /* per-tile maximum-response depth (gutProjector.cuh:364-417) */
+#define GF_KEY_GLOBAL_DEPTH 1    /* camera radial distance (gutProjector.cuh:426-427)           */
+
+/* Renderer configuration.  Replaces SplatRaster(json conf) (bindings.cpp:109)
+ * for the settings that change this path: render.splat.k_buffer_size,
+ * render.gofish.fast_global_depth_key and render.enable_hitcounts. */
+typedef struct gf_tracer_config {
+    int32_t k_buffer_size;     /* 0, 4, 8, 12, 16, 24 or 32 */
+    int32_t sort_key;          /* GF_KEY_* */
+    int32_t enable_hit_counts; /* 1: write the per-pixel hit count */
+    int32_t reserved;
+} gf_tracer_config;
+
+/* Per-call inputs of trace / trace_bwd / trace_inference
+ * (splatRaster.cpp:259-273, :383-393, :469-500). */
+typedef struct gf_trace_inputs {
+    uint32_t frame;
+    int32_t sh_degree;          /* active SH degree, 0..3 (n_active_features) */
+    uint32_t num_particles;     /* N */
+    uint32_t sh_coeffs;         /* coefficients per colour channel in `features`: 1, 4, 9 or 16 */
+    const float* particles;     /* device [N,32] packed particle rows (tracer.py:171-179) */
+    const float* features;      /* device [N, 3*sh_coeffs] SH coefficients */
+    const float* ray_origin;    /* device [H,W,3] sensor-frame ray origins */
+    const float* ray_direction; /* device [H,W,3] sensor-frame unit ray directions */
+    gf_camera camera;           /* width/height must match the ray grid */
+    float pose_start[7];        /* world->sensor [tx,ty,tz,qx,qy,qz,qw] at t0 */
+    float pose_end[7];          /* world->sensor pose at t1 (must equal pose_start) */
+    int64_t timestamp_start;
+    int64_t timestamp_end;
+    const char* tile_token;     /* token of a registered physical tile mask */
+} gf_trace_inputs;
+
+/* Forward outputs (caller-allocated device buffers, initialized by the call
+ * exactly as splatRaster.cpp:293-313 initializes its tensors). */
+typedef struct gf_trace_outputs {
+    float* rgba;          /* [H,W,4] radiance + opacity                       */
+    float* hit_distance;  /* [H,W,1]                                           */
+    float* hit_count;     /* [H,W,1] or NULL                                   */
+    float* visibility;    /* [N,1]: int bit pattern 1 where the particle is admitted to a tile, else 0; or NULL */
+} gf_trace_outputs;
+
+/* Backward inputs/outputs (splatRaster.cpp:469-640). */
+typedef struct gf_trace_grads {
+    const float* rgba;              /* forward [H,W,4] */
+    const float* hit_distance;      /* forward [H,W,1] */
+    const float* grad_rgba;         /* dL/d rgba [H,W,4] */
+    const float* grad_hit_distance; /* dL/d hit distance [H,W,1] */
+    float* grad_particles;          /* out [N,32] (overwritten) */
+    float* grad_features;           /* out [N, 3*sh_coeffs] (overwritten) */
+} gf_trace_grads;
+
+/* Counters of the last forward pass. */
+typedef struct gf_trace_stats {
+    uint64_t num_intersections; /* emitted (tile, particle) pairs */
+    uint32_t num_tiles;
+    uint32_t num_particles;
+    uint32_t kernel_launches;   /* kernels launched by the last trace/trace_bwd call */
+    uint32_t reserved;
+    uint64_t total_kernel_launches; /* kernels launched by this tracer since its creation */
+} gf_trace_stats;
+
+typedef struct gf_tracer gf_tracer;
+
+/* Library ABI version (GF_ABI_VERSION). */
+int gf_abi_version(void);
+
+/* Thread-local description of the last error. */
+const char* gf_last_error(void);
+
+/* SplatRaster::SplatRaster(json) -- bindings.cpp:109, splatRaster.cpp:106-153. */
+gf_tracer* gf_tracer_create(const gf_tracer_config* config);
+
+/* ~SplatRaster. Frees every device buffer the tracer owns. */
+void gf_tracer_destroy(gf_tracer* tracer);
+
+/* SplatRaster::registerPhysicalTileMask -- bindings.cpp:123, splatRaster.cpp:229-248.
+ * `mask` is a device uint8 [tiles_y, tiles_x] array; it is copied. */
+int gf_tracer_register_tile_mask(gf_tracer* tracer, const uint8_t* mask, uint32_t tiles_y, uint32_t tiles_x,
+                                 const char* token, void* stream);
+
+/* SplatRaster::trace -- bindings.cpp:110, splatRaster.cpp:259-380 (colour,
+ * opacity, hit distance, hit count and visibility channels). */
+int gf_tracer_trace(gf_tracer* tracer, const gf_trace_inputs* inputs, const gf_trace_outputs* outputs,
+                    void* stream);
+
+/* SplatRaster::traceBwd -- bindings.cpp:111, splatRaster.cpp:469-640.  Must
+ * follow a gf_tracer_trace with the same inputs on the same stream. */
+int gf_tracer_trace_bwd(gf_tracer* tracer, const gf_trace_inputs* inputs, const gf_trace_grads* grads,
+                        void* stream);
+
+/* SplatRaster::traceInference -- bindings.cpp:113, splatRaster.cpp:383-466. */
+int gf_tracer_trace_inference(gf_tracer* tracer, const gf_trace_inputs* inputs, float* rgba, float* hit_distance,
+                              void* stream);
+
+/* Stages timed by gf_tracer_collect_times. */
+#define GF_STAGE_TILE_RAYS 0
+#define GF_STAGE_PROJECT 1
+#define GF_STAGE_SCAN 2
+#define GF_STAGE_EMIT 3
+#define GF_STAGE_SORT 4
+#define GF_STAGE_RANGES 5
+#define GF_STAGE_RENDER_FWD 6
+#define GF_STAGE_RENDER_BWD 7
+#define GF_STAGE_PROJECT_BWD 8
+#define GF_NUM_STAGES 9
+
+/* Turns per-stage CUDA-event timing on or off (render.enable_kernel_timings,
+ * splatRaster.cpp:155-198).  Events are recorded on the call's stream. */
+int gf_tracer_enable_timing(gf_tracer* tracer, int enable);
+
+/* SplatRaster::collectTimes (splatRaster.cpp:702-732): writes the summed
+ * milliseconds and the launch count of every stage timed since the last
+ * collection into ms[GF_NUM_STAGES] and launches[GF_NUM_STAGES] (either may
+ * be NULL), then clears them.  Waits for the recorded events. */
+int gf_tracer_collect_times(gf_tracer* tracer, float* ms, uint32_t* launches);
+
+/* Counters of the last forward pass (SplatRaster::collectTimes, splatRaster.cpp:702-732, reports timings;
+ * this reports the sizes the timings depend on). */
+int gf_tracer_stats(const gf_tracer* tracer, gf_trace_stats* stats);
+
+/* Copies the last forward pass's intermediate state into caller device
+ * buffers (any pointer may be NULL): projected particle state [N,8]
+ * (center.xy, conic.xyz, opacity, extent.xy), precomputed radiance [N,3],
+ * per-particle tile counts [N], sorted (tile|depth) keys and particle ids
+ * [capacity], and per-tile [begin,end) ranges [T,2].  No reference
+ * counterpart: it exposes GutRenderForwardContext (gutRenderer.cu:229-671)
+ * for parity tests. */
+int gf_tracer_copy_intermediates(const gf_tracer* tracer, float* projected, float* radiance, uint32_t* counts,
+                                 uint64_t* sorted_keys, uint32_t* sorted_ids, uint64_t capacity, uint32_t* ranges,
+                                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GOFISH_B200_H */

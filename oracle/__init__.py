@@ -1,0 +1,237 @@
+"""CPU oracle of the GOFish fisheye tracer -- TEST INFRASTRUCTURE ONLY.
+
+A scalar C++ restatement (gofish_oracle.cpp) of the reference renderer's
+equations, each function citing the reference file:line it follows.  Only
+tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as
+the checker or as the timed CPU baseline; the product never imports it.
+
+Parity status: the reference's CUDA extension cannot be built or run in this
+environment (empty tiny-cuda-nn submodule, no slangc) and the reference ships
+no tests or golden vectors for this path, so the restatement is pinned by
+analytic known-answer tests and finite-difference gradient checks
+(tests/test_oracle_kat.py, tests/test_oracle_gradcheck.py) -- parity
+against the reference binary itself is unpinned.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIBRARY = HERE / "liboracle.so"
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    """Compile liboracle.so with the Makefile beside this file."""
+    src = [HERE / "gofish_oracle.cpp", HERE.parent / "gofish_b200" / "csrc" / "gf_elementary.h"]
+    if force or not LIBRARY.exists() or any(p.stat().st_mtime > LIBRARY.stat().st_mtime for p in src):
+        subprocess.run(["make", "-s", "-B", "-C", str(HERE), "liboracle.so"], check=True)
+    return LIBRARY
+
+
+class OracleCamera(ctypes.Structure):
+    _fields_ = [
+        ("model", ctypes.c_int32),
+        ("width", ctypes.c_int32),
+        ("height", ctypes.c_int32),
+        ("pad0", ctypes.c_int32),
+        ("principal", ctypes.c_float * 2),
+        ("focal", ctypes.c_float * 2),
+        ("radial", ctypes.c_float * 6),
+        ("tangential", ctypes.c_float * 2),
+        ("thin_prism", ctypes.c_float * 4),
+        ("max_angle", ctypes.c_float),
+        ("pad1", ctypes.c_float),
+    ]
+
+
+class OraclePose(ctypes.Structure):
+    _fields_ = [("R", ctypes.c_float * 9), ("t", ctypes.c_float * 3), ("Rinv", ctypes.c_float * 9),
+                ("c", ctypes.c_float * 3)]
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    build()
+    lib = ctypes.CDLL(str(LIBRARY))
+    vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    cam_p, pose_p = ctypes.POINTER(OracleCamera), ctypes.POINTER(OraclePose)
+    sig = {
+        "oracle_prepare_pose": (None, [vp, pose_p]),
+        "oracle_project": (i32, [cam_p, pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
+        "oracle_tile_rays": (i32, [cam_p, pose_p, vp, vp, vp]),
+        "oracle_bin": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64, vp]),
+        "oracle_render_forward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "oracle_render_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp,
+                                         vp]),
+        "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
+        "oracle_visibility": (i32, [i32, vp, vp]),
+        "oracle_num_threads": (i32, []),
+        "oracle_expf": (f32, [f32]),
+        "oracle_logf": (f32, [f32]),
+        "oracle_atan2f": (f32, [f32, f32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def camera(model: int, width: int, height: int, principal, focal, radial, max_angle: float = 0.0,
+           tangential=(0.0, 0.0), thin_prism=(0.0, 0.0, 0.0, 0.0)) -> OracleCamera:
+    cam = OracleCamera()
+    cam.model = int(model)
+    cam.width = int(width)
+    cam.height = int(height)
+    cam.principal[:] = [float(np.float32(v)) for v in principal]
+    cam.focal[:] = [float(np.float32(v)) for v in focal]
+    r = [float(np.float32(v)) for v in radial] + [0.0] * (6 - len(radial))
+    cam.radial[:] = r[:6]
+    cam.tangential[:] = [float(np.float32(v)) for v in tangential]
+    cam.thin_prism[:] = [float(np.float32(v)) for v in thin_prism]
+    cam.max_angle = float(np.float32(max_angle))
+    return cam
+
+
+def prepare_pose(pose7) -> OraclePose:
+    p = np.ascontiguousarray(np.asarray(pose7, dtype=np.float32).reshape(7))
+    out = OraclePose()
+    load().oracle_prepare_pose(_p(p), ctypes.byref(out))
+    return out
+
+
+def num_threads() -> int:
+    return int(load().oracle_num_threads())
+
+
+def tile_grid(cam: OracleCamera) -> tuple[int, int]:
+    return (cam.width + 15) // 16, (cam.height + 15) // 16
+
+
+def project(cam, pose, particles, sh, sh_degree, mask):
+    lib = load()
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    sh = np.ascontiguousarray(sh, dtype=np.float32)
+    mask = np.ascontiguousarray(mask, dtype=np.uint8)
+    n = particles.shape[0]
+    proj = np.zeros((n, 8), dtype=np.float32)
+    rgb = np.zeros((n, 3), dtype=np.float32)
+    counts = np.zeros(n, dtype=np.uint32)
+    lib.oracle_project(ctypes.byref(cam), ctypes.byref(pose), n, _p(particles), _p(sh), sh.shape[1] // 3,
+                       int(sh_degree), _p(mask), _p(proj), _p(rgb), _p(counts))
+    return proj, rgb, counts
+
+
+def tile_rays(cam, pose, ray_o, ray_d):
+    gx, gy = tile_grid(cam)
+    out = np.zeros((gx * gy, 8), dtype=np.float32)
+    ray_o = np.ascontiguousarray(ray_o, dtype=np.float32)
+    ray_d = np.ascontiguousarray(ray_d, dtype=np.float32)
+    load().oracle_tile_rays(ctypes.byref(cam), ctypes.byref(pose), _p(ray_o), _p(ray_d), _p(out))
+    return out
+
+
+def bin(cam, pose, particles, proj, counts, mask, tile_ray_table, key_mode):
+    lib = load()
+    gx, gy = tile_grid(cam)
+    total = int(counts.astype(np.uint64).sum())
+    keys = np.zeros(max(total, 1), dtype=np.uint64)
+    ids = np.zeros(max(total, 1), dtype=np.uint32)
+    ranges = np.zeros((gx * gy, 2), dtype=np.uint32)
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    got = lib.oracle_bin(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                         _p(np.ascontiguousarray(proj)), _p(np.ascontiguousarray(counts)),
+                         _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(tile_ray_table)),
+                         int(key_mode), _p(keys), _p(ids), total, _p(ranges))
+    if got != total:
+        raise RuntimeError("oracle_bin capacity mismatch")
+    return keys[:total], ids[:total], ranges
+
+
+def render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, tiles=None):
+    lib = load()
+    h, w = cam.height, cam.width
+    gx, gy = tile_grid(cam)
+    t0, t1 = (0, gx * gy) if tiles is None else tiles
+    rgba = np.zeros((h, w, 4), dtype=np.float32)
+    hit_t = np.full((h, w), 1e6, dtype=np.float32)
+    count = np.zeros((h, w), dtype=np.float32)
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    lib.oracle_render_forward(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                              _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                              _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                              _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                              _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                              _p(ids), int(k), int(t0), int(t1), _p(rgba), _p(hit_t), _p(count))
+    return rgba, hit_t, count
+
+
+def render_backward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, rgba, hit_t, grad_rgba,
+                    grad_hit_t, tiles=None):
+    lib = load()
+    gx, gy = tile_grid(cam)
+    t0, t1 = (0, gx * gy) if tiles is None else tiles
+    n = particles.shape[0]
+    grad = np.zeros((n, 16), dtype=np.float32)
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    lib.oracle_render_backward(ctypes.byref(cam), ctypes.byref(pose), n,
+                               _p(np.ascontiguousarray(particles, dtype=np.float32)),
+                               _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                               _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                               _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                               _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                               _p(ids), int(k), int(t0), int(t1), _p(np.ascontiguousarray(rgba, dtype=np.float32)),
+                               _p(np.ascontiguousarray(hit_t, dtype=np.float32)),
+                               _p(np.ascontiguousarray(grad_rgba, dtype=np.float32)),
+                               _p(np.ascontiguousarray(grad_hit_t, dtype=np.float32)), _p(grad))
+    return grad
+
+
+def project_backward(pose, particles, sh, sh_degree, counts, grad_record):
+    lib = load()
+    n = particles.shape[0]
+    sh = np.ascontiguousarray(sh, dtype=np.float32)
+    gp = np.zeros((n, 32), dtype=np.float32)
+    gs = np.zeros_like(sh)
+    lib.oracle_project_backward(ctypes.byref(pose), n, _p(np.ascontiguousarray(particles, dtype=np.float32)), _p(sh),
+                                sh.shape[1] // 3, int(sh_degree), _p(np.ascontiguousarray(counts)),
+                                _p(np.ascontiguousarray(grad_record, dtype=np.float32)), _p(gp), _p(gs))
+    return gp, gs
+
+
+def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None):
+    """Full forward pass; returns a dict of every intermediate and output."""
+    pose = prepare_pose(pose7)
+    proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask)
+    tr = tile_rays(cam, pose, ray_o, ray_d)
+    keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode)
+    rgba, hit_t, count = render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, ids, k, tiles)
+    vis = (counts > 0).astype(np.uint32)
+    return dict(pose=pose, proj=proj, rgb=rgb, counts=counts, tile_rays=tr, keys=keys, ids=ids, ranges=ranges,
+                rgba=rgba, hit_t=hit_t, hit_count=count, visibility=vis)
+
+
+def trace_backward(cam, fwd, particles, sh, sh_degree, ray_o, ray_d, mask, k, grad_rgba, grad_hit_t, tiles=None):
+    rec = render_backward(cam, fwd["pose"], particles, fwd["rgb"], ray_o, ray_d, mask, fwd["ranges"], fwd["ids"], k,
+                          fwd["rgba"], fwd["hit_t"], grad_rgba, grad_hit_t, tiles)
+    gp, gs = project_backward(fwd["pose"], particles, sh, sh_degree, fwd["counts"], rec)
+    return gp, gs, rec

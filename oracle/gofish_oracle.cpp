@@ -1,0 +1,1020 @@
+// CPU oracle for the GOFish fisheye tracer hot path -- TEST INFRASTRUCTURE.
+//
+// This file is a scalar C++ restatement of the reference renderer's equations
+// (tuallen/GOFish, threedgut_tracer/...).  It is used only by tests/, by
+// __graft_entry__.smoke() and by bench.py's CPU baseline leg, always as the
+// checker or the timed CPU baseline, never as the product path.
+//
+// Parity pinning: the reference CUDA extension cannot be built or run here
+// (its tiny-cuda-nn submodule is empty and slangc is absent), and the
+// reference has no tests or golden vectors for this path.  The restatement is
+// therefore pinned by analytic known-answer tests in tests/test_oracle_kat.py
+// (on-axis Gaussian, equidistant projection identities, ...), and by the
+// finite-difference gradient checks of tests/test_oracle_gradcheck.py.
+//
+// Floating-point contract (shared with the sm_100a kernels): IEEE single
+// precision, no implicit contraction (-ffp-contract=off), fmaf only where
+// written, transcendental functions from gf_elementary.h.
+//
+// Each function cites the reference file:line it restates.
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include <atomic>
+#include <cstdlib>
+#include <thread>
+
+#include "../gofish_b200/csrc/gf_elementary.h"
+
+using gf::fmaf_rn;
+
+namespace {
+
+// threedgut_tracer/configs/render/3dgut.yaml + include/3dgut/threedgut.cuh:41-68
+constexpr float kAlphaThreshold = 0.00392156862745098f;   // particle_kernel_min_alpha
+constexpr float kMinKernelResponse = 0.0113f;             // particle_kernel_min_response
+constexpr float kMaxAlpha = 0.99f;                         // particle_kernel_max_alpha
+constexpr float kMinTransmittance = 0.0001f;               // min_transmittance
+constexpr float kCovarianceDilation = 0.3f;                // threedgut.cuh:58
+constexpr float kParticleMinSensorZ = 0.2f;                // sensorConstants.cuh:12
+constexpr float kMaxDepthValue = 3.4028235e+38f;           // threedgut.cuh:64
+constexpr float kUtDelta = 1.7320508075688772f;            // sqrt(alpha^2 (D + kappa)), setup_3dgut.py:178
+constexpr float kUtImageMargin = 0.1f;                     // ut_in_image_margin_factor
+constexpr float kUtWeightI = 1.0f / 6.0f;                  // gutProjector.cuh:433 1/(2(D+lambda)), lambda = 0
+constexpr float kUtWeight0 = 2.0f;                         // gutProjector.cuh:502 lambda/(D+lambda) + (1-a^2+b)
+constexpr float kAabbHalfExtent = 1e06f;                   // splatRaster.cpp:345
+constexpr int kTile = 16;                                  // gutRendererParameters.h:21-22
+constexpr uint32_t kInvalidParticle = 0xffffffffu;
+
+struct float2_ { float x, y; };
+struct float3_ { float x, y, z; };
+
+inline float3_ f3(float x, float y, float z) { return {x, y, z}; }
+inline float3_ add(float3_ a, float3_ b) { return {a.x + b.x, a.y + b.y, a.z + b.z}; }
+inline float3_ sub(float3_ a, float3_ b) { return {a.x - b.x, a.y - b.y, a.z - b.z}; }
+inline float3_ scale(float s, float3_ a) { return {s * a.x, s * a.y, s * a.z}; }
+inline float dot(float3_ a, float3_ b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+// M (row-major 3x3) times v, each row summed left to right.
+inline float3_ matvec(const float* m, float3_ v) {
+    return {m[0] * v.x + m[1] * v.y + m[2] * v.z,
+            m[3] * v.x + m[4] * v.y + m[5] * v.z,
+            m[6] * v.x + m[7] * v.y + m[8] * v.z};
+}
+// Fused dot product used by the ray-particle hit test: fma(a.z,b.z,fma(a.y,b.y,a.x*b.x)).
+inline float fdot(float3_ a, float3_ b) { return fmaf_rn(a.z, b.z, fmaf_rn(a.y, b.y, a.x * b.x)); }
+inline float3_ fmatvec(const float* m, float3_ v) {
+    return {fdot(f3(m[0], m[1], m[2]), v), fdot(f3(m[3], m[4], m[5]), v), fdot(f3(m[6], m[7], m[8]), v)};
+}
+
+// Saturating float -> int conversion toward zero (NaN -> 0), the semantics of
+// the GPU's cvt.rzi.s32.f32 that the reference's static_cast<int> compiles to.
+inline int f2i_sat(float f) {
+    if (f != f) return 0;
+    if (f >= 2147483648.0f) return 2147483647;
+    if (f <= -2147483648.0f) return (-2147483647 - 1);
+    return int(f);
+}
+inline float saturate(float x) {  // __saturatef: clamp to [0,1], NaN -> 0
+    if (!(x > 0.0f)) return 0.0f;
+    return x < 1.0f ? x : 1.0f;
+}
+
+
+// Worker count: ORACLE_THREADS, else every host core.
+int worker_count() {
+    const char* env = std::getenv("ORACLE_THREADS");
+    if (env != nullptr && std::atoi(env) > 0) return std::atoi(env);
+    const unsigned n = std::thread::hardware_concurrency();
+    return n == 0 ? 1 : int(n);
+}
+
+// Dynamic parallel loop over [begin, end) in chunks; fn(i, worker).
+template <typename Fn>
+void parallel_for(int begin, int end, int chunk, Fn&& fn) {
+    const int workers = worker_count();
+    std::atomic<int> next(begin);
+    auto body = [&](int worker) {
+        for (;;) {
+            const int b = next.fetch_add(chunk);
+            if (b >= end) break;
+            const int e = std::min(end, b + chunk);
+            for (int i = b; i < e; ++i) fn(i, worker);
+        }
+    };
+    if (workers <= 1 || end - begin <= chunk) {
+        body(0);
+        return;
+    }
+    std::vector<std::thread> pool;
+    for (int w = 1; w < workers; ++w) pool.emplace_back(body, w);
+    body(0);
+    for (auto& t : pool) t.join();
+}
+}  // namespace
+
+extern "C" {
+
+// Camera model parameters: threedgut_tracer/include/3dgut/sensors/cameraModels.h
+// (OpenCVPinholeProjectionParameters / OpenCVFisheyeProjectionParameters).
+struct OracleCamera {
+    int32_t model;   // 0 = OpenCV pinhole, 1 = OpenCV fisheye (Kannala-Brandt)
+    int32_t width;
+    int32_t height;
+    int32_t pad0;
+    float principal[2];
+    float focal[2];
+    float radial[6];
+    float tangential[2];
+    float thin_prism[4];
+    float max_angle;
+    float pad1;
+};
+
+// Prepared global-shutter pose: world->sensor rotation R (row-major) and
+// translation t, its inverse rotation Rinv = R^T and the sensor centre c.
+struct OraclePose {
+    float R[9];
+    float t[3];
+    float Rinv[9];
+    float c[3];
+};
+
+// Prepare an OraclePose from the reference's 7-float world->sensor pose
+// [tx, ty, tz, qx, qy, qz, qw] (tracer.py:466-474, sensors.h:44-73).  Done in
+// double and rounded once, so the product and the oracle see the same floats.
+void oracle_prepare_pose(const float* pose7, OraclePose* out) {
+    const double tx = pose7[0], ty = pose7[1], tz = pose7[2];
+    const double x = pose7[3], y = pose7[4], z = pose7[5], w = pose7[6];
+    double R[9];
+    R[0] = 1.0 - 2.0 * (y * y + z * z);
+    R[1] = 2.0 * (x * y - w * z);
+    R[2] = 2.0 * (x * z + w * y);
+    R[3] = 2.0 * (x * y + w * z);
+    R[4] = 1.0 - 2.0 * (x * x + z * z);
+    R[5] = 2.0 * (y * z - w * x);
+    R[6] = 2.0 * (x * z - w * y);
+    R[7] = 2.0 * (y * z + w * x);
+    R[8] = 1.0 - 2.0 * (x * x + y * y);
+    for (int i = 0; i < 9; ++i) out->R[i] = float(R[i]);
+    out->t[0] = float(tx);
+    out->t[1] = float(ty);
+    out->t[2] = float(tz);
+    for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < 3; ++c) out->Rinv[3 * r + c] = out->R[3 * c + r];
+    // c = -R^T t
+    for (int r = 0; r < 3; ++r) {
+        const double v = -(R[0 * 3 + r] * tx + R[1 * 3 + r] * ty + R[2 * 3 + r] * tz);
+        out->c[r] = float(v);
+    }
+}
+
+}  // extern "C"
+
+namespace {
+
+// cameraProjections.cuh:26-37
+float stable_norm2(float x, float y) {
+    const float ax = gf::abs_f(x), ay = gf::abs_f(y);
+    const float mn = gf::min_f(ax, ay), mx = gf::max_f(ax, ay);
+    if (mx <= 0.0f) return 0.0f;
+    const float r = mn / mx;
+    return mx * sqrtf(1.0f + r * r);
+}
+
+// cameraProjections.cuh:86-122 (OpenCV pinhole), requireRasterBounds = false.
+bool project_pinhole(const OracleCamera& cam, float3_ p, float2_& out) {
+    if (p.z <= 0.0f) {
+        out = {0.0f, 0.0f};
+        return false;
+    }
+    const float u = p.x / p.z, v = p.y / p.z;
+    const float uu = u * u, vv = v * v;
+    const float r2 = uu + vv;
+    const float a1 = 2.0f * u * v;
+    const float a2 = r2 + 2.0f * uu;
+    const float a3 = r2 + 2.0f * vv;
+    const float* k = cam.radial;
+    const float num = 1.0f + r2 * (k[0] + r2 * (k[1] + r2 * k[2]));
+    const float den = 1.0f + r2 * (k[3] + r2 * (k[4] + r2 * k[5]));
+    const float icD = num / den;
+    const float* tg = cam.tangential;
+    const float* tp = cam.thin_prism;
+    const float dx = tg[0] * a1 + tg[1] * a2 + r2 * (tp[0] + r2 * tp[1]);
+    const float dy = tg[0] * a3 + tg[1] * a1 + r2 * (tp[2] + r2 * tp[3]);
+    const float ux = icD * u + dx, uy = icD * v + dy;
+    const bool validRadial = icD > 0.8f && icD < 1.2f;
+    if (validRadial) {
+        out = {ux * cam.focal[0] + cam.principal[0], uy * cam.focal[1] + cam.principal[1]};
+    } else {
+        const float clip = float(std::hypot(double(cam.width), double(cam.height)));
+        const float s = clip / sqrtf(r2);
+        out = {s * u + cam.principal[0], s * v + cam.principal[1]};
+    }
+    return validRadial && gf::isfinite_f(out.x) && gf::isfinite_f(out.y);
+}
+
+// cameraProjections.cuh:124-152 (OpenCV fisheye / Kannala-Brandt), requireRasterBounds = false.
+bool project_fisheye(const OracleCamera& cam, float3_ p, float2_& out) {
+    float rho = stable_norm2(p.x, p.y);
+    if (rho <= 0.0f) rho = FLT_EPSILON;
+    const float thetaFull = gf::gf_atan2f(rho, p.z);
+    const float theta = gf::min_f(thetaFull, cam.max_angle);
+    const float theta2 = theta * theta;
+    // evalPolyHorner<4>(k, theta2): y = k4; y = x*y + k3; ...
+    float poly = cam.radial[3];
+    poly = theta2 * poly + cam.radial[2];
+    poly = theta2 * poly + cam.radial[1];
+    poly = theta2 * poly + cam.radial[0];
+    const float delta = (theta * (poly * theta2 + 1.0f)) / rho;
+    out = {cam.focal[0] * p.x * delta + cam.principal[0], cam.focal[1] * p.y * delta + cam.principal[1]};
+    return theta < cam.max_angle && gf::isfinite_f(out.x) && gf::isfinite_f(out.y);
+}
+
+// cameraProjections.cuh:228-240, global shutter: R * p + t, then project.
+bool project_world(const OracleCamera& cam, const OraclePose& pose, float3_ pw, float2_& out) {
+    const float3_ ps = add(matvec(pose.R, pw), f3(pose.t[0], pose.t[1], pose.t[2]));
+    if (cam.model == 1) return project_fisheye(cam, ps, out);
+    return project_pinhole(cam, ps, out);
+}
+
+// Packed particle row accessors, tracer.py:171-179 / inference.py:43-47.
+struct Particle {
+    float3_ pos;
+    float density;
+    float B[9];     // factor, row-major (slots 12-20)
+    float Binv[9];  // inverse factor, row-major (slots 21-29)
+};
+inline Particle load_particle(const float* row) {
+    Particle p;
+    p.pos = f3(row[0], row[1], row[2]);
+    p.density = row[3];
+    for (int i = 0; i < 9; ++i) p.B[i] = row[12 + i];
+    for (int i = 0; i < 9; ++i) p.Binv[i] = row[21 + i];
+    return p;
+}
+
+struct Projection {
+    float2_ center;
+    float conic[3];
+    float opacity;
+    float2_ extent;
+    bool valid;
+};
+
+// gutProjector.cuh:359-518, unscentedParticleProjection (no partial UT).
+bool unscented_projection(const OracleCamera& cam, const OraclePose& pose, const Particle& P,
+                          float2_& center, float cov[3]) {
+    if (P.density < kAlphaThreshold) return false;  // :375-378
+    const bool fisheye = cam.model == 1;
+    if (fisheye) {
+        // :389-398 cameraNativeRadialNearAdmitted (cameraNativeRayAdmission.cuh:29-35)
+        const float3_ ray = sub(P.pos, f3(pose.c[0], pose.c[1], pose.c[2]));
+        const float r2 = dot(ray, ray);
+        const float near2 = kParticleMinSensorZ * kParticleMinSensorZ;
+        if (!(gf::isfinite_f(r2) && r2 >= near2)) return false;
+    } else {
+        // :399-405 pinhole near plane (z row of the world->sensor matrix)
+        const float z = P.pos.x * pose.R[6] + P.pos.y * pose.R[7] + P.pos.z * pose.R[8] + pose.t[2];
+        if (z < kParticleMinSensorZ) return false;
+    }
+    float2_ s[7];
+    int numValid = 0;
+    const bool c0 = project_world(cam, pose, P.pos, s[0]);  // :413-420
+    if (fisheye && !c0) return false;                         // :421-428
+    if (c0) numValid++;
+    center = {s[0].x * 0.0f, s[0].y * 0.0f};                 // lambda / (D + lambda) = 0
+    for (int i = 0; i < 3; ++i) {                             // :434-462
+        const float3_ col = f3(P.B[0 * 3 + i], P.B[1 * 3 + i], P.B[2 * 3 + i]);
+        const float3_ delta = scale(kUtDelta, col);
+        if (project_world(cam, pose, add(P.pos, delta), s[i + 1])) numValid++;
+        center.x = center.x + kUtWeightI * s[i + 1].x;
+        center.y = center.y + kUtWeightI * s[i + 1].y;
+        if (project_world(cam, pose, sub(P.pos, delta), s[i + 4])) numValid++;
+        center.x = center.x + kUtWeightI * s[i + 4].x;
+        center.y = center.y + kUtWeightI * s[i + 4].y;
+    }
+    if (numValid != 7) return false;  // :467-499 (partial UT off)
+    {
+        const float cx = s[0].x - center.x, cy = s[0].y - center.y;  // :501-506
+        cov[0] = kUtWeight0 * (cx * cx);
+        cov[1] = kUtWeight0 * (cx * cy);
+        cov[2] = kUtWeight0 * (cy * cy);
+    }
+    for (int i = 0; i < 6; ++i) {  // :507-513
+        const float cx = s[i + 1].x - center.x, cy = s[i + 1].y - center.y;
+        cov[0] = cov[0] + kUtWeightI * (cx * cx);
+        cov[1] = cov[1] + kUtWeightI * (cx * cy);
+        cov[2] = cov[2] + kUtWeightI * (cy * cy);
+    }
+    return true;
+}
+
+// gutProjector.cuh:249-288 computeProjectedExtentConicOpacity.
+bool conic_extent(const float cov[3], float opacity, Projection& out) {
+    const float dx = cov[0] + kCovarianceDilation, dy = cov[1], dz = cov[2] + kCovarianceDilation;
+    const float det = dx * dz - dy * dy;
+    if (det == 0.0f) return false;
+    out.conic[0] = dz / det;
+    out.conic[1] = -dy / det;
+    out.conic[2] = dx / det;
+    out.opacity = opacity;
+    if (opacity < kAlphaThreshold) return false;
+    const float maxPower = gf::gf_logf(opacity / kAlphaThreshold);
+    const float extentFactor = gf::min_f(3.33f, sqrtf(2.0f * maxPower));
+    const float mid = 0.5f * (dx + dz);
+    const float lambda = mid + sqrtf(gf::max_f(0.01f, mid * mid - det));
+    const float radius = extentFactor * sqrtf(lambda);
+    out.extent = {gf::min_f(extentFactor * sqrtf(dx), radius), gf::min_f(extentFactor * sqrtf(dz), radius)};
+    return radius > 0.0f;
+}
+
+// gutProjector.cuh:85-96 computeTileSpaceBBox.
+void tile_bbox(int gx, int gy, float2_ c, float2_ e, int& x0, int& y0, int& x1, int& y1) {
+    auto clampg = [](int v, int g) { return std::min(g, std::max(0, v)); };
+    x0 = clampg(f2i_sat(floorf(((c.x - 0.5f) - e.x) / 16.0f)), gx);
+    y0 = clampg(f2i_sat(floorf(((c.y - 0.5f) - e.y) / 16.0f)), gy);
+    x1 = clampg(f2i_sat(ceilf(((c.x - 0.5f) + e.x) / 16.0f)), gx);
+    y1 = clampg(f2i_sat(ceilf(((c.y - 0.5f) + e.y) / 16.0f)), gy);
+}
+
+// gutProjector.cuh:217-246 tileMinParticlePowerResponse.
+float tile_min_power(int tx, int ty, const float conic[3], float2_ m) {
+    const float tminx = 16.0f * float(tx), tminy = 16.0f * float(ty);
+    const float tmaxx = 16.0f + tminx, tmaxy = 16.0f + tminy;
+    const float ox = tminx - m.x, oy = tminy - m.y;
+    const float lax = ox > 0.0f ? 1.0f : 0.0f, lay = oy > 0.0f ? 1.0f : 0.0f;
+    const float nirx = lax + (m.x > tmaxx ? 1.0f : 0.0f);
+    const float niry = lay + (m.y > tmaxy ? 1.0f : 0.0f);
+    if ((nirx + niry) > 0.0f) {
+        const float px = lax != 0.0f ? tminx : tmaxx;
+        const float py = lay != 0.0f ? tminy : tmaxy;
+        const float dxy_x = gf::copysign_f(16.0f, ox), dxy_y = gf::copysign_f(16.0f, oy);
+        const float diffx = m.x - px, diffy = m.y - py;
+        const float rcpx = 1.0f / (256.0f * conic[0]);
+        const float rcpy = 1.0f / (256.0f * conic[2]);
+        const float tx_ = niry * saturate((dxy_x * conic[0] * diffx + dxy_x * conic[1] * diffy) * rcpx);
+        const float ty_ = nirx * saturate((dxy_y * conic[1] * diffx + dxy_y * conic[2] * diffy) * rcpy);
+        const float mx = m.x - (px + tx_ * dxy_x), my = m.y - (py + ty_ * dxy_y);
+        return 0.5f * (conic[0] * mx * mx + conic[2] * my * my) + conic[1] * mx * my;
+    }
+    return 0.0f;
+}
+
+inline bool fast_ut_valid(const Projection& p) {  // gutProjector.cuh:181-184
+    return p.extent.x > 1e-06f && p.opacity >= kAlphaThreshold;
+}
+
+// gutProjector.cuh:186-210 fastAdmittedTiles (scale s = 1), y-major visit order.
+template <typename Visit>
+uint32_t admitted_tiles(int gx, int gy, const uint8_t* mask, const Projection& p, Visit&& visit) {
+    if (!fast_ut_valid(p)) return 0u;
+    int x0, y0, x1, y1;
+    tile_bbox(gx, gy, p.center, p.extent, x0, y0, x1, y1);
+    const float maxPower = gf::gf_logf(p.opacity / kAlphaThreshold) * 1.0f;
+    uint32_t n = 0;
+    for (int y = y0; y < y1; ++y) {
+        for (int x = x0; x < x1; ++x) {
+            if (mask[y * gx + x] == 0u) continue;
+            if (!(tile_min_power(x, y, p.conic, p.center) < maxPower)) continue;
+            visit(x, y);
+            ++n;
+        }
+    }
+    return n;
+}
+
+// SH radiance, gaussianParticles.cuh:181-219 / sphericalHarmonics.slang decode.
+constexpr float SH_C0 = 0.28209479177387814f;
+constexpr float SH_C1 = 0.4886025119029199f;
+constexpr float SH_C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f, -1.0925484305920792f,
+                            0.5462742152960396f};
+constexpr float SH_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f, 0.3731763325901154f,
+                            -0.4570457994644658f, 1.445305721320277f, -0.5900435899266435f};
+
+void sh_basis(int deg, float3_ d, float b[16]) {
+    for (int i = 0; i < 16; ++i) b[i] = 0.0f;
+    b[0] = SH_C0;
+    if (deg > 0) {
+        const float x = d.x, y = d.y, z = d.z;
+        b[1] = -SH_C1 * y;
+        b[2] = SH_C1 * z;
+        b[3] = -SH_C1 * x;
+        if (deg > 1) {
+            const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, yz = y * z, xz = x * z;
+            b[4] = SH_C2[0] * xy;
+            b[5] = SH_C2[1] * yz;
+            b[6] = SH_C2[2] * (2.0f * zz - xx - yy);
+            b[7] = SH_C2[3] * xz;
+            b[8] = SH_C2[4] * (xx - yy);
+            if (deg > 2) {
+                b[9] = SH_C3[0] * y * (3.0f * xx - yy);
+                b[10] = SH_C3[1] * xy * z;
+                b[11] = SH_C3[2] * y * (4.0f * zz - xx - yy);
+                b[12] = SH_C3[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+                b[13] = SH_C3[4] * x * (4.0f * zz - xx - yy);
+                b[14] = SH_C3[5] * z * (xx - yy);
+                b[15] = SH_C3[6] * x * (xx - 3.0f * yy);
+            }
+        }
+    }
+}
+
+// d(basis_k)/d(dir) for k < 16, as three rows (x, y, z).
+void sh_basis_grad(int deg, float3_ d, float gx[16], float gy[16], float gz[16]) {
+    for (int i = 0; i < 16; ++i) gx[i] = gy[i] = gz[i] = 0.0f;
+    if (deg < 1) return;
+    const float x = d.x, y = d.y, z = d.z;
+    gy[1] = -SH_C1;
+    gz[2] = SH_C1;
+    gx[3] = -SH_C1;
+    if (deg < 2) return;
+    gx[4] = SH_C2[0] * y; gy[4] = SH_C2[0] * x;
+    gy[5] = SH_C2[1] * z; gz[5] = SH_C2[1] * y;
+    gx[6] = SH_C2[2] * (-2.0f * x); gy[6] = SH_C2[2] * (-2.0f * y); gz[6] = SH_C2[2] * (4.0f * z);
+    gx[7] = SH_C2[3] * z; gz[7] = SH_C2[3] * x;
+    gx[8] = SH_C2[4] * (2.0f * x); gy[8] = SH_C2[4] * (-2.0f * y);
+    if (deg < 3) return;
+    const float xx = x * x, yy = y * y, zz = z * z;
+    gx[9] = SH_C3[0] * (6.0f * x * y); gy[9] = SH_C3[0] * (3.0f * xx - 3.0f * yy);
+    gx[10] = SH_C3[1] * (y * z); gy[10] = SH_C3[1] * (x * z); gz[10] = SH_C3[1] * (x * y);
+    gx[11] = SH_C3[2] * (-2.0f * x * y); gy[11] = SH_C3[2] * (4.0f * zz - xx - 3.0f * yy); gz[11] = SH_C3[2] * (8.0f * y * z);
+    gx[12] = SH_C3[3] * (-6.0f * x * z); gy[12] = SH_C3[3] * (-6.0f * y * z); gz[12] = SH_C3[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+    gx[13] = SH_C3[4] * (4.0f * zz - 3.0f * xx - yy); gy[13] = SH_C3[4] * (-2.0f * x * y); gz[13] = SH_C3[4] * (8.0f * x * z);
+    gx[14] = SH_C3[5] * (2.0f * x * z); gy[14] = SH_C3[5] * (-2.0f * y * z); gz[14] = SH_C3[5] * (xx - yy);
+    gx[15] = SH_C3[6] * (3.0f * xx - 3.0f * yy); gy[15] = SH_C3[6] * (-6.0f * x * y);
+}
+
+// Incident direction of the SH evaluation: (mu - camera) / |mu - camera|
+// (gutProjector.cuh:239-245, :551).
+float3_ incident_direction(const float3_& mu, const OraclePose& pose, float& dist) {
+    const float3_ v = sub(mu, f3(pose.c[0], pose.c[1], pose.c[2]));
+    dist = sqrtf(dot(v, v));
+    return {v.x / dist, v.y / dist, v.z / dist};
+}
+
+// ------------------------------------------------------------------ render
+struct Ray {
+    float3_ o, d;
+    float tmin, tmax;
+    bool valid;
+};
+
+// bounding_box.h:89-133 ray_intersect against the +-1e6 box; rayPayload.cuh:113-162.
+Ray make_ray(const OraclePose& pose, const float* ro, const float* rd) {
+    Ray r;
+    const float3_ os = f3(ro[0], ro[1], ro[2]);
+    const float3_ ds = f3(rd[0], rd[1], rd[2]);
+    r.o = add(matvec(pose.Rinv, os), f3(pose.c[0], pose.c[1], pose.c[2]));
+    r.d = matvec(pose.Rinv, ds);
+    const float lo = -kAabbHalfExtent, hi = kAabbHalfExtent;
+    float tmin = (lo - r.o.x) / r.d.x, tmax = (hi - r.o.x) / r.d.x;
+    if (tmin > tmax) std::swap(tmin, tmax);
+    float tymin = (lo - r.o.y) / r.d.y, tymax = (hi - r.o.y) / r.d.y;
+    if (tymin > tymax) std::swap(tymin, tymax);
+    if (tmin > tymax || tymin > tmax) {
+        tmin = FLT_MAX;
+        tmax = FLT_MAX;
+    } else {
+        if (tymin > tmin) tmin = tymin;
+        if (tymax < tmax) tmax = tymax;
+        float tzmin = (lo - r.o.z) / r.d.z, tzmax = (hi - r.o.z) / r.d.z;
+        if (tzmin > tzmax) std::swap(tzmin, tzmax);
+        if (tmin > tzmax || tzmin > tmax) {
+            tmin = FLT_MAX;
+            tmax = FLT_MAX;
+        } else {
+            if (tzmin > tmin) tmin = tzmin;
+            if (tzmax < tmax) tmax = tzmax;
+        }
+    }
+    r.tmin = gf::max_f(tmin, 0.0f);
+    r.tmax = tmax;
+    r.valid = r.tmax > r.tmin;
+    return r;
+}
+
+struct HalfRay {
+    float3_ gro, grdu, p;
+    float denom, num, tauLine, tau;
+    bool interior, valid;
+};
+
+// gaussianParticles.slang:293-325 hitInterval == gutHalfRayResponse.cuh:17-37
+// (fused dot products, see the file header).
+HalfRay half_ray(const Ray& r, const Particle& P) {
+    HalfRay h;
+    const float3_ gposc = sub(r.o, P.pos);
+    h.gro = fmatvec(P.Binv, gposc);
+    h.grdu = fmatvec(P.Binv, r.d);
+    h.denom = fdot(h.grdu, h.grdu);
+    h.valid = h.denom > 0.0f && gf::isfinite_f(h.denom) && gf::isfinite_f(r.tmin) && r.tmax > r.tmin;
+    if (!h.valid) {
+        h.num = 0.0f;
+        h.tauLine = 0.0f;
+        h.tau = 0.0f;
+        h.p = h.gro;
+        h.interior = false;
+        return h;
+    }
+    h.num = fdot(h.gro, h.grdu);
+    h.tauLine = -h.num / h.denom;
+    h.tau = gf::min_f(gf::max_f(h.tauLine, r.tmin), r.tmax);
+    h.interior = h.tauLine > r.tmin && h.tauLine < r.tmax;
+    h.p = f3(fmaf_rn(h.tau, h.grdu.x, h.gro.x), fmaf_rn(h.tau, h.grdu.y, h.gro.y), fmaf_rn(h.tau, h.grdu.z, h.gro.z));
+    return h;
+}
+
+struct Hit {
+    uint32_t idx;
+    float hitT;
+    float alpha;
+};
+
+// gaussianParticles.slang:309-338 hit acceptance; returns response.
+bool hit_test(const Ray& r, const Particle& P, float& alpha, float& hitT, float& resp, HalfRay& h) {
+    h = half_ray(r, P);
+    if (!h.valid) return false;
+    const float g = fdot(h.p, h.p);
+    resp = gf::gf_expf(-0.5f * g);
+    alpha = gf::min_f(kMaxAlpha, resp * P.density);
+    hitT = h.tau;
+    return resp > kMinKernelResponse && alpha > kAlphaThreshold;
+}
+
+struct PixelState {
+    float T;
+    float rgb[3];
+    float hitT;
+    uint32_t hitN;
+    bool alive;
+};
+
+// Front-to-back composite of one hit (gutKBufferRenderer.cuh:307-416).
+void composite(PixelState& s, const Hit& h, const float* rgb) {
+    const float w = h.alpha * s.T;
+    s.hitT = s.hitT + h.hitT * w;
+    s.T = s.T * (1.0f - h.alpha);
+    if (w > 0.0f) {
+        const float* c = rgb + 3 * size_t(h.idx);
+        for (int k = 0; k < 3; ++k) s.rgb[k] = fmaf_rn(gf::max_f(c[k], 0.0f), w, s.rgb[k]);
+        s.hitN++;
+    }
+    if (s.T < kMinTransmittance) s.alive = false;
+}
+
+// HitParticleKBufferT (gutKBufferRenderer.cuh:120-166).
+struct KBuffer {
+    int K;
+    uint32_t n;
+    Hit e[64];
+    void init(int k) {
+        K = k;
+        n = 0;
+        for (int i = 0; i < k; ++i) e[i] = {kInvalidParticle, -1.0f, 0.0f};
+    }
+    bool full() const { return K == 0 || n == uint32_t(K); }
+    void insert(Hit h) {
+        if (K == 0) return;
+        if (full()) {
+            e[0].hitT = -1.0f;
+        } else {
+            n++;
+        }
+        for (int i = K - 1; i >= 0; --i) {
+            if (h.hitT > e[i].hitT) std::swap(e[i], h);
+        }
+    }
+};
+
+struct Scene {
+    const OracleCamera* cam;
+    const OraclePose* pose;
+    int N;
+    const float* particles;
+    const float* rgb;
+    const float* rayO;
+    const float* rayD;
+    const uint8_t* mask;
+    const uint32_t* ranges;
+    const uint32_t* sortedIds;
+    int K;
+};
+
+// Walk one pixel's tile list in the order of gutKBufferRenderer.cuh:614-700,
+// calling `hitFn(Hit, state)` for each composited hit.
+template <typename HitFn>
+void traverse(const Scene& sc, uint32_t tile, const Ray& ray, bool& alive, HitFn&& hitFn) {
+    const uint32_t b = sc.ranges[2 * tile], e = sc.ranges[2 * tile + 1];
+    KBuffer kb;
+    kb.init(sc.K);
+    for (uint32_t s = b; s < e && alive; ++s) {
+        const uint32_t idx = sc.sortedIds[s];
+        if (idx == kInvalidParticle) break;
+        const Particle P = load_particle(sc.particles + 32 * size_t(idx));
+        Hit h;
+        h.idx = idx;
+        float resp;
+        HalfRay hr;
+        if (hit_test(ray, P, h.alpha, h.hitT, resp, hr) && h.hitT >= ray.tmin && h.hitT <= ray.tmax) {
+            if (kb.full()) hitFn(sc.K == 0 ? h : kb.e[0]);
+            kb.insert(h);
+        }
+    }
+    if (sc.K > 0) {
+        for (uint32_t i = 0; alive && i < kb.n; ++i) hitFn(kb.e[sc.K - kb.n + i]);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+// Per-particle projected state, gutProjector.cuh:653-286 (projectOnTiles, fast UT
+// admission).  proj[N*8] = center.xy, conic.xyz, opacity, extent.xy (zero when
+// the projection is invalid); rgb[N*3] precomputed radiance; counts[N].
+int oracle_project(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                   const float* sh, int shCoeffs, int shDegree, const uint8_t* mask, float* proj, float* rgb,
+                   uint32_t* counts) {
+    const int gx = (cam->width + kTile - 1) / kTile, gy = (cam->height + kTile - 1) / kTile;
+    parallel_for(0, N, 1024, [&](int i, int) {
+        const Particle P = load_particle(particles + 32 * size_t(i));
+        float2_ center{0.0f, 0.0f};
+        float cov[3] = {0.0f, 0.0f, 0.0f};
+        Projection pr{};
+        bool valid = unscented_projection(*cam, *pose, P, center, cov);
+        if (valid) {
+            pr.center = center;
+            valid = conic_extent(cov, P.density, pr);
+        }
+        if (!valid) pr = Projection{};
+        pr.valid = valid;
+        float* o = proj + 8 * size_t(i);
+        o[0] = pr.center.x; o[1] = pr.center.y;
+        o[2] = pr.conic[0]; o[3] = pr.conic[1]; o[4] = pr.conic[2];
+        o[5] = pr.opacity;
+        o[6] = pr.extent.x; o[7] = pr.extent.y;
+        // SH radiance at the incident direction (gutProjector.cuh:239-245).
+        float dist;
+        const float3_ dir = incident_direction(P.pos, *pose, dist);
+        float basis[16];
+        sh_basis(shDegree, dir, basis);
+        const float* c = sh + size_t(i) * 3 * shCoeffs;
+        const int nb = shDegree >= 3 ? 16 : (shDegree == 2 ? 9 : (shDegree == 1 ? 4 : 1));
+        for (int ch = 0; ch < 3; ++ch) {
+            float acc = basis[0] * c[ch];
+            for (int k = 1; k < nb && k < shCoeffs; ++k) acc = fmaf_rn(basis[k], c[3 * k + ch], acc);
+            const float v = acc + 0.5f;
+            rgb[3 * size_t(i) + ch] = gf::max_f(v, 0.0f);
+        }
+        counts[i] = admitted_tiles(gx, gy, mask, pr, [](int, int) {});
+    });
+    return 0;
+}
+
+// Per-tile central rays for the per-tile depth key (gutProjector.cuh:364-417):
+// tileRays[T*8] = world origin.xyz, flag, world direction.xyz, pad.  flag = 1
+// when the direction is usable, 0 when the key must use the radial fallback.
+int oracle_tile_rays(const OracleCamera* cam, const OraclePose* pose, const float* rayO, const float* rayD,
+                     float* tileRays) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
+    for (int ty = 0; ty < gy; ++ty) {
+        for (int tx = 0; tx < gx; ++tx) {
+            const int xb = tx * kTile, yb = ty * kTile;
+            const int xe = std::min(W - 1, (tx + 1) * kTile - 1), ye = std::min(H - 1, (ty + 1) * kTile - 1);
+            const int xlo = (xb + xe) / 2, xhi = (xb + xe + 1) / 2, ylo = (yb + ye) / 2, yhi = (yb + ye + 1) / 2;
+            const size_t p[4] = {size_t(xlo) + size_t(W) * ylo, size_t(xhi) + size_t(W) * ylo,
+                                 size_t(xlo) + size_t(W) * yhi, size_t(xhi) + size_t(W) * yhi};
+            float3_ so = f3(0, 0, 0), sd = f3(0, 0, 0);
+            for (int k = 0; k < 4; ++k) {
+                so = add(so, f3(rayO[3 * p[k]], rayO[3 * p[k] + 1], rayO[3 * p[k] + 2]));
+                sd = add(sd, f3(rayD[3 * p[k]], rayD[3 * p[k] + 1], rayD[3 * p[k] + 2]));
+            }
+            so = scale(0.25f, so);
+            sd = scale(0.25f, sd);
+            const float3_ wo = add(matvec(pose->Rinv, so), f3(pose->c[0], pose->c[1], pose->c[2]));
+            float* out = tileRays + 8 * size_t(ty * gx + tx);
+            out[0] = wo.x; out[1] = wo.y; out[2] = wo.z;
+            out[3] = 0.0f;
+            out[4] = out[5] = out[6] = out[7] = 0.0f;
+            const float n2 = dot(sd, sd);
+            if (!(n2 > 0.0f) || !gf::isfinite_f(n2)) continue;
+            sd = scale(1.0f / sqrtf(n2), sd);
+            float3_ wd = matvec(pose->Rinv, sd);
+            const float m2 = dot(wd, wd);
+            if (!(m2 > 0.0f) || !gf::isfinite_f(m2)) continue;
+            wd = scale(1.0f / sqrtf(m2), wd);
+            out[3] = 1.0f;
+            out[4] = wd.x; out[5] = wd.y; out[6] = wd.z;
+        }
+    }
+    return 0;
+}
+
+}  // extern "C"
+
+namespace {
+
+// sofDepthFallback.cuh:13-17
+inline float finite_nonneg(float v, float fallbackMax) {
+    if (gf::isfinite_f(v) && v >= 0.0f) return v;
+    return (gf::isfinite_f(fallbackMax) && fallbackMax >= 0.0f) ? fallbackMax : 0.0f;
+}
+
+// Sort key depth of one (particle, tile), gutProjector.cuh:354-417 and
+// sofMaximumResponseDepth.cuh:19-45.  keyMode 0 = per-tile maximum-response
+// depth (training/exact key), 1 = global camera radial distance (real-time key).
+uint32_t depth_key(int keyMode, const Particle& P, const OraclePose& pose, const float* tileRay) {
+    const float3_ cam = f3(pose.c[0], pose.c[1], pose.c[2]);
+    const float3_ v = sub(P.pos, cam);
+    const float camRadial = finite_nonneg(sqrtf(dot(v, v)), kMaxDepthValue);
+    if (keyMode == 1) return gf::f2u(camRadial);
+    const float3_ wo = f3(tileRay[0], tileRay[1], tileRay[2]);
+    const float3_ u = sub(P.pos, wo);
+    const float tileRadial = finite_nonneg(sqrtf(dot(u, u)), camRadial);
+    if (tileRay[3] == 0.0f) return gf::f2u(finite_nonneg(tileRadial, camRadial));
+    const float3_ wd = f3(tileRay[4], tileRay[5], tileRay[6]);
+    const float3_ lo = sub(wo, P.pos);
+    const float3_ co = matvec(P.Binv, lo);
+    const float3_ cd = matvec(P.Binv, wd);
+    const float den = dot(cd, cd);
+    if (!(den > 0.0f) || !gf::isfinite_f(den)) return gf::f2u(finite_nonneg(tileRadial, 0.0f));
+    const float t = -dot(co, cd) / den;
+    if (!gf::isfinite_f(t)) return gf::f2u(finite_nonneg(tileRadial, 0.0f));
+    return gf::f2u(gf::max_f(0.0f, t));
+}
+
+}  // namespace
+
+extern "C" {
+
+// Emit (tile << 32 | depth) keys and particle ids in particle order, then a
+// stable sort and the per-tile ranges (gutProjector.cuh:947-1113 expand,
+// gutRenderer.cu:114-144 computeSortedTileRangeIndices, :1527-1539 CUB
+// stable radix sort).  Returns the number of intersections, or -1 when
+// `capacity` is too small (keys/ids are then untouched).
+int64_t oracle_bin(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                   const float* proj, const uint32_t* counts, const uint8_t* mask, const float* tileRays,
+                   int keyMode, uint64_t* keys, uint32_t* ids, int64_t capacity, uint32_t* ranges) {
+    const int gx = (cam->width + kTile - 1) / kTile, gy = (cam->height + kTile - 1) / kTile;
+    std::vector<uint64_t> offsets(static_cast<size_t>(N) + 1, 0);
+    for (int i = 0; i < N; ++i) offsets[i + 1] = offsets[i] + counts[i];
+    const int64_t total = int64_t(offsets[N]);
+    if (total > capacity) return -1;
+    parallel_for(0, N, 1024, [&](int i, int) {
+        const Particle P = load_particle(particles + 32 * size_t(i));
+        const float* o = proj + 8 * size_t(i);
+        Projection pr{};
+        pr.center = {o[0], o[1]};
+        pr.conic[0] = o[2]; pr.conic[1] = o[3]; pr.conic[2] = o[4];
+        pr.opacity = o[5];
+        pr.extent = {o[6], o[7]};
+        uint64_t k = offsets[i];
+        const uint64_t end = offsets[i + 1];
+        admitted_tiles(gx, gy, mask, pr, [&](int x, int y) {
+            if (k < end) {
+                const uint32_t tile = uint32_t(y * gx + x);
+                keys[k] = (uint64_t(tile) << 32) | depth_key(keyMode, P, *pose, tileRays + 8 * size_t(tile));
+                ids[k] = uint32_t(i);
+            }
+            ++k;
+        });
+    });
+    // Stable sort of (key, id) pairs by key.
+    std::vector<uint64_t> order(static_cast<size_t>(total));
+    for (int64_t i = 0; i < total; ++i) order[i] = uint64_t(i);
+    std::stable_sort(order.begin(), order.end(), [&](uint64_t a, uint64_t b) { return keys[a] < keys[b]; });
+    std::vector<uint64_t> k2(static_cast<size_t>(total));
+    std::vector<uint32_t> i2(static_cast<size_t>(total));
+    for (int64_t i = 0; i < total; ++i) {
+        k2[i] = keys[order[i]];
+        i2[i] = ids[order[i]];
+    }
+    std::memcpy(keys, k2.data(), sizeof(uint64_t) * size_t(total));
+    std::memcpy(ids, i2.data(), sizeof(uint32_t) * size_t(total));
+    const int T = gx * gy;
+    std::memset(ranges, 0, sizeof(uint32_t) * 2 * size_t(T));
+    for (int64_t i = 0; i < total; ++i) {
+        const uint32_t tile = uint32_t(keys[i] >> 32);
+        if (i == 0 || uint32_t(keys[i - 1] >> 32) != tile) ranges[2 * tile] = uint32_t(i);
+        if (i == total - 1 || uint32_t(keys[i + 1] >> 32) != tile) ranges[2 * tile + 1] = uint32_t(i + 1);
+    }
+    return total;
+}
+
+// Per-pixel forward composite over tiles [tileBegin, tileEnd) (render kernel,
+// gutRenderer.cuh:217-265; finalizeRay, rayPayload.cuh:242-322).  Outputs keep
+// their initial values (rgba 0, hitT 1e6, count 0) outside retained tiles
+// and for invalid rays; the caller initializes them.
+int oracle_render_forward(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                          const float* rgb, const float* rayO, const float* rayD, const uint8_t* mask,
+                          const uint32_t* ranges, const uint32_t* sortedIds, int K, int tileBegin, int tileEnd,
+                          float* rgba, float* hitT, float* hitCount) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile;
+    Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
+    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int) {
+        if (mask[tile] == 0u) return;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                PixelState s{1.0f, {0.0f, 0.0f, 0.0f}, 0.0f, 0u, true};
+                traverse(sc, uint32_t(tile), ray, s.alive, [&](const Hit& h) { composite(s, h, rgb); });
+                rgba[4 * pix + 0] = s.rgb[0];
+                rgba[4 * pix + 1] = s.rgb[1];
+                rgba[4 * pix + 2] = s.rgb[2];
+                rgba[4 * pix + 3] = 1.0f - s.T;
+                hitT[pix] = s.hitT;
+                hitCount[pix] = float(s.hitN);
+            }
+        }
+    });
+    return 0;
+}
+
+// Per-pixel backward replay (renderBackward, gutRenderer.cuh:555-626;
+// processHitBwd, gaussianParticles.cuh:736-1155, with the geometric channels
+// inactive).  Accumulates into gradRecord[N*16]: position.xyz, density,
+// inverse factor (row-major, 9), rgb.xyz.  Each worker accumulates into its
+// own buffer; the buffers are summed in worker order.
+int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                           const float* rgb, const float* rayO, const float* rayD, const uint8_t* mask,
+                           const uint32_t* ranges, const uint32_t* sortedIds, int K, int tileBegin, int tileEnd,
+                           const float* rgba, const float* hitT, const float* gradRgba, const float* gradHitT,
+                           float* gradRecord) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile;
+    Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
+    const int nthreads = worker_count();
+    std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads));
+    {
+        parallel_for(tileBegin, tileEnd, 1, [&](int tile, int tid) {
+            std::vector<float>& acc = partial[size_t(tid)];
+            if (acc.empty()) acc.assign(size_t(N) * 16, 0.0f);
+            if (mask[tile] == 0u) return;
+            const int tx = tile % gx, ty = tile / gx;
+            for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
+                for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                    const size_t pix = size_t(px) + size_t(W) * py;
+                    const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                    if (!ray.valid) continue;
+                    // initializeBackwardRay, rayPayloadBackward.cuh:59-120
+                    const float featB[3] = {rgba[4 * pix], rgba[4 * pix + 1], rgba[4 * pix + 2]};
+                    const float featG[3] = {gradRgba[4 * pix], gradRgba[4 * pix + 1], gradRgba[4 * pix + 2]};
+                    const float TB = 1.0f - rgba[4 * pix + 3];
+                    const float TG = -1.0f * gradRgba[4 * pix + 3];
+                    const float hitTB = hitT[pix];
+                    const float hitTG = gradHitT[pix];
+                    float T = 1.0f, depth = 0.0f;
+                    float radiance[3] = {0.0f, 0.0f, 0.0f};
+                    bool alive = true;
+                    traverse(sc, uint32_t(tile), ray, alive, [&](const Hit& hh) {
+                        const Particle P = load_particle(particles + 32 * size_t(hh.idx));
+                        const HalfRay h = half_ray(ray, P);
+                        if (h.valid) {
+                            const float grayDist = fdot(h.p, h.p);
+                            const float gres = gf::gf_expf(-0.5f * grayDist);
+                            const float galphaU = gres * P.density;
+                            const float galpha = gf::min_f(kMaxAlpha, galphaU);
+                            if (gres > kMinKernelResponse && galpha > kAlphaThreshold) {
+                                const float gdist = h.tau;
+                                const float weight = galpha * T;
+                                const float nextT = (1.0f - galpha) * T;
+                                depth = depth + gdist * weight;
+                                const float residualHitT =
+                                    gf::max_f(nextT <= kMinTransmittance ? 0.0f : (hitTB - depth) / nextT, 0.0f);
+                                const float galphaRayHitGrd = (gdist - residualHitT) * T * hitTG;
+                                const float residualTrm = galpha < 0.999999f ? TB / (1.0f - galpha) : T;
+                                const float galphaRayDnsGrd = residualTrm * -TG;
+                                const float* c = rgb + 3 * size_t(hh.idx);
+                                float col[3], resid[3];
+                                for (int k = 0; k < 3; ++k) {
+                                    col[k] = gf::max_f(c[k], 0.0f);
+                                    radiance[k] = fmaf_rn(col[k], weight, radiance[k]);
+                                }
+                                for (int k = 0; k < 3; ++k) {
+                                    resid[k] = gf::max_f(
+                                        nextT <= kMinTransmittance ? 0.0f : (featB[k] - radiance[k]) / nextT, 0.0f);
+                                }
+                                float comp = galphaRayHitGrd + galphaRayDnsGrd;
+                                for (int k = 0; k < 3; ++k) comp += T * (col[k] - resid[k]) * featG[k];
+                                const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
+                                float* g = acc.data() + 16 * size_t(hh.idx);
+                                g[3] += gres * gU;
+                                const float gresGrd = P.density * gU;
+                                const float grayDistGrd = -0.5f * gres * gresGrd;
+                                const float tauGrad = weight * hitTG;
+                                // gutHalfRayResponse.cuh:39-62
+                                const float3_ pointGrad = scale(2.0f * grayDistGrd, h.p);
+                                float3_ groGrd = pointGrad;
+                                float3_ grduGrd = scale(h.tau, pointGrad);
+                                const float totalTauGrad = tauGrad + dot(pointGrad, h.grdu);
+                                if (h.interior) {
+                                    const float3_ tauOriginGrad = scale(-1.0f / h.denom, h.grdu);
+                                    const float3_ tauDirectionGrad =
+                                        add(scale(-1.0f / h.denom, h.gro),
+                                            scale((2.0f * h.num) / (h.denom * h.denom), h.grdu));
+                                    groGrd = add(groGrd, scale(totalTauGrad, tauOriginGrad));
+                                    grduGrd = add(grduGrd, scale(totalTauGrad, tauDirectionGrad));
+                                }
+                                // position: -(Binv^T groGrd); Binv rows: += groGrd[i] gposc + grduGrd[i] d
+                                const float* M = P.Binv;
+                                g[0] -= groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6];
+                                g[1] -= groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7];
+                                g[2] -= groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8];
+                                const float3_ gposc = sub(ray.o, P.pos);
+                                const float gr[3] = {groGrd.x, groGrd.y, groGrd.z};
+                                const float gd[3] = {grduGrd.x, grduGrd.y, grduGrd.z};
+                                for (int r = 0; r < 3; ++r) {
+                                    g[4 + 3 * r + 0] += gr[r] * gposc.x + gd[r] * ray.d.x;
+                                    g[4 + 3 * r + 1] += gr[r] * gposc.y + gd[r] * ray.d.y;
+                                    g[4 + 3 * r + 2] += gr[r] * gposc.z + gd[r] * ray.d.z;
+                                }
+                                for (int k = 0; k < 3; ++k) g[13 + k] += featG[k] * weight;
+                                T = nextT;
+                            }
+                        }
+                        if (T < kMinTransmittance) alive = false;
+                    });
+                }
+            }
+        });
+    }
+    std::memset(gradRecord, 0, sizeof(float) * size_t(N) * 16);
+    for (int t = 0; t < nthreads; ++t) {
+        if (partial[size_t(t)].empty()) continue;
+        const float* a = partial[size_t(t)].data();
+        for (size_t i = 0; i < size_t(N) * 16; ++i) gradRecord[i] += a[i];
+    }
+    return 0;
+}
+
+// Projection backward (projectBackward, gutRenderer.cuh:643 ->
+// gutProjector.cuh:1171-1222; radianceFromSpHBwd, gaussianParticles.cuh:234-310;
+// incidentDirectionFromBuffer VJP): turns the per-particle record gradient into
+// the reference's [N,32] density gradient and [N, 3*shCoeffs] SH gradient.
+int oracle_project_backward(const OraclePose* pose, int N, const float* particles, const float* sh, int shCoeffs,
+                            int shDegree, const uint32_t* counts, const float* gradRecord, float* gradParticles,
+                            float* gradSh) {
+    std::memset(gradParticles, 0, sizeof(float) * size_t(N) * 32);
+    std::memset(gradSh, 0, sizeof(float) * size_t(N) * 3 * shCoeffs);
+    parallel_for(0, N, 4096, [&](int i, int) {
+        const float* g = gradRecord + 16 * size_t(i);
+        float* gp = gradParticles + 32 * size_t(i);
+        gp[0] = g[0]; gp[1] = g[1]; gp[2] = g[2];
+        gp[3] = g[3];
+        for (int k = 0; k < 9; ++k) gp[21 + k] = g[4 + k];
+        if (counts[i] == 0u) return;
+        const Particle P = load_particle(particles + 32 * size_t(i));
+        float dist;
+        const float3_ dir = incident_direction(P.pos, *pose, dist);
+        float basis[16], bx[16], by[16], bz[16];
+        sh_basis(shDegree, dir, basis);
+        sh_basis_grad(shDegree, dir, bx, by, bz);
+        const int nb = shDegree >= 3 ? 16 : (shDegree == 2 ? 9 : (shDegree == 1 ? 4 : 1));
+        const float* c = sh + size_t(i) * 3 * shCoeffs;
+        float* gs = gradSh + size_t(i) * 3 * shCoeffs;
+        float3_ dirGrad = f3(0, 0, 0);
+        for (int ch = 0; ch < 3; ++ch) {
+            float acc = basis[0] * c[ch];
+            for (int k = 1; k < nb && k < shCoeffs; ++k) acc = fmaf_rn(basis[k], c[3 * k + ch], acc);
+            const float masked = (acc + 0.5f) > 0.0f ? g[13 + ch] : 0.0f;
+            for (int k = 0; k < nb && k < shCoeffs; ++k) gs[3 * k + ch] = basis[k] * masked;
+            for (int k = 1; k < nb && k < shCoeffs; ++k) {
+                dirGrad.x += bx[k] * c[3 * k + ch] * masked;
+                dirGrad.y += by[k] * c[3 * k + ch] * masked;
+                dirGrad.z += bz[k] * c[3 * k + ch] * masked;
+            }
+        }
+        // d(v/|v|)/dv^T g = (g - n (n.g)) / |v|
+        const float ndg = dot(dir, dirGrad);
+        gp[0] += (dirGrad.x - dir.x * ndg) / dist;
+        gp[1] += (dirGrad.y - dir.y * ndg) / dist;
+        gp[2] += (dirGrad.z - dir.z * ndg) / dist;
+    });
+    return 0;
+}
+
+// Visibility of gutRenderer.cu:204-209: 1 (as an int bit pattern) when the
+// particle has at least one admitted tile.
+int oracle_visibility(int N, const uint32_t* counts, uint32_t* visibility) {
+    for (int i = 0; i < N; ++i) visibility[i] = counts[i] ? 1u : 0u;
+    return 0;
+}
+
+int oracle_num_threads(void) { return worker_count(); }
+
+// Exported scalar elementary functions, for the accuracy tests.
+float oracle_expf(float x) { return gf::gf_expf(x); }
+float oracle_logf(float x) { return gf::gf_logf(x); }
+float oracle_atan2f(float y, float x) { return gf::gf_atan2f(y, x); }
+
+}  // extern "C"

@@ -1,0 +1,138 @@
+"""Shared inputs for the parity tests: one workload rendered by the oracle and
+by the sm_100a tracer (through SplatRaster, i.e. the C ABI)."""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import numpy as np
+
+import oracle
+from gofish_b200.camera import FisheyeCamera, fisheye_camera, random_kb_coefficients
+from gofish_b200.scene import (IDENTITY_POSE, Scene, pack_particles, pose_world_to_sensor, random_rotation_quaternion_xyzw,
+                               random_scene)
+
+
+def tile_mask(valid_px: np.ndarray) -> np.ndarray:
+    """uint8 [Ty,Tx] mask of tiles holding at least one valid pixel ([H,W] bool input)."""
+    h, w = valid_px.shape
+    ty, tx = (h + 15) // 16, (w + 15) // 16
+    pad = np.zeros((ty * 16, tx * 16), dtype=bool)
+    pad[:h, :w] = valid_px
+    return pad.reshape(ty, 16, tx, 16).any(axis=(1, 3)).astype(np.uint8)
+
+
+def oracle_camera(cam: FisheyeCamera) -> oracle.OracleCamera:
+    return oracle.camera(1, cam.width, cam.height, cam.principal, cam.focal, cam.coefficients, cam.max_angle)
+
+
+@dataclasses.dataclass
+class Case:
+    scene: Scene
+    camera: FisheyeCamera
+    pose: np.ndarray
+    particles: np.ndarray
+    features: np.ndarray
+    ray_o: np.ndarray      # [H,W,3]
+    ray_d: np.ndarray      # [H,W,3]
+    valid: np.ndarray      # [H,W] bool
+    tmask: np.ndarray      # [Ty,Tx] uint8
+
+    @property
+    def ocam(self):
+        return oracle_camera(self.camera)
+
+
+def make_case(scene: Scene, camera: FisheyeCamera, pose, tmask_override=None) -> Case:
+    o, d, valid = camera.rays()
+    valid2 = valid[0, :, :, 0]
+    tm = tile_mask(valid2) if tmask_override is None else tmask_override
+    return Case(scene, camera, np.asarray(pose, dtype=np.float32), pack_particles(scene), scene.features, o[0], d[0],
+                valid2, tm)
+
+
+def small_case(seed: int = 7, n: int = 20_000, size: int = 256, sh_degree: int = 3, fov: float = 200.0,
+               random_pose: bool = True, width: int | None = None) -> Case:
+    scene = random_scene(n, sh_degree, seed)
+    rng = np.random.default_rng(seed + 99)
+    k = random_kb_coefficients(rng, fov)
+    cam = fisheye_camera(width or size, size, fov, k)
+    if random_pose:
+        c = rng.standard_normal(3)
+        c = c / np.linalg.norm(c) * 0.5 * np.cbrt(rng.random())
+        pose = pose_world_to_sensor(c, random_rotation_quaternion_xyzw(rng))
+    else:
+        pose = IDENTITY_POSE.copy()
+    return make_case(scene, cam, pose)
+
+
+def oracle_forward(case: Case, k: int, key_mode: int, tiles=None):
+    return oracle.trace(case.ocam, case.pose, case.particles, case.features, case.scene.sh_degree, case.ray_o,
+                        case.ray_d, case.tmask, k, key_mode, tiles)
+
+
+def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
+    return oracle.trace_backward(case.ocam, fwd, case.particles, case.features, case.scene.sh_degree, case.ray_o,
+                                 case.ray_d, case.tmask, k, grad_rgba, grad_hit, tiles)
+
+
+class GpuTracer:
+    """The product path: SplatRaster over the C ABI on one CUDA device."""
+
+    def __init__(self, case: Case, k: int, key_mode: int, device):
+        import torch
+
+        from gofish_b200.splat_raster import SplatRaster
+
+        self.torch = torch
+        self.case = case
+        self.device = device
+        conf = {"render": {"splat": {"k_buffer_size": k}, "gofish": {"fast_global_depth_key": key_mode == 1},
+                           "enable_hitcounts": True}}
+        self.raster = SplatRaster(conf)
+        self.token = "test-token"
+        self.raster.register_physical_tile_mask(torch.from_numpy(case.tmask).to(device), self.token)
+        self.particles = torch.from_numpy(case.particles).to(device)
+        self.features = torch.from_numpy(np.ascontiguousarray(case.features)).to(device)
+        self.ray_o = torch.from_numpy(case.ray_o[None].copy()).to(device)
+        self.ray_d = torch.from_numpy(case.ray_d[None].copy()).to(device)
+        self.sensor = case.camera.model()
+        self.pose = torch.from_numpy(case.pose.copy())
+
+    def forward(self):
+        torch = self.torch
+        out = self.raster.trace(0, False, self.case.scene.sh_degree, self.particles, self.features, self.ray_o,
+                                self.ray_d, None, self.sensor, 0, 1, self.pose, self.pose, self.token)
+        self.out = out
+        inter = self.raster.copy_intermediates(self.device)
+        torch.cuda.synchronize(self.device)
+        res = {k: v.cpu().numpy() for k, v in inter.items()}
+        res["rgba"] = out[0].cpu().numpy()
+        res["hit_t"] = out[1][..., 0].cpu().numpy()
+        res["hit_count"] = out[2][..., 0].cpu().numpy()
+        res["visibility"] = out[3][:, 0].cpu().numpy().view(np.uint32)
+        return res
+
+    def backward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray):
+        torch = self.torch
+        g_rgba = torch.from_numpy(grad_rgba).to(self.device)
+        g_hit = torch.from_numpy(grad_hit[..., None].copy()).to(self.device)
+        zeros = [torch.zeros(1, device=self.device)] * 14
+        gp, gs = self.raster.trace_bwd(0, False, self.case.scene.sh_degree, self.particles, self.features, self.ray_o,
+                                       self.ray_d, None, self.sensor, 0, 1, self.pose, self.pose, self.out[0], g_rgba,
+                                       self.out[1], g_hit, *zeros, self.token)
+        torch.cuda.synchronize(self.device)
+        return gp.cpu().numpy(), gs.cpu().numpy()
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    denom = max(np.linalg.norm(b), 1e-30)
+    return float(np.linalg.norm(a - b) / denom)
+
+
+def psnr(a: np.ndarray, b: np.ndarray) -> float:
+    mse = float(np.mean((np.asarray(a, np.float64) - np.asarray(b, np.float64)) ** 2))
+    return math.inf if mse == 0 else 10 * math.log10(1.0 / mse)

@@ -113,7 +113,12 @@ _SIGNATURES = [
     ("gf_tracer_copy_intermediates", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
       ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),
+    ("gf_sort_tile_keys_static", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
+      ctypes.c_void_p]),
 ]
+
+STATIC_SORT_MAX_PAIRS = 262144
 
 EXPORTED_SYMBOLS = [name for name, _, _ in _SIGNATURES]
 

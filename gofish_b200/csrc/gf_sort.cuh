@@ -8,12 +8,16 @@
 // ranks a block's 4096 items warp by warp in input order (match.any peer
 // groups), stages them in shared memory in digit order and writes each digit
 // run contiguously.  Equal keys keep their input order, as CUB's does.
+//
+// Everything here has internal linkage (anonymous namespace) so that every
+// translation unit that includes this header gets its own kernels.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace gf {
+namespace {
 
 constexpr int kScanThreads = 512;
 constexpr int kScanItems = 8;  // items per thread
@@ -227,4 +231,5 @@ __global__ __launch_bounds__(kSortThreads) void k_radix_scatter(const uint64_t* 
     }
 }
 
+}  // namespace
 }  // namespace gf

@@ -39,6 +39,16 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+}  // namespace
+
+// Records an error for gf_last_error() from the library's other translation units.
+int gf_record_error(int code, const char* message) {
+    g_lastError = message;
+    return code;
+}
+
+namespace {
+
 #define GF_CUDA(call)                                                                                     \
     do {                                                                                                  \
         const cudaError_t e_ = (call);                                                                    \

@@ -192,6 +192,26 @@ int gf_tracer_copy_intermediates(const gf_tracer* tracer, float* projected, floa
                                  uint64_t* sorted_keys, uint32_t* sorted_ids, uint64_t capacity, uint32_t* ranges,
                                  void* stream);
 
+/* Largest number of (key, id) pairs gf_sort_tile_keys_static accepts. */
+#define GF_STATIC_SORT_MAX_PAIRS 262144u
+
+/* Stable sort of (tile << 32 | depth bits) keys and their particle ids by the
+ * key bits [0, end_bit), the same order as the sort inside gf_tracer_trace.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory while they render -- code running inside a CUDA stream
+ * capture (where cudaMalloc is not allowed), hosts that give the library a
+ * fixed device budget and forbid allocation on the frame path, tools that only
+ * pass preallocated buffers.  It allocates nothing: its scratch is a fixed
+ * file-scope device array sized for GF_STATIC_SORT_MAX_PAIRS pairs (about
+ * 3.1 MiB, held by every GPU that loads the library until exit).  Larger
+ * inputs are rejected with GF_ERR_CAPACITY.  The first call on a device
+ * resolves the array's device address and must come before any stream
+ * capture.  All calls on a device share the array: calls whose GPU work
+ * overlaps race and must be serialized by the caller.  Inputs are read only
+ * and must not alias the outputs. */
+int gf_sort_tile_keys_static(const uint64_t* keys_in, const uint32_t* ids_in, uint64_t* keys_out, uint32_t* ids_out,
+                             uint32_t n, int end_bit, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

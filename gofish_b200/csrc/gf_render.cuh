@@ -1,0 +1,706 @@
+// Per-pixel k-buffer compositing, forward and backward (reference render /
+// renderBackward kernels, gutRenderer.cuh:217-265, :555-626; evalKBuffer,
+// gutKBufferRenderer.cuh:614-700; processHitParticle, :207-416;
+// processHitBwd, gaussianParticles.cuh:736-1155).
+//
+// One CTA per 16x16 tile, one thread per pixel.  Tile candidates are staged
+// in shared memory 256 at a time.  When every ray of the tile starts at the
+// same point (a central camera) the canonical ray origin B^-1 (o - mu) of
+// each candidate is computed once per tile instead of once per pixel.
+//
+// The k-buffer lives in shared memory as a per-pixel ring of K entries
+// (hit distance, alpha, particle) kept sorted by hit distance.  It reproduces
+// the reference's register network exactly: HitParticleKBufferT::insert
+// (gutKBufferRenderer.cuh:132-147) sinks the new hit from the top with
+// compare-and-swap (`hit > entry` strict).  For a sorted buffer that network
+// (a) keeps every entry whose distance is >= the new hit's in place, (b)
+// places the new hit below them, (c) moves every entry below it down by one
+// slot, except that inside a run of equal distances only the run's top entry
+// moves -- to the bottom of the run -- while the others stay.  The ring
+// keeps a count of adjacent equal pairs; with no equal pairs (the usual case)
+// an insertion is a plain sorted insert from the top, O(entries moved), and
+// otherwise a general path applies rule (c) explicitly.
+#pragma once
+
+#include "gf_tracer_kernels.cuh"
+
+namespace gf {
+
+struct RenderArgs {
+    FrameArgs f;
+    const uint8_t* mask;
+    const uint2* ranges;
+    const uint32_t* sortedIds;
+    const float4* records;
+    const float* bounds;  // per-particle support radius (sphere around the mean containing the 3-sigma ellipsoid)
+    const float* rayO;
+    const float* rayD;
+};
+
+struct RenderBwdArgs {
+    RenderArgs r;
+    const float* rgba;
+    const float* hitDistance;
+    const float* gradRgba;
+    const float* gradHitDistance;
+    float4* gradRecords;  // [N,4] float4: pos.xyz+density | Binv row0 + row1.x | row1.yz + row2.xy | row2.z + rgb
+};
+
+constexpr int kBatch = kTileThreads;
+
+// A staged candidate: the 64-byte render record, its canonical ray origin for
+// the tile's common ray origin, and the cone from that origin that contains
+// its support sphere (used to skip warps whose rays all miss the sphere).
+struct Staged {
+    float4 a, b, c, d;  // pos.xyz density | Binv r0, r1.x | r1.yz, r2.xy | r2.z, rgb
+    float4 g;           // B^-1 (o - mu) | sin of the cone half-angle
+    float4 u;           // unit direction o -> mu | cos of the cone half-angle (-3: never skipped)
+};
+
+// Warp-level culling.  Each warp covers an 8x4 pixel block; its rays (central
+// tile only) lie in a cone (axis, half-angle theta).  A ray that misses a
+// candidate's support sphere has g > 9 everywhere along it (the sphere
+// contains the 3-sigma ellipsoid), so the hit test would reject it: a warp
+// whose cone does not reach the candidate's cone skips the candidate.  The
+// test adds 1e-3 rad to theta, far above its rounding error, so it never
+// skips a hit and the outputs are unchanged.
+constexpr float kCullMarginRad = 1e-3f;
+constexpr int kMaskWords = kBatch / 32;
+
+struct WarpCone {
+    float ax, ay, az;
+    float cosT, sinT;
+    bool enabled;
+};
+
+// Shared memory of a render CTA: the staged batch, its particle ids, and the
+// per-pixel rings (hit distance + alpha, sorted candidate position).
+__host__ __device__ constexpr size_t render_smem_bytes(int K) {
+    return sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch +
+           size_t(K > 0 ? K : 1) * kTileThreads * (sizeof(float2) + sizeof(uint32_t));
+}
+
+__device__ __forceinline__ Record load_record(const float4* __restrict__ records, uint32_t idx) {
+    const float4* r = records + 4 * size_t(idx);
+    Record q;
+    q.a = __ldg(r);
+    q.b = __ldg(r + 1);
+    q.c = __ldg(r + 2);
+    q.d = __ldg(r + 3);
+    return q;
+}
+
+__device__ __forceinline__ V3 binv_times(const float4& b, const float4& c, const float4& d, V3 v) {
+    return v3(__fmaf_rn(b.z, v.z, __fmaf_rn(b.y, v.y, b.x * v.x)), __fmaf_rn(c.y, v.z, __fmaf_rn(c.x, v.y, b.w * v.x)),
+              __fmaf_rn(d.x, v.z, __fmaf_rn(c.w, v.y, c.z * v.x)));
+}
+
+// Hit test of one candidate with a given canonical ray origin `gro`
+// (reference gaussianParticles.slang:293-338; identical arithmetic to half_ray).
+__device__ __forceinline__ bool hit_with_origin(const Ray& ray, V3 gro, const float4& b, const float4& c,
+                                                const float4& d, float density, float& alpha, float& hitT) {
+    const V3 grdu = binv_times(b, c, d, ray.d);
+    const float denom = fdot3(grdu, grdu);
+    if (!(denom > 0.0f && isfinite_f(denom) && isfinite_f(ray.tmin) && ray.tmax > ray.tmin)) return false;
+    const float num = fdot3(gro, grdu);
+    const float tauLine = -num / denom;
+    const float tau = fminf(fmaxf(tauLine, ray.tmin), ray.tmax);
+    const V3 p = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y), __fmaf_rn(tau, grdu.z, gro.z));
+    const float g = fdot3(p, p);
+    if (g > kResponseCutoff2) return false;
+    const float resp = gf_expf(-0.5f * g);
+    alpha = fminf(kMaxAlpha, resp * density);
+    hitT = tau;
+    return resp > kMinKernelResponse && alpha > kAlphaThreshold && hitT >= ray.tmin && hitT <= ray.tmax;
+}
+
+// ------------------------------------------------------------------ ring k-buffer
+template <int K>
+struct RingKBuffer {
+    float2* ta;    // [K][kTileThreads] (hit distance, alpha)
+    uint32_t* id;  // [K][kTileThreads] sorted position of the candidate in the tile list
+    int tid;
+    int head;
+    int n;
+    int ties;  // adjacent entries with equal hit distance
+
+    __device__ __forceinline__ void init(float2* ta_, uint32_t* id_, int tid_) {
+        ta = ta_;
+        id = id_;
+        tid = tid_;
+        head = 0;
+        n = 0;
+        ties = 0;
+    }
+    __device__ __forceinline__ bool full() const { return n == K; }
+    __device__ __forceinline__ int slot(int i) const {
+        const int s = head + i;
+        return s >= K ? s - K : s;
+    }
+    __device__ __forceinline__ float2 getTA(int s) const { return ta[s * kTileThreads + tid]; }
+    __device__ __forceinline__ uint32_t getId(int s) const { return id[s * kTileThreads + tid]; }
+    __device__ __forceinline__ void put(int s, float2 v, uint32_t i) {
+        ta[s * kTileThreads + tid] = v;
+        id[s * kTileThreads + tid] = i;
+    }
+    // Removes the nearest entry (the reference's kb[0], composited when full).
+    __device__ __forceinline__ void pop_front(float& t, float& a, uint32_t& idx) {
+        const float2 v = getTA(head);
+        t = v.x;
+        a = v.y;
+        idx = getId(head);
+        if (n > 1 && getTA(slot(1)).x == t) --ties;
+        head = head + 1 == K ? 0 : head + 1;
+        --n;
+    }
+    // Entry i in drain order (nearest first).
+    __device__ __forceinline__ void entry(int i, float& t, float& a, uint32_t& idx) const {
+        const int s = slot(i);
+        const float2 v = getTA(s);
+        t = v.x;
+        a = v.y;
+        idx = getId(s);
+    }
+    // Insert with the reference network's semantics; requires n < K.
+    __device__ __forceinline__ void insert(float t, float a, uint32_t idx) {
+        if (ties != 0) {
+            insert_general(t, a, idx);
+            return;
+        }
+        int i = n - 1;
+        float above = -1.0f;
+        while (i >= 0) {
+            const int s = slot(i);
+            const float2 v = getTA(s);
+            if (!(v.x >= t)) break;
+            put(slot(i + 1), v, getId(s));
+            above = v.x;
+            --i;
+        }
+        put(slot(i + 1), make_float2(t, a), idx);
+        if (i + 1 < n && above == t) ++ties;
+        ++n;
+    }
+    __device__ __noinline__ void insert_general(float t, float a, uint32_t idx) {
+        int p = 0;
+        while (p < n && getTA(slot(p)).x < t) ++p;
+        // Entries below the new hit: every run of equal distances moves its top entry to its bottom.
+        int r = 0;
+        while (r < p) {
+            const float tr = getTA(slot(r)).x;
+            int e = r + 1;
+            while (e < p && getTA(slot(e)).x == tr) ++e;
+            if (e - r >= 2) {
+                const int top = slot(e - 1);
+                const float2 topTA = getTA(top);
+                const uint32_t topId = getId(top);
+                for (int q = e - 1; q > r; --q) {
+                    const int src = slot(q - 1);
+                    put(slot(q), getTA(src), getId(src));
+                }
+                put(slot(r), topTA, topId);
+            }
+            r = e;
+        }
+        for (int q = n; q > p; --q) {
+            const int src = slot(q - 1);
+            put(slot(q), getTA(src), getId(src));
+        }
+        put(slot(p), make_float2(t, a), idx);
+        if (p < n && getTA(slot(p + 1)).x == t) ++ties;
+        ++n;
+    }
+};
+
+// ------------------------------------------------------------------ shared set-up
+struct TileSetup {
+    int tile, px, py;
+    bool inImage;
+    size_t pix;
+    Ray ray;
+    bool central;  // every in-image ray of the tile starts at the same point
+    V3 origin;     // that point
+    WarpCone cone;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Initializes the pixel's ray and decides whether the tile is central (block-uniform).
+__device__ __forceinline__ TileSetup tile_setup(const RenderArgs& a, bool retained) {
+    __shared__ float sOrigin[3];
+    TileSetup ts;
+    const FrameArgs& f = a.f;
+    ts.tile = blockIdx.x;
+    const int tx = ts.tile % f.gx, ty = ts.tile / f.gx;
+    // warp w covers the 8x4 block (w & 1, w >> 1) of the tile; lane -> (lane & 7, lane >> 3)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    ts.px = tx * kTile + (warp & 1) * 8 + (lane & 7);
+    ts.py = ty * kTile + (warp >> 1) * 4 + (lane >> 3);
+    ts.inImage = ts.px < f.W && ts.py < f.H;
+    ts.pix = size_t(ts.px) + size_t(f.W) * ts.py;
+    ts.ray.valid = false;
+    ts.ray.o = v3(0.0f, 0.0f, 0.0f);
+    if (ts.inImage && retained) {
+        ts.ray = make_ray(f.pose, v3(a.rayO[3 * ts.pix], a.rayO[3 * ts.pix + 1], a.rayO[3 * ts.pix + 2]),
+                          v3(a.rayD[3 * ts.pix], a.rayD[3 * ts.pix + 1], a.rayD[3 * ts.pix + 2]));
+    }
+    if (threadIdx.x == 0) {
+        sOrigin[0] = ts.ray.o.x;
+        sOrigin[1] = ts.ray.o.y;
+        sOrigin[2] = ts.ray.o.z;
+    }
+    __syncthreads();
+    ts.origin = v3(sOrigin[0], sOrigin[1], sOrigin[2]);
+    const bool same = !ts.inImage ||
+                      (__float_as_uint(ts.ray.o.x) == __float_as_uint(ts.origin.x) &&
+                       __float_as_uint(ts.ray.o.y) == __float_as_uint(ts.origin.y) &&
+                       __float_as_uint(ts.ray.o.z) == __float_as_uint(ts.origin.z));
+    // thread 0 is always in the image for a non-empty tile
+    ts.central = __syncthreads_and(same) != 0;
+    // Cone of the warp's valid rays.
+    const bool valid = ts.ray.valid;
+    const float sx = warp_sum(valid ? ts.ray.d.x : 0.0f);
+    const float sy = warp_sum(valid ? ts.ray.d.y : 0.0f);
+    const float sz = warp_sum(valid ? ts.ray.d.z : 0.0f);
+    const float sn = sqrtf(sx * sx + sy * sy + sz * sz);
+    ts.cone.enabled = false;
+    ts.cone.ax = ts.cone.ay = ts.cone.az = 0.0f;
+    ts.cone.cosT = 1.0f;
+    ts.cone.sinT = 0.0f;
+    if (__any_sync(0xffffffffu, valid) && ts.central && sn > 0.0f) {
+        ts.cone.ax = sx / sn;
+        ts.cone.ay = sy / sn;
+        ts.cone.az = sz / sn;
+        const float dl = sqrtf(dot3(ts.ray.d, ts.ray.d));
+        const float c = valid ? (ts.cone.ax * ts.ray.d.x + ts.cone.ay * ts.ray.d.y + ts.cone.az * ts.ray.d.z) / dl : 1.0f;
+        const float cmin = warp_min(fminf(1.0f, fmaxf(-1.0f, c)));
+        const float theta = acosf(cmin) + kCullMarginRad;
+        if (theta < 1.5f) {
+            ts.cone.cosT = cosf(theta);
+            ts.cone.sinT = sinf(theta);
+            ts.cone.enabled = true;
+        }
+    }
+    return ts;
+}
+
+// Bit i: candidate k*32+i of the staged batch may reach a ray of this warp.
+__device__ __forceinline__ uint32_t warp_mask(const TileSetup& ts, const Staged* sRec, int cnt, int k) {
+    const int j = k * 32 + (threadIdx.x & 31);
+    bool pass = j < cnt;
+    if (pass && ts.cone.enabled) {
+        const float4 u = sRec[j].u;
+        const float sinB = sRec[j].g.w;
+        const float lhs = ts.cone.ax * u.x + ts.cone.ay * u.y + ts.cone.az * u.z;
+        const float rhs = ts.cone.cosT * u.w - ts.cone.sinT * sinB;
+        pass = !(lhs < rhs);
+    }
+    return __ballot_sync(0xffffffffu, pass);
+}
+
+__device__ __forceinline__ uint32_t idxOf(const RenderArgs& a, uint32_t sIdx) { return __ldg(a.sortedIds + sIdx); }
+
+// Stages candidate sIdx into shared memory (thread-private slot).
+__device__ __forceinline__ void stage(const RenderArgs& a, const TileSetup& ts, uint32_t sIdx, Staged& out) {
+    const Record q = load_record(a.records, idxOf(a, sIdx));
+    out.a = q.a;
+    out.b = q.b;
+    out.c = q.c;
+    out.d = q.d;
+    if (ts.central) {
+        const V3 gro = binv_times(q.b, q.c, q.d, v3(ts.origin.x - q.a.x, ts.origin.y - q.a.y, ts.origin.z - q.a.z));
+        const V3 v = v3(q.a.x - ts.origin.x, q.a.y - ts.origin.y, q.a.z - ts.origin.z);
+        const float dist = sqrtf(dot3(v, v));
+        const float radius = __ldg(a.bounds + idxOf(a, sIdx));
+        float sinB = 0.0f, cosB = -3.0f;
+        float4 u = make_float4(0.0f, 0.0f, 0.0f, cosB);
+        if (dist > radius && isfinite_f(dist) && isfinite_f(radius)) {
+            sinB = radius / dist;
+            cosB = sqrtf(fmaxf(0.0f, 1.0f - sinB * sinB));
+            u = make_float4(v.x / dist, v.y / dist, v.z / dist, cosB);
+        }
+        out.g = make_float4(gro.x, gro.y, gro.z, sinB);
+        out.u = u;
+    }
+}
+
+__device__ __forceinline__ bool hit_staged(const TileSetup& ts, const Staged& q, float& alpha, float& ht) {
+    V3 gro;
+    if (ts.central) {
+        gro = v3(q.g.x, q.g.y, q.g.z);
+    } else {
+        gro = binv_times(q.b, q.c, q.d, v3(ts.ray.o.x - q.a.x, ts.ray.o.y - q.a.y, ts.ray.o.z - q.a.z));
+    }
+    return hit_with_origin(ts.ray, gro, q.b, q.c, q.d, q.a.w, alpha, ht);
+}
+
+// ------------------------------------------------------------------ forward
+struct PixelFwd {
+    float T, hitT;
+    float r, g, b;
+    uint32_t hitN;
+    bool alive;
+};
+
+// The staged batch in shared memory: candidates [base, base + cnt) of the tile's sorted list.
+struct Batch {
+    const Staged* rec;
+    const uint32_t* ids;
+    uint32_t base, cnt;
+};
+
+// Render record of the candidate at sorted position sp: from the staged batch
+// when it is there, else from global memory.
+__device__ __forceinline__ Record record_at(const RenderArgs& a, const Batch& b, uint32_t sp, uint32_t& idx) {
+    const uint32_t j = sp - b.base;
+    Record q;
+    if (j < b.cnt) {
+        const Staged& st = b.rec[j];
+        q.a = st.a;
+        q.b = st.b;
+        q.c = st.c;
+        q.d = st.d;
+        idx = b.ids[j];
+    } else {
+        idx = __ldg(a.sortedIds + sp);
+        q = load_record(a.records, idx);
+    }
+    return q;
+}
+
+__device__ __forceinline__ float4 color_at(const RenderArgs& a, const Batch& b, uint32_t sp) {
+    const uint32_t j = sp - b.base;
+    if (j < b.cnt) return b.rec[j].d;
+    return __ldg(a.records + 4 * size_t(__ldg(a.sortedIds + sp)) + 3);
+}
+
+// Front-to-back composite of one hit (reference gutKBufferRenderer.cuh:307-416);
+// c.yzw is the particle's colour.
+__device__ __forceinline__ void composite_fwd(PixelFwd& s, float ht, float ha, float4 c) {
+    const float w = ha * s.T;
+    s.hitT = s.hitT + ht * w;
+    s.T = s.T * (1.0f - ha);
+    if (w > 0.0f) {
+        s.r = __fmaf_rn(fmaxf(c.y, 0.0f), w, s.r);
+        s.g = __fmaf_rn(fmaxf(c.z, 0.0f), w, s.g);
+        s.b = __fmaf_rn(fmaxf(c.w, 0.0f), w, s.b);
+        s.hitN++;
+    }
+    if (s.T < kMinTransmittance) s.alive = false;
+}
+
+__device__ __forceinline__ float2* ring_ta(unsigned char* smem) {
+    return reinterpret_cast<float2*>(smem + sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch);
+}
+template <int K>
+__device__ __forceinline__ uint32_t* ring_id(unsigned char* smem) {
+    return reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch +
+                                       sizeof(float2) * K * kTileThreads);
+}
+
+template <int K>
+__global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float* __restrict__ rgba,
+                                                             float* __restrict__ hitDistance,
+                                                             float* __restrict__ hitCount) {
+    constexpr int KR = K > 0 ? K : 1;
+    extern __shared__ __align__(16) unsigned char smem[];
+    Staged* sRec = reinterpret_cast<Staged*>(smem);
+    uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
+    const bool retained = a.mask[blockIdx.x] != 0u;
+    const TileSetup ts = tile_setup(a, retained);
+    PixelFwd s{1.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0u, ts.ray.valid};
+    RingKBuffer<KR> kb;
+    kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
+    Batch bt{sRec, sId, 0u, 0u};
+    if (retained) {
+        const uint2 range = a.ranges[ts.tile];
+        for (uint32_t base = range.x; base < range.y; base += kBatch) {
+            if (__syncthreads_and(!s.alive)) break;
+            const uint32_t sIdx = base + threadIdx.x;
+            if (sIdx < range.y) {
+                sId[threadIdx.x] = __ldg(a.sortedIds + sIdx);
+                stage(a, ts, sIdx, sRec[threadIdx.x]);
+            }
+            __syncthreads();
+            const int cnt = min(uint32_t(kBatch), range.y - base);
+            bt.base = base;
+            bt.cnt = uint32_t(cnt);
+            const int words = (cnt + 31) >> 5;
+#pragma unroll 1
+            for (int k = 0; k < words && __any_sync(0xffffffffu, s.alive); ++k) {
+                uint32_t m = warp_mask(ts, sRec, cnt, k);
+                while (m != 0u && s.alive) {
+                    const int j = k * 32 + __ffs(m) - 1;
+                    m &= m - 1u;
+                    float alpha, ht;
+                    if (hit_staged(ts, sRec[j], alpha, ht)) {
+                        if constexpr (K == 0) {
+                            composite_fwd(s, ht, alpha, sRec[j].d);
+                        } else {
+                            if (kb.full()) {
+                                float t0, a0;
+                                uint32_t s0;
+                                kb.pop_front(t0, a0, s0);
+                                composite_fwd(s, t0, a0, color_at(a, bt, s0));
+                            }
+                            kb.insert(ht, alpha, base + uint32_t(j));
+                        }
+                    }
+                }
+            }
+        }
+        if constexpr (K > 0) {
+            for (int i = 0; s.alive && i < kb.n; ++i) {
+                float ht, ha;
+                uint32_t sp;
+                kb.entry(i, ht, ha, sp);
+                composite_fwd(s, ht, ha, color_at(a, bt, sp));
+            }
+        }
+    }
+    if (!ts.inImage) return;
+    float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float hd = 1e06f, hc = 0.0f;
+    if (ts.ray.valid) {
+        out = make_float4(s.r, s.g, s.b, 1.0f - s.T);
+        hd = s.hitT;
+        hc = float(s.hitN);
+    }
+    reinterpret_cast<float4*>(rgba)[ts.pix] = out;
+    hitDistance[ts.pix] = hd;
+    if (hitCount != nullptr) hitCount[ts.pix] = hc;
+}
+
+// ------------------------------------------------------------------ backward
+struct PixelBwd {
+    float T, depth;
+    float r, g, b;
+    float featB[3], featG[3];
+    float TB, TG, hitTB, hitTG;
+    bool alive;
+};
+
+// Gradient of one composited hit with closest-point parameter tau and
+// opacity galpha from the hit test (reference processHitBwd,
+// gaussianParticles.cuh:736-1155, geometric channels inactive).  The walking
+// state (T, depth, colour) advances with the forward's exact arithmetic;
+// quotients that only scale gradients use fast reciprocals.
+__device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Record& q, float tau, float galpha,
+                                        float4 g[4]) {
+    const V3 gp = v3(ray.o.x - q.a.x, ray.o.y - q.a.y, ray.o.z - q.a.z);
+    const V3 gro = binv_times(q.b, q.c, q.d, gp);
+    const V3 grdu = binv_times(q.b, q.c, q.d, ray.d);
+    const float denom = fdot3(grdu, grdu);
+    const float num = fdot3(gro, grdu);
+    const bool interior = tau > ray.tmin && tau < ray.tmax;
+    const V3 p = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y), __fmaf_rn(tau, grdu.z, gro.z));
+    const float grayDist = fdot3(p, p);
+    const float gres = gf_expf(-0.5f * grayDist);
+    const float density = q.a.w;
+    const float galphaU = gres * density;
+    if (!(gres > kMinKernelResponse && galpha > kAlphaThreshold)) return false;
+    const float gdist = tau;
+    const float weight = galpha * s.T;
+    const float nextT = (1.0f - galpha) * s.T;
+    s.depth = s.depth + gdist * weight;
+    const bool tail = nextT <= kMinTransmittance;
+    const float invNext = tail ? 0.0f : __fdividef(1.0f, nextT);
+    const float residualHitT = fmaxf((s.hitTB - s.depth) * invNext, 0.0f);
+    const float galphaRayHitGrd = (gdist - residualHitT) * s.T * s.hitTG;
+    const float residualTrm = galpha < 0.999999f ? s.TB * __fdividef(1.0f, 1.0f - galpha) : s.T;
+    const float galphaRayDnsGrd = residualTrm * -s.TG;
+    const float cr = fmaxf(q.d.y, 0.0f), cg = fmaxf(q.d.z, 0.0f), cb = fmaxf(q.d.w, 0.0f);
+    s.r = __fmaf_rn(cr, weight, s.r);
+    s.g = __fmaf_rn(cg, weight, s.g);
+    s.b = __fmaf_rn(cb, weight, s.b);
+    const float rr = fmaxf((s.featB[0] - s.r) * invNext, 0.0f);
+    const float rg = fmaxf((s.featB[1] - s.g) * invNext, 0.0f);
+    const float rb = fmaxf((s.featB[2] - s.b) * invNext, 0.0f);
+    float comp = galphaRayHitGrd + galphaRayDnsGrd;
+    comp += s.T * (cr - rr) * s.featG[0];
+    comp += s.T * (cg - rg) * s.featG[1];
+    comp += s.T * (cb - rb) * s.featG[2];
+    const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
+    const float gDensity = gres * gU;
+    const float gresGrd = density * gU;
+    const float grayDistGrd = -0.5f * gres * gresGrd;
+    const float tauGrad = weight * s.hitTG;
+    // Closest-point VJP (reference gutHalfRayResponse.cuh:39-62).
+    const V3 pointGrad = (2.0f * grayDistGrd) * p;
+    V3 groGrd = pointGrad;
+    V3 grduGrd = tau * pointGrad;
+    const float totalTauGrad = tauGrad + dot3(pointGrad, grdu);
+    if (interior) {
+        const float invDen = __fdividef(1.0f, denom);
+        const float inv = -invDen;
+        const V3 tauOriginGrad = inv * grdu;
+        const V3 tauDirectionGrad = inv * gro + ((2.0f * num) * (invDen * invDen)) * grdu;
+        groGrd = groGrd + totalTauGrad * tauOriginGrad;
+        grduGrd = grduGrd + totalTauGrad * tauDirectionGrad;
+    }
+    // Binv rows: r0 = (b.x b.y b.z), r1 = (b.w c.x c.y), r2 = (c.z c.w d.x).
+    const float gpx = -(groGrd.x * q.b.x + groGrd.y * q.b.w + groGrd.z * q.c.z);
+    const float gpy = -(groGrd.x * q.b.y + groGrd.y * q.c.x + groGrd.z * q.c.w);
+    const float gpz = -(groGrd.x * q.b.z + groGrd.y * q.c.y + groGrd.z * q.d.x);
+    const float m00 = groGrd.x * gp.x + grduGrd.x * ray.d.x, m01 = groGrd.x * gp.y + grduGrd.x * ray.d.y,
+                m02 = groGrd.x * gp.z + grduGrd.x * ray.d.z;
+    const float m10 = groGrd.y * gp.x + grduGrd.y * ray.d.x, m11 = groGrd.y * gp.y + grduGrd.y * ray.d.y,
+                m12 = groGrd.y * gp.z + grduGrd.y * ray.d.z;
+    const float m20 = groGrd.z * gp.x + grduGrd.z * ray.d.x, m21 = groGrd.z * gp.y + grduGrd.z * ray.d.y,
+                m22 = groGrd.z * gp.z + grduGrd.z * ray.d.z;
+    g[0] = make_float4(gpx, gpy, gpz, gDensity);
+    g[1] = make_float4(m00, m01, m02, m10);
+    g[2] = make_float4(m11, m12, m20, m21);
+    g[3] = make_float4(m22, s.featG[0] * weight, s.featG[1] * weight, s.featG[2] * weight);
+    s.T = nextT;
+    return true;
+}
+
+__device__ __forceinline__ float4 shfl_down4(float4 v, int o) {
+    return make_float4(__shfl_down_sync(0xffffffffu, v.x, o), __shfl_down_sync(0xffffffffu, v.y, o),
+                       __shfl_down_sync(0xffffffffu, v.z, o), __shfl_down_sync(0xffffffffu, v.w, o));
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// Warp-aggregated accumulation of one gradient per lane: when every active
+// lane of the warp holds the same particle the 16 components are reduced
+// with shuffles and written by one lane, otherwise each lane adds its own
+// (vector red.global.add of 4 floats).
+__device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords, bool have, uint32_t idx,
+                                                float4 g[4]) {
+    const uint32_t hm = __ballot_sync(0xffffffffu, have);
+    if (hm == 0u) return;
+    const int lane = threadIdx.x & 31;
+    const int leader = __ffs(hm) - 1;
+    const uint32_t leaderIdx = __shfl_sync(0xffffffffu, idx, leader);
+    const bool uniform = __all_sync(0xffffffffu, !have || idx == leaderIdx);
+    if (uniform && __popc(hm) > 1) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = have ? g[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = add4(v[k], shfl_down4(v[k], o));
+        }
+        if (lane == 0) {
+            float4* dst = gradRecords + 4 * size_t(leaderIdx);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) atomicAdd(dst + k, v[k]);
+        }
+    } else if (have) {
+        float4* dst = gradRecords + 4 * size_t(idx);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) atomicAdd(dst + k, g[k]);
+    }
+}
+
+// Backward replay: the identical traversal and k-buffer, each composited hit
+// back-propagated from the final pixel values.  Loops are warp-uniform so
+// the gradient reduction can use full-warp shuffles.
+template <int K>
+__global__ __launch_bounds__(kTileThreads) void k_render_bwd(RenderBwdArgs a) {
+    constexpr int KR = K > 0 ? K : 1;
+    extern __shared__ __align__(16) unsigned char smem[];
+    Staged* sRec = reinterpret_cast<Staged*>(smem);
+    uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
+    if (a.r.mask[blockIdx.x] == 0u) return;  // block-uniform
+    const TileSetup ts = tile_setup(a.r, true);
+    const Ray& ray = ts.ray;
+    PixelBwd s;
+    s.T = 1.0f;
+    s.depth = 0.0f;
+    s.r = s.g = s.b = 0.0f;
+    s.alive = ray.valid;
+    if (ray.valid) {
+        const float4 fo = reinterpret_cast<const float4*>(a.rgba)[ts.pix];
+        const float4 go = reinterpret_cast<const float4*>(a.gradRgba)[ts.pix];
+        s.featB[0] = fo.x; s.featB[1] = fo.y; s.featB[2] = fo.z;
+        s.featG[0] = go.x; s.featG[1] = go.y; s.featG[2] = go.z;
+        s.TB = 1.0f - fo.w;
+        s.TG = -1.0f * go.w;
+        s.hitTB = a.hitDistance[ts.pix];
+        s.hitTG = a.gradHitDistance[ts.pix];
+    }
+    RingKBuffer<KR> kb;
+    kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
+    Batch bt{sRec, sId, 0u, 0u};
+    const uint2 range = a.r.ranges[ts.tile];
+    for (uint32_t base = range.x; base < range.y; base += kBatch) {
+        if (__syncthreads_and(!s.alive)) break;
+        const uint32_t sIdx = base + threadIdx.x;
+        if (sIdx < range.y) {
+            sId[threadIdx.x] = __ldg(a.r.sortedIds + sIdx);
+            stage(a.r, ts, sIdx, sRec[threadIdx.x]);
+        }
+        __syncthreads();
+        const int cnt = min(uint32_t(kBatch), range.y - base);
+        bt.base = base;
+        bt.cnt = uint32_t(cnt);
+        const int words = (cnt + 31) >> 5;
+        bool warpAlive = __any_sync(0xffffffffu, s.alive);
+#pragma unroll 1
+        for (int k = 0; k < words && warpAlive; ++k) {
+            uint32_t m = warp_mask(ts, sRec, cnt, k);
+            while (m != 0u) {
+                warpAlive = __any_sync(0xffffffffu, s.alive);
+                if (!warpAlive) break;
+                const int j = k * 32 + __ffs(m) - 1;
+                m &= m - 1u;
+                bool have = false;
+                uint32_t cid = kInvalidParticle;
+                float4 g[4] = {};
+                if (s.alive) {
+                    float alpha, ht;
+                    if (hit_staged(ts, sRec[j], alpha, ht)) {
+                        if constexpr (K == 0) {
+                            const Record q = record_at(a.r, bt, base + uint32_t(j), cid);
+                            have = hit_vjp(s, ray, q, ht, alpha, g);
+                        } else {
+                            if (kb.full()) {
+                                float t0, a0;
+                                uint32_t s0;
+                                kb.pop_front(t0, a0, s0);
+                                const Record q = record_at(a.r, bt, s0, cid);
+                                have = hit_vjp(s, ray, q, t0, a0, g);
+                            }
+                            kb.insert(ht, alpha, base + uint32_t(j));
+                        }
+                        if (s.T < kMinTransmittance) s.alive = false;
+                    }
+                }
+                accumulate_grad(a.gradRecords, have, cid, g);
+            }
+        }
+    }
+    if constexpr (K > 0) {
+        for (int i = 0; i < K; ++i) {
+            if (!__any_sync(0xffffffffu, s.alive && i < kb.n)) break;
+            bool have = false;
+            uint32_t cid = kInvalidParticle;
+            float4 g[4] = {};
+            if (s.alive && i < kb.n) {
+                float ht, ha;
+                uint32_t sp;
+                kb.entry(i, ht, ha, sp);
+                const Record q = record_at(a.r, bt, sp, cid);
+                have = hit_vjp(s, ray, q, ht, ha, g);
+                if (s.T < kMinTransmittance) s.alive = false;
+            }
+            accumulate_grad(a.gradRecords, have, cid, g);
+        }
+    }
+}
+
+}  // namespace gf

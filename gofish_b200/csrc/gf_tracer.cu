@@ -22,6 +22,7 @@
 
 #include "../../include/gofish_b200.h"
 #include "gf_sort.cuh"
+#include "gf_render.cuh"
 #include "gf_tracer_kernels.cuh"
 
 namespace {
@@ -111,7 +112,7 @@ struct gf_tracer {
     std::map<std::string, TileMask> masks;
 
     // Forward context.
-    DeviceBuffer proj, records, counts, offsets, scanTiles, total, tileRays, ranges;
+    DeviceBuffer proj, records, bounds, counts, offsets, scanTiles, total, tileRays, ranges;
     DeviceBuffer keys[2], ids[2], hist;
     DeviceBuffer gradRecords;
     uint64_t* hostTotal = nullptr;
@@ -284,12 +285,16 @@ int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream) {
 template <int K>
 void launch_render_fwd(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
                        cudaStream_t stream) {
-    gf::k_render_fwd<K><<<tiles, gf::kTileThreads, 0, stream>>>(a, rgba, hd, hc);
+    const size_t smem = gf::render_smem_bytes(K);
+    cudaFuncSetAttribute(gf::k_render_fwd<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_fwd<K><<<tiles, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
 }
 
 template <int K>
 void launch_render_bwd(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
-    gf::k_render_bwd<K><<<tiles, gf::kTileThreads, 0, stream>>>(a);
+    const size_t smem = gf::render_smem_bytes(K);
+    cudaFuncSetAttribute(gf::k_render_bwd<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_bwd<K><<<tiles, gf::kTileThreads, smem, stream>>>(a);
 }
 
 int dispatch_fwd(int K, const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
@@ -348,6 +353,7 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     if (int e = t->proj.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->records.ensure(sizeof(float4) * 4 * size_t(N) + 16, stream)) return e;
     if (int e = t->counts.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
+    if (int e = t->bounds.ensure(sizeof(float) * size_t(N) + 16, stream)) return e;
     if (int e = t->offsets.ensure(sizeof(uint64_t) * size_t(N) + 16, stream)) return e;
     if (int e = t->total.ensure(sizeof(uint64_t) * 2, stream)) return e;
     if (int e = t->tileRays.ensure(sizeof(float4) * 2 * size_t(T), stream)) return e;
@@ -364,7 +370,8 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
         StageTimer st(t, GF_STAGE_PROJECT, stream);
         gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
                                                           t->proj.as<float4>(), t->records.as<float4>(),
-                                                          t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis));
+                                                          t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),
+                                                          t->bounds.as<float>());
         t->launches += 1;
         GF_LAUNCH_CHECK();
     }
@@ -415,6 +422,7 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     a.ranges = t->ranges.as<uint2>();
     a.sortedIds = t->ids[t->finalBuf].as<uint32_t>();
     a.records = t->records.as<float4>();
+    a.bounds = t->bounds.as<float>();
     a.rayO = in->ray_origin;
     a.rayD = in->ray_direction;
     {
@@ -465,7 +473,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaGetDevice(&prev);
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
-        DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->counts, &t->offsets, &t->scanTiles, &t->total,
+        DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
                                 &t->hist,    &t->gradRecords};
         for (DeviceBuffer* b : bufs) b->release();
@@ -531,6 +539,7 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     a.r.ranges = t->ranges.as<uint2>();
     a.r.sortedIds = t->ids[t->finalBuf].as<uint32_t>();
     a.r.records = t->records.as<float4>();
+    a.r.bounds = t->bounds.as<float>();
     a.r.rayO = t->frameRayO;
     a.r.rayD = t->frameRayD;
     a.rgba = g->rgba;

@@ -42,7 +42,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
-    p.add_argument("--workload", choices=["single_view", "cpu_scale"], default="single_view")
+    p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale"], default="single_view")
+    p.add_argument("--views-per-gpu", type=int, default=8, help="views per rank and step (multi_view)")
     p.add_argument("--num-gaussians", type=int, default=None, help="override the workload's Gaussian count")
     p.add_argument("--size", type=int, default=None, help="override the raster size")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -51,12 +52,20 @@ def parse_args():
 
 
 # ----------------------------------------------------------------------------- workload
-def build_workload(args, rank: int):
+def build_workload(args, rank: int, world: int = 1):
+    """The workload and the poses of the views this rank renders each step."""
     from gofish_b200 import scene as sc
-    from gofish_b200.camera import random_kb_coefficients  # noqa: F401
 
     if args.workload == "cpu_scale":
         w = sc.workload_cpu_scale()
+    elif args.workload == "multi_view":
+        kw = {"views": max(64, args.views_per_gpu * world)}
+        if args.num_gaussians:
+            kw["n"] = args.num_gaussians
+        if args.size:
+            kw["size"] = args.size
+        w = sc.workload_multi_view(**kw)
+        return w, w.poses[rank * args.views_per_gpu:(rank + 1) * args.views_per_gpu]
     else:
         kw = {}
         if args.num_gaussians:
@@ -71,10 +80,10 @@ def build_workload(args, rank: int):
         c = rng.standard_normal(3)
         c = c / np.linalg.norm(c) * 0.5 * np.cbrt(rng.random())
         pose = sc.pose_world_to_sensor(c, sc.random_rotation_quaternion_xyzw(rng))
-    return w, pose
+    return w, [pose]
 
 
-def workload_config(w, args, world: int) -> dict:
+def workload_config(w, args, world: int, views_per_rank: int = 1) -> dict:
     cam = w.camera
     return {
         "workload": w.name,
@@ -83,7 +92,7 @@ def workload_config(w, args, world: int) -> dict:
         "camera": f"OPENCV_FISHEYE (Kannala-Brandt) 200deg {cam.width}x{cam.height}",
         "k_buffer": w.k_buffer,
         "sort_key": "per-tile max-response depth",
-        "views_per_step": world,
+        "views_per_step": world * views_per_rank,
         "loss": "L1 vs U[0,1] target",
         "l2_policy": "inputs larger than L2 (packed particles + SH + rays > 126 MB)",
         "parallelism": f"dp{world} (views sharded, NCCL all-reduce of particle gradients)" if world > 1 else "single GPU",
@@ -181,13 +190,15 @@ def run_gpu(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
-    w, pose = build_workload(args, rank)
+    from gofish_b200.multiview import multiview_step
+
+    w, poses = build_workload(args, rank, world)
     cam = w.camera
     ray_o_np, ray_d_np, valid_np = cam.rays()
     particles_host = torch.from_numpy(pack_particles(w.scene)).pin_memory()
     features_host = torch.from_numpy(np.ascontiguousarray(w.scene.features)).pin_memory()
     rng = np.random.default_rng(777 + rank)
-    target_host = torch.from_numpy(rng.random((cam.height, cam.width, 3), dtype=np.float32)).pin_memory()
+    target_host = torch.from_numpy(rng.random((len(poses), cam.height, cam.width, 3), dtype=np.float32)).pin_memory()
 
     particles = particles_host.to(device)
     features = features_host.to(device)
@@ -207,26 +218,35 @@ def run_gpu(args):
     raster = SplatRaster(conf)
     raster.register_physical_tile_mask(binding.mask, binding.token)
     sensor = cam.model()
-    pose_t = torch.from_numpy(np.asarray(pose, dtype=np.float32))
+    pose_ts = [torch.from_numpy(np.asarray(p, dtype=np.float32)) for p in poses]
     zeros14 = [torch.zeros(1, device=device)] * 14
     scale = 1.0 / (3.0 * n_valid)
     zero_hit = torch.zeros((cam.height, cam.width, 1), device=device)
+    accum = [torch.empty_like(particles), torch.empty_like(features)]
+    view_intersections: list[int] = []
+    loss_acc = torch.zeros((), device=device)
 
     def step(p, f, tgt, want_loss=False):
-        out = raster.trace(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
-                           binding.token)
-        rgba = out[0]
-        diff = rgba[..., :3] - tgt
-        grad = torch.zeros_like(rgba)
-        grad[..., :3] = torch.sign(diff) * (valid_f * scale)
-        gp, gs = raster.trace_bwd(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
-                                  rgba, grad, out[1], zero_hit, *zeros14, binding.token)
-        if world > 1:
-            dist.all_reduce(gp)
-            dist.all_reduce(gs)
-        if want_loss:
-            return (diff.abs() * valid_f).sum() * scale
-        return None
+        """Forward, L1 loss gradient and backward of every local view, the
+        per-Gaussian gradients summed over the views and all-reduced over ranks."""
+        loss_acc.zero_()
+
+        def render_view(v):
+            pose_t = pose_ts[v]
+            out = raster.trace(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
+                               binding.token)
+            view_intersections.append(int(raster.stats().num_intersections))
+            rgba = out[0]
+            diff = rgba[..., :3] - tgt[v]
+            grad = torch.zeros_like(rgba)
+            grad[..., :3] = torch.sign(diff) * (valid_f * scale)
+            if want_loss:
+                loss_acc.add_((diff.abs() * valid_f).sum() * scale)
+            return raster.trace_bwd(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t,
+                                    pose_t, rgba, grad, out[1], zero_hit, *zeros14, binding.token)
+
+        multiview_step(render_view, range(len(pose_ts)), accum)
+        return loss_acc if want_loss else None
 
     for _ in range(args.warmup):
         step(particles, features, target)
@@ -234,6 +254,7 @@ def run_gpu(args):
     intersections = int(raster.stats().num_intersections)
 
     # --- device-timed region: inputs resident in HBM
+    view_intersections.clear()
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
     launches_before = int(raster.stats().total_kernel_launches)
@@ -254,6 +275,7 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
     elapsed_ms = t0.elapsed_time(t1)
+    timed_intersections = list(view_intersections)
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
     launches = int(raster.stats().total_kernel_launches) - launches_before
@@ -262,7 +284,8 @@ def run_gpu(args):
         dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
     elapsed_ms = float(ms_max.item())
     pixels = cam.width * cam.height
-    value = world * pixels * args.steps / (elapsed_ms / 1000.0) / 1e6
+    views_per_rank = len(poses)
+    value = world * views_per_rank * pixels * args.steps / (elapsed_ms / 1000.0) / 1e6
 
     # --- end to end through the public API with host buffers
     e2e = None
@@ -294,7 +317,7 @@ def run_gpu(args):
         ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * pixels * args.steps / (float(ems.item()) / 1000.0) / 1e6, "unit": UNIT,
+        e2e = {"value": world * views_per_rank * pixels * args.steps / (float(ems.item()) / 1000.0) / 1e6, "unit": UNIT,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4}
 
     # --- roofline of the dominant kernel (average launch duration from stage events)
@@ -302,6 +325,8 @@ def run_gpu(args):
     dominant = max(("render_fwd", "render_bwd"), key=lambda s: stages[s][0])
     dom_ms, dom_launches = stages[dominant]
     avg_s = dom_ms / max(1, dom_launches) / 1000.0
+    # per-launch bytes use the mean intersection count of the timed views
+    intersections = int(round(float(np.mean(timed_intersections)))) if timed_intersections else intersections
     if dominant == "render_bwd":
         alg = intersections * BWD_RENDER_BYTES_PER_INTERSECTION + pixels * BWD_RENDER_BYTES_PER_PIXEL
     else:
@@ -316,7 +341,7 @@ def run_gpu(args):
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
-        "config": workload_config(w, args, world), "e2e": e2e, "roofline": roofline,
+        "config": workload_config(w, args, world, views_per_rank), "e2e": e2e, "roofline": roofline,
         "gpu_launches": int(launches),
         "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
         "intersections_per_view": intersections,
@@ -324,7 +349,7 @@ def run_gpu(args):
     if clock_info is not None:
         result["clocks"] = clock_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(w, pose, ray_o_np, ray_d_np, valid_np, budget_s=20.0)
+        result["cpu_baseline"] = cpu_baseline(w, poses[0], ray_o_np, ray_d_np, valid_np, budget_s=20.0)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -393,7 +418,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    w, pose = build_workload(args, 0)
+    w, poses = build_workload(args, 0)
+    pose = poses[0]
     cam = w.camera
     ray_o, ray_d, valid = cam.rays()
     values = []

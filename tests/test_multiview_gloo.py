@@ -1,0 +1,68 @@
+"""Host-side multi-view data parallelism on two CPU ranks (gloo): view
+sharding and the gradient all-reduce give every rank the gradient of the
+whole batch, equal to the serial sum over all views."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gofish_b200.multiview import multiview_step, shard_views
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _fake_view_grads(v: int):
+    g = torch.Generator().manual_seed(1000 + v)
+    return torch.randn(37, 32, generator=g), torch.randn(37, 48, generator=g)
+
+
+def _worker(rank, world, port, num_views, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        accum = [torch.empty(37, 32), torch.empty(37, 48)]
+        multiview_step(_fake_view_grads, shard_views(num_views, rank, world), accum)
+        out[rank] = [a.clone() for a in accum]
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("num_views", [5, 8])
+def test_two_rank_gradient_allreduce_matches_serial_sum(num_views):
+    world = 2
+    port = _free_port()
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, world, port, num_views, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    serial = [torch.zeros(37, 32), torch.zeros(37, 48)]
+    for v in range(num_views):
+        for s, g in zip(serial, _fake_view_grads(v)):
+            s += g
+    for r in range(world):
+        for got, want in zip(out[r], serial):
+            torch.testing.assert_close(got, want, rtol=1e-6, atol=1e-5)
+
+
+def test_shard_views_partitions_the_batch():
+    for world in (1, 2, 3, 8):
+        views = sorted(v for r in range(world) for v in shard_views(64, r, world))
+        assert views == list(range(64))
+        sizes = [len(shard_views(64, r, world)) for r in range(world)]
+        assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_views(8, 2, 2)

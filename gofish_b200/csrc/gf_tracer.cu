@@ -21,28 +21,15 @@
 #include <vector>
 
 #include "../../include/gofish_b200.h"
-#include "gf_sort.cuh"
+#include "gf_host.cuh"
 #include "gf_render.cuh"
 #include "gf_tracer_kernels.cuh"
 
 namespace {
-
 thread_local std::string g_lastError;
-
-int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
-int fail(int code, const char* fmt, ...) {
-    char buf[1024];
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(buf, sizeof(buf), fmt, ap);
-    va_end(ap);
-    g_lastError = buf;
-    return code;
-}
-
 }  // namespace
 
-// Records an error for gf_last_error() from the library's other translation units.
+// Records an error for gf_last_error() from every translation unit of the library.
 int gf_record_error(int code, const char* message) {
     g_lastError = message;
     return code;
@@ -50,57 +37,10 @@ int gf_record_error(int code, const char* message) {
 
 namespace {
 
-#define GF_CUDA(call)                                                                                     \
-    do {                                                                                                  \
-        const cudaError_t e_ = (call);                                                                    \
-        if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
-    } while (0)
-
-#define GF_LAUNCH_CHECK()                                                                                  \
-    do {                                                                                                   \
-        const cudaError_t e_ = cudaGetLastError();                                                         \
-        if (e_ != cudaSuccess) return fail(GF_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e_)); \
-    } while (0)
-
-struct DeviceBuffer {
-    void* ptr = nullptr;
-    size_t bytes = 0;
-    int ensure(size_t need, cudaStream_t stream) {
-        if (need <= bytes) return GF_OK;
-        if (ptr != nullptr) {
-            GF_CUDA(cudaFreeAsync(ptr, stream));
-            ptr = nullptr;
-            bytes = 0;
-        }
-        const size_t grown = need + need / 4 + 256;
-        GF_CUDA(cudaMallocAsync(&ptr, grown, stream));
-        bytes = grown;
-        return GF_OK;
-    }
-    void release() {
-        if (ptr != nullptr) cudaFree(ptr);
-        ptr = nullptr;
-        bytes = 0;
-    }
-    template <typename T>
-    T* as() const {
-        return static_cast<T*>(ptr);
-    }
-};
-
 struct TileMask {
     DeviceBuffer buf;
     uint32_t ty = 0, tx = 0;
 };
-
-uint32_t bit_length(uint32_t n) {
-    uint32_t b = 0;
-    while (n != 0u) {
-        ++b;
-        n >>= 1;
-    }
-    return b;
-}
 
 bool valid_k(int k) { return k == 0 || k == 4 || k == 8 || k == 12 || k == 16 || k == 24 || k == 32; }
 
@@ -170,31 +110,6 @@ struct StageTimer {
     }
 };
 
-void prepare_pose(const float* pose7, gf::Pose& out) {
-    // Same double-precision construction as the oracle's oracle_prepare_pose:
-    // world->sensor rotation of quaternion (x, y, z, w), its transpose, and the
-    // sensor centre c = -R^T t.
-    const double tx = pose7[0], ty = pose7[1], tz = pose7[2];
-    const double x = pose7[3], y = pose7[4], z = pose7[5], w = pose7[6];
-    double R[9];
-    R[0] = 1.0 - 2.0 * (y * y + z * z);
-    R[1] = 2.0 * (x * y - w * z);
-    R[2] = 2.0 * (x * z + w * y);
-    R[3] = 2.0 * (x * y + w * z);
-    R[4] = 1.0 - 2.0 * (x * x + z * z);
-    R[5] = 2.0 * (y * z - w * x);
-    R[6] = 2.0 * (x * z - w * y);
-    R[7] = 2.0 * (y * z + w * x);
-    R[8] = 1.0 - 2.0 * (x * x + y * y);
-    for (int i = 0; i < 9; ++i) out.R[i] = float(R[i]);
-    out.t[0] = float(tx);
-    out.t[1] = float(ty);
-    out.t[2] = float(tz);
-    for (int r = 0; r < 3; ++r)
-        for (int c = 0; c < 3; ++c) out.Rinv[3 * r + c] = out.R[3 * c + r];
-    for (int r = 0; r < 3; ++r) out.c[r] = float(-(R[0 * 3 + r] * tx + R[1 * 3 + r] * ty + R[2 * 3 + r] * tz));
-}
-
 int bind_device(gf_tracer* t) {
     int dev = -1;
     GF_CUDA(cudaGetDevice(&dev));
@@ -239,47 +154,11 @@ int validate_inputs(const gf_tracer* t, const gf_trace_inputs* in, const TileMas
 
 template <typename In, typename Out>
 int exclusive_scan(gf_tracer* t, const In* in, uint64_t n, Out* out, Out* grandTotal, cudaStream_t stream) {
-    const uint32_t tiles = uint32_t((n + gf::kScanTile - 1) / gf::kScanTile);
-    if (tiles == 0) {
-        GF_CUDA(cudaMemsetAsync(grandTotal, 0, sizeof(Out), stream));
-        return GF_OK;
-    }
-    if (int e = t->scanTiles.ensure(sizeof(Out) * tiles, stream)) return e;
-    Out* ts = t->scanTiles.as<Out>();
-    gf::k_scan_reduce<In, Out><<<tiles, gf::kScanThreads, 0, stream>>>(in, n, ts);
-    gf::k_scan_tiles<Out><<<1, gf::kScanThreads, 0, stream>>>(ts, tiles, grandTotal);
-    gf::k_scan_downsweep<In, Out><<<tiles, gf::kScanThreads, 0, stream>>>(in, n, ts, out);
-    t->launches += 3;
-    GF_LAUNCH_CHECK();
-    return GF_OK;
+    return scan_exclusive<In, Out>(t->scanTiles, t->launches, in, n, out, grandTotal, stream);
 }
 
 int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream) {
-    t->finalBuf = 0;
-    if (n == 0) return GF_OK;
-    const uint32_t blocks = (n + gf::kSortTile - 1) / gf::kSortTile;
-    if (int e = t->hist.ensure(sizeof(uint32_t) * (size_t(blocks) * gf::kRadixBins + 1), stream)) return e;
-    uint32_t* hist = t->hist.as<uint32_t>();
-    const int smem = int(sizeof(gf::SortScatterSmem));
-    GF_CUDA(cudaFuncSetAttribute(gf::k_radix_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    int src = 0;
-    for (int shift = 0; shift < endBit; shift += 8) {
-        gf::k_radix_histogram<<<blocks, gf::kSortThreads, 0, stream>>>(t->keys[src].as<uint64_t>(), n, shift, blocks,
-                                                                      hist);
-        t->launches += 1;
-        GF_LAUNCH_CHECK();
-        if (int e = exclusive_scan<uint32_t, uint32_t>(t, hist, uint64_t(blocks) * gf::kRadixBins, hist,
-                                                        hist + size_t(blocks) * gf::kRadixBins, stream))
-            return e;
-        gf::k_radix_scatter<<<blocks, gf::kSortThreads, smem, stream>>>(
-            t->keys[src].as<uint64_t>(), t->ids[src].as<uint32_t>(), t->keys[src ^ 1].as<uint64_t>(),
-            t->ids[src ^ 1].as<uint32_t>(), n, shift, blocks, hist);
-        t->launches += 1;
-        GF_LAUNCH_CHECK();
-        src ^= 1;
-    }
-    t->finalBuf = src;
-    return GF_OK;
+    return sort_pairs(t->hist, t->scanTiles, t->launches, t->keys, t->ids, n, 0, endBit, &t->finalBuf, stream);
 }
 
 template <int K>

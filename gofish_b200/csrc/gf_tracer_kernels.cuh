@@ -81,42 +81,7 @@ __device__ __forceinline__ uint32_t for_admitted_tiles(const FrameArgs& f, const
 
 // One thread per particle: UT projection, conic, admitted-tile count, SH
 // radiance, and the 64-byte render record (reference projectOnTiles,
-// gutProjector.cuh:653-286).
-// Radius of a sphere around mu that contains the particle's 3-sigma ellipsoid
-// {x : |B^-1 (x - mu)| <= 3}: 3 / sigma_min(B^-1), from the smallest
-// eigenvalue of B^-T B^-1 (closed-form trigonometric solution, double
-// precision), inflated by 1%.  Returns +inf when the bound is not reliable.
-__device__ __forceinline__ float support_radius(const float* Binv) {
-    double m[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) m[i] = double(Binv[i]);
-    // S = M^T M
-    double s00 = 0, s01 = 0, s02 = 0, s11 = 0, s12 = 0, s22 = 0;
-#pragma unroll
-    for (int r = 0; r < 3; ++r) {
-        const double a = m[3 * r], b = m[3 * r + 1], c = m[3 * r + 2];
-        s00 += a * a; s01 += a * b; s02 += a * c; s11 += b * b; s12 += b * c; s22 += c * c;
-    }
-    const double q = (s00 + s11 + s22) / 3.0;
-    const double p1 = s01 * s01 + s02 * s02 + s12 * s12;
-    const double p2 = (s00 - q) * (s00 - q) + (s11 - q) * (s11 - q) + (s22 - q) * (s22 - q) + 2.0 * p1;
-    double lmin, lmax;
-    if (p2 <= 1e-30 * q * q) {
-        lmin = lmax = q;
-    } else {
-        const double pp = sqrt(p2 / 6.0);
-        const double b00 = (s00 - q) / pp, b11 = (s11 - q) / pp, b22 = (s22 - q) / pp;
-        const double b01 = s01 / pp, b02 = s02 / pp, b12 = s12 / pp;
-        const double det = b00 * (b11 * b22 - b12 * b12) - b01 * (b01 * b22 - b12 * b02) + b02 * (b01 * b12 - b11 * b02);
-        const double r = fmin(1.0, fmax(-1.0, 0.5 * det));
-        const double phi = acos(r) / 3.0;
-        lmax = q + 2.0 * pp * cos(phi);
-        lmin = q + 2.0 * pp * cos(phi + 2.0943951023931957);  // + 2 pi / 3
-    }
-    if (!(lmin > 1e-9 * lmax) || !(lmax < 1e300)) return __int_as_float(0x7f800000);
-    return float(3.03 / sqrt(lmin)) * 1.0001f + 1e-6f;
-}
-
+// gutProjector.cuh:653-945).
 __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __restrict__ particles,
                                                  const float* __restrict__ features,
                                                  const uint8_t* __restrict__ mask, float4* __restrict__ proj,

@@ -78,6 +78,7 @@ def load():
                                          vp]),
         "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
         "oracle_visibility": (i32, [i32, vp, vp]),
+        "oracle_field_camera": (i32, [cam_p, pose_p, i32, vp, vp, vp, i32, vp, vp, vp]),
         "oracle_num_threads": (i32, []),
         "oracle_expf": (f32, [f32]),
         "oracle_logf": (f32, [f32]),
@@ -235,3 +236,52 @@ def trace_backward(cam, fwd, particles, sh, sh_degree, ray_o, ray_d, mask, k, gr
                           fwd["rgba"], fwd["hit_t"], grad_rgba, grad_hit_t, tiles)
     gp, gs = project_backward(fwd["pose"], particles, sh, sh_degree, fwd["counts"], rec)
     return gp, gs, rec
+
+
+def field_camera(cam, pose7, particles, ray_o, points, pixel_mask=None):
+    """One camera of the opacity field: (opacity [Q] float32, observed [Q] uint8)."""
+    lib = load()
+    pose = prepare_pose(pose7)
+    points = np.ascontiguousarray(points, dtype=np.float32).reshape(-1, 3)
+    q = points.shape[0]
+    opacity = np.zeros(q, dtype=np.float32)
+    observed = np.zeros(q, dtype=np.uint8)
+    mask = None if pixel_mask is None else np.ascontiguousarray(pixel_mask, dtype=np.uint8)
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    ray_o = np.ascontiguousarray(ray_o, dtype=np.float32)
+    lib.oracle_field_camera(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles), _p(ray_o),
+                            None if mask is None else _p(mask), q, _p(points), _p(opacity), _p(observed))
+    return opacity, observed
+
+
+def evaluate_field(views, particles, points):
+    """Camera-min field over views, each (cam, pose7, ray_o, pixel_mask or None).
+
+    Returns (opacity [Q] with 0 where unobserved, observed [Q], above [Q]):
+    the outputs of the reference's finish_opacity_field
+    (opacityFieldBinding.inl:318-338)."""
+    q = np.asarray(points).reshape(-1, 3).shape[0]
+    minimum = np.ones(q, dtype=np.float32)
+    observed = np.zeros(q, dtype=np.uint8)
+    for cam, pose7, ray_o, mask in views:
+        op, ob = field_camera(cam, pose7, particles, ray_o, points, mask)
+        first = (ob != 0) & (observed == 0)
+        both = (ob != 0) & (observed != 0)
+        minimum[first] = op[first]
+        minimum[both] = np.minimum(minimum[both], op[both])
+        observed |= ob
+    opacity = np.where(observed != 0, minimum, np.float32(0.0)).astype(np.float32)
+    above = ((observed != 0) & (opacity >= np.float32(0.5))).astype(np.uint8)
+    return opacity, observed, above
+
+
+def bisection_round(views, particles, points):
+    """One bisection round's (above, observed, exact) vectors.
+
+    The reference's tie-aware round (bisectionTableImpl.inl:222-357) stops a
+    camera once its opacity is strictly above 1/2 and then classifies; since
+    T only decreases, that equals: above = observed and min >= 1/2, exact =
+    observed and min == 1/2, with min the camera-min field."""
+    opacity, observed, above = evaluate_field(views, particles, points)
+    exact = ((observed != 0) & (opacity == np.float32(0.5))).astype(np.uint8)
+    return above, observed, exact

@@ -1012,6 +1012,56 @@ int oracle_visibility(int N, const uint32_t* counts, uint32_t* visibility) {
 
 int oracle_num_threads(void) { return worker_count(); }
 
+// ------------------------------------------------------------------ mesh opacity field
+// One camera of the matched camera-min opacity field (gofish/mesh/field.py:4-11;
+// opacityField.cuh:699-745 preprocessPoints, :775-829 integratePoints,
+// :172-185 fixed8ResponseAlphaUpdate).  The reference's candidate admission
+// is complete (native UT union certified support cap), so its product equals
+// the product over every particle whose hit test passes on the segment
+// [0, t_query], in ascending particle id; this restatement evaluates exactly
+// that by brute force.  For each query point: opacity[q] = 1 - prod(1 - alpha)
+// and observed[q] = 1 when the point projects into the raster, onto an
+// unmasked pixel, at a positive finite range; otherwise observed[q] = 0.
+int oracle_field_camera(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                        const float* rayO, const uint8_t* pixelMask, int Q, const float* points, float* opacity,
+                        uint8_t* observed) {
+    const int W = cam->width, H = cam->height;
+    parallel_for(0, Q, 256, [&](int q, int) {
+        opacity[q] = 0.0f;
+        observed[q] = 0u;
+        const float3_ x = f3(points[3 * size_t(q)], points[3 * size_t(q) + 1], points[3 * size_t(q) + 2]);
+        float2_ pr;
+        if (!project_world(*cam, *pose, x, pr)) return;
+        // requireRasterBounds with zero tolerance (cameraProjections.cuh:69-73)
+        if (!(pr.x >= 0.0f && pr.y >= 0.0f && pr.x < float(W) && pr.y < float(H))) return;
+        const int px = int(floorf(pr.x)), py = int(floorf(pr.y));
+        if (px < 0 || py < 0 || px >= W || py >= H) return;
+        const size_t pix = size_t(px) + size_t(W) * size_t(py);
+        if (pixelMask != nullptr && pixelMask[pix] == 0u) return;
+        const float3_ os = f3(rayO[3 * pix], rayO[3 * pix + 1], rayO[3 * pix + 2]);
+        const float3_ o = add(matvec(pose->Rinv, os), f3(pose->c[0], pose->c[1], pose->c[2]));
+        const float3_ delta = sub(x, o);
+        const float range = sqrtf(dot(delta, delta));
+        if (!(range > 0.0f) || !gf::isfinite_f(range)) return;
+        Ray ray;
+        ray.o = o;
+        ray.d = f3(delta.x / range, delta.y / range, delta.z / range);
+        ray.tmin = 0.0f;
+        ray.tmax = range;
+        ray.valid = true;
+        float T = 1.0f;
+        for (int i = 0; i < N; ++i) {
+            const Particle P = load_particle(particles + 32 * size_t(i));
+            float alpha, hitT, resp;
+            HalfRay h;
+            if (hit_test(ray, P, alpha, hitT, resp, h)) T = T * (1.0f - alpha);
+        }
+        opacity[q] = 1.0f - T;
+        observed[q] = 1u;
+    });
+    return 0;
+}
+
 // Exported scalar elementary functions, for the accuracy tests.
 float oracle_expf(float x) { return gf::gf_expf(x); }
 float oracle_logf(float x) { return gf::gf_logf(x); }

@@ -93,6 +93,32 @@ class GfTraceStats(ctypes.Structure):
     ]
 
 
+class GfFieldCamera(ctypes.Structure):
+    _fields_ = [
+        ("frame_number", ctypes.c_uint32),
+        ("reserved0", ctypes.c_uint32),
+        ("camera", GfCamera),
+        ("ray_origin", ctypes.c_void_p),
+        ("pixel_mask", ctypes.c_void_p),
+        ("timestamp_start", ctypes.c_int64),
+        ("timestamp_end", ctypes.c_int64),
+        ("pose_start", ctypes.c_float * 7),
+        ("pose_end", ctypes.c_float * 7),
+    ]
+
+
+class GfFieldStats(ctypes.Structure):
+    _fields_ = [
+        ("evaluations", ctypes.c_uint64),
+        ("pairs", ctypes.c_uint64),
+        ("cameras", ctypes.c_uint64),
+        ("kernel_launches", ctypes.c_uint64),
+        ("reserved", ctypes.c_uint64 * 4),
+    ]
+
+
+_vp, _u32, _i64p = ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int64)
+
 # (name, restype, argtypes) of every exported symbol of include/gofish_b200.h.
 _SIGNATURES = [
     ("gf_abi_version", ctypes.c_int, []),
@@ -116,6 +142,19 @@ _SIGNATURES = [
     ("gf_sort_tile_keys_static", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int,
       ctypes.c_void_p]),
+    ("gf_field_create", _vp, []),
+    ("gf_field_destroy", None, [_vp]),
+    ("gf_field_begin", ctypes.c_int, [_vp, _vp, _vp, _u32, _vp, _u32, _i64p, _vp]),
+    ("gf_field_integrate_camera", ctypes.c_int, [_vp, ctypes.c_int64, ctypes.POINTER(GfFieldCamera), _vp]),
+    ("gf_field_finish", ctypes.c_int, [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp]),
+    ("gf_field_release", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
+    ("gf_field_begin_table", ctypes.c_int, [_vp, _vp, _vp, _u32, _vp, _u32, _i64p, _vp]),
+    ("gf_field_stage_camera", ctypes.c_int, [_vp, ctypes.c_int64, ctypes.POINTER(GfFieldCamera), _vp]),
+    ("gf_field_seal_table", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
+    ("gf_field_evaluate_round", ctypes.c_int, [_vp, ctypes.c_int64, _vp, _u32, _u32, _vp, _vp, _vp, _vp]),
+    ("gf_field_reset_batch", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
+    ("gf_field_release_table", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
+    ("gf_field_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(GfFieldStats)]),
 ]
 
 STATIC_SORT_MAX_PAIRS = 262144

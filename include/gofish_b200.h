@@ -212,6 +212,85 @@ int gf_tracer_copy_intermediates(const gf_tracer* tracer, float* projected, floa
 int gf_sort_tile_keys_static(const uint64_t* keys_in, const uint32_t* ids_in, uint64_t* keys_out, uint32_t* ids_out,
                              uint32_t n, int end_bit, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Mesh opacity field.  Replaces the reference's mesh SplatRaster methods
+ * (gofish/mesh/native/bindings.cpp:84-114, implemented in
+ * gofish/mesh/native/include/3dgut/kernels/cuda/common/opacityFieldBinding.inl).
+ *
+ * O_v(x) = 1 - prod(1 - alpha_i) over every Gaussian i whose hit test passes
+ * on the segment from camera v's centre to x, in ascending Gaussian id; the
+ * field is the minimum of O_v over the cameras that observe x (x projects
+ * into the raster, onto an unmasked pixel, at a positive range).
+ * ------------------------------------------------------------------------ */
+
+/* One camera: the arguments of integrate_opacity_field_camera and
+ * stage_bisection_camera (bindings.cpp:87-105).  Global shutter only, with
+ * identical finite start and end poses (opacityFieldBinding.inl:170-196).
+ * Every pixel's ray origin must be the same point (one camera centre per
+ * view); a point that lands on a pixel with another origin makes
+ * gf_field_finish / gf_field_evaluate_round fail. */
+typedef struct gf_field_camera {
+    uint32_t frame_number;
+    uint32_t reserved0;
+    gf_camera camera;            /* width x height is the ray raster */
+    const float* ray_origin;     /* device [H,W,3], sensor frame */
+    const uint8_t* pixel_mask;   /* device [H,W] physical-domain mask, or NULL */
+    int64_t timestamp_start;
+    int64_t timestamp_end;
+    float pose_start[7];         /* world -> sensor [t, q(x,y,z,w)] */
+    float pose_end[7];
+} gf_field_camera;
+
+typedef struct gf_field gf_field;
+
+typedef struct gf_field_stats {
+    uint64_t evaluations;      /* (point, camera) evaluations integrated so far */
+    uint64_t pairs;            /* (cell, Gaussian) candidate pairs so far */
+    uint64_t cameras;          /* camera passes so far */
+    uint64_t kernel_launches;  /* kernels launched so far */
+    uint64_t reserved[4];
+} gf_field_stats;
+
+gf_field* gf_field_create(void);
+void gf_field_destroy(gf_field* field);
+
+/* begin_opacity_field (opacityFieldBinding.inl:203-268): copies the packed
+ * Gaussians [N,32] (positions 0-2, density 3, B^-1 row-major 21-29) and the
+ * query points [Q,3]; sigma_max [N] is validated but the support bound is
+ * derived from B^-1 itself.  N > 0, Q > 0.  One context at a time. */
+int gf_field_begin(gf_field* field, const float* particles, const float* sigma_max, uint32_t num_particles,
+                   const float* points, uint32_t num_points, int64_t* token, void* stream);
+/* integrate_opacity_field_camera (opacityFieldBinding.inl:270-316). */
+int gf_field_integrate_camera(gf_field* field, int64_t token, const gf_field_camera* camera, void* stream);
+/* finish_opacity_field (opacityFieldBinding.inl:318-338): opacity [Q] (0 where
+ * unobserved), observed [Q], above [Q] = observed and opacity >= 1/2. */
+int gf_field_finish(gf_field* field, int64_t token, float* opacity, uint8_t* observed, uint8_t* above,
+                    void* stream);
+/* release_opacity_field (opacityFieldBinding.inl:340-347). */
+int gf_field_release(gf_field* field, int64_t token, void* stream);
+
+/* begin_bisection_table (opacityFieldBinding.inl:349-368): as gf_field_begin;
+ * the probe points fix the round capacity Q. */
+int gf_field_begin_table(gf_field* field, const float* particles, const float* sigma_max, uint32_t num_particles,
+                         const float* probe_points, uint32_t num_points, int64_t* token, void* stream);
+/* stage_bisection_camera (opacityFieldBinding.inl:370-431): copies the
+ * camera's ray origins and mask. */
+int gf_field_stage_camera(gf_field* field, int64_t token, const gf_field_camera* camera, void* stream);
+/* seal_bisection_table (opacityFieldBinding.inl:433-478). */
+int gf_field_seal_table(gf_field* field, int64_t token, void* stream);
+/* evaluate_bisection_round (opacityFieldBinding.inl:480-521): rounds run in
+ * order 0..7 over Q points; above = observed and no camera below 1/2, exact =
+ * above and the minimum equals 1/2 exactly; all [Q] uint8.  Synchronizes the
+ * stream once, as the reference does. */
+int gf_field_evaluate_round(gf_field* field, int64_t token, const float* points, uint32_t num_points,
+                            uint32_t round, uint8_t* above, uint8_t* observed, uint8_t* exact, void* stream);
+/* reset_bisection_batch (opacityFieldBinding.inl:523-531): after round 7. */
+int gf_field_reset_batch(gf_field* field, int64_t token, void* stream);
+/* release_bisection_table (opacityFieldBinding.inl:533-545): after round 7. */
+int gf_field_release_table(gf_field* field, int64_t token, void* stream);
+/* Counters of work done.  No reference counterpart (bench accounting). */
+int gf_field_get_stats(const gf_field* field, gf_field_stats* stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,7 +42,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
-    p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale"], default="single_view")
+    p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale", "mesh_query"],
+                   default="single_view")
+    p.add_argument("--views", type=int, default=None, help="override the mesh query's view count")
+    p.add_argument("--edges", type=int, default=50_000_000, help="bisection edges of the mesh query (0: skip)")
     p.add_argument("--views-per-gpu", type=int, default=8, help="views per rank and step (multi_view)")
     p.add_argument("--num-gaussians", type=int, default=None, help="override the workload's Gaussian count")
     p.add_argument("--size", type=int, default=None, help="override the raster size")
@@ -357,6 +360,233 @@ def run_gpu(args):
         print(json.dumps(result), flush=True)
 
 
+# ----------------------------------------------------------------------------- mesh opacity query
+MESH_METRIC = "mesh opacity queries/s"
+MESH_UNIT = "Mqueries/s"  # million (point, view) evaluations per second
+# Algorithmic bytes of the ordered-integration kernel: per staged candidate
+# its id (4) and records (cull 16 + hit 64); per point its sorted index (4),
+# direction + range (16), camera-min read + write (8) and observed (2).
+FIELD_BYTES_PER_CANDIDATE = 4 + 16 + 64
+FIELD_BYTES_PER_POINT = 4 + 16 + 8 + 2
+
+
+def mesh_workload(args):
+    from gofish_b200 import scene as sc
+    from gofish_b200.mesh.cameras import fisheye_training_camera
+    from gofish_b200.mesh.shape import effective_shape
+    from gofish_b200.mesh.sites import generate_sites
+
+    kw = {}
+    if args.num_gaussians:
+        kw["n"] = args.num_gaussians
+    if args.size:
+        kw["size"] = args.size
+    if args.views:
+        kw["views"] = args.views
+    w = sc.workload_mesh_query(**kw)
+    shape = effective_shape(w.scene.positions, w.scene.scales, w.scene.rotations, w.scene.density)
+    points = generate_sites(shape).points
+    cameras = [fisheye_training_camera(v, w.camera, pose, masked=True) for v, pose in enumerate(w.poses)]
+    return w, shape, points, cameras
+
+
+def mesh_config(w, points_total: int, world: int, edges: int) -> dict:
+    cam = w.camera
+    return {
+        "workload": w.name, "gaussians": w.scene.num, "query_points": int(points_total),
+        "views": len(w.poses), "camera": f"OPENCV_FISHEYE equidistant 200deg {cam.width}x{cam.height}, 2 m ring",
+        "bisection_edges": int(edges), "bisection_rounds": 8,
+        "l2_policy": "inputs larger than L2 (27M points + 3M packed Gaussians + per-view records > 126 MB)",
+        "parallelism": f"points sharded over {world} GPUs, no collective" if world > 1 else "single GPU",
+    }
+
+
+def run_mesh(args):
+    import torch
+    import torch.distributed as dist
+
+    from gofish_b200.mesh import SplatRaster
+    from gofish_b200.mesh.bisection import refine_crossings
+    from gofish_b200.mesh.field import camera_inputs, evaluate_field, signed_field
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+
+    w, shape, points_all, cameras = mesh_workload(args)
+    q_total = points_all.shape[0]
+    lo, hi = q_total * rank // world, q_total * (rank + 1) // world
+    points = np.ascontiguousarray(points_all[lo:hi])
+    views = len(cameras)
+
+    raster = SplatRaster()
+    packed = torch.from_numpy(shape.packed_density()).to(device)
+    sigma = torch.from_numpy(np.ascontiguousarray(shape.sigma_max)).to(device)
+    query = torch.from_numpy(points).to(device)
+    cam_args = [camera_inputs(c, device) for c in cameras]
+
+    def field_pass():
+        token = raster.begin_opacity_field(packed, sigma, query)
+        for a in cam_args:
+            raster.integrate_opacity_field_camera(token, *a)
+        out = raster.finish_opacity_field(token)
+        raster.release_opacity_field(token)
+        return out
+
+    for _ in range(args.warmup):
+        field_pass()
+    torch.cuda.synchronize(device)
+
+    stats0 = raster.stats()
+    raster.collect_stage_times()
+    raster.enable_stage_timing(True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        out = field_pass()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    clock_info = clocks.stop()
+    raster.enable_stage_timing(False)
+    stages = raster.collect_stage_times()
+    stats1 = raster.stats()
+    elapsed = torch.tensor([t0.elapsed_time(t1)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(elapsed.item())
+    value = q_total * views * args.steps / (elapsed_ms / 1000.0) / 1e6
+    minimum, observed = out[0].cpu().numpy(), out[1].cpu().numpy()
+
+    # --- roofline of the ordered-integration kernel
+    peak, peak_kind = measured_peaks()
+    integ_ms, integ_launches = stages["integrate"]
+    integ_launches = max(1, integ_launches)
+    cand = stats1.candidate_loads - stats0.candidate_loads
+    evals = stats1.evaluations - stats0.evaluations
+    tests = stats1.hit_tests - stats0.hit_tests
+    hits = stats1.hits - stats0.hits
+    iters = stats1.warp_iterations - stats0.warp_iterations
+    alg = (cand * FIELD_BYTES_PER_CANDIDATE + evals * FIELD_BYTES_PER_POINT) / integ_launches
+    avg_s = integ_ms / integ_launches / 1000.0
+    achieved = alg / avg_s / 1e9
+    roofline = {"kernel": "k_field_integrate<false>", "bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "alg_bytes_per_launch": int(alg),
+                "avg_launch_ms": round(avg_s * 1000.0, 4),
+                "hit_tests_per_launch": int(tests / integ_launches),
+                "hits_per_launch": int(hits / integ_launches),
+                "warp_iterations_per_launch": int(iters / integ_launches),
+                "hit_tests_per_s": round(tests / (integ_ms / 1000.0), 1) if integ_ms > 0 else None}
+
+    # --- end to end through evaluate_field with host inputs and host results
+    e2e = None
+    if not args.no_e2e:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        evaluate_field(raster, shape, cameras, points, device)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0.record(stream)
+        for _ in range(args.steps):
+            evaluate_field(raster, shape, cameras, points, device)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        h2d = packed.numel() * 4 + sigma.numel() * 4 + points.nbytes
+        for c in cameras:
+            h2d += c.ray_direction.numel() * 4 + 12 + (0 if c.physical_mask is None else c.physical_mask.numel())
+        e2e = {"value": round(q_total * views * args.steps / (float(ems.item()) / 1000.0) / 1e6, 3),
+               "unit": MESH_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(points.shape[0] * 5)}
+
+    # --- bisection of crossing edges (pairs of this rank's solid and free sites)
+    bisection = None
+    if args.edges > 0:
+        f = signed_field(minimum, observed)
+        solid, free = np.flatnonzero(f <= 0), np.flatnonzero(f > 0)
+        e_local = args.edges * (rank + 1) // world - args.edges * rank // world
+        if solid.size and free.size and e_local > 0:
+            rng = np.random.default_rng(4242 + rank)
+            a, b = rng.choice(solid, e_local), rng.choice(free, e_local)
+            endpoints = np.ascontiguousarray(np.stack([points[a], points[b]], axis=1), dtype=np.float32)
+            fields = np.ascontiguousarray(np.stack([f[a], f[b]], axis=1), dtype=np.float32)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record(stream)
+            refine_crossings(raster, shape, cameras, endpoints, fields, device)
+            b1.record(stream)
+            torch.cuda.synchronize(device)
+            bms = torch.tensor([b0.elapsed_time(b1)], device=device, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(bms, op=dist.ReduceOp.MAX)
+            bms = float(bms.item())
+            bisection = {"edges": int(args.edges), "rounds": 8, "ms": round(bms, 2),
+                         "value": round(args.edges * 8 * views / (bms / 1000.0) / 1e6, 3), "unit": MESH_UNIT,
+                         "note": "refine_crossings end to end (host endpoints in, host vertices out)"}
+
+    result = {
+        "metric": MESH_METRIC, "value": round(value, 3), "unit": MESH_UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
+        "config": mesh_config(w, q_total, world, args.edges), "e2e": e2e, "roofline": roofline,
+        "gpu_launches": int((stats1.kernel_launches - stats0.kernel_launches)),
+        "points_per_s": round(q_total * args.steps / (elapsed_ms / 1000.0), 1),
+        "stage_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in stages.items()},
+        "candidate_pairs_per_view": int((stats1.pairs - stats0.pairs) / max(1, args.steps * views)),
+        "observed_fraction": round(float(observed.mean()), 4), "bisection": bisection,
+    }
+    if clock_info is not None:
+        result["clocks"] = clock_info
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = mesh_cpu_baseline(w, shape, points_all, cameras)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def mesh_cpu_baseline(w, shape, points, cameras, budget_s: float = 15.0) -> dict:
+    """Times the oracle's field (scalar C++, every Gaussian tested per point,
+    as the restatement of the reference's complete admission) on a sample of
+    points and views; reports (point, view) evaluations per second."""
+    import oracle
+
+    cam = w.camera
+    ocam = oracle.camera(1, cam.width, cam.height, cam.principal, cam.focal, cam.coefficients, cam.max_angle)
+    packed = shape.packed_density()
+    ray_o = np.zeros((cam.height, cam.width, 3), np.float32)
+    rng = np.random.default_rng(99)
+    sample = 16
+    spent, evals = 0.0, 0
+    while spent < budget_s / 2:
+        pts = points[rng.choice(points.shape[0], sample, replace=False)]
+        t = time.perf_counter()
+        for c in cameras[:2]:
+            oracle.field_camera(ocam, c.poses.T_world_sensors[0].numpy(), packed, ray_o, pts,
+                                c.physical_mask.numpy())
+        spent += time.perf_counter() - t
+        evals += 2 * sample
+        sample *= 2
+    return {"value": round(evals / spent / 1e6, 6), "unit": MESH_UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{evals} (point, view) evaluations of random sites over 2 views, every one of "
+                      f"{w.scene.num} Gaussians tested per point ({spent:.1f} s)"}
+
+
 # ----------------------------------------------------------------------------- CPU (oracle) arm
 def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
     """Times the oracle (scalar C++ restatement of the reference equations) on
@@ -414,9 +644,30 @@ def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
                        "frame")}
 
 
+def run_reference_mesh(args):
+    w, shape, points, cameras = mesh_workload(args)
+    values, base = [], None
+    for i in range(args.warmup + args.steps):
+        base = mesh_cpu_baseline(w, shape, points, cameras, budget_s=4.0)
+        if i >= args.warmup:
+            values.append(base["value"])
+    value = float(np.median(values))
+    print(json.dumps({
+        "metric": MESH_METRIC, "value": round(value, 6), "unit": MESH_UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded scene, see config)", "impl": "reference",
+        "config": mesh_config(w, points.shape[0], 1, args.edges), "cpu_baseline": {**base, "value": round(value, 6)},
+        "e2e": {"value": round(value, 6), "unit": MESH_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "mesh_query":
+        run_reference_mesh(args)
         return
     w, poses = build_workload(args, 0)
     pose = poses[0]
@@ -444,6 +695,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mesh_query":
+        run_mesh(args)
     else:
         run_gpu(args)
 

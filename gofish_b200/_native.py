@@ -113,8 +113,14 @@ class GfFieldStats(ctypes.Structure):
         ("pairs", ctypes.c_uint64),
         ("cameras", ctypes.c_uint64),
         ("kernel_launches", ctypes.c_uint64),
-        ("reserved", ctypes.c_uint64 * 4),
+        ("candidate_loads", ctypes.c_uint64),
+        ("hit_tests", ctypes.c_uint64),
+        ("hits", ctypes.c_uint64),
+        ("warp_iterations", ctypes.c_uint64),
     ]
+
+
+FIELD_STAGES = ("points", "cones", "candidates", "sort", "integrate", "finish")
 
 
 _vp, _u32, _i64p = ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int64)
@@ -155,6 +161,8 @@ _SIGNATURES = [
     ("gf_field_reset_batch", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
     ("gf_field_release_table", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
     ("gf_field_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(GfFieldStats)]),
+    ("gf_field_enable_timing", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("gf_field_collect_times", ctypes.c_int, [_vp, _vp, _vp]),
 ]
 
 STATIC_SORT_MAX_PAIRS = 262144

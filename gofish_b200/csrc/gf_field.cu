@@ -58,15 +58,28 @@ struct gf_field {
     DeviceBuffer posd, binv, points, minimum, observed, active, exact, err;
     DeviceBuffer pixKey, info, sorted, hist, pointStart, coneA, coneB, cellBlocks, blockStart;
     DeviceBuffer cull, hit, counts, offsets, totals, keys[2], ids[2], sortHist, scanTiles, cellRanges;
+    DeviceBuffer bigList, bigCount;  // Gaussians binned by warps (over the per-thread traversal budget)
     std::vector<StagedCamera> staged;
     uint64_t* host = nullptr;  // pinned: pairs, blocks | valid points, error flag
     uint32_t launches = 0;
     gf_field_stats stats{};
+    DeviceBuffer counters;  // u64 [4]: candidates staged, exact hit tests, hits, warp candidate iterations
+
+    // Per-stage event timing (gf_field_enable_timing).
+    bool timing = false;
+    struct StageEvent {
+        int stage;
+        uint32_t launches;
+        cudaEvent_t start, end;
+    };
+    std::vector<StageEvent> pending;
+    std::vector<cudaEvent_t> eventPool;
 };
 
 namespace {
 
 constexpr uint32_t kMaxRaster = 32768;
+constexpr uint32_t kBigBlocks = 148 * 8;  // warp-cooperative binning grid (8 warps per block)
 
 #define GF_TRY(...)                           \
     do {                                      \
@@ -94,6 +107,40 @@ int require_context(gf_field* f, int64_t token, cudaStream_t stream, const char*
         return fail(GF_ERR_STATE, "%s: the opacity field must run on the stream it was created on", operation);
     return GF_OK;
 }
+
+cudaEvent_t take_event(gf_field* f) {
+    if (!f->eventPool.empty()) {
+        cudaEvent_t e = f->eventPool.back();
+        f->eventPool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    return e;
+}
+
+// Brackets one stage with events (when timing is on) and attributes the
+// kernels launched inside it.
+struct StageTimer {
+    gf_field* f;
+    int stage;
+    cudaStream_t stream;
+    uint32_t launches0;
+    cudaEvent_t start = nullptr;
+    StageTimer(gf_field* f_, int stage_, cudaStream_t s) : f(f_), stage(stage_), stream(s), launches0(f_->launches) {
+        if (f->timing) {
+            start = take_event(f);
+            if (start != nullptr) cudaEventRecord(start, stream);
+        }
+    }
+    ~StageTimer() {
+        if (start == nullptr) return;
+        cudaEvent_t end = take_event(f);
+        if (end == nullptr) return;
+        cudaEventRecord(end, stream);
+        f->pending.push_back({stage, f->launches - launches0, start, end});
+    }
+};
 
 bool finite7(const float* p) {
     for (int k = 0; k < 7; ++k)
@@ -129,7 +176,7 @@ int make_levels(uint32_t W, uint32_t H, gf::field::Levels& L, uint32_t& totalNod
         L.offset[L.n] = totalNodes;
         totalNodes += gx * gy;
         ++L.n;
-        if (gx * gy <= uint32_t(gf::field::kMaxTopNodes)) break;
+        if (gx * gy == 1u) break;
         gx = (gx + gf::field::kFan - 1) / gf::field::kFan;
         gy = (gy + gf::field::kFan - 1) / gf::field::kFan;
     }
@@ -163,6 +210,8 @@ int run_camera(gf_field* f, const CameraView& v, bool round, const float* points
     GF_TRY(f->offsets.ensure(sizeof(uint64_t) * N, s));
     GF_TRY(f->totals.ensure(sizeof(uint64_t) * 2, s));
     GF_TRY(f->cellRanges.ensure(sizeof(uint2) * cells, s));
+    GF_TRY(f->bigList.ensure(sizeof(uint32_t) * N, s));
+    GF_TRY(f->bigCount.ensure(sizeof(uint32_t), s));
 
     CameraArgs a{};
     a.cam = v.cam;
@@ -178,41 +227,58 @@ int run_camera(gf_field* f, const CameraView& v, bool round, const float* points
 
     uint32_t* hist = f->hist.as<uint32_t>();
     uint32_t* pointStart = f->pointStart.as<uint32_t>();
-    GF_CUDA(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * pixKeys, s));
     const uint32_t qBlocks = (Q + 255) / 256;
-    k_field_points<<<qBlocks, 256, 0, s>>>(a, points, Q, round ? f->active.as<uint8_t>() : nullptr,
-                                           f->pixKey.as<uint32_t>(), f->info.as<float4>(), hist,
-                                           f->err.as<uint32_t>());
-    f->launches += 1;
-    GF_LAUNCH_CHECK();
-    GF_TRY(scan_exclusive<uint32_t, uint32_t>(f->scanTiles, f->launches, hist, pixKeys, pointStart,
-                                              pointStart + pixKeys, s));
-    k_field_scatter<<<qBlocks, 256, 0, s>>>(f->pixKey.as<uint32_t>(), Q, pointStart, hist, f->sorted.as<uint32_t>());
-    k_cell_cones<<<(cells * 32 + 255) / 256, 256, 0, s>>>(pointStart, f->sorted.as<uint32_t>(), f->info.as<float4>(),
-                                                         cells, f->coneA.as<float4>(), f->coneB.as<float4>());
-    f->launches += 2;
-    GF_LAUNCH_CHECK();
-    for (int l = 1; l < L.n; ++l) {
-        const uint32_t nodes = L.gx[l] * L.gy[l];
-        k_cone_reduce<<<(nodes + 255) / 256, 256, 0, s>>>(
-            f->coneA.as<float4>() + L.offset[l - 1], f->coneB.as<float4>() + L.offset[l - 1], L.gx[l - 1], L.gy[l - 1],
-            f->coneA.as<float4>() + L.offset[l], f->coneB.as<float4>() + L.offset[l], L.gx[l], L.gy[l]);
+    {
+        StageTimer st(f, GF_FIELD_STAGE_POINTS, s);
+        GF_CUDA(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * pixKeys, s));
+        k_field_points<<<qBlocks, 256, 0, s>>>(a, points, Q, round ? f->active.as<uint8_t>() : nullptr,
+                                               f->pixKey.as<uint32_t>(), f->info.as<float4>(), hist,
+                                               f->err.as<uint32_t>());
+        f->launches += 1;
+        GF_LAUNCH_CHECK();
+        GF_TRY(scan_exclusive<uint32_t, uint32_t>(f->scanTiles, f->launches, hist, pixKeys, pointStart,
+                                                  pointStart + pixKeys, s));
+        k_field_scatter<<<qBlocks, 256, 0, s>>>(f->pixKey.as<uint32_t>(), Q, pointStart, hist,
+                                                f->sorted.as<uint32_t>());
         f->launches += 1;
         GF_LAUNCH_CHECK();
     }
-    k_cell_blocks<<<(cells + 255) / 256, 256, 0, s>>>(pointStart, cells, f->cellBlocks.as<uint32_t>());
-    f->launches += 1;
-    GF_LAUNCH_CHECK();
-    uint32_t* totals32 = reinterpret_cast<uint32_t*>(f->totals.as<uint64_t>() + 1);
-    GF_TRY(scan_exclusive<uint32_t, uint32_t>(f->scanTiles, f->launches, f->cellBlocks.as<uint32_t>(), cells,
-                                              f->blockStart.as<uint32_t>(), totals32, s));
-    ParticleArgs p{f->posd.as<float4>(), f->binv.as<float4>(), N};
-    k_field_particles<<<(N + 255) / 256, 256, 0, s>>>(a, p, L, f->cull.as<float4>(), f->hit.as<float4>(),
-                                                      f->counts.as<uint32_t>());
-    f->launches += 1;
-    GF_LAUNCH_CHECK();
-    GF_TRY(scan_exclusive<uint32_t, uint64_t>(f->scanTiles, f->launches, f->counts.as<uint32_t>(), N,
-                                              f->offsets.as<uint64_t>(), f->totals.as<uint64_t>(), s));
+    {
+        StageTimer st(f, GF_FIELD_STAGE_CONES, s);
+        k_cell_cones<<<(cells * 32 + 255) / 256, 256, 0, s>>>(pointStart, f->sorted.as<uint32_t>(), f->info.as<float4>(),
+                                                             cells, f->coneA.as<float4>(), f->coneB.as<float4>());
+        f->launches += 1;
+        GF_LAUNCH_CHECK();
+        for (int l = 1; l < L.n; ++l) {
+            const uint32_t nodes = L.gx[l] * L.gy[l];
+            k_cone_reduce<<<(nodes + 255) / 256, 256, 0, s>>>(
+                f->coneA.as<float4>() + L.offset[l - 1], f->coneB.as<float4>() + L.offset[l - 1], L.gx[l - 1], L.gy[l - 1],
+                f->coneA.as<float4>() + L.offset[l], f->coneB.as<float4>() + L.offset[l], L.gx[l], L.gy[l]);
+            f->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
+        k_cell_blocks<<<(cells + 255) / 256, 256, 0, s>>>(pointStart, cells, f->cellBlocks.as<uint32_t>());
+        f->launches += 1;
+        GF_LAUNCH_CHECK();
+        uint32_t* totals32 = reinterpret_cast<uint32_t*>(f->totals.as<uint64_t>() + 1);
+        GF_TRY(scan_exclusive<uint32_t, uint32_t>(f->scanTiles, f->launches, f->cellBlocks.as<uint32_t>(), cells,
+                                                  f->blockStart.as<uint32_t>(), totals32, s));
+    }
+    {
+        StageTimer st(f, GF_FIELD_STAGE_CANDIDATES, s);
+        ParticleArgs p{f->posd.as<float4>(), f->binv.as<float4>(), N};
+        GF_CUDA(cudaMemsetAsync(f->bigCount.ptr, 0, sizeof(uint32_t), s));
+        k_field_particles<<<(N + 255) / 256, 256, 0, s>>>(a, p, L, f->cull.as<float4>(), f->hit.as<float4>(),
+                                                          f->counts.as<uint32_t>(), f->bigList.as<uint32_t>(),
+                                                          f->bigCount.as<uint32_t>());
+        k_field_big<false><<<kBigBlocks, 256, 0, s>>>(L, f->bigList.as<uint32_t>(), f->bigCount.as<uint32_t>(),
+                                                      f->cull.as<float4>(), f->hit.as<float4>(),
+                                                      f->counts.as<uint32_t>(), nullptr, nullptr, nullptr);
+        f->launches += 2;
+        GF_LAUNCH_CHECK();
+        GF_TRY(scan_exclusive<uint32_t, uint64_t>(f->scanTiles, f->launches, f->counts.as<uint32_t>(), N,
+                                                  f->offsets.as<uint64_t>(), f->totals.as<uint64_t>(), s));
+    }
     GF_CUDA(cudaMemcpyAsync(f->host, f->totals.ptr, 2 * sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
     GF_CUDA(cudaMemcpyAsync(reinterpret_cast<uint32_t*>(f->host + 2), pointStart + pixKeys, sizeof(uint32_t),
                             cudaMemcpyDeviceToHost, s));
@@ -227,29 +293,38 @@ int run_camera(gf_field* f, const CameraView& v, bool round, const float* points
         GF_TRY(f->keys[b].ensure(sizeof(uint64_t) * (pairs + 1), s));
         GF_TRY(f->ids[b].ensure(sizeof(uint32_t) * (pairs + 1), s));
     }
-    if (pairs > 0) {
-        k_field_emit<<<(N + 255) / 256, 256, 0, s>>>(L, N, f->cull.as<float4>(), f->hit.as<float4>(),
-                                                     f->counts.as<uint32_t>(), f->offsets.as<uint64_t>(),
-                                                     f->keys[0].as<uint64_t>(), f->ids[0].as<uint32_t>());
-        f->launches += 1;
-        GF_LAUNCH_CHECK();
-    }
     int finalBuf = 0;
-    GF_TRY(sort_pairs(f->sortHist, f->scanTiles, f->launches, f->keys, f->ids, uint32_t(pairs), 32,
-                      32 + int(bit_length(cells)), &finalBuf, s));
-    GF_CUDA(cudaMemsetAsync(f->cellRanges.ptr, 0, sizeof(uint2) * cells, s));
-    if (pairs > 0) {
-        k_cell_ranges<<<uint32_t((pairs + 255) / 256), 256, 0, s>>>(f->keys[finalBuf].as<uint64_t>(), uint32_t(pairs),
-                                                                    f->cellRanges.as<uint2>());
-        f->launches += 1;
-        GF_LAUNCH_CHECK();
+    {
+        StageTimer st(f, GF_FIELD_STAGE_SORT, s);
+        if (pairs > 0) {
+            k_field_emit<<<(N + 255) / 256, 256, 0, s>>>(L, N, f->cull.as<float4>(), f->hit.as<float4>(),
+                                                         f->counts.as<uint32_t>(), f->offsets.as<uint64_t>(),
+                                                         f->keys[0].as<uint64_t>(), f->ids[0].as<uint32_t>());
+            k_field_big<true><<<kBigBlocks, 256, 0, s>>>(L, f->bigList.as<uint32_t>(), f->bigCount.as<uint32_t>(),
+                                                         f->cull.as<float4>(), f->hit.as<float4>(),
+                                                         f->counts.as<uint32_t>(), f->offsets.as<uint64_t>(),
+                                                         f->keys[0].as<uint64_t>(), f->ids[0].as<uint32_t>());
+            f->launches += 2;
+            GF_LAUNCH_CHECK();
+        }
+        GF_TRY(sort_pairs(f->sortHist, f->scanTiles, f->launches, f->keys, f->ids, uint32_t(pairs), 32,
+                          32 + int(bit_length(cells)), &finalBuf, s));
+        GF_CUDA(cudaMemsetAsync(f->cellRanges.ptr, 0, sizeof(uint2) * cells, s));
+        if (pairs > 0) {
+            k_cell_ranges<<<uint32_t((pairs + 255) / 256), 256, 0, s>>>(f->keys[finalBuf].as<uint64_t>(), uint32_t(pairs),
+                                                                        f->cellRanges.as<uint2>());
+            f->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
     }
     if (blocks > 0) {
+        StageTimer st(f, GF_FIELD_STAGE_INTEGRATE, s);
         IntegrateArgs ia{};
         ia.blockStart = f->blockStart.as<uint32_t>();
         ia.cells = cells;
         ia.pointStart = pointStart;
         ia.sorted = f->sorted.as<uint32_t>();
+        ia.pixKey = f->pixKey.as<uint32_t>();
         ia.info = f->info.as<float4>();
         ia.cellRanges = f->cellRanges.as<uint2>();
         ia.candIds = f->ids[finalBuf].as<uint32_t>();
@@ -259,6 +334,7 @@ int run_camera(gf_field* f, const CameraView& v, bool round, const float* points
         ia.observed = f->observed.as<uint8_t>();
         ia.active = f->active.as<uint8_t>();
         ia.exact = f->exact.as<uint8_t>();
+        ia.counters = f->counters.as<unsigned long long>();
         if (round) k_field_integrate<true><<<blocks, kBlock, 0, s>>>(ia);
         else k_field_integrate<false><<<blocks, kBlock, 0, s>>>(ia);
         f->launches += 1;
@@ -289,6 +365,10 @@ int begin_context(gf_field* f, const float* particles, const float* sigmaMax, ui
     GF_TRY(f->active.ensure(Q, s));
     GF_TRY(f->exact.ensure(Q, s));
     GF_TRY(f->err.ensure(sizeof(uint32_t), s));
+    if (f->counters.ptr == nullptr) {
+        GF_TRY(f->counters.ensure(4 * sizeof(unsigned long long), s));
+        GF_CUDA(cudaMemsetAsync(f->counters.ptr, 0, 4 * sizeof(unsigned long long), s));
+    }
     gf::field::k_field_pack<<<(N + 255) / 256, 256, 0, s>>>(particles, N, f->posd.as<float4>(), f->binv.as<float4>());
     f->stats.kernel_launches += 1;
     GF_LAUNCH_CHECK();
@@ -343,6 +423,14 @@ void gf_field_destroy(gf_field* f) {
                                 &f->offsets,   &f->totals,     &f->keys[0],    &f->keys[1], &f->ids[0],
                                 &f->ids[1],    &f->sortHist,   &f->scanTiles,  &f->cellRanges};
         for (DeviceBuffer* b : bufs) b->release();
+        f->counters.release();
+        f->bigList.release();
+        f->bigCount.release();
+        for (auto& e : f->pending) {
+            cudaEventDestroy(e.start);
+            cudaEventDestroy(e.end);
+        }
+        for (cudaEvent_t e : f->eventPool) cudaEventDestroy(e);
         for (StagedCamera& c : f->staged) {
             c.rayO.release();
             c.mask.release();
@@ -383,10 +471,15 @@ int gf_field_finish(gf_field* f, int64_t token, float* opacity, uint8_t* observe
     if (f->cameras == 0) return fail(GF_ERR_STATE, "the opacity field has no camera");
     if (opacity == nullptr || observed == nullptr || above == nullptr)
         return fail(GF_ERR_BAD_INPUT, "output buffers must not be NULL");
-    gf::field::k_field_finish<<<(f->Q + 255) / 256, 256, 0, s>>>(f->minimum.as<float>(), f->observed.as<uint8_t>(),
-                                                                 f->Q, opacity, observed, above);
-    f->stats.kernel_launches += 1;
-    GF_LAUNCH_CHECK();
+    {
+        StageTimer st(f, GF_FIELD_STAGE_FINISH, s);
+        gf::field::k_field_finish<<<(f->Q + 255) / 256, 256, 0, s>>>(
+            f->minimum.as<float>(), f->observed.as<uint8_t>(), f->Q, opacity, observed, above);
+        f->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    f->stats.kernel_launches += f->launches;
+    f->launches = 0;
     GF_TRY(check_error_flag(f, s));
     f->finished = true;
     return GF_OK;
@@ -475,10 +568,15 @@ int gf_field_evaluate_round(gf_field* f, int64_t token, const float* points, uin
         CameraView v{c.cam, c.pose, c.rayO.as<float>(), c.masked ? c.mask.as<uint8_t>() : nullptr};
         GF_TRY(run_camera(f, v, true, points, s));
     }
-    gf::field::k_round_finalize<<<(f->Q + 255) / 256, 256, 0, s>>>(
-        f->active.as<uint8_t>(), f->observed.as<uint8_t>(), f->exact.as<uint8_t>(), f->Q, above, observed, exact);
-    f->stats.kernel_launches += 1;
-    GF_LAUNCH_CHECK();
+    {
+        StageTimer st(f, GF_FIELD_STAGE_FINISH, s);
+        gf::field::k_round_finalize<<<(f->Q + 255) / 256, 256, 0, s>>>(
+            f->active.as<uint8_t>(), f->observed.as<uint8_t>(), f->exact.as<uint8_t>(), f->Q, above, observed, exact);
+        f->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
+    f->stats.kernel_launches += f->launches;
+    f->launches = 0;
     GF_TRY(check_error_flag(f, s));
     ++f->round;
     if (f->round == 8u) f->finished = true;
@@ -511,10 +609,51 @@ int gf_field_release_table(gf_field* f, int64_t token, void* stream) {
     return GF_OK;
 }
 
-int gf_field_get_stats(const gf_field* f, gf_field_stats* stats) {
+int gf_field_get_stats(gf_field* f, gf_field_stats* stats) {
     if (f == nullptr || stats == nullptr) return fail(GF_ERR_BAD_INPUT, "field or stats is NULL");
     *stats = f->stats;
+    if (f->counters.ptr != nullptr) {
+        unsigned long long c[4] = {0, 0, 0, 0};
+        GF_CUDA(cudaMemcpy(c, f->counters.ptr, sizeof(c), cudaMemcpyDeviceToHost));
+        stats->candidate_loads = c[0];
+        stats->hit_tests = c[1];
+        stats->hits = c[2];
+        stats->warp_iterations = c[3];
+    }
     return GF_OK;
+}
+
+int gf_field_enable_timing(gf_field* f, int enable) {
+    if (f == nullptr) return fail(GF_ERR_BAD_INPUT, "field is NULL");
+    f->timing = enable != 0;
+    return GF_OK;
+}
+
+int gf_field_collect_times(gf_field* f, float* ms, uint32_t* launches) {
+    if (f == nullptr) return fail(GF_ERR_BAD_INPUT, "field is NULL");
+    float acc[GF_FIELD_STAGES] = {0};
+    uint32_t cnt[GF_FIELD_STAGES] = {0};
+    int status = GF_OK;
+    for (auto& e : f->pending) {
+        float t = 0.0f;
+        if (status == GF_OK) {
+            cudaError_t ce = cudaEventSynchronize(e.end);
+            if (ce == cudaSuccess) ce = cudaEventElapsedTime(&t, e.start, e.end);
+            if (ce != cudaSuccess) status = fail(GF_ERR_CUDA, "stage timing failed: %s", cudaGetErrorString(ce));
+        }
+        if (e.stage >= 0 && e.stage < GF_FIELD_STAGES) {
+            acc[e.stage] += t;
+            cnt[e.stage] += e.launches;
+        }
+        f->eventPool.push_back(e.start);
+        f->eventPool.push_back(e.end);
+    }
+    f->pending.clear();
+    for (int i = 0; i < GF_FIELD_STAGES; ++i) {
+        if (ms != nullptr) ms[i] = acc[i];
+        if (launches != nullptr) launches[i] = cnt[i];
+    }
+    return status;
 }
 
 }  // extern "C"

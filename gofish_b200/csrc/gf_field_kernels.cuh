@@ -36,9 +36,9 @@ constexpr int kCellShift = 3;  // 8 x 8-pixel cells
 constexpr int kCell = 1 << kCellShift;
 constexpr int kCellPixels = kCell * kCell;
 constexpr int kFan = 4;  // quadtree fan-out per axis
-constexpr int kMaxTopNodes = 64;
-constexpr int kMaxLevels = 6;
-constexpr int kStack = 1 + (kFan * kFan - 1) * (kMaxLevels - 1) + 8;
+constexpr int kMaxLevels = 8;  // cells up to the single root cone
+constexpr int kStack = 112;    // traversal stack (test-before-push: at most 15 per level + 16)
+constexpr int kVisitBudget = 256;  // node tests one thread may spend on a Gaussian
 constexpr int kBlock = 256;  // points per integration block and candidates per batch
 constexpr uint32_t kNoKey = 0xffffffffu;
 constexpr float kCapAll = -2.0f;       // cos(theta) marker: the support sphere holds the camera centre
@@ -63,8 +63,9 @@ __device__ __forceinline__ V3 camera_centre(const CameraArgs& a, V3& os0) {
     return mat3(a.pose.Rinv, os0) + v3(a.pose.c[0], a.pose.c[1], a.pose.c[2]);
 }
 
-// Quadtree of direction cones, level 0 = cells.  Node arrays are
-// concatenated: level l occupies [offset[l], offset[l] + gx[l] * gy[l]).
+// Quadtree of direction cones, level 0 = cells, level n-1 = one root cone.
+// Node arrays are concatenated: level l occupies [offset[l], offset[l] +
+// gx[l] * gy[l]).
 // A: (axis.xyz, cos phi); A.w > 1.5 marks an empty node.
 // B: (sin phi, largest range, phi, number of points).
 struct Levels {
@@ -256,42 +257,97 @@ __global__ __launch_bounds__(256) void k_cone_reduce(const float4* __restrict__ 
     pB[node] = make_float4(sinf(phi), mr, phi, cnt);
 }
 
-// Visits every cell whose cone meets the cap and whose points reach the
-// support's lower range bound (depth-first over the quadtree).
+// Does the cap reach node c of level l: the node holds points, some of them
+// beyond the support's lower range bound, and its cone meets the cap?
+__device__ __forceinline__ bool node_passes(const Levels& L, int l, uint32_t c, float vx, float vy, float vz,
+                                            float cosT, float sinT, float lower) {
+    const uint32_t idx = L.offset[l] + c;
+    const float4 A = L.A[idx];
+    if (A.w > 1.5f) return false;
+    const float4 B = L.B[idx];
+    if (lower > B.y) return false;
+    return cap_meets_cone(vx, vy, vz, cosT, sinT, A, B);
+}
+
+// Visits every cell the cap reaches, depth first from the root, testing
+// children before pushing them.  Returns false, having visited only some
+// cells, once more than kVisitBudget nodes were tested (such Gaussians are
+// binned cooperatively by a warp instead).
 template <typename Visit>
-__device__ __forceinline__ void for_cells(const Levels& L, float vx, float vy, float vz, float cosT, float sinT,
+__device__ __forceinline__ bool for_cells(const Levels& L, float vx, float vy, float vz, float cosT, float sinT,
                                           float lower, Visit visit) {
-    uint32_t stack[kStack];
     const int top = L.n - 1;
-    const uint32_t topCount = L.gx[top] * L.gy[top];
-    for (uint32_t t = 0; t < topCount; ++t) {
-        int sp = 0;
-        stack[sp++] = (uint32_t(top) << 28) | t;
-        while (sp > 0) {
-            const uint32_t e = stack[--sp];
-            const int l = int(e >> 28);
-            const uint32_t node = e & 0x0fffffffu;
-            const uint32_t idx = L.offset[l] + node;
-            const float4 A = L.A[idx];
-            if (A.w > 1.5f) continue;
-            const float4 B = L.B[idx];
-            if (lower > B.y) continue;
-            if (!cap_meets_cone(vx, vy, vz, cosT, sinT, A, B)) continue;
-            if (l == 0) {
-                visit(node);
-                continue;
-            }
-            const uint32_t nx = node % L.gx[l], ny = node / L.gx[l];
-            const uint32_t cgx = L.gx[l - 1], cgy = L.gy[l - 1];
-            for (int j = kFan - 1; j >= 0; --j) {
-                for (int i = kFan - 1; i >= 0; --i) {
-                    const uint32_t cx = nx * kFan + uint32_t(i), cy = ny * kFan + uint32_t(j);
-                    if (cx >= cgx || cy >= cgy) continue;
-                    stack[sp++] = (uint32_t(l - 1) << 28) | (cy * cgx + cx);
+    if (!node_passes(L, top, 0u, vx, vy, vz, cosT, sinT, lower)) return true;
+    if (top == 0) {
+        visit(0u);
+        return true;
+    }
+    uint32_t stack[kStack];
+    int sp = 0, tests = 0;
+    stack[sp++] = uint32_t(top) << 28;
+    while (sp > 0) {
+        const uint32_t e = stack[--sp];
+        const int l = int(e >> 28);
+        const uint32_t node = e & 0x0fffffffu;
+        const uint32_t nx = node % L.gx[l], ny = node / L.gx[l];
+        const int cl = l - 1;
+        const uint32_t cgx = L.gx[cl], cgy = L.gy[cl];
+        for (int j = 0; j < kFan; ++j) {
+            for (int i = 0; i < kFan; ++i) {
+                const uint32_t cx = nx * kFan + uint32_t(i), cy = ny * kFan + uint32_t(j);
+                if (cx >= cgx || cy >= cgy) continue;
+                if (++tests > kVisitBudget) return false;
+                const uint32_t c = cy * cgx + cx;
+                if (!node_passes(L, cl, c, vx, vy, vz, cosT, sinT, lower)) continue;
+                if (cl == 0) {
+                    visit(c);
+                } else {
+                    if (sp >= kStack) return false;
+                    stack[sp++] = (uint32_t(cl) << 28) | c;
                 }
             }
         }
     }
+    return true;
+}
+
+// Warp-cooperative version for Gaussians over the budget: the warp tests the
+// level-1 nodes 32 at a time and the 16 cells of every node that passes.
+// Calls emit(k, cell) for the k-th cell found (k counts from 0 in the same
+// order on every call) and returns the number of cells (warp-uniform).
+template <typename Emit>
+__device__ __forceinline__ uint32_t warp_cells(const Levels& L, float vx, float vy, float vz, float cosT, float sinT,
+                                               float lower, uint32_t lane, Emit emit) {
+    uint32_t n = 0;
+    const uint32_t below = (1u << lane) - 1u;
+    if (L.n == 1) {
+        const uint32_t g0 = L.gx[0] * L.gy[0];
+        for (uint32_t base = 0; base < g0; base += 32u) {
+            const uint32_t c = base + lane;
+            const bool ok = c < g0 && node_passes(L, 0, c, vx, vy, vz, cosT, sinT, lower);
+            const uint32_t m = __ballot_sync(0xffffffffu, ok);
+            if (ok) emit(n + uint32_t(__popc(m & below)), c);
+            n += uint32_t(__popc(m));
+        }
+        return n;
+    }
+    const uint32_t g1 = L.gx[1] * L.gy[1], gx1 = L.gx[1], gx0 = L.gx[0], gy0 = L.gy[0];
+    for (uint32_t base = 0; base < g1; base += 32u) {
+        const uint32_t idx = base + lane;
+        const bool pass = idx < g1 && node_passes(L, 1, idx, vx, vy, vz, cosT, sinT, lower);
+        uint32_t m = __ballot_sync(0xffffffffu, pass);
+        while (m != 0u) {
+            const uint32_t n1 = base + uint32_t(__ffs(m) - 1);
+            m &= m - 1u;
+            const uint32_t cx = (n1 % gx1) * kFan + (lane & 3u), cy = (n1 / gx1) * kFan + (lane >> 2);
+            const bool ok = lane < 16u && cx < gx0 && cy < gy0 &&
+                            node_passes(L, 0, cy * gx0 + cx, vx, vy, vz, cosT, sinT, lower);
+            const uint32_t cm = __ballot_sync(0xffffffffu, ok);
+            if (ok) emit(n + uint32_t(__popc(cm & below)), cy * gx0 + cx);
+            n += uint32_t(__popc(cm));
+        }
+    }
+    return n;
 }
 
 // Compact per-Gaussian data, made once per context from the packed [N,32]
@@ -333,7 +389,8 @@ struct ParticleArgs {
 // at most 1/255 can never pass the alpha test and reach no cell.
 __global__ __launch_bounds__(256) void k_field_particles(CameraArgs a, ParticleArgs p, Levels L,
                                                          float4* __restrict__ cull, float4* __restrict__ hit,
-                                                         uint32_t* __restrict__ counts) {
+                                                         uint32_t* __restrict__ counts, uint32_t* __restrict__ big,
+                                                         uint32_t* __restrict__ bigCount) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= p.N) return;
     const float4 pd = p.posd[i];
@@ -357,14 +414,47 @@ __global__ __launch_bounds__(256) void k_field_particles(CameraArgs a, ParticleA
     const V3 gro = v3(__fmaf_rn(b0.z, g.z, __fmaf_rn(b0.y, g.y, b0.x * g.x)),
                       __fmaf_rn(b1.y, g.z, __fmaf_rn(b1.x, g.y, b0.w * g.x)),
                       __fmaf_rn(b2.x, g.z, __fmaf_rn(b1.w, g.y, b1.z * g.x)));
+    uint32_t n = 0;
+    bool small = true;
+    if (!(pd.w <= kAlphaThreshold)) small = for_cells(L, vx, vy, vz, cosT, sinT, lower, [&](uint32_t) { ++n; });
     cull[i] = make_float4(vx, vy, vz, cosT);
     hit[4 * size_t(i)] = make_float4(gro.x, gro.y, gro.z, pd.w);
     hit[4 * size_t(i) + 1] = b0;
     hit[4 * size_t(i) + 2] = b1;
-    hit[4 * size_t(i) + 3] = make_float4(b2.x, lower, sinT, 0.0f);
-    uint32_t n = 0;
-    if (!(pd.w <= kAlphaThreshold)) for_cells(L, vx, vy, vz, cosT, sinT, lower, [&](uint32_t) { ++n; });
-    counts[i] = n;
+    hit[4 * size_t(i) + 3] = make_float4(b2.x, lower, sinT, small ? 0.0f : 1.0f);
+    if (!small) big[atomicAdd(bigCount, 1u)] = i;
+    counts[i] = small ? n : 0u;
+}
+
+// Cell counts (kEmit false) or keys (kEmit true) of the Gaussians over the
+// traversal budget, one warp per Gaussian.
+template <bool kEmit>
+__global__ __launch_bounds__(256) void k_field_big(Levels L, const uint32_t* __restrict__ big,
+                                                   const uint32_t* __restrict__ bigCount,
+                                                   const float4* __restrict__ cull, const float4* __restrict__ hit,
+                                                   uint32_t* __restrict__ counts, const uint64_t* __restrict__ offsets,
+                                                   uint64_t* __restrict__ keys, uint32_t* __restrict__ ids) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t total = *bigCount;
+    for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+        const uint32_t i = big[w];
+        const float4 c = cull[i];
+        const float4 h3 = hit[4 * size_t(i) + 3];
+        if (kEmit) {
+            const uint64_t o = offsets[i];
+            const uint32_t cap = counts[i];
+            warp_cells(L, c.x, c.y, c.z, c.w, h3.z, h3.y, lane, [&](uint32_t k, uint32_t cell) {
+                if (k < cap) {
+                    keys[o + k] = (uint64_t(cell) << 32) | uint64_t(i);
+                    ids[o + k] = i;
+                }
+            });
+        } else {
+            const uint32_t n = warp_cells(L, c.x, c.y, c.z, c.w, h3.z, h3.y, lane, [](uint32_t, uint32_t) {});
+            if (lane == 0) counts[i] = n;
+        }
+    }
 }
 
 // 5. Emit (cell << 32 | id) keys at the scanned offsets, in id order.
@@ -375,8 +465,9 @@ __global__ __launch_bounds__(256) void k_field_emit(Levels L, uint32_t N, const 
                                                     uint32_t* __restrict__ ids) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= N || counts[i] == 0u) return;
-    const float4 c = cull[i];
     const float4 h3 = hit[4 * size_t(i) + 3];
+    if (h3.w != 0.0f) return;  // binned by k_field_big
+    const float4 c = cull[i];
     uint64_t o = offsets[i];
     const uint64_t end = o + counts[i];
     for_cells(L, c.x, c.y, c.z, c.w, h3.z, h3.y, [&](uint32_t cell) {
@@ -412,6 +503,7 @@ struct IntegrateArgs {
     uint32_t cells;
     const uint32_t* pointStart;  // exclusive scan of per-pixel-key point counts
     const uint32_t* sorted;
+    const uint32_t* pixKey;
     const float4* info;
     const uint2* cellRanges;
     const uint32_t* candIds;
@@ -421,20 +513,66 @@ struct IntegrateArgs {
     uint8_t* observed;  // field and rounds
     uint8_t* active;    // rounds: no camera below 1/2 yet
     uint8_t* exact;     // rounds: some camera exactly 1/2
+    unsigned long long* counters;  // candidates staged, exact hit tests, hits, warp candidate iterations
 };
+
+// Alpha of one candidate for a point's segment [0, range] (0 when it is not
+// a hit): the range and cap pre-tests, then the hit test with the arithmetic
+// of half_ray / hit_test (gaussianParticles.slang hitInterval).
+__device__ __forceinline__ float candidate_alpha(float4 c, float4 h0, float4 h1, float4 h2, float4 h3, float4 di,
+                                                 uint32_t& tests) {
+    if (h3.y > di.w) return 0.0f;                                                        // support beyond the point
+    if (c.w > -1.5f && di.x * c.x + di.y * c.y + di.z * c.z < c.w) return 0.0f;        // ray misses the cap
+    ++tests;
+    const V3 grdu = v3(__fmaf_rn(h1.z, di.z, __fmaf_rn(h1.y, di.y, h1.x * di.x)),
+                       __fmaf_rn(h2.y, di.z, __fmaf_rn(h2.x, di.y, h1.w * di.x)),
+                       __fmaf_rn(h3.x, di.z, __fmaf_rn(h2.w, di.y, h2.z * di.x)));
+    const float denom = fdot3(grdu, grdu);
+    if (!(denom > 0.0f) || !isfinite_f(denom)) return 0.0f;
+    const V3 gro = v3(h0.x, h0.y, h0.z);
+    const float num = fdot3(gro, grdu);
+    const float tauLine = -num / denom;
+    const float tau = fminf(fmaxf(tauLine, 0.0f), di.w);
+    const V3 pc = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y), __fmaf_rn(tau, grdu.z, gro.z));
+    const float g2 = fdot3(pc, pc);
+    if (g2 > kResponseCutoff2) return 0.0f;
+    const float resp = gf_expf(-0.5f * g2);
+    const float alpha = min_f(kMaxAlpha, resp * h0.w);
+    return (resp > kMinKernelResponse && alpha > kAlphaThreshold) ? alpha : 0.0f;
+}
+
+// T <- T (1 - alpha).  Round lanes stop once the opacity 1 - T exceeds 1/2
+// (the reference's threshold rounds do the same).  Field lanes stop once
+// 1 - T rounds to exactly 1: later factors lie in [0.01, 1], so T can only
+// shrink, and since rounding is monotone the final 1 - T is then exactly 1
+// as well -- the full ordered product gives the same float.
+template <bool kRound>
+__device__ __forceinline__ void apply_alpha(float alpha, float& T, bool& done, bool& strictlyAbove) {
+    T = T * (1.0f - alpha);
+    if (kRound) {
+        if (1.0f - T > 0.5f) {
+            strictlyAbove = true;
+            done = true;
+        }
+    } else if (1.0f - T == 1.0f) {
+        done = true;
+    }
+}
 
 // 6. Ordered integration (reference integratePoints, opacityField.cuh:775-829,
 // and the threshold round, bisectionTableImpl.inl:222-304).  One block
 // integrates up to kBlock points of one cell against the cell's candidates
-// in ascending id.  Field mode keeps the exact product (a lane stops only
-// when T reaches 0, after which it cannot change); round mode stops a lane
-// once 1 - T > 1/2 and classifies the camera as the reference's
-// classifyCamera does.
+// in ascending id.  Field mode keeps the exact float result (a lane stops
+// only once 1 - T has rounded to 1, which no later factor can change); round
+// mode stops a lane once 1 - T > 1/2 and classifies the camera as the
+// reference's classifyCamera does.
 template <bool kRound>
 __global__ __launch_bounds__(kBlock) void k_field_integrate(IntegrateArgs a) {
     __shared__ float4 sCull[kBlock];
     __shared__ float4 sH0[kBlock], sH1[kBlock], sH2[kBlock], sH3[kBlock];
     __shared__ uint32_t sCell;
+    __shared__ unsigned long long sKey[kBlock];
+    __shared__ uint32_t sPoint[kBlock];
     const uint32_t tid = threadIdx.x, lane = tid & 31u;
     if (tid == 0) {
         // the last cell whose first block is at or before this one
@@ -450,28 +588,50 @@ __global__ __launch_bounds__(kBlock) void k_field_integrate(IntegrateArgs a) {
     const uint32_t cell = sCell;
     const uint32_t pb = a.pointStart[cell * kCellPixels] + (blockIdx.x - a.blockStart[cell]) * kBlock;
     const uint32_t pe = min(pb + kBlock, a.pointStart[(cell + 1) * kCellPixels]);
-    const bool valid = pb + tid < pe;
-    const uint32_t q = valid ? a.sorted[pb + tid] : 0u;
+    // Order the block's points by (pixel, range) so that each warp's points
+    // share both a direction and a depth range (bitonic sort in shared memory).
+    {
+        const bool mine = pb + tid < pe;
+        const uint32_t q0 = mine ? a.sorted[pb + tid] : 0u;
+        sKey[tid] = mine ? (static_cast<unsigned long long>(a.pixKey[q0] & uint32_t(kCellPixels - 1)) << 32) |
+                               __float_as_uint(a.info[q0].w)
+                         : ~0ull;
+        sPoint[tid] = q0;
+        __syncthreads();
+        for (uint32_t k = 2; k <= uint32_t(kBlock); k <<= 1) {
+            for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+                const uint32_t ixj = tid ^ j;
+                if (ixj > tid) {
+                    const unsigned long long x = sKey[tid], y = sKey[ixj];
+                    if ((x > y) == ((tid & k) == 0u)) {
+                        sKey[tid] = y;
+                        sKey[ixj] = x;
+                        const uint32_t t = sPoint[tid];
+                        sPoint[tid] = sPoint[ixj];
+                        sPoint[ixj] = t;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+    }
+    const bool valid = sKey[tid] != ~0ull;
+    const uint32_t q = valid ? sPoint[tid] : 0u;
     const float4 di = valid ? a.info[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 
-    // The warp's direction cone and largest range.
+    // The warp's direction cone (axis from all its points; half angle and
+    // largest range refreshed per batch over the points still integrating).
     const float sx = warp_sum(di.x), sy = warp_sum(di.y), sz = warp_sum(di.z);
     const float sn = sqrtf(sx * sx + sy * sy + sz * sz);
-    float ax = 0.0f, ay = 0.0f, az = 1.0f, phi = kPiF;
-    if (sn > 1e-12f) {
-        ax = sx / sn;
-        ay = sy / sn;
-        az = sz / sn;
-        phi = warp_max(valid ? unit_angle(ax, ay, az, di.x, di.y, di.z) : 0.0f);
-        phi = phi * 1.0001f + kAngleMargin;
-    }
-    const bool wide = phi >= kWideCone;
-    const float cphi = cosf(phi), sphi = sinf(phi);
-    const float maxRange = warp_max(valid ? di.w : 0.0f);
+    const bool axisOk = sn > 1e-12f;
+    const float ax = axisOk ? sx / sn : 0.0f, ay = axisOk ? sy / sn : 0.0f, az = axisOk ? sz / sn : 1.0f;
+    const float myAngle = valid ? unit_angle(ax, ay, az, di.x, di.y, di.z) : 0.0f;
 
     float T = 1.0f;
     bool done = !valid, strictlyAbove = false;
+    uint32_t tests = 0, hits = 0, iterations = 0;
     const uint2 cr = a.cellRanges[cell];
+    if (tid == 0) atomicAdd(&a.counters[0], static_cast<unsigned long long>(cr.y - cr.x));
     for (uint32_t base = cr.x; base < cr.y; base += kBlock) {
         if (__syncthreads_and(done)) break;
         const uint32_t idx = base + tid;
@@ -485,6 +645,11 @@ __global__ __launch_bounds__(kBlock) void k_field_integrate(IntegrateArgs a) {
         }
         __syncthreads();
         const uint32_t n = min(uint32_t(kBlock), cr.y - base);
+        float phi = warp_max(done ? 0.0f : myAngle);
+        phi = axisOk ? phi * 1.0001f + kAngleMargin : kPiF;
+        const bool wide = phi >= kWideCone;
+        const float cphi = cosf(phi), sphi = sinf(phi);
+        const float maxRange = warp_max(done ? 0.0f : di.w);
         for (uint32_t s = 0; s * 32u < n; ++s) {
             if (__all_sync(0xffffffffu, done)) break;
             const uint32_t k = s * 32u + lane;
@@ -498,43 +663,26 @@ __global__ __launch_bounds__(kBlock) void k_field_integrate(IntegrateArgs a) {
                 }
             }
             uint32_t m = __ballot_sync(0xffffffffu, pass);
+            iterations += uint32_t(__popc(m));
             while (m != 0u) {
                 const uint32_t slot = s * 32u + uint32_t(__ffs(m) - 1);
                 m &= m - 1u;
                 if (done) continue;
-                const float4 h3 = sH3[slot];
-                if (h3.y > di.w) continue;  // support beyond the point
-                const float4 c = sCull[slot];
-                if (c.w > -1.5f && di.x * c.x + di.y * c.y + di.z * c.z < c.w) continue;  // ray misses the cap
-                const float4 h0 = sH0[slot], h1 = sH1[slot], h2 = sH2[slot];
-                // Hit test on [0, range], the arithmetic of half_ray / hit_test.
-                const V3 grdu = v3(__fmaf_rn(h1.z, di.z, __fmaf_rn(h1.y, di.y, h1.x * di.x)),
-                                   __fmaf_rn(h2.y, di.z, __fmaf_rn(h2.x, di.y, h1.w * di.x)),
-                                   __fmaf_rn(h3.x, di.z, __fmaf_rn(h2.w, di.y, h2.z * di.x)));
-                const float denom = fdot3(grdu, grdu);
-                if (!(denom > 0.0f) || !isfinite_f(denom)) continue;
-                const V3 gro = v3(h0.x, h0.y, h0.z);
-                const float num = fdot3(gro, grdu);
-                const float tauLine = -num / denom;
-                const float tau = fminf(fmaxf(tauLine, 0.0f), di.w);
-                const V3 pc = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y),
-                                 __fmaf_rn(tau, grdu.z, gro.z));
-                const float g2 = fdot3(pc, pc);
-                if (g2 > kResponseCutoff2) continue;
-                const float resp = gf_expf(-0.5f * g2);
-                const float alpha = min_f(kMaxAlpha, resp * h0.w);
-                if (!(resp > kMinKernelResponse && alpha > kAlphaThreshold)) continue;
-                T = T * (1.0f - alpha);
-                if (kRound) {
-                    if (1.0f - T > 0.5f) {
-                        strictlyAbove = true;
-                        done = true;
-                    }
-                } else if (T == 0.0f) {
-                    done = true;
+                const float alpha = candidate_alpha(sCull[slot], sH0[slot], sH1[slot], sH2[slot], sH3[slot], di,
+                                                    tests);
+                if (alpha > 0.0f) {
+                    ++hits;
+                    apply_alpha<kRound>(alpha, T, done, strictlyAbove);
                 }
             }
         }
+    }
+    const uint32_t warpTests = __reduce_add_sync(0xffffffffu, tests);
+    const uint32_t warpHits = __reduce_add_sync(0xffffffffu, hits);
+    if (lane == 0) {
+        atomicAdd(&a.counters[1], static_cast<unsigned long long>(warpTests));
+        atomicAdd(&a.counters[2], static_cast<unsigned long long>(warpHits));
+        atomicAdd(&a.counters[3], static_cast<unsigned long long>(iterations));
     }
     if (!valid) return;
     if (!kRound) {

@@ -13,7 +13,7 @@ import ctypes
 import torch
 
 from .. import _native
-from .._native import GfFieldCamera, GfFieldStats
+from .._native import FIELD_STAGES, GfFieldCamera, GfFieldStats
 
 
 def _stream(device: torch.device) -> int:
@@ -203,3 +203,14 @@ class SplatRaster:
         out = GfFieldStats()
         _native.check(self._lib.gf_field_get_stats(self._handle, ctypes.byref(out)), "field stats")
         return out
+
+    def enable_stage_timing(self, enable: bool = True) -> None:
+        """CUDA-event timing of every stage of later camera passes."""
+        _native.check(self._lib.gf_field_enable_timing(self._handle, 1 if enable else 0), "field timing")
+
+    def collect_stage_times(self) -> dict[str, tuple[float, int]]:
+        """{stage: (milliseconds, kernel launches)} since the last collect."""
+        ms = (ctypes.c_float * len(FIELD_STAGES))()
+        launches = (ctypes.c_uint32 * len(FIELD_STAGES))()
+        _native.check(self._lib.gf_field_collect_times(self._handle, ms, launches), "field timing")
+        return {name: (float(ms[i]), int(launches[i])) for i, name in enumerate(FIELD_STAGES)}

@@ -212,3 +212,20 @@ def workload_multi_view(seed: int = 1236, n: int = 3_000_000, views: int = 64, s
         poses.append(look_outward_pose(center, yaw))
     return Workload("multi_view_fwd_bwd", scene, cam, poses, 16,
                     f"{n} Gaussians SH3, {views} KB 200deg {size}x{size} views on a 2 m ring, K=16")
+
+
+def workload_mesh_query(seed: int = 1237, n: int = 3_000_000, views: int = 32, size: int = 800) -> Workload:
+    """GOF-style mesh opacity query: 3M Gaussians with the CPU-scale
+    distributions (SH degree 0), queried at their sites (centre + 8 support-box
+    corners, about 27M points) from 32 equidistant (k = 0) 200 deg fisheye
+    views at 800x800, placed evenly on a 2 m ring and looking outward."""
+    scene = random_scene(n, 0, seed)
+    cam = fisheye_camera(size, size, 200.0)
+    poses = []
+    for v in range(views):
+        yaw = 2.0 * math.pi * v / views
+        centre = np.array([2.0 * math.cos(yaw), 2.0 * math.sin(yaw), 0.0])
+        poses.append(look_outward_pose(centre, yaw))
+    return Workload("mesh_opacity_query", scene, cam, poses, 0,
+                    f"{n} Gaussians, sites (centre + 8 corners), {views} equidistant 200deg {size}x{size} views "
+                    "on a 2 m ring")

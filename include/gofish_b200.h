@@ -248,8 +248,20 @@ typedef struct gf_field_stats {
     uint64_t pairs;            /* (cell, Gaussian) candidate pairs so far */
     uint64_t cameras;          /* camera passes so far */
     uint64_t kernel_launches;  /* kernels launched so far */
-    uint64_t reserved[4];
+    uint64_t candidate_loads;  /* candidates staged by the integration blocks so far */
+    uint64_t hit_tests;        /* exact per-point hit tests so far */
+    uint64_t hits;             /* accepted hits so far */
+    uint64_t warp_iterations;  /* (warp, candidate) steps of the integration so far */
 } gf_field_stats;
+
+/* Stages of a camera pass, for gf_field_collect_times. */
+#define GF_FIELD_STAGE_POINTS 0     /* project, key, counting sort of the points */
+#define GF_FIELD_STAGE_CONES 1      /* cell cones, quadtree, block counts */
+#define GF_FIELD_STAGE_CANDIDATES 2 /* per-Gaussian caps and cell counts, scan */
+#define GF_FIELD_STAGE_SORT 3       /* emit, cell-key sort, cell ranges */
+#define GF_FIELD_STAGE_INTEGRATE 4  /* ordered integration */
+#define GF_FIELD_STAGE_FINISH 5     /* finish / round decision vectors */
+#define GF_FIELD_STAGES 6
 
 gf_field* gf_field_create(void);
 void gf_field_destroy(gf_field* field);
@@ -288,8 +300,14 @@ int gf_field_evaluate_round(gf_field* field, int64_t token, const float* points,
 int gf_field_reset_batch(gf_field* field, int64_t token, void* stream);
 /* release_bisection_table (opacityFieldBinding.inl:533-545): after round 7. */
 int gf_field_release_table(gf_field* field, int64_t token, void* stream);
-/* Counters of work done.  No reference counterpart (bench accounting). */
-int gf_field_get_stats(const gf_field* field, gf_field_stats* stats);
+/* Counters of work done (synchronizes the device).  No reference
+ * counterpart (bench accounting). */
+int gf_field_get_stats(gf_field* field, gf_field_stats* stats);
+/* Per-stage CUDA-event timing of later calls.  No reference counterpart. */
+int gf_field_enable_timing(gf_field* field, int enable);
+/* Milliseconds and launch counts per GF_FIELD_STAGE_* since the last collect
+ * (arrays of GF_FIELD_STAGES; synchronizes the recorded events). */
+int gf_field_collect_times(gf_field* field, float* ms, uint32_t* launches);
 
 #ifdef __cplusplus
 }

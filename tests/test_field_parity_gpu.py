@@ -48,11 +48,16 @@ def test_field_matches_oracle(cuda_device, masked):
     assert_field_equal(got, want)
 
 
-def test_field_dense_scene(cuda_device):
-    # Many candidates per cell and per warp: 12k larger Gaussians in a 1-2.5 m shell.
-    case = field_case(seed=5, n=12000, size=128, num_views=3, site_gaussians=800, extra_points=4000,
-                      scale_boost=1.5, r_max=2.5, ring=1.5)
+@pytest.mark.parametrize("n,boost", [(12000, 1.5), (40000, 4.0)])
+def test_field_dense_scene(cuda_device, n, boost):
+    # Many candidates per cell and per warp: larger Gaussians in a 1-2.5 m
+    # shell; in the 40k case almost every observed point saturates (1 - T
+    # rounds to 1 long before its last candidate).
+    case = field_case(seed=5, n=n, size=128, num_views=3, site_gaussians=800, extra_points=4000,
+                      scale_boost=boost, r_max=2.5, ring=1.5)
     want = oracle_field(case)
+    if boost > 2.0:
+        assert (want[0][want[1] != 0] == np.float32(1.0)).mean() > 0.5
     got = gpu_field(SplatRaster(), case, cuda_device)
     assert_field_equal(got, want)
 

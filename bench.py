@@ -368,6 +368,10 @@ MESH_UNIT = "Mqueries/s"  # million (point, view) evaluations per second
 # direction + range (16), camera-min read + write (8) and observed (2).
 FIELD_BYTES_PER_CANDIDATE = 4 + 16 + 64
 FIELD_BYTES_PER_POINT = 4 + 16 + 8 + 2
+# DRAM bytes per algorithmic byte of k_field_integrate in one ncu capture of a
+# 300k-Gaussian, 2.7M-site case (67.4 MB for 136.7 MB; profiles/
+# k_field_integrate_mesh_query.md); the full-size traffic is scaled by it.
+FIELD_TRAFFIC_PER_ALG_BYTE = 67.37 / 136.68
 
 
 def mesh_workload(args):
@@ -481,7 +485,9 @@ def run_mesh(args):
     avg_s = integ_ms / integ_launches / 1000.0
     achieved = alg / avg_s / 1e9
     roofline = {"kernel": "k_field_integrate<false>", "bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
-                "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
+                "unit": "GB/s", "frac": round(achieved / peak, 5),
+                "traffic": int(alg * FIELD_TRAFFIC_PER_ALG_BYTE),
+                "traffic_source": "scaled from an ncu capture of a 300k-Gaussian case by algorithmic bytes",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "alg_bytes_per_launch": int(alg),
                 "avg_launch_ms": round(avg_s * 1000.0, 4),
                 "hit_tests_per_launch": int(tests / integ_launches),

@@ -162,6 +162,9 @@ _SIGNATURES = [
     ("gf_field_release_table", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
     ("gf_field_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(GfFieldStats)]),
     ("gf_field_enable_timing", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("gf_mip_best_rate", ctypes.c_int,
+     [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, _vp,
+      ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]),
     ("gf_field_collect_times", ctypes.c_int, [_vp, _vp, _vp]),
 ]
 

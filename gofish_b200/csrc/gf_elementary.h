@@ -224,4 +224,69 @@ GF_HD float gf_atan2f(float y, float x) {
     return copysign_f(a, y);
 }
 
+// ---------------------------------------------------------------- double
+// Double-precision atan2 for the physical-mip search, shared by the oracle
+// and the sm_100a kernel so both round identically.  |y|/|x| (or its
+// reciprocal) lies in [0, 1]; with c = k/8 the nearest eighth,
+// atan(t) = atan(c) + atan((t - c) / (1 + t c)), |(t - c)/(1 + t c)| <= 1/16,
+// and the odd Taylor series of atan to the u^21 term leaves a truncation
+// error below 1e-27 of u.  atan(k/8), pi/2 and pi are double head + tail
+// pairs (the tail is the rounding error of the head).
+GF_HD double atan_unit_d(double t) {
+    const double HI[9] = {0.0, 0.12435499454676144, 0.24497866312686414, 0.35877067027057225, 0.4636476090008061,
+                          0.5585993153435624, 0.6435011087932844, 0.7188299996216245, 0.7853981633974483};
+    const double LO[9] = {0.0, -3.1253241424539383e-18, 1.0698755618734451e-17, -2.4623815582638635e-17,
+                          2.2698777452961687e-17, -5.4556305485916264e-18, 1.5834785051444286e-17,
+                          -2.1478388444456983e-17, 3.061616997868383e-17};
+    const int k = int(t * 8.0 + 0.5);
+    const double c = double(k) * 0.125;
+    const double u = (t - c) / (1.0 + t * c);
+    const double q = u * u;
+    // S(q) = 1/3 - q/5 + q^2/7 - ... - q^9/21, atan(u) = u - u q S(q).
+    double p = -1.0 / 21.0;
+    p = p * q + 1.0 / 19.0;
+    p = p * q - 1.0 / 17.0;
+    p = p * q + 1.0 / 15.0;
+    p = p * q - 1.0 / 13.0;
+    p = p * q + 1.0 / 11.0;
+    p = p * q - 1.0 / 9.0;
+    p = p * q + 1.0 / 7.0;
+    p = p * q - 1.0 / 5.0;
+    p = p * q + 1.0 / 3.0;
+    return HI[k] + (LO[k] + (u - (u * q) * p));
+}
+
+GF_HD bool isnan_d(double x) { return x != x; }
+GF_HD bool isfinite_d(double x) { return x - x == 0.0; }
+
+// atan2(y, x) in [-pi, pi] for finite arguments; NaN in, NaN out.
+GF_HD double gf_atan2d(double y, double x) {
+    if (isnan_d(x) || isnan_d(y)) return x + y;
+    const double PI_HI = 3.141592653589793, PI_LO = 1.2246467991473532e-16;
+    const double PI_2_HI = 1.5707963267948966, PI_2_LO = 6.123233995736766e-17;
+    const double ax = x < 0.0 ? -x : x;
+    const double ay = y < 0.0 ? -y : y;
+    const bool xneg = x < 0.0 || (x == 0.0 && 1.0 / x < 0.0);
+    const bool yneg = y < 0.0 || (y == 0.0 && 1.0 / y < 0.0);
+    double a;
+    if (ax == 0.0 && ay == 0.0) {
+        a = xneg ? PI_HI : 0.0;
+    } else if (!isfinite_d(ax) || !isfinite_d(ay)) {
+        if (!isfinite_d(ax) && !isfinite_d(ay)) a = 0.5 * PI_2_HI;
+        else a = isfinite_d(ax) ? PI_2_HI : 0.0;
+        if (xneg) a = PI_HI - a;
+    } else {
+        const bool swap = ay > ax;
+        const double t = swap ? ax / ay : ay / ax;  // [0, 1]
+        a = atan_unit_d(t);
+        if (swap) a = (PI_2_HI - a) + PI_2_LO;
+        if (xneg) a = (PI_HI - a) + PI_LO;
+    }
+    return yneg ? -a : a;
+}
+
+// sqrt(x^2 + y^2) in this operation order (no rescaling: the physical-mip
+// arguments are far from the overflow and underflow ranges).
+GF_HD double gf_hypotd(double x, double y) { return sqrt(x * x + y * y); }
+
 }  // namespace gf

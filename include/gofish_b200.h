@@ -309,6 +309,28 @@ int gf_field_enable_timing(gf_field* field, int enable);
  * (arrays of GF_FIELD_STAGES; synchronizes the recorded events). */
 int gf_field_collect_times(gf_field* field, float* ms, uint32_t* launches);
 
+/* ------------------------------------------------------------------------
+ * Physical-mip 3-D filter search.  Replaces best_rate of the reference's
+ * gofish_physical_mip extension (threedgrut/physical_mip_csrc/bindings.cpp:
+ * 34-101, fused_refresh_cuda.cu:40-219).  For each point [N,3] (float64): the
+ * finest pixel sampling rate over the frames whose calibrated support holds
+ * its projection (best_rate [N] float64, 0 when none), the winning frame's
+ * index (owner [N] int32, -1 when none; equal rates go to the smaller
+ * frame_rank), observed [N] uint8, and the unit direction from the winner's
+ * centre (direction [N,3] float64, 0 when none).  Frame table: rotations
+ * [F,3,3] camera-to-world, centers [F,3], frame_camera / frame_index [F]
+ * int32, frame_rank [F] int64.  Camera table (C <= 64): camera_model
+ * (threedgrut/physical_mip.py:37-45 ids), width, height [C] int32,
+ * camera_params [C,12] float64 as [fx, fy, cx, cy, distortion...],
+ * camera_max_angle [C] float64 (-1: none), row_lo / row_hi [C,row_stride]
+ * int32 valid column runs per raster row.  All device memory. */
+int gf_mip_best_rate(const double* positions, int64_t num_points, const double* rotations, const double* centers,
+                     const int32_t* frame_camera, const int32_t* frame_index, const int64_t* frame_rank,
+                     int64_t num_frames, const int32_t* camera_model, const int32_t* camera_width,
+                     const int32_t* camera_height, const double* camera_params, const double* camera_max_angle,
+                     int32_t num_cameras, const int32_t* row_lo, const int32_t* row_hi, int64_t row_stride,
+                     double* best_rate, int32_t* owner, uint8_t* observed, double* direction, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -79,6 +79,9 @@ def load():
         "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
         "oracle_visibility": (i32, [i32, vp, vp]),
         "oracle_field_camera": (i32, [cam_p, pose_p, i32, vp, vp, vp, i32, vp, vp, vp]),
+        "oracle_mip_best_rate": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp, vp,
+                                       vp]),
+        "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_num_threads": (i32, []),
         "oracle_expf": (f32, [f32]),
         "oracle_logf": (f32, [f32]),
@@ -285,3 +288,31 @@ def bisection_round(views, particles, points):
     opacity, observed, above = evaluate_field(views, particles, points)
     exact = ((observed != 0) & (opacity == np.float32(0.5))).astype(np.uint8)
     return above, observed, exact
+
+
+def mip_best_rate(points, rotations, centers, frame_camera, frame_index, frame_rank, camera_model, camera_width,
+                  camera_height, camera_params, camera_max_angle, row_lo, row_hi):
+    """The physical-mip search on numpy arrays: (best [N] f64, owner [N] i32,
+    observed [N] u8, direction [N,3] f64)."""
+    lib = load()
+    c = lambda a, dt: np.ascontiguousarray(a, dtype=dt)  # noqa: E731
+    pts = c(points, np.float64).reshape(-1, 3)
+    n = pts.shape[0]
+    rot = c(rotations, np.float64)
+    f = rot.shape[0]
+    lo = c(row_lo, np.int32)
+    args = [c(centers, np.float64), c(frame_camera, np.int32), c(frame_index, np.int32), c(frame_rank, np.int64)]
+    cam = [c(camera_model, np.int32), c(camera_width, np.int32), c(camera_height, np.int32),
+           c(camera_params, np.float64), c(camera_max_angle, np.float64)]
+    hi = c(row_hi, np.int32)
+    best = np.zeros(n, np.float64)
+    owner = np.full(n, -1, np.int32)
+    observed = np.zeros(n, np.uint8)
+    direction = np.zeros((n, 3), np.float64)
+    lib.oracle_mip_best_rate(_p(pts), n, _p(rot), *(_p(a) for a in args), f, *(_p(a) for a in cam), _p(lo), _p(hi),
+                             lo.shape[1], _p(best), _p(owner), _p(observed), _p(direction))
+    return best, owner, observed, direction
+
+
+def atan2d(y: float, x: float) -> float:
+    return float(load().oracle_atan2d(float(y), float(x)))

@@ -1062,9 +1062,194 @@ int oracle_field_camera(const OracleCamera* cam, const OraclePose* pose, int N, 
     return 0;
 }
 
+// ------------------------------------------------------------------ physical-mip 3-D filter
+// Finest pixel sampling rate of a point over the training frames
+// (threedgrut/physical_mip_csrc/fused_refresh_cuda.cu:40-219,
+// camera_local_validity.cuh; physical_mip.py:226-245).  Double precision,
+// no contraction; atan2 and hypot from gf_elementary.h.
+namespace mip {
+
+constexpr double kCenterEps = 1.0e-12;  // fused_refresh_cuda.cu:22
+constexpr double kNear = 0.2;           // camera_local_validity.cuh:15
+constexpr int kParams = 12;
+
+struct Projection {
+    double u = 0.0, v = 0.0;
+    double J[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // d(u,v)/d(camera xyz), row-major 2x3
+    bool ok = false;
+};
+
+// SIMPLE_PINHOLE / PINHOLE (model 0, 1): fused_refresh_cuda.cu:90-103.
+Projection pinhole(const double* P, double x, double y, double z) {
+    Projection o;
+    const double fx = P[0], fy = P[1], cx = P[2], cy = P[3];
+    const double zs = fabs(z) > DBL_MIN ? z : 1.0;
+    o.u = fx * x / zs + cx;
+    o.v = fy * y / zs + cy;
+    o.J[0] = fx / zs;
+    o.J[2] = -fx * x / (zs * zs);
+    o.J[4] = fy / zs;
+    o.J[5] = -fy * y / (zs * zs);
+    o.ok = z > 0.0;
+    return o;
+}
+
+// SIMPLE_RADIAL / RADIAL / OPENCV / FULL_OPENCV (3..6): fused_refresh_cuda.cu:104-150.
+Projection radial(int model, const double* P, double x, double y, double z) {
+    Projection o;
+    const double fx = P[0], fy = P[1], cx = P[2], cy = P[3], k1 = P[4];
+    const double k2 = model >= 4 ? P[5] : 0.0;
+    const double p1 = model >= 5 ? P[6] : 0.0;
+    const double p2 = model >= 5 ? P[7] : 0.0;
+    const double k3 = model == 6 ? P[8] : 0.0;
+    const double k4 = model == 6 ? P[9] : 0.0;
+    const double k5 = model == 6 ? P[10] : 0.0;
+    const double k6 = model == 6 ? P[11] : 0.0;
+    const double zs = fabs(z) > DBL_MIN ? z : 1.0;
+    const double a = x / zs, b = y / zs;
+    const double r2 = a * a + b * b;
+    const double r4 = r2 * r2, r6 = r4 * r2;
+    const double num = 1.0 + k1 * r2 + k2 * r4 + k3 * r6;
+    const double den = 1.0 + k4 * r2 + k5 * r4 + k6 * r6;
+    const double dens = fabs(den) > DBL_MIN ? den : 1.0;
+    const double g = num / dens;
+    const double gp = ((k1 + 2.0 * k2 * r2 + 3.0 * k3 * r4) * dens - num * (k4 + 2.0 * k5 * r2 + 3.0 * k6 * r4)) /
+                      (dens * dens);
+    const double xd = a * g + 2.0 * p1 * a * b + p2 * (r2 + 2.0 * a * a);
+    const double yd = b * g + p1 * (r2 + 2.0 * b * b) + 2.0 * p2 * a * b;
+    o.u = fx * xd + cx;
+    o.v = fy * yd + cy;
+    const double xa = g + 2.0 * a * a * gp + 2.0 * p1 * b + 6.0 * p2 * a;
+    const double xb = 2.0 * a * b * gp + 2.0 * p1 * a + 2.0 * p2 * b;
+    const double ya = 2.0 * a * b * gp + 2.0 * p1 * a + 2.0 * p2 * b;
+    const double yb = g + 2.0 * b * b * gp + 6.0 * p1 * b + 2.0 * p2 * a;
+    const double iz = 1.0 / zs;
+    o.J[0] = fx * xa * iz;
+    o.J[1] = fx * xb * iz;
+    o.J[2] = -fx * (xa * a + xb * b) * iz;
+    o.J[3] = fy * ya * iz;
+    o.J[4] = fy * yb * iz;
+    o.J[5] = -fy * (ya * a + yb * b) * iz;
+    o.ok = z > 0.0 && fabs(den) > DBL_MIN;
+    return o;
+}
+
+// OPENCV_FISHEYE (2): fused_refresh_cuda.cu:151-183.
+Projection fisheye(const double* P, double x, double y, double z, double dist, double rho, double theta) {
+    Projection o;
+    const double fx = P[0], fy = P[1], cx = P[2], cy = P[3];
+    const double k1 = P[4], k2 = P[5], k3 = P[6], k4 = P[7];
+    const double t2 = theta * theta;
+    const double q = theta * (1.0 + t2 * (k1 + t2 * (k2 + t2 * (k3 + t2 * k4))));
+    const double dq = 1.0 + t2 * (3.0 * k1 + t2 * (5.0 * k2 + t2 * (7.0 * k3 + t2 * 9.0 * k4)));
+    const double rs = fmax(rho, sqrt(DBL_MIN));
+    const double d2 = fmax(dist * dist, DBL_MIN);
+    const double c = x / rs, s = y / rs;
+    o.u = fx * q * c + cx;
+    o.v = fy * q * s + cy;
+    const double dth[3] = {z * x / (rs * d2), z * y / (rs * d2), -rho / d2};
+    const double dph[3] = {-y / (rs * rs), x / (rs * rs), 0.0};
+    for (int k = 0; k < 3; ++k) {
+        o.J[k] = fx * (dq * c * dth[k] - q * s * dph[k]);
+        o.J[3 + k] = fy * (dq * s * dth[k] + q * c * dph[k]);
+    }
+    if (rho <= kCenterEps && z > 0.0) {
+        o.u = cx;
+        o.v = cy;
+        for (int k = 0; k < 6; ++k) o.J[k] = 0.0;
+        o.J[0] = fx / dist;
+        o.J[4] = fy / dist;
+    }
+    o.ok = (rho > kCenterEps || z > 0.0) && dq > 0.0;
+    return o;
+}
+
+}  // namespace mip
+
+int oracle_mip_best_rate(const double* positions, int64_t N, const double* rotations, const double* centers,
+                         const int32_t* frameCamera, const int32_t* frameIndex, const int64_t* frameRank,
+                         int64_t F, const int32_t* cameraModel, const int32_t* cameraWidth,
+                         const int32_t* cameraHeight, const double* cameraParams, const double* cameraMaxAngle,
+                         const int32_t* rowLo, const int32_t* rowHi, int64_t rowStride, double* best,
+                         int32_t* owner, uint8_t* observed, double* direction) {
+    parallel_for(0, int(N), 64, [&](int i, int) {
+        const double px = positions[3 * size_t(i)], py = positions[3 * size_t(i) + 1],
+                     pz = positions[3 * size_t(i) + 2];
+        double bestRate = 0.0, bx = 0.0, by = 0.0, bz = 0.0;
+        int64_t bestRank = INT64_MAX;
+        int32_t bestFrame = -1;
+        for (int64_t f = 0; f < F; ++f) {
+            const int cam = frameCamera[f];
+            const int model = cameraModel[cam];
+            const double* R = rotations + 9 * f;  // camera-to-world, row-major
+            const double dx = px - centers[3 * f], dy = py - centers[3 * f + 1], dz = pz - centers[3 * f + 2];
+            // camera coordinates: R^T (p - c)
+            const double x = dx * R[0] + dy * R[3] + dz * R[6];
+            const double y = dx * R[1] + dy * R[4] + dz * R[7];
+            const double z = dx * R[2] + dy * R[5] + dz * R[8];
+            const double dist = sqrt(x * x + y * y + z * z);
+            const double rho = gf::gf_hypotd(x, y);
+            const double theta = gf::gf_atan2d(rho, z);
+            const double* P = cameraParams + mip::kParams * cam;
+            mip::Projection pr;
+            if (model == 0 || model == 1) pr = mip::pinhole(P, x, y, z);
+            else if (model >= 3 && model <= 6) pr = mip::radial(model, P, x, y, z);
+            else if (model == 2) pr = mip::fisheye(P, x, y, z, dist, rho, theta);
+            else continue;
+            const double local = model == 2 ? dist : z;
+            bool ok = local > mip::kNear && pr.ok;
+            for (int k = 0; k < 6; ++k) ok = ok && std::isfinite(pr.J[k]);
+            ok = ok && std::isfinite(pr.u) && std::isfinite(pr.v);
+            ok = ok && pr.u >= 0.0 && pr.u < cameraWidth[cam] && pr.v >= 0.0 && pr.v < cameraHeight[cam];
+            if (cameraMaxAngle[cam] >= 0.0) ok = ok && theta < cameraMaxAngle[cam];
+            if (ok) {
+                const int64_t ix = int64_t(floor(pr.u)), iy = int64_t(floor(pr.v));
+                ok = iy >= 0 && iy < cameraHeight[cam] && ix >= rowLo[cam * rowStride + iy] &&
+                     ix < rowHi[cam * rowStride + iy];
+            }
+            if (!ok) continue;
+            // world Jacobian rows J R^T
+            double w0[3], w1[3];
+            for (int k = 0; k < 3; ++k) {
+                w0[k] = pr.J[0] * R[3 * k] + pr.J[1] * R[3 * k + 1] + pr.J[2] * R[3 * k + 2];
+                w1[k] = pr.J[3] * R[3 * k] + pr.J[4] * R[3 * k + 1] + pr.J[5] * R[3 * k + 2];
+            }
+            const double a = w0[0] * w0[0] + w0[1] * w0[1] + w0[2] * w0[2];
+            const double b = w0[0] * w1[0] + w0[1] * w1[1] + w0[2] * w1[2];
+            const double c = w1[0] * w1[0] + w1[1] * w1[1] + w1[2] * w1[2];
+            const double lmax = 0.5 * (a + c + gf::gf_hypotd(a - c, 2.0 * b));
+            const double lmin = (a * c - b * b) / lmax;
+            if (!std::isfinite(lmax) || !std::isfinite(lmin) || !(lmax > 0.0) || !(lmin > 0.0)) continue;
+            const double rate = sqrt(lmin);
+            const int64_t rank = frameRank[f];
+            if (rate > bestRate || (rate == bestRate && rank < bestRank)) {
+                bestRate = rate;
+                bestRank = rank;
+                bestFrame = frameIndex[f];
+                bx = dx;
+                by = dy;
+                bz = dz;
+            }
+        }
+        best[i] = bestRate;
+        owner[i] = bestFrame;
+        observed[i] = bestFrame >= 0 ? 1u : 0u;
+        if (bestFrame >= 0) {
+            const double n = sqrt(bx * bx + by * by + bz * bz);
+            direction[3 * size_t(i)] = bx / n;
+            direction[3 * size_t(i) + 1] = by / n;
+            direction[3 * size_t(i) + 2] = bz / n;
+        } else {
+            direction[3 * size_t(i)] = direction[3 * size_t(i) + 1] = direction[3 * size_t(i) + 2] = 0.0;
+        }
+    });
+    return 0;
+}
+
 // Exported scalar elementary functions, for the accuracy tests.
 float oracle_expf(float x) { return gf::gf_expf(x); }
 float oracle_logf(float x) { return gf::gf_logf(x); }
 float oracle_atan2f(float y, float x) { return gf::gf_atan2f(y, x); }
+double oracle_atan2d(double y, double x) { return gf::gf_atan2d(y, x); }
 
 }  // extern "C"

@@ -123,6 +123,18 @@ class GfFieldStats(ctypes.Structure):
 FIELD_STAGES = ("points", "cones", "candidates", "sort", "integrate", "finish")
 
 
+class GfShapeCamera(ctypes.Structure):
+    _fields_ = [
+        ("c2w", ctypes.c_float * 16),
+        ("fisheye", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("focal_length", ctypes.c_float * 2),
+        ("radial", ctypes.c_float * 4),
+        ("max_angle", ctypes.c_float),
+        ("reserved1", ctypes.c_float),
+    ]
+
+
 _vp, _u32, _i64p = ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_int64)
 
 # (name, restype, argtypes) of every exported symbol of include/gofish_b200.h.
@@ -162,6 +174,14 @@ _SIGNATURES = [
     ("gf_field_release_table", ctypes.c_int, [_vp, ctypes.c_int64, _vp]),
     ("gf_field_get_stats", ctypes.c_int, [_vp, ctypes.POINTER(GfFieldStats)]),
     ("gf_field_enable_timing", ctypes.c_int, [_vp, ctypes.c_int]),
+    ("gf_view_q6", ctypes.c_int, [_vp, ctypes.c_int64, ctypes.POINTER(GfShapeCamera), ctypes.c_double, _vp, _vp, _vp,
+                                  _vp]),
+    ("gf_full_shape", ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_double, ctypes.c_int,
+                                     ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("gf_full_shape_bwd", ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.c_double, ctypes.c_int,
+                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("gf_view_shape_packed", ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.POINTER(GfShapeCamera),
+                                            ctypes.c_double, ctypes.c_int, _vp, _vp, _vp]),
     ("gf_mip_best_rate", ctypes.c_int,
      [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, _vp,
       ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]),

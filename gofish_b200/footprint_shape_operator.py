@@ -1,0 +1,146 @@
+"""Autograd boundary of the per-view full-shape operator
+(threedgut_tracer/footprint_shape_operator.py:51-351).
+
+For each Gaussian and view: C = Sigma + Q_v, the factor B = C^{1/2} R and
+B^-1, the mass-preserving factor m and the density m * o, with the VJP back
+to the intrinsic scale, rotation quaternion (w, x, y, z) and opacity.  Both
+directions are single sm_100a float64 kernels (gf_full_shape,
+gf_full_shape_bwd); rows are independent and are processed in the contiguous
+chunks the footprint planner gives.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native
+from .footprint_chunk_planner import plan_footprint_chunks
+from .view_observation_filter import FILTER_VARIANCE_PIXELS
+
+MODES = {"exact": 0, "cholesky": 1}
+_STATUS_TEXT = {1: "covariance not positive definite", 2: "degenerate projected covariance",
+                4: "non-finite output"}
+
+
+class FootprintNumericalError(RuntimeError):
+    """Numerical failure of the operator, with the offending global row."""
+
+    def __init__(self, message: str, *, global_row: int | None, completed_native_chunks: int):
+        super().__init__(message)
+        self.global_row = global_row
+        self.completed_native_chunks = int(completed_native_chunks)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode):
+    n = scales.shape[0]
+    dev = scales.device
+    cov = torch.empty((n, 3, 3), dtype=torch.float32, device=dev)
+    factor = torch.empty_like(cov)
+    inverse = torch.empty_like(cov)
+    comp = torch.empty(n, dtype=torch.float32, device=dev)
+    dens = torch.empty_like(density)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    lib = _native.load()
+    _native.check(lib.gf_full_shape(scales.data_ptr(), quaternion.data_ptr(), density.data_ptr(), q6.data_ptr(),
+                                    jacobian.data_ptr(), observed.data_ptr(), n, float(gamma), int(mass_preserving),
+                                    MODES[mode], cov.data_ptr(), factor.data_ptr(), inverse.data_ptr(),
+                                    comp.data_ptr(), dens.data_ptr(), status.data_ptr(), _stream(scales)),
+                  "full shape")
+    flags = status.cpu()
+    if int(flags[0]) != 0:
+        row = int(flags[2:].view(torch.int64)[0])
+        text = ", ".join(v for k, v in _STATUS_TEXT.items() if int(flags[0]) & k)
+        raise FootprintNumericalError(f"footprint full-shape failure ({text}) local_row={row}", global_row=row,
+                                      completed_native_chunks=0)
+    return cov, factor, inverse, comp, dens
+
+
+class _FullShape(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode):
+        s, q, d = scales.detach().float().contiguous(), quaternion.detach().float().contiguous(), \
+            density.detach().float().contiguous()
+        ob = observed.detach().to(torch.uint8).contiguous()
+        q6c, jc = q6.detach().contiguous(), jacobian.detach().contiguous()
+        outs = _forward(s, q, d, q6c, jc, ob, mass_preserving, gamma, mode)
+        ctx.save_for_backward(s, q, d, q6c, jc, ob)
+        ctx.mass_preserving, ctx.gamma, ctx.mode = bool(mass_preserving), float(gamma), mode
+        ctx.set_materialize_grads(False)
+        return outs
+
+    @staticmethod
+    def backward(ctx, g_cov, g_factor, g_inverse, g_comp, g_dens):
+        if ctx.mode != "exact":
+            raise RuntimeError("the Cholesky full shape is forward only (inference)")
+        s, q, d, q6, jac, ob = ctx.saved_tensors
+        n = s.shape[0]
+        gs = torch.empty_like(s)
+        gq = torch.empty_like(q)
+        gd = torch.empty_like(d)
+
+        # float32 contiguous copies, held until the kernel has been enqueued
+        keep = [None if t is None else t.float().contiguous() for t in (g_cov, g_factor, g_inverse, g_comp, g_dens)]
+
+        def ptr(t):
+            return None if t is None else t.data_ptr()
+
+        lib = _native.load()
+        _native.check(lib.gf_full_shape_bwd(s.data_ptr(), q.data_ptr(), d.data_ptr(), q6.data_ptr(), jac.data_ptr(),
+                                            ob.data_ptr(), n, ctx.gamma, int(ctx.mass_preserving),
+                                            *(ptr(t) for t in keep), gs.data_ptr(), gq.data_ptr(), gd.data_ptr(),
+                                            _stream(s)), "full shape backward")
+        return gs, gq, gd, None, None, None, None, None, None
+
+
+@dataclass(frozen=True)
+class FullShape:
+    covariance: torch.Tensor
+    factor: torch.Tensor
+    inverse_factor: torch.Tensor
+    compensation: torch.Tensor
+    density: torch.Tensor
+    observed: torch.Tensor
+
+
+def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mass_preserving: bool = True,
+                     pixel_variance: float = FILTER_VARIANCE_PIXELS, mode: str = "exact") -> FullShape:
+    """Full-shape factors for detached Q (float64 [N,6]) and Jacobian (float32 [N,2,3])."""
+    n = scales.shape[0]
+    if q6.requires_grad or q6.dtype != torch.float64 or tuple(q6.shape) != (n, 6):
+        raise ValueError("q6 must be detached float64 with shape [N,6]")
+    if jacobian.requires_grad or jacobian.dtype != torch.float32 or tuple(jacobian.shape) != (n, 2, 3):
+        raise ValueError("jacobian must be detached float32 with shape [N,2,3]")
+    if observed.requires_grad or observed.dtype != torch.bool:
+        raise ValueError("observed must be a detached bool tensor")
+    if mode not in MODES:
+        raise ValueError(f"unknown full-shape mode {mode!r}")
+    free, total = torch.cuda.mem_get_info(scales.device)
+    plan = plan_footprint_chunks(n, driver_free_bytes=int(free), device_total_bytes=int(total),
+                                 allocator_reserved_bytes=int(torch.cuda.memory_reserved(scales.device)),
+                                 allocator_allocated_bytes=int(torch.cuda.memory_allocated(scales.device)))
+    rows = plan.chunk_rows if n else 0
+    parts = []
+    for index, start in enumerate(range(0, n, max(1, rows)) if n else []):
+        stop = min(n, start + rows)
+        try:
+            parts.append(_FullShape.apply(scales[start:stop], quaternion[start:stop], density[start:stop],
+                                          q6[start:stop], jacobian[start:stop], observed[start:stop],
+                                          bool(mass_preserving), float(pixel_variance), mode))
+        except FootprintNumericalError as error:
+            row = None if error.global_row is None else start + error.global_row
+            raise FootprintNumericalError(str(error) + f" global_row={row}", global_row=row,
+                                          completed_native_chunks=index) from error
+    if not parts:
+        empty = scales.new_zeros((0, 3, 3))
+        return FullShape(empty, empty, empty, scales.new_zeros(0), density[:0], observed)
+    outs = parts[0] if len(parts) == 1 else tuple(torch.cat([p[i] for p in parts], 0) for i in range(5))
+    return FullShape(*outs, observed=observed)
+
+
+__all__ = ["FootprintNumericalError", "FullShape", "build_full_shape"]

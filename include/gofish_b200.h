@@ -331,6 +331,61 @@ int gf_mip_best_rate(const double* positions, int64_t num_points, const double* 
                      int32_t num_cameras, const int32_t* row_lo, const int32_t* row_hi, int64_t row_stride,
                      double* best_rate, int32_t* owner, uint8_t* observed, double* direction, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Per-view full-shape operator (replaces view_observation_filter.
+ * current_view_q6, threedgut_tracer/view_observation_filter.py:232-330, the
+ * native footprint full-shape operator, footprint_shape_operator.py:51-228 /
+ * src/footprint_shape_operator_cuda.cu, and the fused inference kernel
+ * src/fast_shape.cu).  All arrays are device memory; float64 arithmetic.
+ * ------------------------------------------------------------------------ */
+
+/* The active camera of one view: camera-to-world pose (row-major 4x4), and
+ * either OPENCV_FISHEYE (focal, k1..k4, max_angle) or an ideal pinhole
+ * (focal only). */
+typedef struct gf_shape_camera {
+    float c2w[16];
+    int32_t fisheye;
+    int32_t reserved0;
+    float focal_length[2];
+    float radial[4];
+    float max_angle;
+    float reserved1;
+} gf_shape_camera;
+
+/* current_view_q6: q6 [N,6] float64 (upper triangle of Q = gamma J^+ J^+^T,
+ * order xx xy xz yy yz zz), jacobian [N,2,3] float32 (zero where not
+ * observed), observed [N] uint8. */
+int gf_view_q6(const float* positions, int64_t n, const gf_shape_camera* camera, double gamma, double* q6,
+               float* jacobian, uint8_t* observed, void* stream);
+
+/* Full shape of every row: covariance C = R S^2 R^T + Q, factor B,
+ * inverse_factor B^-1 (all [N,3,3] float32), compensation m [N] and
+ * out_density [N] (m * density when mass_preserving).  mode 0: B = C^{1/2} R
+ * (symmetric root, the training operator); mode 1: B = chol(C).  Unobserved
+ * rows: B = R S, m = 1.  status (device, 4 int32): flags in status[0]
+ * (1 not positive definite, 2 degenerate projected covariance, 4 non-finite
+ * output), the first failing row as uint64 in status[2..3]; reset by the call. */
+int gf_full_shape(const float* scales, const float* quaternions, const float* density, const double* q6,
+                  const float* jacobian, const uint8_t* observed, int64_t n, double gamma, int mass_preserving,
+                  int mode, float* covariance, float* factor, float* inverse_factor, float* compensation,
+                  float* out_density, int32_t* status, void* stream);
+
+/* VJP of gf_full_shape (mode 0) to scales [N,3], quaternions [N,4] and
+ * density [N]; any output gradient may be NULL (zero). */
+int gf_full_shape_bwd(const float* scales, const float* quaternions, const float* density, const double* q6,
+                      const float* jacobian, const uint8_t* observed, int64_t n, double gamma, int mass_preserving,
+                      const float* grad_covariance, const float* grad_factor, const float* grad_inverse_factor,
+                      const float* grad_compensation, const float* grad_density, float* grad_scales,
+                      float* grad_quaternions, float* grad_density_in, void* stream);
+
+/* One inference frame: Q, the full shape and m of every row written into the
+ * packed [N,32] rows (density slot 3, B 12-20, B^-1 21-29).  mode 0 exact,
+ * mode 1 Cholesky with the stored shape for rows whose factorization fails
+ * (fast_shape.cu:136-197).  status as for gf_full_shape. */
+int gf_view_shape_packed(const float* positions, const float* quaternions, const float* scales,
+                         const float* density, int64_t n, const gf_shape_camera* camera, double gamma, int mode,
+                         float* packed, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,8 @@ GF_CAMERA_OPENCV_PINHOLE = 0
 GF_CAMERA_OPENCV_FISHEYE = 1
 GF_KEY_PER_TILE_DEPTH = 0
 GF_KEY_GLOBAL_DEPTH = 1
+GF_FALLBACK_NONE = 0
+GF_FALLBACK_CONE = 1
 STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
 
 
@@ -39,7 +41,7 @@ class GfTracerConfig(ctypes.Structure):
         ("k_buffer_size", ctypes.c_int32),
         ("sort_key", ctypes.c_int32),
         ("enable_hit_counts", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("admission_fallback", ctypes.c_int32),
     ]
 
 

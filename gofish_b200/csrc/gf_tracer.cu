@@ -55,6 +55,7 @@ struct gf_tracer {
     DeviceBuffer proj, records, bounds, counts, offsets, scanTiles, total, tileRays, ranges;
     DeviceBuffer keys[2], ids[2], hist;
     DeviceBuffer gradRecords;
+    DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
     uint64_t* hostTotal = nullptr;
     int finalBuf = 0;
     bool haveForward = false;
@@ -238,21 +239,76 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     if (int e = t->tileRays.ensure(sizeof(float4) * 2 * size_t(T), stream)) return e;
     if (int e = t->ranges.ensure(sizeof(uint2) * size_t(T), stream)) return e;
 
-    if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
+    gf::FallbackArgs fa{};
+    fa.enabled = t->cfg.admission_fallback == GF_FALLBACK_CONE ? 1 : 0;
+    if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
+    if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
+    if (int e = t->bigCount.ensure(sizeof(uint32_t), stream)) return e;
+    fa.caps = t->caps.as<float4>();
+    fa.big = t->bigList.as<uint32_t>();
+    fa.bigCount = t->bigCount.as<uint32_t>();
+    {
         StageTimer st(t, GF_STAGE_TILE_RAYS, stream);
-        gf::k_tile_rays<<<(T + 127) / 128, 128, 0, stream>>>(f, in->ray_origin, in->ray_direction,
-                                                              t->tileRays.as<float4>());
-        t->launches += 1;
-        GF_LAUNCH_CHECK();
+        if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
+            gf::k_tile_rays<<<(T + 127) / 128, 128, 0, stream>>>(f, in->ray_origin, in->ray_direction,
+                                                                  t->tileRays.as<float4>());
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
+        if (fa.enabled) {
+            // tile ray-cone quadtree, leaves (tiles) up to one root
+            gf::fb::TileTree& tr = fa.tree;
+            tr.n = 0;
+            uint32_t nodes = 0;
+            int gx = f.gx, gy = f.gy;
+            // the warp descent packs (level << 24 | node)
+            if (T >= (1u << 24)) return fail(GF_ERR_BAD_INPUT, "raster too large for the tile cone tree");
+            while (true) {
+                if (tr.n >= gf::fb::kMaxLevels) return fail(GF_ERR_BAD_INPUT, "raster too large for the tile cone tree");
+                tr.gx[tr.n] = gx;
+                tr.gy[tr.n] = gy;
+                tr.offset[tr.n] = nodes;
+                nodes += uint32_t(gx * gy);
+                ++tr.n;
+                if (gx == 1 && gy == 1) break;
+                gx = (gx + gf::fb::kFan - 1) / gf::fb::kFan;
+                gy = (gy + gf::fb::kFan - 1) / gf::fb::kFan;
+            }
+            if (int e = t->coneA.ensure(sizeof(float4) * nodes, stream)) return e;
+            if (int e = t->coneS.ensure(sizeof(float) * nodes, stream)) return e;
+            float4* A = t->coneA.as<float4>();
+            float* S = t->coneS.as<float>();
+            tr.A = A;
+            tr.S = S;
+            // one warp per tile, four tiles per block
+            gf::fb::k_tile_cones<<<(T + 3) / 4, 128, 0, stream>>>(f, mask->buf.as<uint8_t>(), in->ray_direction, A,
+                                                                  S);
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+            for (int l = 1; l < tr.n; ++l) {
+                const int pn = tr.gx[l] * tr.gy[l];
+                gf::fb::k_tile_cone_level<<<pn, 256, 0, stream>>>(tr, l, A, S);
+                t->launches += 1;
+                GF_LAUNCH_CHECK();
+            }
+        }
     }
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT, stream);
+        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, sizeof(uint32_t), stream));
         gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
                                                           t->proj.as<float4>(), t->records.as<float4>(),
                                                           t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),
-                                                          t->bounds.as<float>());
+                                                          t->bounds.as<float>(), fa);
         t->launches += 1;
         GF_LAUNCH_CHECK();
+        if (fa.enabled) {
+            gf::k_fallback_big<false><<<148 * 8, 256, 0, stream>>>(
+                f, fa, mask->buf.as<uint8_t>(), t->records.as<float4>(), t->tileRays.as<float4>(),
+                t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis), nullptr, nullptr, nullptr);
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
     }
     {
         StageTimer st(t, GF_STAGE_SCAN, stream);
@@ -276,9 +332,17 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
         gf::k_emit<<<(N + 255) / 256, 256, 0, stream>>>(f, t->proj.as<float4>(), t->records.as<float4>(),
                                                         mask->buf.as<uint8_t>(), t->tileRays.as<float4>(),
                                                         t->offsets.as<uint64_t>(), t->counts.as<uint32_t>(),
-                                                        t->keys[0].as<uint64_t>(), t->ids[0].as<uint32_t>());
+                                                        t->keys[0].as<uint64_t>(), t->ids[0].as<uint32_t>(), fa);
         t->launches += 1;
         GF_LAUNCH_CHECK();
+        if (fa.enabled) {
+            gf::k_fallback_big<true><<<148 * 8, 256, 0, stream>>>(
+                f, fa, mask->buf.as<uint8_t>(), t->records.as<float4>(), t->tileRays.as<float4>(),
+                t->counts.as<uint32_t>(), nullptr, t->offsets.as<uint64_t>(), t->keys[0].as<uint64_t>(),
+                t->ids[0].as<uint32_t>());
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
     }
     const int endBit = 32 + int(bit_length(T));
     {
@@ -340,6 +404,10 @@ gf_tracer* gf_tracer_create(const gf_tracer_config* config) {
         fail(GF_ERR_BAD_INPUT, "unknown sort key %d", config->sort_key);
         return nullptr;
     }
+    if (config->admission_fallback != GF_FALLBACK_NONE && config->admission_fallback != GF_FALLBACK_CONE) {
+        fail(GF_ERR_BAD_INPUT, "unknown admission fallback %d", config->admission_fallback);
+        return nullptr;
+    }
     gf_tracer* t = new gf_tracer();
     t->cfg = *config;
     return t;
@@ -352,6 +420,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaGetDevice(&prev);
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
+        for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
                                 &t->hist,    &t->gradRecords};

@@ -56,6 +56,374 @@ __global__ void k_tile_rays(FrameArgs f, const float* __restrict__ rayO, const f
     tileRays[2 * tile + 1] = d;
 }
 
+// ------------------------------------------------------------ cone fallback admission
+// Particles whose unscented projection is invalid (wide-angle rim, near the
+// camera, straddling the field-of-view boundary) are admitted by a
+// conservative angular test of their bounding sphere against a quadtree of
+// tile ray cones (reference fastFallbackTiles, gutProjector.cuh:100-183,
+// render.gofish.fast_admission_fallback = "cone").  Leaf cone = the world
+// directions of a retained tile's pixel rays; parents contain their 4x4
+// children.  A tile is admitted when its cone and every ancestor's meet the
+// particle's cap; a sphere that holds the camera centre admits every
+// retained tile.  Only +, -, *, /, sqrt and the shared gf_logf enter these
+// tests, in a fixed order, so the oracle admits exactly the same tiles.
+namespace fb {
+
+constexpr int kFan = 4;
+constexpr int kMaxLevels = 8;
+constexpr float kEps = 1e-6f;
+
+enum CapMode : int { kNone = 0, kCone = 1, kAll = 2 };
+
+struct TileTree {
+    int n;
+    int gx[kMaxLevels], gy[kMaxLevels];
+    uint32_t offset[kMaxLevels];
+    const float4* A;  // axis.xyz, cos phi (> 1.5: empty)
+    const float* S;   // sin phi
+};
+
+struct Cap {
+    float ux, uy, uz, cosA, sinA;
+    int mode;
+};
+
+// Bounding sphere of the opacity support: sigma_max(B) (Gershgorin bound on
+// the largest eigenvalue of B B^T) times the canonical radius where
+// min(0.99, rho) exp(-r^2/2) falls to the minimum alpha (capped by the kernel
+// cut-off), seen from the camera centre.
+__device__ __forceinline__ Cap fallback_cap(const float B[9], V3 mu, float density, V3 cam) {
+    Cap c{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, kNone};
+    const float m00 = B[0] * B[0] + B[1] * B[1] + B[2] * B[2];
+    const float m01 = B[0] * B[3] + B[1] * B[4] + B[2] * B[5];
+    const float m02 = B[0] * B[6] + B[1] * B[7] + B[2] * B[8];
+    const float m11 = B[3] * B[3] + B[4] * B[4] + B[5] * B[5];
+    const float m12 = B[3] * B[6] + B[4] * B[7] + B[5] * B[8];
+    const float m22 = B[6] * B[6] + B[7] * B[7] + B[8] * B[8];
+    const float g0 = m00 + abs_f(m01) + abs_f(m02);
+    const float g1 = abs_f(m01) + m11 + abs_f(m12);
+    const float g2 = abs_f(m02) + abs_f(m12) + m22;
+    const float lam = max_f(g0, max_f(g1, g2));
+    const float rho = min_f(kMaxAlpha, density);
+    const float canonical = min_f(2.994f, __fsqrt_rn(max_f(0.0f, 2.0f * gf_logf(rho / kAlphaThreshold))));
+    const float r = canonical * __fsqrt_rn(lam) * 1.001f;
+    const V3 v = mu - cam;
+    const float D = __fsqrt_rn(dot3(v, v));
+    if (!(isfinite_f(r) && isfinite_f(D)) || !(r > 0.0f)) return c;
+    if (D <= r) {
+        c.mode = kAll;
+        return c;
+    }
+    c.ux = v.x / D;
+    c.uy = v.y / D;
+    c.uz = v.z / D;
+    c.sinA = min_f(1.0f, (r / D) * 1.0001f);
+    c.cosA = __fsqrt_rn(max_f(0.0f, 1.0f - c.sinA * c.sinA));
+    c.mode = kCone;
+    return c;
+}
+
+// Cone (axis, phi) meets cap (u, alpha) iff angle(axis, u) <= phi + alpha:
+// always when phi + alpha >= pi (sin(phi + alpha) < 0), else
+// axis . u >= cos(phi + alpha) = cos phi cos alpha - sin phi sin alpha.
+__device__ __forceinline__ bool node_pass(const TileTree& t, int l, uint32_t node, const Cap& c) {
+    const float4 A = t.A[t.offset[l] + node];
+    if (A.w > 1.5f) return false;
+    const float S = t.S[t.offset[l] + node];
+    if (S * c.cosA + A.w * c.sinA < 0.0f) return true;
+    const float d = A.x * c.ux + A.y * c.uy + A.z * c.uz;
+    return d >= A.w * c.cosA - S * c.sinA - kEps;
+}
+
+// Does every ancestor (levels >= 2) of level-1 node (x, y) meet the cap?
+__device__ __forceinline__ bool ancestors_pass(const TileTree& t, uint32_t x, uint32_t y, const Cap& c) {
+    for (int l = 2; l < t.n; ++l) {
+        x /= kFan;
+        y /= kFan;
+        if (!node_pass(t, l, y * uint32_t(t.gx[l]) + x, c)) return false;
+    }
+    return true;
+}
+
+// The admitted tiles of one particle, found by one warp.  kAll: every
+// retained tile.  kCone: every leaf that meets the cap together with all its
+// ancestors, by a depth-first descent that expands the two top nodes of a
+// shared-memory stack per step (16 children each, one per lane), pushing the
+// inner children that pass and emitting the leaves.  Pending nodes stay below
+// 32 per level, so kWarpStack entries suffice; were it ever exceeded, the
+// level-1 scan below recomputes the same set.  emit(k, tile) receives the
+// k-th admitted tile (in an order the sorted output does not depend on);
+// returns the number of tiles (warp-uniform).
+constexpr int kWarpStack = 32 * kMaxLevels;
+
+template <typename Emit>
+__device__ __forceinline__ uint32_t warp_tiles(const TileTree& t, const uint8_t* __restrict__ mask, const Cap& c,
+                                               uint32_t lane, uint32_t* __restrict__ stack, Emit&& emit) {
+    uint32_t n = 0;
+    const uint32_t below = (1u << lane) - 1u;
+    const uint32_t g0 = uint32_t(t.gx[0] * t.gy[0]);
+    if (c.mode == kAll || t.n == 1) {
+        for (uint32_t base = 0; base < g0; base += 32u) {
+            const uint32_t tile = base + lane;
+            bool ok = tile < g0 && mask[tile] != 0u;
+            if (ok && c.mode != kAll) ok = node_pass(t, 0, tile, c);
+            const uint32_t m = __ballot_sync(0xffffffffu, ok);
+            if (ok) emit(n + uint32_t(__popc(m & below)), tile);
+            n += uint32_t(__popc(m));
+        }
+        return n;
+    }
+    if (c.mode != kCone) return 0u;
+    const int top = t.n - 1;
+    if (!node_pass(t, top, 0u, c)) return 0u;
+    if (lane == 0) stack[0] = uint32_t(top) << 24;
+    __syncwarp();
+    int sp = 1;
+    bool overflow = false;
+    while (sp > 0) {
+        const int take = min(sp, 2);
+        const int g = int(lane >> 4);
+        const bool active = g < take;
+        const uint32_t e = active ? stack[sp - 1 - g] : 0u;
+        __syncwarp();  // the popped slots are reused by this step's pushes
+        sp -= take;
+        bool pass = false;
+        int cl = 0;
+        uint32_t child = 0u;
+        if (active) {
+            const int l = int(e >> 24);
+            const uint32_t node = e & 0x00ffffffu;
+            cl = l - 1;
+            const uint32_t cx = (node % uint32_t(t.gx[l])) * kFan + (lane & 3u);
+            const uint32_t cy = (node / uint32_t(t.gx[l])) * kFan + ((lane >> 2) & 3u);
+            if (cx < uint32_t(t.gx[cl]) && cy < uint32_t(t.gy[cl])) {
+                child = cy * uint32_t(t.gx[cl]) + cx;
+                pass = node_pass(t, cl, child, c);
+            }
+        }
+        const uint32_t leaves = __ballot_sync(0xffffffffu, pass && cl == 0);
+        const uint32_t inner = __ballot_sync(0xffffffffu, pass && cl > 0);
+        if (pass && cl == 0) emit(n + uint32_t(__popc(leaves & below)), child);
+        n += uint32_t(__popc(leaves));
+        const int pushes = __popc(inner);
+        if (sp + pushes > kWarpStack) {
+            overflow = true;
+            break;
+        }
+        if (pass && cl > 0) stack[sp + __popc(inner & below)] = (uint32_t(cl) << 24) | child;
+        sp += pushes;
+        __syncwarp();
+    }
+    if (!overflow) return n;
+    // Level-1 scan: nodes whose ancestors all pass, then their 16 leaves.
+    n = 0;
+    const uint32_t gx1 = uint32_t(t.gx[1]), g1 = gx1 * uint32_t(t.gy[1]);
+    const uint32_t gx0 = uint32_t(t.gx[0]), gy0 = uint32_t(t.gy[0]);
+    for (uint32_t base = 0; base < g1; base += 32u) {
+        const uint32_t node = base + lane;
+        const bool pass = node < g1 && node_pass(t, 1, node, c) && ancestors_pass(t, node % gx1, node / gx1, c);
+        uint32_t m = __ballot_sync(0xffffffffu, pass);
+        while (m != 0u) {
+            const uint32_t n1 = base + uint32_t(__ffs(m) - 1);
+            m &= m - 1u;
+            const uint32_t cx = (n1 % gx1) * kFan + (lane & 3u), cy = (n1 / gx1) * kFan + (lane >> 2);
+            const bool ok = lane < 16u && cx < gx0 && cy < gy0 && node_pass(t, 0, cy * gx0 + cx, c);
+            const uint32_t cm = __ballot_sync(0xffffffffu, ok);
+            if (ok) emit(n + uint32_t(__popc(cm & below)), cy * gx0 + cx);
+            n += uint32_t(__popc(cm));
+        }
+    }
+    return n;
+}
+
+// Leaf cones: one warp per tile, lane r < 16 walking pixel row r; the row
+// partials (sums, first minima) are combined in row order, so the result is
+// the same float for float as the oracle's row-then-rows loop.
+__device__ __forceinline__ bool pixel_dir(const FrameArgs& f, const float* __restrict__ rayD, int x, int y, V3& u) {
+    const size_t p = size_t(x) + size_t(f.W) * size_t(y);
+    const V3 d = v3(rayD[3 * p], rayD[3 * p + 1], rayD[3 * p + 2]);
+    const float n2 = dot3(d, d);
+    if (!(n2 > 0.0f) || !isfinite_f(n2)) return false;
+    const V3 w = mat3(f.pose.Rinv, d);
+    const float wn = __fsqrt_rn(dot3(w, w));
+    u = v3(w.x / wn, w.y / wn, w.z / wn);
+    return true;
+}
+
+__global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* __restrict__ mask,
+                                                    const float* __restrict__ rayD, float4* __restrict__ A,
+                                                    float* __restrict__ S) {
+    const int tile = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (tile >= f.gx * f.gy) return;  // warp-uniform
+    const int tx = tile % f.gx, ty = tile / f.gx;
+    const int x0 = tx * kTile, y0 = ty * kTile, x1 = min(f.W, x0 + kTile), y1 = min(f.H, y0 + kTile);
+    const int y = y0 + lane;
+    const bool row = lane < kTile && y < y1 && mask[tile] != 0u;
+    // pass 0: row sums and counts
+    V3 sum = v3(0.0f, 0.0f, 0.0f);
+    int count = 0;
+    if (row)
+        for (int x = x0; x < x1; ++x) {
+            V3 u;
+            if (!pixel_dir(f, rayD, x, y, u)) continue;
+            sum = sum + u;
+            ++count;
+        }
+    V3 total = v3(0.0f, 0.0f, 0.0f);
+    int all = 0;
+    for (int r = 0; r < kTile; ++r) {
+        const V3 rs = v3(__shfl_sync(0xffffffffu, sum.x, r), __shfl_sync(0xffffffffu, sum.y, r),
+                         __shfl_sync(0xffffffffu, sum.z, r));
+        const int rc = __shfl_sync(0xffffffffu, count, r);
+        if (rc > 0) total = total + rs;
+        all += rc;
+    }
+    if (mask[tile] == 0u || all == 0) {
+        if (lane == 0) {
+            A[tile] = make_float4(0.0f, 0.0f, 1.0f, 2.0f);
+            S[tile] = 0.0f;
+        }
+        return;
+    }
+    const float sn = __fsqrt_rn(dot3(total, total));
+    if (!(sn > 0.0f) || !isfinite_f(sn)) {
+        if (lane == 0) {
+            A[tile] = make_float4(0.0f, 0.0f, 1.0f, -1.0f);
+            S[tile] = 0.0f;
+        }
+        return;
+    }
+    const V3 mean = v3(total.x / sn, total.y / sn, total.z / sn);
+    // passes 1, 2: the ray farthest from the mean, then the ray farthest from it
+    V3 far1 = mean, far2 = mean;
+    for (int pass = 0; pass < 2; ++pass) {
+        const V3 ref = pass == 0 ? mean : far1;
+        float best = 2.0f;
+        V3 bu = ref;
+        if (row)
+            for (int x = x0; x < x1; ++x) {
+                V3 u;
+                if (!pixel_dir(f, rayD, x, y, u)) continue;
+                const float c = dot3(ref, u);
+                if (c < best) {
+                    best = c;
+                    bu = u;
+                }
+            }
+        float gbest = 2.0f;
+        V3 gu = ref;
+        for (int r = 0; r < kTile; ++r) {
+            const float rb = __shfl_sync(0xffffffffu, best, r);
+            const V3 ru = v3(__shfl_sync(0xffffffffu, bu.x, r), __shfl_sync(0xffffffffu, bu.y, r),
+                             __shfl_sync(0xffffffffu, bu.z, r));
+            if (rb < gbest) {
+                gbest = rb;
+                gu = ru;
+            }
+        }
+        if (pass == 0) far1 = gu;
+        else far2 = gu;
+    }
+    const V3 mid = far1 + far2;
+    const float mn2 = __fsqrt_rn(dot3(mid, mid));
+    const V3 ax = (mn2 > 1e-3f && isfinite_f(mn2)) ? v3(mid.x / mn2, mid.y / mn2, mid.z / mn2) : mean;
+    // pass 3: the smallest cosine to the axis
+    float mn = 1.0f;
+    if (row)
+        for (int x = x0; x < x1; ++x) {
+            V3 u;
+            if (!pixel_dir(f, rayD, x, y, u)) continue;
+            mn = min_f(mn, dot3(ax, u));
+        }
+    float gmn = 1.0f;
+    for (int r = 0; r < kTile; ++r) gmn = min_f(gmn, __shfl_sync(0xffffffffu, mn, r));
+    if (lane != 0) return;
+    const float cphi = max_f(-1.0f, gmn - kEps);
+    A[tile] = make_float4(ax.x, ax.y, ax.z, cphi);
+    S[tile] = __fsqrt_rn(max_f(0.0f, 1.0f - cphi * cphi));
+}
+
+// Parent cones of level l >= 1, one block per node: axis = normalised sum of
+// the 4x4 child axes (row-major order); cos phi = the smallest, over the
+// non-empty leaves under the node, of cos(angle(axis, leaf axis) + phi_leaf)
+// = (axis . a) cos phi_leaf - |axis x a| sin phi_leaf, less kEps; a leaf
+// reaching past pi (sin of the sum < 0) makes the node cover the sphere
+// (cos -1, sin 0).  A minimum is exact in any order, so the block reduction
+// gives the oracle's value.
+__global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, float4* __restrict__ A,
+                                                         float* __restrict__ S) {
+    __shared__ float axis[4];
+    __shared__ float wmin[8];
+    const int node = blockIdx.x;
+    const int pgx = t.gx[l], cgx = t.gx[l - 1], cgy = t.gy[l - 1];
+    const int px = node % pgx, py = node / pgx;
+    if (threadIdx.x == 0) {
+        V3 sum = v3(0.0f, 0.0f, 0.0f);
+        bool any = false;
+        for (int j = 0; j < kFan; ++j)
+            for (int i = 0; i < kFan; ++i) {
+                const int cx = px * kFan + i, cy = py * kFan + j;
+                if (cx >= cgx || cy >= cgy) continue;
+                const float4 a = A[t.offset[l - 1] + uint32_t(cy * cgx + cx)];
+                if (a.w > 1.5f) continue;
+                any = true;
+                sum = sum + v3(a.x, a.y, a.z);
+            }
+        const float sn = __fsqrt_rn(dot3(sum, sum));
+        const bool ok = sn > 0.0f && isfinite_f(sn);
+        axis[0] = ok ? sum.x / sn : 0.0f;
+        axis[1] = ok ? sum.y / sn : 0.0f;
+        axis[2] = ok ? sum.z / sn : 1.0f;
+        axis[3] = !any ? 2.0f : (ok ? 1.0f : -1.0f);  // empty / bounded / whole sphere
+    }
+    __syncthreads();
+    const V3 ax = v3(axis[0], axis[1], axis[2]);
+    const float state = axis[3];
+    if (state != 1.0f) {
+        if (threadIdx.x == 0) {
+            A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, state);
+            S[t.offset[l] + node] = 0.0f;
+        }
+        return;
+    }
+    int span = 1;
+    for (int k = 0; k < l; ++k) span *= kFan;
+    const int gx0 = t.gx[0], gy0 = t.gy[0];
+    const int x0 = px * span, y0 = py * span, x1 = min(gx0, x0 + span), y1 = min(gy0, y0 + span);
+    const int w = x1 - x0, cnt = w * (y1 - y0);
+    float mn = 1.0f;
+    bool full = false;
+    for (int k = threadIdx.x; k < cnt; k += blockDim.x) {
+        const int leaf = (y0 + k / w) * gx0 + x0 + k % w;
+        const float4 a = A[leaf];
+        if (a.w > 1.5f) continue;
+        const float cs = S[leaf];
+        const V3 ca = v3(a.x, a.y, a.z);
+        const V3 cr = v3(ax.y * ca.z - ax.z * ca.y, ax.z * ca.x - ax.x * ca.z, ax.x * ca.y - ax.y * ca.x);
+        const float sang = __fsqrt_rn(dot3(cr, cr));
+        const float cang = dot3(ax, ca);
+        if (sang * a.w + cang * cs < 0.0f) full = true;
+        else mn = min_f(mn, cang * a.w - sang * cs);
+    }
+    full = __syncthreads_or(full) != 0;
+    for (int o = 16; o > 0; o >>= 1) mn = min_f(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    if ((threadIdx.x & 31) == 0) wmin[threadIdx.x >> 5] = mn;
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    for (int k = 0; k < int(blockDim.x >> 5); ++k) mn = min_f(mn, wmin[k]);
+    if (full) {
+        A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, -1.0f);
+        S[t.offset[l] + node] = 0.0f;
+        return;
+    }
+    const float cphi = max_f(-1.0f, mn - kEps);
+    A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, cphi);
+    S[t.offset[l] + node] = __fsqrt_rn(max_f(0.0f, 1.0f - cphi * cphi));
+}
+
+}  // namespace fb
+
 // ------------------------------------------------------------ projection
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
@@ -82,11 +450,20 @@ __device__ __forceinline__ uint32_t for_admitted_tiles(const FrameArgs& f, const
 // One thread per particle: UT projection, conic, admitted-tile count, SH
 // radiance, and the 64-byte render record (reference projectOnTiles,
 // gutProjector.cuh:653-945).
+struct FallbackArgs {
+    int enabled;
+    fb::TileTree tree;
+    float4* caps;       // [N,2] for particles without a valid projection: (u, cos), (sin, mode, 0, 0)
+    uint32_t* big;      // particles left to the warp kernel
+    uint32_t* bigCount;
+};
+
 __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __restrict__ particles,
                                                  const float* __restrict__ features,
                                                  const uint8_t* __restrict__ mask, float4* __restrict__ proj,
                                                  float4* __restrict__ records, uint32_t* __restrict__ counts,
-                                                 uint32_t* __restrict__ visibility, float* __restrict__ bounds) {
+                                                 uint32_t* __restrict__ visibility, float* __restrict__ bounds,
+                                                 FallbackArgs fa) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= f.N) return;
     const float* row = particles + 32 * size_t(i);
@@ -134,11 +511,85 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
     rec[3] = make_float4(r7.y, rgb[0], rgb[1], rgb[2]);
 
     const uint32_t n = for_admitted_tiles(f, mask, p, [](int, int, uint32_t) {});
+    bool deferred = false;
+    if (!fast_ut_valid(p)) {
+        // Without a valid projection: the cone fallback, left to the warp
+        // kernel once the cap meets the root cone.
+        fb::Cap c{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, fb::kNone};
+        if (fa.enabled && density >= kAlphaThreshold) {
+            c = fb::fallback_cap(B, mu, density, v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]));
+            if (c.mode == fb::kCone && !fb::node_pass(fa.tree, fa.tree.n - 1, 0u, c)) c.mode = fb::kNone;
+            deferred = c.mode != fb::kNone;
+        }
+        fa.caps[2 * size_t(i)] = make_float4(c.ux, c.uy, c.uz, c.cosA);
+        fa.caps[2 * size_t(i) + 1] = make_float4(c.sinA, float(c.mode), 0.0f, 0.0f);
+    }
+    // warp-aggregated append to the fallback list
+    const uint32_t live = __activemask();
+    const uint32_t dm = __ballot_sync(live, deferred);
+    if (dm != 0u) {
+        const uint32_t lane = threadIdx.x & 31u;
+        const int leader = __ffs(dm) - 1;
+        uint32_t base = 0u;
+        if (int(lane) == leader) base = atomicAdd(fa.bigCount, uint32_t(__popc(dm)));
+        base = __shfl_sync(live, base, leader);
+        if (deferred) fa.big[base + uint32_t(__popc(dm & ((1u << lane) - 1u)))] = i;
+    }
     counts[i] = n;
-    if (visibility != nullptr) visibility[i] = n ? 1u : 0u;
-    if (n != 0u) {
+    if (visibility != nullptr && !deferred) visibility[i] = n ? 1u : 0u;
+    if (n != 0u || deferred) {
         const float Binv[9] = {r5.y, r5.z, r5.w, r6.x, r6.y, r6.z, r6.w, r7.x, r7.y};
         bounds[i] = support_radius(Binv);
+    }
+}
+
+// Per-tile sort key of particle i (per-tile max-response depth or radial depth).
+__device__ __forceinline__ uint32_t tile_depth_key(int keyMode, V3 mu, const float Binv[9], float camRadial,
+                                                   const float4* __restrict__ tileRays, uint32_t tile) {
+    if (keyMode == GF_KEY_GLOBAL_DEPTH) return __float_as_uint(camRadial);
+    return depth_key_per_tile(mu, Binv, camRadial, tileRays[2 * tile], tileRays[2 * tile + 1]);
+}
+
+// Cone-fallback particles (no valid projection, cap meeting the root cone or
+// sphere holding the camera): one warp each, counting (kEmit false) or
+// emitting keys at the scanned offsets.
+template <bool kEmit>
+__global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs fa, const uint8_t* __restrict__ mask,
+                                                      const float4* __restrict__ records,
+                                                      const float4* __restrict__ tileRays,
+                                                      uint32_t* __restrict__ counts, uint32_t* __restrict__ visibility,
+                                                      const uint64_t* __restrict__ offsets,
+                                                      uint64_t* __restrict__ keys, uint32_t* __restrict__ ids) {
+    __shared__ uint32_t stacks[8][fb::kWarpStack];
+    const uint32_t lane = threadIdx.x & 31u;
+    uint32_t* stack = stacks[threadIdx.x >> 5];
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t total = *fa.bigCount;
+    for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+        const uint32_t i = fa.big[w];
+        const float4 c0 = fa.caps[2 * size_t(i)], c1 = fa.caps[2 * size_t(i) + 1];
+        const fb::Cap c{c0.x, c0.y, c0.z, c0.w, c1.x, int(c1.y)};
+        if (!kEmit) {
+            const uint32_t n = fb::warp_tiles(fa.tree, mask, c, lane, stack, [](uint32_t, uint32_t) {});
+            if (lane == 0) {
+                counts[i] = n;
+                if (visibility != nullptr) visibility[i] = n ? 1u : 0u;
+            }
+        } else {
+            const float4 a = records[4 * size_t(i)], b = records[4 * size_t(i) + 1], cc = records[4 * size_t(i) + 2],
+                         d = records[4 * size_t(i) + 3];
+            const V3 mu = v3(a.x, a.y, a.z);
+            const float Binv[9] = {b.x, b.y, b.z, b.w, cc.x, cc.y, cc.z, cc.w, d.x};
+            const V3 cv = mu - v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]);
+            const float camRadial = finite_nonneg(__fsqrt_rn(dot3(cv, cv)), kMaxDepthValue);
+            const uint64_t begin = offsets[i];
+            const uint32_t reserved = counts[i];
+            fb::warp_tiles(fa.tree, mask, c, lane, stack, [&](uint32_t k, uint32_t tile) {
+                if (k >= reserved) return;
+                keys[begin + k] = (uint64_t(tile) << 32) | tile_depth_key(f.keyMode, mu, Binv, camRadial, tileRays, tile);
+                ids[begin + k] = i;
+            });
+        }
     }
 }
 
@@ -148,14 +599,14 @@ __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restr
                                               const float4* __restrict__ records, const uint8_t* __restrict__ mask,
                                               const float4* __restrict__ tileRays, const uint64_t* __restrict__ offsets,
                                               const uint32_t* __restrict__ counts, uint64_t* __restrict__ keys,
-                                              uint32_t* __restrict__ ids) {
+                                              uint32_t* __restrict__ ids, FallbackArgs fa) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= f.N) return;
     const float4 p0 = proj[2 * i], p1 = proj[2 * i + 1];
     Projected p;
     p.cx = p0.x; p.cy = p0.y; p.conic0 = p0.z; p.conic1 = p0.w;
     p.conic2 = p1.x; p.opacity = p1.y; p.ex = p1.z; p.ey = p1.w;
-    if (!fast_ut_valid(p)) return;
+    if (!fast_ut_valid(p)) return;  // cone-fallback particles: k_fallback_big<true>
     const float4 a = records[4 * size_t(i)], b = records[4 * size_t(i) + 1], c = records[4 * size_t(i) + 2],
                  d = records[4 * size_t(i) + 3];
     const V3 mu = v3(a.x, a.y, a.z);

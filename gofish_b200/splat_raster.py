@@ -58,6 +58,10 @@ class SplatRaster:
         cfg.sort_key = (_native.GF_KEY_GLOBAL_DEPTH if bool(_select(conf, "render.gofish.fast_global_depth_key", False))
                         else _native.GF_KEY_PER_TILE_DEPTH)
         cfg.enable_hit_counts = 1 if bool(_select(conf, "render.enable_hitcounts", True)) else 0
+        fallback = str(_select(conf, "render.gofish.fast_admission_fallback", "cone"))
+        if fallback not in ("none", "cone"):
+            raise ValueError(f"render.gofish.fast_admission_fallback must be 'none' or 'cone' (got {fallback!r})")
+        cfg.admission_fallback = _native.GF_FALLBACK_CONE if fallback == "cone" else _native.GF_FALLBACK_NONE
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())

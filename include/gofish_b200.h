@@ -71,8 +71,14 @@ typedef struct gf_tracer_config {
     int32_t k_buffer_size;     /* 0, 4, 8, 12, 16, 24 or 32 */
     int32_t sort_key;          /* GF_KEY_* */
     int32_t enable_hit_counts; /* 1: write the per-pixel hit count */
-    int32_t reserved;
+    int32_t admission_fallback; /* GF_FALLBACK_*: admission of particles without a valid projection */
 } gf_tracer_config;
+
+/* render.gofish.fast_admission_fallback (setup_3dgut.py:232-239): "none"
+ * drops particles whose unscented projection is invalid; "cone" admits them
+ * by their bounding sphere against the tile ray cones. */
+#define GF_FALLBACK_NONE 0
+#define GF_FALLBACK_CONE 1
 
 /* Per-call inputs of trace / trace_bwd / trace_inference
  * (splatRaster.cpp:259-273, :383-393, :469-500). */

@@ -60,6 +60,15 @@ def _p(a: np.ndarray):
     return a.ctypes.data_as(ctypes.c_void_p)
 
 
+def _opt(a):
+    """Contiguous float32 copy of optional ray directions (held by the caller for the call)."""
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _po(a):
+    return None if a is None else _p(a)
+
+
 def load():
     global _lib
     if _lib is not None:
@@ -70,9 +79,9 @@ def load():
     cam_p, pose_p = ctypes.POINTER(OracleCamera), ctypes.POINTER(OraclePose)
     sig = {
         "oracle_prepare_pose": (None, [vp, pose_p]),
-        "oracle_project": (i32, [cam_p, pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
+        "oracle_project": (i32, [cam_p, pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp, vp]),
         "oracle_tile_rays": (i32, [cam_p, pose_p, vp, vp, vp]),
-        "oracle_bin": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64, vp]),
+        "oracle_bin": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i32, vp, vp, i64, vp]),
         "oracle_render_forward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
         "oracle_render_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp,
                                          vp]),
@@ -126,17 +135,21 @@ def tile_grid(cam: OracleCamera) -> tuple[int, int]:
     return (cam.width + 15) // 16, (cam.height + 15) // 16
 
 
-def project(cam, pose, particles, sh, sh_degree, mask):
+def project(cam, pose, particles, sh, sh_degree, mask, ray_d=None):
+    """UT projection, radiance and tile counts; with ``ray_d`` ([H,W,3] sensor
+    ray directions) particles without a valid projection use the cone
+    fallback admission."""
     lib = load()
     particles = np.ascontiguousarray(particles, dtype=np.float32)
     sh = np.ascontiguousarray(sh, dtype=np.float32)
     mask = np.ascontiguousarray(mask, dtype=np.uint8)
+    ray_d = _opt(ray_d)
     n = particles.shape[0]
     proj = np.zeros((n, 8), dtype=np.float32)
     rgb = np.zeros((n, 3), dtype=np.float32)
     counts = np.zeros(n, dtype=np.uint32)
     lib.oracle_project(ctypes.byref(cam), ctypes.byref(pose), n, _p(particles), _p(sh), sh.shape[1] // 3,
-                       int(sh_degree), _p(mask), _p(proj), _p(rgb), _p(counts))
+                       int(sh_degree), _p(mask), _po(ray_d), _p(proj), _p(rgb), _p(counts))
     return proj, rgb, counts
 
 
@@ -149,7 +162,8 @@ def tile_rays(cam, pose, ray_o, ray_d):
     return out
 
 
-def bin(cam, pose, particles, proj, counts, mask, tile_ray_table, key_mode):
+def bin(cam, pose, particles, proj, counts, mask, tile_ray_table, key_mode, ray_d=None):
+    ray_d = _opt(ray_d)
     lib = load()
     gx, gy = tile_grid(cam)
     total = int(counts.astype(np.uint64).sum())
@@ -160,7 +174,7 @@ def bin(cam, pose, particles, proj, counts, mask, tile_ray_table, key_mode):
     got = lib.oracle_bin(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
                          _p(np.ascontiguousarray(proj)), _p(np.ascontiguousarray(counts)),
                          _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(tile_ray_table)),
-                         int(key_mode), _p(keys), _p(ids), total, _p(ranges))
+                         _po(ray_d), int(key_mode), _p(keys), _p(ids), total, _p(ranges))
     if got != total:
         raise RuntimeError("oracle_bin capacity mismatch")
     return keys[:total], ids[:total], ranges
@@ -222,12 +236,15 @@ def project_backward(pose, particles, sh, sh_degree, counts, grad_record):
     return gp, gs
 
 
-def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None):
-    """Full forward pass; returns a dict of every intermediate and output."""
+def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None, fallback=True):
+    """Full forward pass; returns a dict of every intermediate and output.
+    ``fallback`` admits particles without a valid projection by the cone test
+    (render.gofish.fast_admission_fallback = "cone")."""
     pose = prepare_pose(pose7)
-    proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask)
+    rd = ray_d if fallback else None
+    proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask, rd)
     tr = tile_rays(cam, pose, ray_o, ray_d)
-    keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode)
+    keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode, rd)
     rgba, hit_t, count = render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, ids, k, tiles)
     vis = (counts > 0).astype(np.uint32)
     return dict(pose=pose, proj=proj, rgb=rgb, counts=counts, tile_rays=tr, keys=keys, ids=ids, ranges=ranges,

@@ -388,6 +388,245 @@ uint32_t admitted_tiles(int gx, int gy, const uint8_t* mask, const Projection& p
     return n;
 }
 
+// Cone fallback admission for particles without a valid projection
+// (gutProjector.cuh:100-183 fastFallbackTiles; fast_admission_fallback =
+// "cone").  Tile ray cones over a 4x4 quadtree up to one root; a tile is
+// admitted when its cone and every ancestor's meet the particle's cap (the
+// bounding sphere seen from the camera); a sphere holding the camera admits
+// every retained tile.  Same arithmetic, in the same order, as the sm_100a
+// kernels (cos/sin forms only: +, -, *, /, sqrt and gf_logf).
+namespace fallback {
+
+constexpr float kEps = 1e-6f;
+constexpr int kFan = 4;
+
+struct Node {
+    float ax, ay, az, c;  // axis, cos phi (> 1.5: empty)
+    float s;              // sin phi
+};
+
+struct Tree {
+    std::vector<int> gx, gy;
+    std::vector<std::vector<Node>> level;
+};
+
+inline float3_ matvec_plain(const float* m, float3_ v) { return matvec(m, v); }
+
+// Unit world direction of pixel (x, y); false for a zero or non-finite ray.
+inline bool pixel_dir(const OraclePose& pose, const float* rayD, int W, int x, int y, float3_& u) {
+    const size_t p = size_t(x) + size_t(W) * size_t(y);
+    const float3_ d = f3(rayD[3 * p], rayD[3 * p + 1], rayD[3 * p + 2]);
+    const float n2 = dot(d, d);
+    if (!(n2 > 0.0f) || !gf::isfinite_f(n2)) return false;
+    const float3_ w = matvec_plain(pose.Rinv, d);
+    const float wn = sqrtf(dot(w, w));
+    u = f3(w.x / wn, w.y / wn, w.z / wn);
+    return true;
+}
+
+// Leaf cone of one tile: mean of its unit pixel rays (row sums added in row
+// order), axis = midpoint of the two mutually farthest rays found from the
+// mean (first minimum in row-major order), half-angle = the widest ray.
+Node leaf_cone(const OraclePose& pose, const float* rayD, int W, int x0, int y0, int x1, int y1) {
+    float3_ sum = f3(0.0f, 0.0f, 0.0f);
+    int all = 0;
+    for (int y = y0; y < y1; ++y) {
+        float3_ rs = f3(0.0f, 0.0f, 0.0f);
+        int rc = 0;
+        for (int x = x0; x < x1; ++x) {
+            float3_ u;
+            if (!pixel_dir(pose, rayD, W, x, y, u)) continue;
+            rs = add(rs, u);
+            ++rc;
+        }
+        if (rc > 0) sum = add(sum, rs);
+        all += rc;
+    }
+    if (all == 0) return Node{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+    const float sn = sqrtf(dot(sum, sum));
+    if (!(sn > 0.0f) || !gf::isfinite_f(sn)) return Node{0.0f, 0.0f, 1.0f, -1.0f, 0.0f};
+    const float3_ mean = f3(sum.x / sn, sum.y / sn, sum.z / sn);
+    float3_ far1 = mean, far2 = mean;
+    for (int pass = 0; pass < 2; ++pass) {
+        const float3_ ref = pass == 0 ? mean : far1;
+        float best = 2.0f;
+        float3_ bu = ref;
+        for (int y = y0; y < y1; ++y)
+            for (int x = x0; x < x1; ++x) {
+                float3_ u;
+                if (!pixel_dir(pose, rayD, W, x, y, u)) continue;
+                const float c = dot(ref, u);
+                if (c < best) {
+                    best = c;
+                    bu = u;
+                }
+            }
+        if (pass == 0) far1 = bu;
+        else far2 = bu;
+    }
+    const float3_ mid = add(far1, far2);
+    const float mn2 = sqrtf(dot(mid, mid));
+    const float3_ a = (mn2 > 1e-3f && gf::isfinite_f(mn2)) ? f3(mid.x / mn2, mid.y / mn2, mid.z / mn2) : mean;
+    float mn = 1.0f;
+    for (int y = y0; y < y1; ++y)
+        for (int x = x0; x < x1; ++x) {
+            float3_ u;
+            if (!pixel_dir(pose, rayD, W, x, y, u)) continue;
+            mn = gf::min_f(mn, dot(a, u));
+        }
+    const float cphi = gf::max_f(-1.0f, mn - kEps);
+    return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
+}
+
+// Parent cone at level l: axis = normalised sum of the 4x4 child axes in
+// row-major order; cos phi = the smallest, over the non-empty leaves under the
+// node, of cos(angle(axis, leaf axis) + phi_leaf) = (axis . a) cos phi_leaf -
+// |axis x a| sin phi_leaf, less kEps; a leaf reaching past pi makes the node
+// cover the sphere (cos -1, sin 0).
+Node parent_cone(const Tree& t, int l, int px, int py) {
+    const std::vector<Node>& ch = t.level[size_t(l) - 1];
+    const int gx = t.gx[size_t(l) - 1], gy = t.gy[size_t(l) - 1];
+    float3_ sum = f3(0.0f, 0.0f, 0.0f);
+    bool any = false;
+    for (int j = 0; j < kFan; ++j)
+        for (int i = 0; i < kFan; ++i) {
+            const int cx = px * kFan + i, cy = py * kFan + j;
+            if (cx >= gx || cy >= gy) continue;
+            const Node& a = ch[size_t(cy) * gx + cx];
+            if (a.c > 1.5f) continue;
+            any = true;
+            sum = add(sum, f3(a.ax, a.ay, a.az));
+        }
+    if (!any) return Node{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+    const float sn = sqrtf(dot(sum, sum));
+    if (!(sn > 0.0f) || !gf::isfinite_f(sn)) return Node{0.0f, 0.0f, 1.0f, -1.0f, 0.0f};
+    const float3_ a = f3(sum.x / sn, sum.y / sn, sum.z / sn);
+    int span = 1;
+    for (int k = 0; k < l; ++k) span *= kFan;
+    const int gx0 = t.gx[0], gy0 = t.gy[0];
+    const int x0 = px * span, y0 = py * span, x1 = std::min(gx0, x0 + span), y1 = std::min(gy0, y0 + span);
+    float cphi = 1.0f;
+    for (int y = y0; y < y1; ++y)
+        for (int x = x0; x < x1; ++x) {
+            const Node& c = t.level[0][size_t(y) * gx0 + x];
+            if (c.c > 1.5f) continue;
+            const float3_ ca = f3(c.ax, c.ay, c.az);
+            const float3_ cr = f3(a.y * ca.z - a.z * ca.y, a.z * ca.x - a.x * ca.z, a.x * ca.y - a.y * ca.x);
+            const float sang = sqrtf(dot(cr, cr));
+            const float cang = dot(a, ca);
+            if (sang * c.c + cang * c.s < 0.0f) return Node{a.x, a.y, a.z, -1.0f, 0.0f};
+            cphi = gf::min_f(cphi, cang * c.c - sang * c.s);
+        }
+    cphi = gf::max_f(-1.0f, cphi - kEps);
+    return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
+}
+
+Tree build(const OracleCamera& cam, const OraclePose& pose, const uint8_t* mask, const float* rayD) {
+    Tree t;
+    const int W = cam.width, H = cam.height;
+    int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
+    std::vector<Node> leaves(size_t(gx) * gy);
+    for (int tile = 0; tile < gx * gy; ++tile) {
+        Node nd{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+        if (mask[tile] != 0u) {
+            const int tx = tile % gx, ty = tile / gx;
+            const int x0 = tx * kTile, y0 = ty * kTile;
+            nd = leaf_cone(pose, rayD, W, x0, y0, std::min(W, x0 + kTile), std::min(H, y0 + kTile));
+        }
+        leaves[tile] = nd;
+    }
+    t.gx.push_back(gx);
+    t.gy.push_back(gy);
+    t.level.push_back(std::move(leaves));
+    while (!(gx == 1 && gy == 1)) {
+        const int pgx = (gx + kFan - 1) / kFan, pgy = (gy + kFan - 1) / kFan;
+        std::vector<Node> par(size_t(pgx) * pgy);
+        t.gx.push_back(pgx);
+        t.gy.push_back(pgy);
+        const int l = int(t.gx.size()) - 1;
+        for (int node = 0; node < pgx * pgy; ++node) par[node] = parent_cone(t, l, node % pgx, node / pgx);
+        gx = pgx;
+        gy = pgy;
+        t.level.push_back(std::move(par));
+    }
+    return t;
+}
+
+struct Cap {
+    float ux, uy, uz, cosA, sinA;
+    int mode;  // 0 none, 1 cone, 2 every retained tile
+};
+
+Cap cap_of(const Particle& P, const OraclePose& pose) {
+    Cap c{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0};
+    const float* B = P.B;
+    const float m00 = B[0] * B[0] + B[1] * B[1] + B[2] * B[2];
+    const float m01 = B[0] * B[3] + B[1] * B[4] + B[2] * B[5];
+    const float m02 = B[0] * B[6] + B[1] * B[7] + B[2] * B[8];
+    const float m11 = B[3] * B[3] + B[4] * B[4] + B[5] * B[5];
+    const float m12 = B[3] * B[6] + B[4] * B[7] + B[5] * B[8];
+    const float m22 = B[6] * B[6] + B[7] * B[7] + B[8] * B[8];
+    const float g0 = m00 + gf::abs_f(m01) + gf::abs_f(m02);
+    const float g1 = gf::abs_f(m01) + m11 + gf::abs_f(m12);
+    const float g2 = gf::abs_f(m02) + gf::abs_f(m12) + m22;
+    const float lam = gf::max_f(g0, gf::max_f(g1, g2));
+    const float rho = gf::min_f(kMaxAlpha, P.density);
+    const float canonical =
+        gf::min_f(2.994f, sqrtf(gf::max_f(0.0f, 2.0f * gf::gf_logf(rho / kAlphaThreshold))));
+    const float r = canonical * sqrtf(lam) * 1.001f;
+    const float3_ v = sub(P.pos, f3(pose.c[0], pose.c[1], pose.c[2]));
+    const float D = sqrtf(dot(v, v));
+    if (!(gf::isfinite_f(r) && gf::isfinite_f(D)) || !(r > 0.0f)) return c;
+    if (D <= r) {
+        c.mode = 2;
+        return c;
+    }
+    c.ux = v.x / D;
+    c.uy = v.y / D;
+    c.uz = v.z / D;
+    c.sinA = gf::min_f(1.0f, (r / D) * 1.0001f);
+    c.cosA = sqrtf(gf::max_f(0.0f, 1.0f - c.sinA * c.sinA));
+    c.mode = 1;
+    return c;
+}
+
+// Cone (axis, phi) meets cap (u, alpha) iff angle(axis, u) <= phi + alpha:
+// always once phi + alpha passes pi (sin(phi + alpha) < 0), else
+// axis . u >= cos phi cos alpha - sin phi sin alpha.
+inline bool pass(const Node& n, const Cap& c) {
+    if (n.c > 1.5f) return false;
+    if (n.s * c.cosA + n.c * c.sinA < 0.0f) return true;
+    const float d = n.ax * c.ux + n.ay * c.uy + n.az * c.uz;
+    return d >= n.c * c.cosA - n.s * c.sinA - kEps;
+}
+
+// Visits the admitted tiles of one cap in tile order.
+template <typename Visit>
+uint32_t tiles(const Tree& t, const uint8_t* mask, const Cap& c, Visit&& visit) {
+    uint32_t n = 0;
+    if (c.mode == 0) return 0;
+    const int gx = t.gx[0], gy = t.gy[0];
+    for (int tile = 0; tile < gx * gy; ++tile) {
+        if (c.mode == 2) {
+            if (mask[tile] == 0u) continue;
+        } else {
+            int x = tile % gx, y = tile / gx;
+            bool ok = true;
+            for (size_t l = 0; l < t.level.size() && ok; ++l) {
+                ok = pass(t.level[l][size_t(y) * t.gx[l] + x], c);
+                x /= kFan;
+                y /= kFan;
+            }
+            if (!ok) continue;
+        }
+        visit(tile % gx, tile / gx);
+        ++n;
+    }
+    return n;
+}
+
+}  // namespace fallback
+
 // SH radiance, gaussianParticles.cuh:181-219 / sphericalHarmonics.slang decode.
 constexpr float SH_C0 = 0.28209479177387814f;
 constexpr float SH_C1 = 0.4886025119029199f;
@@ -638,9 +877,11 @@ extern "C" {
 // admission).  proj[N*8] = center.xy, conic.xyz, opacity, extent.xy (zero when
 // the projection is invalid); rgb[N*3] precomputed radiance; counts[N].
 int oracle_project(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
-                   const float* sh, int shCoeffs, int shDegree, const uint8_t* mask, float* proj, float* rgb,
-                   uint32_t* counts) {
+                   const float* sh, int shCoeffs, int shDegree, const uint8_t* mask, const float* rayD,
+                   float* proj, float* rgb, uint32_t* counts) {
     const int gx = (cam->width + kTile - 1) / kTile, gy = (cam->height + kTile - 1) / kTile;
+    fallback::Tree tree;
+    if (rayD != nullptr) tree = fallback::build(*cam, *pose, mask, rayD);
     parallel_for(0, N, 1024, [&](int i, int) {
         const Particle P = load_particle(particles + 32 * size_t(i));
         float2_ center{0.0f, 0.0f};
@@ -672,6 +913,8 @@ int oracle_project(const OracleCamera* cam, const OraclePose* pose, int N, const
             rgb[3 * size_t(i) + ch] = gf::max_f(v, 0.0f);
         }
         counts[i] = admitted_tiles(gx, gy, mask, pr, [](int, int) {});
+        if (rayD != nullptr && !fast_ut_valid(pr) && P.density >= kAlphaThreshold)
+            counts[i] = fallback::tiles(tree, mask, fallback::cap_of(P, *pose), [](int, int) {});
     });
     return 0;
 }
@@ -760,8 +1003,11 @@ extern "C" {
 // `capacity` is too small (keys/ids are then untouched).
 int64_t oracle_bin(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
                    const float* proj, const uint32_t* counts, const uint8_t* mask, const float* tileRays,
-                   int keyMode, uint64_t* keys, uint32_t* ids, int64_t capacity, uint32_t* ranges) {
+                   const float* rayD, int keyMode, uint64_t* keys, uint32_t* ids, int64_t capacity,
+                   uint32_t* ranges) {
     const int gx = (cam->width + kTile - 1) / kTile, gy = (cam->height + kTile - 1) / kTile;
+    fallback::Tree tree;
+    if (rayD != nullptr) tree = fallback::build(*cam, *pose, mask, rayD);
     std::vector<uint64_t> offsets(static_cast<size_t>(N) + 1, 0);
     for (int i = 0; i < N; ++i) offsets[i + 1] = offsets[i] + counts[i];
     const int64_t total = int64_t(offsets[N]);
@@ -776,14 +1022,17 @@ int64_t oracle_bin(const OracleCamera* cam, const OraclePose* pose, int N, const
         pr.extent = {o[6], o[7]};
         uint64_t k = offsets[i];
         const uint64_t end = offsets[i + 1];
-        admitted_tiles(gx, gy, mask, pr, [&](int x, int y) {
+        auto emit = [&](int x, int y) {
             if (k < end) {
                 const uint32_t tile = uint32_t(y * gx + x);
                 keys[k] = (uint64_t(tile) << 32) | depth_key(keyMode, P, *pose, tileRays + 8 * size_t(tile));
                 ids[k] = uint32_t(i);
             }
             ++k;
-        });
+        };
+        admitted_tiles(gx, gy, mask, pr, emit);
+        if (rayD != nullptr && !fast_ut_valid(pr) && P.density >= kAlphaThreshold)
+            fallback::tiles(tree, mask, fallback::cap_of(P, *pose), emit);
     });
     // Stable sort of (key, id) pairs by key.
     std::vector<uint64_t> order(static_cast<size_t>(total));

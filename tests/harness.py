@@ -67,9 +67,9 @@ def small_case(seed: int = 7, n: int = 20_000, size: int = 256, sh_degree: int =
     return make_case(scene, cam, pose)
 
 
-def oracle_forward(case: Case, k: int, key_mode: int, tiles=None):
+def oracle_forward(case: Case, k: int, key_mode: int, tiles=None, fallback: bool = True):
     return oracle.trace(case.ocam, case.pose, case.particles, case.features, case.scene.sh_degree, case.ray_o,
-                        case.ray_d, case.tmask, k, key_mode, tiles)
+                        case.ray_d, case.tmask, k, key_mode, tiles, fallback)
 
 
 def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
@@ -80,7 +80,7 @@ def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
 class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
-    def __init__(self, case: Case, k: int, key_mode: int, device):
+    def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True):
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -88,7 +88,9 @@ class GpuTracer:
         self.torch = torch
         self.case = case
         self.device = device
-        conf = {"render": {"splat": {"k_buffer_size": k}, "gofish": {"fast_global_depth_key": key_mode == 1},
+        conf = {"render": {"splat": {"k_buffer_size": k},
+                           "gofish": {"fast_global_depth_key": key_mode == 1,
+                                      "fast_admission_fallback": "cone" if fallback else "none"},
                            "enable_hitcounts": True}}
         self.raster = SplatRaster(conf)
         self.token = "test-token"
@@ -136,3 +138,30 @@ def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
 def psnr(a: np.ndarray, b: np.ndarray) -> float:
     mse = float(np.mean((np.asarray(a, np.float64) - np.asarray(b, np.float64)) ** 2))
     return math.inf if mse == 0 else 10 * math.log10(1.0 / mse)
+
+
+def horizon_case(seed: int = 31, n: int = 6000, big: int = 300, size: int = 192) -> Case:
+    """A scene with large Gaussians (scale 0.5-2 m) within 1 m of the camera,
+    many straddling the 100 degree horizon of a 200 degree fisheye or holding
+    the camera centre: their unscented projection is invalid, so only the cone
+    fallback admits them."""
+    import dataclasses as dc
+
+    scene = random_scene(n, 1, seed)
+    rng = np.random.default_rng(seed + 1)
+    u = rng.standard_normal((big, 3))
+    u /= np.linalg.norm(u, axis=1, keepdims=True)
+    u[: big // 2, 2] = rng.uniform(-0.25, 0.1, big // 2)  # near the horizon of a +z camera
+    u /= np.linalg.norm(u, axis=1, keepdims=True)
+    pos = (u * rng.uniform(0.05, 3.0, (big, 1))).astype(np.float32)
+    scales = rng.uniform(0.5, 2.0, (big, 3)).astype(np.float32) * np.float32(0.12)
+    positions = np.concatenate([scene.positions, pos]).astype(np.float32)
+    sc = np.concatenate([scene.scales, scales]).astype(np.float32)
+    q = rng.standard_normal((big, 4))
+    rot = np.concatenate([scene.rotations, (q / np.linalg.norm(q, axis=1, keepdims=True)).astype(np.float32)])
+    dens = np.concatenate([scene.density, rng.uniform(0.05, 0.6, (big, 1)).astype(np.float32)])
+    feats = np.concatenate([scene.features, (rng.standard_normal((big, scene.features.shape[1])) * 0.2)
+                            .astype(np.float32)])
+    scene = dc.replace(scene, positions=positions, scales=sc, rotations=rot, density=dens, features=feats)
+    cam = fisheye_camera(size, size, 200.0, random_kb_coefficients(rng, 200.0))
+    return make_case(scene, cam, IDENTITY_POSE.copy())

@@ -86,18 +86,26 @@ def test_ragged_resolution_and_partial_mask(cuda_device):
     assert np.all(got["hit_t"][masked_px] == 1e6)
 
 
-def test_empty_and_invisible_scenes(cuda_device):
+@pytest.mark.parametrize("fallback", [False, True])
+def test_particles_inside_the_near_radius(cuda_device, fallback):
     case = harness.small_case(seed=3, n=500, size=64, random_pose=False)
-    # every particle behind the near radius: no projection, no intersection
+    # every particle inside the 0.2 m radial near gate: no valid projection.
+    # Without a fallback nothing is admitted; the cone fallback admits them.
     scene = case.scene
     scene.positions[:] = np.array([0.05, 0.0, 0.05], dtype=np.float32)
     case = harness.make_case(scene, case.camera, case.pose)
-    ref = harness.oracle_forward(case, 16, 0)
-    gpu = harness.GpuTracer(case, 16, 0, cuda_device)
+    ref = harness.oracle_forward(case, 16, 0, fallback=fallback)
+    gpu = harness.GpuTracer(case, 16, 0, cuda_device, fallback=fallback)
     got = gpu.forward()
-    assert got["keys"].size == 0 and ref["keys"].size == 0
     _compare_forward(ref, got)
-    assert np.all(got["hit_count"] == 0)
+    if fallback:
+        # every particle is admitted (wide caps); those whose support sphere
+        # holds the camera take every retained tile
+        assert np.all(ref["counts"] > 0)
+        assert int(ref["counts"].max()) == int(case.tmask.sum())
+    else:
+        assert got["keys"].size == 0 and ref["keys"].size == 0
+        assert np.all(got["hit_count"] == 0)
 
 
 def test_deterministic_repeat(cuda_device):
@@ -149,6 +157,35 @@ def test_kbuffer_exact_ties_from_duplicated_particles(cuda_device, k):
     g_rgba = rng2.uniform(-1, 1, ref["rgba"].shape).astype(np.float32)
     g_hit = np.zeros(ref["hit_t"].shape, dtype=np.float32)
     gp_ref, gs_ref, _ = harness.oracle_backward(case, ref, k, g_rgba, g_hit)
+    gp, gs = gpu.backward(g_rgba, g_hit)
+    assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
+    assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("fallback", [True, False])
+def test_horizon_particles_cone_fallback(cuda_device, fallback):
+    """Large Gaussians around the camera (many straddle the 100 degree horizon
+    or hold the camera centre) have no valid projection: the cone fallback
+    admits them (single-thread walks and warp-cooperative ones), 'none' drops
+    them; either way keys, ranges and hit counts match the oracle bit for bit."""
+    case = harness.horizon_case()
+    ref = harness.oracle_forward(case, 16, 0, fallback=fallback)
+    gpu = harness.GpuTracer(case, 16, 0, cuda_device, fallback=fallback)
+    got = gpu.forward()
+    _compare_forward(ref, got)
+    big = slice(case.scene.num - 300, case.scene.num)
+    invalid = ref["proj"][big, 6] <= 1e-6
+    assert invalid.sum() > 50
+    admitted = ref["counts"][big][invalid]
+    if fallback:
+        assert (admitted > 0).mean() > 0.5
+        assert admitted.max() == case.tmask.sum()  # spheres holding the camera admit every retained tile
+    else:
+        assert admitted.max() == 0
+    rng = np.random.default_rng(8)
+    g_rgba = rng.uniform(-1, 1, ref["rgba"].shape).astype(np.float32)
+    g_hit = np.zeros(ref["hit_t"].shape, dtype=np.float32)
+    gp_ref, gs_ref, _ = harness.oracle_backward(case, ref, 16, g_rgba, g_hit)
     gp, gs = gpu.backward(g_rgba, g_hit)
     assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
     assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2

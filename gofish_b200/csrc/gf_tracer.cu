@@ -274,15 +274,17 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
                 gx = (gx + gf::fb::kFan - 1) / gf::fb::kFan;
                 gy = (gy + gf::fb::kFan - 1) / gf::fb::kFan;
             }
-            if (int e = t->coneA.ensure(sizeof(float4) * nodes, stream)) return e;
-            if (int e = t->coneS.ensure(sizeof(float) * nodes, stream)) return e;
+            tr.second = nodes;     // the leaves' second cones follow the levels,
+            tr.sums = nodes + T;   // then one ray sum per node
+            if (int e = t->coneA.ensure(sizeof(float4) * (2 * size_t(nodes) + T), stream)) return e;
+            if (int e = t->coneS.ensure(sizeof(float) * (size_t(nodes) + T), stream)) return e;
             float4* A = t->coneA.as<float4>();
             float* S = t->coneS.as<float>();
             tr.A = A;
             tr.S = S;
             // one warp per tile, four tiles per block
             gf::fb::k_tile_cones<<<(T + 3) / 4, 128, 0, stream>>>(f, mask->buf.as<uint8_t>(), in->ray_direction, A,
-                                                                  S);
+                                                                  S, tr.second, tr.sums);
             t->launches += 1;
             GF_LAUNCH_CHECK();
             for (int l = 1; l < tr.n; ++l) {

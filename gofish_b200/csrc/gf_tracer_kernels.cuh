@@ -79,6 +79,8 @@ struct TileTree {
     int n;
     int gx[kMaxLevels], gy[kMaxLevels];
     uint32_t offset[kMaxLevels];
+    uint32_t second;  // offset of the leaves' second cones
+    uint32_t sums;    // offset (in A) of each node's sum of unit pixel rays
     const float4* A;  // axis.xyz, cos phi (> 1.5: empty)
     const float* S;   // sin phi
 };
@@ -126,13 +128,20 @@ __device__ __forceinline__ Cap fallback_cap(const float B[9], V3 mu, float densi
 // Cone (axis, phi) meets cap (u, alpha) iff angle(axis, u) <= phi + alpha:
 // always when phi + alpha >= pi (sin(phi + alpha) < 0), else
 // axis . u >= cos(phi + alpha) = cos phi cos alpha - sin phi sin alpha.
-__device__ __forceinline__ bool node_pass(const TileTree& t, int l, uint32_t node, const Cap& c) {
-    const float4 A = t.A[t.offset[l] + node];
+__device__ __forceinline__ bool cone_meets(const TileTree& t, uint32_t k, const Cap& c) {
+    const float4 A = t.A[k];
     if (A.w > 1.5f) return false;
-    const float S = t.S[t.offset[l] + node];
+    const float S = t.S[k];
     if (S * c.cosA + A.w * c.sinA < 0.0f) return true;
     const float d = A.x * c.ux + A.y * c.uy + A.z * c.uz;
     return d >= A.w * c.cosA - S * c.sinA - kEps;
+}
+
+// A leaf (tile) holds two cones, one per cluster of its pixel rays; inner
+// nodes hold one.
+__device__ __forceinline__ bool node_pass(const TileTree& t, int l, uint32_t node, const Cap& c) {
+    if (cone_meets(t, t.offset[l] + node, c)) return true;
+    return l == 0 && cone_meets(t, t.second + node, c);
 }
 
 // Does every ancestor (levels >= 2) of level-1 node (x, y) meet the cap?
@@ -236,9 +245,14 @@ __device__ __forceinline__ uint32_t warp_tiles(const TileTree& t, const uint8_t*
     return n;
 }
 
-// Leaf cones: one warp per tile, lane r < 16 walking pixel row r; the row
-// partials (sums, first minima) are combined in row order, so the result is
-// the same float for float as the oracle's row-then-rows loop.
+// Leaf cones: one warp per tile, lane r < 16 walking pixel row r; row
+// partials (sums, first minima) are combined in row order, so every value is
+// the oracle's float for float.  The tile's rays are split in two clusters by
+// the nearer of the two mutually farthest rays (far1 the farthest from the
+// mean ray, far2 the farthest from far1; ties to far1), so that a tile mixing
+// rim rays with the forward rays of pixels outside the image circle gets two
+// narrow cones instead of one wide one.  Cone k: axis = normalised sum of its
+// rays, cos phi = smallest cosine to the axis less kEps.
 __device__ __forceinline__ bool pixel_dir(const FrameArgs& f, const float* __restrict__ rayD, int x, int y, V3& u) {
     const size_t p = size_t(x) + size_t(f.W) * size_t(y);
     const V3 d = v3(rayD[3 * p], rayD[3 * p + 1], rayD[3 * p + 2]);
@@ -250,9 +264,33 @@ __device__ __forceinline__ bool pixel_dir(const FrameArgs& f, const float* __res
     return true;
 }
 
+__device__ __forceinline__ V3 shfl_v3(V3 v, int r) {
+    return v3(__shfl_sync(0xffffffffu, v.x, r), __shfl_sync(0xffffffffu, v.y, r), __shfl_sync(0xffffffffu, v.z, r));
+}
+
+// Sum of the row partials in row order (rows with no ray skipped).
+__device__ __forceinline__ V3 rows_sum(V3 part, int cnt, int& all) {
+    V3 total = v3(0.0f, 0.0f, 0.0f);
+    all = 0;
+    for (int r = 0; r < kTile; ++r) {
+        const V3 rs = shfl_v3(part, r);
+        const int rc = __shfl_sync(0xffffffffu, cnt, r);
+        if (rc > 0) total = total + rs;
+        all += rc;
+    }
+    return total;
+}
+
+// Cone of axis a (or the whole sphere for a degenerate sum) from its minimum cosine.
+__device__ __forceinline__ void store_cone(float4* A, float* S, uint32_t k, V3 a, float mn) {
+    const float cphi = max_f(-1.0f, mn - kEps);
+    A[k] = make_float4(a.x, a.y, a.z, cphi);
+    S[k] = __fsqrt_rn(max_f(0.0f, 1.0f - cphi * cphi));
+}
+
 __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* __restrict__ mask,
                                                     const float* __restrict__ rayD, float4* __restrict__ A,
-                                                    float* __restrict__ S) {
+                                                    float* __restrict__ S, uint32_t second, uint32_t sums) {
     const int tile = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (tile >= f.gx * f.gy) return;  // warp-uniform
@@ -260,7 +298,8 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
     const int x0 = tx * kTile, y0 = ty * kTile, x1 = min(f.W, x0 + kTile), y1 = min(f.H, y0 + kTile);
     const int y = y0 + lane;
     const bool row = lane < kTile && y < y1 && mask[tile] != 0u;
-    // pass 0: row sums and counts
+    const float4 empty = make_float4(0.0f, 0.0f, 1.0f, 2.0f);
+    // pass 0: the mean ray
     V3 sum = v3(0.0f, 0.0f, 0.0f);
     int count = 0;
     if (row)
@@ -270,19 +309,15 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
             sum = sum + u;
             ++count;
         }
-    V3 total = v3(0.0f, 0.0f, 0.0f);
     int all = 0;
-    for (int r = 0; r < kTile; ++r) {
-        const V3 rs = v3(__shfl_sync(0xffffffffu, sum.x, r), __shfl_sync(0xffffffffu, sum.y, r),
-                         __shfl_sync(0xffffffffu, sum.z, r));
-        const int rc = __shfl_sync(0xffffffffu, count, r);
-        if (rc > 0) total = total + rs;
-        all += rc;
-    }
+    const V3 total = rows_sum(sum, count, all);
+    if (lane == 0) A[sums + tile] = make_float4(total.x, total.y, total.z, 0.0f);
     if (mask[tile] == 0u || all == 0) {
         if (lane == 0) {
-            A[tile] = make_float4(0.0f, 0.0f, 1.0f, 2.0f);
+            A[tile] = empty;
             S[tile] = 0.0f;
+            A[second + tile] = empty;
+            S[second + tile] = 0.0f;
         }
         return;
     }
@@ -291,6 +326,8 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
         if (lane == 0) {
             A[tile] = make_float4(0.0f, 0.0f, 1.0f, -1.0f);
             S[tile] = 0.0f;
+            A[second + tile] = empty;
+            S[second + tile] = 0.0f;
         }
         return;
     }
@@ -315,8 +352,7 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
         V3 gu = ref;
         for (int r = 0; r < kTile; ++r) {
             const float rb = __shfl_sync(0xffffffffu, best, r);
-            const V3 ru = v3(__shfl_sync(0xffffffffu, bu.x, r), __shfl_sync(0xffffffffu, bu.y, r),
-                             __shfl_sync(0xffffffffu, bu.z, r));
+            const V3 ru = shfl_v3(bu, r);
             if (rb < gbest) {
                 gbest = rb;
                 gu = ru;
@@ -325,32 +361,72 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
         if (pass == 0) far1 = gu;
         else far2 = gu;
     }
-    const V3 mid = far1 + far2;
-    const float mn2 = __fsqrt_rn(dot3(mid, mid));
-    const V3 ax = (mn2 > 1e-3f && isfinite_f(mn2)) ? v3(mid.x / mn2, mid.y / mn2, mid.z / mn2) : mean;
-    // pass 3: the smallest cosine to the axis
-    float mn = 1.0f;
+    // pass 3: cluster sums
+    V3 s0 = v3(0.0f, 0.0f, 0.0f), s1 = v3(0.0f, 0.0f, 0.0f);
+    int n0 = 0, n1 = 0;
     if (row)
         for (int x = x0; x < x1; ++x) {
             V3 u;
             if (!pixel_dir(f, rayD, x, y, u)) continue;
-            mn = min_f(mn, dot3(ax, u));
+            if (dot3(far1, u) >= dot3(far2, u)) {
+                s0 = s0 + u;
+                ++n0;
+            } else {
+                s1 = s1 + u;
+                ++n1;
+            }
         }
-    float gmn = 1.0f;
-    for (int r = 0; r < kTile; ++r) gmn = min_f(gmn, __shfl_sync(0xffffffffu, mn, r));
+    int all0 = 0, all1 = 0;
+    const V3 t0 = rows_sum(s0, n0, all0);
+    const V3 t1 = rows_sum(s1, n1, all1);
+    const float l0 = __fsqrt_rn(dot3(t0, t0)), l1 = __fsqrt_rn(dot3(t1, t1));
+    const bool ok0 = l0 > 0.0f && isfinite_f(l0), ok1 = l1 > 0.0f && isfinite_f(l1);
+    const V3 a0 = ok0 ? v3(t0.x / l0, t0.y / l0, t0.z / l0) : mean;
+    const V3 a1 = ok1 ? v3(t1.x / l1, t1.y / l1, t1.z / l1) : mean;
+    // pass 4: the smallest cosine of each cluster to its axis
+    float m0 = 1.0f, m1 = 1.0f;
+    if (row)
+        for (int x = x0; x < x1; ++x) {
+            V3 u;
+            if (!pixel_dir(f, rayD, x, y, u)) continue;
+            if (dot3(far1, u) >= dot3(far2, u)) m0 = min_f(m0, dot3(a0, u));
+            else m1 = min_f(m1, dot3(a1, u));
+        }
+    for (int r = 0; r < kTile; ++r) {
+        const float r0 = __shfl_sync(0xffffffffu, m0, r), r1 = __shfl_sync(0xffffffffu, m1, r);
+        if (lane == 0) {
+            m0 = min_f(m0, r0);
+            m1 = min_f(m1, r1);
+        }
+    }
     if (lane != 0) return;
-    const float cphi = max_f(-1.0f, gmn - kEps);
-    A[tile] = make_float4(ax.x, ax.y, ax.z, cphi);
-    S[tile] = __fsqrt_rn(max_f(0.0f, 1.0f - cphi * cphi));
+    if (ok0) store_cone(A, S, uint32_t(tile), a0, m0);
+    else if (all0 > 0) A[tile] = make_float4(a0.x, a0.y, a0.z, -1.0f), S[tile] = 0.0f;
+    else A[tile] = empty, S[tile] = 0.0f;
+    if (ok1) store_cone(A, S, second + uint32_t(tile), a1, m1);
+    else if (all1 > 0) A[second + tile] = make_float4(a1.x, a1.y, a1.z, -1.0f), S[second + tile] = 0.0f;
+    else A[second + tile] = empty, S[second + tile] = 0.0f;
 }
 
-// Parent cones of level l >= 1, one block per node: axis = normalised sum of
-// the 4x4 child axes (row-major order); cos phi = the smallest, over the
-// non-empty leaves under the node, of cos(angle(axis, leaf axis) + phi_leaf)
-// = (axis . a) cos phi_leaf - |axis x a| sin phi_leaf, less kEps; a leaf
-// reaching past pi (sin of the sum < 0) makes the node cover the sphere
-// (cos -1, sin 0).  A minimum is exact in any order, so the block reduction
-// gives the oracle's value.
+// Parent cones of level l >= 1, one block per node: the node's ray sum is the
+// sum of its 4x4 children's (row-major order) and its axis that sum
+// normalised, the mean direction of the pixel rays under it; the node is
+// empty when all its children are; cos phi = the smallest, over the non-empty
+// cones of the leaves
+// under the node, of cos(angle(axis, a) + phi_a) = (axis . a) cos phi_a -
+// |axis x a| sin phi_a, less kEps; a cone reaching past pi (sin of the sum
+// < 0) makes the node cover the sphere (cos -1, sin 0).  A minimum is exact
+// in any order, so the block reduction gives the oracle's value.
+__device__ __forceinline__ void bound_cone(V3 ax, float4 a, float cs, float& mn, bool& full) {
+    if (a.w > 1.5f) return;
+    const V3 ca = v3(a.x, a.y, a.z);
+    const V3 cr = v3(ax.y * ca.z - ax.z * ca.y, ax.z * ca.x - ax.x * ca.z, ax.x * ca.y - ax.y * ca.x);
+    const float sang = __fsqrt_rn(dot3(cr, cr));
+    const float cang = dot3(ax, ca);
+    if (sang * a.w + cang * cs < 0.0f) full = true;
+    else mn = min_f(mn, cang * a.w - sang * cs);
+}
+
 __global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, float4* __restrict__ A,
                                                          float* __restrict__ S) {
     __shared__ float axis[4];
@@ -365,11 +441,13 @@ __global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, floa
             for (int i = 0; i < kFan; ++i) {
                 const int cx = px * kFan + i, cy = py * kFan + j;
                 if (cx >= cgx || cy >= cgy) continue;
-                const float4 a = A[t.offset[l - 1] + uint32_t(cy * cgx + cx)];
-                if (a.w > 1.5f) continue;
-                any = true;
-                sum = sum + v3(a.x, a.y, a.z);
+                const uint32_t child = t.offset[l - 1] + uint32_t(cy * cgx + cx);
+                const float4 r = A[t.sums + child];
+                sum = sum + v3(r.x, r.y, r.z);
+                if (A[child].w <= 1.5f) any = true;
+                if (l == 1 && A[t.second + uint32_t(cy * cgx + cx)].w <= 1.5f) any = true;
             }
+        A[t.sums + t.offset[l] + uint32_t(node)] = make_float4(sum.x, sum.y, sum.z, 0.0f);
         const float sn = __fsqrt_rn(dot3(sum, sum));
         const bool ok = sn > 0.0f && isfinite_f(sn);
         axis[0] = ok ? sum.x / sn : 0.0f;
@@ -395,16 +473,9 @@ __global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, floa
     float mn = 1.0f;
     bool full = false;
     for (int k = threadIdx.x; k < cnt; k += blockDim.x) {
-        const int leaf = (y0 + k / w) * gx0 + x0 + k % w;
-        const float4 a = A[leaf];
-        if (a.w > 1.5f) continue;
-        const float cs = S[leaf];
-        const V3 ca = v3(a.x, a.y, a.z);
-        const V3 cr = v3(ax.y * ca.z - ax.z * ca.y, ax.z * ca.x - ax.x * ca.z, ax.x * ca.y - ax.y * ca.x);
-        const float sang = __fsqrt_rn(dot3(cr, cr));
-        const float cang = dot3(ax, ca);
-        if (sang * a.w + cang * cs < 0.0f) full = true;
-        else mn = min_f(mn, cang * a.w - sang * cs);
+        const uint32_t leaf = uint32_t((y0 + k / w) * gx0 + x0 + k % w);
+        bound_cone(ax, A[leaf], S[leaf], mn, full);
+        bound_cone(ax, A[t.second + leaf], S[t.second + leaf], mn, full);
     }
     full = __syncthreads_or(full) != 0;
     for (int o = 16; o > 0; o >>= 1) mn = min_f(mn, __shfl_xor_sync(0xffffffffu, mn, o));

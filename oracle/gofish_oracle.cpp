@@ -408,6 +408,8 @@ struct Node {
 struct Tree {
     std::vector<int> gx, gy;
     std::vector<std::vector<Node>> level;
+    std::vector<Node> second;                // the leaves' second cones
+    std::vector<std::vector<float3_>> sums;  // per node: sum of its unit pixel rays
 };
 
 inline float3_ matvec_plain(const float* m, float3_ v) { return matvec(m, v); }
@@ -424,27 +426,51 @@ inline bool pixel_dir(const OraclePose& pose, const float* rayD, int W, int x, i
     return true;
 }
 
-// Leaf cone of one tile: mean of its unit pixel rays (row sums added in row
-// order), axis = midpoint of the two mutually farthest rays found from the
-// mean (first minimum in row-major order), half-angle = the widest ray.
-Node leaf_cone(const OraclePose& pose, const float* rayD, int W, int x0, int y0, int x1, int y1) {
+// Sum of the unit rays of rows y0..y1 for which keep(u) holds, each row summed
+// left to right and the non-empty row sums added in row order.
+template <typename Keep>
+float3_ row_sums(const OraclePose& pose, const float* rayD, int W, int x0, int y0, int x1, int y1, Keep&& keep,
+                 int& all) {
     float3_ sum = f3(0.0f, 0.0f, 0.0f);
-    int all = 0;
+    all = 0;
     for (int y = y0; y < y1; ++y) {
         float3_ rs = f3(0.0f, 0.0f, 0.0f);
         int rc = 0;
         for (int x = x0; x < x1; ++x) {
             float3_ u;
-            if (!pixel_dir(pose, rayD, W, x, y, u)) continue;
+            if (!pixel_dir(pose, rayD, W, x, y, u) || !keep(u)) continue;
             rs = add(rs, u);
             ++rc;
         }
         if (rc > 0) sum = add(sum, rs);
         all += rc;
     }
-    if (all == 0) return Node{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+    return sum;
+}
+
+inline Node cone_from(float3_ a, float mn) {
+    const float cphi = gf::max_f(-1.0f, mn - kEps);
+    return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
+}
+
+// The two cones of one tile: its unit pixel rays split by the nearer of the
+// two mutually farthest rays (far1 = first ray farthest from the mean ray in
+// row-major order, far2 = first ray farthest from far1; ties to far1); cone k
+// = normalised sum of its rays, cos phi = smallest cosine to that axis less
+// kEps.  A tile mixing rim rays with the forward rays of pixels outside the
+// image circle gets two narrow cones instead of one wide one.
+void leaf_cones(const OraclePose& pose, const float* rayD, int W, int x0, int y0, int x1, int y1, Node& c0,
+                Node& c1, float3_& sum) {
+    const Node empty{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+    c0 = c1 = empty;
+    int all = 0;
+    sum = row_sums(pose, rayD, W, x0, y0, x1, y1, [](float3_) { return true; }, all);
+    if (all == 0) return;
     const float sn = sqrtf(dot(sum, sum));
-    if (!(sn > 0.0f) || !gf::isfinite_f(sn)) return Node{0.0f, 0.0f, 1.0f, -1.0f, 0.0f};
+    if (!(sn > 0.0f) || !gf::isfinite_f(sn)) {
+        c0 = Node{0.0f, 0.0f, 1.0f, -1.0f, 0.0f};
+        return;
+    }
     const float3_ mean = f3(sum.x / sn, sum.y / sn, sum.z / sn);
     float3_ far1 = mean, far2 = mean;
     for (int pass = 0; pass < 2; ++pass) {
@@ -464,38 +490,61 @@ Node leaf_cone(const OraclePose& pose, const float* rayD, int W, int x0, int y0,
         if (pass == 0) far1 = bu;
         else far2 = bu;
     }
-    const float3_ mid = add(far1, far2);
-    const float mn2 = sqrtf(dot(mid, mid));
-    const float3_ a = (mn2 > 1e-3f && gf::isfinite_f(mn2)) ? f3(mid.x / mn2, mid.y / mn2, mid.z / mn2) : mean;
-    float mn = 1.0f;
+    auto first = [&](float3_ u) { return dot(far1, u) >= dot(far2, u); };
+    int all0 = 0, all1 = 0;
+    const float3_ t0 = row_sums(pose, rayD, W, x0, y0, x1, y1, first, all0);
+    const float3_ t1 = row_sums(pose, rayD, W, x0, y0, x1, y1, [&](float3_ u) { return !first(u); }, all1);
+    const float l0 = sqrtf(dot(t0, t0)), l1 = sqrtf(dot(t1, t1));
+    const bool ok0 = l0 > 0.0f && gf::isfinite_f(l0), ok1 = l1 > 0.0f && gf::isfinite_f(l1);
+    const float3_ a0 = ok0 ? f3(t0.x / l0, t0.y / l0, t0.z / l0) : mean;
+    const float3_ a1 = ok1 ? f3(t1.x / l1, t1.y / l1, t1.z / l1) : mean;
+    float m0 = 1.0f, m1 = 1.0f;
     for (int y = y0; y < y1; ++y)
         for (int x = x0; x < x1; ++x) {
             float3_ u;
             if (!pixel_dir(pose, rayD, W, x, y, u)) continue;
-            mn = gf::min_f(mn, dot(a, u));
+            if (first(u)) m0 = gf::min_f(m0, dot(a0, u));
+            else m1 = gf::min_f(m1, dot(a1, u));
         }
-    const float cphi = gf::max_f(-1.0f, mn - kEps);
-    return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
+    if (ok0) c0 = cone_from(a0, m0);
+    else if (all0 > 0) c0 = Node{a0.x, a0.y, a0.z, -1.0f, 0.0f};
+    if (ok1) c1 = cone_from(a1, m1);
+    else if (all1 > 0) c1 = Node{a1.x, a1.y, a1.z, -1.0f, 0.0f};
 }
 
-// Parent cone at level l: axis = normalised sum of the 4x4 child axes in
-// row-major order; cos phi = the smallest, over the non-empty leaves under the
-// node, of cos(angle(axis, leaf axis) + phi_leaf) = (axis . a) cos phi_leaf -
-// |axis x a| sin phi_leaf, less kEps; a leaf reaching past pi makes the node
-// cover the sphere (cos -1, sin 0).
-Node parent_cone(const Tree& t, int l, int px, int py) {
+// cos(angle(axis, a) + phi_a) of one non-empty cone into the running minimum;
+// false once the sum reaches past pi.
+inline bool bound_cone(float3_ a, const Node& c, float& cphi) {
+    if (c.c > 1.5f) return true;
+    const float3_ ca = f3(c.ax, c.ay, c.az);
+    const float3_ cr = f3(a.y * ca.z - a.z * ca.y, a.z * ca.x - a.x * ca.z, a.x * ca.y - a.y * ca.x);
+    const float sang = sqrtf(dot(cr, cr));
+    const float cang = dot(a, ca);
+    if (sang * c.c + cang * c.s < 0.0f) return false;
+    cphi = gf::min_f(cphi, cang * c.c - sang * c.s);
+    return true;
+}
+
+// Parent cone at level l: ray sum = the sum of the 4x4 children's ray sums in
+// row-major order, axis = that sum normalised (the mean direction of the
+// pixel rays under the node), empty when every child is; cos phi = the
+// smallest, over the non-empty cones of the leaves under the
+// node, of cos(angle(axis, a) + phi_a) = (axis . a) cos phi_a - |axis x a|
+// sin phi_a, less kEps; a cone reaching past pi makes the node cover the
+// sphere (cos -1, sin 0).
+Node parent_cone(const Tree& t, int l, int px, int py, float3_& sum) {
     const std::vector<Node>& ch = t.level[size_t(l) - 1];
+    const std::vector<float3_>& cs = t.sums[size_t(l) - 1];
     const int gx = t.gx[size_t(l) - 1], gy = t.gy[size_t(l) - 1];
-    float3_ sum = f3(0.0f, 0.0f, 0.0f);
+    sum = f3(0.0f, 0.0f, 0.0f);
     bool any = false;
     for (int j = 0; j < kFan; ++j)
         for (int i = 0; i < kFan; ++i) {
             const int cx = px * kFan + i, cy = py * kFan + j;
             if (cx >= gx || cy >= gy) continue;
-            const Node& a = ch[size_t(cy) * gx + cx];
-            if (a.c > 1.5f) continue;
-            any = true;
-            sum = add(sum, f3(a.ax, a.ay, a.az));
+            const size_t k = size_t(cy) * gx + cx;
+            sum = add(sum, cs[k]);
+            if (ch[k].c <= 1.5f || (l == 1 && t.second[k].c <= 1.5f)) any = true;
         }
     if (!any) return Node{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
     const float sn = sqrtf(dot(sum, sum));
@@ -508,14 +557,9 @@ Node parent_cone(const Tree& t, int l, int px, int py) {
     float cphi = 1.0f;
     for (int y = y0; y < y1; ++y)
         for (int x = x0; x < x1; ++x) {
-            const Node& c = t.level[0][size_t(y) * gx0 + x];
-            if (c.c > 1.5f) continue;
-            const float3_ ca = f3(c.ax, c.ay, c.az);
-            const float3_ cr = f3(a.y * ca.z - a.z * ca.y, a.z * ca.x - a.x * ca.z, a.x * ca.y - a.y * ca.x);
-            const float sang = sqrtf(dot(cr, cr));
-            const float cang = dot(a, ca);
-            if (sang * c.c + cang * c.s < 0.0f) return Node{a.x, a.y, a.z, -1.0f, 0.0f};
-            cphi = gf::min_f(cphi, cang * c.c - sang * c.s);
+            const size_t k = size_t(y) * gx0 + x;
+            if (!bound_cone(a, t.level[0][k], cphi) || !bound_cone(a, t.second[k], cphi))
+                return Node{a.x, a.y, a.z, -1.0f, 0.0f};
         }
     cphi = gf::max_f(-1.0f, cphi - kEps);
     return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
@@ -525,16 +569,18 @@ Tree build(const OracleCamera& cam, const OraclePose& pose, const uint8_t* mask,
     Tree t;
     const int W = cam.width, H = cam.height;
     int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
-    std::vector<Node> leaves(size_t(gx) * gy);
+    const Node empty{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
+    std::vector<Node> leaves(size_t(gx) * gy, empty);
+    std::vector<float3_> leafSums(size_t(gx) * gy, f3(0.0f, 0.0f, 0.0f));
+    t.second.assign(size_t(gx) * gy, empty);
     for (int tile = 0; tile < gx * gy; ++tile) {
-        Node nd{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
-        if (mask[tile] != 0u) {
-            const int tx = tile % gx, ty = tile / gx;
-            const int x0 = tx * kTile, y0 = ty * kTile;
-            nd = leaf_cone(pose, rayD, W, x0, y0, std::min(W, x0 + kTile), std::min(H, y0 + kTile));
-        }
-        leaves[tile] = nd;
+        if (mask[tile] == 0u) continue;
+        const int tx = tile % gx, ty = tile / gx;
+        const int x0 = tx * kTile, y0 = ty * kTile;
+        leaf_cones(pose, rayD, W, x0, y0, std::min(W, x0 + kTile), std::min(H, y0 + kTile), leaves[tile],
+                   t.second[tile], leafSums[tile]);
     }
+    t.sums.push_back(std::move(leafSums));
     t.gx.push_back(gx);
     t.gy.push_back(gy);
     t.level.push_back(std::move(leaves));
@@ -544,10 +590,13 @@ Tree build(const OracleCamera& cam, const OraclePose& pose, const uint8_t* mask,
         t.gx.push_back(pgx);
         t.gy.push_back(pgy);
         const int l = int(t.gx.size()) - 1;
-        for (int node = 0; node < pgx * pgy; ++node) par[node] = parent_cone(t, l, node % pgx, node / pgx);
+        std::vector<float3_> parSums(size_t(pgx) * pgy);
+        for (int node = 0; node < pgx * pgy; ++node)
+            par[node] = parent_cone(t, l, node % pgx, node / pgx, parSums[node]);
         gx = pgx;
         gy = pgy;
         t.level.push_back(std::move(par));
+        t.sums.push_back(std::move(parSums));
     }
     return t;
 }
@@ -613,7 +662,8 @@ uint32_t tiles(const Tree& t, const uint8_t* mask, const Cap& c, Visit&& visit) 
             int x = tile % gx, y = tile / gx;
             bool ok = true;
             for (size_t l = 0; l < t.level.size() && ok; ++l) {
-                ok = pass(t.level[l][size_t(y) * t.gx[l] + x], c);
+                const size_t k = size_t(y) * t.gx[l] + x;
+                ok = pass(t.level[l][k], c) || (l == 0 && pass(t.second[k], c));
                 x /= kFan;
                 y /= kFan;
             }

@@ -42,8 +42,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
-    p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale", "mesh_query"],
+    p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale", "mesh_query", "inference"],
                    default="single_view")
+    p.add_argument("--frames", type=int, default=240, help="frames of the inference orbit")
+    p.add_argument("--shape", choices=["exact", "fused"], default="exact",
+                   help="per-frame full-shape mode of the inference renderer")
     p.add_argument("--views", type=int, default=None, help="override the mesh query's view count")
     p.add_argument("--edges", type=int, default=50_000_000, help="bisection edges of the mesh query (0: skip)")
     p.add_argument("--views-per-gpu", type=int, default=8, help="views per rank and step (multi_view)")
@@ -615,9 +618,9 @@ def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
     o, d = ray_o[0], ray_d[0]
     t0 = time.perf_counter()
     pose_o = oracle.prepare_pose(pose)
-    proj, rgb, counts = oracle.project(ocam, pose_o, parts, w.scene.features, w.scene.sh_degree, tmask)
+    proj, rgb, counts = oracle.project(ocam, pose_o, parts, w.scene.features, w.scene.sh_degree, tmask, d)
     tr = oracle.tile_rays(ocam, pose_o, o, d)
-    keys, ids, ranges = oracle.bin(ocam, pose_o, parts, proj, counts, tmask, tr, 0)
+    keys, ids, ranges = oracle.bin(ocam, pose_o, parts, proj, counts, tmask, tr, 0, d)
     t_pb = time.perf_counter() - t0
     # band of tile rows around the centre, grown until the budget is used
     rows = 1
@@ -650,6 +653,233 @@ def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
                        "frame")}
 
 
+# ----------------------------------------------------------------------------- inference orbit
+INF_METRIC = "fisheye inference frames/s"
+INF_UNIT = "frames/s"
+INF_GAMMA = 0.3          # pixel footprint variance (render.gofish.pixel_footprint_variance)
+INF_FILTER_VARIANCE = 0.2  # physical-mip 3-D filter: sqrt(0.2) / best sampling rate
+
+
+def inference_workload(args):
+    from gofish_b200 import scene as sc
+
+    return sc.workload_inference(n=args.num_gaussians or 6_000_000, frames=args.frames, size=args.size or 2560)
+
+
+def inference_config(w, args, world: int) -> dict:
+    cam = w.camera
+    return {
+        "workload": w.name, "gaussians": w.scene.num, "large_gaussians": int(len(w.big_rows)),
+        "large_gaussian_sigma_m": [0.05, 0.2], "sh_degree": w.scene.sh_degree,
+        "camera": f"OPENCV_FISHEYE equisolid (KB 4-term Taylor) 205deg {cam.width}x{cam.height}",
+        "k_buffer": w.k_buffer, "frames": len(w.poses), "frames_per_step": world, "orbit": "2 m ring, outward",
+        "shape": args.shape, "pixel_footprint_variance": INF_GAMMA,
+        "physical_mip_filter": f"on (filter_3D from all {len(w.poses)} frames, once per scene)",
+        "admission": "fast UT + cone fallback", "sort_key": "per-tile max-response depth",
+        "l2_policy": "inputs larger than L2 (packed particles 768 MB + SH 1152 MB)",
+        "parallelism": f"replicas: frames sharded over {world} GPUs" if world > 1 else "single GPU",
+    }
+
+
+def run_inference(args):
+    """Frames/s of the forward-only inference renderer over the orbit: each
+    step renders one frame per rank (the per-frame full shape, then the
+    trace); frames are sharded round-robin over the ranks (weak scaling, no
+    collective on the data path)."""
+    import torch
+    import torch.distributed as dist
+
+    from gofish_b200 import scene as sc
+    from gofish_b200.batch import Batch
+    from gofish_b200.inference import FrozenGaussians, InferenceTracer
+    from gofish_b200.physical_mip import compute_filter, pack_camera_table
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    w = inference_workload(args)
+    cam = w.camera
+    ray_o_np, ray_d_np, valid_np = cam.rays()
+    rays = (torch.from_numpy(ray_o_np).to(device), torch.from_numpy(ray_d_np).to(device))
+    mask = torch.from_numpy(valid_np).to(device)
+    cams, frames = sc.mip_camera_records(cam, w.poses, valid_np[0, :, :, 0])
+    table = pack_camera_table(cams, frames, device)
+    positions = torch.from_numpy(w.scene.positions).to(device)
+    torch.cuda.synchronize(device)
+    f0 = time.perf_counter()
+    filter_3d, _ = compute_filter(positions, table, INF_FILTER_VARIANCE)
+    torch.cuda.synchronize(device)
+    filter_ms = (time.perf_counter() - f0) * 1000.0
+    model = FrozenGaussians.from_scene(w.scene, device, filter_3d)
+    conf = {"render": {"splat": {"k_buffer_size": w.k_buffer}, "gofish": {"pixel_footprint_variance": INF_GAMMA}}}
+    tracer = InferenceTracer(conf, model, shape=args.shape)
+    intr = cam.intrinsics()
+    batches = [Batch(rays[0], rays[1], torch.from_numpy(sc.pose_to_c2w(p)[None]).float(),
+                     intrinsics_OpenCVFisheyeCameraModelParameters=intr, physical_fov_mask=mask,
+                     physical_fov_key="equisolid-205") for p in w.poses]
+
+    def frame_of(step: int) -> int:
+        return (step * world + rank) % len(batches)
+
+    raster = tracer.wrapper
+    for s_ in range(args.warmup):
+        tracer.render(batches[frame_of(s_)])
+    torch.cuda.synchronize(device)
+    raster.collect_stage_times()
+    raster.enable_stage_timing(True)
+    launches_before = int(raster.stats().total_kernel_launches)
+    inter = []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    stream = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s_ in range(args.steps):
+        tracer.render(batches[frame_of(args.warmup + s_)])
+        inter.append(int(raster.stats().num_intersections))
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    clock_info = clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    raster.enable_stage_timing(False)
+    stages = raster.collect_stage_times()
+    # the tracer's launches plus the per-frame shape kernels (view Q + full shape, or the fused one)
+    launches = int(raster.stats().total_kernel_launches) - launches_before
+    launches += args.steps * (2 if args.shape == "exact" else 1)
+    ms_max = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(ms_max.item())
+    value = world * args.steps / (elapsed_ms / 1000.0)
+
+    e2e = None
+    if not args.no_e2e:
+        h, wd = cam.height, cam.width
+        rgb_host = torch.empty((1, h, wd, 3), dtype=torch.float32).pin_memory()
+        alpha_host = torch.empty((1, h, wd, 1), dtype=torch.float32).pin_memory()
+        dist_host = torch.empty((1, h, wd, 1), dtype=torch.float32).pin_memory()
+
+        def e2e_frame(step):
+            out = tracer.render(batches[frame_of(step)])
+            rgb_host.copy_(out["pred_features"], non_blocking=True)
+            alpha_host.copy_(out["pred_opacity"], non_blocking=True)
+            dist_host.copy_(out["pred_dist"], non_blocking=True)
+
+        for s_ in range(max(1, args.warmup // 2)):
+            e2e_frame(s_)
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s_ in range(args.steps):
+            e2e_frame(args.warmup + s_)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(world * args.steps / (float(ems.item()) / 1000.0), 4), "unit": INF_UNIT,
+               "h2d_bytes_per_step": 64, "d2h_bytes_per_step": int(h * wd * 5 * 4)}
+
+    peak, peak_kind = measured_peaks()
+    fwd_ms, fwd_launches = stages["render_fwd"]
+    avg_s = fwd_ms / max(1, fwd_launches) / 1000.0
+    intersections = int(round(float(np.mean(inter)))) if inter else 0
+    pixels = cam.width * cam.height
+    alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
+    achieved = alg / avg_s / 1e9 if avg_s > 0 else 0.0
+    result = {
+        "metric": INF_METRIC, "value": round(value, 4), "unit": INF_UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
+        "config": inference_config(w, args, world), "e2e": e2e,
+        "roofline": {"kernel": f"k_render_fwd<{w.k_buffer}>", "bound": "hbm", "achieved": round(achieved, 2),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "alg_bytes_per_launch": int(alg),
+                     "avg_launch_ms": round(avg_s * 1000.0, 4)},
+        "gpu_launches": int(launches),
+        "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
+        "intersections_per_frame": intersections, "filter_3d_ms_once": round(filter_ms, 2),
+    }
+    if clock_info is not None:
+        result["clocks"] = clock_info
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = inference_cpu_baseline(w, tracer, batches[0], ray_o_np, ray_d_np, valid_np)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def inference_cpu_baseline(w, tracer, batch, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:
+    """The oracle on a bounded sample of one inference frame: the float64
+    full shape of a 1% row sample (scaled to every row), projection with the
+    cone fallback, binning and sort of every Gaussian on the frame's packed
+    rows, and the k-buffer forward of a band of tile rows scaled by the
+    retained-tile ratio."""
+    import oracle
+    from oracle import full_shape as ofs
+    from gofish_b200.batch import create_camera_parameters
+
+    cam = w.camera
+    ocam = oracle.camera(1, cam.width, cam.height, cam.principal, cam.focal, cam.coefficients, cam.max_angle)
+    tracer.render(batch)
+    parts = tracer.packed.cpu().numpy()
+    _sensor, poses = create_camera_parameters(batch)
+    pose7 = poses.T_world_sensors[0]
+    # full shape of a row sample (the GPU computes it for every row each frame)
+    rng = np.random.default_rng(5)
+    sample = rng.choice(w.scene.num, size=max(1, w.scene.num // 100), replace=False)
+    c2w = np.asarray(batch.T_to_world[0], dtype=np.float64)
+    t0 = time.perf_counter()
+    J, chart = ofs.view_jacobian(w.scene.positions[sample].astype(np.float64), c2w, True, cam.focal,
+                                 cam.coefficients, cam.max_angle)
+    Q, ob = ofs.minimum_norm_q(J, chart, INF_GAMMA)
+    ofs.full_shape(parts[sample, 8:11], parts[sample, 4:8], parts[sample, 11], Q, J, ob, INF_GAMMA, True, "exact")
+    t_shape = (time.perf_counter() - t0) * w.scene.num / sample.size
+    valid2 = valid[0, :, :, 0]
+    h, wd = valid2.shape
+    ty, tx = (h + 15) // 16, (wd + 15) // 16
+    pad = np.zeros((ty * 16, tx * 16), dtype=bool)
+    pad[:h, :wd] = valid2
+    tmask = pad.reshape(ty, 16, tx, 16).any(axis=(1, 3)).astype(np.uint8)
+    o, d = ray_o[0], ray_d[0]
+    t0 = time.perf_counter()
+    pose_o = oracle.prepare_pose(pose7)
+    proj, rgb, counts = oracle.project(ocam, pose_o, parts, w.scene.features, w.scene.sh_degree, tmask, d)
+    tr = oracle.tile_rays(ocam, pose_o, o, d)
+    keys, ids, ranges = oracle.bin(ocam, pose_o, parts, proj, counts, tmask, tr, 0, d)
+    t_pb = time.perf_counter() - t0
+    rows, centre, t_render, rendered = 1, ty // 2, 0.0, 0
+    while True:
+        r0 = max(0, centre - rows // 2)
+        r1 = min(ty, r0 + rows)
+        tiles = (r0 * tx, r1 * tx)
+        t1 = time.perf_counter()
+        oracle.render_forward(ocam, pose_o, parts, rgb, o, d, tmask, ranges, ids, w.k_buffer, tiles)
+        t_render = time.perf_counter() - t1
+        rendered = int(tmask.reshape(-1)[tiles[0]:tiles[1]].sum())
+        if t_shape + t_pb + t_render > budget_s / 2 or r1 - r0 >= ty:
+            break
+        rows *= 2
+    retained = int(tmask.sum())
+    full = t_shape + t_pb + t_render * retained / max(1, rendered)
+    return {"value": round(1.0 / full, 6), "unit": INF_UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": (f"full shape of {sample.size} of {w.scene.num} rows ({t_shape:.2f} s scaled), projection+sort "
+                       f"of all Gaussians ({t_pb:.2f} s), forward of {rendered} of {retained} retained tiles "
+                       f"({t_render:.2f} s), scaled to one {cam.width}x{cam.height} frame")}
+
+
 def run_reference_mesh(args):
     w, shape, points, cameras = mesh_workload(args)
     values, base = [], None
@@ -668,12 +898,50 @@ def run_reference_mesh(args):
     }), flush=True)
 
 
+def run_reference_inference(args):
+    """The oracle's frame rate on the inference orbit (rank 0); the GPU only
+    builds the frame's packed rows that the oracle then renders."""
+    import torch
+
+    from gofish_b200 import scene as sc
+    from gofish_b200.batch import Batch
+    from gofish_b200.inference import FrozenGaussians, InferenceTracer
+
+    w = inference_workload(args)
+    cam = w.camera
+    ray_o, ray_d, valid = cam.rays()
+    device = torch.device("cuda", 0)
+    conf = {"render": {"splat": {"k_buffer_size": w.k_buffer}, "gofish": {"pixel_footprint_variance": INF_GAMMA}}}
+    tracer = InferenceTracer(conf, FrozenGaussians.from_scene(w.scene, device), shape="exact")
+    batch = Batch(torch.from_numpy(ray_o).to(device), torch.from_numpy(ray_d).to(device),
+                  torch.from_numpy(sc.pose_to_c2w(w.poses[0])[None]).float(),
+                  intrinsics_OpenCVFisheyeCameraModelParameters=cam.intrinsics(),
+                  physical_fov_mask=torch.from_numpy(valid).to(device), physical_fov_key="equisolid-205")
+    values, base = [], None
+    for i in range(args.warmup + args.steps):
+        base = inference_cpu_baseline(w, tracer, batch, ray_o, ray_d, valid, budget_s=6.0)
+        if i >= args.warmup:
+            values.append(base["value"])
+    value = float(np.median(values))
+    print(json.dumps({
+        "metric": INF_METRIC, "value": round(value, 6), "unit": INF_UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded scene, see config)", "impl": "reference", "config": inference_config(w, args, 1),
+        "cpu_baseline": {**base, "value": round(value, 6)},
+        "e2e": {"value": round(value, 6), "unit": INF_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     if args.workload == "mesh_query":
         run_reference_mesh(args)
+        return
+    if args.workload == "inference":
+        run_reference_inference(args)
         return
     w, poses = build_workload(args, 0)
     pose = poses[0]
@@ -703,6 +971,8 @@ def main():
         run_reference(args)
     elif args.workload == "mesh_query":
         run_mesh(args)
+    elif args.workload == "inference":
+        run_inference(args)
     else:
         run_gpu(args)
 

@@ -172,6 +172,12 @@ class FisheyeCamera:
             np.array(self.principal, dtype=np.float32), np.array(self.focal, dtype=np.float32),
             np.array(self.coefficients, dtype=np.float32), self.max_angle)
 
+    def intrinsics(self) -> dict:
+        """The batch's ``intrinsics_OpenCVFisheyeCameraModelParameters`` record."""
+        return {"resolution": [self.width, self.height], "shutter_type": "GLOBAL",
+                "principal_point": list(self.principal), "focal_length": list(self.focal),
+                "radial_coeffs": list(self.coefficients), "max_angle": float(self.max_angle)}
+
     def rays(self):
         """Sensor-frame rays at pixel centres: origins [1,H,W,3] (zero),
         directions [1,H,W,3] and the physical mask [1,H,W,1] (bool)."""

@@ -177,6 +177,7 @@ class Workload:
     poses: list          # list of 7-float world->sensor poses
     k_buffer: int
     description: str
+    big_rows: np.ndarray | None = None  # rows of the large Gaussians beside the camera path
 
 
 def workload_cpu_scale(seed: int = 1234) -> Workload:
@@ -229,3 +230,80 @@ def workload_mesh_query(seed: int = 1237, n: int = 3_000_000, views: int = 32, s
     return Workload("mesh_opacity_query", scene, cam, poses, 0,
                     f"{n} Gaussians, sites (centre + 8 corners), {views} equidistant 200deg {size}x{size} views "
                     "on a 2 m ring")
+
+
+def orbit_poses(frames: int, radius: float = 2.0) -> list:
+    """World->sensor poses of ``frames`` cameras evenly spaced on a horizontal
+    ring of ``radius`` metres around the origin, each looking outward."""
+    poses = []
+    for v in range(frames):
+        yaw = 2.0 * math.pi * v / frames
+        poses.append(look_outward_pose(np.array([radius * math.cos(yaw), radius * math.sin(yaw), 0.0]), yaw))
+    return poses
+
+
+def workload_inference(seed: int = 1238, n: int = 6_000_000, frames: int = 240, size: int = 2560,
+                       big_fraction: float = 0.05, big_sigma=(0.05, 0.2), orbit_radius: float = 2.0) -> Workload:
+    """High-resolution inference orbit: ``n`` Gaussians SH3 with the common
+    distributions, of which ``big_fraction`` are large Gaussians beside the
+    camera path (centres within 1 m of the orbit ring, in the plane
+    perpendicular to the local outward optical axis, so that they straddle the
+    theta = 90 deg horizon of the nearby frames; per-axis scale s * exp(N(0,
+    0.2^2)), s ~ U(big_sigma)); equisolid (KB 4-term Taylor) 205 deg fisheye at
+    size x size; ``frames`` outward-looking views on a ring of ``orbit_radius``
+    metres; k = 32."""
+    scene = random_scene(n, 3, seed)
+    rng = np.random.default_rng(seed + 1000)
+    nb = int(round(big_fraction * n))
+    rows = np.zeros(0, dtype=np.int64)
+    if nb > 0:
+        rows = np.sort(rng.choice(n, size=nb, replace=False))
+        phi = rng.uniform(0.0, 2.0 * math.pi, nb)
+        rho = rng.uniform(0.2, 1.0, nb)
+        psi = rng.uniform(0.0, 2.0 * math.pi, nb)
+        ring = np.stack([orbit_radius * np.cos(phi), orbit_radius * np.sin(phi), np.zeros(nb)], axis=1)
+        tangent = np.stack([-np.sin(phi), np.cos(phi), np.zeros(nb)], axis=1)
+        outward = np.stack([np.cos(phi), np.sin(phi), np.zeros(nb)], axis=1)
+        up = np.array([0.0, 0.0, 1.0])
+        centre = (ring + rho[:, None] * (np.cos(psi)[:, None] * tangent + np.sin(psi)[:, None] * up)
+                  + rng.uniform(-0.1, 0.1, nb)[:, None] * outward)
+        s = rng.uniform(big_sigma[0], big_sigma[1], nb)
+        scene.positions[rows] = centre.astype(np.float32)
+        scene.scales[rows] = (s[:, None] * np.exp(rng.normal(0.0, 0.2, (nb, 3)))).astype(np.float32)
+    cam = fisheye_camera(size, size, 205.0, EQUISOLID_KB4)
+    return Workload("inference_orbit", scene, cam, orbit_poses(frames, orbit_radius), 32,
+                    f"{n} Gaussians SH3 ({nb} large beside the camera path), equisolid 205deg {size}x{size}, "
+                    f"{frames}-frame {orbit_radius:g} m orbit, K=32, physical-mip filter on", rows)
+
+
+def pose_to_c2w(pose7) -> np.ndarray:
+    """4x4 camera-to-world matrix of a world->sensor pose [t, q(x, y, z, w)]."""
+    t = np.asarray(pose7[:3], dtype=np.float64)
+    x, y, z, w = (float(v) for v in pose7[3:7])
+    R = quaternion_to_matrix(np.array([[w, x, y, z]]))[0]
+    c2w = np.eye(4)
+    c2w[:3, :3] = R.T
+    c2w[:3, 3] = -R.T @ t
+    return c2w
+
+
+def camera_valid_runs(valid: np.ndarray) -> list:
+    """[lo, hi) column run of valid pixels per row of a convex [H,W] mask
+    ([0, 0] for a row without one)."""
+    runs = []
+    for row in np.asarray(valid, dtype=bool):
+        cols = np.flatnonzero(row)
+        runs.append([int(cols[0]), int(cols[-1]) + 1] if cols.size else [0, 0])
+    return runs
+
+
+def mip_camera_records(camera: FisheyeCamera, poses: list, valid: np.ndarray, camera_id: int = 0):
+    """Physical-mip camera and frame records (pack_camera_table format) of one
+    fisheye camera seen from ``poses``; tie ranks follow the frame order."""
+    cam = {"camera_id": camera_id, "model": "OPENCV_FISHEYE", "width": camera.width, "height": camera.height,
+           "params": [*camera.focal, *camera.principal, *camera.coefficients], "max_angle": float(camera.max_angle),
+           "rows": camera_valid_runs(valid)}
+    frames = [{"frame_index": k, "camera_id": camera_id, "c2w": pose_to_c2w(p).reshape(-1).tolist(),
+               "tie_break": f"{k:06d}"} for k, p in enumerate(poses)]
+    return [cam], frames
+

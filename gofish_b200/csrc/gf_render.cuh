@@ -181,7 +181,7 @@ struct RingKBuffer {
         if (i + 1 < n && above == t) ++ties;
         ++n;
     }
-    __device__ __noinline__ void insert_general(float t, float a, uint32_t idx) {
+    __device__ __forceinline__ void insert_general(float t, float a, uint32_t idx) {
         int p = 0;
         while (p < n && getTA(slot(p)).x < t) ++p;
         // Entries below the new hit: every run of equal distances moves its top entry to its bottom.
@@ -610,7 +610,7 @@ __device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords
 // back-propagated from the final pixel values.  Loops are warp-uniform so
 // the gradient reduction can use full-warp shuffles.
 template <int K>
-__global__ __launch_bounds__(kTileThreads) void k_render_bwd(RenderBwdArgs a) {
+__global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a) {
     constexpr int KR = K > 0 ? K : 1;
     extern __shared__ __align__(16) unsigned char smem[];
     Staged* sRec = reinterpret_cast<Staged*>(smem);

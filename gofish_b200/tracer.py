@@ -1,0 +1,274 @@
+"""Training renderer: ``Tracer(conf).render(gaussians, gpu_batch, train, frame_id)``
+(reference threedgut_tracer/tracer.py:142-525).
+
+One render of one view:
+
+1. the physical tile mask of the camera is registered once per (domain,
+   device, raster) under its token (tracer.py:380-404);
+2. the per-view full shape is built from the model's intrinsic shape:
+   Q_v of the active camera, C = R S^2 R^T + Q_v, its factor B = C^(1/2) R,
+   B^-1 and the mass-preserving density m * o (``build_intrinsic_view_shape``,
+   tracer.py:406-433), all differentiable;
+3. ``Tracer._Autograd`` packs the reference's [N,32] particle rows and calls
+   the native ``SplatRaster.trace``; its backward calls ``trace_bwd`` and
+   splits the [N,32] row gradient into the per-slot gradients in the
+   reference's order (tracer.py:142-353), so autograd carries them back
+   through the full-shape VJP to the scale, rotation and opacity.
+
+The geometric training channels (normals, distortion moments, quantile and
+exact-crossing depths, extent, opacity field, inverse-depth moments) are
+returned as zeros and carry no gradient, as the reference's buffers are with
+its normal channel compiled out; a configuration whose losses read them
+(``loss.lambda_distortion``, ``lambda_dnc``, ``lambda_esmooth``, ``lambda_opa``,
+``lambda_extent``, ``lambda_normal_variance`` > 0) is refused when the tracer
+is built, and so is the CoMe colour confidence (``loss.color_confidence``).
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+
+from .batch import create_camera_parameters
+from .physical_mip import scale_with_3d_filter
+from .physical_tile_mask import build_physical_tile_binding
+from .splat_raster import SplatRaster, _select
+from .view_observation_filter import build_intrinsic_view_shape, pixel_footprint_variance
+
+# Row layout of the packed particle ABI (gaussianParticles.cuh:33-46) and the
+# gradient split of tracer.py:334-343.
+PACKED_SPLIT = (3, 1, 4, 3, 1, 9, 9, 2)
+
+GEOMETRIC_LOSSES = ("lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_opa", "lambda_extent",
+                    "lambda_normal_variance")
+
+
+def _conf_value(conf, path: str, default):
+    if isinstance(conf, dict) or conf is None:
+        return _select(conf, path, default)
+    node: Any = conf
+    for part in path.split("."):
+        node = getattr(node, part, None) if not isinstance(node, dict) else node.get(part)
+        if node is None:
+            return default
+    return node
+
+
+class Tracer:
+    """Differentiable fisheye renderer of a Gaussian scene (reference ``Tracer``)."""
+
+    class _Autograd(torch.autograd.Function):
+        """Argument order of tracer.py:144-164; gradients in the same order."""
+
+        @staticmethod
+        def forward(ctx, tracer_wrapper, physical_tile_token, frame_id, sof_exact_opacity_active, n_active_features,
+                    ray_ori, ray_dir, mog_pos, mog_rot, mog_scl, mog_dns, mog_intrinsic_dns, mog_factor,
+                    mog_inverse_factor, mog_sph, sensor_params, sensor_poses, mog_confidence):
+            n = mog_pos.shape[0]
+            if mog_confidence.numel() != 0:
+                raise NotImplementedError("CoMe colour confidence is not rendered by this tracer")
+            if mog_factor.shape != (n, 3, 3) or mog_inverse_factor.shape != mog_factor.shape:
+                raise ValueError("full-shape factor tensors must have shape [N,3,3]")
+            particle_density = torch.cat(
+                [mog_pos, mog_dns.reshape(n, 1), mog_rot, mog_scl, mog_intrinsic_dns.reshape(n, 1),
+                 mog_factor.reshape(n, 9), mog_inverse_factor.reshape(n, 9), mog_pos.new_zeros((n, 2))],
+                dim=1).float().contiguous()
+            particle_features = mog_sph.float().contiguous()
+            t0, t1 = sensor_poses.timestamps_us[0], sensor_poses.timestamps_us[1]
+            p0, p1 = sensor_poses.T_world_sensors[0], sensor_poses.T_world_sensors[1]
+            outs = tracer_wrapper.trace(frame_id, sof_exact_opacity_active, n_active_features, particle_density,
+                                        particle_features, ray_ori, ray_dir, None, sensor_params, t0, t1, p0, p1,
+                                        physical_tile_token)
+            rgba, hit_distance = outs[0], outs[1]
+            ctx.save_for_backward(ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features)
+            ctx.frame_id = frame_id
+            ctx.sof_exact_opacity_active = bool(sof_exact_opacity_active)
+            ctx.n_active_features = n_active_features
+            ctx.sensor_params = sensor_params
+            ctx.sensor_poses = sensor_poses
+            ctx.tracer_wrapper = tracer_wrapper
+            ctx.physical_tile_token = physical_tile_token
+            ctx.set_materialize_grads(False)
+            ctx.mark_non_differentiable(*outs[2:])
+            return outs
+
+        @staticmethod
+        def backward(ctx, ray_features_density_grd, ray_hit_distance_grd, *_unused):
+            ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features = ctx.saved_tensors
+            if ray_features_density_grd is None and ray_hit_distance_grd is None:
+                return (None,) * 18
+            if ray_features_density_grd is None:
+                ray_features_density_grd = torch.zeros_like(rgba)
+            poses = ctx.sensor_poses
+            grad_density, grad_features = ctx.tracer_wrapper.trace_bwd(
+                ctx.frame_id, ctx.sof_exact_opacity_active, ctx.n_active_features, particle_density,
+                particle_features, ray_ori, ray_dir, None, ctx.sensor_params, poses.timestamps_us[0],
+                poses.timestamps_us[1], poses.T_world_sensors[0], poses.T_world_sensors[1], rgba,
+                ray_features_density_grd, hit_distance, ray_hit_distance_grd, ctx.physical_tile_token)
+            g_pos, g_dns, g_rot, g_scl, g_intrinsic, g_factor, g_inverse, _g_pad = torch.split(
+                grad_density, list(PACKED_SPLIT), dim=1)
+            return (None, None, None, None, None, None, None,
+                    g_pos.contiguous(), g_rot.contiguous(), g_scl.contiguous(), g_dns.contiguous(),
+                    g_intrinsic.contiguous(), g_factor.reshape(-1, 3, 3), g_inverse.reshape(-1, 3, 3),
+                    grad_features.contiguous(), None, None, None)
+
+    def __init__(self, conf):
+        self.device = "cuda"
+        self.conf = conf
+        if _conf_value(conf, "render.primitive_type", "instances") == "trisurfel":
+            raise RuntimeError("GOFish renders volumetric Gaussians only")
+        used = [name for name in GEOMETRIC_LOSSES if float(_conf_value(conf, f"loss.{name}", 0.0) or 0.0) > 0.0]
+        if used:
+            raise NotImplementedError("losses on the geometric training channels are not supported by this tracer: "
+                                      + ", ".join(used))
+        if bool(_conf_value(conf, "loss.color_confidence", False)):
+            raise NotImplementedError("CoMe colour confidence (loss.color_confidence) is not rendered by this tracer")
+        self._view_observation_filter = True
+        self._pixel_footprint_variance = pixel_footprint_variance(conf)
+        self.tracer_wrapper = SplatRaster(_plain(conf))
+        self._physical_tile_binding_cache: dict = {}
+        self._physical_tile_registration_cache: set = set()
+
+    def _physical_tile_token(self, wrapper, gpu_batch, rays) -> str:
+        """The tile mask of the batch's calibrated domain, registered once per camera."""
+        mask = getattr(gpu_batch, "physical_fov_mask", None)
+        domain = getattr(gpu_batch, "physical_fov_key", None)
+        if domain is None:
+            domain = "full-raster" if mask is None else f"mask:{id(mask)}"
+        key = (str(domain), str(rays.device), int(rays.shape[1]), int(rays.shape[2]))
+        binding = self._physical_tile_binding_cache.get(key)
+        if binding is None:
+            binding = build_physical_tile_binding(gpu_batch, rays, str(domain))
+            self._physical_tile_binding_cache[key] = binding
+        registration = (id(wrapper), binding.token)
+        if registration not in self._physical_tile_registration_cache:
+            wrapper.register_physical_tile_mask(binding.mask, binding.token)
+            self._physical_tile_registration_cache.add(registration)
+        return binding.token
+
+    def _density_shape_inputs(self, gaussians, gpu_batch=None, detach=False, frame_id=None):
+        """(rotation, intrinsic scale, view density m*o, intrinsic density, B, B^-1) of this view."""
+        if gpu_batch is None:
+            raise RuntimeError("the per-view footprint requires the active camera batch")
+        rotation = gaussians.get_rotation()
+        raw_density = gaussians.get_density()
+        physical_scale = (gaussians.get_scale_with_3D_filter()
+                          if bool(getattr(gaussians, "_use_physical_mip3d_filter", False)) else gaussians.get_scale())
+        if detach:
+            rotation, raw_density, physical_scale = rotation.detach(), raw_density.detach(), physical_scale.detach()
+        shape = build_intrinsic_view_shape(physical_scale, rotation, raw_density, gaussians.positions.detach(),
+                                           gpu_batch, pixel_footprint_variance=self._pixel_footprint_variance,
+                                           frame_id=frame_id)
+        return rotation, physical_scale, shape.density, raw_density, shape.factor, shape.inverse_factor
+
+    @property
+    def timings(self):
+        return self.tracer_wrapper.collect_times()
+
+    def build_acc(self, gaussians, rebuild=True):
+        """No acceleration structure for a rasterised tracer (tracer.py:443-444)."""
+
+    def render(self, gaussians, gpu_batch, train=False, frame_id=0) -> dict[str, Any]:
+        rays_o = gpu_batch.rays_ori
+        rays_d = gpu_batch.rays_dir
+        token = self._physical_tile_token(self.tracer_wrapper, gpu_batch, rays_d)
+        sensor, poses = create_camera_parameters(gpu_batch)
+        rot, scale, dens, intrinsic_dens, factor, inverse_factor = self._density_shape_inputs(
+            gaussians, gpu_batch, detach=False, frame_id=frame_id)
+        confidence = gaussians.positions.new_empty((0, 1))
+        (features_alpha, pred_dist, hits_count, visibility, normal, depth_var, quant, extent, opacity_field, invd,
+         invd2) = Tracer._Autograd.apply(
+            self.tracer_wrapper, token, frame_id, False, gaussians.n_active_features, rays_o.contiguous(),
+            rays_d.contiguous(), gaussians.positions.contiguous(), rot.contiguous(), scale.contiguous(),
+            dens.contiguous(), intrinsic_dens.contiguous(), factor.contiguous(), inverse_factor.contiguous(),
+            gaussians.get_features().contiguous(), sensor, poses, confidence)
+        f = gaussians.ray_feature_dim
+        timings = self.tracer_wrapper.collect_times()
+        return {
+            "pred_features": features_alpha[..., :f].unsqueeze(0).contiguous(),
+            "pred_opacity": features_alpha[..., f:].unsqueeze(0).contiguous(),
+            "pred_dist": pred_dist.unsqueeze(0).contiguous(),
+            "pred_normals": normal.unsqueeze(0).contiguous(),
+            "pred_depth_var": depth_var.unsqueeze(0).contiguous(),
+            "pred_quant": quant.unsqueeze(0).contiguous(),
+            "pred_crossing": quant[..., 8:9].unsqueeze(0).contiguous(),
+            "pred_crossing_rate": quant[..., 9:10].unsqueeze(0).contiguous(),
+            "pred_extent": extent.unsqueeze(0).contiguous(),
+            "pred_opacity_field": opacity_field.unsqueeze(0).contiguous(),
+            "pred_invd": invd.unsqueeze(0).contiguous(),
+            "pred_invd2": invd2.unsqueeze(0).contiguous(),
+            "hits_count": hits_count.unsqueeze(0).contiguous(),
+            "frame_time_ms": timings.get("forward_render", 0.0),
+            "mog_visibility": visibility,
+        }
+
+
+class SceneGaussians:
+    """A Gaussian scene with the accessors the tracer reads (the reference
+    model's ``positions``, ``get_rotation``, ``get_scale``,
+    ``get_scale_with_3D_filter``, ``get_density``, ``get_features``), holding
+    activated values.  Tensors that require grad receive the render's
+    gradients."""
+
+    def __init__(self, positions, rotations, scales, density, features, sh_degree: int, filter_3d=None):
+        self.positions = positions
+        self.rotation = rotations
+        self.scale = scales
+        self.density = density
+        self.features = features
+        self.n_active_features = int(sh_degree)
+        self.ray_feature_dim = 3
+        self.filter_3d = filter_3d
+        self._use_physical_mip3d_filter = filter_3d is not None
+
+    @classmethod
+    def from_scene(cls, scene, device, requires_grad: bool = True, filter_3d=None) -> "SceneGaussians":
+        def t(a, shape=None):
+            v = torch.as_tensor(a, dtype=torch.float32).to(device)
+            v = (v.reshape(shape) if shape is not None else v).contiguous()
+            return v.requires_grad_(requires_grad)
+
+        n = scene.num
+        return cls(t(scene.positions), t(scene.rotations), t(scene.scales), t(scene.density, (n, 1)),
+                   t(scene.features), scene.sh_degree, filter_3d)
+
+    @property
+    def num_gaussians(self) -> int:
+        return int(self.positions.shape[0])
+
+    def parameters(self) -> list[torch.Tensor]:
+        return [self.positions, self.rotation, self.scale, self.density, self.features]
+
+    def get_rotation(self):
+        return self.rotation
+
+    def get_scale(self):
+        return self.scale
+
+    def get_scale_with_3D_filter(self):
+        return scale_with_3d_filter(self.scale, self.filter_3d)
+
+    def get_density(self):
+        return self.density
+
+    def get_features(self):
+        return self.features
+
+
+def _plain(conf):
+    """A nested dict view of ``conf`` for the native renderer's settings."""
+    if conf is None or isinstance(conf, dict):
+        return conf
+    to_container = getattr(type(conf), "to_container", None)
+    if to_container is not None:
+        return to_container(conf)
+    out = {}
+    for section in ("render", "loss"):
+        node = getattr(conf, section, None)
+        if node is not None:
+            out[section] = node if isinstance(node, dict) else dict(vars(node))
+    return out
+
+
+__all__ = ["PACKED_SPLIT", "SceneGaussians", "Tracer"]

@@ -3,9 +3,12 @@
 
 Workload (default ``single_view``): 1,000,000 Gaussians with SH degree 3, a
 Kannala-Brandt 200 deg fisheye at 1600x1600, k-buffer 16, L1 loss against a
-U[0,1] target.  One step = trace forward, L1 loss gradient, trace backward
-(and, with N > 1 ranks, the NCCL all-reduce of the per-Gaussian gradients);
-every rank renders its own view of the same scene (weak scaling).
+U[0,1] target.  One step = one training render through the public entry
+point ``Tracer.render`` per view (the per-view full shape with a 0.3 px^2
+pixel footprint, trace forward, L1 loss, trace backward and the full-shape
+VJP to the model's position, rotation, scale, opacity and SH) and, with N > 1
+ranks, the NCCL all-reduce of the [N,59] model gradients; every rank renders
+its own views of the same scene (weak scaling).
 
 ``--impl reference`` times the CPU restatement of the reference's equations
 (oracle/) on the host cores: the reference renders only on the GPU and its
@@ -100,8 +103,11 @@ def workload_config(w, args, world: int, views_per_rank: int = 1) -> dict:
         "sort_key": "per-tile max-response depth",
         "views_per_step": world * views_per_rank,
         "loss": "L1 vs U[0,1] target",
-        "l2_policy": "inputs larger than L2 (packed particles + SH + rays > 126 MB)",
-        "parallelism": f"dp{world} (views sharded, NCCL all-reduce of particle gradients)" if world > 1 else "single GPU",
+        "entry_point": "Tracer.render (per-view full shape, trace, trace_bwd, full-shape VJP)",
+        "pixel_footprint_variance": BENCH_GAMMA,
+        "l2_policy": "inputs larger than L2 (model 236 B/Gaussian + packed rows + rays > 126 MB)",
+        "parallelism": (f"dp{world} (views sharded, NCCL all-reduce of the [N,59] model gradients)" if world > 1
+                        else "single GPU"),
     }
 
 
@@ -178,6 +184,15 @@ FWD_RENDER_BYTES_PER_INTERSECTION = 4 + 88 + 12     # id, particle fetch (pos, B
 FWD_RENDER_BYTES_PER_PIXEL = 48                     # rays 24, rgba 16, hit distance 4, hit count 4
 BWD_RENDER_BYTES_PER_INTERSECTION = 144             # id 4 + particle record 128 + rgb 12
 BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output gradients
+# DRAM bytes per algorithmic byte of the render kernels in one full ncu capture
+# of this workload (k_render_fwd<16>: 167.6 MB for 469.5 MB; k_render_bwd<16>:
+# 262.5 MB for 644.0 MB); the bench line's traffic is the live algorithmic
+# bytes scaled by them.
+FWD_TRAFFIC_PER_ALG_BYTE = 167.6 / 469.5
+BWD_TRAFFIC_PER_ALG_BYTE = 262.5 / 644.0
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio to the algorithmic bytes"
+# pixel footprint variance of the per-view full shape (render.gofish.pixel_footprint_variance)
+BENCH_GAMMA = 0.3
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -185,8 +200,11 @@ def run_gpu(args):
     import torch
     import torch.distributed as dist
 
-    from gofish_b200.splat_raster import SplatRaster
-    from gofish_b200.scene import pack_particles
+    from gofish_b200.batch import Batch
+    from gofish_b200.footprint_chunk_planner import plan_footprint_chunks
+    from gofish_b200.multiview import allreduce_gradients
+    from gofish_b200.scene import pose_to_c2w
+    from gofish_b200.tracer import SceneGaussians, Tracer
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -196,66 +214,59 @@ def run_gpu(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
-    from gofish_b200.multiview import multiview_step
-
     w, poses = build_workload(args, rank, world)
     cam = w.camera
     ray_o_np, ray_d_np, valid_np = cam.rays()
-    particles_host = torch.from_numpy(pack_particles(w.scene)).pin_memory()
-    features_host = torch.from_numpy(np.ascontiguousarray(w.scene.features)).pin_memory()
+    scene = w.scene
+    n = scene.num
+    host = {"positions": scene.positions, "rotation": scene.rotations, "scale": scene.scales,
+            "density": np.asarray(scene.density, np.float32).reshape(n, 1), "features": scene.features}
+    host = {k: torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).pin_memory() for k, v in host.items()}
     rng = np.random.default_rng(777 + rank)
     target_host = torch.from_numpy(rng.random((len(poses), cam.height, cam.width, 3), dtype=np.float32)).pin_memory()
 
-    particles = particles_host.to(device)
-    features = features_host.to(device)
+    model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in
+                             ("positions", "rotation", "scale", "density", "features")), scene.sh_degree)
+    params = model.parameters()
     target = target_host.to(device)
     ray_o = torch.from_numpy(ray_o_np).to(device)
     ray_d = torch.from_numpy(ray_d_np).to(device)
-    valid = torch.from_numpy(valid_np[0]).to(device)  # [H,W,1] bool
-    valid_f = valid.float()
+    mask = torch.from_numpy(valid_np).to(device)            # [1,H,W,1] bool
+    valid_f = mask[0].float()
     n_valid = max(1.0, float(valid_np.sum()))
-    from gofish_b200.physical_tile_mask import build_physical_tile_binding
-
-    class _Batch:
-        physical_fov_mask = valid[None]
-
-    binding = build_physical_tile_binding(_Batch, ray_d, "bench")
-    conf = {"render": {"splat": {"k_buffer_size": w.k_buffer}, "enable_hitcounts": True}}
-    raster = SplatRaster(conf)
-    raster.register_physical_tile_mask(binding.mask, binding.token)
-    sensor = cam.model()
-    pose_ts = [torch.from_numpy(np.asarray(p, dtype=np.float32)) for p in poses]
-    zeros14 = [torch.zeros(1, device=device)] * 14
+    batches = [Batch(ray_o, ray_d, torch.from_numpy(pose_to_c2w(p)[None]).float(),
+                     intrinsics_OpenCVFisheyeCameraModelParameters=cam.intrinsics(), physical_fov_mask=mask,
+                     physical_fov_key="bench") for p in poses]
+    conf = {"render": {"splat": {"k_buffer_size": w.k_buffer}, "enable_hitcounts": True,
+                       "gofish": {"pixel_footprint_variance": BENCH_GAMMA}}}
+    tracer = Tracer(conf)
+    raster = tracer.tracer_wrapper
     scale = 1.0 / (3.0 * n_valid)
-    zero_hit = torch.zeros((cam.height, cam.width, 1), device=device)
-    accum = [torch.empty_like(particles), torch.empty_like(features)]
     view_intersections: list[int] = []
+    view_fallback: list[int] = []
     loss_acc = torch.zeros((), device=device)
 
-    def step(p, f, tgt, want_loss=False):
-        """Forward, L1 loss gradient and backward of every local view, the
-        per-Gaussian gradients summed over the views and all-reduced over ranks."""
+    def step(tgt, want_loss=False):
+        """Forward, L1 loss and backward of every local view through
+        Tracer.render (per-view full shape, trace, trace_bwd, shape VJP); the
+        model gradients [N,59] summed over the views and all-reduced over ranks."""
+        for p in params:
+            p.grad = None
         loss_acc.zero_()
-
-        def render_view(v):
-            pose_t = pose_ts[v]
-            out = raster.trace(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t, pose_t,
-                               binding.token)
-            view_intersections.append(int(raster.stats().num_intersections))
-            rgba = out[0]
-            diff = rgba[..., :3] - tgt[v]
-            grad = torch.zeros_like(rgba)
-            grad[..., :3] = torch.sign(diff) * (valid_f * scale)
+        for v, batch in enumerate(batches):
+            out = tracer.render(model, batch, train=True, frame_id=v)
+            st = raster.stats()
+            view_intersections.append(int(st.num_intersections))
+            view_fallback.append(int(st.fallback_particles))
+            loss = ((out["pred_features"][0] - tgt[v]).abs() * valid_f).sum() * scale
+            loss.backward()
             if want_loss:
-                loss_acc.add_((diff.abs() * valid_f).sum() * scale)
-            return raster.trace_bwd(0, False, w.scene.sh_degree, p, f, ray_o, ray_d, None, sensor, 0, 1, pose_t,
-                                    pose_t, rgba, grad, out[1], zero_hit, *zeros14, binding.token)
-
-        multiview_step(render_view, range(len(pose_ts)), accum)
+                loss_acc.add_(loss.detach())
+        allreduce_gradients([p.grad for p in params])
         return loss_acc if want_loss else None
 
     for _ in range(args.warmup):
-        step(particles, features, target)
+        step(target)
     torch.cuda.synchronize(device)
     intersections = int(raster.stats().num_intersections)
 
@@ -274,7 +285,7 @@ def run_gpu(args):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        step(particles, features, target)
+        step(target)
     t1.record(stream)
     torch.cuda.synchronize(device)
     clock_info = clocks.stop()
@@ -285,6 +296,12 @@ def run_gpu(args):
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
     launches = int(raster.stats().total_kernel_launches) - launches_before
+    # the full-shape kernels: Q_v, the shape forward and its VJP per view (one chunk each at these sizes)
+    free, total = torch.cuda.mem_get_info(device)
+    chunks = plan_footprint_chunks(n, driver_free_bytes=int(free), device_total_bytes=int(total),
+                                   allocator_reserved_bytes=int(torch.cuda.memory_reserved(device)),
+                                   allocator_allocated_bytes=int(torch.cuda.memory_allocated(device))).chunk_count
+    launches += args.steps * len(batches) * (1 + 2 * max(1, chunks))
     ms_max = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
@@ -296,17 +313,16 @@ def run_gpu(args):
     # --- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        h2d = particles_host.numel() * 4 + features_host.numel() * 4 + target_host.numel() * 4
-        p_dev = torch.empty_like(particles)
-        f_dev = torch.empty_like(features)
+        h2d = sum(t.numel() * 4 for t in host.values()) + target_host.numel() * 4
         t_dev = torch.empty_like(target)
         loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
         def e2e_step():
-            p_dev.copy_(particles_host, non_blocking=True)
-            f_dev.copy_(features_host, non_blocking=True)
+            with torch.no_grad():
+                for p, k in zip(params, ("positions", "rotation", "scale", "density", "features")):
+                    p.copy_(host[k], non_blocking=True)
             t_dev.copy_(target_host, non_blocking=True)
-            loss = step(p_dev, f_dev, t_dev, want_loss=True)
+            loss = step(t_dev, want_loss=True)
             loss_host.copy_(loss, non_blocking=True)
 
         for _ in range(max(1, args.warmup // 2)):
@@ -335,12 +351,15 @@ def run_gpu(args):
     intersections = int(round(float(np.mean(timed_intersections)))) if timed_intersections else intersections
     if dominant == "render_bwd":
         alg = intersections * BWD_RENDER_BYTES_PER_INTERSECTION + pixels * BWD_RENDER_BYTES_PER_PIXEL
+        traffic = alg * BWD_TRAFFIC_PER_ALG_BYTE
     else:
         alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
+        traffic = alg * FWD_TRAFFIC_PER_ALG_BYTE
     achieved = alg / avg_s / 1e9
     roofline = {"kernel": f"k_render_{dominant.split('_')[1]}<{w.k_buffer}>", "bound": "hbm",
                 "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5),
-                "traffic": None, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": int(traffic), "traffic_source": TRAFFIC_SOURCE,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                 "alg_bytes_per_launch": int(alg), "avg_launch_ms": round(avg_s * 1000.0, 4)}
 
     result = {
@@ -351,6 +370,7 @@ def run_gpu(args):
         "gpu_launches": int(launches),
         "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
         "intersections_per_view": intersections,
+        "fallback_particles_per_view": int(round(float(np.mean(view_fallback)))) if view_fallback else 0,
     }
     if clock_info is not None:
         result["clocks"] = clock_info

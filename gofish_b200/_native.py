@@ -42,6 +42,7 @@ class GfTracerConfig(ctypes.Structure):
         ("sort_key", ctypes.c_int32),
         ("enable_hit_counts", ctypes.c_int32),
         ("admission_fallback", ctypes.c_int32),
+        ("composite_log_capacity", ctypes.c_int32),
     ]
 
 
@@ -90,7 +91,7 @@ class GfTraceStats(ctypes.Structure):
         ("num_tiles", ctypes.c_uint32),
         ("num_particles", ctypes.c_uint32),
         ("kernel_launches", ctypes.c_uint32),
-        ("reserved", ctypes.c_uint32),
+        ("fallback_particles", ctypes.c_uint32),
         ("total_kernel_launches", ctypes.c_uint64),
     ]
 
@@ -184,6 +185,8 @@ _SIGNATURES = [
                                          _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("gf_view_shape_packed", ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int64, ctypes.POINTER(GfShapeCamera),
                                             ctypes.c_double, ctypes.c_int, _vp, _vp, _vp]),
+    ("gf_pack_particle_rows", ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp]),
+    ("gf_unpack_particle_rows", ctypes.c_int, [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("gf_mip_best_rate", ctypes.c_int,
      [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, _vp,
       ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]),
@@ -216,7 +219,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 1:
+    if lib.gf_abi_version() != 2:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

@@ -26,6 +26,21 @@
 
 namespace gf {
 
+// Composite log of a training forward: for every pixel, the ids of the
+// particles in the order the k-buffer composited them, so that the backward
+// re-evaluates only the composited hits instead of replaying every candidate
+// through the k-buffer.  Entry i of the pixel at thread p of tile t is
+// ids[(i * tiles + t) * kTileThreads + p] (coalesced across a warp).  A pixel
+// that composites more than `capacity` hits marks its tile in `overflow`; the
+// backward replays such tiles.  ids == nullptr: no log (inference).
+struct CompositeLog {
+    uint32_t* ids;       // [capacity][tiles][kTileThreads]
+    uint32_t* count;     // [tiles][kTileThreads] entries logged, at most capacity
+    uint32_t* overflow;  // [tiles] 1 when a pixel of the tile exceeded the capacity
+    uint32_t capacity;
+    uint32_t tiles;
+};
+
 struct RenderArgs {
     FrameArgs f;
     const uint8_t* mask;
@@ -35,6 +50,7 @@ struct RenderArgs {
     const float* bounds;  // per-particle support radius (sphere around the mean containing the 3-sigma ellipsoid)
     const float* rayO;
     const float* rayD;
+    CompositeLog log;
 };
 
 struct RenderBwdArgs {
@@ -383,6 +399,20 @@ __device__ __forceinline__ float4 color_at(const RenderArgs& a, const Batch& b, 
     return __ldg(a.records + 4 * size_t(__ldg(a.sortedIds + sp)) + 3);
 }
 
+__device__ __forceinline__ uint32_t id_at(const RenderArgs& a, const Batch& b, uint32_t sp) {
+    const uint32_t j = sp - b.base;
+    if (j < b.cnt) return b.ids[j];
+    return __ldg(a.sortedIds + sp);
+}
+
+// Appends one composited particle to the pixel's log (entries past the
+// capacity are counted, not stored).
+__device__ __forceinline__ void log_composite(const CompositeLog& lg, uint32_t tile, uint32_t& n, uint32_t id) {
+    if (lg.ids == nullptr) return;
+    if (n < lg.capacity) lg.ids[(size_t(n) * lg.tiles + tile) * kTileThreads + threadIdx.x] = id;
+    ++n;
+}
+
 // Front-to-back composite of one hit (reference gutKBufferRenderer.cuh:307-416);
 // c.yzw is the particle's colour.
 __device__ __forceinline__ void composite_fwd(PixelFwd& s, float ht, float ha, float4 c) {
@@ -421,6 +451,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
     RingKBuffer<KR> kb;
     kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
+    uint32_t nlog = 0;
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
         for (uint32_t base = range.x; base < range.y; base += kBatch) {
@@ -444,12 +475,14 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                     float alpha, ht;
                     if (hit_staged(ts, sRec[j], alpha, ht)) {
                         if constexpr (K == 0) {
+                            log_composite(a.log, uint32_t(ts.tile), nlog, sId[j]);
                             composite_fwd(s, ht, alpha, sRec[j].d);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
                                 uint32_t s0;
                                 kb.pop_front(t0, a0, s0);
+                                log_composite(a.log, uint32_t(ts.tile), nlog, id_at(a, bt, s0));
                                 composite_fwd(s, t0, a0, color_at(a, bt, s0));
                             }
                             kb.insert(ht, alpha, base + uint32_t(j));
@@ -463,9 +496,16 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                 float ht, ha;
                 uint32_t sp;
                 kb.entry(i, ht, ha, sp);
+                log_composite(a.log, uint32_t(ts.tile), nlog, id_at(a, bt, sp));
                 composite_fwd(s, ht, ha, color_at(a, bt, sp));
             }
         }
+    }
+    if (a.log.ids != nullptr) {
+        const CompositeLog& lg = a.log;
+        lg.count[size_t(ts.tile) * kTileThreads + threadIdx.x] = min(nlog, lg.capacity);
+        const int over = __syncthreads_or(nlog > lg.capacity);
+        if (threadIdx.x == 0) lg.overflow[ts.tile] = over ? 1u : 0u;
     }
     if (!ts.inImage) return;
     float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -616,6 +656,8 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
     Staged* sRec = reinterpret_cast<Staged*>(smem);
     uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
     if (a.r.mask[blockIdx.x] == 0u) return;  // block-uniform
+    // with a composite log only the tiles whose log overflowed are replayed
+    if (a.r.log.ids != nullptr && a.r.log.overflow[blockIdx.x] == 0u) return;
     const TileSetup ts = tile_setup(a.r, true);
     const Ray& ray = ts.ray;
     PixelBwd s;
@@ -700,6 +742,73 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
             }
             accumulate_grad(a.gradRecords, have, cid, g);
         }
+    }
+}
+
+// Backward from the composite log: each pixel re-evaluates only the hits the
+// forward composited, in the logged order, with the forward's arithmetic
+// (the canonical origin B^-1 (o - mu) of a central tile equals the per-pixel
+// one bit for bit), and back-propagates them exactly as the replay does.
+// Tiles whose log overflowed are left to k_render_bwd.  The loop runs to the
+// warp's longest log so that the gradient reduction can use full-warp
+// shuffles.
+__global__ __launch_bounds__(kTileThreads) void k_render_bwd_log(RenderBwdArgs a) {
+    const uint32_t tile = blockIdx.x;
+    if (a.r.mask[tile] == 0u) return;                    // block-uniform
+    const CompositeLog& lg = a.r.log;
+    if (lg.overflow[tile] != 0u) return;                 // block-uniform
+    const FrameArgs& f = a.r.f;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int px = int(tile % uint32_t(f.gx)) * kTile + (warp & 1) * 8 + (lane & 7);
+    const int py = int(tile / uint32_t(f.gx)) * kTile + (warp >> 1) * 4 + (lane >> 3);
+    const bool inImage = px < f.W && py < f.H;
+    const size_t pix = size_t(px) + size_t(f.W) * size_t(py);
+    Ray ray;
+    ray.valid = false;
+    ray.o = v3(0.0f, 0.0f, 0.0f);
+    ray.d = v3(0.0f, 0.0f, 1.0f);
+    ray.tmin = 0.0f;
+    ray.tmax = 0.0f;
+    if (inImage) {
+        ray = make_ray(f.pose, v3(a.r.rayO[3 * pix], a.r.rayO[3 * pix + 1], a.r.rayO[3 * pix + 2]),
+                       v3(a.r.rayD[3 * pix], a.r.rayD[3 * pix + 1], a.r.rayD[3 * pix + 2]));
+    }
+    PixelBwd s;
+    s.T = 1.0f;
+    s.depth = 0.0f;
+    s.r = s.g = s.b = 0.0f;
+    s.alive = ray.valid;
+    uint32_t n = 0;
+    if (ray.valid) {
+        const float4 fo = reinterpret_cast<const float4*>(a.rgba)[pix];
+        const float4 go = reinterpret_cast<const float4*>(a.gradRgba)[pix];
+        s.featB[0] = fo.x; s.featB[1] = fo.y; s.featB[2] = fo.z;
+        s.featG[0] = go.x; s.featG[1] = go.y; s.featG[2] = go.z;
+        s.TB = 1.0f - fo.w;
+        s.TG = -1.0f * go.w;
+        s.hitTB = a.hitDistance[pix];
+        s.hitTG = a.gradHitDistance[pix];
+        n = lg.count[size_t(tile) * kTileThreads + threadIdx.x];
+    }
+    uint32_t warpN = n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) warpN = max(warpN, __shfl_xor_sync(0xffffffffu, warpN, o));
+    const uint32_t* ids = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
+    const size_t stride = size_t(lg.tiles) * kTileThreads;
+#pragma unroll 1
+    for (uint32_t i = 0; i < warpN; ++i) {
+        bool have = false;
+        uint32_t cid = kInvalidParticle;
+        float4 g[4] = {};
+        if (i < n && s.alive) {
+            cid = __ldg(ids + i * stride);
+            const Record q = load_record(a.r.records, cid);
+            const V3 gro = binv_times(q.b, q.c, q.d, v3(ray.o.x - q.a.x, ray.o.y - q.a.y, ray.o.z - q.a.z));
+            float alpha, ht;
+            if (hit_with_origin(ray, gro, q.b, q.c, q.d, q.a.w, alpha, ht)) have = hit_vjp(s, ray, q, ht, alpha, g);
+            if (s.T < kMinTransmittance) s.alive = false;
+        }
+        accumulate_grad(a.gradRecords, have, cid, g);
     }
 }
 

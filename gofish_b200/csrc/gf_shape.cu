@@ -663,6 +663,72 @@ int launch_check() {
 
 unsigned blocks_for(int64_t n) { return unsigned((n + kThreads - 1) / kThreads); }
 
+// ------------------------------------------------------------------ row packing
+// The training renderer's [N,32] particle rows from the model's per-slot
+// tensors, and the row gradient back to them (reference tracer.py:171-179,
+// :334-343).  One thread per row; the row is written and read as 8 float4.
+struct PackPtrs {
+    const float* pos;      // [N,3]
+    const float* dens;     // [N]
+    const float* rot;      // [N,4]
+    const float* scale;    // [N,3]
+    const float* idens;    // [N]
+    const float* factor;   // [N,9]
+    const float* inverse;  // [N,9]
+};
+
+__global__ __launch_bounds__(kThreads) void k_pack_rows(PackPtrs p, int64_t n, float4* __restrict__ out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* f = p.factor + 9 * i;
+    const float* v = p.inverse + 9 * i;
+    float4* o = out + 8 * i;
+    o[0] = make_float4(p.pos[3 * i], p.pos[3 * i + 1], p.pos[3 * i + 2], p.dens[i]);
+    o[1] = make_float4(p.rot[4 * i], p.rot[4 * i + 1], p.rot[4 * i + 2], p.rot[4 * i + 3]);
+    o[2] = make_float4(p.scale[3 * i], p.scale[3 * i + 1], p.scale[3 * i + 2], p.idens[i]);
+    o[3] = make_float4(f[0], f[1], f[2], f[3]);
+    o[4] = make_float4(f[4], f[5], f[6], f[7]);
+    o[5] = make_float4(f[8], v[0], v[1], v[2]);
+    o[6] = make_float4(v[3], v[4], v[5], v[6]);
+    o[7] = make_float4(v[7], v[8], 0.0f, 0.0f);
+}
+
+struct UnpackPtrs {
+    float* pos;
+    float* dens;
+    float* rot;
+    float* scale;
+    float* idens;
+    float* factor;
+    float* inverse;
+};
+
+__global__ __launch_bounds__(kThreads) void k_unpack_rows(const float4* __restrict__ in, int64_t n, UnpackPtrs p) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float4* r = in + 8 * i;
+    const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3], r4 = r[4], r5 = r[5], r6 = r[6], r7 = r[7];
+    p.pos[3 * i] = r0.x;
+    p.pos[3 * i + 1] = r0.y;
+    p.pos[3 * i + 2] = r0.z;
+    p.dens[i] = r0.w;
+    p.rot[4 * i] = r1.x;
+    p.rot[4 * i + 1] = r1.y;
+    p.rot[4 * i + 2] = r1.z;
+    p.rot[4 * i + 3] = r1.w;
+    p.scale[3 * i] = r2.x;
+    p.scale[3 * i + 1] = r2.y;
+    p.scale[3 * i + 2] = r2.z;
+    p.idens[i] = r2.w;
+    float* f = p.factor + 9 * i;
+    float* v = p.inverse + 9 * i;
+    f[0] = r3.x; f[1] = r3.y; f[2] = r3.z; f[3] = r3.w;
+    f[4] = r4.x; f[5] = r4.y; f[6] = r4.z; f[7] = r4.w;
+    f[8] = r5.x; v[0] = r5.y; v[1] = r5.z; v[2] = r5.w;
+    v[3] = r6.x; v[4] = r6.y; v[5] = r6.z; v[6] = r6.w;
+    v[7] = r7.x; v[8] = r7.y;
+}
+
 }  // namespace
 
 extern "C" {
@@ -757,6 +823,38 @@ int gf_view_shape_packed(const float* positions, const float* quaternions, const
     a.status = status;
     a.firstRow = reinterpret_cast<unsigned long long*>(status + 2);
     k_view_shape_packed<<<blocks_for(n), kThreads, 0, s>>>(a);
+    return launch_check();
+}
+
+int gf_pack_particle_rows(const float* positions, const float* density, const float* rotations,
+                          const float* scales, const float* intrinsic_density, const float* factor,
+                          const float* inverse_factor, int64_t n, float* rows, void* stream) {
+    if (n < 0) return gf_record_error(GF_ERR_BAD_INPUT, "pack rows: negative row count");
+    if (n == 0) return GF_OK;
+    if (positions == nullptr || density == nullptr || rotations == nullptr || scales == nullptr ||
+        intrinsic_density == nullptr || factor == nullptr || inverse_factor == nullptr || rows == nullptr)
+        return gf_record_error(GF_ERR_BAD_INPUT, "pack rows: buffers must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(rows) & 15u) != 0u)
+        return gf_record_error(GF_ERR_BAD_INPUT, "pack rows: output rows must be 16-byte aligned");
+    PackPtrs p{positions, density, rotations, scales, intrinsic_density, factor, inverse_factor};
+    k_pack_rows<<<blocks_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p, n,
+                                                                                  reinterpret_cast<float4*>(rows));
+    return launch_check();
+}
+
+int gf_unpack_particle_rows(const float* rows, int64_t n, float* positions, float* density, float* rotations,
+                            float* scales, float* intrinsic_density, float* factor, float* inverse_factor,
+                            void* stream) {
+    if (n < 0) return gf_record_error(GF_ERR_BAD_INPUT, "unpack rows: negative row count");
+    if (n == 0) return GF_OK;
+    if (positions == nullptr || density == nullptr || rotations == nullptr || scales == nullptr ||
+        intrinsic_density == nullptr || factor == nullptr || inverse_factor == nullptr || rows == nullptr)
+        return gf_record_error(GF_ERR_BAD_INPUT, "unpack rows: buffers must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(rows) & 15u) != 0u)
+        return gf_record_error(GF_ERR_BAD_INPUT, "unpack rows: input rows must be 16-byte aligned");
+    UnpackPtrs p{positions, density, rotations, scales, intrinsic_density, factor, inverse_factor};
+    k_unpack_rows<<<blocks_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float4*>(rows), n, p);
     return launch_check();
 }
 

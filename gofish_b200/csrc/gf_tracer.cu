@@ -12,6 +12,7 @@
 // eight times, gutRenderer.cu:843-1599).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -56,7 +57,10 @@ struct gf_tracer {
     DeviceBuffer keys[2], ids[2], hist;
     DeviceBuffer gradRecords;
     DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
-    uint64_t* hostTotal = nullptr;
+    DeviceBuffer logIds, logCount, logOverflow;           // composite log of the last training forward
+    gf::CompositeLog frameLog{};
+    uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size (low 32 bits)
+    uint32_t fallbackParticles = 0;
     int finalBuf = 0;
     bool haveForward = false;
     gf::FrameArgs frame{};
@@ -116,7 +120,7 @@ int bind_device(gf_tracer* t) {
     GF_CUDA(cudaGetDevice(&dev));
     if (t->device < 0) {
         t->device = dev;
-        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), sizeof(uint64_t), cudaHostAllocDefault));
+        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), 2 * sizeof(uint64_t), cudaHostAllocDefault));
     } else if (t->device != dev) {
         return fail(GF_ERR_STATE, "tracer bound to device %d, called on device %d", t->device, dev);
     }
@@ -206,9 +210,16 @@ int dispatch_bwd(int K, const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t
     return GF_OK;
 }
 
-// Projection, binning, sort and forward composite.
+// Composite log capacity: entries per pixel (128 covers the deepest pixels of
+// the 1M-Gaussian 200 deg view; deeper tiles are replayed), bounded so that
+// the log stays within 4 GiB.
+constexpr uint32_t kLogCapacity = 128;
+constexpr size_t kLogBudgetBytes = size_t(4) << 30;
+
+// Projection, binning, sort and forward composite; a training forward
+// (logComposites) also records the composite log for the backward.
 int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, float* hc, float* vis,
-            cudaStream_t stream) {
+            bool logComposites, cudaStream_t stream) {
     if (int e = bind_device(t)) return e;
     const TileMask* mask = nullptr;
     if (int e = validate_inputs(t, in, &mask)) return e;
@@ -274,6 +285,9 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
                 gx = (gx + gf::fb::kFan - 1) / gf::fb::kFan;
                 gy = (gy + gf::fb::kFan - 1) / gf::fb::kFan;
             }
+            tr.optical[0] = f.pose.Rinv[2];
+            tr.optical[1] = f.pose.Rinv[5];
+            tr.optical[2] = f.pose.Rinv[8];
             tr.second = nodes;     // the leaves' second cones follow the levels,
             tr.sums = nodes + T;   // then one ray sum per node
             if (int e = t->coneA.ensure(sizeof(float4) * (2 * size_t(nodes) + T), stream)) return e;
@@ -319,8 +333,12 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
             return e;
     }
     GF_CUDA(cudaMemcpyAsync(t->hostTotal, t->total.ptr, sizeof(uint64_t), cudaMemcpyDeviceToHost, stream));
+    t->hostTotal[1] = 0;
+    if (fa.enabled && N > 0)
+        GF_CUDA(cudaMemcpyAsync(t->hostTotal + 1, fa.bigCount, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
     GF_CUDA(cudaStreamSynchronize(stream));
     const uint64_t I = *t->hostTotal;
+    t->fallbackParticles = uint32_t(t->hostTotal[1]);
     if (I > 0xffffffffull - gf::kSortTile)
         return fail(GF_ERR_CAPACITY, "%llu tile intersections exceed the 32-bit index range",
                     static_cast<unsigned long long>(I));
@@ -370,6 +388,21 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     a.bounds = t->bounds.as<float>();
     a.rayO = in->ray_origin;
     a.rayD = in->ray_direction;
+    a.log = gf::CompositeLog{};
+    if (logComposites && T > 0 && t->cfg.composite_log_capacity >= 0) {
+        const size_t perEntry = size_t(T) * gf::kTileThreads * sizeof(uint32_t);
+        const size_t want = t->cfg.composite_log_capacity > 0 ? size_t(t->cfg.composite_log_capacity) : kLogCapacity;
+        const uint32_t cap = uint32_t(std::min<size_t>(want, std::max<size_t>(1, kLogBudgetBytes / perEntry)));
+        if (int e = t->logIds.ensure(perEntry * cap, stream)) return e;
+        if (int e = t->logCount.ensure(perEntry, stream)) return e;
+        if (int e = t->logOverflow.ensure(sizeof(uint32_t) * size_t(T), stream)) return e;
+        a.log.ids = t->logIds.as<uint32_t>();
+        a.log.count = t->logCount.as<uint32_t>();
+        a.log.overflow = t->logOverflow.as<uint32_t>();
+        a.log.capacity = cap;
+        a.log.tiles = T;
+    }
+    t->frameLog = a.log;
     {
         StageTimer st(t, GF_STAGE_RENDER_FWD, stream);
         if (int e = dispatch_fwd(t->cfg.k_buffer_size, a, T, rgba, hd, hc, stream)) return e;
@@ -423,6 +456,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
         for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount}) b->release();
+        for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
                                 &t->hist,    &t->gradRecords};
@@ -457,13 +491,13 @@ int gf_tracer_register_tile_mask(gf_tracer* t, const uint8_t* mask, uint32_t til
 int gf_tracer_trace(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_outputs* out, void* stream) {
     if (t == nullptr || out == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
     return forward(t, in, out->rgba, out->hit_distance, t->cfg.enable_hit_counts ? out->hit_count : nullptr,
-                   out->visibility, static_cast<cudaStream_t>(stream));
+                   out->visibility, true, static_cast<cudaStream_t>(stream));
 }
 
 int gf_tracer_trace_inference(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hit_distance,
                               void* stream) {
     if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
-    return forward(t, in, rgba, hit_distance, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+    return forward(t, in, rgba, hit_distance, nullptr, nullptr, false, static_cast<cudaStream_t>(stream));
 }
 
 int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_grads* g, void* stream) {
@@ -492,6 +526,7 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     a.r.bounds = t->bounds.as<float>();
     a.r.rayO = t->frameRayO;
     a.r.rayD = t->frameRayD;
+    a.r.log = t->frameLog;
     a.rgba = g->rgba;
     a.hitDistance = g->hit_distance;
     a.gradRgba = g->grad_rgba;
@@ -499,6 +534,12 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     a.gradRecords = t->gradRecords.as<float4>();
     {
         StageTimer st(t, GF_STAGE_RENDER_BWD, s);
+        if (a.r.log.ids != nullptr) {
+            // tiles with a complete log, then the replay of the tiles whose log overflowed
+            gf::k_render_bwd_log<<<T, gf::kTileThreads, 0, s>>>(a);
+            t->launches += 1;
+            GF_LAUNCH_CHECK();
+        }
         if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, T, s)) return e;
     }
     t->launches += 1;
@@ -548,7 +589,7 @@ int gf_tracer_stats(const gf_tracer* t, gf_trace_stats* st) {
     st->num_tiles = uint32_t(t->frame.gx * t->frame.gy);
     st->num_particles = t->frame.N;
     st->kernel_launches = t->launches;
-    st->reserved = 0;
+    st->fallback_particles = t->fallbackParticles;
     st->total_kernel_launches = t->totalLaunches;
     return GF_OK;
 }

@@ -83,6 +83,7 @@ struct TileTree {
     uint32_t sums;    // offset (in A) of each node's sum of unit pixel rays
     const float4* A;  // axis.xyz, cos phi (> 1.5: empty)
     const float* S;   // sin phi
+    float optical[3]; // the camera's optical axis in world coordinates (third column of R^-1, not normalised)
 };
 
 struct Cap {
@@ -156,18 +157,54 @@ __device__ __forceinline__ bool ancestors_pass(const TileTree& t, uint32_t x, ui
 
 // The admitted tiles of one particle, found by one warp.  kAll: every
 // retained tile.  kCone: every leaf that meets the cap together with all its
-// ancestors, by a depth-first descent that expands the two top nodes of a
-// shared-memory stack per step (16 children each, one per lane), pushing the
-// inner children that pass and emitting the leaves.  Pending nodes stay below
-// 32 per level, so kWarpStack entries suffice; were it ever exceeded, the
-// level-1 scan below recomputes the same set.  emit(k, tile) receives the
-// k-th admitted tile (in an order the sorted output does not depend on);
-// returns the number of tiles (warp-uniform).
-constexpr int kWarpStack = 32 * kMaxLevels;
+// ancestors, by a level-synchronous walk that keeps all 32 lanes testing:
+// the frontier (nodes of one level whose path from the root passes) is kept
+// in shared memory and its children are tested 32 at a time; from level 2
+// the passing level-1 children of each batch of 32 are expanded at once into
+// their leaves, two level-1 nodes (16 leaves each) per step.  A frontier
+// larger than kFrontier entries (a raster beyond 4096x4096 pixels) falls back
+// to the level-1 scan below, which yields the same set.  emit(k, tile)
+// receives the k-th admitted tile (in an order the sorted output does not
+// depend on: one particle's keys name distinct tiles); returns the number of
+// tiles (warp-uniform).
+constexpr int kFrontier = 256;
+constexpr int kWarpScratch = 2 * kFrontier;
+
+// Leaves of the level-1 nodes in `nodes` (bit i: level-1 node base1 + i of
+// the candidate list `list`), two nodes per step.
+template <typename Emit>
+__device__ __forceinline__ void warp_leaves(const TileTree& t, const Cap& c, uint32_t lane, uint32_t below,
+                                            uint32_t nodes, const uint32_t* list, uint32_t& n, Emit& emit) {
+    const uint32_t gx1 = uint32_t(t.gx[1]);
+    const uint32_t gx0 = uint32_t(t.gx[0]), gy0 = uint32_t(t.gy[0]);
+    while (nodes != 0u) {
+        const uint32_t a = uint32_t(__ffs(nodes) - 1);
+        nodes &= nodes - 1u;
+        uint32_t b = 32u;
+        if (nodes != 0u) {
+            b = uint32_t(__ffs(nodes) - 1);
+            nodes &= nodes - 1u;
+        }
+        const uint32_t pick = lane < 16u ? a : b;
+        bool ok = false;
+        uint32_t leaf = 0u;
+        if (pick < 32u) {
+            const uint32_t n1 = list[pick];
+            const uint32_t cx = (n1 % gx1) * kFan + (lane & 3u), cy = (n1 / gx1) * kFan + ((lane >> 2) & 3u);
+            if (cx < gx0 && cy < gy0) {
+                leaf = cy * gx0 + cx;
+                ok = node_pass(t, 0, leaf, c);
+            }
+        }
+        const uint32_t m = __ballot_sync(0xffffffffu, ok);
+        if (ok) emit(n + uint32_t(__popc(m & below)), leaf);
+        n += uint32_t(__popc(m));
+    }
+}
 
 template <typename Emit>
 __device__ __forceinline__ uint32_t warp_tiles(const TileTree& t, const uint8_t* __restrict__ mask, const Cap& c,
-                                               uint32_t lane, uint32_t* __restrict__ stack, Emit&& emit) {
+                                               uint32_t lane, uint32_t* __restrict__ scratch, Emit&& emit) {
     uint32_t n = 0;
     const uint32_t below = (1u << lane) - 1u;
     const uint32_t g0 = uint32_t(t.gx[0] * t.gy[0]);
@@ -185,62 +222,88 @@ __device__ __forceinline__ uint32_t warp_tiles(const TileTree& t, const uint8_t*
     if (c.mode != kCone) return 0u;
     const int top = t.n - 1;
     if (!node_pass(t, top, 0u, c)) return 0u;
-    if (lane == 0) stack[0] = uint32_t(top) << 24;
+    uint32_t* cur = scratch;
+    uint32_t* nxt = scratch + kFrontier;
+    uint32_t* l1 = scratch + kFrontier;  // the level-1 batch reuses the spare frontier
+    if (lane == 0) cur[0] = 0u;
     __syncwarp();
-    int sp = 1;
+    uint32_t curN = 1;
+    int level = top;
     bool overflow = false;
-    while (sp > 0) {
-        const int take = min(sp, 2);
-        const int g = int(lane >> 4);
-        const bool active = g < take;
-        const uint32_t e = active ? stack[sp - 1 - g] : 0u;
-        __syncwarp();  // the popped slots are reused by this step's pushes
-        sp -= take;
-        bool pass = false;
-        int cl = 0;
-        uint32_t child = 0u;
-        if (active) {
-            const int l = int(e >> 24);
-            const uint32_t node = e & 0x00ffffffu;
-            cl = l - 1;
-            const uint32_t cx = (node % uint32_t(t.gx[l])) * kFan + (lane & 3u);
-            const uint32_t cy = (node / uint32_t(t.gx[l])) * kFan + ((lane >> 2) & 3u);
-            if (cx < uint32_t(t.gx[cl]) && cy < uint32_t(t.gy[cl])) {
-                child = cy * uint32_t(t.gx[cl]) + cx;
-                pass = node_pass(t, cl, child, c);
+    // levels >= 3: expand the frontier one level down
+    while (level >= 3 && !overflow) {
+        const int cl = level - 1;
+        const uint32_t pgx = uint32_t(t.gx[level]), cgx = uint32_t(t.gx[cl]), cgy = uint32_t(t.gy[cl]);
+        const uint32_t total = curN * 16u;
+        uint32_t nextN = 0;
+        for (uint32_t base = 0; base < total; base += 32u) {
+            const uint32_t idx = base + lane;
+            bool pass = false;
+            uint32_t child = 0u;
+            if (idx < total) {
+                const uint32_t node = cur[idx >> 4];
+                const uint32_t cx = (node % pgx) * kFan + (idx & 3u), cy = (node / pgx) * kFan + ((idx >> 2) & 3u);
+                if (cx < cgx && cy < cgy) {
+                    child = cy * cgx + cx;
+                    pass = node_pass(t, cl, child, c);
+                }
             }
+            const uint32_t m = __ballot_sync(0xffffffffu, pass);
+            if (nextN + uint32_t(__popc(m)) > uint32_t(kFrontier)) {
+                overflow = true;
+                break;
+            }
+            if (pass) nxt[nextN + uint32_t(__popc(m & below))] = child;
+            nextN += uint32_t(__popc(m));
         }
-        const uint32_t leaves = __ballot_sync(0xffffffffu, pass && cl == 0);
-        const uint32_t inner = __ballot_sync(0xffffffffu, pass && cl > 0);
-        if (pass && cl == 0) emit(n + uint32_t(__popc(leaves & below)), child);
-        n += uint32_t(__popc(leaves));
-        const int pushes = __popc(inner);
-        if (sp + pushes > kWarpStack) {
-            overflow = true;
-            break;
-        }
-        if (pass && cl > 0) stack[sp + __popc(inner & below)] = (uint32_t(cl) << 24) | child;
-        sp += pushes;
         __syncwarp();
+        uint32_t* tmp = cur;
+        cur = nxt;
+        nxt = tmp;
+        l1 = nxt;
+        curN = nextN;
+        level = cl;
     }
-    if (!overflow) return n;
+    if (!overflow) {
+        if (level == 1) {
+            // a two-level tree: the root is the only level-1 node
+            warp_leaves(t, c, lane, below, 1u, cur, n, emit);
+            return n;
+        }
+        // level 2: its level-1 children, 32 at a time, then their leaves
+        const uint32_t pgx = uint32_t(t.gx[2]), cgx = uint32_t(t.gx[1]), cgy = uint32_t(t.gy[1]);
+        const uint32_t total = curN * 16u;
+        for (uint32_t base = 0; base < total; base += 32u) {
+            const uint32_t idx = base + lane;
+            bool pass = false;
+            uint32_t child = 0u;
+            if (idx < total) {
+                const uint32_t node = cur[idx >> 4];
+                const uint32_t cx = (node % pgx) * kFan + (idx & 3u), cy = (node / pgx) * kFan + ((idx >> 2) & 3u);
+                if (cx < cgx && cy < cgy) {
+                    child = cy * cgx + cx;
+                    pass = node_pass(t, 1, child, c);
+                }
+            }
+            const uint32_t m = __ballot_sync(0xffffffffu, pass);
+            l1[lane] = child;
+            __syncwarp();
+            warp_leaves(t, c, lane, below, m, l1, n, emit);
+            __syncwarp();
+        }
+        return n;
+    }
     // Level-1 scan: nodes whose ancestors all pass, then their 16 leaves.
     n = 0;
     const uint32_t gx1 = uint32_t(t.gx[1]), g1 = gx1 * uint32_t(t.gy[1]);
-    const uint32_t gx0 = uint32_t(t.gx[0]), gy0 = uint32_t(t.gy[0]);
     for (uint32_t base = 0; base < g1; base += 32u) {
         const uint32_t node = base + lane;
         const bool pass = node < g1 && node_pass(t, 1, node, c) && ancestors_pass(t, node % gx1, node / gx1, c);
-        uint32_t m = __ballot_sync(0xffffffffu, pass);
-        while (m != 0u) {
-            const uint32_t n1 = base + uint32_t(__ffs(m) - 1);
-            m &= m - 1u;
-            const uint32_t cx = (n1 % gx1) * kFan + (lane & 3u), cy = (n1 / gx1) * kFan + (lane >> 2);
-            const bool ok = lane < 16u && cx < gx0 && cy < gy0 && node_pass(t, 0, cy * gx0 + cx, c);
-            const uint32_t cm = __ballot_sync(0xffffffffu, ok);
-            if (ok) emit(n + uint32_t(__popc(cm & below)), cy * gx0 + cx);
-            n += uint32_t(__popc(cm));
-        }
+        const uint32_t m = __ballot_sync(0xffffffffu, pass);
+        __syncwarp();
+        scratch[lane] = node;
+        __syncwarp();
+        warp_leaves(t, c, lane, below, m, scratch, n, emit);
     }
     return n;
 }
@@ -408,15 +471,18 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
     else A[second + tile] = empty, S[second + tile] = 0.0f;
 }
 
-// Parent cones of level l >= 1, one block per node: the node's ray sum is the
-// sum of its 4x4 children's (row-major order) and its axis that sum
-// normalised, the mean direction of the pixel rays under it; the node is
-// empty when all its children are; cos phi = the smallest, over the non-empty
-// cones of the leaves
-// under the node, of cos(angle(axis, a) + phi_a) = (axis . a) cos phi_a -
-// |axis x a| sin phi_a, less kEps; a cone reaching past pi (sin of the sum
-// < 0) makes the node cover the sphere (cos -1, sin 0).  A minimum is exact
-// in any order, so the block reduction gives the oracle's value.
+// Parent cones of level l >= 1, one block per node.  The node's ray sum is
+// the sum of its 4x4 children's (row-major order).  Two axes are tried: the
+// normalised ray sum (the mean direction of the pixel rays under the node)
+// and the camera's optical axis; for each, cos phi = the smallest, over the
+// non-empty cones of the leaves under the node, of cos(angle(axis, a) +
+// phi_a) = (axis . a) cos phi_a - |axis x a| sin phi_a, and a cone reaching
+// past pi makes the bound cover the sphere.  The node keeps the axis with the
+// larger cos phi (the mean on ties), less kEps.  The mean alone fails for
+// wide nodes: over a 200 deg field the rim rays can outweigh the centre and
+// turn the sum backwards, so that the root would cover the whole sphere.  The
+// node is empty when all its children are.  Minima are exact in any order, so
+// the block reduction gives the oracle's values.
 __device__ __forceinline__ void bound_cone(V3 ax, float4 a, float cs, float& mn, bool& full) {
     if (a.w > 1.5f) return;
     const V3 ca = v3(a.x, a.y, a.z);
@@ -429,8 +495,8 @@ __device__ __forceinline__ void bound_cone(V3 ax, float4 a, float cs, float& mn,
 
 __global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, float4* __restrict__ A,
                                                          float* __restrict__ S) {
-    __shared__ float axis[4];
-    __shared__ float wmin[8];
+    __shared__ float axis[8];
+    __shared__ float wmin[2][8];
     const int node = blockIdx.x;
     const int pgx = t.gx[l], cgx = t.gx[l - 1], cgy = t.gy[l - 1];
     const int px = node % pgx, py = node / pgx;
@@ -453,42 +519,68 @@ __global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, floa
         axis[0] = ok ? sum.x / sn : 0.0f;
         axis[1] = ok ? sum.y / sn : 0.0f;
         axis[2] = ok ? sum.z / sn : 1.0f;
-        axis[3] = !any ? 2.0f : (ok ? 1.0f : -1.0f);  // empty / bounded / whole sphere
+        axis[3] = !any ? 2.0f : (ok ? 1.0f : -1.0f);  // empty / mean usable / mean degenerate
+        const V3 o = v3(t.optical[0], t.optical[1], t.optical[2]);
+        const float on = __fsqrt_rn(dot3(o, o));
+        const bool ook = on > 0.0f && isfinite_f(on);
+        axis[4] = ook ? o.x / on : 0.0f;
+        axis[5] = ook ? o.y / on : 0.0f;
+        axis[6] = ook ? o.z / on : 1.0f;
+        axis[7] = ook ? 1.0f : -1.0f;
     }
     __syncthreads();
-    const V3 ax = v3(axis[0], axis[1], axis[2]);
     const float state = axis[3];
-    if (state != 1.0f) {
+    if (state > 1.5f) {
         if (threadIdx.x == 0) {
-            A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, state);
+            A[t.offset[l] + node] = make_float4(axis[0], axis[1], axis[2], 2.0f);
             S[t.offset[l] + node] = 0.0f;
         }
         return;
     }
+    const V3 am = v3(axis[0], axis[1], axis[2]);
+    const V3 ao = v3(axis[4], axis[5], axis[6]);
     int span = 1;
     for (int k = 0; k < l; ++k) span *= kFan;
     const int gx0 = t.gx[0], gy0 = t.gy[0];
     const int x0 = px * span, y0 = py * span, x1 = min(gx0, x0 + span), y1 = min(gy0, y0 + span);
     const int w = x1 - x0, cnt = w * (y1 - y0);
-    float mn = 1.0f;
-    bool full = false;
+    float mm = 1.0f, mo = 1.0f;
+    bool fm = state < 0.0f, fo = axis[7] < 0.0f;
     for (int k = threadIdx.x; k < cnt; k += blockDim.x) {
         const uint32_t leaf = uint32_t((y0 + k / w) * gx0 + x0 + k % w);
-        bound_cone(ax, A[leaf], S[leaf], mn, full);
-        bound_cone(ax, A[t.second + leaf], S[t.second + leaf], mn, full);
+        const float4 a0 = A[leaf], a1 = A[t.second + leaf];
+        const float s0 = S[leaf], s1 = S[t.second + leaf];
+        bound_cone(am, a0, s0, mm, fm);
+        bound_cone(am, a1, s1, mm, fm);
+        bound_cone(ao, a0, s0, mo, fo);
+        bound_cone(ao, a1, s1, mo, fo);
     }
-    full = __syncthreads_or(full) != 0;
-    for (int o = 16; o > 0; o >>= 1) mn = min_f(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    if ((threadIdx.x & 31) == 0) wmin[threadIdx.x >> 5] = mn;
+    fm = __syncthreads_or(fm) != 0;
+    fo = __syncthreads_or(fo) != 0;
+    for (int o = 16; o > 0; o >>= 1) {
+        mm = min_f(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        mo = min_f(mo, __shfl_xor_sync(0xffffffffu, mo, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        wmin[0][threadIdx.x >> 5] = mm;
+        wmin[1][threadIdx.x >> 5] = mo;
+    }
     __syncthreads();
     if (threadIdx.x != 0) return;
-    for (int k = 0; k < int(blockDim.x >> 5); ++k) mn = min_f(mn, wmin[k]);
-    if (full) {
+    for (int k = 0; k < int(blockDim.x >> 5); ++k) {
+        mm = min_f(mm, wmin[0][k]);
+        mo = min_f(mo, wmin[1][k]);
+    }
+    const float vm = fm ? -2.0f : mm, vo = fo ? -2.0f : mo;
+    const bool useOptical = vo > vm;
+    const V3 ax = useOptical ? ao : am;
+    const float best = useOptical ? vo : vm;
+    if (best < -1.5f) {
         A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, -1.0f);
         S[t.offset[l] + node] = 0.0f;
         return;
     }
-    const float cphi = max_f(-1.0f, mn - kEps);
+    const float cphi = max_f(-1.0f, best - kEps);
     A[t.offset[l] + node] = make_float4(ax.x, ax.y, ax.z, cphi);
     S[t.offset[l] + node] = __fsqrt_rn(max_f(0.0f, 1.0f - cphi * cphi));
 }
@@ -631,9 +723,9 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
                                                       uint32_t* __restrict__ counts, uint32_t* __restrict__ visibility,
                                                       const uint64_t* __restrict__ offsets,
                                                       uint64_t* __restrict__ keys, uint32_t* __restrict__ ids) {
-    __shared__ uint32_t stacks[8][fb::kWarpStack];
+    __shared__ uint32_t scratch[8][fb::kWarpScratch];
     const uint32_t lane = threadIdx.x & 31u;
-    uint32_t* stack = stacks[threadIdx.x >> 5];
+    uint32_t* stack = scratch[threadIdx.x >> 5];
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t total = *fa.bigCount;
     for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {

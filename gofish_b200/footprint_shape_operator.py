@@ -37,7 +37,7 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
-def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode):
+def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode, pending, start):
     n = scales.shape[0]
     dev = scales.device
     cov = torch.empty((n, 3, 3), dtype=torch.float32, device=dev)
@@ -52,23 +52,36 @@ def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preservin
                                     MODES[mode], cov.data_ptr(), factor.data_ptr(), inverse.data_ptr(),
                                     comp.data_ptr(), dens.data_ptr(), status.data_ptr(), _stream(scales)),
                   "full shape")
-    flags = status.cpu()
-    if int(flags[0]) != 0:
-        row = int(flags[2:].view(torch.int64)[0])
-        text = ", ".join(v for k, v in _STATUS_TEXT.items() if int(flags[0]) & k)
-        raise FootprintNumericalError(f"footprint full-shape failure ({text}) local_row={row}", global_row=row,
-                                      completed_native_chunks=0)
+    # the status words reach pinned host memory without a host synchronization;
+    # FullShape.check() reads them once the copy's event has completed
+    host = torch.empty(4, dtype=torch.int32, pin_memory=True)
+    host.copy_(status, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(dev))
+    pending.append((host, done, start, status))
     return cov, factor, inverse, comp, dens
+
+
+def _raise_failures(pending) -> None:
+    for index, (host, done, start, _status) in enumerate(pending):
+        done.synchronize()
+        flags = host
+        if int(flags[0]) != 0:
+            local = int(flags[2:].view(torch.int64)[0])
+            row = start + local
+            text = ", ".join(v for k, v in _STATUS_TEXT.items() if int(flags[0]) & k)
+            raise FootprintNumericalError(f"footprint full-shape failure ({text}) local_row={local} global_row={row}",
+                                          global_row=row, completed_native_chunks=index)
 
 
 class _FullShape(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode):
+    def forward(ctx, scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode, pending, start):
         s, q, d = scales.detach().float().contiguous(), quaternion.detach().float().contiguous(), \
             density.detach().float().contiguous()
         ob = observed.detach().to(torch.uint8).contiguous()
         q6c, jc = q6.detach().contiguous(), jacobian.detach().contiguous()
-        outs = _forward(s, q, d, q6c, jc, ob, mass_preserving, gamma, mode)
+        outs = _forward(s, q, d, q6c, jc, ob, mass_preserving, gamma, mode, pending, start)
         ctx.save_for_backward(s, q, d, q6c, jc, ob)
         ctx.mass_preserving, ctx.gamma, ctx.mode = bool(mass_preserving), float(gamma), mode
         ctx.set_materialize_grads(False)
@@ -95,7 +108,7 @@ class _FullShape(torch.autograd.Function):
                                             ob.data_ptr(), n, ctx.gamma, int(ctx.mass_preserving),
                                             *(ptr(t) for t in keep), gs.data_ptr(), gq.data_ptr(), gd.data_ptr(),
                                             _stream(s)), "full shape backward")
-        return gs, gq, gd, None, None, None, None, None, None
+        return gs, gq, gd, None, None, None, None, None, None, None, None
 
 
 @dataclass(frozen=True)
@@ -106,11 +119,23 @@ class FullShape:
     compensation: torch.Tensor
     density: torch.Tensor
     observed: torch.Tensor
+    pending: tuple = ()
+
+    def check(self) -> None:
+        """Raises FootprintNumericalError for the first failed row (waits for
+        the status words of the operator's launches)."""
+        _raise_failures(self.pending)
 
 
 def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mass_preserving: bool = True,
-                     pixel_variance: float = FILTER_VARIANCE_PIXELS, mode: str = "exact") -> FullShape:
-    """Full-shape factors for detached Q (float64 [N,6]) and Jacobian (float32 [N,2,3])."""
+                     pixel_variance: float = FILTER_VARIANCE_PIXELS, mode: str = "exact",
+                     defer_check: bool = False) -> FullShape:
+    """Full-shape factors for detached Q (float64 [N,6]) and Jacobian (float32 [N,2,3]).
+
+    A numerical failure raises FootprintNumericalError with the global row.
+    With ``defer_check`` the call does not wait for the device: the caller
+    runs ``FullShape.check()`` later (the training renderer does so once the
+    trace has synchronised its stream)."""
     n = scales.shape[0]
     if q6.requires_grad or q6.dtype != torch.float64 or tuple(q6.shape) != (n, 6):
         raise ValueError("q6 must be detached float64 with shape [N,6]")
@@ -126,21 +151,19 @@ def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mas
                                  allocator_allocated_bytes=int(torch.cuda.memory_allocated(scales.device)))
     rows = plan.chunk_rows if n else 0
     parts = []
-    for index, start in enumerate(range(0, n, max(1, rows)) if n else []):
+    pending: list = []
+    for start in range(0, n, max(1, rows)) if n else []:
         stop = min(n, start + rows)
-        try:
-            parts.append(_FullShape.apply(scales[start:stop], quaternion[start:stop], density[start:stop],
-                                          q6[start:stop], jacobian[start:stop], observed[start:stop],
-                                          bool(mass_preserving), float(pixel_variance), mode))
-        except FootprintNumericalError as error:
-            row = None if error.global_row is None else start + error.global_row
-            raise FootprintNumericalError(str(error) + f" global_row={row}", global_row=row,
-                                          completed_native_chunks=index) from error
+        parts.append(_FullShape.apply(scales[start:stop], quaternion[start:stop], density[start:stop],
+                                      q6[start:stop], jacobian[start:stop], observed[start:stop],
+                                      bool(mass_preserving), float(pixel_variance), mode, pending, start))
+    if not defer_check:
+        _raise_failures(pending)
     if not parts:
         empty = scales.new_zeros((0, 3, 3))
         return FullShape(empty, empty, empty, scales.new_zeros(0), density[:0], observed)
     outs = parts[0] if len(parts) == 1 else tuple(torch.cat([p[i] for p in parts], 0) for i in range(5))
-    return FullShape(*outs, observed=observed)
+    return FullShape(*outs, observed=observed, pending=tuple(pending))
 
 
 __all__ = ["FootprintNumericalError", "FullShape", "build_full_shape"]

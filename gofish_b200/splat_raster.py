@@ -62,6 +62,8 @@ class SplatRaster:
         if fallback not in ("none", "cone"):
             raise ValueError(f"render.gofish.fast_admission_fallback must be 'none' or 'cone' (got {fallback!r})")
         cfg.admission_fallback = _native.GF_FALLBACK_CONE if fallback == "cone" else _native.GF_FALLBACK_NONE
+        # entries per pixel of the composite log the backward reads (0: default, < 0: replay every tile)
+        cfg.composite_log_capacity = int(_select(conf, "render.splat.composite_log_capacity", 0))
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())

@@ -30,6 +30,7 @@ from typing import Any
 
 import torch
 
+from . import _native
 from .batch import create_camera_parameters
 from .physical_mip import scale_with_3d_filter
 from .physical_tile_mask import build_physical_tile_binding
@@ -70,10 +71,8 @@ class Tracer:
                 raise NotImplementedError("CoMe colour confidence is not rendered by this tracer")
             if mog_factor.shape != (n, 3, 3) or mog_inverse_factor.shape != mog_factor.shape:
                 raise ValueError("full-shape factor tensors must have shape [N,3,3]")
-            particle_density = torch.cat(
-                [mog_pos, mog_dns.reshape(n, 1), mog_rot, mog_scl, mog_intrinsic_dns.reshape(n, 1),
-                 mog_factor.reshape(n, 9), mog_inverse_factor.reshape(n, 9), mog_pos.new_zeros((n, 2))],
-                dim=1).float().contiguous()
+            particle_density = _pack_rows(mog_pos, mog_dns, mog_rot, mog_scl, mog_intrinsic_dns, mog_factor,
+                                          mog_inverse_factor)
             particle_features = mog_sph.float().contiguous()
             t0, t1 = sensor_poses.timestamps_us[0], sensor_poses.timestamps_us[1]
             p0, p1 = sensor_poses.T_world_sensors[0], sensor_poses.T_world_sensors[1]
@@ -106,12 +105,9 @@ class Tracer:
                 particle_features, ray_ori, ray_dir, None, ctx.sensor_params, poses.timestamps_us[0],
                 poses.timestamps_us[1], poses.T_world_sensors[0], poses.T_world_sensors[1], rgba,
                 ray_features_density_grd, hit_distance, ray_hit_distance_grd, ctx.physical_tile_token)
-            g_pos, g_dns, g_rot, g_scl, g_intrinsic, g_factor, g_inverse, _g_pad = torch.split(
-                grad_density, list(PACKED_SPLIT), dim=1)
-            return (None, None, None, None, None, None, None,
-                    g_pos.contiguous(), g_rot.contiguous(), g_scl.contiguous(), g_dns.contiguous(),
-                    g_intrinsic.contiguous(), g_factor.reshape(-1, 3, 3), g_inverse.reshape(-1, 3, 3),
-                    grad_features.contiguous(), None, None, None)
+            g_pos, g_dns, g_rot, g_scl, g_intrinsic, g_factor, g_inverse = _unpack_rows(grad_density)
+            return (None, None, None, None, None, None, None, g_pos, g_rot, g_scl, g_dns, g_intrinsic, g_factor,
+                    g_inverse, grad_features.contiguous(), None, None, None)
 
     def __init__(self, conf):
         self.device = "cuda"
@@ -129,6 +125,7 @@ class Tracer:
         self.tracer_wrapper = SplatRaster(_plain(conf))
         self._physical_tile_binding_cache: dict = {}
         self._physical_tile_registration_cache: set = set()
+        self._pending_shape = None
 
     def _physical_tile_token(self, wrapper, gpu_batch, rays) -> str:
         """The tile mask of the batch's calibrated domain, registered once per camera."""
@@ -159,7 +156,8 @@ class Tracer:
             rotation, raw_density, physical_scale = rotation.detach(), raw_density.detach(), physical_scale.detach()
         shape = build_intrinsic_view_shape(physical_scale, rotation, raw_density, gaussians.positions.detach(),
                                            gpu_batch, pixel_footprint_variance=self._pixel_footprint_variance,
-                                           frame_id=frame_id)
+                                           frame_id=frame_id, defer_check=True)
+        self._pending_shape = shape
         return rotation, physical_scale, shape.density, raw_density, shape.factor, shape.inverse_factor
 
     @property
@@ -183,6 +181,9 @@ class Tracer:
             rays_d.contiguous(), gaussians.positions.contiguous(), rot.contiguous(), scale.contiguous(),
             dens.contiguous(), intrinsic_dens.contiguous(), factor.contiguous(), inverse_factor.contiguous(),
             gaussians.get_features().contiguous(), sensor, poses, confidence)
+        # the trace has synchronised its stream, so the shape's status words are on the host
+        shape, self._pending_shape = self._pending_shape, None
+        shape.check()
         f = gaussians.ray_feature_dim
         timings = self.tracer_wrapper.collect_times()
         return {
@@ -254,6 +255,38 @@ class SceneGaussians:
 
     def get_features(self):
         return self.features
+
+
+def _pack_rows(pos, dns, rot, scl, idns, factor, inverse):
+    """The [N,32] particle rows (reference tracer.py:171-179): one sm_100a
+    kernel for CUDA tensors, a concatenation for host tensors."""
+    n = pos.shape[0]
+    parts = [t.detach().float().contiguous() for t in (pos, dns, rot, scl, idns, factor, inverse)]
+    if not pos.is_cuda:
+        return torch.cat([parts[0], parts[1].reshape(n, 1), parts[2], parts[3], parts[4].reshape(n, 1),
+                          parts[5].reshape(n, 9), parts[6].reshape(n, 9), pos.new_zeros((n, 2))], dim=1)
+    rows = torch.empty((n, 32), dtype=torch.float32, device=pos.device)
+    _native.check(_native.load().gf_pack_particle_rows(*(t.data_ptr() for t in parts), n, rows.data_ptr(),
+                                                       torch.cuda.current_stream(pos.device).cuda_stream),
+                  "pack particle rows")
+    return rows
+
+
+def _unpack_rows(grad):
+    """Per-slot gradients of the [N,32] row gradient (reference tracer.py:334-343):
+    position [N,3], view density [N,1], rotation [N,4], scale [N,3],
+    intrinsic density [N,1], factor [N,3,3], inverse factor [N,3,3]."""
+    n = grad.shape[0]
+    if not grad.is_cuda:
+        g_pos, g_dns, g_rot, g_scl, g_idns, g_factor, g_inverse, _pad = torch.split(grad, list(PACKED_SPLIT), dim=1)
+        return (g_pos.contiguous(), g_dns.contiguous(), g_rot.contiguous(), g_scl.contiguous(), g_idns.contiguous(),
+                g_factor.reshape(-1, 3, 3), g_inverse.reshape(-1, 3, 3))
+    out = [grad.new_empty(shape) for shape in ((n, 3), (n, 1), (n, 4), (n, 3), (n, 1), (n, 3, 3), (n, 3, 3))]
+    _native.check(_native.load().gf_unpack_particle_rows(grad.contiguous().data_ptr(), n,
+                                                         *(t.data_ptr() for t in out),
+                                                         torch.cuda.current_stream(grad.device).cuda_stream),
+                  "unpack particle rows")
+    return tuple(out)
 
 
 def _plain(conf):

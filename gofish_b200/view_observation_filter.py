@@ -118,14 +118,16 @@ def current_view_q6(positions: torch.Tensor, gpu_batch: Any, pixel_variance: flo
 
 
 def build_intrinsic_view_shape(scales, quaternion, density, positions, gpu_batch, *,
-                               pixel_footprint_variance: float = FILTER_VARIANCE_PIXELS, frame_id=None):
-    """C = Sigma + Q_v, its factors and the m-compensated density of one view."""
+                               pixel_footprint_variance: float = FILTER_VARIANCE_PIXELS, frame_id=None,
+                               defer_check: bool = False):
+    """C = Sigma + Q_v, its factors and the m-compensated density of one view
+    (``defer_check``: see build_full_shape)."""
     from .footprint_shape_operator import build_full_shape
 
     del frame_id
     q6, jacobian, observed = current_view_q6(positions, gpu_batch, pixel_footprint_variance)
     return build_full_shape(scales, quaternion, density, q6, jacobian, observed, mass_preserving=True,
-                            pixel_variance=pixel_footprint_variance)
+                            pixel_variance=pixel_footprint_variance, defer_check=defer_check)
 
 
 __all__ = ["FILTER_VARIANCE_PIXELS", "footprint_covariance", "mass_preserving_factor", "build_intrinsic_view_shape",

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 1
+#define GF_ABI_VERSION 2
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -72,6 +72,9 @@ typedef struct gf_tracer_config {
     int32_t sort_key;          /* GF_KEY_* */
     int32_t enable_hit_counts; /* 1: write the per-pixel hit count */
     int32_t admission_fallback; /* GF_FALLBACK_*: admission of particles without a valid projection */
+    int32_t composite_log_capacity; /* entries per pixel of the training forward's composite log, read by the
+                                       backward: 0 = default (128), < 0 = no log (the backward replays every
+                                       tile through the k-buffer) */
 } gf_tracer_config;
 
 /* render.gofish.fast_admission_fallback (setup_3dgut.py:232-239): "none"
@@ -124,7 +127,7 @@ typedef struct gf_trace_stats {
     uint32_t num_tiles;
     uint32_t num_particles;
     uint32_t kernel_launches;   /* kernels launched by the last trace/trace_bwd call */
-    uint32_t reserved;
+    uint32_t fallback_particles; /* particles without a UT footprint handed to the cone admission */
     uint64_t total_kernel_launches; /* kernels launched by this tracer since its creation */
 } gf_trace_stats;
 
@@ -391,6 +394,22 @@ int gf_full_shape_bwd(const float* scales, const float* quaternions, const float
 int gf_view_shape_packed(const float* positions, const float* quaternions, const float* scales,
                          const float* density, int64_t n, const gf_shape_camera* camera, double gamma, int mode,
                          float* packed, int32_t* status, void* stream);
+
+/* The training renderer's packed [N,32] particle rows from the model's
+ * per-slot tensors: position [N,3], view density [N], rotation [N,4],
+ * intrinsic scale [N,3], intrinsic density [N], factor B [N,9] and B^-1
+ * [N,9], padding words zero.  Replaces the torch.concat of
+ * threedgut_tracer/tracer.py:171-179.  rows must be 16-byte aligned. */
+int gf_pack_particle_rows(const float* positions, const float* density, const float* rotations,
+                          const float* scales, const float* intrinsic_density, const float* factor,
+                          const float* inverse_factor, int64_t n, float* rows, void* stream);
+
+/* The [N,32] row gradient split back into the per-slot gradients (same
+ * layout as gf_pack_particle_rows; padding dropped).  Replaces the
+ * torch.split of threedgut_tracer/tracer.py:334-343. */
+int gf_unpack_particle_rows(const float* rows, int64_t n, float* positions, float* density, float* rotations,
+                            float* scales, float* intrinsic_density, float* factor, float* inverse_factor,
+                            void* stream);
 
 #ifdef __cplusplus
 }

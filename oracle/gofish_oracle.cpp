@@ -410,6 +410,7 @@ struct Tree {
     std::vector<std::vector<Node>> level;
     std::vector<Node> second;                // the leaves' second cones
     std::vector<std::vector<float3_>> sums;  // per node: sum of its unit pixel rays
+    float3_ optical;                         // the camera's optical axis in world coordinates (not normalised)
 };
 
 inline float3_ matvec_plain(const float* m, float3_ v) { return matvec(m, v); }
@@ -526,12 +527,14 @@ inline bool bound_cone(float3_ a, const Node& c, float& cphi) {
 }
 
 // Parent cone at level l: ray sum = the sum of the 4x4 children's ray sums in
-// row-major order, axis = that sum normalised (the mean direction of the
-// pixel rays under the node), empty when every child is; cos phi = the
-// smallest, over the non-empty cones of the leaves under the
-// node, of cos(angle(axis, a) + phi_a) = (axis . a) cos phi_a - |axis x a|
-// sin phi_a, less kEps; a cone reaching past pi makes the node cover the
-// sphere (cos -1, sin 0).
+// row-major order; empty when every child is.  Two axes are bounded: the
+// normalised ray sum (the mean direction of the pixel rays under the node)
+// and the camera's optical axis.  For each, cos phi = the smallest, over the
+// non-empty cones of the leaves under the node, of cos(angle(axis, a) +
+// phi_a) = (axis . a) cos phi_a - |axis x a| sin phi_a, or the whole sphere
+// once a cone reaches past pi.  The node keeps the axis with the larger
+// cos phi (the mean on ties), less kEps; a node whose both bounds cover the
+// sphere gets (cos -1, sin 0).
 Node parent_cone(const Tree& t, int l, int px, int py, float3_& sum) {
     const std::vector<Node>& ch = t.level[size_t(l) - 1];
     const std::vector<float3_>& cs = t.sums[size_t(l) - 1];
@@ -546,27 +549,37 @@ Node parent_cone(const Tree& t, int l, int px, int py, float3_& sum) {
             sum = add(sum, cs[k]);
             if (ch[k].c <= 1.5f || (l == 1 && t.second[k].c <= 1.5f)) any = true;
         }
-    if (!any) return Node{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};
     const float sn = sqrtf(dot(sum, sum));
-    if (!(sn > 0.0f) || !gf::isfinite_f(sn)) return Node{0.0f, 0.0f, 1.0f, -1.0f, 0.0f};
-    const float3_ a = f3(sum.x / sn, sum.y / sn, sum.z / sn);
+    const bool meanOk = sn > 0.0f && gf::isfinite_f(sn);
+    const float3_ am = meanOk ? f3(sum.x / sn, sum.y / sn, sum.z / sn) : f3(0.0f, 0.0f, 1.0f);
+    if (!any) return Node{am.x, am.y, am.z, 2.0f, 0.0f};
+    const float on = sqrtf(dot(t.optical, t.optical));
+    const bool optOk = on > 0.0f && gf::isfinite_f(on);
+    const float3_ ao = optOk ? f3(t.optical.x / on, t.optical.y / on, t.optical.z / on) : f3(0.0f, 0.0f, 1.0f);
     int span = 1;
     for (int k = 0; k < l; ++k) span *= kFan;
     const int gx0 = t.gx[0], gy0 = t.gy[0];
     const int x0 = px * span, y0 = py * span, x1 = std::min(gx0, x0 + span), y1 = std::min(gy0, y0 + span);
-    float cphi = 1.0f;
+    float mm = 1.0f, mo = 1.0f;
+    bool fm = !meanOk, fo = !optOk;
     for (int y = y0; y < y1; ++y)
         for (int x = x0; x < x1; ++x) {
             const size_t k = size_t(y) * gx0 + x;
-            if (!bound_cone(a, t.level[0][k], cphi) || !bound_cone(a, t.second[k], cphi))
-                return Node{a.x, a.y, a.z, -1.0f, 0.0f};
+            if (!bound_cone(am, t.level[0][k], mm) || !bound_cone(am, t.second[k], mm)) fm = true;
+            if (!bound_cone(ao, t.level[0][k], mo) || !bound_cone(ao, t.second[k], mo)) fo = true;
         }
-    cphi = gf::max_f(-1.0f, cphi - kEps);
+    const float vm = fm ? -2.0f : mm, vo = fo ? -2.0f : mo;
+    const bool useOptical = vo > vm;
+    const float3_ a = useOptical ? ao : am;
+    const float best = useOptical ? vo : vm;
+    if (best < -1.5f) return Node{a.x, a.y, a.z, -1.0f, 0.0f};
+    const float cphi = gf::max_f(-1.0f, best - kEps);
     return Node{a.x, a.y, a.z, cphi, sqrtf(gf::max_f(0.0f, 1.0f - cphi * cphi))};
 }
 
 Tree build(const OracleCamera& cam, const OraclePose& pose, const uint8_t* mask, const float* rayD) {
     Tree t;
+    t.optical = f3(pose.Rinv[2], pose.Rinv[5], pose.Rinv[8]);
     const int W = cam.width, H = cam.height;
     int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
     const Node empty{0.0f, 0.0f, 1.0f, 2.0f, 0.0f};

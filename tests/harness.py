@@ -80,7 +80,7 @@ def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
 class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
-    def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True):
+    def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0):
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -88,7 +88,7 @@ class GpuTracer:
         self.torch = torch
         self.case = case
         self.device = device
-        conf = {"render": {"splat": {"k_buffer_size": k},
+        conf = {"render": {"splat": {"k_buffer_size": k, "composite_log_capacity": log_capacity},
                            "gofish": {"fast_global_depth_key": key_mode == 1,
                                       "fast_admission_fallback": "cone" if fallback else "none"},
                            "enable_hitcounts": True}}

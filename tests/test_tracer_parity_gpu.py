@@ -189,3 +189,93 @@ def test_horizon_particles_cone_fallback(cuda_device, fallback):
     gp, gs = gpu.backward(g_rgba, g_hit)
     assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
     assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2
+
+
+def _inside_cloud_case(size: int, seed: int = 61):
+    """A camera inside the Gaussian shell (on a 2 m ring, looking outward) with
+    extra large Gaussians within 0.6 m of it: many particles without a UT
+    footprint, wide fallback caps and spheres holding the camera."""
+    import math
+
+    from gofish_b200.camera import fisheye_camera, random_kb_coefficients
+    from gofish_b200.scene import Scene, look_outward_pose, random_scene
+
+    base = random_scene(40_000, 3, seed)
+    rng = np.random.default_rng(seed + 1)
+    center = np.array([2.0, 0.0, 0.0])
+    m = 400
+    d = rng.standard_normal((m, 3))
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    near = (center + d * (0.05 + 0.55 * rng.random((m, 1)))).astype(np.float32)
+    scales = np.exp(rng.normal(math.log(0.08), 0.6, size=(m, 3))).astype(np.float32)
+    q = rng.standard_normal((m, 4))
+    scene = Scene(np.concatenate([base.positions, near]), np.concatenate([base.rotations,
+                                                                           (q / np.linalg.norm(q, axis=1,
+                                                                                               keepdims=True)).astype(
+                                                                               np.float32)]),
+                  np.concatenate([base.scales, scales]),
+                  np.concatenate([base.density, rng.uniform(0.05, 0.95, (m, 1)).astype(np.float32)]),
+                  np.concatenate([base.features, base.features[:m]]), 3)
+    cam = fisheye_camera(size, size, 200.0, random_kb_coefficients(rng, 200.0))
+    return harness.make_case(scene, cam, look_outward_pose(center, 0.3))
+
+
+def test_camera_inside_the_cloud_parity(cuda_device):
+    """400x400: a 4-level tile cone tree, full trace, forward and backward."""
+    case = _inside_cloud_case(400)
+    ref = harness.oracle_forward(case, 16, 0)
+    no_footprint = (ref["proj"][:, 6] <= 0.0) & (ref["counts"] > 0)
+    retained = int(case.tmask.sum())
+    assert int(no_footprint.sum()) >= 50
+    assert int((ref["counts"][no_footprint] >= retained).sum()) >= 1  # a sphere holding the camera
+    assert int(((ref["counts"] > retained // 4) & (ref["counts"] < retained) & no_footprint).sum()) >= 1
+    gpu = harness.GpuTracer(case, 16, 0, cuda_device)
+    got = gpu.forward()
+    _compare_forward(ref, got)
+    rng = np.random.default_rng(8)
+    g_rgba = rng.standard_normal(ref["rgba"].shape).astype(np.float32)
+    g_hit = np.zeros(ref["hit_t"].shape, np.float32)
+    gp_ref, gs_ref, _ = harness.oracle_backward(case, ref, 16, g_rgba, g_hit)
+    gp, gs = gpu.backward(g_rgba, g_hit)
+    assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
+    assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2
+
+
+def test_camera_inside_the_cloud_binning_5_levels(cuda_device):
+    """1040x1040: a 5-level tree (65x65 tiles); projection, keys, ids and ranges."""
+    import oracle
+
+    case = _inside_cloud_case(1040, seed=62)
+    pose = oracle.prepare_pose(case.pose)
+    proj, rgb, counts = oracle.project(case.ocam, pose, case.particles, case.features, 3, case.tmask, case.ray_d)
+    tr = oracle.tile_rays(case.ocam, pose, case.ray_o, case.ray_d)
+    keys, ids, ranges = oracle.bin(case.ocam, pose, case.particles, proj, counts, case.tmask, tr, 0, case.ray_d)
+    gpu = harness.GpuTracer(case, 16, 0, cuda_device)
+    got = gpu.forward()
+    np.testing.assert_array_equal(got["counts"].astype(np.uint32), counts)
+    np.testing.assert_array_equal(got["keys"].view(np.uint64), keys)
+    np.testing.assert_array_equal(got["ids"].view(np.uint32), ids)
+    np.testing.assert_array_equal(got["ranges"].view(np.uint32), ranges)
+    assert int(((proj[:, 6] <= 0.0) & (counts > 0)).sum()) >= 50
+
+
+@pytest.mark.parametrize("k", [0, 16])
+@pytest.mark.parametrize("log_capacity", [-1, 6, 0])
+def test_backward_paths_agree(cuda_device, k, log_capacity):
+    """The backward from the composite log (default capacity), the k-buffer
+    replay (no log) and their mix (a 6-entry log: most tiles overflow and are
+    replayed) give the oracle's gradients; the forward is unchanged."""
+    case = harness.small_case(seed=17, n=20_000, size=256)
+    ref = harness.oracle_forward(case, k, 0)
+    gpu = harness.GpuTracer(case, k, 0, cuda_device, log_capacity=log_capacity)
+    got = gpu.forward()
+    _compare_forward(ref, got)
+    if log_capacity == 6:
+        assert int((ref["hit_count"] > 6).sum()) > 0 and int((ref["hit_count"] <= 6).sum()) > 0
+    rng = np.random.default_rng(19)
+    g_rgba = rng.standard_normal(ref["rgba"].shape).astype(np.float32)
+    g_hit = (0.1 * rng.standard_normal(ref["hit_t"].shape)).astype(np.float32)
+    gp_ref, gs_ref, _ = harness.oracle_backward(case, ref, k, g_rgba, g_hit)
+    gp, gs = gpu.backward(g_rgba, g_hit)
+    assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
+    assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2

@@ -140,3 +140,19 @@ def test_gradients_match_the_oracle_chain(view, cuda_device):
 def test_geometric_losses_are_refused():
     with pytest.raises(NotImplementedError, match="lambda_dnc"):
         Tracer({"render": {}, "loss": {"lambda_dnc": 0.05}})
+
+
+def test_shape_failure_is_raised_by_render(view, cuda_device):
+    """A row whose full shape is not positive definite raises
+    FootprintNumericalError with its global row from the same render call,
+    although the status words are read only after the trace."""
+    from gofish_b200.footprint_shape_operator import FootprintNumericalError
+
+    scene, cam, batch, valid = view
+    model = SceneGaussians.from_scene(scene, cuda_device, requires_grad=False)
+    _q6, _jac, obs = current_view_q6(model.positions, batch, GAMMA)
+    row = int(torch.nonzero(obs).reshape(-1)[11])
+    model.scale[row] = 0.0  # C = Q_v has rank 2
+    with pytest.raises(FootprintNumericalError) as err:
+        Tracer(_conf()).render(model, batch, train=True)
+    assert err.value.global_row == row

@@ -126,7 +126,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -137,6 +137,15 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_ready(self, timeout_s: float = 10.0) -> None:
+        """Waits for the first sample, so that nvidia-smi's start-up (which
+        holds the driver) falls before the timed region; the statistics keep
+        the last sample before the region and every one inside it."""
+        end = time.time() + timeout_s
+        while self.proc is not None and not self.lines and time.time() < end:
+            time.sleep(0.02)
+        del self.lines[:-1]
 
     def stop(self) -> dict | None:
         if self.proc is None:
@@ -275,12 +284,12 @@ def run_gpu(args):
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
     launches_before = int(raster.stats().total_kernel_launches)
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.wait_ready()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -471,12 +480,12 @@ def run_mesh(args):
     stats0 = raster.stats()
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.wait_ready()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
@@ -753,12 +762,12 @@ def run_inference(args):
     raster.enable_stage_timing(True)
     launches_before = int(raster.stats().total_kernel_launches)
     inter = []
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.wait_ready()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)

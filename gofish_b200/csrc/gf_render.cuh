@@ -26,15 +26,16 @@
 
 namespace gf {
 
-// Composite log of a training forward: for every pixel, the ids of the
-// particles in the order the k-buffer composited them, so that the backward
+// Composite log of a training forward: for every pixel, the candidates the
+// k-buffer composited, in order, as positions in the tile's sorted candidate
+// list (relative to the tile's range start), so that the backward
 // re-evaluates only the composited hits instead of replaying every candidate
 // through the k-buffer.  Entry i of the pixel at thread p of tile t is
 // ids[(i * tiles + t) * kTileThreads + p] (coalesced across a warp).  A pixel
 // that composites more than `capacity` hits marks its tile in `overflow`; the
 // backward replays such tiles.  ids == nullptr: no log (inference).
 struct CompositeLog {
-    uint32_t* ids;       // [capacity][tiles][kTileThreads]
+    uint32_t* ids;       // [capacity][tiles][kTileThreads] candidate positions within the tile
     uint32_t* count;     // [tiles][kTileThreads] entries logged, at most capacity
     uint32_t* overflow;  // [tiles] 1 when a pixel of the tile exceeded the capacity
     uint32_t capacity;
@@ -113,12 +114,27 @@ __device__ __forceinline__ V3 binv_times(const float4& b, const float4& c, const
 
 // Hit test of one candidate with a given canonical ray origin `gro`
 // (reference gaussianParticles.slang:293-338; identical arithmetic to half_ray).
+//
+// With `pretest`, `miss` = A - (G + 1e-5 A) rounded, where A = |gro|^2 and G
+// = min(9.001, 2 ln(255 rho) + 1e-3) is the squared canonical distance
+// beyond which the hit test cannot pass (response below the 0.0113 cut-off,
+// or alpha below 1/255).  The candidate is rejected before the division when
+// denom * miss > num^2, i.e. when the squared distance of the ray's line to
+// the centre, A - num^2/denom, exceeds G.  With unit roundoff u the rounding
+// of A, denom, num and the products changes that quantity by less than 15u A,
+// inside the 1e-5 A margin, and the squared distance the full test computes
+// at the clamped closest point is at least (1 - 6u) times the line's (the
+// point is one FMA per coordinate); G carries the 1e-3 margin against the
+// rounding of exp and of the alpha product.  So a rejected candidate always
+// fails the full test: the outputs do not change.
 __device__ __forceinline__ bool hit_with_origin(const Ray& ray, V3 gro, const float4& b, const float4& c,
-                                                const float4& d, float density, float& alpha, float& hitT) {
+                                                const float4& d, float density, float& alpha, float& hitT,
+                                                bool pretest = false, float miss = 0.0f) {
     const V3 grdu = binv_times(b, c, d, ray.d);
     const float denom = fdot3(grdu, grdu);
     if (!(denom > 0.0f && isfinite_f(denom) && isfinite_f(ray.tmin) && ray.tmax > ray.tmin)) return false;
     const float num = fdot3(gro, grdu);
+    if (pretest && __fmul_rn(denom, miss) > __fmul_rn(num, num)) return false;
     const float tauLine = -num / denom;
     const float tau = fminf(fmaxf(tauLine, ray.tmin), ray.tmax);
     const V3 p = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y), __fmaf_rn(tau, grdu.z, gro.z));
@@ -325,7 +341,18 @@ __device__ __forceinline__ uint32_t warp_mask(const TileSetup& ts, const Staged*
 
 __device__ __forceinline__ uint32_t idxOf(const RenderArgs& a, uint32_t sIdx) { return __ldg(a.sortedIds + sIdx); }
 
-// Stages candidate sIdx into shared memory (thread-private slot).
+// Squared canonical distance beyond which a particle of density rho cannot
+// pass the hit test, with margin (see hit_with_origin): min(9.001,
+// 2 ln(255 rho) + 1e-3); -1 for rho <= 0 (never a hit).
+__device__ __forceinline__ float miss_distance2(float density) {
+    if (!(density > 0.0f)) return -1.0f;
+    return fminf(9.001f, __fadd_rn(__fmul_rn(2.0f, gf_logf(__fmul_rn(255.0f, density))), 1e-3f));
+}
+
+// Stages candidate sIdx into shared memory (thread-private slot).  The
+// forward (kFwd) of a central tile does not read the position again and
+// keeps there the pre-test threshold of hit_with_origin.
+template <bool kFwd = false>
 __device__ __forceinline__ void stage(const RenderArgs& a, const TileSetup& ts, uint32_t sIdx, Staged& out) {
     const Record q = load_record(a.records, idxOf(a, sIdx));
     out.a = q.a;
@@ -334,6 +361,10 @@ __device__ __forceinline__ void stage(const RenderArgs& a, const TileSetup& ts, 
     out.d = q.d;
     if (ts.central) {
         const V3 gro = binv_times(q.b, q.c, q.d, v3(ts.origin.x - q.a.x, ts.origin.y - q.a.y, ts.origin.z - q.a.z));
+        if constexpr (kFwd) {
+            const float A = fdot3(gro, gro);
+            out.a.x = __fsub_rn(A, __fadd_rn(miss_distance2(q.a.w), __fmul_rn(1e-5f, A)));
+        }
         const V3 v = v3(q.a.x - ts.origin.x, q.a.y - ts.origin.y, q.a.z - ts.origin.z);
         const float dist = sqrtf(dot3(v, v));
         const float radius = __ldg(a.bounds + idxOf(a, sIdx));
@@ -349,13 +380,12 @@ __device__ __forceinline__ void stage(const RenderArgs& a, const TileSetup& ts, 
     }
 }
 
+template <bool kFwd = false>
 __device__ __forceinline__ bool hit_staged(const TileSetup& ts, const Staged& q, float& alpha, float& ht) {
-    V3 gro;
     if (ts.central) {
-        gro = v3(q.g.x, q.g.y, q.g.z);
-    } else {
-        gro = binv_times(q.b, q.c, q.d, v3(ts.ray.o.x - q.a.x, ts.ray.o.y - q.a.y, ts.ray.o.z - q.a.z));
+        return hit_with_origin(ts.ray, v3(q.g.x, q.g.y, q.g.z), q.b, q.c, q.d, q.a.w, alpha, ht, kFwd, q.a.x);
     }
+    const V3 gro = binv_times(q.b, q.c, q.d, v3(ts.ray.o.x - q.a.x, ts.ray.o.y - q.a.y, ts.ray.o.z - q.a.z));
     return hit_with_origin(ts.ray, gro, q.b, q.c, q.d, q.a.w, alpha, ht);
 }
 
@@ -399,17 +429,11 @@ __device__ __forceinline__ float4 color_at(const RenderArgs& a, const Batch& b, 
     return __ldg(a.records + 4 * size_t(__ldg(a.sortedIds + sp)) + 3);
 }
 
-__device__ __forceinline__ uint32_t id_at(const RenderArgs& a, const Batch& b, uint32_t sp) {
-    const uint32_t j = sp - b.base;
-    if (j < b.cnt) return b.ids[j];
-    return __ldg(a.sortedIds + sp);
-}
-
-// Appends one composited particle to the pixel's log (entries past the
-// capacity are counted, not stored).
-__device__ __forceinline__ void log_composite(const CompositeLog& lg, uint32_t tile, uint32_t& n, uint32_t id) {
+// Appends one composited candidate (its position in the tile's list) to the
+// pixel's log; entries past the capacity are counted, not stored.
+__device__ __forceinline__ void log_composite(const CompositeLog& lg, uint32_t tile, uint32_t& n, uint32_t local) {
     if (lg.ids == nullptr) return;
-    if (n < lg.capacity) lg.ids[(size_t(n) * lg.tiles + tile) * kTileThreads + threadIdx.x] = id;
+    if (n < lg.capacity) lg.ids[(size_t(n) * lg.tiles + tile) * kTileThreads + threadIdx.x] = local;
     ++n;
 }
 
@@ -459,7 +483,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
             const uint32_t sIdx = base + threadIdx.x;
             if (sIdx < range.y) {
                 sId[threadIdx.x] = __ldg(a.sortedIds + sIdx);
-                stage(a, ts, sIdx, sRec[threadIdx.x]);
+                stage<true>(a, ts, sIdx, sRec[threadIdx.x]);
             }
             __syncthreads();
             const int cnt = min(uint32_t(kBatch), range.y - base);
@@ -473,16 +497,16 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                     const int j = k * 32 + __ffs(m) - 1;
                     m &= m - 1u;
                     float alpha, ht;
-                    if (hit_staged(ts, sRec[j], alpha, ht)) {
+                    if (hit_staged<true>(ts, sRec[j], alpha, ht)) {
                         if constexpr (K == 0) {
-                            log_composite(a.log, uint32_t(ts.tile), nlog, sId[j]);
+                            log_composite(a.log, uint32_t(ts.tile), nlog, base + uint32_t(j) - range.x);
                             composite_fwd(s, ht, alpha, sRec[j].d);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
                                 uint32_t s0;
                                 kb.pop_front(t0, a0, s0);
-                                log_composite(a.log, uint32_t(ts.tile), nlog, id_at(a, bt, s0));
+                                log_composite(a.log, uint32_t(ts.tile), nlog, s0 - range.x);
                                 composite_fwd(s, t0, a0, color_at(a, bt, s0));
                             }
                             kb.insert(ht, alpha, base + uint32_t(j));
@@ -496,7 +520,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                 float ht, ha;
                 uint32_t sp;
                 kb.entry(i, ht, ha, sp);
-                log_composite(a.log, uint32_t(ts.tile), nlog, id_at(a, bt, sp));
+                log_composite(a.log, uint32_t(ts.tile), nlog, sp - range.x);
                 composite_fwd(s, ht, ha, color_at(a, bt, sp));
             }
         }
@@ -529,25 +553,33 @@ struct PixelBwd {
     bool alive;
 };
 
-// Gradient of one composited hit with closest-point parameter tau and
-// opacity galpha from the hit test (reference processHitBwd,
-// gaussianParticles.cuh:736-1155, geometric channels inactive).  The walking
-// state (T, depth, colour) advances with the forward's exact arithmetic;
-// quotients that only scale gradients use fast reciprocals.
-__device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Record& q, float tau, float galpha,
-                                        float4 g[4]) {
+// Gradient of one composited hit (reference processHitBwd,
+// gaussianParticles.cuh:736-1155, geometric channels inactive).  The hit is
+// evaluated here with the forward hit test's exact arithmetic
+// (hit_with_origin: the same closest point, response and alpha, so the same
+// tau and alpha the forward composited) and back-propagated in the same
+// pass.  The walking state (T, depth, colour) advances with the forward's
+// exact arithmetic; quotients that only scale gradients use fast
+// reciprocals.  Returns false (state unchanged) when the candidate is not a
+// hit, which a composited entry always is.
+__device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Record& q, float4 g[4]) {
     const V3 gp = v3(ray.o.x - q.a.x, ray.o.y - q.a.y, ray.o.z - q.a.z);
     const V3 gro = binv_times(q.b, q.c, q.d, gp);
     const V3 grdu = binv_times(q.b, q.c, q.d, ray.d);
     const float denom = fdot3(grdu, grdu);
+    if (!(denom > 0.0f && isfinite_f(denom) && isfinite_f(ray.tmin) && ray.tmax > ray.tmin)) return false;
     const float num = fdot3(gro, grdu);
-    const bool interior = tau > ray.tmin && tau < ray.tmax;
+    const float tauLine = -num / denom;
+    const float tau = fminf(fmaxf(tauLine, ray.tmin), ray.tmax);
     const V3 p = v3(__fmaf_rn(tau, grdu.x, gro.x), __fmaf_rn(tau, grdu.y, gro.y), __fmaf_rn(tau, grdu.z, gro.z));
     const float grayDist = fdot3(p, p);
+    if (grayDist > kResponseCutoff2) return false;
     const float gres = gf_expf(-0.5f * grayDist);
     const float density = q.a.w;
     const float galphaU = gres * density;
-    if (!(gres > kMinKernelResponse && galpha > kAlphaThreshold)) return false;
+    const float galpha = fminf(kMaxAlpha, galphaU);
+    if (!(gres > kMinKernelResponse && galpha > kAlphaThreshold && tau >= ray.tmin && tau <= ray.tmax)) return false;
+    const bool interior = tau > ray.tmin && tau < ray.tmax;
     const float gdist = tau;
     const float weight = galpha * s.T;
     const float nextT = (1.0f - galpha) * s.T;
@@ -708,14 +740,14 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
                     if (hit_staged(ts, sRec[j], alpha, ht)) {
                         if constexpr (K == 0) {
                             const Record q = record_at(a.r, bt, base + uint32_t(j), cid);
-                            have = hit_vjp(s, ray, q, ht, alpha, g);
+                            have = hit_vjp(s, ray, q, g);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
                                 uint32_t s0;
                                 kb.pop_front(t0, a0, s0);
                                 const Record q = record_at(a.r, bt, s0, cid);
-                                have = hit_vjp(s, ray, q, t0, a0, g);
+                                have = hit_vjp(s, ray, q, g);
                             }
                             kb.insert(ht, alpha, base + uint32_t(j));
                         }
@@ -737,7 +769,7 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
                 uint32_t sp;
                 kb.entry(i, ht, ha, sp);
                 const Record q = record_at(a.r, bt, sp, cid);
-                have = hit_vjp(s, ray, q, ht, ha, g);
+                have = hit_vjp(s, ray, q, g);
                 if (s.T < kMinTransmittance) s.alive = false;
             }
             accumulate_grad(a.gradRecords, have, cid, g);
@@ -745,18 +777,49 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
     }
 }
 
-// Backward from the composite log: each pixel re-evaluates only the hits the
+// Backward from the composite log.  Each pixel re-evaluates only the hits the
 // forward composited, in the logged order, with the forward's arithmetic
 // (the canonical origin B^-1 (o - mu) of a central tile equals the per-pixel
 // one bit for bit), and back-propagates them exactly as the replay does.
-// Tiles whose log overflowed are left to k_render_bwd.  The loop runs to the
-// warp's longest log so that the gradient reduction can use full-warp
-// shuffles.
-__global__ __launch_bounds__(kTileThreads) void k_render_bwd_log(RenderBwdArgs a) {
+// The render records of the tile's first kBwdSlots candidates (read by every
+// pixel that composites them) are staged in shared memory, one array per
+// float4 of the record so that lanes reading different candidates spread
+// over the banks; later candidates are read from global memory.  The next log
+// entry is loaded one step ahead.  Gradients go to the particles' records
+// with vector atomics (warp-reduced when every lane holds the same
+// particle): neighbouring pixels often composite the same particle in the
+// same step, and shared-memory atomics on one address serialise.  Tiles whose
+// log overflowed are left to k_render_bwd.  The loop runs to the warp's
+// longest log so that the gradient reduction can use full-warp shuffles.
+constexpr int kBwdSlots = 512;
+
+__host__ __device__ constexpr size_t bwd_log_smem_bytes() {
+    return size_t(kBwdSlots) * (4 * sizeof(float4) + sizeof(uint32_t));
+}
+
+#ifndef GF_BWD_LOG_MIN_BLOCKS
+#define GF_BWD_LOG_MIN_BLOCKS 3
+#endif
+__global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_bwd_log(RenderBwdArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float4* sRec = reinterpret_cast<float4*>(smem);                                      // [4][kBwdSlots]
+    uint32_t* sIds = reinterpret_cast<uint32_t*>(smem + 4 * sizeof(float4) * kBwdSlots);  // [kBwdSlots]
     const uint32_t tile = blockIdx.x;
     if (a.r.mask[tile] == 0u) return;                    // block-uniform
     const CompositeLog& lg = a.r.log;
     if (lg.overflow[tile] != 0u) return;                 // block-uniform
+    const uint2 range = a.r.ranges[tile];
+    const uint32_t staged = min(range.y - range.x, uint32_t(kBwdSlots));
+    for (uint32_t j = threadIdx.x; j < staged; j += kTileThreads) {
+        const uint32_t id = __ldg(a.r.sortedIds + range.x + j);
+        sIds[j] = id;
+        const Record q = load_record(a.r.records, id);
+        sRec[j] = q.a;
+        sRec[kBwdSlots + j] = q.b;
+        sRec[2 * kBwdSlots + j] = q.c;
+        sRec[3 * kBwdSlots + j] = q.d;
+    }
+    __syncthreads();
     const FrameArgs& f = a.r.f;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int px = int(tile % uint32_t(f.gx)) * kTile + (warp & 1) * 8 + (lane & 7);
@@ -793,19 +856,30 @@ __global__ __launch_bounds__(kTileThreads) void k_render_bwd_log(RenderBwdArgs a
     uint32_t warpN = n;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) warpN = max(warpN, __shfl_xor_sync(0xffffffffu, warpN, o));
-    const uint32_t* ids = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
+    const uint32_t* entries = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
     const size_t stride = size_t(lg.tiles) * kTileThreads;
+    uint32_t next = n > 0 ? __ldg(entries) : 0u;
 #pragma unroll 1
     for (uint32_t i = 0; i < warpN; ++i) {
+        const bool active = i < n && s.alive;
+        const uint32_t local = next;
+        if (i + 1 < n) next = __ldg(entries + (i + 1) * stride);
         bool have = false;
         uint32_t cid = kInvalidParticle;
         float4 g[4] = {};
-        if (i < n && s.alive) {
-            cid = __ldg(ids + i * stride);
-            const Record q = load_record(a.r.records, cid);
-            const V3 gro = binv_times(q.b, q.c, q.d, v3(ray.o.x - q.a.x, ray.o.y - q.a.y, ray.o.z - q.a.z));
-            float alpha, ht;
-            if (hit_with_origin(ray, gro, q.b, q.c, q.d, q.a.w, alpha, ht)) have = hit_vjp(s, ray, q, ht, alpha, g);
+        if (active) {
+            Record q;
+            if (local < staged) {
+                cid = sIds[local];
+                q.a = sRec[local];
+                q.b = sRec[kBwdSlots + local];
+                q.c = sRec[2 * kBwdSlots + local];
+                q.d = sRec[3 * kBwdSlots + local];
+            } else {
+                cid = __ldg(a.r.sortedIds + range.x + local);
+                q = load_record(a.r.records, cid);
+            }
+            have = hit_vjp(s, ray, q, g);
             if (s.T < kMinTransmittance) s.alive = false;
         }
         accumulate_grad(a.gradRecords, have, cid, g);

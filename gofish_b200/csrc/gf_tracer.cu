@@ -536,7 +536,9 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
         StageTimer st(t, GF_STAGE_RENDER_BWD, s);
         if (a.r.log.ids != nullptr) {
             // tiles with a complete log, then the replay of the tiles whose log overflowed
-            gf::k_render_bwd_log<<<T, gf::kTileThreads, 0, s>>>(a);
+            const size_t smem = gf::bwd_log_smem_bytes();
+            cudaFuncSetAttribute(gf::k_render_bwd_log, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            gf::k_render_bwd_log<<<T, gf::kTileThreads, smem, s>>>(a);
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }

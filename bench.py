@@ -211,7 +211,7 @@ def run_gpu(args):
 
     from gofish_b200.batch import Batch
     from gofish_b200.footprint_chunk_planner import plan_footprint_chunks
-    from gofish_b200.multiview import allreduce_gradients
+    from gofish_b200.multiview import GradientBucket
     from gofish_b200.scene import pose_to_c2w
     from gofish_b200.tracer import SceneGaussians, Tracer
 
@@ -237,6 +237,7 @@ def run_gpu(args):
     model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in
                              ("positions", "rotation", "scale", "density", "features")), scene.sh_degree)
     params = model.parameters()
+    bucket = GradientBucket(params) if world > 1 else None  # one all-reduce of the [N,59] gradients
     target = target_host.to(device)
     ray_o = torch.from_numpy(ray_o_np).to(device)
     ray_d = torch.from_numpy(ray_d_np).to(device)
@@ -259,8 +260,11 @@ def run_gpu(args):
         """Forward, L1 loss and backward of every local view through
         Tracer.render (per-view full shape, trace, trace_bwd, shape VJP); the
         model gradients [N,59] summed over the views and all-reduced over ranks."""
-        for p in params:
-            p.grad = None
+        if bucket is not None:
+            bucket.attach()
+        else:
+            for p in params:
+                p.grad = None
         loss_acc.zero_()
         for v, batch in enumerate(batches):
             out = tracer.render(model, batch, train=True, frame_id=v)
@@ -271,7 +275,8 @@ def run_gpu(args):
             loss.backward()
             if want_loss:
                 loss_acc.add_(loss.detach())
-        allreduce_gradients([p.grad for p in params])
+        if bucket is not None:
+            bucket.allreduce()
         return loss_acc if want_loss else None
 
     for _ in range(args.warmup):

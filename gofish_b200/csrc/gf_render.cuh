@@ -38,6 +38,8 @@ struct CompositeLog {
     uint32_t* ids;       // [capacity][tiles][kTileThreads] candidate positions within the tile
     uint32_t* count;     // [tiles][kTileThreads] entries logged, at most capacity
     uint32_t* overflow;  // [tiles] 1 when a pixel of the tile exceeded the capacity
+    uint32_t* overflowList;   // the flagged tiles, in no particular order
+    uint32_t* overflowCount;  // their number (zeroed before the forward)
     uint32_t capacity;
     uint32_t tiles;
 };
@@ -267,11 +269,11 @@ __device__ __forceinline__ float warp_min(float v) {
 }
 
 // Initializes the pixel's ray and decides whether the tile is central (block-uniform).
-__device__ __forceinline__ TileSetup tile_setup(const RenderArgs& a, bool retained) {
+__device__ __forceinline__ TileSetup tile_setup(const RenderArgs& a, bool retained, int tile) {
     __shared__ float sOrigin[3];
     TileSetup ts;
     const FrameArgs& f = a.f;
-    ts.tile = blockIdx.x;
+    ts.tile = tile;
     const int tx = ts.tile % f.gx, ty = ts.tile / f.gx;
     // warp w covers the 8x4 block (w & 1, w >> 1) of the tile; lane -> (lane & 7, lane >> 3)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -470,7 +472,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
     Staged* sRec = reinterpret_cast<Staged*>(smem);
     uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
     const bool retained = a.mask[blockIdx.x] != 0u;
-    const TileSetup ts = tile_setup(a, retained);
+    const TileSetup ts = tile_setup(a, retained, int(blockIdx.x));
     PixelFwd s{1.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0u, ts.ray.valid};
     RingKBuffer<KR> kb;
     kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
@@ -529,7 +531,10 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
         const CompositeLog& lg = a.log;
         lg.count[size_t(ts.tile) * kTileThreads + threadIdx.x] = min(nlog, lg.capacity);
         const int over = __syncthreads_or(nlog > lg.capacity);
-        if (threadIdx.x == 0) lg.overflow[ts.tile] = over ? 1u : 0u;
+        if (threadIdx.x == 0) {
+            lg.overflow[ts.tile] = over ? 1u : 0u;
+            if (over) lg.overflowList[atomicAdd(lg.overflowCount, 1u)] = uint32_t(ts.tile);
+        }
     }
     if (!ts.inImage) return;
     float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -682,15 +687,12 @@ __device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords
 // back-propagated from the final pixel values.  Loops are warp-uniform so
 // the gradient reduction can use full-warp shuffles.
 template <int K>
-__global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a) {
+__device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned char* smem, int tile) {
     constexpr int KR = K > 0 ? K : 1;
-    extern __shared__ __align__(16) unsigned char smem[];
     Staged* sRec = reinterpret_cast<Staged*>(smem);
     uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
-    if (a.r.mask[blockIdx.x] == 0u) return;  // block-uniform
-    // with a composite log only the tiles whose log overflowed are replayed
-    if (a.r.log.ids != nullptr && a.r.log.overflow[blockIdx.x] == 0u) return;
-    const TileSetup ts = tile_setup(a.r, true);
+    if (a.r.mask[tile] == 0u) return;  // block-uniform
+    const TileSetup ts = tile_setup(a.r, true, tile);
     const Ray& ray = ts.ray;
     PixelBwd s;
     s.T = 1.0f;
@@ -774,6 +776,23 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
             }
             accumulate_grad(a.gradRecords, have, cid, g);
         }
+    }
+}
+
+// Backward replay kernel: one block per tile, or, when the forward kept a
+// composite log, a resident grid that walks the list of tiles whose log
+// overflowed (usually empty).
+template <int K>
+__global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    if (a.r.log.ids == nullptr) {
+        replay_tile<K>(a, smem, int(blockIdx.x));
+        return;
+    }
+    const uint32_t count = *a.r.log.overflowCount;
+    for (uint32_t w = blockIdx.x; w < count; w += gridDim.x) {
+        replay_tile<K>(a, smem, int(a.r.log.overflowList[w]));
+        __syncthreads();  // the next tile restages the shared batch
     }
 }
 

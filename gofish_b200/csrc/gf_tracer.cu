@@ -57,7 +57,8 @@ struct gf_tracer {
     DeviceBuffer keys[2], ids[2], hist;
     DeviceBuffer gradRecords;
     DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
-    DeviceBuffer logIds, logCount, logOverflow;           // composite log of the last training forward
+    DeviceBuffer logIds, logCount, logOverflow, logList;  // composite log of the last training forward
+    int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
     gf::CompositeLog frameLog{};
     uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size (low 32 bits)
     uint32_t fallbackParticles = 0;
@@ -179,6 +180,14 @@ void launch_render_bwd(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t 
     const size_t smem = gf::render_smem_bytes(K);
     cudaFuncSetAttribute(gf::k_render_bwd<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     gf::k_render_bwd<K><<<tiles, gf::kTileThreads, smem, stream>>>(a);
+}
+
+// Blocks of the replay grid that walks the overflowed tiles: 3 per SM.
+uint32_t resident_blocks() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148u * 3u;
+    return uint32_t(sms) * 3u;
 }
 
 int dispatch_fwd(int K, const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
@@ -396,9 +405,13 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
         if (int e = t->logIds.ensure(perEntry * cap, stream)) return e;
         if (int e = t->logCount.ensure(perEntry, stream)) return e;
         if (int e = t->logOverflow.ensure(sizeof(uint32_t) * size_t(T), stream)) return e;
+        if (int e = t->logList.ensure(sizeof(uint32_t) * (size_t(T) + 1), stream)) return e;
         a.log.ids = t->logIds.as<uint32_t>();
         a.log.count = t->logCount.as<uint32_t>();
         a.log.overflow = t->logOverflow.as<uint32_t>();
+        a.log.overflowCount = t->logList.as<uint32_t>();
+        a.log.overflowList = t->logList.as<uint32_t>() + 1;
+        GF_CUDA(cudaMemsetAsync(a.log.overflowCount, 0, sizeof(uint32_t), stream));
         a.log.capacity = cap;
         a.log.tiles = T;
     }
@@ -456,7 +469,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
         for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount}) b->release();
-        for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow}) b->release();
+        for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow, &t->logList}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
                                 &t->hist,    &t->gradRecords};
@@ -542,7 +555,9 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }
-        if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, T, s)) return e;
+        if (t->residentBlocks == 0) t->residentBlocks = int(resident_blocks());
+        const uint32_t grid = a.r.log.ids != nullptr ? std::min<uint32_t>(T, uint32_t(t->residentBlocks)) : T;
+        if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, grid, s)) return e;
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();

@@ -66,3 +66,45 @@ def test_shard_views_partitions_the_batch():
         assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         shard_views(8, 2, 2)
+
+
+def _bucket_worker(rank, world, port, out):
+    from gofish_b200.multiview import GradientBucket
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(7)
+        pos = torch.randn(11, 3, generator=g).requires_grad_(True)
+        sh = torch.randn(11, 48, generator=g).requires_grad_(True)
+        bucket = GradientBucket([pos, sh])
+        for step in range(2):
+            bucket.attach()
+            for v in range(2):  # two views per rank, accumulated in the bucket
+                w = float(1 + rank * 2 + v + step)
+                (w * (pos ** 2).sum() + w * sh.sum()).backward()
+            assert pos.grad.data_ptr() == bucket.views[0].data_ptr()
+            bucket.allreduce()
+        out[rank] = (pos.grad.clone(), sh.grad.clone(), pos.detach().clone())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_bucket_single_allreduce_matches_sum():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    out = manager.dict()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    pos = out[0][2]
+    # last step: weights (1 + 2r + v + 1) over ranks r and views v: 2+3+4+5 = 14
+    for r in range(world):
+        torch.testing.assert_close(out[r][0], 14.0 * 2.0 * pos)
+        torch.testing.assert_close(out[r][1], torch.full((11, 48), 14.0))

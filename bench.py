@@ -194,11 +194,11 @@ FWD_RENDER_BYTES_PER_PIXEL = 48                     # rays 24, rgba 16, hit dist
 BWD_RENDER_BYTES_PER_INTERSECTION = 144             # id 4 + particle record 128 + rgb 12
 BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output gradients
 # DRAM bytes per algorithmic byte of the render kernels in one full ncu capture
-# of this workload (k_render_fwd<16>: 167.6 MB for 469.5 MB; k_render_bwd<16>:
-# 262.5 MB for 644.0 MB); the bench line's traffic is the live algorithmic
-# bytes scaled by them.
-FWD_TRAFFIC_PER_ALG_BYTE = 167.6 / 469.5
-BWD_TRAFFIC_PER_ALG_BYTE = 262.5 / 644.0
+# of this workload (k_render_fwd<16>: 872.4 MB for 473.6 MB, the excess being
+# the composite-log write; k_render_bwd_log: 867.8 MB for 649.7 MB, the log
+# read); the bench line's traffic is the live algorithmic bytes scaled by them.
+FWD_TRAFFIC_PER_ALG_BYTE = 872.4 / 473.6
+BWD_TRAFFIC_PER_ALG_BYTE = 867.8 / 649.7
 TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio to the algorithmic bytes"
 # pixel footprint variance of the per-view full shape (render.gofish.pixel_footprint_variance)
 BENCH_GAMMA = 0.3
@@ -370,7 +370,8 @@ def run_gpu(args):
         alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
         traffic = alg * FWD_TRAFFIC_PER_ALG_BYTE
     achieved = alg / avg_s / 1e9
-    roofline = {"kernel": f"k_render_{dominant.split('_')[1]}<{w.k_buffer}>", "bound": "hbm",
+    kernel = "k_render_bwd_log" if dominant == "render_bwd" else f"k_render_fwd<{w.k_buffer}>"
+    roofline = {"kernel": kernel, "bound": "hbm",
                 "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5),
                 "traffic": int(traffic), "traffic_source": TRAFFIC_SOURCE,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",

@@ -43,6 +43,7 @@ class GfTracerConfig(ctypes.Structure):
         ("enable_hit_counts", ctypes.c_int32),
         ("admission_fallback", ctypes.c_int32),
         ("composite_log_capacity", ctypes.c_int32),
+        ("enable_normals", ctypes.c_int32),
     ]
 
 
@@ -71,6 +72,12 @@ class GfTraceOutputs(ctypes.Structure):
         ("hit_distance", ctypes.c_void_p),
         ("hit_count", ctypes.c_void_p),
         ("visibility", ctypes.c_void_p),
+        ("normal", ctypes.c_void_p),
+        ("depth_var", ctypes.c_void_p),
+        ("quant", ctypes.c_void_p),
+        ("extent", ctypes.c_void_p),
+        ("inv_depth", ctypes.c_void_p),
+        ("inv_depth2", ctypes.c_void_p),
     ]
 
 
@@ -82,6 +89,16 @@ class GfTraceGrads(ctypes.Structure):
         ("grad_hit_distance", ctypes.c_void_p),
         ("grad_particles", ctypes.c_void_p),
         ("grad_features", ctypes.c_void_p),
+        ("normal", ctypes.c_void_p),
+        ("grad_normal", ctypes.c_void_p),
+        ("depth_var", ctypes.c_void_p),
+        ("grad_depth_var", ctypes.c_void_p),
+        ("extent", ctypes.c_void_p),
+        ("grad_extent", ctypes.c_void_p),
+        ("inv_depth", ctypes.c_void_p),
+        ("grad_inv_depth", ctypes.c_void_p),
+        ("inv_depth2", ctypes.c_void_p),
+        ("grad_inv_depth2", ctypes.c_void_p),
     ]
 
 
@@ -219,7 +236,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 2:
+    if lib.gf_abi_version() != 3:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

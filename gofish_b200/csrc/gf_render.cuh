@@ -44,6 +44,18 @@ struct CompositeLog {
     uint32_t tiles;
 };
 
+// Geometric training channels (rayPayload.cuh:242-322), written by the
+// forward of a tracer created with enable_normals; any pointer may be NULL.
+struct GeoOut {
+    float* normal;    // [H,W,3]
+    float* depthVar;  // [H,W,1]
+    float* quant;     // [H,W,10]
+    float* extent;    // [H,W,1]
+    float* invD;      // [H,W,1]
+    float* invD2;     // [H,W,1]
+    const float* particles;  // packed [N,32] rows: quaternion (slots 4-7), intrinsic scale (8-10)
+};
+
 struct RenderArgs {
     FrameArgs f;
     const uint8_t* mask;
@@ -54,6 +66,7 @@ struct RenderArgs {
     const float* rayO;
     const float* rayD;
     CompositeLog log;
+    GeoOut geo;
 };
 
 struct RenderBwdArgs {
@@ -454,6 +467,181 @@ __device__ __forceinline__ void composite_fwd(PixelFwd& s, float ht, float ha, f
     if (s.T < kMinTransmittance) s.alive = false;
 }
 
+// ------------------------------------------------------------------ geometric channels
+// Per-hit terms of the training channels, accumulated for every composited
+// hit in composite order (reference processHitParticle,
+// gutKBufferRenderer.cuh:330-392): w = alpha T_before,
+//   normal    += w n,  n = -normalize(B^-T normalize(B^-1 d))
+//                      (canonicalRayNormal, gaussianParticles.slang:254-265)
+//   depth var += (w t) t
+//   extent    += w |s * (R^T d)|   (intrinsic rotation and scale of the row,
+//                      gaussianParticles.cuh:131-141; R from the quaternion)
+//   inv depth += w / max(t s_d, 0.2), inv depth2 += w / max(t s_d, 0.2)^2
+//                      (sofDistortionCoordinate, sensorConstants.cuh:28-42;
+//                      s_d = sensor ray z for a pinhole, 1 for a fisheye)
+//   quantiles: the first hit depth at which 1 - T_after reaches each of
+//              0.05 .. 0.50; max-weight hit depth; the exact 0.5 crossing
+//              (finiteIntervalExactCrossing.cuh:42-109) inside the Gaussian
+//              that carries T across 0.5.
+// Sums use explicit fused multiply-adds; exp, log, division and square root
+// are the shared IEEE/elementary ones, so the oracle reproduces every value.
+constexpr int kQuantiles = 7;
+constexpr int kQuantStride = kQuantiles + 3;
+
+__device__ __forceinline__ float quantile_threshold(int i) {
+    return i == 0 ? 0.05f : i == 1 ? 0.10f : i == 2 ? 0.15f : i == 3 ? 0.20f : i == 4 ? 0.30f : i == 5 ? 0.40f : 0.50f;
+}
+
+struct PixelGeo {
+    float n[3];
+    float sumWD2, sumExt, sumInvD, sumInvD2;
+    float q[kQuantiles];
+    float tauMaxW, tauMaxD, exactDepth, exactRate;
+    float dscale;
+};
+
+__device__ __forceinline__ void geo_init(PixelGeo& g, float dscale) {
+    g.n[0] = g.n[1] = g.n[2] = 0.0f;
+    g.sumWD2 = g.sumExt = g.sumInvD = g.sumInvD2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kQuantiles; ++i) g.q[i] = 0.0f;
+    g.tauMaxW = g.tauMaxD = g.exactDepth = g.exactRate = 0.0f;
+    g.dscale = dscale;
+}
+
+// Along-ray standard deviation of the intrinsic shape: |s * (R^T d)|, with
+// R^T rows from the quaternion (w, x, y, z) as quaternionWXYZToMatrix
+// (gaussianParticles.cuh:55-75).
+__device__ __forceinline__ V3 rotate_transpose(float4 q, V3 d) {
+    const float r = q.x, x = q.y, y = q.z, z = q.w;
+    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z, rx = r * x, ry = r * y,
+                rz = r * z;
+    const V3 r0 = v3(1.0f - 2.0f * (yy + zz), 2.0f * (xy + rz), 2.0f * (xz - ry));
+    const V3 r1 = v3(2.0f * (xy - rz), 1.0f - 2.0f * (xx + zz), 2.0f * (yz + rx));
+    const V3 r2 = v3(2.0f * (xz + ry), 2.0f * (yz - rx), 1.0f - 2.0f * (xx + yy));
+    return v3(fdot3(r0, d), fdot3(r1, d), fdot3(r2, d));
+}
+
+__device__ __forceinline__ float extent_sigma(float4 q, float4 sc, V3 d) {
+    const V3 rd = rotate_transpose(q, d);
+    const V3 sd = v3(sc.x * rd.x, sc.y * rd.y, sc.z * rd.z);
+    return __fsqrt_rn(fdot3(sd, sd) + 1e-18f);
+}
+
+__device__ __forceinline__ float crossing_alpha(float AA, float BB, float CC, float density, float t) {
+    const float qd = fmaxf(__fmaf_rn(__fmaf_rn(AA, t, BB), t, CC), 0.0f);
+    return fminf(kMaxAlpha, density * gf_expf(-0.5f * qd));
+}
+
+// The 0.5-opacity crossing inside one Gaussian on the closed ray interval
+// (finiteIntervalExactCrossing.cuh:42-109): alpha(t) = rho exp(-q(t)/2),
+// q(t) = AA t^2 + BB t + CC, and T_before (1 - alpha(t)) = 0.5 at the near
+// root; the rate is dO/dt there.  False when there is no crossing.
+__device__ __forceinline__ bool exact_crossing(float AA, float BB, float CC, float density, float tBefore, float tmin,
+                                               float tmax, float& depth, float& rate) {
+    const float threshold = 0.5f;
+    if (!(isfinite_f(AA) && isfinite_f(BB) && isfinite_f(CC) && isfinite_f(density) && isfinite_f(tBefore) &&
+          isfinite_f(tmin) && isfinite_f(tmax)))
+        return false;
+    if (!(AA > 0.0f) || !(density > 0.0f) || !(tmax > tmin) || !(tBefore > threshold) || !(tBefore <= 1.0f))
+        return false;
+    const float tLine = -BB / (2.0f * AA);
+    const float tPeak = fminf(fmaxf(tLine, tmin), tmax);
+    const float peakAlpha = crossing_alpha(AA, BB, CC, density, tPeak);
+    const float required = 1.0f - threshold / tBefore;
+    if (!(required > 0.0f) || !(required < kMaxAlpha) || !(peakAlpha >= required)) return false;
+    const float level = required / density;
+    if (!(level > 0.0f) || !(level <= 1.0f) || !isfinite_f(level)) return false;
+    const float con = CC + 2.0f * gf_logf(level);
+    const float disc = BB * BB - (4.0f * AA) * con;
+    if (!(disc >= 0.0f) || !isfinite_f(disc)) return false;
+    const float nearRoot = (-BB - __fsqrt_rn(disc)) / (2.0f * AA);
+    if (!isfinite_f(nearRoot)) return false;
+    if (nearRoot <= tmin || nearRoot >= tmax) {
+        const float edge = nearRoot <= tmin ? tmin : tmax;
+        if (!(crossing_alpha(AA, BB, CC, density, edge) >= required)) return false;
+        depth = edge;
+        rate = 0.0f;
+        return true;
+    }
+    const float r = -0.5f * (tBefore - threshold) * (2.0f * AA * nearRoot + BB);
+    depth = nearRoot;
+    rate = (disc == 0.0f || !isfinite_f(r) || !(r > 0.0f)) ? 0.0f : r;
+    return true;
+}
+
+// One composited hit into the geometric channels.  rec: the particle's render
+// record; row: its packed [N,32] row (quaternion, intrinsic scale).
+__device__ __forceinline__ void geo_hit(PixelGeo& g, const Ray& ray, const Record& rec, const float* __restrict__ row,
+                                        float hitT, float w, float tBefore, float tAfter) {
+    const V3 grdu = binv_times(rec.b, rec.c, rec.d, ray.d);
+    const float len = __fsqrt_rn(fdot3(grdu, grdu));
+    const V3 grd = v3(grdu.x / len, grdu.y / len, grdu.z / len);
+    // B^-T grd; B^-1 rows: r0 = (b.x b.y b.z), r1 = (b.w c.x c.y), r2 = (c.z c.w d.x)
+    const V3 nu = v3(__fmaf_rn(rec.c.z, grd.z, __fmaf_rn(rec.b.w, grd.y, rec.b.x * grd.x)),
+                     __fmaf_rn(rec.c.w, grd.z, __fmaf_rn(rec.c.x, grd.y, rec.b.y * grd.x)),
+                     __fmaf_rn(rec.d.x, grd.z, __fmaf_rn(rec.c.y, grd.y, rec.b.z * grd.x)));
+    const float inv = -1.0f / __fsqrt_rn(fdot3(nu, nu));
+    g.n[0] = __fmaf_rn(w, inv * nu.x, g.n[0]);
+    g.n[1] = __fmaf_rn(w, inv * nu.y, g.n[1]);
+    g.n[2] = __fmaf_rn(w, inv * nu.z, g.n[2]);
+    g.sumWD2 = __fmaf_rn(w * hitT, hitT, g.sumWD2);
+    const float dd = hitT * g.dscale;
+    const bool active = dd > kParticleMinSensorZ;
+    const float invD = active ? 1.0f / dd : 1.0f / kParticleMinSensorZ;
+    const float invD2 = active ? 1.0f / ((hitT * hitT) * (g.dscale * g.dscale))
+                               : 1.0f / (kParticleMinSensorZ * kParticleMinSensorZ);
+    g.sumInvD = __fmaf_rn(w, invD, g.sumInvD);
+    g.sumInvD2 = __fmaf_rn(w, invD2, g.sumInvD2);
+    g.sumExt = __fmaf_rn(w, extent_sigma(__ldg(reinterpret_cast<const float4*>(row + 4)),
+                                         __ldg(reinterpret_cast<const float4*>(row + 8)), ray.d), g.sumExt);
+    const float oAcc = 1.0f - tAfter;
+#pragma unroll
+    for (int i = 0; i < kQuantiles; ++i)
+        if (g.q[i] == 0.0f && oAcc >= quantile_threshold(i)) g.q[i] = hitT;
+    if (w > g.tauMaxW) {
+        g.tauMaxW = w;
+        g.tauMaxD = hitT;
+    }
+    if (g.exactDepth == 0.0f && tBefore > 0.5f && tAfter <= 0.5f) {
+        const V3 gro = binv_times(rec.b, rec.c, rec.d, v3(ray.o.x - rec.a.x, ray.o.y - rec.a.y, ray.o.z - rec.a.z));
+        float depth = hitT, rate = 0.0f;
+        if (!exact_crossing(fdot3(grdu, grdu), 2.0f * fdot3(gro, grdu), fdot3(gro, gro), rec.a.w, tBefore, ray.tmin,
+                            ray.tmax, depth, rate)) {
+            depth = hitT;
+            rate = 0.0f;
+        }
+        g.exactDepth = depth;
+        g.exactRate = rate;
+    }
+}
+
+__device__ __forceinline__ void geo_store(const GeoOut& o, size_t pix, const PixelGeo& g, bool valid) {
+    if (o.normal != nullptr) {
+        o.normal[3 * pix] = valid ? g.n[0] : 0.0f;
+        o.normal[3 * pix + 1] = valid ? g.n[1] : 0.0f;
+        o.normal[3 * pix + 2] = valid ? g.n[2] : 0.0f;
+    }
+    if (o.depthVar != nullptr) o.depthVar[pix] = valid ? g.sumWD2 : 0.0f;
+    if (o.extent != nullptr) o.extent[pix] = valid ? g.sumExt : 0.0f;
+    if (o.invD != nullptr) o.invD[pix] = valid ? g.sumInvD : 0.0f;
+    if (o.invD2 != nullptr) o.invD2[pix] = valid ? g.sumInvD2 : 0.0f;
+    if (o.quant != nullptr) {
+        float* q = o.quant + size_t(kQuantStride) * pix;
+#pragma unroll
+        for (int i = 0; i < kQuantiles; ++i) q[i] = valid ? g.q[i] : 0.0f;
+        q[kQuantiles] = valid ? g.tauMaxD : 0.0f;
+        q[kQuantiles + 1] = valid ? g.exactDepth : 0.0f;
+        q[kQuantiles + 2] = valid ? g.exactRate : 0.0f;
+    }
+}
+
+__device__ __forceinline__ uint32_t id_at(const RenderArgs& a, const Batch& b, uint32_t sp) {
+    const uint32_t j = sp - b.base;
+    if (j < b.cnt) return b.ids[j];
+    return __ldg(a.sortedIds + sp);
+}
+
 __device__ __forceinline__ float2* ring_ta(unsigned char* smem) {
     return reinterpret_cast<float2*>(smem + sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch);
 }
@@ -463,7 +651,7 @@ __device__ __forceinline__ uint32_t* ring_id(unsigned char* smem) {
                                        sizeof(float2) * K * kTileThreads);
 }
 
-template <int K>
+template <int K, bool kGeo>
 __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float* __restrict__ rgba,
                                                              float* __restrict__ hitDistance,
                                                              float* __restrict__ hitCount) {
@@ -478,6 +666,18 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
     kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
     uint32_t nlog = 0;
+    PixelGeo geo;
+    if constexpr (kGeo) {
+        const bool pinhole = a.f.cam.model == GF_CAMERA_OPENCV_PINHOLE;
+        geo_init(geo, (pinhole && ts.inImage && retained) ? a.rayD[3 * ts.pix + 2] : 1.0f);
+    }
+    // one composited hit into the geometric channels (T before and after it)
+    auto geoHit = [&](uint32_t id, float ht, float ha, float tBefore) {
+        if constexpr (kGeo) {
+            const Record rec = load_record(a.records, id);
+            geo_hit(geo, ts.ray, rec, a.geo.particles + 32 * size_t(id), ht, ha * tBefore, tBefore, s.T);
+        }
+    };
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
         for (uint32_t base = range.x; base < range.y; base += kBatch) {
@@ -502,14 +702,18 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                     if (hit_staged<true>(ts, sRec[j], alpha, ht)) {
                         if constexpr (K == 0) {
                             log_composite(a.log, uint32_t(ts.tile), nlog, base + uint32_t(j) - range.x);
+                            const float tBefore = s.T;
                             composite_fwd(s, ht, alpha, sRec[j].d);
+                            geoHit(sId[j], ht, alpha, tBefore);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
                                 uint32_t s0;
                                 kb.pop_front(t0, a0, s0);
                                 log_composite(a.log, uint32_t(ts.tile), nlog, s0 - range.x);
+                                const float tBefore = s.T;
                                 composite_fwd(s, t0, a0, color_at(a, bt, s0));
+                                if constexpr (kGeo) geoHit(id_at(a, bt, s0), t0, a0, tBefore);
                             }
                             kb.insert(ht, alpha, base + uint32_t(j));
                         }
@@ -523,7 +727,9 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
                 uint32_t sp;
                 kb.entry(i, ht, ha, sp);
                 log_composite(a.log, uint32_t(ts.tile), nlog, sp - range.x);
+                const float tBefore = s.T;
                 composite_fwd(s, ht, ha, color_at(a, bt, sp));
+                if constexpr (kGeo) geoHit(id_at(a, bt, sp), ht, ha, tBefore);
             }
         }
     }
@@ -547,6 +753,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
     reinterpret_cast<float4*>(rgba)[ts.pix] = out;
     hitDistance[ts.pix] = hd;
     if (hitCount != nullptr) hitCount[ts.pix] = hc;
+    if constexpr (kGeo) geo_store(a.geo, ts.pix, geo, ts.ray.valid);
 }
 
 // ------------------------------------------------------------------ backward

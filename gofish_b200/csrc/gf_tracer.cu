@@ -60,6 +60,7 @@ struct gf_tracer {
     DeviceBuffer logIds, logCount, logOverflow, logList;  // composite log of the last training forward
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
     gf::CompositeLog frameLog{};
+    bool frameGeo = false;                                // the last forward wrote the geometric channels
     uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size (low 32 bits)
     uint32_t fallbackParticles = 0;
     int finalBuf = 0;
@@ -167,12 +168,19 @@ int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream) {
     return sort_pairs(t->hist, t->scanTiles, t->launches, t->keys, t->ids, n, 0, endBit, &t->finalBuf, stream);
 }
 
+template <int K, bool kGeo>
+void launch_render_fwd_geo(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
+                           cudaStream_t stream) {
+    const size_t smem = gf::render_smem_bytes(K);
+    cudaFuncSetAttribute(gf::k_render_fwd<K, kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_fwd<K, kGeo><<<tiles, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
+}
+
 template <int K>
 void launch_render_fwd(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
                        cudaStream_t stream) {
-    const size_t smem = gf::render_smem_bytes(K);
-    cudaFuncSetAttribute(gf::k_render_fwd<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    gf::k_render_fwd<K><<<tiles, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
+    if (a.geo.particles != nullptr) launch_render_fwd_geo<K, true>(a, tiles, rgba, hd, hc, stream);
+    else launch_render_fwd_geo<K, false>(a, tiles, rgba, hd, hc, stream);
 }
 
 template <int K>
@@ -228,7 +236,7 @@ constexpr size_t kLogBudgetBytes = size_t(4) << 30;
 // Projection, binning, sort and forward composite; a training forward
 // (logComposites) also records the composite log for the backward.
 int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, float* hc, float* vis,
-            bool logComposites, cudaStream_t stream) {
+            bool logComposites, const gf_trace_outputs* geoOut, cudaStream_t stream) {
     if (int e = bind_device(t)) return e;
     const TileMask* mask = nullptr;
     if (int e = validate_inputs(t, in, &mask)) return e;
@@ -416,6 +424,17 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
         a.log.tiles = T;
     }
     t->frameLog = a.log;
+    a.geo = gf::GeoOut{};
+    if (geoOut != nullptr) {
+        a.geo.normal = geoOut->normal;
+        a.geo.depthVar = geoOut->depth_var;
+        a.geo.quant = geoOut->quant;
+        a.geo.extent = geoOut->extent;
+        a.geo.invD = geoOut->inv_depth;
+        a.geo.invD2 = geoOut->inv_depth2;
+        a.geo.particles = in->particles;
+    }
+    t->frameGeo = geoOut != nullptr;
     {
         StageTimer st(t, GF_STAGE_RENDER_FWD, stream);
         if (int e = dispatch_fwd(t->cfg.k_buffer_size, a, T, rgba, hd, hc, stream)) return e;
@@ -504,13 +523,13 @@ int gf_tracer_register_tile_mask(gf_tracer* t, const uint8_t* mask, uint32_t til
 int gf_tracer_trace(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_outputs* out, void* stream) {
     if (t == nullptr || out == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
     return forward(t, in, out->rgba, out->hit_distance, t->cfg.enable_hit_counts ? out->hit_count : nullptr,
-                   out->visibility, true, static_cast<cudaStream_t>(stream));
+                   out->visibility, true, t->cfg.enable_normals ? out : nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int gf_tracer_trace_inference(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hit_distance,
                               void* stream) {
     if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
-    return forward(t, in, rgba, hit_distance, nullptr, nullptr, false, static_cast<cudaStream_t>(stream));
+    return forward(t, in, rgba, hit_distance, nullptr, nullptr, false, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_grads* g, void* stream) {

@@ -64,6 +64,8 @@ class SplatRaster:
         cfg.admission_fallback = _native.GF_FALLBACK_CONE if fallback == "cone" else _native.GF_FALLBACK_NONE
         # entries per pixel of the composite log the backward reads (0: default, < 0: replay every tile)
         cfg.composite_log_capacity = int(_select(conf, "render.splat.composite_log_capacity", 0))
+        # the geometric training channels (normals, depth moments, quantile depths, extent, inverse depth)
+        cfg.enable_normals = 1 if bool(_select(conf, "render.enable_normals", False)) else 0
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())
@@ -155,15 +157,19 @@ class SplatRaster:
         out.hit_distance = hit_distance.data_ptr()
         out.hit_count = hit_count.data_ptr()
         out.visibility = visibility.data_ptr() if n > 0 else None
+        zeros = lambda c: torch.zeros((height, width, c), **f32)  # noqa: E731
+        # normal, depth var, quantiles, extent, opacity field, inverse depth, inverse depth squared
+        geo = [zeros(3), zeros(1), zeros(QUANT_CHANNELS), zeros(1), zeros(1), zeros(1), zeros(1)]
+        if self.config.enable_normals:
+            out.normal, out.depth_var, out.quant, out.extent = (t.data_ptr() for t in geo[:4])
+            out.inv_depth, out.inv_depth2 = geo[5].data_ptr(), geo[6].data_ptr()
         with torch.cuda.device(device):
             end = self._timed("forward_render", device)
             check(self._lib.gf_tracer_trace(self._handle, ctypes.byref(inp), ctypes.byref(out), _stream(device)),
                   "trace")
             if end is not None:
                 end.record(torch.cuda.current_stream(device))
-        zeros = lambda c: torch.zeros((height, width, c), **f32)  # noqa: E731
-        return (rgba, hit_distance, hit_count, visibility, zeros(3), zeros(1), zeros(QUANT_CHANNELS), zeros(1),
-                zeros(1), zeros(1), zeros(1))
+        return (rgba, hit_distance, hit_count, visibility, *geo)
 
     def trace_inference(self, n_active_features, particle_density, particle_radiance, ray_ori, ray_dir, sensor, t0,
                         t1, pose0, pose1, token):

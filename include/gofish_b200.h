@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 2
+#define GF_ABI_VERSION 3
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -75,6 +75,8 @@ typedef struct gf_tracer_config {
     int32_t composite_log_capacity; /* entries per pixel of the training forward's composite log, read by the
                                        backward: 0 = default (128), < 0 = no log (the backward replays every
                                        tile through the k-buffer) */
+    int32_t enable_normals;         /* render.enable_normals: 1 computes the geometric training channels
+                                       (gf_trace_outputs.normal ... inv_depth2) and their gradients */
 } gf_tracer_config;
 
 /* render.gofish.fast_admission_fallback (setup_3dgut.py:232-239): "none"
@@ -109,6 +111,16 @@ typedef struct gf_trace_outputs {
     float* hit_distance;  /* [H,W,1]                                           */
     float* hit_count;     /* [H,W,1] or NULL                                   */
     float* visibility;    /* [N,1]: int bit pattern 1 where the particle is admitted to a tile, else 0; or NULL */
+    /* Geometric training channels (rayPayload.cuh:242-322), written when the
+     * tracer was created with enable_normals; each may be NULL. */
+    float* normal;        /* [H,W,3] sum_i w_i n_i, n_i = -normalize(B^-T normalize(B^-1 d)) */
+    float* depth_var;     /* [H,W,1] sum_i w_i t_i^2 */
+    float* quant;         /* [H,W,10] depths where the accumulated opacity first reaches 0.05, 0.10, 0.15,
+                             0.20, 0.30, 0.40, 0.50; the largest-weight hit's depth; the exact 0.5-crossing
+                             depth and its opacity rate */
+    float* extent;        /* [H,W,1] sum_i w_i sigma_i, sigma_i = |s_i * (R_i^T d)| of the intrinsic shape */
+    float* inv_depth;     /* [H,W,1] sum_i w_i / max(d_i, 0.2) */
+    float* inv_depth2;    /* [H,W,1] sum_i w_i / max(d_i, 0.2)^2 */
 } gf_trace_outputs;
 
 /* Backward inputs/outputs (splatRaster.cpp:469-640). */
@@ -119,6 +131,19 @@ typedef struct gf_trace_grads {
     const float* grad_hit_distance; /* dL/d hit distance [H,W,1] */
     float* grad_particles;          /* out [N,32] (overwritten) */
     float* grad_features;           /* out [N, 3*sh_coeffs] (overwritten) */
+    /* Geometric channels (enable_normals): forward values and their
+     * gradients, NULL pairs for channels without a gradient.  The extent's
+     * gradient reaches the rotation and scale slots (4-10) of grad_particles. */
+    const float* normal;
+    const float* grad_normal;
+    const float* depth_var;
+    const float* grad_depth_var;
+    const float* extent;
+    const float* grad_extent;
+    const float* inv_depth;
+    const float* grad_inv_depth;
+    const float* inv_depth2;
+    const float* grad_inv_depth2;
 } gf_trace_grads;
 
 /* Counters of the last forward pass. */

@@ -83,6 +83,8 @@ def load():
         "oracle_tile_rays": (i32, [cam_p, pose_p, vp, vp, vp]),
         "oracle_bin": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i32, vp, vp, i64, vp]),
         "oracle_render_forward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "oracle_render_forward_geo": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
+                                            vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_render_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp,
                                          vp]),
         "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
@@ -199,6 +201,35 @@ def render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted
                               _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
                               _p(ids), int(k), int(t0), int(t1), _p(rgba), _p(hit_t), _p(count))
     return rgba, hit_t, count
+
+
+def render_forward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, tiles=None,
+                       pinhole=False):
+    """render_forward plus the geometric training channels: a dict with rgba,
+    hit_t, hit_count, normal [H,W,3], depth_var, quant [H,W,10], extent,
+    inv_depth, inv_depth2 (zeros outside retained tiles and for invalid rays)."""
+    lib = load()
+    h, w = cam.height, cam.width
+    gx, gy = tile_grid(cam)
+    t0, t1 = (0, gx * gy) if tiles is None else tiles
+    out = dict(rgba=np.zeros((h, w, 4), np.float32), hit_t=np.full((h, w), 1e6, np.float32),
+               hit_count=np.zeros((h, w), np.float32), normal=np.zeros((h, w, 3), np.float32),
+               depth_var=np.zeros((h, w), np.float32), quant=np.zeros((h, w, 10), np.float32),
+               extent=np.zeros((h, w), np.float32), inv_depth=np.zeros((h, w), np.float32),
+               inv_depth2=np.zeros((h, w), np.float32))
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    lib.oracle_render_forward_geo(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                                  _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                                  _p(ids), int(k), int(t0), int(t1), int(bool(pinhole)),
+                                  *(_p(out[k_]) for k_ in ("rgba", "hit_t", "hit_count", "normal", "depth_var",
+                                                           "quant", "extent", "inv_depth", "inv_depth2")))
+    return out
 
 
 def render_backward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, rgba, hit_t, grad_rgba,

@@ -246,6 +246,8 @@ bool project_world(const OracleCamera& cam, const OraclePose& pose, float3_ pw, 
 struct Particle {
     float3_ pos;
     float density;
+    float quat[4];  // intrinsic rotation (w, x, y, z), slots 4-7
+    float scale[3]; // intrinsic scale, slots 8-10
     float B[9];     // factor, row-major (slots 12-20)
     float Binv[9];  // inverse factor, row-major (slots 21-29)
 };
@@ -253,6 +255,8 @@ inline Particle load_particle(const float* row) {
     Particle p;
     p.pos = f3(row[0], row[1], row[2]);
     p.density = row[3];
+    for (int i = 0; i < 4; ++i) p.quat[i] = row[4 + i];
+    for (int i = 0; i < 3; ++i) p.scale[i] = row[8 + i];
     for (int i = 0; i < 9; ++i) p.B[i] = row[12 + i];
     for (int i = 0; i < 9; ++i) p.Binv[i] = row[21 + i];
     return p;
@@ -932,6 +936,122 @@ void traverse(const Scene& sc, uint32_t tile, const Ray& ray, bool& alive, HitFn
     }
 }
 
+// ------------------------------------------------------------------ geometric channels
+// The training channels of processHitParticle (gutKBufferRenderer.cuh:330-392)
+// and finalizeRay (rayPayload.cuh:242-322), per composited hit, w = alpha T_before:
+// normal += w n with n = -normalize(B^-T normalize(B^-1 d))
+// (gaussianParticles.slang:254-265); depth var += (w t) t; extent += w
+// |s * (R^T d)| of the intrinsic rotation and scale (gaussianParticles.cuh:131-141,
+// quaternionWXYZToMatrix :55-75); inverse depth moments with the 0.2 near clip
+// (sensorConstants.cuh:28-42); the first depth where 1 - T_after reaches each
+// opacity threshold; the largest-weight depth; the exact 0.5 crossing
+// (finiteIntervalExactCrossing.cuh:42-109).
+constexpr int kQuantiles = 7;
+constexpr float kQuantileThresholds[kQuantiles] = {0.05f, 0.10f, 0.15f, 0.20f, 0.30f, 0.40f, 0.50f};
+
+struct GeoState {
+    float n[3];
+    float sumWD2, sumExt, sumInvD, sumInvD2;
+    float q[kQuantiles];
+    float tauMaxW, tauMaxD, exactDepth, exactRate;
+    float dscale;
+};
+
+inline float3_ rotate_transpose(const float* q, float3_ d) {
+    const float r = q[0], x = q[1], y = q[2], z = q[3];
+    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z, rx = r * x, ry = r * y,
+                rz = r * z;
+    const float3_ r0 = f3(1.0f - 2.0f * (yy + zz), 2.0f * (xy + rz), 2.0f * (xz - ry));
+    const float3_ r1 = f3(2.0f * (xy - rz), 1.0f - 2.0f * (xx + zz), 2.0f * (yz + rx));
+    const float3_ r2 = f3(2.0f * (xz + ry), 2.0f * (yz - rx), 1.0f - 2.0f * (xx + yy));
+    return f3(fdot(r0, d), fdot(r1, d), fdot(r2, d));
+}
+
+inline float extent_sigma(const Particle& P, float3_ d) {
+    const float3_ rd = rotate_transpose(P.quat, d);
+    const float3_ sd = f3(P.scale[0] * rd.x, P.scale[1] * rd.y, P.scale[2] * rd.z);
+    return std::sqrt(fdot(sd, sd) + 1e-18f);
+}
+
+inline float crossing_alpha(float AA, float BB, float CC, float density, float t) {
+    const float qd = gf::max_f(fmaf_rn(fmaf_rn(AA, t, BB), t, CC), 0.0f);
+    return gf::min_f(kMaxAlpha, density * gf::gf_expf(-0.5f * qd));
+}
+
+inline bool exact_crossing(float AA, float BB, float CC, float density, float tBefore, float tmin, float tmax,
+                           float& depth, float& rate) {
+    const float threshold = 0.5f;
+    if (!(gf::isfinite_f(AA) && gf::isfinite_f(BB) && gf::isfinite_f(CC) && gf::isfinite_f(density) &&
+          gf::isfinite_f(tBefore) && gf::isfinite_f(tmin) && gf::isfinite_f(tmax)))
+        return false;
+    if (!(AA > 0.0f) || !(density > 0.0f) || !(tmax > tmin) || !(tBefore > threshold) || !(tBefore <= 1.0f))
+        return false;
+    const float tLine = -BB / (2.0f * AA);
+    const float tPeak = gf::min_f(gf::max_f(tLine, tmin), tmax);
+    const float peakAlpha = crossing_alpha(AA, BB, CC, density, tPeak);
+    const float required = 1.0f - threshold / tBefore;
+    if (!(required > 0.0f) || !(required < kMaxAlpha) || !(peakAlpha >= required)) return false;
+    const float level = required / density;
+    if (!(level > 0.0f) || !(level <= 1.0f) || !gf::isfinite_f(level)) return false;
+    const float con = CC + 2.0f * gf::gf_logf(level);
+    const float disc = BB * BB - (4.0f * AA) * con;
+    if (!(disc >= 0.0f) || !gf::isfinite_f(disc)) return false;
+    const float nearRoot = (-BB - std::sqrt(disc)) / (2.0f * AA);
+    if (!gf::isfinite_f(nearRoot)) return false;
+    if (nearRoot <= tmin || nearRoot >= tmax) {
+        const float edge = nearRoot <= tmin ? tmin : tmax;
+        if (!(crossing_alpha(AA, BB, CC, density, edge) >= required)) return false;
+        depth = edge;
+        rate = 0.0f;
+        return true;
+    }
+    const float r = -0.5f * (tBefore - threshold) * (2.0f * AA * nearRoot + BB);
+    depth = nearRoot;
+    rate = (disc == 0.0f || !gf::isfinite_f(r) || !(r > 0.0f)) ? 0.0f : r;
+    return true;
+}
+
+void geo_hit(GeoState& g, const Ray& ray, const Particle& P, float hitT, float w, float tBefore, float tAfter) {
+    const float3_ grdu = fmatvec(P.Binv, ray.d);
+    const float len = std::sqrt(fdot(grdu, grdu));
+    const float3_ grd = f3(grdu.x / len, grdu.y / len, grdu.z / len);
+    const float* M = P.Binv;  // B^-T grd
+    const float3_ nu = f3(fmaf_rn(M[6], grd.z, fmaf_rn(M[3], grd.y, M[0] * grd.x)),
+                          fmaf_rn(M[7], grd.z, fmaf_rn(M[4], grd.y, M[1] * grd.x)),
+                          fmaf_rn(M[8], grd.z, fmaf_rn(M[5], grd.y, M[2] * grd.x)));
+    const float inv = -1.0f / std::sqrt(fdot(nu, nu));
+    g.n[0] = fmaf_rn(w, inv * nu.x, g.n[0]);
+    g.n[1] = fmaf_rn(w, inv * nu.y, g.n[1]);
+    g.n[2] = fmaf_rn(w, inv * nu.z, g.n[2]);
+    g.sumWD2 = fmaf_rn(w * hitT, hitT, g.sumWD2);
+    const float dd = hitT * g.dscale;
+    const bool active = dd > kParticleMinSensorZ;
+    const float invD = active ? 1.0f / dd : 1.0f / kParticleMinSensorZ;
+    const float invD2 = active ? 1.0f / ((hitT * hitT) * (g.dscale * g.dscale))
+                               : 1.0f / (kParticleMinSensorZ * kParticleMinSensorZ);
+    g.sumInvD = fmaf_rn(w, invD, g.sumInvD);
+    g.sumInvD2 = fmaf_rn(w, invD2, g.sumInvD2);
+    g.sumExt = fmaf_rn(w, extent_sigma(P, ray.d), g.sumExt);
+    const float oAcc = 1.0f - tAfter;
+    for (int i = 0; i < kQuantiles; ++i)
+        if (g.q[i] == 0.0f && oAcc >= kQuantileThresholds[i]) g.q[i] = hitT;
+    if (w > g.tauMaxW) {
+        g.tauMaxW = w;
+        g.tauMaxD = hitT;
+    }
+    if (g.exactDepth == 0.0f && tBefore > 0.5f && tAfter <= 0.5f) {
+        const float3_ gro = fmatvec(P.Binv, sub(ray.o, P.pos));
+        float depth = hitT, rate = 0.0f;
+        if (!exact_crossing(fdot(grdu, grdu), 2.0f * fdot(gro, grdu), fdot(gro, gro), P.density, tBefore, ray.tmin,
+                            ray.tmax, depth, rate)) {
+            depth = hitT;
+            rate = 0.0f;
+        }
+        g.exactDepth = depth;
+        g.exactRate = rate;
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -1146,6 +1266,57 @@ int oracle_render_forward(const OracleCamera* cam, const OraclePose* pose, int N
                 rgba[4 * pix + 3] = 1.0f - s.T;
                 hitT[pix] = s.hitT;
                 hitCount[pix] = float(s.hitN);
+            }
+        }
+    });
+    return 0;
+}
+
+// The forward of oracle_render_forward with the geometric training channels
+// (enable_normals): normal[P*3], depthVar[P], quant[P*10], extent[P],
+// invD[P], invD2[P]; pinhole selects the sensor ray's z as the distortion
+// depth scale (rayPayload.cuh:129-136), a fisheye uses 1.
+int oracle_render_forward_geo(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                              const float* rgb, const float* rayO, const float* rayD, const uint8_t* mask,
+                              const uint32_t* ranges, const uint32_t* sortedIds, int K, int tileBegin, int tileEnd,
+                              int pinhole, float* rgba, float* hitT, float* hitCount, float* normal, float* depthVar,
+                              float* quant, float* extent, float* invD, float* invD2) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile;
+    Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
+    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int) {
+        if (mask[tile] == 0u) return;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                PixelState s{1.0f, {0.0f, 0.0f, 0.0f}, 0.0f, 0u, true};
+                GeoState g{};
+                g.dscale = pinhole ? rayD[3 * pix + 2] : 1.0f;
+                traverse(sc, uint32_t(tile), ray, s.alive, [&](const Hit& h) {
+                    const float tBefore = s.T;
+                    composite(s, h, rgb);
+                    const Particle P = load_particle(particles + 32 * size_t(h.idx));
+                    geo_hit(g, ray, P, h.hitT, h.alpha * tBefore, tBefore, s.T);
+                });
+                rgba[4 * pix + 0] = s.rgb[0];
+                rgba[4 * pix + 1] = s.rgb[1];
+                rgba[4 * pix + 2] = s.rgb[2];
+                rgba[4 * pix + 3] = 1.0f - s.T;
+                hitT[pix] = s.hitT;
+                hitCount[pix] = float(s.hitN);
+                for (int k = 0; k < 3; ++k) normal[3 * pix + k] = g.n[k];
+                depthVar[pix] = g.sumWD2;
+                extent[pix] = g.sumExt;
+                invD[pix] = g.sumInvD;
+                invD2[pix] = g.sumInvD2;
+                float* q = quant + 10 * pix;
+                for (int k = 0; k < kQuantiles; ++k) q[k] = g.q[k];
+                q[kQuantiles] = g.tauMaxD;
+                q[kQuantiles + 1] = g.exactDepth;
+                q[kQuantiles + 2] = g.exactRate;
             }
         }
     });

@@ -80,7 +80,8 @@ def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
 class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
-    def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0):
+    def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0,
+                 enable_normals: bool = False):
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -91,7 +92,7 @@ class GpuTracer:
         conf = {"render": {"splat": {"k_buffer_size": k, "composite_log_capacity": log_capacity},
                            "gofish": {"fast_global_depth_key": key_mode == 1,
                                       "fast_admission_fallback": "cone" if fallback else "none"},
-                           "enable_hitcounts": True}}
+                           "enable_hitcounts": True, "enable_normals": enable_normals}}
         self.raster = SplatRaster(conf)
         self.token = "test-token"
         self.raster.register_physical_tile_mask(torch.from_numpy(case.tmask).to(device), self.token)
@@ -114,6 +115,9 @@ class GpuTracer:
         res["hit_t"] = out[1][..., 0].cpu().numpy()
         res["hit_count"] = out[2][..., 0].cpu().numpy()
         res["visibility"] = out[3][:, 0].cpu().numpy().view(np.uint32)
+        for name, t in zip(("normal", "depth_var", "quant", "extent", "opacity_field", "inv_depth", "inv_depth2"),
+                           out[4:]):
+            res[name] = t.cpu().numpy()
         return res
 
     def backward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray):

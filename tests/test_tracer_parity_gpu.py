@@ -279,3 +279,35 @@ def test_backward_paths_agree(cuda_device, k, log_capacity):
     gp, gs = gpu.backward(g_rgba, g_hit)
     assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
     assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("k", [0, 16])
+def test_geometric_channels_forward(cuda_device, k):
+    """enable_normals: normal sum, sum w t^2, extent, inverse-depth moments,
+    quantile depths, max-weight depth and the exact 0.5 crossing equal the
+    oracle's (the same hits in the same order with the same arithmetic); the
+    colour outputs are unchanged."""
+    import oracle
+
+    case = harness.small_case(seed=23, n=20_000, size=256)
+    ref = harness.oracle_forward(case, k, 0)
+    geo = oracle.render_forward_geo(case.ocam, ref["pose"], case.particles, ref["rgb"], case.ray_o, case.ray_d,
+                                    case.tmask, ref["ranges"], ref["ids"], k)
+    gpu = harness.GpuTracer(case, k, 0, cuda_device, enable_normals=True)
+    got = gpu.forward()
+    _compare_forward(ref, got)
+    np.testing.assert_array_equal(got["normal"], geo["normal"])
+    for name in ("depth_var", "extent", "inv_depth", "inv_depth2"):
+        np.testing.assert_array_equal(got[name][..., 0], geo[name], err_msg=name)
+    np.testing.assert_array_equal(got["quant"], geo["quant"])
+    assert not got["opacity_field"].any()
+    valid = case.valid & (ref["rgba"][..., 3] > 0.6)
+    assert valid.sum() > 100
+    # sanity of the channels: normals are weighted unit vectors, every
+    # threshold up to 0.5 and the 0.5 crossing are reached on opaque rays (the
+    # quantile depths follow the composite order, which is the sorted tile
+    # order, not each ray's own depth order)
+    assert np.all(np.linalg.norm(got["normal"][valid], axis=-1) <= ref["rgba"][..., 3][valid] + 1e-4)
+    q = got["quant"][valid]
+    assert np.all((q[:, 8] > 0) & (q[:, :7] > 0).all(axis=1))
+    assert np.count_nonzero(q[:, 9]) > 0

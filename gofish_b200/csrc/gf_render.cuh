@@ -69,6 +69,23 @@ struct RenderArgs {
     GeoOut geo;
 };
 
+// Forward values and output gradients of the geometric channels in a backward
+// (NULL pairs: the channel has no gradient).
+struct GeoBwd {
+    const float* normal;
+    const float* gradNormal;
+    const float* depthVar;
+    const float* gradDepthVar;
+    const float* extent;
+    const float* gradExtent;
+    const float* invD;
+    const float* gradInvD;
+    const float* invD2;
+    const float* gradInvD2;
+    const float* particles;    // packed [N,32] rows: quaternion (slots 4-7), intrinsic scale (8-10)
+    float4* gradShape;         // [N,2] float4: quaternion (w, x, y, z) | scale.xyz, 0  (extent gradient)
+};
+
 struct RenderBwdArgs {
     RenderArgs r;
     const float* rgba;
@@ -76,6 +93,7 @@ struct RenderBwdArgs {
     const float* gradRgba;
     const float* gradHitDistance;
     float4* gradRecords;  // [N,4] float4: pos.xyz+density | Binv row0 + row1.x | row1.yz + row2.xy | row2.z + rgb
+    GeoBwd geo;
 };
 
 constexpr int kBatch = kTileThreads;
@@ -765,6 +783,59 @@ struct PixelBwd {
     bool alive;
 };
 
+// Geometric channels in the backward: running sums (re-accumulated exactly as
+// the forward accumulated them), the forward's final values and the output
+// gradients (rayPayloadBackward.cuh:110-150).
+struct PixelGeoBwd {
+    float n[3], wd2;                          // running (the channels whose residuals reach alpha)
+    float nB[3], wd2B;                        // forward outputs
+    float nG[3], wd2G, extG, invDG, invD2G;   // output gradients
+    float dscale;
+};
+
+__device__ __forceinline__ void geo_bwd_init(PixelGeoBwd& g, const GeoBwd& a, size_t pix, float dscale) {
+    const auto val = [&](const float* p, size_t i) { return p != nullptr ? p[i] : 0.0f; };
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        g.n[k] = 0.0f;
+        g.nB[k] = val(a.normal, 3 * pix + k);
+        g.nG[k] = a.normal != nullptr ? val(a.gradNormal, 3 * pix + k) : 0.0f;
+    }
+    g.wd2 = 0.0f;
+    g.wd2B = val(a.depthVar, pix);
+    g.wd2G = a.depthVar != nullptr ? val(a.gradDepthVar, pix) : 0.0f;
+    g.extG = val(a.gradExtent, pix);
+    g.invDG = val(a.gradInvD, pix);
+    g.invD2G = val(a.gradInvD2, pix);
+    g.dscale = dscale;
+}
+
+// d/dv of v / |v| applied to the output gradient go (safe_normalize_bw,
+// mathUtils.cuh:411-421): go / |v| - v (v . go) / |v|^3; zero for v = 0.
+__device__ __forceinline__ V3 normalize_vjp(V3 v, V3 go) {
+    const float l = v.x * v.x + v.y * v.y + v.z * v.z;
+    if (!(l > 0.0f)) return v3(0.0f, 0.0f, 0.0f);
+    const float il = 1.0f / __fsqrt_rn(l);
+    const float il3 = il * il * il;
+    return v3(il * go.x - il3 * (go.x * (v.x * v.x) + go.y * (v.y * v.x) + go.z * (v.z * v.x)),
+              il * go.y - il3 * (go.x * (v.x * v.y) + go.y * (v.y * v.y) + go.z * (v.z * v.y)),
+              il * go.z - il3 * (go.x * (v.x * v.z) + go.y * (v.y * v.z) + go.z * (v.z * v.z)));
+}
+
+// Gradient with respect to the quaternion (w, x, y, z) of y = M(q) p, where
+// M's rows are those of rotate_transpose, for dL/dy = go.
+__device__ __forceinline__ float4 rotate_transpose_vjp(float4 q, V3 p, V3 go) {
+    const float r = q.x, x = q.y, y = q.z, z = q.w;
+    const float G00 = go.x * p.x, G01 = go.x * p.y, G02 = go.x * p.z;
+    const float G10 = go.y * p.x, G11 = go.y * p.y, G12 = go.y * p.z;
+    const float G20 = go.z * p.x, G21 = go.z * p.y, G22 = go.z * p.z;
+    const float dr = 2.0f * (z * G01 - y * G02 - z * G10 + x * G12 + y * G20 - x * G21);
+    const float dx = 2.0f * (y * G01 + z * G02 + y * G10 + r * G12 + z * G20 - r * G21) - 4.0f * x * (G11 + G22);
+    const float dy = 2.0f * (x * G01 - r * G02 + x * G10 + z * G12 + r * G20 + z * G21) - 4.0f * y * (G00 + G22);
+    const float dz = 2.0f * (r * G01 + x * G02 - r * G10 + y * G12 + x * G20 + y * G21) - 4.0f * z * (G00 + G11);
+    return make_float4(dr, dx, dy, dz);
+}
+
 // Gradient of one composited hit (reference processHitBwd,
 // gaussianParticles.cuh:736-1155, geometric channels inactive).  The hit is
 // evaluated here with the forward hit test's exact arithmetic
@@ -774,7 +845,10 @@ struct PixelBwd {
 // exact arithmetic; quotients that only scale gradients use fast
 // reciprocals.  Returns false (state unchanged) when the candidate is not a
 // hit, which a composited entry always is.
-__device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Record& q, float4 g[4]) {
+template <bool kGeo = false>
+__device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Record& q, float4 g[4],
+                                        PixelGeoBwd* geo = nullptr, const float* row = nullptr,
+                                        float4* gShape = nullptr) {
     const V3 gp = v3(ray.o.x - q.a.x, ray.o.y - q.a.y, ray.o.z - q.a.z);
     const V3 gro = binv_times(q.b, q.c, q.d, gp);
     const V3 grdu = binv_times(q.b, q.c, q.d, ray.d);
@@ -813,11 +887,68 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     comp += s.T * (cr - rr) * s.featG[0];
     comp += s.T * (cg - rg) * s.featG[1];
     comp += s.T * (cb - rb) * s.featG[2];
+    float tauGrad = weight * s.hitTG;
+    // Geometric channels (gaussianParticles.cuh:786-1062): the depth moment
+    // and the normal sum reach alpha through their residuals; the depth moment
+    // and the inverse-depth moments reach tau; the normal reaches B^-1 and the
+    // ray's canonical direction; the extent reaches the intrinsic rotation and
+    // scale only.
+    V3 grduGeo = v3(0.0f, 0.0f, 0.0f);
+    float gBinvN[9];
+    if constexpr (kGeo) {
+        PixelGeoBwd& G = *geo;
+        const float gsq = gdist * gdist;
+        G.wd2 = __fmaf_rn(weight * gdist, gdist, G.wd2);
+        const float residualWD2 = fmaxf((G.wd2B - G.wd2) * invNext, 0.0f);
+        comp += (gsq - residualWD2) * s.T * G.wd2G;
+        tauGrad += 2.0f * gdist * weight * G.wd2G;
+        // inverse-depth moments (detached from alpha)
+        const float dd = gdist * G.dscale;
+        const bool active = dd > kParticleMinSensorZ;
+        if (active) {
+            tauGrad += (-weight / (G.dscale * gdist * gdist)) * G.invDG;
+            tauGrad += (-2.0f * weight / ((G.dscale * G.dscale) * gdist * gdist * gdist)) * G.invD2G;
+        }
+        // normal n = -normalize(B^-T normalize(grdu))
+        const float len = __fsqrt_rn(denom);
+        const V3 grd = v3(grdu.x / len, grdu.y / len, grdu.z / len);
+        const V3 nu = v3(__fmaf_rn(q.c.z, grd.z, __fmaf_rn(q.b.w, grd.y, q.b.x * grd.x)),
+                         __fmaf_rn(q.c.w, grd.z, __fmaf_rn(q.c.x, grd.y, q.b.y * grd.x)),
+                         __fmaf_rn(q.d.x, grd.z, __fmaf_rn(q.c.y, grd.y, q.b.z * grd.x)));
+        const float inv = -1.0f / __fsqrt_rn(fdot3(nu, nu));
+        const V3 n = v3(inv * nu.x, inv * nu.y, inv * nu.z);
+        G.n[0] = __fmaf_rn(weight, n.x, G.n[0]);
+        G.n[1] = __fmaf_rn(weight, n.y, G.n[1]);
+        G.n[2] = __fmaf_rn(weight, n.z, G.n[2]);
+        const V3 resN = tail ? v3(0.0f, 0.0f, 0.0f)
+                             : v3((G.nB[0] - G.n[0]) * invNext, (G.nB[1] - G.n[1]) * invNext,
+                                  (G.nB[2] - G.n[2]) * invNext);
+        comp += s.T * ((n.x - resN.x) * G.nG[0] + (n.y - resN.y) * G.nG[1] + (n.z - resN.z) * G.nG[2]);
+        const V3 nuGrd = normalize_vjp(nu, v3(-weight * G.nG[0], -weight * G.nG[1], -weight * G.nG[2]));
+        // nu_j = sum_i B^-1[i][j] grd_i: d/dB^-1[i][j] = grd_i nuGrd_j; d/dgrd = B^-1 nuGrd
+        const float gd[3] = {grd.x, grd.y, grd.z};
+        const float ng[3] = {nuGrd.x, nuGrd.y, nuGrd.z};
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) gBinvN[3 * i + j] = gd[i] * ng[j];
+        const V3 grdGrd = binv_times(q.b, q.c, q.d, nuGrd);
+        grduGeo = normalize_vjp(grdu, grdGrd);
+        // extent sigma = |s * (R^T d)|
+        const float4 quat = __ldg(reinterpret_cast<const float4*>(row + 4));
+        const float4 sc = __ldg(reinterpret_cast<const float4*>(row + 8));
+        const V3 rd = rotate_transpose(quat, ray.d);
+        const V3 sd = v3(sc.x * rd.x, sc.y * rd.y, sc.z * rd.z);
+        const float sigma = __fsqrt_rn(fdot3(sd, sd) + 1e-18f);
+        const float nG = (weight * G.extG) / sigma;
+        const V3 rdGrd = v3(nG * (sc.x * sc.x * rd.x), nG * (sc.y * sc.y * rd.y), nG * (sc.z * sc.z * rd.z));
+        gShape[0] = rotate_transpose_vjp(quat, ray.d, rdGrd);
+        gShape[1] = make_float4(nG * (sc.x * rd.x * rd.x), nG * (sc.y * rd.y * rd.y), nG * (sc.z * rd.z * rd.z), 0.0f);
+    }
     const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
     const float gDensity = gres * gU;
     const float gresGrd = density * gU;
     const float grayDistGrd = -0.5f * gres * gresGrd;
-    const float tauGrad = weight * s.hitTG;
     // Closest-point VJP (reference gutHalfRayResponse.cuh:39-62).
     const V3 pointGrad = (2.0f * grayDistGrd) * p;
     V3 groGrd = pointGrad;
@@ -845,6 +976,18 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     g[1] = make_float4(m00, m01, m02, m10);
     g[2] = make_float4(m11, m12, m20, m21);
     g[3] = make_float4(m22, s.featG[0] * weight, s.featG[1] * weight, s.featG[2] * weight);
+    if constexpr (kGeo) {
+        // the normal's B^-1 term and its canonical-direction term through grdu = B^-1 d
+        g[1].x += gBinvN[0] + grduGeo.x * ray.d.x;
+        g[1].y += gBinvN[1] + grduGeo.x * ray.d.y;
+        g[1].z += gBinvN[2] + grduGeo.x * ray.d.z;
+        g[1].w += gBinvN[3] + grduGeo.y * ray.d.x;
+        g[2].x += gBinvN[4] + grduGeo.y * ray.d.y;
+        g[2].y += gBinvN[5] + grduGeo.y * ray.d.z;
+        g[2].z += gBinvN[6] + grduGeo.z * ray.d.x;
+        g[2].w += gBinvN[7] + grduGeo.z * ray.d.y;
+        g[3].x += gBinvN[8] + grduGeo.z * ray.d.z;
+    }
     s.T = nextT;
     return true;
 }
@@ -893,7 +1036,7 @@ __device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords
 // Backward replay: the identical traversal and k-buffer, each composited hit
 // back-propagated from the final pixel values.  Loops are warp-uniform so
 // the gradient reduction can use full-warp shuffles.
-template <int K>
+template <int K, bool kGeo>
 __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned char* smem, int tile) {
     constexpr int KR = K > 0 ? K : 1;
     Staged* sRec = reinterpret_cast<Staged*>(smem);
@@ -916,6 +1059,24 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
         s.hitTB = a.hitDistance[ts.pix];
         s.hitTG = a.gradHitDistance[ts.pix];
     }
+    PixelGeoBwd geo;
+    if constexpr (kGeo) {
+        const bool pinhole = a.r.f.cam.model == GF_CAMERA_OPENCV_PINHOLE;
+        geo_bwd_init(geo, a.geo, ray.valid ? ts.pix : 0, (pinhole && ray.valid) ? a.r.rayD[3 * ts.pix + 2] : 1.0f);
+    }
+    auto vjp = [&](const Record& q, uint32_t cid, float4* g) -> bool {
+        if constexpr (kGeo) {
+            float4 gs[2] = {};
+            const bool h = hit_vjp<true>(s, ray, q, g, &geo, a.geo.particles + 32 * size_t(cid), gs);
+            if (h) {
+                atomicAdd(a.geo.gradShape + 2 * size_t(cid), gs[0]);
+                atomicAdd(a.geo.gradShape + 2 * size_t(cid) + 1, gs[1]);
+            }
+            return h;
+        } else {
+            return hit_vjp(s, ray, q, g);
+        }
+    };
     RingKBuffer<KR> kb;
     kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
@@ -949,14 +1110,14 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
                     if (hit_staged(ts, sRec[j], alpha, ht)) {
                         if constexpr (K == 0) {
                             const Record q = record_at(a.r, bt, base + uint32_t(j), cid);
-                            have = hit_vjp(s, ray, q, g);
+                            have = vjp(q, cid, g);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
                                 uint32_t s0;
                                 kb.pop_front(t0, a0, s0);
                                 const Record q = record_at(a.r, bt, s0, cid);
-                                have = hit_vjp(s, ray, q, g);
+                                have = vjp(q, cid, g);
                             }
                             kb.insert(ht, alpha, base + uint32_t(j));
                         }
@@ -978,7 +1139,7 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
                 uint32_t sp;
                 kb.entry(i, ht, ha, sp);
                 const Record q = record_at(a.r, bt, sp, cid);
-                have = hit_vjp(s, ray, q, g);
+                have = vjp(q, cid, g);
                 if (s.T < kMinTransmittance) s.alive = false;
             }
             accumulate_grad(a.gradRecords, have, cid, g);
@@ -989,16 +1150,16 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
 // Backward replay kernel: one block per tile, or, when the forward kept a
 // composite log, a resident grid that walks the list of tiles whose log
 // overflowed (usually empty).
-template <int K>
+template <int K, bool kGeo>
 __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     if (a.r.log.ids == nullptr) {
-        replay_tile<K>(a, smem, int(blockIdx.x));
+        replay_tile<K, kGeo>(a, smem, int(blockIdx.x));
         return;
     }
     const uint32_t count = *a.r.log.overflowCount;
     for (uint32_t w = blockIdx.x; w < count; w += gridDim.x) {
-        replay_tile<K>(a, smem, int(a.r.log.overflowList[w]));
+        replay_tile<K, kGeo>(a, smem, int(a.r.log.overflowList[w]));
         __syncthreads();  // the next tile restages the shared batch
     }
 }
@@ -1026,6 +1187,7 @@ __host__ __device__ constexpr size_t bwd_log_smem_bytes() {
 #ifndef GF_BWD_LOG_MIN_BLOCKS
 #define GF_BWD_LOG_MIN_BLOCKS 3
 #endif
+template <bool kGeo>
 __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_bwd_log(RenderBwdArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     float4* sRec = reinterpret_cast<float4*>(smem);                                      // [4][kBwdSlots]
@@ -1079,6 +1241,11 @@ __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_
         s.hitTG = a.gradHitDistance[pix];
         n = lg.count[size_t(tile) * kTileThreads + threadIdx.x];
     }
+    PixelGeoBwd geo;
+    if constexpr (kGeo) {
+        const bool pinhole = f.cam.model == GF_CAMERA_OPENCV_PINHOLE;
+        geo_bwd_init(geo, a.geo, ray.valid ? pix : 0, (pinhole && ray.valid) ? a.r.rayD[3 * pix + 2] : 1.0f);
+    }
     uint32_t warpN = n;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) warpN = max(warpN, __shfl_xor_sync(0xffffffffu, warpN, o));
@@ -1105,7 +1272,16 @@ __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_
                 cid = __ldg(a.r.sortedIds + range.x + local);
                 q = load_record(a.r.records, cid);
             }
-            have = hit_vjp(s, ray, q, g);
+            if constexpr (kGeo) {
+                float4 gs[2] = {};
+                have = hit_vjp<true>(s, ray, q, g, &geo, a.geo.particles + 32 * size_t(cid), gs);
+                if (have) {
+                    atomicAdd(a.geo.gradShape + 2 * size_t(cid), gs[0]);
+                    atomicAdd(a.geo.gradShape + 2 * size_t(cid) + 1, gs[1]);
+                }
+            } else {
+                have = hit_vjp(s, ray, q, g);
+            }
             if (s.T < kMinTransmittance) s.alive = false;
         }
         accumulate_grad(a.gradRecords, have, cid, g);

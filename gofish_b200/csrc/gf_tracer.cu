@@ -56,6 +56,7 @@ struct gf_tracer {
     DeviceBuffer proj, records, bounds, counts, offsets, scanTiles, total, tileRays, ranges;
     DeviceBuffer keys[2], ids[2], hist;
     DeviceBuffer gradRecords;
+    DeviceBuffer gradShape;  // extent gradient: quaternion, intrinsic scale [N,2] float4 (enable_normals)
     DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
     DeviceBuffer logIds, logCount, logOverflow, logList;  // composite log of the last training forward
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
@@ -183,11 +184,24 @@ void launch_render_fwd(const gf::RenderArgs& a, uint32_t tiles, float* rgba, flo
     else launch_render_fwd_geo<K, false>(a, tiles, rgba, hd, hc, stream);
 }
 
+template <int K, bool kGeo>
+void launch_render_bwd_geo(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
+    const size_t smem = gf::render_smem_bytes(K);
+    cudaFuncSetAttribute(gf::k_render_bwd<K, kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_bwd<K, kGeo><<<tiles, gf::kTileThreads, smem, stream>>>(a);
+}
+
 template <int K>
 void launch_render_bwd(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
-    const size_t smem = gf::render_smem_bytes(K);
-    cudaFuncSetAttribute(gf::k_render_bwd<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    gf::k_render_bwd<K><<<tiles, gf::kTileThreads, smem, stream>>>(a);
+    if (a.geo.gradShape != nullptr) launch_render_bwd_geo<K, true>(a, tiles, stream);
+    else launch_render_bwd_geo<K, false>(a, tiles, stream);
+}
+
+template <bool kGeo>
+void launch_render_bwd_log(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
+    const size_t smem = gf::bwd_log_smem_bytes();
+    cudaFuncSetAttribute(gf::k_render_bwd_log<kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_bwd_log<kGeo><<<tiles, gf::kTileThreads, smem, stream>>>(a);
 }
 
 // Blocks of the replay grid that walks the overflowed tiles: 3 per SM.
@@ -491,7 +505,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow, &t->logList}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
-                                &t->hist,    &t->gradRecords};
+                                &t->hist,    &t->gradRecords, &t->gradShape};
         for (DeviceBuffer* b : bufs) b->release();
         for (auto& kv : t->masks) kv.second.buf.release();
         for (auto& ev : t->pending) {
@@ -564,13 +578,29 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     a.gradRgba = g->grad_rgba;
     a.gradHitDistance = g->grad_hit_distance;
     a.gradRecords = t->gradRecords.as<float4>();
+    a.geo = gf::GeoBwd{};
+    if (t->cfg.enable_normals && t->frameGeo) {
+        a.geo.normal = g->normal;
+        a.geo.gradNormal = g->grad_normal;
+        a.geo.depthVar = g->depth_var;
+        a.geo.gradDepthVar = g->grad_depth_var;
+        a.geo.extent = g->extent;
+        a.geo.gradExtent = g->grad_extent;
+        a.geo.invD = g->inv_depth;
+        a.geo.gradInvD = g->grad_inv_depth;
+        a.geo.invD2 = g->inv_depth2;
+        a.geo.gradInvD2 = g->grad_inv_depth2;
+        a.geo.particles = in->particles;
+        if (int e = t->gradShape.ensure(sizeof(float4) * 2 * size_t(N) + 16, s)) return e;
+        GF_CUDA(cudaMemsetAsync(t->gradShape.ptr, 0, sizeof(float4) * 2 * size_t(N), s));
+        a.geo.gradShape = t->gradShape.as<float4>();
+    }
     {
         StageTimer st(t, GF_STAGE_RENDER_BWD, s);
         if (a.r.log.ids != nullptr) {
             // tiles with a complete log, then the replay of the tiles whose log overflowed
-            const size_t smem = gf::bwd_log_smem_bytes();
-            cudaFuncSetAttribute(gf::k_render_bwd_log, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            gf::k_render_bwd_log<<<T, gf::kTileThreads, smem, s>>>(a);
+            if (a.geo.gradShape != nullptr) launch_render_bwd_log<true>(a, T, s);
+            else launch_render_bwd_log<false>(a, T, s);
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }
@@ -583,8 +613,8 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT_BWD, s);
         gf::k_project_bwd<<<(N + 255) / 256, 256, 0, s>>>(f, in->particles, in->features, t->counts.as<uint32_t>(),
-                                                          t->gradRecords.as<float4>(), g->grad_particles,
-                                                          g->grad_features);
+                                                          t->gradRecords.as<float4>(), a.geo.gradShape,
+                                                          g->grad_particles, g->grad_features);
         t->launches += 1;
         GF_LAUNCH_CHECK();
     }

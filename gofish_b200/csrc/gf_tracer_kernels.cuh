@@ -809,6 +809,7 @@ __global__ __launch_bounds__(256) void k_project_bwd(FrameArgs f, const float* _
                                                      const float* __restrict__ features,
                                                      const uint32_t* __restrict__ counts,
                                                      const float4* __restrict__ gradRecords,
+                                                     const float4* __restrict__ gradShape,
                                                      float* __restrict__ gradParticles,
                                                      float* __restrict__ gradFeatures) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -856,9 +857,12 @@ __global__ __launch_bounds__(256) void k_project_bwd(FrameArgs f, const float* _
         for (uint32_t k = 0; k < 3 * f.shCoeffs; ++k) gs[k] = 0.0f;
     }
     float4* out = reinterpret_cast<float4*>(gradParticles + 32 * size_t(i));
+    // rotation and intrinsic scale receive the extent channel's gradient (enable_normals)
+    const float4 gq = gradShape != nullptr ? gradShape[2 * size_t(i)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4 gsc = gradShape != nullptr ? gradShape[2 * size_t(i) + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     out[0] = make_float4(gp0, gp1, gp2, g0.w);                      // pos, density
-    out[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // rotation
-    out[2] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // scale, intrinsic density
+    out[1] = gq;                                                    // rotation
+    out[2] = make_float4(gsc.x, gsc.y, gsc.z, 0.0f);                // scale, intrinsic density
     out[3] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 0..3
     out[4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 4..7
     out[5] = make_float4(0.0f, g1.x, g1.y, g1.z);                   // factor 8 | Binv 0..2

@@ -196,8 +196,6 @@ class SplatRaster:
         *geometry, token = geometry_and_token
         if len(geometry) not in (0, 14):
             raise TypeError("trace_bwd expects the seven (value, gradient) geometric channel pairs and the token")
-        # The geometric channels are outputs of zeros here; their gradients do
-        # not reach the particles (Tracer refuses a loss that uses them).
         device = ray_ori.device
         n = particle_density.shape[0]
         grad_particles = torch.empty((n, 32), dtype=torch.float32, device=device)
@@ -215,6 +213,7 @@ class SplatRaster:
         g.grad_hit_distance = ghd.data_ptr()
         g.grad_particles = grad_particles.data_ptr()
         g.grad_features = grad_features.data_ptr()
+        keep = self._geometry_grads(g, geometry, int(ray_ori.shape[1]), int(ray_ori.shape[2]))
         with torch.cuda.device(device):
             end = self._timed("backward_render", device)
             check(self._lib.gf_tracer_trace_bwd(self._handle, ctypes.byref(inp), ctypes.byref(g), _stream(device)),
@@ -222,6 +221,32 @@ class SplatRaster:
             if end is not None:
                 end.record(torch.cuda.current_stream(device))
         return grad_particles, grad_features
+
+    # (value, gradient) pairs of trace_bwd in the reference's order (splatRaster.cpp:469-500) and their
+    # channel widths; the opacity field and the quantile/crossing channel have no gradient path here
+    GEOMETRY_PAIRS = (("depth_var", 1), ("extent", 1), ("opacity_field", 1), ("quant", QUANT_CHANNELS),
+                      ("normal", 3), ("inv_depth", 1), ("inv_depth2", 1))
+
+    def _geometry_grads(self, g: GfTraceGrads, geometry, height: int, width: int) -> list:
+        """Fills the geometric channel pairs of ``g`` (enable_normals); returns the
+        tensors that must outlive the call."""
+        keep = []
+        if not geometry or not self.config.enable_normals:
+            return keep
+        for i, (name, channels) in enumerate(self.GEOMETRY_PAIRS):
+            value, grad = geometry[2 * i], geometry[2 * i + 1]
+            if grad is None or value is None or grad.numel() != height * width * channels:
+                continue
+            if name in ("opacity_field", "quant"):
+                if bool(torch.count_nonzero(grad)):
+                    raise NotImplementedError(f"the gradient of the {name} channel is not propagated by this tracer")
+                continue
+            v = value.float().contiguous()
+            d = grad.float().contiguous()
+            keep += [v, d]
+            setattr(g, name, v.data_ptr())
+            setattr(g, "grad_" + name, d.data_ptr())
+        return keep
 
     # ------------------------------------------------------------------ introspection
     def collect_times(self) -> dict[str, float]:

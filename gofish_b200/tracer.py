@@ -15,13 +15,14 @@ One render of one view:
    reference's order (tracer.py:142-353), so autograd carries them back
    through the full-shape VJP to the scale, rotation and opacity.
 
-The geometric training channels (normals, distortion moments, quantile and
-exact-crossing depths, extent, opacity field, inverse-depth moments) are
-returned as zeros and carry no gradient, as the reference's buffers are with
-its normal channel compiled out; a configuration whose losses read them
-(``loss.lambda_distortion``, ``lambda_dnc``, ``lambda_esmooth``, ``lambda_opa``,
-``lambda_extent``, ``lambda_normal_variance`` > 0) is refused when the tracer
-is built, and so is the CoMe colour confidence (``loss.color_confidence``).
+With ``render.enable_normals`` the geometric training channels are rendered
+(normal sum, sum w t^2, quantile and exact 0.5-crossing depths, intrinsic
+extent, inverse-depth moments) and the normal, depth-moment, extent and
+inverse-depth channels carry gradients; without it they are zeros, as the
+reference's buffers are with its normal channel compiled out.  The SOF
+opacity field (``loss.lambda_opa``) and the CoMe colour confidence
+(``loss.color_confidence``) are refused when the tracer is built; a gradient
+on the quantile/crossing channel raises.
 """
 
 from __future__ import annotations
@@ -41,8 +42,10 @@ from .view_observation_filter import build_intrinsic_view_shape, pixel_footprint
 # gradient split of tracer.py:334-343.
 PACKED_SPLIT = (3, 1, 4, 3, 1, 9, 9, 2)
 
-GEOMETRIC_LOSSES = ("lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_opa", "lambda_extent",
-                    "lambda_normal_variance")
+# Losses on the geometric training channels (they need render.enable_normals),
+# and the one whose channel (the SOF opacity field) is not rendered here.
+GEOMETRIC_LOSSES = ("lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_extent", "lambda_normal_variance")
+UNSUPPORTED_LOSSES = ("lambda_opa",)
 
 
 def _conf_value(conf, path: str, default):
@@ -80,7 +83,9 @@ class Tracer:
                                         particle_features, ray_ori, ray_dir, None, sensor_params, t0, t1, p0, p1,
                                         physical_tile_token)
             rgba, hit_distance = outs[0], outs[1]
-            ctx.save_for_backward(ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features)
+            # forward values of the geometric channels (normal ... inverse depth squared) for the backward
+            ctx.save_for_backward(ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features,
+                                  *outs[4:])
             ctx.frame_id = frame_id
             ctx.sof_exact_opacity_active = bool(sof_exact_opacity_active)
             ctx.n_active_features = n_active_features
@@ -89,13 +94,17 @@ class Tracer:
             ctx.tracer_wrapper = tracer_wrapper
             ctx.physical_tile_token = physical_tile_token
             ctx.set_materialize_grads(False)
-            ctx.mark_non_differentiable(*outs[2:])
+            ctx.mark_non_differentiable(outs[2], outs[3])
             return outs
 
         @staticmethod
-        def backward(ctx, ray_features_density_grd, ray_hit_distance_grd, *_unused):
-            ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features = ctx.saved_tensors
-            if ray_features_density_grd is None and ray_hit_distance_grd is None:
+        def backward(ctx, ray_features_density_grd, ray_hit_distance_grd, _count_grd, _visibility_grd, normal_grd,
+                     depth_var_grd, quant_grd, extent_grd, opacity_field_grd, invd_grd, invd2_grd):
+            (ray_ori, ray_dir, rgba, hit_distance, particle_density, particle_features, normal, depth_var, quant,
+             extent, opacity_field, invd, invd2) = ctx.saved_tensors
+            geometric = (normal_grd, depth_var_grd, quant_grd, extent_grd, opacity_field_grd, invd_grd, invd2_grd)
+            if ray_features_density_grd is None and ray_hit_distance_grd is None and all(
+                    g is None for g in geometric):
                 return (None,) * 18
             if ray_features_density_grd is None:
                 ray_features_density_grd = torch.zeros_like(rgba)
@@ -104,7 +113,9 @@ class Tracer:
                 ctx.frame_id, ctx.sof_exact_opacity_active, ctx.n_active_features, particle_density,
                 particle_features, ray_ori, ray_dir, None, ctx.sensor_params, poses.timestamps_us[0],
                 poses.timestamps_us[1], poses.T_world_sensors[0], poses.T_world_sensors[1], rgba,
-                ray_features_density_grd, hit_distance, ray_hit_distance_grd, ctx.physical_tile_token)
+                ray_features_density_grd, hit_distance, ray_hit_distance_grd, depth_var, depth_var_grd, extent,
+                extent_grd, opacity_field, opacity_field_grd, quant, quant_grd, normal, normal_grd, invd, invd_grd,
+                invd2, invd2_grd, ctx.physical_tile_token)
             g_pos, g_dns, g_rot, g_scl, g_intrinsic, g_factor, g_inverse = _unpack_rows(grad_density)
             return (None, None, None, None, None, None, None, g_pos, g_rot, g_scl, g_dns, g_intrinsic, g_factor,
                     g_inverse, grad_features.contiguous(), None, None, None)
@@ -114,10 +125,14 @@ class Tracer:
         self.conf = conf
         if _conf_value(conf, "render.primitive_type", "instances") == "trisurfel":
             raise RuntimeError("GOFish renders volumetric Gaussians only")
-        used = [name for name in GEOMETRIC_LOSSES if float(_conf_value(conf, f"loss.{name}", 0.0) or 0.0) > 0.0]
-        if used:
-            raise NotImplementedError("losses on the geometric training channels are not supported by this tracer: "
-                                      + ", ".join(used))
+        def active(names):
+            return [name for name in names if float(_conf_value(conf, f"loss.{name}", 0.0) or 0.0) > 0.0]
+
+        if active(UNSUPPORTED_LOSSES):
+            raise NotImplementedError("the SOF opacity-field loss (loss.lambda_opa) is not supported by this tracer")
+        if active(GEOMETRIC_LOSSES) and not bool(_conf_value(conf, "render.enable_normals", False)):
+            raise ValueError("losses on the geometric channels (" + ", ".join(active(GEOMETRIC_LOSSES)) +
+                             ") need render.enable_normals")
         if bool(_conf_value(conf, "loss.color_confidence", False)):
             raise NotImplementedError("CoMe colour confidence (loss.color_confidence) is not rendered by this tracer")
         self._view_observation_filter = True

@@ -85,6 +85,8 @@ def load():
         "oracle_render_forward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
         "oracle_render_forward_geo": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
                                             vp, vp, vp, vp, vp, vp, vp, vp]),
+        "oracle_render_backward_geo": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
+                                             vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_render_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp,
                                          vp]),
         "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
@@ -253,6 +255,42 @@ def render_backward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorte
                                _p(np.ascontiguousarray(grad_rgba, dtype=np.float32)),
                                _p(np.ascontiguousarray(grad_hit_t, dtype=np.float32)), _p(grad))
     return grad
+
+
+def render_backward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, fwd, grads,
+                        tiles=None, pinhole=False):
+    """render_backward with the geometric channels.  fwd: render_forward_geo's
+    dict; grads: dict of output gradients (rgba, hit_t, and any of normal,
+    depth_var, extent, inv_depth, inv_depth2).  Returns (grad record [N,16],
+    shape gradient [N,8]: quaternion w,x,y,z | scale xyz, 0)."""
+    lib = load()
+    gx, gy = tile_grid(cam)
+    t0, t1 = (0, gx * gy) if tiles is None else tiles
+    n = particles.shape[0]
+    grad = np.zeros((n, 16), dtype=np.float32)
+    gshape = np.zeros((n, 8), dtype=np.float32)
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+
+    def opt(d, key):
+        return None if d.get(key) is None else _p(np.ascontiguousarray(d[key], dtype=np.float32))
+
+    keep = {key: np.ascontiguousarray(fwd[key], dtype=np.float32) for key in ("rgba", "hit_t", "normal", "depth_var")}
+    lib.oracle_render_backward_geo(ctypes.byref(cam), ctypes.byref(pose), n,
+                                   _p(np.ascontiguousarray(particles, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                                   _p(ids), int(k), int(t0), int(t1), int(bool(pinhole)), _p(keep["rgba"]),
+                                   _p(keep["hit_t"]), opt(grads, "rgba"), opt(grads, "hit_t"),
+                                   _p(keep["normal"]) if grads.get("normal") is not None else None,
+                                   opt(grads, "normal"),
+                                   _p(keep["depth_var"]) if grads.get("depth_var") is not None else None,
+                                   opt(grads, "depth_var"), opt(grads, "extent"), opt(grads, "inv_depth"),
+                                   opt(grads, "inv_depth2"), _p(grad), _p(gshape))
+    return grad, gshape
 
 
 def project_backward(pose, particles, sh, sh_degree, counts, grad_record):

@@ -1011,6 +1011,30 @@ inline bool exact_crossing(float AA, float BB, float CC, float density, float tB
     return true;
 }
 
+// d/dv of v/|v| applied to the output gradient go (safe_normalize_bw,
+// mathUtils.cuh:411-421): go/|v| - v (v . go)/|v|^3; zero for v = 0.
+inline float3_ normalize_vjp(float3_ v, float3_ go) {
+    const float l = v.x * v.x + v.y * v.y + v.z * v.z;
+    if (!(l > 0.0f)) return f3(0.0f, 0.0f, 0.0f);
+    const float il = 1.0f / std::sqrt(l);
+    const float il3 = il * il * il;
+    return f3(il * go.x - il3 * (go.x * (v.x * v.x) + go.y * (v.y * v.x) + go.z * (v.z * v.x)),
+              il * go.y - il3 * (go.x * (v.x * v.y) + go.y * (v.y * v.y) + go.z * (v.z * v.y)),
+              il * go.z - il3 * (go.x * (v.x * v.z) + go.y * (v.y * v.z) + go.z * (v.z * v.z)));
+}
+
+// d/dq (w, x, y, z) of y = M(q) p (the rows of rotate_transpose) for dL/dy = go.
+inline void rotate_transpose_vjp(const float* q, float3_ p, float3_ go, float* out) {
+    const float r = q[0], x = q[1], y = q[2], z = q[3];
+    const float G00 = go.x * p.x, G01 = go.x * p.y, G02 = go.x * p.z;
+    const float G10 = go.y * p.x, G11 = go.y * p.y, G12 = go.y * p.z;
+    const float G20 = go.z * p.x, G21 = go.z * p.y, G22 = go.z * p.z;
+    out[0] = 2.0f * (z * G01 - y * G02 - z * G10 + x * G12 + y * G20 - x * G21);
+    out[1] = 2.0f * (y * G01 + z * G02 + y * G10 + r * G12 + z * G20 - r * G21) - 4.0f * x * (G11 + G22);
+    out[2] = 2.0f * (x * G01 - r * G02 + x * G10 + z * G12 + r * G20 + z * G21) - 4.0f * y * (G00 + G22);
+    out[3] = 2.0f * (r * G01 + x * G02 - r * G10 + y * G12 + x * G20 + y * G21) - 4.0f * z * (G00 + G11);
+}
+
 void geo_hit(GeoState& g, const Ray& ray, const Particle& P, float hitT, float w, float tBefore, float tAfter) {
     const float3_ grdu = fmatvec(P.Binv, ray.d);
     const float len = std::sqrt(fdot(grdu, grdu));
@@ -1436,6 +1460,187 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
         if (partial[size_t(t)].empty()) continue;
         const float* a = partial[size_t(t)].data();
         for (size_t i = 0; i < size_t(N) * 16; ++i) gradRecord[i] += a[i];
+    }
+    return 0;
+}
+
+// The backward of oracle_render_backward with the geometric training
+// channels (gaussianParticles.cuh:786-1062): each channel pointer pair (value,
+// gradient) may be NULL.  The depth moment and the normal sum reach alpha
+// through their residuals, the depth moment and the inverse-depth moments
+// reach the closest-point parameter tau, the normal reaches B^-1 and the
+// canonical direction, and the extent reaches the intrinsic quaternion and
+// scale only, accumulated into gradShape[N*8] (quaternion w,x,y,z | scale xyz, 0).
+int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                               const float* rgb, const float* rayO, const float* rayD, const uint8_t* mask,
+                               const uint32_t* ranges, const uint32_t* sortedIds, int K, int tileBegin, int tileEnd,
+                               int pinhole, const float* rgba, const float* hitT, const float* gradRgba,
+                               const float* gradHitT, const float* normal, const float* gradNormal,
+                               const float* depthVar, const float* gradDepthVar, const float* gradExtent,
+                               const float* gradInvD, const float* gradInvD2, float* gradRecord, float* gradShape) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile;
+    Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
+    const int nthreads = worker_count();
+    std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads)), partialShape(static_cast<size_t>(nthreads));
+    const auto val = [](const float* p, size_t i) { return p != nullptr ? p[i] : 0.0f; };
+    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int tid) {
+        std::vector<float>& acc = partial[size_t(tid)];
+        std::vector<float>& accS = partialShape[size_t(tid)];
+        if (acc.empty()) acc.assign(size_t(N) * 16, 0.0f);
+        if (accS.empty()) accS.assign(size_t(N) * 8, 0.0f);
+        if (mask[tile] == 0u) return;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                const float featB[3] = {rgba[4 * pix], rgba[4 * pix + 1], rgba[4 * pix + 2]};
+                const float featG[3] = {gradRgba[4 * pix], gradRgba[4 * pix + 1], gradRgba[4 * pix + 2]};
+                const float TB = 1.0f - rgba[4 * pix + 3];
+                const float TG = -1.0f * gradRgba[4 * pix + 3];
+                const float hitTB = hitT[pix];
+                const float hitTG = gradHitT[pix];
+                float nB[3], nG[3];
+                for (int k = 0; k < 3; ++k) {
+                    nB[k] = val(normal, 3 * pix + k);
+                    nG[k] = normal != nullptr ? val(gradNormal, 3 * pix + k) : 0.0f;
+                }
+                const float wd2B = val(depthVar, pix);
+                const float wd2G = depthVar != nullptr ? val(gradDepthVar, pix) : 0.0f;
+                const float extG = val(gradExtent, pix), invDG = val(gradInvD, pix), invD2G = val(gradInvD2, pix);
+                const float dscale = pinhole ? rayD[3 * pix + 2] : 1.0f;
+                float T = 1.0f, depth = 0.0f, wd2 = 0.0f;
+                float nRun[3] = {0.0f, 0.0f, 0.0f};
+                float radiance[3] = {0.0f, 0.0f, 0.0f};
+                bool alive = true;
+                traverse(sc, uint32_t(tile), ray, alive, [&](const Hit& hh) {
+                    const Particle P = load_particle(particles + 32 * size_t(hh.idx));
+                    const HalfRay h = half_ray(ray, P);
+                    if (h.valid) {
+                        const float grayDist = fdot(h.p, h.p);
+                        const float gres = gf::gf_expf(-0.5f * grayDist);
+                        const float galphaU = gres * P.density;
+                        const float galpha = gf::min_f(kMaxAlpha, galphaU);
+                        if (gres > kMinKernelResponse && galpha > kAlphaThreshold) {
+                            const float gdist = h.tau;
+                            const float weight = galpha * T;
+                            const float nextT = (1.0f - galpha) * T;
+                            const bool tail = nextT <= kMinTransmittance;
+                            depth = depth + gdist * weight;
+                            const float residualHitT = gf::max_f(tail ? 0.0f : (hitTB - depth) / nextT, 0.0f);
+                            const float galphaRayHitGrd = (gdist - residualHitT) * T * hitTG;
+                            const float residualTrm = galpha < 0.999999f ? TB / (1.0f - galpha) : T;
+                            const float galphaRayDnsGrd = residualTrm * -TG;
+                            const float* c = rgb + 3 * size_t(hh.idx);
+                            float col[3], resid[3];
+                            for (int k = 0; k < 3; ++k) {
+                                col[k] = gf::max_f(c[k], 0.0f);
+                                radiance[k] = fmaf_rn(col[k], weight, radiance[k]);
+                            }
+                            for (int k = 0; k < 3; ++k)
+                                resid[k] = gf::max_f(tail ? 0.0f : (featB[k] - radiance[k]) / nextT, 0.0f);
+                            float comp = galphaRayHitGrd + galphaRayDnsGrd;
+                            for (int k = 0; k < 3; ++k) comp += T * (col[k] - resid[k]) * featG[k];
+                            float tauGrad = weight * hitTG;
+                            // depth moment
+                            const float gsq = gdist * gdist;
+                            wd2 = fmaf_rn(weight * gdist, gdist, wd2);
+                            const float residualWD2 = gf::max_f(tail ? 0.0f : (wd2B - wd2) / nextT, 0.0f);
+                            comp += (gsq - residualWD2) * T * wd2G;
+                            tauGrad += 2.0f * gdist * weight * wd2G;
+                            // inverse-depth moments
+                            const float dd = gdist * dscale;
+                            if (dd > kParticleMinSensorZ) {
+                                tauGrad += (-weight / (dscale * gdist * gdist)) * invDG;
+                                tauGrad += (-2.0f * weight / ((dscale * dscale) * gdist * gdist * gdist)) * invD2G;
+                            }
+                            // normal
+                            const float len = std::sqrt(h.denom);
+                            const float3_ grd = f3(h.grdu.x / len, h.grdu.y / len, h.grdu.z / len);
+                            const float* M = P.Binv;
+                            const float3_ nu = f3(fmaf_rn(M[6], grd.z, fmaf_rn(M[3], grd.y, M[0] * grd.x)),
+                                                  fmaf_rn(M[7], grd.z, fmaf_rn(M[4], grd.y, M[1] * grd.x)),
+                                                  fmaf_rn(M[8], grd.z, fmaf_rn(M[5], grd.y, M[2] * grd.x)));
+                            const float inv = -1.0f / std::sqrt(fdot(nu, nu));
+                            const float n[3] = {inv * nu.x, inv * nu.y, inv * nu.z};
+                            for (int k = 0; k < 3; ++k) nRun[k] = fmaf_rn(weight, n[k], nRun[k]);
+                            float resN[3];
+                            for (int k = 0; k < 3; ++k) resN[k] = tail ? 0.0f : (nB[k] - nRun[k]) / nextT;
+                            comp += T * ((n[0] - resN[0]) * nG[0] + (n[1] - resN[1]) * nG[1] + (n[2] - resN[2]) * nG[2]);
+                            const float3_ nuGrd = normalize_vjp(nu, f3(-weight * nG[0], -weight * nG[1], -weight * nG[2]));
+                            const float gdv[3] = {grd.x, grd.y, grd.z};
+                            const float ngv[3] = {nuGrd.x, nuGrd.y, nuGrd.z};
+                            float gBinvN[9];
+                            for (int i = 0; i < 3; ++i)
+                                for (int j = 0; j < 3; ++j) gBinvN[3 * i + j] = gdv[i] * ngv[j];
+                            const float3_ grdGrd = fmatvec(M, nuGrd);
+                            const float3_ grduGeo = normalize_vjp(h.grdu, grdGrd);
+                            // extent
+                            const float3_ rd = rotate_transpose(P.quat, ray.d);
+                            const float3_ sd = f3(P.scale[0] * rd.x, P.scale[1] * rd.y, P.scale[2] * rd.z);
+                            const float sigma = std::sqrt(fdot(sd, sd) + 1e-18f);
+                            const float nGe = (weight * extG) / sigma;
+                            const float3_ rdGrd = f3(nGe * (P.scale[0] * P.scale[0] * rd.x),
+                                                     nGe * (P.scale[1] * P.scale[1] * rd.y),
+                                                     nGe * (P.scale[2] * P.scale[2] * rd.z));
+                            float gq[4];
+                            rotate_transpose_vjp(P.quat, ray.d, rdGrd, gq);
+                            float* gs = accS.data() + 8 * size_t(hh.idx);
+                            for (int k = 0; k < 4; ++k) gs[k] += gq[k];
+                            gs[4] += nGe * (P.scale[0] * rd.x * rd.x);
+                            gs[5] += nGe * (P.scale[1] * rd.y * rd.y);
+                            gs[6] += nGe * (P.scale[2] * rd.z * rd.z);
+                            // alpha, response, closest point
+                            const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
+                            float* g = acc.data() + 16 * size_t(hh.idx);
+                            g[3] += gres * gU;
+                            const float gresGrd = P.density * gU;
+                            const float grayDistGrd = -0.5f * gres * gresGrd;
+                            const float3_ pointGrad = scale(2.0f * grayDistGrd, h.p);
+                            float3_ groGrd = pointGrad;
+                            float3_ grduGrd = scale(h.tau, pointGrad);
+                            const float totalTauGrad = tauGrad + dot(pointGrad, h.grdu);
+                            if (h.interior) {
+                                const float3_ tauOriginGrad = scale(-1.0f / h.denom, h.grdu);
+                                const float3_ tauDirectionGrad =
+                                    add(scale(-1.0f / h.denom, h.gro), scale((2.0f * h.num) / (h.denom * h.denom), h.grdu));
+                                groGrd = add(groGrd, scale(totalTauGrad, tauOriginGrad));
+                                grduGrd = add(grduGrd, scale(totalTauGrad, tauDirectionGrad));
+                            }
+                            g[0] -= groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6];
+                            g[1] -= groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7];
+                            g[2] -= groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8];
+                            const float3_ gposc = sub(ray.o, P.pos);
+                            const float gr[3] = {groGrd.x, groGrd.y, groGrd.z};
+                            const float gd[3] = {grduGrd.x, grduGrd.y, grduGrd.z};
+                            const float gn[3] = {grduGeo.x, grduGeo.y, grduGeo.z};
+                            for (int r = 0; r < 3; ++r) {
+                                g[4 + 3 * r + 0] += gr[r] * gposc.x + gd[r] * ray.d.x + (gBinvN[3 * r + 0] + gn[r] * ray.d.x);
+                                g[4 + 3 * r + 1] += gr[r] * gposc.y + gd[r] * ray.d.y + (gBinvN[3 * r + 1] + gn[r] * ray.d.y);
+                                g[4 + 3 * r + 2] += gr[r] * gposc.z + gd[r] * ray.d.z + (gBinvN[3 * r + 2] + gn[r] * ray.d.z);
+                            }
+                            for (int k = 0; k < 3; ++k) g[13 + k] += featG[k] * weight;
+                            T = nextT;
+                        }
+                    }
+                    if (T < kMinTransmittance) alive = false;
+                });
+            }
+        }
+    });
+    std::memset(gradRecord, 0, sizeof(float) * size_t(N) * 16);
+    std::memset(gradShape, 0, sizeof(float) * size_t(N) * 8);
+    for (int t = 0; t < nthreads; ++t) {
+        if (!partial[size_t(t)].empty()) {
+            const float* a = partial[size_t(t)].data();
+            for (size_t i = 0; i < size_t(N) * 16; ++i) gradRecord[i] += a[i];
+        }
+        if (!partialShape[size_t(t)].empty()) {
+            const float* a = partialShape[size_t(t)].data();
+            for (size_t i = 0; i < size_t(N) * 8; ++i) gradShape[i] += a[i];
+        }
     }
     return 0;
 }

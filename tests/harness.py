@@ -120,14 +120,26 @@ class GpuTracer:
             res[name] = t.cpu().numpy()
         return res
 
-    def backward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray):
+    def backward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray, geometry: dict | None = None):
+        """geometry: output gradients of the geometric channels by name (normal,
+        depth_var, extent, inv_depth, inv_depth2), [H,W] or [H,W,3] arrays."""
         torch = self.torch
         g_rgba = torch.from_numpy(grad_rgba).to(self.device)
         g_hit = torch.from_numpy(grad_hit[..., None].copy()).to(self.device)
-        zeros = [torch.zeros(1, device=self.device)] * 14
+        pairs = [torch.zeros(1, device=self.device)] * 14
+        if geometry:
+            names = ("depth_var", "extent", "opacity_field", "quant", "normal", "inv_depth", "inv_depth2")
+            index = {"depth_var": 5, "extent": 7, "opacity_field": 8, "quant": 6, "normal": 4, "inv_depth": 9,
+                     "inv_depth2": 10}
+            pairs = []
+            for name in names:
+                value = self.out[index[name]]
+                grad = geometry.get(name)
+                pairs += [value, None if grad is None else
+                          torch.from_numpy(np.ascontiguousarray(grad, np.float32)).to(self.device).reshape(value.shape)]
         gp, gs = self.raster.trace_bwd(0, False, self.case.scene.sh_degree, self.particles, self.features, self.ray_o,
                                        self.ray_d, None, self.sensor, 0, 1, self.pose, self.pose, self.out[0], g_rgba,
-                                       self.out[1], g_hit, *zeros, self.token)
+                                       self.out[1], g_hit, *pairs, self.token)
         torch.cuda.synchronize(self.device)
         return gp.cpu().numpy(), gs.cpu().numpy()
 

@@ -29,8 +29,11 @@ class FakeRaster:
         return rgba, hit, count, vis, z(3), z(1), z(10), z(1), z(1), z(1), z(1)
 
     def trace_bwd(self, frame_id, sof, n_active, density, features, ray_ori, ray_dir, ray_time, sensor, t0, t1, p0, p1,
-                  rgba, grad_rgba, hit, grad_hit, token):
-        self.calls.append(("trace_bwd", grad_rgba.clone(), None if grad_hit is None else grad_hit.clone(), token))
+                  rgba, grad_rgba, hit, grad_hit, *geometry_and_token):
+        *geometry, token = geometry_and_token
+        assert len(geometry) == 14
+        self.calls.append(("trace_bwd", grad_rgba.clone(), None if grad_hit is None else grad_hit.clone(), token,
+                           geometry))
         # row gradient = slot index + 100 * row, so the split is visible
         slots = torch.arange(32, dtype=torch.float32)[None, :]
         rows = torch.arange(self.n, dtype=torch.float32)[:, None]
@@ -81,7 +84,7 @@ def test_gradient_split_and_order():
     assert len(outs) == 11
     g = torch.randn(raster.h, raster.w, 4)
     (outs[0] * g).sum().backward()
-    kind, grad_rgba, grad_hit, _token = raster.calls[1]
+    kind, grad_rgba, grad_hit, _token, _geometry = raster.calls[1]
     assert kind == "trace_bwd"
     assert torch.equal(grad_rgba, g)
     assert grad_hit is None
@@ -107,7 +110,7 @@ def test_hit_distance_only_loss_sends_zero_colour_gradient():
     x = _inputs(n)
     outs = _apply(raster, x, n)
     outs[1].sum().backward()
-    _kind, grad_rgba, grad_hit, _ = raster.calls[1]
+    _kind, grad_rgba, grad_hit, _, _geometry = raster.calls[1]
     assert not bool(grad_rgba.any())
     assert torch.equal(grad_hit, torch.ones_like(grad_hit))
 
@@ -123,8 +126,26 @@ def test_confidence_is_refused():
                                x["idns"], x["fac"], x["inv"], x["sph"], None, poses, torch.ones((n, 1)))
 
 
-@pytest.mark.parametrize("loss", ["lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_opa", "lambda_extent",
+def test_opacity_field_loss_is_refused():
+    with pytest.raises(NotImplementedError, match="lambda_opa"):
+        Tracer({"render": {"enable_normals": True}, "loss": {"lambda_opa": 0.004}})
+
+
+@pytest.mark.parametrize("loss", ["lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_extent",
                                   "lambda_normal_variance"])
-def test_geometric_losses_are_refused(loss):
-    with pytest.raises(NotImplementedError, match=loss):
+def test_geometric_losses_need_normals(loss):
+    with pytest.raises(ValueError, match=loss):
         Tracer({"render": {}, "loss": {loss: 0.01}})
+
+
+def test_geometric_channel_gradients_reach_trace_bwd():
+    n = 4
+    raster = FakeRaster(n)
+    x = _inputs(n)
+    outs = _apply(raster, x, n)
+    (outs[0].sum() + 2.0 * outs[4].sum() + 3.0 * outs[5].sum()).backward()
+    geometry = raster.calls[1][4]
+    # pairs in the reference's order: depth var, extent, opacity field, quant, normal, inv depth, inv depth^2
+    assert torch.equal(geometry[1], torch.full((raster.h, raster.w, 1), 3.0))  # depth var gradient
+    assert torch.equal(geometry[9], torch.full((raster.h, raster.w, 3), 2.0))  # normal gradient
+    assert geometry[3] is None and geometry[5] is None and geometry[7] is None

@@ -311,3 +311,44 @@ def test_geometric_channels_forward(cuda_device, k):
     q = got["quant"][valid]
     assert np.all((q[:, 8] > 0) & (q[:, :7] > 0).all(axis=1))
     assert np.count_nonzero(q[:, 9]) > 0
+
+
+@pytest.mark.parametrize("k,log_capacity", [(16, 0), (16, -1), (16, 6), (0, 0)])
+def test_geometric_channels_backward(cuda_device, k, log_capacity):
+    """Gradients of the normal sum, sum w t^2, extent and inverse-depth
+    moments (with colour and hit-distance gradients) match the oracle's
+    restatement of processHitBwd's geometric terms, through the log backward,
+    the replay and their mix; the extent's gradient reaches the rotation and
+    scale slots of the row gradient."""
+    import oracle
+
+    case = harness.small_case(seed=29, n=15_000, size=192)
+    ref = harness.oracle_forward(case, k, 0)
+    fwd = oracle.render_forward_geo(case.ocam, ref["pose"], case.particles, ref["rgb"], case.ray_o, case.ray_d,
+                                    case.tmask, ref["ranges"], ref["ids"], k)
+    gpu = harness.GpuTracer(case, k, 0, cuda_device, log_capacity=log_capacity, enable_normals=True)
+    got = gpu.forward()
+    np.testing.assert_array_equal(got["normal"], fwd["normal"])
+    rng = np.random.default_rng(31)
+    h, w = case.camera.height, case.camera.width
+    grads = {"rgba": rng.standard_normal((h, w, 4)).astype(np.float32),
+             "hit_t": (0.1 * rng.standard_normal((h, w))).astype(np.float32),
+             "normal": rng.standard_normal((h, w, 3)).astype(np.float32),
+             "depth_var": (0.05 * rng.standard_normal((h, w))).astype(np.float32),
+             "extent": rng.standard_normal((h, w)).astype(np.float32),
+             "inv_depth": rng.standard_normal((h, w)).astype(np.float32),
+             "inv_depth2": rng.standard_normal((h, w)).astype(np.float32)}
+    rec, shape = oracle.render_backward_geo(case.ocam, ref["pose"], case.particles, ref["rgb"], case.ray_o,
+                                            case.ray_d, case.tmask, ref["ranges"], ref["ids"], k, fwd, grads)
+    gp_ref, gs_ref = oracle.project_backward(ref["pose"], case.particles, case.features, case.scene.sh_degree,
+                                             ref["counts"], rec)
+    gp_ref = gp_ref.copy()
+    gp_ref[:, 4:8] += shape[:, 0:4]
+    gp_ref[:, 8:11] += shape[:, 4:7]
+    geometry = {name: grads[name] for name in ("normal", "depth_var", "extent", "inv_depth", "inv_depth2")}
+    gp, gs = gpu.backward(grads["rgba"], grads["hit_t"], geometry)
+    for cols, name in ((slice(0, 3), "position"), (slice(3, 4), "density"), (slice(4, 8), "rotation"),
+                       (slice(8, 11), "scale"), (slice(21, 30), "inverse factor")):
+        assert float(np.linalg.norm(gp_ref[:, cols])) > 0.0, name
+        assert harness.rel_l2(gp[:, cols], gp_ref[:, cols]) <= GRAD_RTOL_L2, name
+    assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2

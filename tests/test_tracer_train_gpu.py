@@ -96,14 +96,31 @@ def test_forward_equals_composed_pipeline_and_oracle(view, cuda_device):
     assert float(want["rgba"][..., 3].max()) > 0.5
 
 
-def test_gradients_match_the_oracle_chain(view, cuda_device):
+@pytest.mark.parametrize("geometry", [False, True])
+def test_gradients_match_the_oracle_chain(view, cuda_device, geometry):
+    """geometry: render.enable_normals with a loss on the normal, depth-moment,
+    extent and inverse-depth channels besides the colour."""
     scene, cam, batch, valid = view
     model = SceneGaussians.from_scene(scene, cuda_device, requires_grad=True)
-    out = Tracer(_conf()).render(model, batch, train=True)
+    conf = _conf()
+    conf["render"]["enable_normals"] = geometry
+    out = Tracer(conf).render(model, batch, train=True)
     rng = np.random.default_rng(5)
     g_rgba = rng.uniform(-1.0, 1.0, (cam.height, cam.width, 4)).astype(np.float32)
     g = torch.from_numpy(g_rgba).to(cuda_device)
     loss = (out["pred_features"][0] * g[..., :3]).sum() + (out["pred_opacity"][0] * g[..., 3:]).sum()
+    h, w = cam.height, cam.width
+    geo_grads = {"normal": rng.standard_normal((h, w, 3)).astype(np.float32),
+                 "depth_var": (0.05 * rng.standard_normal((h, w))).astype(np.float32),
+                 "extent": rng.standard_normal((h, w)).astype(np.float32),
+                 "inv_depth": rng.standard_normal((h, w)).astype(np.float32),
+                 "inv_depth2": rng.standard_normal((h, w)).astype(np.float32)}
+    if geometry:
+        keys = {"normal": "pred_normals", "depth_var": "pred_depth_var", "extent": "pred_extent",
+                "inv_depth": "pred_invd", "inv_depth2": "pred_invd2"}
+        for name, key in keys.items():
+            gg = torch.from_numpy(geo_grads[name]).to(cuda_device).reshape(out[key].shape)
+            loss = loss + (out[key] * gg).sum()
     loss.backward()
 
     # oracle chain on the same view: render + projection backward, then the full-shape VJP
@@ -114,9 +131,20 @@ def test_gradients_match_the_oracle_chain(view, cuda_device):
     ocam = harness.oracle_camera(cam)
     ro, rd, tm = batch.rays_ori[0].cpu().numpy(), batch.rays_dir[0].cpu().numpy(), harness.tile_mask(valid)
     fwd = oracle.trace(ocam, poses.T_world_sensors[0], packed, scene.features, 3, ro, rd, tm, K, 0)
-    gp, gsh, _ = oracle.trace_backward(ocam, fwd, packed, scene.features, 3, ro, rd, tm, K, g_rgba,
-                                       np.zeros((cam.height, cam.width), np.float32))
-    gp = gp.astype(np.float64)
+    if geometry:
+        geo_fwd = oracle.render_forward_geo(ocam, fwd["pose"], packed, fwd["rgb"], ro, rd, tm, fwd["ranges"],
+                                            fwd["ids"], K)
+        grads = dict(geo_grads, rgba=g_rgba, hit_t=np.zeros((h, w), np.float32))
+        rec, shape = oracle.render_backward_geo(ocam, fwd["pose"], packed, fwd["rgb"], ro, rd, tm, fwd["ranges"],
+                                                fwd["ids"], K, geo_fwd, grads)
+        gp, gsh = oracle.project_backward(fwd["pose"], packed, scene.features, 3, fwd["counts"], rec)
+        gp = gp.astype(np.float64)
+        gp[:, 4:8] += shape[:, 0:4]
+        gp[:, 8:11] += shape[:, 4:7]
+    else:
+        gp, gsh, _ = oracle.trace_backward(ocam, fwd, packed, scene.features, 3, ro, rd, tm, K, g_rgba,
+                                           np.zeros((cam.height, cam.width), np.float32))
+        gp = gp.astype(np.float64)
     q = q6.cpu().numpy()
     Q = np.stack([q[:, 0], q[:, 1], q[:, 2], q[:, 1], q[:, 3], q[:, 4], q[:, 2], q[:, 4], q[:, 5]], 1).reshape(-1, 3, 3)
     n = scene.num
@@ -137,9 +165,9 @@ def test_gradients_match_the_oracle_chain(view, cuda_device):
         assert harness.rel_l2(got.cpu().numpy(), w) <= 1e-3, name
 
 
-def test_geometric_losses_are_refused():
-    with pytest.raises(NotImplementedError, match="lambda_dnc"):
-        Tracer({"render": {}, "loss": {"lambda_dnc": 0.05}})
+def test_opacity_field_loss_is_refused():
+    with pytest.raises(NotImplementedError, match="lambda_opa"):
+        Tracer({"render": {"enable_normals": True}, "loss": {"lambda_opa": 0.004}})
 
 
 def test_shape_failure_is_raised_by_render(view, cuda_device):

@@ -58,6 +58,7 @@ struct gf_tracer {
     DeviceBuffer gradRecords;
     DeviceBuffer gradShape;  // extent gradient: quaternion, intrinsic scale [N,2] float4 (enable_normals)
     DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
+    DeviceBuffer wideList;                                // projected particles with a large tile box
     DeviceBuffer logIds, logCount, logOverflow, logList;  // composite log of the last training forward
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
     gf::CompositeLog frameLog{};
@@ -285,10 +286,13 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     fa.enabled = t->cfg.admission_fallback == GF_FALLBACK_CONE ? 1 : 0;
     if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
-    if (int e = t->bigCount.ensure(sizeof(uint32_t), stream)) return e;
+    if (int e = t->bigCount.ensure(sizeof(uint32_t) * 2, stream)) return e;
+    if (int e = t->wideList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
     fa.caps = t->caps.as<float4>();
     fa.big = t->bigList.as<uint32_t>();
     fa.bigCount = t->bigCount.as<uint32_t>();
+    fa.wide = t->wideList.as<uint32_t>();
+    fa.wideCount = t->bigCount.as<uint32_t>() + 1;
     {
         StageTimer st(t, GF_STAGE_TILE_RAYS, stream);
         if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
@@ -342,7 +346,7 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     }
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT, stream);
-        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, sizeof(uint32_t), stream));
+        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, 2 * sizeof(uint32_t), stream));  // fallback and wide lists
         gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
                                                           t->proj.as<float4>(), t->records.as<float4>(),
                                                           t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),
@@ -356,6 +360,12 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }
+        gf::k_wide<false><<<148 * 8, 256, 0, stream>>>(f, fa, mask->buf.as<uint8_t>(), t->proj.as<float4>(),
+                                                      t->records.as<float4>(), t->tileRays.as<float4>(),
+                                                      t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),
+                                                      nullptr, nullptr, nullptr);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
     }
     {
         StageTimer st(t, GF_STAGE_SCAN, stream);
@@ -394,6 +404,12 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }
+        gf::k_wide<true><<<148 * 8, 256, 0, stream>>>(f, fa, mask->buf.as<uint8_t>(), t->proj.as<float4>(),
+                                                     t->records.as<float4>(), t->tileRays.as<float4>(),
+                                                     t->counts.as<uint32_t>(), nullptr, t->offsets.as<uint64_t>(),
+                                                     t->keys[0].as<uint64_t>(), t->ids[0].as<uint32_t>());
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
     }
     const int endBit = 32 + int(bit_length(T));
     {
@@ -501,7 +517,8 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaGetDevice(&prev);
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
-        for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount}) b->release();
+        for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount, &t->wideList})
+            b->release();
         for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow, &t->logList}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],

@@ -619,7 +619,18 @@ struct FallbackArgs {
     float4* caps;       // [N,2] for particles without a valid projection: (u, cos), (sin, mode, 0, 0)
     uint32_t* big;      // particles left to the warp kernel
     uint32_t* bigCount;
+    uint32_t* wide;     // projected particles whose tile box exceeds kWideTiles, left to k_wide
+    uint32_t* wideCount;
 };
+
+// Projected particles whose tile bounding box holds more tiles than this are
+// counted and emitted by one warp (k_wide) instead of one thread, so that a
+// large Gaussian near the camera does not serialise thousands of tile tests.
+constexpr int kWideTiles = 64;
+
+__device__ __forceinline__ bool wide_box(const TileBox& b) {
+    return (b.x1 - b.x0) * (b.y1 - b.y0) > kWideTiles;
+}
 
 __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __restrict__ particles,
                                                  const float* __restrict__ features,
@@ -673,7 +684,9 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
     rec[2] = make_float4(r6.y, r6.z, r6.w, r7.x);
     rec[3] = make_float4(r7.y, rgb[0], rgb[1], rgb[2]);
 
-    const uint32_t n = for_admitted_tiles(f, mask, p, [](int, int, uint32_t) {});
+    bool wide = false;
+    if (fast_ut_valid(p)) wide = wide_box(tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey));
+    const uint32_t n = wide ? 0u : for_admitted_tiles(f, mask, p, [](int, int, uint32_t) {});
     bool deferred = false;
     if (!fast_ut_valid(p)) {
         // Without a valid projection: the cone fallback, left to the warp
@@ -698,9 +711,19 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
         base = __shfl_sync(live, base, leader);
         if (deferred) fa.big[base + uint32_t(__popc(dm & ((1u << lane) - 1u)))] = i;
     }
+    // warp-aggregated append to the wide list
+    const uint32_t wm = __ballot_sync(live, wide);
+    if (wm != 0u) {
+        const uint32_t lane = threadIdx.x & 31u;
+        const int leader = __ffs(wm) - 1;
+        uint32_t base = 0u;
+        if (int(lane) == leader) base = atomicAdd(fa.wideCount, uint32_t(__popc(wm)));
+        base = __shfl_sync(live, base, leader);
+        if (wide) fa.wide[base + uint32_t(__popc(wm & ((1u << lane) - 1u)))] = i;
+    }
     counts[i] = n;
-    if (visibility != nullptr && !deferred) visibility[i] = n ? 1u : 0u;
-    if (n != 0u || deferred) {
+    if (visibility != nullptr && !deferred && !wide) visibility[i] = n ? 1u : 0u;
+    if (n != 0u || deferred || wide) {
         const float Binv[9] = {r5.y, r5.z, r5.w, r6.x, r6.y, r6.z, r6.w, r7.x, r7.y};
         bounds[i] = support_radius(Binv);
     }
@@ -756,6 +779,77 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
     }
 }
 
+// Wide projected particles (tile box above kWideTiles): one warp each walks
+// the box 32 tiles at a time with the same admission tests as
+// for_admitted_tiles, counting (kEmit false) or emitting keys at the scanned
+// offsets.  The admitted set is the per-thread walk's; only the order inside
+// one particle's keys differs, and the sorted output does not depend on it
+// (one particle's keys name distinct tiles).
+template <bool kEmit>
+__global__ __launch_bounds__(256) void k_wide(FrameArgs f, FallbackArgs fa, const uint8_t* __restrict__ mask,
+                                              const float4* __restrict__ proj, const float4* __restrict__ records,
+                                              const float4* __restrict__ tileRays, uint32_t* __restrict__ counts,
+                                              uint32_t* __restrict__ visibility, const uint64_t* __restrict__ offsets,
+                                              uint64_t* __restrict__ keys, uint32_t* __restrict__ ids) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t below = (1u << lane) - 1u;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t total = *fa.wideCount;
+    for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+        const uint32_t i = fa.wide[w];
+        const float4 p0 = proj[2 * i], p1 = proj[2 * i + 1];
+        Projected p;
+        p.cx = p0.x; p.cy = p0.y; p.conic0 = p0.z; p.conic1 = p0.w;
+        p.conic2 = p1.x; p.opacity = p1.y; p.ex = p1.z; p.ey = p1.w;
+        const TileBox b = tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey);
+        const float maxPower = gf_logf(p.opacity / kAlphaThreshold) * 1.0f;
+        const int bw = b.x1 - b.x0;
+        const uint32_t area = uint32_t(bw * (b.y1 - b.y0));
+        V3 mu{};
+        float Binv[9] = {};
+        float camRadial = 0.0f;
+        uint64_t begin = 0;
+        uint32_t reserved = 0;
+        if constexpr (kEmit) {
+            const float4 a = records[4 * size_t(i)], rb = records[4 * size_t(i) + 1], rc = records[4 * size_t(i) + 2],
+                         rd = records[4 * size_t(i) + 3];
+            mu = v3(a.x, a.y, a.z);
+            const float bi[9] = {rb.x, rb.y, rb.z, rb.w, rc.x, rc.y, rc.z, rc.w, rd.x};
+#pragma unroll
+            for (int k = 0; k < 9; ++k) Binv[k] = bi[k];
+            const V3 cv = mu - v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]);
+            camRadial = finite_nonneg(__fsqrt_rn(dot3(cv, cv)), kMaxDepthValue);
+            begin = offsets[i];
+            reserved = counts[i];
+        }
+        uint32_t n = 0;
+        for (uint32_t base = 0; base < area; base += 32u) {
+            const uint32_t t = base + lane;
+            bool ok = false;
+            int x = 0, y = 0;
+            if (t < area) {
+                x = b.x0 + int(t % uint32_t(bw));
+                y = b.y0 + int(t / uint32_t(bw));
+                ok = mask[y * f.gx + x] != 0u && tile_min_power(x, y, p) < maxPower;
+            }
+            const uint32_t m = __ballot_sync(0xffffffffu, ok);
+            if constexpr (kEmit) {
+                const uint32_t k = n + uint32_t(__popc(m & below));
+                if (ok && k < reserved) {
+                    const uint32_t tile = uint32_t(y * f.gx + x);
+                    keys[begin + k] = (uint64_t(tile) << 32) | tile_depth_key(f.keyMode, mu, Binv, camRadial, tileRays, tile);
+                    ids[begin + k] = i;
+                }
+            }
+            n += uint32_t(__popc(m));
+        }
+        if (!kEmit && lane == 0) {
+            counts[i] = n;
+            if (visibility != nullptr) visibility[i] = n ? 1u : 0u;
+        }
+    }
+}
+
 // Emits (tile << 32 | depth bits) keys and particle ids at the scanned offsets
 // (reference expandTileProjections, gutProjector.cuh:947-1113).
 __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restrict__ proj,
@@ -770,6 +864,7 @@ __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restr
     p.cx = p0.x; p.cy = p0.y; p.conic0 = p0.z; p.conic1 = p0.w;
     p.conic2 = p1.x; p.opacity = p1.y; p.ex = p1.z; p.ey = p1.w;
     if (!fast_ut_valid(p)) return;  // cone-fallback particles: k_fallback_big<true>
+    if (wide_box(tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey))) return;  // k_wide<true>
     const float4 a = records[4 * size_t(i)], b = records[4 * size_t(i) + 1], c = records[4 * size_t(i) + 2],
                  d = records[4 * size_t(i) + 3];
     const V3 mu = v3(a.x, a.y, a.z);

@@ -242,11 +242,12 @@ int dispatch_bwd(int K, const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t
     return GF_OK;
 }
 
-// Composite log capacity: entries per pixel (128 covers the deepest pixels of
-// the 1M-Gaussian 200 deg view; deeper tiles are replayed), bounded so that
-// the log stays within 4 GiB.
-constexpr uint32_t kLogCapacity = 128;
-constexpr size_t kLogBudgetBytes = size_t(4) << 30;
+// Composite log capacity: entries per pixel (256 covers the deepest pixels of
+// the 1M-Gaussian 200 deg view with the 0.3 px^2 footprint; a tile with a
+// deeper pixel is replayed through the k-buffer, at several times the cost of
+// the log backward), bounded so that the log stays within 8 GiB.
+constexpr uint32_t kLogCapacity = 256;
+constexpr size_t kLogBudgetBytes = size_t(8) << 30;
 
 // Projection, binning, sort and forward composite; a training forward
 // (logComposites) also records the composite log for the backward.

@@ -73,7 +73,7 @@ typedef struct gf_tracer_config {
     int32_t enable_hit_counts; /* 1: write the per-pixel hit count */
     int32_t admission_fallback; /* GF_FALLBACK_*: admission of particles without a valid projection */
     int32_t composite_log_capacity; /* entries per pixel of the training forward's composite log, read by the
-                                       backward: 0 = default (128), < 0 = no log (the backward replays every
+                                       backward: 0 = default (256), < 0 = no log (the backward replays every
                                        tile through the k-buffer) */
     int32_t enable_normals;         /* render.enable_normals: 1 computes the geometric training channels
                                        (gf_trace_outputs.normal ... inv_depth2) and their gradients */

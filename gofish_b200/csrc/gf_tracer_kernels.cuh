@@ -672,10 +672,14 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
     const float* c = features + size_t(i) * 3 * f.shCoeffs;
     const int nb = min(sh_count(f.shDegree), int(f.shCoeffs));
     float rgb[3];
+    // loops unrolled over all 16 coefficients with a predicate, so that the
+    // basis stays in registers (a runtime bound would put it in local memory)
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
         float acc = basis[0] * __ldg(c + ch);
-        for (int k = 1; k < nb; ++k) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
+#pragma unroll
+        for (int k = 1; k < 16; ++k)
+            if (k < nb) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
         rgb[ch] = fmaxf(acc + 0.5f, 0.0f);
     }
     float4* rec = records + 4 * size_t(i);
@@ -926,17 +930,25 @@ __global__ __launch_bounds__(256) void k_project_bwd(FrameArgs f, const float* _
         const float* c = features + size_t(i) * 3 * f.shCoeffs;
         const float gr[3] = {g3.y, g3.z, g3.w};
         V3 dg = v3(0.0f, 0.0f, 0.0f);
+        // unrolled with predicates: the basis arrays stay in registers
 #pragma unroll
         for (int ch = 0; ch < 3; ++ch) {
             float acc = basis[0] * __ldg(c + ch);
-            for (int k = 1; k < nb; ++k) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
+#pragma unroll
+            for (int k = 1; k < 16; ++k)
+                if (k < nb) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
             const float m = (acc + 0.5f) > 0.0f ? gr[ch] : 0.0f;
-            for (int k = 0; k < nb; ++k) gs[3 * k + ch] = basis[k] * m;
-            for (int k = 1; k < nb; ++k) {
-                const float ck = __ldg(c + 3 * k + ch) * m;
-                dg.x += bx[k] * ck;
-                dg.y += by[k] * ck;
-                dg.z += bz[k] * ck;
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                if (k < nb) gs[3 * k + ch] = basis[k] * m;
+#pragma unroll
+            for (int k = 1; k < 16; ++k) {
+                if (k < nb) {
+                    const float ck = __ldg(c + 3 * k + ch) * m;
+                    dg.x += bx[k] * ck;
+                    dg.y += by[k] * ck;
+                    dg.z += bz[k] * ck;
+                }
             }
         }
         for (int k = nb; k < int(f.shCoeffs); ++k) {

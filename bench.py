@@ -310,6 +310,7 @@ def run_gpu(args):
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
     launches = int(raster.stats().total_kernel_launches) - launches_before
+    log_overflow = raster.log_overflow_tiles()
     # the full-shape kernels: Q_v, the shape forward and its VJP per view (one chunk each at these sizes)
     free, total = torch.cuda.mem_get_info(device)
     chunks = plan_footprint_chunks(n, driver_free_bytes=int(free), device_total_bytes=int(total),
@@ -386,6 +387,7 @@ def run_gpu(args):
         "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
         "intersections_per_view": intersections,
         "fallback_particles_per_view": int(round(float(np.mean(view_fallback)))) if view_fallback else 0,
+        "log_overflow_tiles_last_view": log_overflow,
     }
     if clock_info is not None:
         result["clocks"] = clock_info

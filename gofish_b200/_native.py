@@ -174,6 +174,7 @@ _SIGNATURES = [
     ("gf_tracer_enable_timing", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     ("gf_tracer_collect_times", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     ("gf_tracer_stats", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(GfTraceStats)]),
+    ("gf_tracer_log_overflow_tiles", ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint32)]),
     ("gf_tracer_copy_intermediates", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
       ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),

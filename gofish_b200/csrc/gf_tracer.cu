@@ -63,8 +63,10 @@ struct gf_tracer {
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
     gf::CompositeLog frameLog{};
     bool frameGeo = false;                                // the last forward wrote the geometric channels
-    uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size (low 32 bits)
+    uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size, [2] log overflow tiles (low 32 bits)
     uint32_t fallbackParticles = 0;
+    cudaEvent_t logCopied = nullptr;  // recorded after the copy of the last forward's log overflow count
+    bool logCounted = false;
     int finalBuf = 0;
     bool haveForward = false;
     gf::FrameArgs frame{};
@@ -124,7 +126,7 @@ int bind_device(gf_tracer* t) {
     GF_CUDA(cudaGetDevice(&dev));
     if (t->device < 0) {
         t->device = dev;
-        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), 2 * sizeof(uint64_t), cudaHostAllocDefault));
+        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), 3 * sizeof(uint64_t), cudaHostAllocDefault));
     } else if (t->device != dev) {
         return fail(GF_ERR_STATE, "tracer bound to device %d, called on device %d", t->device, dev);
     }
@@ -472,6 +474,15 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();
+    // the overflow count for gf_tracer_stats, read without a synchronization here
+    t->logCounted = false;
+    if (a.log.ids != nullptr) {
+        if (t->logCopied == nullptr) GF_CUDA(cudaEventCreateWithFlags(&t->logCopied, cudaEventDisableTiming));
+        t->hostTotal[2] = 0;
+        GF_CUDA(cudaMemcpyAsync(t->hostTotal + 2, a.log.overflowCount, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+        GF_CUDA(cudaEventRecord(t->logCopied, stream));
+        t->logCounted = true;
+    }
     t->frameMask = a.mask;
     t->frameRayO = in->ray_origin;
     t->frameRayD = in->ray_direction;
@@ -531,6 +542,7 @@ void gf_tracer_destroy(gf_tracer* t) {
             cudaEventDestroy(ev.end);
         }
         for (cudaEvent_t e : t->eventPool) cudaEventDestroy(e);
+        if (t->logCopied != nullptr) cudaEventDestroy(t->logCopied);
         if (t->hostTotal != nullptr) cudaFreeHost(t->hostTotal);
         if (prev >= 0) cudaSetDevice(prev);
     }
@@ -675,6 +687,16 @@ int gf_tracer_stats(const gf_tracer* t, gf_trace_stats* st) {
     st->kernel_launches = t->launches;
     st->fallback_particles = t->fallbackParticles;
     st->total_kernel_launches = t->totalLaunches;
+    return GF_OK;
+}
+
+int gf_tracer_log_overflow_tiles(const gf_tracer* t, uint32_t* tiles) {
+    if (t == nullptr || tiles == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    *tiles = 0;
+    if (t->logCounted) {
+        GF_CUDA(cudaEventSynchronize(t->logCopied));
+        *tiles = uint32_t(t->hostTotal[2]);
+    }
     return GF_OK;
 }
 

@@ -273,6 +273,14 @@ class SplatRaster:
         check(self._lib.gf_tracer_stats(self._handle, ctypes.byref(st)), "stats")
         return st
 
+    def log_overflow_tiles(self) -> int:
+        """Tiles of the last training forward replayed by the backward because a
+        pixel composited more hits than the composite log holds (waits for
+        that forward's render)."""
+        tiles = ctypes.c_uint32(0)
+        check(self._lib.gf_tracer_log_overflow_tiles(self._handle, ctypes.byref(tiles)), "log_overflow_tiles")
+        return int(tiles.value)
+
     def copy_intermediates(self, device) -> dict[str, torch.Tensor]:
         """Projected state, radiance, counts, sorted keys/ids and tile ranges of the last forward."""
         st = self.stats()

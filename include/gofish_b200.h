@@ -215,6 +215,12 @@ int gf_tracer_collect_times(gf_tracer* tracer, float* ms, uint32_t* launches);
  * this reports the sizes the timings depend on). */
 int gf_tracer_stats(const gf_tracer* tracer, gf_trace_stats* stats);
 
+/* Tiles of the last training forward holding a pixel that composited more
+ * hits than the composite log holds (0 without a log); trace_bwd replays
+ * them through the k-buffer (renderBackward, gutRenderer.cuh:555-712).
+ * Waits for that forward's render to finish. */
+int gf_tracer_log_overflow_tiles(const gf_tracer* tracer, uint32_t* tiles);
+
 /* Copies the last forward pass's intermediate state into caller device
  * buffers (any pointer may be NULL): projected particle state [N,8]
  * (center.xy, conic.xyz, opacity, extent.xy), precomputed radiance [N,3],

@@ -272,6 +272,19 @@ def test_backward_paths_agree(cuda_device, k, log_capacity):
     _compare_forward(ref, got)
     if log_capacity == 6:
         assert int((ref["hit_count"] > 6).sum()) > 0 and int((ref["hit_count"] <= 6).sum()) > 0
+    # a pixel overflows the log only if it hit more particles than the log holds
+    cap = 256 if log_capacity == 0 else log_capacity
+    h, w = ref["hit_count"].shape
+    deep = np.zeros((-(-h // 16) * 16, -(-w // 16) * 16), bool)
+    deep[:h, :w] = ref["hit_count"] > cap
+    deep_tiles = int(deep.reshape(deep.shape[0] // 16, 16, deep.shape[1] // 16, 16).any(axis=(1, 3)).sum())
+    overflow = gpu.raster.log_overflow_tiles()
+    if log_capacity < 0:
+        assert overflow == 0
+    else:
+        assert overflow <= deep_tiles
+    if log_capacity == 6:
+        assert overflow > 0
     rng = np.random.default_rng(19)
     g_rgba = rng.standard_normal(ref["rgba"].shape).astype(np.float32)
     g_hit = (0.1 * rng.standard_normal(ref["hit_t"].shape)).astype(np.float32)

@@ -20,7 +20,9 @@ Prints one JSON line (rank 0).
 from __future__ import annotations
 
 import argparse
+import atexit
 import datetime
+import gc
 import json
 import math
 import os
@@ -28,6 +30,7 @@ import subprocess
 import sys
 import threading
 import time
+from types import SimpleNamespace
 
 import numpy as np
 
@@ -131,6 +134,7 @@ class ClockSampler:
         except (OSError, ValueError):
             self.proc = None
             return
+        atexit.register(self._end)  # an exception before stop() must not leave nvidia-smi running
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
@@ -138,23 +142,28 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def wait_ready(self, timeout_s: float = 10.0) -> None:
-        """Waits for the first sample, so that nvidia-smi's start-up (which
-        holds the driver) falls before the timed region; the statistics keep
-        the last sample before the region and every one inside it."""
+    def mark(self, timeout_s: float = 10.0) -> None:
+        """Starts the window of the statistics: the last sample before this
+        call and every later one.  The sampler is started long before (at
+        process start), so that nvidia-smi's start-up, which holds the driver
+        and on a freshly booted box stretched a timed region, is over."""
         end = time.time() + timeout_s
         while self.proc is not None and not self.lines and time.time() < end:
             time.sleep(0.02)
         del self.lines[:-1]
 
+    def _end(self) -> None:
+        if self.proc is not None and self.proc.poll() is None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._end()
         if self.thread is not None:
             self.thread.join(timeout=2)
         sm, smax, reasons = [], [], set()
@@ -222,6 +231,8 @@ def run_gpu(args):
     torch.cuda.set_device(device)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    clocks = ClockSampler(local)
+    clocks.start()
 
     w, poses = build_workload(args, rank, world)
     cam = w.camera
@@ -234,11 +245,17 @@ def run_gpu(args):
     rng = np.random.default_rng(777 + rank)
     target_host = torch.from_numpy(rng.random((len(poses), cam.height, cam.width, 3), dtype=np.float32)).pin_memory()
 
-    model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in
-                             ("positions", "rotation", "scale", "density", "features")), scene.sh_degree)
-    params = model.parameters()
-    bucket = GradientBucket(params) if world > 1 else None  # one all-reduce of the [N,59] gradients
-    target = target_host.to(device)
+    param_keys = ("positions", "rotation", "scale", "density", "features")
+
+    def input_set():
+        """A model, its gradient bucket (one all-reduce of the [N,59]
+        gradients), a target and a loss accumulator on the device."""
+        model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in param_keys), scene.sh_degree)
+        params = model.parameters()
+        return SimpleNamespace(model=model, params=params, bucket=GradientBucket(params) if world > 1 else None,
+                               target=target_host.to(device), loss=torch.zeros((), device=device))
+
+    resident = input_set()
     ray_o = torch.from_numpy(ray_o_np).to(device)
     ray_d = torch.from_numpy(ray_d_np).to(device)
     mask = torch.from_numpy(valid_np).to(device)            # [1,H,W,1] bool
@@ -254,33 +271,33 @@ def run_gpu(args):
     scale = 1.0 / (3.0 * n_valid)
     view_intersections: list[int] = []
     view_fallback: list[int] = []
-    loss_acc = torch.zeros((), device=device)
 
-    def step(tgt, want_loss=False):
-        """Forward, L1 loss and backward of every local view through
-        Tracer.render (per-view full shape, trace, trace_bwd, shape VJP); the
-        model gradients [N,59] summed over the views and all-reduced over ranks."""
-        if bucket is not None:
-            bucket.attach()
+    def step(s, want_loss=False):
+        """Forward, L1 loss and backward of every local view of input set s
+        through Tracer.render (per-view full shape, trace, trace_bwd, shape
+        VJP); the model gradients [N,59] summed over the views and
+        all-reduced over ranks."""
+        if s.bucket is not None:
+            s.bucket.attach()
         else:
-            for p in params:
+            for p in s.params:
                 p.grad = None
-        loss_acc.zero_()
+        s.loss.zero_()
         for v, batch in enumerate(batches):
-            out = tracer.render(model, batch, train=True, frame_id=v)
+            out = tracer.render(s.model, batch, train=True, frame_id=v)
             st = raster.stats()
             view_intersections.append(int(st.num_intersections))
             view_fallback.append(int(st.fallback_particles))
-            loss = ((out["pred_features"][0] - tgt[v]).abs() * valid_f).sum() * scale
+            loss = ((out["pred_features"][0] - s.target[v]).abs() * valid_f).sum() * scale
             loss.backward()
             if want_loss:
-                loss_acc.add_(loss.detach())
-        if bucket is not None:
-            bucket.allreduce()
-        return loss_acc if want_loss else None
+                s.loss.add_(loss.detach())
+        if s.bucket is not None:
+            s.bucket.allreduce()
+        return s.loss if want_loss else None
 
     for _ in range(args.warmup):
-        step(target)
+        step(resident)
     torch.cuda.synchronize(device)
     intersections = int(raster.stats().num_intersections)
 
@@ -289,9 +306,10 @@ def run_gpu(args):
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
     launches_before = int(raster.stats().total_kernel_launches)
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_ready()
+    # the set-up's garbage is collected, and what survives is kept out of later collections
+    gc.collect()
+    gc.freeze()
+    clocks.mark()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -299,7 +317,7 @@ def run_gpu(args):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(args.steps):
-        step(target)
+        step(resident)
     t1.record(stream)
     torch.cuda.synchronize(device)
     clock_info = clocks.stop()
@@ -328,27 +346,47 @@ def run_gpu(args):
     # --- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        # Every step copies its inputs (the model parameters and the target)
+        # from pinned host memory and reads its loss back.  Two input sets
+        # alternate so that the copy of step i+1 runs on a copy stream while
+        # step i computes; events order each copy after the step that last
+        # read its set, and each step after its own copy.
         h2d = sum(t.numel() * 4 for t in host.values()) + target_host.numel() * 4
-        t_dev = torch.empty_like(target)
-        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        sets = [resident, input_set()]
+        copy_stream = torch.cuda.Stream(device)
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        consumed = [torch.cuda.Event(), torch.cuda.Event()]
+        loss_host = torch.empty(max(args.steps, args.warmup, 1), dtype=torch.float32).pin_memory()
 
-        def e2e_step():
-            with torch.no_grad():
-                for p, k in zip(params, ("positions", "rotation", "scale", "density", "features")):
-                    p.copy_(host[k], non_blocking=True)
-            t_dev.copy_(target_host, non_blocking=True)
-            loss = step(t_dev, want_loss=True)
-            loss_host.copy_(loss, non_blocking=True)
+        def upload(i, start):
+            s = sets[i % 2]
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(start if i < 2 else consumed[i % 2])
+                with torch.no_grad():
+                    for p, k in zip(s.params, param_keys):
+                        p.copy_(host[k], non_blocking=True)
+                    s.target.copy_(target_host, non_blocking=True)
+                copied[i % 2].record(copy_stream)
 
-        for _ in range(max(1, args.warmup // 2)):
-            e2e_step()
+        def run(steps, start):
+            upload(0, start)
+            for i in range(steps):
+                if i + 1 < steps:
+                    upload(i + 1, start)
+                stream.wait_event(copied[i % 2])
+                loss = step(sets[i % 2], want_loss=True)
+                loss_host[i].copy_(loss, non_blocking=True)
+                consumed[i % 2].record(stream)
+
+        warm = torch.cuda.Event()
+        warm.record(stream)
+        run(max(1, args.warmup // 2), warm)
         torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        run(args.steps, e0)
         e1.record(stream)
         torch.cuda.synchronize(device)
         ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
@@ -460,6 +498,8 @@ def run_mesh(args):
     torch.cuda.set_device(device)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    clocks = ClockSampler(local)
+    clocks.start()
 
     w, shape, points_all, cameras = mesh_workload(args)
     q_total = points_all.shape[0]
@@ -488,9 +528,9 @@ def run_mesh(args):
     stats0 = raster.stats()
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_ready()
+    gc.collect()
+    gc.freeze()
+    clocks.mark()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -738,6 +778,8 @@ def run_inference(args):
     torch.cuda.set_device(device)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    clocks = ClockSampler(local)
+    clocks.start()
     w = inference_workload(args)
     cam = w.camera
     ray_o_np, ray_d_np, valid_np = cam.rays()
@@ -770,9 +812,9 @@ def run_inference(args):
     raster.enable_stage_timing(True)
     launches_before = int(raster.stats().total_kernel_launches)
     inter = []
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_ready()
+    gc.collect()
+    gc.freeze()
+    clocks.mark()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)

@@ -109,7 +109,8 @@ def workload_config(w, args, world: int, views_per_rank: int = 1) -> dict:
         "entry_point": "Tracer.render (per-view full shape, trace, trace_bwd, full-shape VJP)",
         "pixel_footprint_variance": BENCH_GAMMA,
         "l2_policy": "inputs larger than L2 (model 236 B/Gaussian + packed rows + rays > 126 MB)",
-        "parallelism": (f"dp{world} (views sharded, NCCL all-reduce of the [N,59] model gradients)" if world > 1
+        "parallelism": (f"dp{world} (views sharded, NCCL all-reduce of the [N,59] model gradients, the SH part "
+                        "overlapping the full-shape VJP)" if world > 1
                         else "single GPU"),
     }
 
@@ -248,12 +249,15 @@ def run_gpu(args):
     param_keys = ("positions", "rotation", "scale", "density", "features")
 
     def input_set():
-        """A model, its gradient bucket (one all-reduce of the [N,59]
-        gradients), a target and a loss accumulator on the device."""
+        """A model, its gradient bucket (the [N,59] gradients in one buffer;
+        the SH part, 48 floats per Gaussian, is all-reduced as soon as the
+        last view's render backward has produced it, overlapping the
+        full-shape VJP; the rest after), a target and a loss accumulator."""
         model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in param_keys), scene.sh_degree)
         params = model.parameters()
-        return SimpleNamespace(model=model, params=params, bucket=GradientBucket(params) if world > 1 else None,
-                               target=target_host.to(device), loss=torch.zeros((), device=device))
+        bucket = GradientBucket(params, early=[model.features]) if world > 1 else None
+        return SimpleNamespace(model=model, params=params, bucket=bucket, target=target_host.to(device),
+                               loss=torch.zeros((), device=device))
 
     resident = input_set()
     ray_o = torch.from_numpy(ray_o_np).to(device)
@@ -289,6 +293,8 @@ def run_gpu(args):
             view_intersections.append(int(st.num_intersections))
             view_fallback.append(int(st.fallback_particles))
             loss = ((out["pred_features"][0] - s.target[v]).abs() * valid_f).sum() * scale
+            if s.bucket is not None and v == len(batches) - 1:
+                s.bucket.arm()
             loss.backward()
             if want_loss:
                 s.loss.add_(loss.detach())

@@ -30,37 +30,88 @@ class GradientBucket:
     59 floats per Gaussian at SH degree 3).
 
     ``attach()`` zeroes the buffer and sets each parameter's ``.grad`` to
-    its view; autograd then accumulates the step's gradients in place."""
+    its view; autograd then accumulates the step's gradients in place.
 
-    def __init__(self, params: Sequence[torch.Tensor]):
-        self.params = list(params)
-        if not self.params:
+    ``early`` names parameters whose gradient is complete before the others
+    in the step's last backward (the SH gradient of the tracer comes out of
+    the render backward, before the full-shape VJP that produces the
+    position, rotation, scale and opacity gradients).  They sit at the end
+    of the buffer.  After ``arm()``, called before the last backward of a
+    step, the accumulation of the last of them starts an asynchronous
+    all-reduce of that tail, which overlaps the rest of the backward;
+    ``allreduce()`` then reduces the head and orders the stream after both.
+    Every rank must arm before the same backward."""
+
+    def __init__(self, params: Sequence[torch.Tensor], early: Sequence[torch.Tensor] = ()):
+        params = list(params)
+        if not params:
             raise ValueError("no parameters")
-        sizes = [p.numel() for p in self.params]
-        first = self.params[0]
-        self.flat = torch.zeros(sum(sizes), dtype=first.dtype, device=first.device)
-        self.views = []
+        early_ids = {id(p) for p in early}
+        if not early_ids <= {id(p) for p in params}:
+            raise ValueError("early parameters must be among the bucket's parameters")
+        late = [p for p in params if id(p) not in early_ids]
+        tail = [p for p in params if id(p) in early_ids]
+        self.params = params
+        first = params[0]
+        self.head_numel = sum(p.numel() for p in late)
+        self.flat = torch.zeros(self.head_numel + sum(p.numel() for p in tail), dtype=first.dtype,
+                                device=first.device)
+        view_of = {}
         offset = 0
-        for p, n in zip(self.params, sizes):
-            self.views.append(self.flat[offset:offset + n].view(p.shape))
-            offset += n
+        for p in late + tail:
+            view_of[id(p)] = self.flat[offset:offset + p.numel()].view(p.shape)
+            offset += p.numel()
+        self.views = [view_of[id(p)] for p in params]
+        self._early = tail
+        self._pending: set[int] = set()
+        self._armed = False
+        self._group = None
+        self._work = None
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_accumulated) for p in tail]
 
     def attach(self) -> None:
         self.flat.zero_()
         for p, v in zip(self.params, self.views):
             p.grad = v
 
+    def arm(self, group=None) -> None:
+        """The next backward is the step's last: start the tail's all-reduce
+        as soon as its gradients are accumulated."""
+        if not self._early or not _distributed(group):
+            return
+        self._armed = True
+        self._group = group
+        self._pending = {id(p) for p in self._early}
+
+    def _on_accumulated(self, param: torch.Tensor) -> None:
+        if not self._armed:
+            return
+        self._pending.discard(id(param))
+        if not self._pending and self._work is None:
+            self._work = dist.all_reduce(self.flat[self.head_numel:], op=dist.ReduceOp.SUM, group=self._group,
+                                         async_op=True)
+
     def allreduce(self, group=None) -> None:
         """Sums the bucket over the ranks (no-op on one rank)."""
         for p, v in zip(self.params, self.views):
             if p.grad is not v:
                 raise RuntimeError("a gradient left its bucket view; call attach() before backward")
-        allreduce_gradients([self.flat], group)
+        work, self._work, self._armed = self._work, None, False
+        if work is None:
+            allreduce_gradients([self.flat], group)
+            return
+        if self.head_numel > 0:
+            dist.all_reduce(self.flat[:self.head_numel], op=dist.ReduceOp.SUM, group=group)
+        work.wait()
+
+
+def _distributed(group=None) -> bool:
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
 
 
 def allreduce_gradients(grads: Sequence[torch.Tensor], group=None) -> None:
     """Sums each gradient tensor over the ranks in place (one collective per tensor)."""
-    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size(group) == 1:
+    if not _distributed(group):
         return
     for g in grads:
         dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)

@@ -68,7 +68,7 @@ def test_shard_views_partitions_the_batch():
         shard_views(8, 2, 2)
 
 
-def _bucket_worker(rank, world, port, out):
+def _bucket_worker(rank, world, port, out, early=False):
     from gofish_b200.multiview import GradientBucket
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -78,12 +78,19 @@ def _bucket_worker(rank, world, port, out):
         g = torch.Generator().manual_seed(7)
         pos = torch.randn(11, 3, generator=g).requires_grad_(True)
         sh = torch.randn(11, 48, generator=g).requires_grad_(True)
-        bucket = GradientBucket([pos, sh])
+        bucket = GradientBucket([pos, sh], early=[sh] if early else ())
+        if early:
+            # the early parameter sits at the end of the flat buffer
+            assert bucket.views[1].data_ptr() == bucket.flat[bucket.head_numel:].data_ptr()
         for step in range(2):
             bucket.attach()
             for v in range(2):  # two views per rank, accumulated in the bucket
                 w = float(1 + rank * 2 + v + step)
+                if early and v == 1:
+                    bucket.arm()  # the tail's all-reduce starts inside this backward
                 (w * (pos ** 2).sum() + w * sh.sum()).backward()
+                if early:
+                    assert (bucket._work is not None) == (v == 1)
             assert pos.grad.data_ptr() == bucket.views[0].data_ptr()
             bucket.allreduce()
         out[rank] = (pos.grad.clone(), sh.grad.clone(), pos.detach().clone())
@@ -91,13 +98,16 @@ def _bucket_worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_gradient_bucket_single_allreduce_matches_sum():
+@pytest.mark.parametrize("early", [False, True])
+def test_gradient_bucket_single_allreduce_matches_sum(early):
+    """One all-reduce of the flat bucket, or (early) the SH tail reduced
+    asynchronously from inside the last backward and the head after it."""
     world = 2
     port = _free_port()
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     out = manager.dict()
-    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, out)) for r in range(world)]
+    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, out, early)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -108,3 +118,18 @@ def test_gradient_bucket_single_allreduce_matches_sum():
     for r in range(world):
         torch.testing.assert_close(out[r][0], 14.0 * 2.0 * pos)
         torch.testing.assert_close(out[r][1], torch.full((11, 48), 14.0))
+
+
+def test_gradient_bucket_early_is_a_no_op_on_one_process():
+    from gofish_b200.multiview import GradientBucket
+
+    pos = torch.ones(4, 3, requires_grad=True)
+    sh = torch.ones(4, 48, requires_grad=True)
+    bucket = GradientBucket([pos, sh], early=[sh])
+    bucket.attach()
+    bucket.arm()
+    (2.0 * pos.sum() + 3.0 * sh.sum()).backward()
+    bucket.allreduce()
+    assert torch.equal(pos.grad, torch.full((4, 3), 2.0)) and torch.equal(sh.grad, torch.full((4, 48), 3.0))
+    with pytest.raises(ValueError):
+        GradientBucket([pos], early=[sh])

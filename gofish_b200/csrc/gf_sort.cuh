@@ -131,10 +131,16 @@ __global__ __launch_bounds__(kSortThreads) void k_radix_histogram(const uint64_t
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t base = blockIdx.x * kSortTile + warp * kSortWarpItems;
-#pragma unroll 4
+    // all loads first, so that their latencies overlap
+    uint64_t key[kSortItemsPerThread];
+#pragma unroll
     for (int k = 0; k < kSortItemsPerThread; ++k) {
         const uint32_t i = base + k * 32 + lane;
-        if (i < n) atomicAdd(&h[warp][digit_of(__ldg(keys + i), shift)], 1u);
+        key[k] = i < n ? __ldg(keys + i) : 0ull;
+    }
+#pragma unroll
+    for (int k = 0; k < kSortItemsPerThread; ++k) {
+        if (base + k * 32 + lane < n) atomicAdd(&h[warp][digit_of(key[k], shift)], 1u);
     }
     __syncthreads();
     for (int d = threadIdx.x; d < kRadixBins; d += kSortThreads) {
@@ -153,7 +159,7 @@ struct SortScatterSmem {
     uint32_t globalStart[kRadixBins];           // first global position of this block's digit run
 };
 
-__global__ __launch_bounds__(kSortThreads) void k_radix_scatter(const uint64_t* __restrict__ keysIn,
+__global__ __launch_bounds__(kSortThreads, 2) void k_radix_scatter(const uint64_t* __restrict__ keysIn,
                                                                 const uint32_t* __restrict__ valsIn,
                                                                 uint64_t* __restrict__ keysOut,
                                                                 uint32_t* __restrict__ valsOut, uint32_t n,
@@ -172,13 +178,20 @@ __global__ __launch_bounds__(kSortThreads) void k_radix_scatter(const uint64_t* 
     uint64_t key[kSortItemsPerThread];
     uint32_t val[kSortItemsPerThread];
     uint32_t rank[kSortItemsPerThread];
+    // All loads first: the ranking below synchronises the warp per item, and
+    // a load issued inside that loop would wait out its full latency each time.
+#pragma unroll
+    for (int k = 0; k < kSortItemsPerThread; ++k) {
+        const uint32_t i = base + k * 32 + lane;
+        const bool valid = i < n;
+        key[k] = valid ? __ldg(keysIn + i) : ~0ull;
+        val[k] = valid ? __ldg(valsIn + i) : 0u;
+    }
     // Warp-local stable ranks, item order = (k, lane) within the warp's 512-item run.
 #pragma unroll
     for (int k = 0; k < kSortItemsPerThread; ++k) {
         const uint32_t i = base + k * 32 + lane;
         const bool valid = i < n;
-        key[k] = valid ? keysIn[i] : ~0ull;
-        val[k] = valid ? valsIn[i] : 0u;
         const uint32_t d = digit_of(key[k], shift);
         const uint32_t validMask = __ballot_sync(0xffffffffu, valid);
         uint32_t peers = __match_any_sync(0xffffffffu, d) & validMask;

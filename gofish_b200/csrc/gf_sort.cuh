@@ -151,10 +151,19 @@ __global__ __launch_bounds__(kSortThreads) void k_radix_histogram(const uint64_t
     }
 }
 
+// A warp ranks its 16 items per lane as kSortChains independent chains of
+// kSortChainItems items (item k in chain k / kSortChainItems), each with its
+// own digit counters, advanced together: item order (warp, chain, item, lane)
+// is the input order, so the ranks stay stable, and the chains' shared-memory
+// round trips overlap instead of following one another.
+constexpr int kSortChains = 4;
+constexpr int kSortChainItems = kSortItemsPerThread / kSortChains;
+constexpr int kSortCounters = kSortWarps * kSortChains;
+
 struct SortScatterSmem {
     uint64_t keys[kSortTile];
     uint32_t vals[kSortTile];
-    uint32_t warpHist[kSortWarps][kRadixBins];  // running counts, then warp offsets within the block
+    uint32_t warpHist[kSortCounters][kRadixBins];  // running counts per (warp, chain), then their offsets
     uint32_t blockStart[kRadixBins];            // first block-local position of each digit
     uint32_t globalStart[kRadixBins];           // first global position of this block's digit run
 };
@@ -168,7 +177,7 @@ __global__ __launch_bounds__(kSortThreads, 2) void k_radix_scatter(const uint64_
     extern __shared__ __align__(16) unsigned char smemRaw[];
     SortScatterSmem& sm = *reinterpret_cast<SortScatterSmem*>(smemRaw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < kSortWarps * kRadixBins; i += kSortThreads) (&sm.warpHist[0][0])[i] = 0u;
+    for (int i = threadIdx.x; i < kSortCounters * kRadixBins; i += kSortThreads) (&sm.warpHist[0][0])[i] = 0u;
     for (int d = threadIdx.x; d < kRadixBins; d += kSortThreads)
         sm.globalStart[d] = histScanned[uint64_t(d) * numBlocks + blockIdx.x];
     __syncthreads();
@@ -187,27 +196,36 @@ __global__ __launch_bounds__(kSortThreads, 2) void k_radix_scatter(const uint64_
         key[k] = valid ? __ldg(keysIn + i) : ~0ull;
         val[k] = valid ? __ldg(valsIn + i) : 0u;
     }
-    // Warp-local stable ranks, item order = (k, lane) within the warp's 512-item run.
+    // Chain-local stable ranks, item order = (k, lane) within the warp's 512-item run.
 #pragma unroll
-    for (int k = 0; k < kSortItemsPerThread; ++k) {
-        const uint32_t i = base + k * 32 + lane;
-        const bool valid = i < n;
-        const uint32_t d = digit_of(key[k], shift);
-        const uint32_t validMask = __ballot_sync(0xffffffffu, valid);
-        uint32_t peers = __match_any_sync(0xffffffffu, d) & validMask;
-        const uint32_t before = sm.warpHist[warp][d];
-        rank[k] = before + __popc(peers & lanesBelow);
+    for (int j = 0; j < kSortChainItems; ++j) {
+        uint32_t dig[kSortChains], cnt[kSortChains];
+        bool lead[kSortChains];
+#pragma unroll
+        for (int c = 0; c < kSortChains; ++c) {
+            const int k = c * kSortChainItems + j;
+            const bool valid = base + k * 32 + lane < n;
+            dig[c] = digit_of(key[k], shift);
+            const uint32_t peers = __match_any_sync(0xffffffffu, dig[c]) & __ballot_sync(0xffffffffu, valid);
+            const uint32_t before = sm.warpHist[warp * kSortChains + c][dig[c]];
+            rank[k] = before + __popc(peers & lanesBelow);
+            cnt[c] = before + __popc(peers);
+            lead[c] = valid && (peers & lanesBelow) == 0u;
+        }
         __syncwarp();
-        if (valid && (peers & lanesBelow) == 0u) sm.warpHist[warp][d] = before + __popc(peers);
+#pragma unroll
+        for (int c = 0; c < kSortChains; ++c)
+            if (lead[c]) sm.warpHist[warp * kSortChains + c][dig[c]] = cnt[c];
         __syncwarp();
     }
     __syncthreads();
-    // Per digit: exclusive prefix over warps (in place) and the block-local digit start.
+    // Per digit: exclusive prefix over (warp, chain) in item order (in place)
+    // and the block-local digit start.
     if (threadIdx.x < kRadixBins) {
         const int d = threadIdx.x;
         uint32_t s = 0;
 #pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) {
+        for (int w = 0; w < kSortCounters; ++w) {
             const uint32_t c = sm.warpHist[w][d];
             sm.warpHist[w][d] = s;
             s += c;
@@ -228,7 +246,7 @@ __global__ __launch_bounds__(kSortThreads, 2) void k_radix_scatter(const uint64_
         const uint32_t i = base + k * 32 + lane;
         if (i < n) {
             const uint32_t d = digit_of(key[k], shift);
-            const uint32_t pos = sm.blockStart[d] + sm.warpHist[warp][d] + rank[k];
+            const uint32_t pos = sm.blockStart[d] + sm.warpHist[warp * kSortChains + k / kSortChainItems][d] + rank[k];
             sm.keys[pos] = key[k];
             sm.vals[pos] = val[k];
         }

@@ -165,7 +165,9 @@ __device__ __forceinline__ bool hit_with_origin(const Ray& ray, V3 gro, const fl
                                                 bool pretest = false, float miss = 0.0f) {
     const V3 grdu = binv_times(b, c, d, ray.d);
     const float denom = fdot3(grdu, grdu);
-    if (!(denom > 0.0f && isfinite_f(denom) && isfinite_f(ray.tmin) && ray.tmax > ray.tmin)) return false;
+    // callers test valid rays only, and make_ray's valid (tmax > tmin, tmin =
+    // max(., 0)) already means a finite tmin below tmax
+    if (!(denom > 0.0f && isfinite_f(denom))) return false;
     const float num = fdot3(gro, grdu);
     if (pretest && __fmul_rn(denom, miss) > __fmul_rn(num, num)) return false;
     const float tauLine = -num / denom;
@@ -853,7 +855,9 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     const V3 gro = binv_times(q.b, q.c, q.d, gp);
     const V3 grdu = binv_times(q.b, q.c, q.d, ray.d);
     const float denom = fdot3(grdu, grdu);
-    if (!(denom > 0.0f && isfinite_f(denom) && isfinite_f(ray.tmin) && ray.tmax > ray.tmin)) return false;
+    // callers test valid rays only, and make_ray's valid (tmax > tmin, tmin =
+    // max(., 0)) already means a finite tmin below tmax
+    if (!(denom > 0.0f && isfinite_f(denom))) return false;
     const float num = fdot3(gro, grdu);
     const float tauLine = -num / denom;
     const float tau = fminf(fmaxf(tauLine, ray.tmin), ray.tmax);

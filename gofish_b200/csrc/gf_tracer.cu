@@ -339,9 +339,12 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
                                                                   S, tr.second, tr.sums);
             t->launches += 1;
             GF_LAUNCH_CHECK();
+            int span = 1;  // leaves per node side at level l
             for (int l = 1; l < tr.n; ++l) {
                 const int pn = tr.gx[l] * tr.gy[l];
-                gf::fb::k_tile_cone_level<<<pn, 256, 0, stream>>>(tr, l, A, S);
+                span *= gf::fb::kFan;
+                const int threads = gf::fb::cone_level_threads(std::min(span, f.gx) * std::min(span, f.gy));
+                gf::fb::k_tile_cone_level<<<pn, threads, 0, stream>>>(tr, l, A, S);
                 t->launches += 1;
                 GF_LAUNCH_CHECK();
             }

@@ -493,10 +493,16 @@ __device__ __forceinline__ void bound_cone(V3 ax, float4 a, float cs, float& mn,
     else mn = min_f(mn, cang * a.w - sang * cs);
 }
 
-__global__ __launch_bounds__(256) void k_tile_cone_level(TileTree t, int l, float4* __restrict__ A,
-                                                         float* __restrict__ S) {
+// One block per node of level l; any multiple of 32 threads up to 1024 (the
+// bound is a min / or over the node's leaves, whatever their split over threads).
+__host__ __device__ constexpr int cone_level_threads(int leaves) {
+    return leaves >= 1024 ? 1024 : ((leaves + 31) / 32) * 32;
+}
+
+__global__ __launch_bounds__(1024) void k_tile_cone_level(TileTree t, int l, float4* __restrict__ A,
+                                                          float* __restrict__ S) {
     __shared__ float axis[8];
-    __shared__ float wmin[2][8];
+    __shared__ float wmin[2][32];
     const int node = blockIdx.x;
     const int pgx = t.gx[l], cgx = t.gx[l - 1], cgy = t.gy[l - 1];
     const int px = node % pgx, py = node / pgx;

@@ -362,16 +362,26 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
     const int y = y0 + lane;
     const bool row = lane < kTile && y < y1 && mask[tile] != 0u;
     const float4 empty = make_float4(0.0f, 0.0f, 1.0f, 2.0f);
+    // the row's unit pixel directions, once (bit i of ok: pixel x0 + i has one);
+    // every pass below visits them in x order, as a loop over the row would
+    V3 ud[kTile];
+    uint32_t ok = 0u;
+    if (row) {
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+            ud[i] = v3(0.0f, 0.0f, 1.0f);
+            if (x0 + i < x1 && pixel_dir(f, rayD, x0 + i, y, ud[i])) ok |= 1u << i;
+        }
+    }
     // pass 0: the mean ray
     V3 sum = v3(0.0f, 0.0f, 0.0f);
     int count = 0;
-    if (row)
-        for (int x = x0; x < x1; ++x) {
-            V3 u;
-            if (!pixel_dir(f, rayD, x, y, u)) continue;
-            sum = sum + u;
-            ++count;
-        }
+#pragma unroll
+    for (int i = 0; i < kTile; ++i) {
+        if (!((ok >> i) & 1u)) continue;
+        sum = sum + ud[i];
+        ++count;
+    }
     int all = 0;
     const V3 total = rows_sum(sum, count, all);
     if (lane == 0) A[sums + tile] = make_float4(total.x, total.y, total.z, 0.0f);
@@ -401,16 +411,15 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
         const V3 ref = pass == 0 ? mean : far1;
         float best = 2.0f;
         V3 bu = ref;
-        if (row)
-            for (int x = x0; x < x1; ++x) {
-                V3 u;
-                if (!pixel_dir(f, rayD, x, y, u)) continue;
-                const float c = dot3(ref, u);
-                if (c < best) {
-                    best = c;
-                    bu = u;
-                }
+#pragma unroll
+        for (int i = 0; i < kTile; ++i) {
+            if (!((ok >> i) & 1u)) continue;
+            const float c = dot3(ref, ud[i]);
+            if (c < best) {
+                best = c;
+                bu = ud[i];
             }
+        }
         float gbest = 2.0f;
         V3 gu = ref;
         for (int r = 0; r < kTile; ++r) {
@@ -427,18 +436,19 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
     // pass 3: cluster sums
     V3 s0 = v3(0.0f, 0.0f, 0.0f), s1 = v3(0.0f, 0.0f, 0.0f);
     int n0 = 0, n1 = 0;
-    if (row)
-        for (int x = x0; x < x1; ++x) {
-            V3 u;
-            if (!pixel_dir(f, rayD, x, y, u)) continue;
-            if (dot3(far1, u) >= dot3(far2, u)) {
-                s0 = s0 + u;
-                ++n0;
-            } else {
-                s1 = s1 + u;
-                ++n1;
-            }
+    uint32_t first = 0u;  // bit i: pixel x0 + i belongs to the first cluster
+#pragma unroll
+    for (int i = 0; i < kTile; ++i) {
+        if (!((ok >> i) & 1u)) continue;
+        if (dot3(far1, ud[i]) >= dot3(far2, ud[i])) {
+            s0 = s0 + ud[i];
+            ++n0;
+            first |= 1u << i;
+        } else {
+            s1 = s1 + ud[i];
+            ++n1;
         }
+    }
     int all0 = 0, all1 = 0;
     const V3 t0 = rows_sum(s0, n0, all0);
     const V3 t1 = rows_sum(s1, n1, all1);
@@ -448,13 +458,12 @@ __global__ __launch_bounds__(128) void k_tile_cones(FrameArgs f, const uint8_t* 
     const V3 a1 = ok1 ? v3(t1.x / l1, t1.y / l1, t1.z / l1) : mean;
     // pass 4: the smallest cosine of each cluster to its axis
     float m0 = 1.0f, m1 = 1.0f;
-    if (row)
-        for (int x = x0; x < x1; ++x) {
-            V3 u;
-            if (!pixel_dir(f, rayD, x, y, u)) continue;
-            if (dot3(far1, u) >= dot3(far2, u)) m0 = min_f(m0, dot3(a0, u));
-            else m1 = min_f(m1, dot3(a1, u));
-        }
+#pragma unroll
+    for (int i = 0; i < kTile; ++i) {
+        if (!((ok >> i) & 1u)) continue;
+        if ((first >> i) & 1u) m0 = min_f(m0, dot3(a0, ud[i]));
+        else m1 = min_f(m1, dot3(a1, ud[i]));
+    }
     for (int r = 0; r < kTile; ++r) {
         const float r0 = __shfl_sync(0xffffffffu, m0, r), r1 = __shfl_sync(0xffffffffu, m1, r);
         if (lane == 0) {

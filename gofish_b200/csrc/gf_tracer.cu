@@ -645,9 +645,10 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     GF_LAUNCH_CHECK();
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT_BWD, s);
-        gf::k_project_bwd<<<(N + 255) / 256, 256, 0, s>>>(f, in->particles, in->features, t->counts.as<uint32_t>(),
-                                                          t->gradRecords.as<float4>(), a.geo.gradShape,
-                                                          g->grad_particles, g->grad_features);
+        gf::k_project_bwd<<<(N + gf::kProjectBwdThreads - 1) / gf::kProjectBwdThreads, gf::kProjectBwdThreads,
+                             gf::project_bwd_smem_bytes(f.shCoeffs), s>>>(
+            f, in->particles, in->features, t->counts.as<uint32_t>(), t->gradRecords.as<float4>(), a.geo.gradShape,
+            g->grad_particles, g->grad_features);
         t->launches += 1;
         GF_LAUNCH_CHECK();
     }

@@ -919,77 +919,106 @@ __global__ void k_tile_ranges(const uint64_t* __restrict__ keys, uint32_t n, uin
 // Projection backward: record gradients to the reference's [N,32] density
 // gradient and [N,3*C] SH gradient (reference projectBackward,
 // gutProjector.cuh:1171-1222; radianceFromSpHBwd, gaussianParticles.cuh:234-310).
-__global__ __launch_bounds__(256) void k_project_bwd(FrameArgs f, const float* __restrict__ particles,
-                                                     const float* __restrict__ features,
-                                                     const uint32_t* __restrict__ counts,
-                                                     const float4* __restrict__ gradRecords,
-                                                     const float4* __restrict__ gradShape,
-                                                     float* __restrict__ gradParticles,
-                                                     float* __restrict__ gradFeatures) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= f.N) return;
-    const float4 g0 = gradRecords[4 * size_t(i)], g1 = gradRecords[4 * size_t(i) + 1],
-                 g2 = gradRecords[4 * size_t(i) + 2], g3 = gradRecords[4 * size_t(i) + 3];
-    float gp0 = g0.x, gp1 = g0.y, gp2 = g0.z;
-    float* gs = gradFeatures + size_t(i) * 3 * f.shCoeffs;
-    if (counts[i] != 0u) {
-        const float4 r0 = ldg4(particles + 32 * size_t(i));
-        const V3 mu = v3(r0.x, r0.y, r0.z);
-        const V3 v = mu - v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]);
-        const float dist = __fsqrt_rn(dot3(v, v));
-        const V3 dir = v3(v.x / dist, v.y / dist, v.z / dist);
-        float basis[16], bx[16], by[16], bz[16];
-        sh_basis(f.shDegree, dir, basis);
-        sh_basis_grad(f.shDegree, dir, bx, by, bz);
-        const int nb = min(sh_count(f.shDegree), int(f.shCoeffs));
-        const float* c = features + size_t(i) * 3 * f.shCoeffs;
-        const float gr[3] = {g3.y, g3.z, g3.w};
-        V3 dg = v3(0.0f, 0.0f, 0.0f);
-        // unrolled with predicates: the basis arrays stay in registers
-#pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-            float acc = basis[0] * __ldg(c + ch);
-#pragma unroll
-            for (int k = 1; k < 16; ++k)
-                if (k < nb) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
-            const float m = (acc + 0.5f) > 0.0f ? gr[ch] : 0.0f;
-#pragma unroll
-            for (int k = 0; k < 16; ++k)
-                if (k < nb) gs[3 * k + ch] = basis[k] * m;
-#pragma unroll
-            for (int k = 1; k < 16; ++k) {
-                if (k < nb) {
-                    const float ck = __ldg(c + 3 * k + ch) * m;
-                    dg.x += bx[k] * ck;
-                    dg.y += by[k] * ck;
-                    dg.z += bz[k] * ck;
-                }
-            }
-        }
-        for (int k = nb; k < int(f.shCoeffs); ++k) {
-            gs[3 * k] = 0.0f;
-            gs[3 * k + 1] = 0.0f;
-            gs[3 * k + 2] = 0.0f;
-        }
-        const float ndg = dot3(dir, dg);
-        gp0 += (dg.x - dir.x * ndg) / dist;
-        gp1 += (dg.y - dir.y * ndg) / dist;
-        gp2 += (dg.z - dir.z * ndg) / dist;
-    } else {
-        for (uint32_t k = 0; k < 3 * f.shCoeffs; ++k) gs[k] = 0.0f;
+// The block's SH rows (3 * shCoeffs floats per particle, contiguous over the
+// block's particles) are staged in shared memory, one padded row per thread,
+// so that their loads and the SH gradient stores are coalesced; each thread
+// reads its row, then overwrites it with the gradient column by column.
+constexpr int kProjectBwdThreads = 128;
+
+__host__ __device__ constexpr size_t project_bwd_smem_bytes(uint32_t shCoeffs) {
+    return sizeof(float) * kProjectBwdThreads * (3 * size_t(shCoeffs) + 1);
+}
+
+__global__ __launch_bounds__(kProjectBwdThreads) void k_project_bwd(FrameArgs f, const float* __restrict__ particles,
+                                                                    const float* __restrict__ features,
+                                                                    const uint32_t* __restrict__ counts,
+                                                                    const float4* __restrict__ gradRecords,
+                                                                    const float4* __restrict__ gradShape,
+                                                                    float* __restrict__ gradParticles,
+                                                                    float* __restrict__ gradFeatures) {
+    extern __shared__ float shRows[];  // [kProjectBwdThreads][3 * shCoeffs + 1]
+    const uint32_t rowLen = 3 * f.shCoeffs, pitch = rowLen + 1;
+    const uint32_t i0 = blockIdx.x * kProjectBwdThreads;
+    const uint32_t blockRows = min(uint32_t(kProjectBwdThreads), f.N - i0);
+    const float* src = features + size_t(i0) * rowLen;
+    for (uint32_t e = threadIdx.x; e < blockRows * rowLen; e += kProjectBwdThreads) {
+        const uint32_t p = e / rowLen;
+        shRows[p * pitch + (e - p * rowLen)] = __ldg(src + e);
     }
-    float4* out = reinterpret_cast<float4*>(gradParticles + 32 * size_t(i));
-    // rotation and intrinsic scale receive the extent channel's gradient (enable_normals)
-    const float4 gq = gradShape != nullptr ? gradShape[2 * size_t(i)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float4 gsc = gradShape != nullptr ? gradShape[2 * size_t(i) + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    out[0] = make_float4(gp0, gp1, gp2, g0.w);                      // pos, density
-    out[1] = gq;                                                    // rotation
-    out[2] = make_float4(gsc.x, gsc.y, gsc.z, 0.0f);                // scale, intrinsic density
-    out[3] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 0..3
-    out[4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 4..7
-    out[5] = make_float4(0.0f, g1.x, g1.y, g1.z);                   // factor 8 | Binv 0..2
-    out[6] = make_float4(g1.w, g2.x, g2.y, g2.z);                   // Binv 3..6
-    out[7] = make_float4(g2.w, g3.x, 0.0f, 0.0f);                   // Binv 7..8 | padding
+    __syncthreads();
+    const uint32_t i = i0 + threadIdx.x;
+    if (i < f.N) {
+        float* row = shRows + threadIdx.x * pitch;
+        const float4 g0 = gradRecords[4 * size_t(i)], g1 = gradRecords[4 * size_t(i) + 1],
+                     g2 = gradRecords[4 * size_t(i) + 2], g3 = gradRecords[4 * size_t(i) + 3];
+        float gp0 = g0.x, gp1 = g0.y, gp2 = g0.z;
+        float* gs = row;
+        if (counts[i] != 0u) {
+            const float4 r0 = ldg4(particles + 32 * size_t(i));
+            const V3 mu = v3(r0.x, r0.y, r0.z);
+            const V3 v = mu - v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]);
+            const float dist = __fsqrt_rn(dot3(v, v));
+            const V3 dir = v3(v.x / dist, v.y / dist, v.z / dist);
+            float basis[16], bx[16], by[16], bz[16];
+            sh_basis(f.shDegree, dir, basis);
+            sh_basis_grad(f.shDegree, dir, bx, by, bz);
+            const int nb = min(sh_count(f.shDegree), int(f.shCoeffs));
+            const float* c = row;
+            const float gr[3] = {g3.y, g3.z, g3.w};
+            V3 dg = v3(0.0f, 0.0f, 0.0f);
+            // unrolled with predicates: the basis arrays stay in registers; column
+            // ch of the row is read in full before its gradient overwrites it
+    #pragma unroll
+            for (int ch = 0; ch < 3; ++ch) {
+                float acc = basis[0] * c[ch];
+    #pragma unroll
+                for (int k = 1; k < 16; ++k)
+                    if (k < nb) acc = __fmaf_rn(basis[k], c[3 * k + ch], acc);
+                const float m = (acc + 0.5f) > 0.0f ? gr[ch] : 0.0f;
+    #pragma unroll
+                for (int k = 1; k < 16; ++k) {
+                    if (k < nb) {
+                        const float ck = c[3 * k + ch] * m;
+                        dg.x += bx[k] * ck;
+                        dg.y += by[k] * ck;
+                        dg.z += bz[k] * ck;
+                    }
+                }
+    #pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    if (k < nb) gs[3 * k + ch] = basis[k] * m;
+            }
+            for (int k = nb; k < int(f.shCoeffs); ++k) {
+                gs[3 * k] = 0.0f;
+                gs[3 * k + 1] = 0.0f;
+                gs[3 * k + 2] = 0.0f;
+            }
+            const float ndg = dot3(dir, dg);
+            gp0 += (dg.x - dir.x * ndg) / dist;
+            gp1 += (dg.y - dir.y * ndg) / dist;
+            gp2 += (dg.z - dir.z * ndg) / dist;
+        } else {
+            for (uint32_t k = 0; k < 3 * f.shCoeffs; ++k) gs[k] = 0.0f;
+        }
+        float4* out = reinterpret_cast<float4*>(gradParticles + 32 * size_t(i));
+        // rotation and intrinsic scale receive the extent channel's gradient (enable_normals)
+        const float4 gq = gradShape != nullptr ? gradShape[2 * size_t(i)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 gsc = gradShape != nullptr ? gradShape[2 * size_t(i) + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        out[0] = make_float4(gp0, gp1, gp2, g0.w);                      // pos, density
+        out[1] = gq;                                                    // rotation
+        out[2] = make_float4(gsc.x, gsc.y, gsc.z, 0.0f);                // scale, intrinsic density
+        out[3] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 0..3
+        out[4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 4..7
+        out[5] = make_float4(0.0f, g1.x, g1.y, g1.z);                   // factor 8 | Binv 0..2
+        out[6] = make_float4(g1.w, g2.x, g2.y, g2.z);                   // Binv 3..6
+        out[7] = make_float4(g2.w, g3.x, 0.0f, 0.0f);                   // Binv 7..8 | padding
+    }
+    __syncthreads();
+    float* dst = gradFeatures + size_t(i0) * rowLen;
+    for (uint32_t e = threadIdx.x; e < blockRows * rowLen; e += kProjectBwdThreads) {
+        const uint32_t p = e / rowLen;
+        dst[e] = shRows[p * pitch + (e - p * rowLen)];
+    }
 }
 
 }  // namespace gf

@@ -681,20 +681,36 @@ struct PackPtrs {
     const float* inverse;  // [N,9]
 };
 
+// The block's kThreads rows pass through shared memory (pitch 33 floats), so
+// that the [N,32] rows and every per-slot array are read and written with
+// consecutive threads on consecutive words.
+constexpr int kRowPitch = 33;
+
 __global__ __launch_bounds__(kThreads) void k_pack_rows(PackPtrs p, int64_t n, float4* __restrict__ out) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const float* f = p.factor + 9 * i;
-    const float* v = p.inverse + 9 * i;
-    float4* o = out + 8 * i;
-    o[0] = make_float4(p.pos[3 * i], p.pos[3 * i + 1], p.pos[3 * i + 2], p.dens[i]);
-    o[1] = make_float4(p.rot[4 * i], p.rot[4 * i + 1], p.rot[4 * i + 2], p.rot[4 * i + 3]);
-    o[2] = make_float4(p.scale[3 * i], p.scale[3 * i + 1], p.scale[3 * i + 2], p.idens[i]);
-    o[3] = make_float4(f[0], f[1], f[2], f[3]);
-    o[4] = make_float4(f[4], f[5], f[6], f[7]);
-    o[5] = make_float4(f[8], v[0], v[1], v[2]);
-    o[6] = make_float4(v[3], v[4], v[5], v[6]);
-    o[7] = make_float4(v[7], v[8], 0.0f, 0.0f);
+    __shared__ float rows[kThreads * kRowPitch];
+    const int64_t i0 = int64_t(blockIdx.x) * kThreads;
+    const int cnt = int(n - i0 < kThreads ? n - i0 : kThreads);
+    const int tid = threadIdx.x;
+    // slot s of the row <- width-w array, for the block's particles
+    auto gather = [&](const float* src, int w, int s0) {
+        for (int e = tid; e < w * cnt; e += kThreads) {
+            const int r = e / w;
+            rows[r * kRowPitch + s0 + (e - r * w)] = src[w * i0 + e];
+        }
+    };
+    gather(p.pos, 3, 0);
+    gather(p.dens, 1, 3);
+    gather(p.rot, 4, 4);
+    gather(p.scale, 3, 8);
+    gather(p.idens, 1, 11);
+    gather(p.factor, 9, 12);
+    gather(p.inverse, 9, 21);
+    for (int r = tid; r < cnt; r += kThreads) rows[r * kRowPitch + 30] = rows[r * kRowPitch + 31] = 0.0f;
+    __syncthreads();
+    for (int e = tid; e < 8 * cnt; e += kThreads) {
+        const float* q = rows + (e >> 3) * kRowPitch + 4 * (e & 7);
+        out[8 * i0 + e] = make_float4(q[0], q[1], q[2], q[3]);
+    }
 }
 
 struct UnpackPtrs {
@@ -708,29 +724,33 @@ struct UnpackPtrs {
 };
 
 __global__ __launch_bounds__(kThreads) void k_unpack_rows(const float4* __restrict__ in, int64_t n, UnpackPtrs p) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const float4* r = in + 8 * i;
-    const float4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3], r4 = r[4], r5 = r[5], r6 = r[6], r7 = r[7];
-    p.pos[3 * i] = r0.x;
-    p.pos[3 * i + 1] = r0.y;
-    p.pos[3 * i + 2] = r0.z;
-    p.dens[i] = r0.w;
-    p.rot[4 * i] = r1.x;
-    p.rot[4 * i + 1] = r1.y;
-    p.rot[4 * i + 2] = r1.z;
-    p.rot[4 * i + 3] = r1.w;
-    p.scale[3 * i] = r2.x;
-    p.scale[3 * i + 1] = r2.y;
-    p.scale[3 * i + 2] = r2.z;
-    p.idens[i] = r2.w;
-    float* f = p.factor + 9 * i;
-    float* v = p.inverse + 9 * i;
-    f[0] = r3.x; f[1] = r3.y; f[2] = r3.z; f[3] = r3.w;
-    f[4] = r4.x; f[5] = r4.y; f[6] = r4.z; f[7] = r4.w;
-    f[8] = r5.x; v[0] = r5.y; v[1] = r5.z; v[2] = r5.w;
-    v[3] = r6.x; v[4] = r6.y; v[5] = r6.z; v[6] = r6.w;
-    v[7] = r7.x; v[8] = r7.y;
+    __shared__ float rows[kThreads * kRowPitch];
+    const int64_t i0 = int64_t(blockIdx.x) * kThreads;
+    const int cnt = int(n - i0 < kThreads ? n - i0 : kThreads);
+    const int tid = threadIdx.x;
+    for (int e = tid; e < 8 * cnt; e += kThreads) {
+        const float4 v = in[8 * i0 + e];
+        float* q = rows + (e >> 3) * kRowPitch + 4 * (e & 7);
+        q[0] = v.x;
+        q[1] = v.y;
+        q[2] = v.z;
+        q[3] = v.w;
+    }
+    __syncthreads();
+    // width-w array <- slot s of the row, for the block's particles
+    auto scatter = [&](float* dst, int w, int s0) {
+        for (int e = tid; e < w * cnt; e += kThreads) {
+            const int r = e / w;
+            dst[w * i0 + e] = rows[r * kRowPitch + s0 + (e - r * w)];
+        }
+    };
+    scatter(p.pos, 3, 0);
+    scatter(p.dens, 1, 3);
+    scatter(p.rot, 4, 4);
+    scatter(p.scale, 3, 8);
+    scatter(p.idens, 1, 11);
+    scatter(p.factor, 9, 12);
+    scatter(p.inverse, 9, 21);
 }
 
 }  // namespace

@@ -289,13 +289,14 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     fa.enabled = t->cfg.admission_fallback == GF_FALLBACK_CONE ? 1 : 0;
     if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
-    if (int e = t->bigCount.ensure(sizeof(uint32_t) * 2, stream)) return e;
+    if (int e = t->bigCount.ensure(sizeof(uint32_t) * 4, stream)) return e;
     if (int e = t->wideList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
     fa.caps = t->caps.as<float4>();
     fa.big = t->bigList.as<uint32_t>();
     fa.bigCount = t->bigCount.as<uint32_t>();
     fa.wide = t->wideList.as<uint32_t>();
     fa.wideCount = t->bigCount.as<uint32_t>() + 1;
+    fa.bigCursor = t->bigCount.as<uint32_t>() + 2;
     {
         StageTimer st(t, GF_STAGE_TILE_RAYS, stream);
         if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
@@ -352,7 +353,8 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     }
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT, stream);
-        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, 2 * sizeof(uint32_t), stream));  // fallback and wide lists
+        // fallback and wide lists, and the fallback kernels' cursors
+        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, 4 * sizeof(uint32_t), stream));
         gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
                                                           t->proj.as<float4>(), t->records.as<float4>(),
                                                           t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),

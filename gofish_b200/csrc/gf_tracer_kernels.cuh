@@ -634,6 +634,7 @@ struct FallbackArgs {
     float4* caps;       // [N,2] for particles without a valid projection: (u, cos), (sin, mode, 0, 0)
     uint32_t* big;      // particles left to the warp kernel
     uint32_t* bigCount;
+    uint32_t* bigCursor;  // [2] next list entry of k_fallback_big (count, emit), zeroed per frame
     uint32_t* wide;     // projected particles whose tile box exceeds kWideTiles, left to k_wide
     uint32_t* wideCount;
 };
@@ -768,9 +769,16 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
     __shared__ uint32_t scratch[8][fb::kWarpScratch];
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* stack = scratch[threadIdx.x >> 5];
-    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
     const uint32_t total = *fa.bigCount;
-    for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
+    // each warp takes the next listed particle when it is done: the walks
+    // differ by orders of magnitude (caps near the camera span most tiles)
+    uint32_t* cursor = fa.bigCursor + (kEmit ? 1 : 0);
+    const auto next = [&]() {
+        uint32_t w = 0u;
+        if (lane == 0) w = atomicAdd(cursor, 1u);
+        return __shfl_sync(0xffffffffu, w, 0);
+    };
+    for (uint32_t w = next(); w < total; w = next()) {
         const uint32_t i = fa.big[w];
         const float4 c0 = fa.caps[2 * size_t(i)], c1 = fa.caps[2 * size_t(i) + 1];
         const fb::Cap c{c0.x, c0.y, c0.z, c0.w, c1.x, int(c1.y)};

@@ -87,11 +87,13 @@ def build_workload(args, rank: int, world: int = 1):
         w = sc.workload_single_view(**kw)
     pose = w.poses[0]
     if rank > 0:
-        # weak scaling: every further rank renders its own random view of the same scene
+        # weak scaling: every further rank renders its own view of the same
+        # scene, from rank 0's camera centre with its own random orientation,
+        # so that the ranks' work is comparable (the centre sets how close the
+        # nearest Gaussians are, which dominates a view's cost)
         rng = np.random.default_rng(5000 + rank)
-        c = rng.standard_normal(3)
-        c = c / np.linalg.norm(c) * 0.5 * np.cbrt(rng.random())
-        pose = sc.pose_world_to_sensor(c, sc.random_rotation_quaternion_xyzw(rng))
+        centre = sc.pose_to_c2w(pose)[:3, 3]
+        pose = sc.pose_world_to_sensor(centre, sc.random_rotation_quaternion_xyzw(rng))
     return w, [pose]
 
 

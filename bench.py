@@ -40,6 +40,9 @@ if ROOT not in sys.path:
 
 METRIC = "fisheye Mpix/s fwd+bwd"
 UNIT = "Mpix/s"
+SETTLE_WINDOW = 10     # untimed settling steps per window
+SETTLE_RATIO = 1.3     # a window is settled when no step exceeds this times its median
+SETTLE_CAP_S = 60.0    # settling ends after this long in any case
 
 
 def parse_args():
@@ -304,6 +307,26 @@ def run_gpu(args):
             s.bucket.allreduce()
         return s.loss if want_loss else None
 
+    # Settling (untimed): on a freshly booted box the host pauses for 30-40 ms
+    # now and then during its first minute or two, and a pause drains the one
+    # step of work queued on the GPU.  Steps run, synchronized, in windows of
+    # SETTLE_WINDOW until no step of a window (on any rank) takes more than
+    # SETTLE_RATIO times the window's median, or SETTLE_CAP_S have passed.
+    settle_steps = 0
+    settle_start = time.perf_counter()
+    while True:
+        times = []
+        for _ in range(SETTLE_WINDOW):
+            t_a = time.perf_counter()
+            step(resident)
+            torch.cuda.synchronize(device)
+            times.append(time.perf_counter() - t_a)
+        settle_steps += SETTLE_WINDOW
+        unsettled = torch.tensor([float(max(times) > SETTLE_RATIO * float(np.median(times)))], device=device)
+        if world > 1:
+            dist.all_reduce(unsettled, op=dist.ReduceOp.MAX)
+        if float(unsettled.item()) == 0.0 or time.perf_counter() - settle_start > SETTLE_CAP_S:
+            break
     for _ in range(args.warmup):
         step(resident)
     torch.cuda.synchronize(device)
@@ -430,6 +453,7 @@ def run_gpu(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
         "config": workload_config(w, args, world, views_per_rank), "e2e": e2e, "roofline": roofline,
         "gpu_launches": int(launches),
+        "settle_steps": settle_steps,
         "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
         "intersections_per_view": intersections,
         "fallback_particles_per_view": int(round(float(np.mean(view_fallback)))) if view_fallback else 0,

@@ -40,7 +40,8 @@ if ROOT not in sys.path:
 
 METRIC = "fisheye Mpix/s fwd+bwd"
 UNIT = "Mpix/s"
-SETTLE_WINDOW = 10     # untimed settling steps per window
+SETTLE_WINDOW = 25     # untimed settling steps per window
+SETTLE_CLEAN = 2       # consecutive settled windows that end the settling
 SETTLE_RATIO = 1.3     # a window is settled when no step exceeds this times its median
 SETTLE_CAP_S = 60.0    # settling ends after this long in any case
 
@@ -310,9 +311,11 @@ def run_gpu(args):
     # Settling (untimed): on a freshly booted box the host pauses for 30-40 ms
     # now and then during its first minute or two, and a pause drains the one
     # step of work queued on the GPU.  Steps run, synchronized, in windows of
-    # SETTLE_WINDOW until no step of a window (on any rank) takes more than
-    # SETTLE_RATIO times the window's median, or SETTLE_CAP_S have passed.
+    # SETTLE_WINDOW until SETTLE_CLEAN windows in a row have no step (on any
+    # rank) longer than SETTLE_RATIO times the window's median, or
+    # SETTLE_CAP_S have passed.
     settle_steps = 0
+    clean = 0
     settle_start = time.perf_counter()
     while True:
         times = []
@@ -325,7 +328,8 @@ def run_gpu(args):
         unsettled = torch.tensor([float(max(times) > SETTLE_RATIO * float(np.median(times)))], device=device)
         if world > 1:
             dist.all_reduce(unsettled, op=dist.ReduceOp.MAX)
-        if float(unsettled.item()) == 0.0 or time.perf_counter() - settle_start > SETTLE_CAP_S:
+        clean = clean + 1 if float(unsettled.item()) == 0.0 else 0
+        if clean >= SETTLE_CLEAN or time.perf_counter() - settle_start > SETTLE_CAP_S:
             break
     for _ in range(args.warmup):
         step(resident)

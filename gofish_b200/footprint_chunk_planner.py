@@ -1,3 +1,7 @@
+# Interface and decision logic follow tuallen/GOFish (threedgut_tracer), which carries:
+# Copyright Amazon.com, Inc. or its affiliates. All Rights Reserved.
+# SPDX-License-Identifier: CC-BY-NC-4.0
+
 """Memory plan for the per-view full-shape operator over N Gaussians
 (threedgut_tracer/footprint_chunk_planner.py:13-124, the same inputs,
 constants, decisions and FootprintChunkPlan record, so a caller's plan is

@@ -1,3 +1,7 @@
+# Portions derived from GOF (https://github.com/autonomousvision/gaussian-opacity-fields)
+# by way of tuallen/GOFish, distributed under the Gaussian-Splatting License (Inria / MPII;
+# non-commercial research and evaluation use).
+
 """Matched camera-min opacity field O(x) at query points
 (gofish/mesh/field.py:4-65).
 

@@ -1,3 +1,7 @@
+# Portions derived from GOF (https://github.com/autonomousvision/gaussian-opacity-fields)
+# by way of tuallen/GOFish, distributed under the Gaussian-Splatting License (Inria / MPII;
+# non-commercial research and evaluation use).
+
 """Tetrahedralization sites: each retained Gaussian's centre and the eight
 corners of its support box (gofish/mesh/sites.py:43-83).
 

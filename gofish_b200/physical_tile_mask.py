@@ -1,3 +1,7 @@
+# Interface and decision logic follow tuallen/GOFish (threedgut_tracer), which carries:
+# Copyright Amazon.com, Inc. or its affiliates. All Rights Reserved.
+# SPDX-License-Identifier: CC-BY-NC-4.0
+
 """16x16 tile mask of the calibrated camera domain (reference
 threedgut_tracer/physical_tile_mask.py:1-65, same token and semantics).
 

@@ -9,8 +9,7 @@
  *
  * Each entry point replaces one method of the reference's pybind module
  * (tuallen/GOFish, threedgut_tracer/bindings.cpp:106-165 and
- * src/splatRaster.cpp); the binding a maintainer adds on the reference side
- * is shown in INTEGRATION.md.
+ * src/splatRaster.cpp).
  */
 #ifndef GOFISH_B200_H
 #define GOFISH_B200_H

@@ -64,7 +64,9 @@ def random_shape(mods, n: int, seed: int):
 
 
 def main():
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/reference")
+    root = Path(sys.argv[1])
     mods = load_reference(root)
     shape = random_shape(mods, 257, seed=31)
     sites = mods["sites"].generate_sites(shape)

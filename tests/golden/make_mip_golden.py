@@ -57,7 +57,9 @@ def records():
 
 
 def main():
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/reference")
+    root = Path(sys.argv[1])
     mip = load(root)
     cameras, frames = records()
     table = mip.pack_camera_table(cameras, frames, "cpu")

@@ -32,7 +32,9 @@ CASES = [
 
 
 def main():
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/reference")
+    root = Path(sys.argv[1])
     spec = importlib.util.spec_from_file_location("ref_planner", root / "threedgut_tracer" /
                                                   "footprint_chunk_planner.py")
     mod = importlib.util.module_from_spec(spec)

@@ -58,7 +58,9 @@ def points(rng, m, n):
 
 
 def main():
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/reference")
+    root = Path(sys.argv[1])
     vof = load(root)
     rng = np.random.default_rng(8)
     out = {}

@@ -216,8 +216,31 @@ BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output grad
 FWD_TRAFFIC_PER_ALG_BYTE = 872.4 / 473.6
 BWD_TRAFFIC_PER_ALG_BYTE = 867.8 / 649.7
 TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio to the algorithmic bytes"
+# Warp instructions per tile intersection of the render kernels: ncu
+# smsp__inst_executed.sum of one full-size launch of this workload divided by
+# its intersections (3,373,688).  The kernels are bound by instruction issue:
+# the bench line's issue fraction is the instructions of the average launch
+# over the SMs' issue slots in its duration (148 SMs x 4 schedulers x one warp
+# instruction per cycle at the median SM clock sampled during the region).
+FWD_INST_PER_INTERSECTION = 2.22e9 / 3_373_688
+BWD_INST_PER_INTERSECTION = 2.07e9 / 3_373_688
+INST_SOURCE = "ncu smsp__inst_executed.sum of one full-size launch, per intersection"
+SM_COUNT = 148
+SCHEDULERS_PER_SM = 4
 # pixel footprint variance of the per-view full shape (render.gofish.pixel_footprint_variance)
 BENCH_GAMMA = 0.3
+
+
+def issue_roofline(inst_per_launch: float, avg_launch_s: float, clock_info, source: str) -> dict:
+    """Issue-slot fraction of a launch: warp instructions per second over
+    SM_COUNT x SCHEDULERS_PER_SM warp instructions per cycle at the median
+    sampled SM clock (the maximum clock when no sample was taken)."""
+    mhz = float(clock_info["sm_mhz"]) if clock_info else 1965.0
+    peak = SM_COUNT * SCHEDULERS_PER_SM * mhz * 1e6
+    achieved = inst_per_launch / avg_launch_s if avg_launch_s > 0 else 0.0
+    return {"unit": "G warp inst/s", "achieved": round(achieved / 1e9, 2), "peak": round(peak / 1e9, 2),
+            "frac": round(achieved / peak, 4), "inst_per_launch": int(inst_per_launch), "sm_mhz": mhz,
+            "inst_source": source}
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -445,7 +468,11 @@ def run_gpu(args):
         traffic = alg * FWD_TRAFFIC_PER_ALG_BYTE
     achieved = alg / avg_s / 1e9
     kernel = "k_render_bwd_log" if dominant == "render_bwd" else f"k_render_fwd<{w.k_buffer}>"
-    roofline = {"kernel": kernel, "bound": "hbm",
+    inst = intersections * (BWD_INST_PER_INTERSECTION if dominant == "render_bwd" else FWD_INST_PER_INTERSECTION)
+    roofline = {"kernel": kernel, "bound": "issue",
+                "issue": issue_roofline(inst, avg_s, clock_info, INST_SOURCE),
+                "note": "achieved/peak/frac are the HBM roofline of an instruction-issue-bound kernel; "
+                        "issue.frac is the binding one",
                 "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5),
                 "traffic": int(traffic), "traffic_source": TRAFFIC_SOURCE,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
@@ -600,7 +627,8 @@ def run_mesh(args):
     alg = (cand * FIELD_BYTES_PER_CANDIDATE + evals * FIELD_BYTES_PER_POINT) / integ_launches
     avg_s = integ_ms / integ_launches / 1000.0
     achieved = alg / avg_s / 1e9
-    roofline = {"kernel": "k_field_integrate<false>", "bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+    roofline = {"kernel": "k_field_integrate<false>", "bound": "issue", "achieved": round(achieved, 2), "peak": peak,
+                "note": "achieved/peak/frac are the HBM roofline of an instruction-issue-bound kernel",
                 "unit": "GB/s", "frac": round(achieved / peak, 5),
                 "traffic": int(alg * FIELD_TRAFFIC_PER_ALG_BYTE),
                 "traffic_source": "scaled from an ncu capture of a 300k-Gaussian case by algorithmic bytes",
@@ -704,22 +732,69 @@ def mesh_cpu_baseline(w, shape, points, cameras, budget_s: float = 15.0) -> dict
         spent += time.perf_counter() - t
         evals += 2 * sample
         sample *= 2
-    return {"value": round(evals / spent / 1e6, 6), "unit": MESH_UNIT, "cores": oracle.num_threads(), "kind": "port",
+    return {"value": round(evals / spent / 1e6, 6), "unit": MESH_UNIT, "cores": oracle.num_threads(), "cpu": cpu_model(), "kind": "port",
             "sample": f"{evals} (point, view) evaluations of random sites over 2 views, every one of "
                       f"{w.scene.num} Gaussians tested per point ({spent:.1f} s)"}
 
 
 # ----------------------------------------------------------------------------- CPU (oracle) arm
-def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0, cache: dict | None = None) -> dict:
-    """Times the oracle (scalar C++ restatement of the reference equations) on
-    a bounded sample: projection, binning and sort of every Gaussian, then
-    forward + backward compositing of a band of tile rows through the image
-    centre; the full-frame time is the projection/sort time plus the band time
-    scaled by the retained-tile ratio.  With ``cache``, the projection/sort
-    is timed on the first call only and its time and results are reused, and
-    the band grows until its own time exceeds half the budget."""
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo) and its logical CPU count."""
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{name} ({os.cpu_count()} logical CPUs)"
+
+
+def cpu_view_rows(w, pose, gamma: float = BENCH_GAMMA) -> np.ndarray:
+    """The [N,32] rows of one view as Tracer.render traces them (per-view full
+    shape with pixel variance ``gamma``), from the float64 oracle of the shape
+    operator."""
+    from gofish_b200.scene import pose_to_c2w
+    from oracle import full_shape as fs
+
+    cam, sc = w.camera, w.scene
+    n = sc.num
+    J, chart = fs.view_jacobian(sc.positions, pose_to_c2w(pose), True, cam.focal, cam.coefficients, cam.max_angle)
+    Q, observed = fs.minimum_norm_q(J, chart, gamma)
+    _C, B, Bi, _m, d = fs.full_shape(sc.scales, sc.rotations, sc.density[:, 0], Q, J, observed, gamma, True, "exact")
+    rows = np.zeros((n, 32), np.float32)
+    rows[:, 0:3] = sc.positions
+    rows[:, 3] = d
+    rows[:, 4:8] = sc.rotations
+    rows[:, 8:11] = sc.scales
+    rows[:, 11] = sc.density[:, 0]
+    rows[:, 12:21] = B.reshape(n, 9)
+    rows[:, 21:30] = Bi.reshape(n, 9)
+    return rows
+
+
+def spread_order(n: int) -> list:
+    """0..n-1 in bit-reversed (van der Corput) order: every window of the
+    list is spread evenly over the range."""
+    bits = max(1, (n - 1).bit_length())
+    return sorted(range(n), key=lambda i: int(format(i, f"0{bits}b")[::-1], 2))
+
+
+def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0, cache: dict | None = None,
+                 seed: int = 0) -> dict:
+    """Times the oracle (scalar C++ restatement of the reference equations,
+    all host threads) on a bounded sample of the benchmarked view: the
+    per-view full shape (float64 numpy oracle), projection, binning and sort
+    of every Gaussian, then forward + backward compositing of a sample of
+    whole tile rows spread over the frame (bit-reversed row order, rotated by
+    ``seed``), in rounds of doubling size until half the budget is spent.
+    The full-frame time is the shape/projection/sort time plus the sampled
+    compositing time scaled by retained tiles.  With ``cache``, the
+    shape/projection/sort is timed on the first call only and its time and
+    results are reused."""
     import oracle
-    from gofish_b200.scene import pack_particles
 
     cam = w.camera
     ocam = oracle.camera(1, cam.width, cam.height, cam.principal, cam.focal, cam.coefficients, cam.max_angle)
@@ -731,11 +806,11 @@ def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0, cache: di
         pose_o, rgb, ids, ranges, t_pb, parts, tmask = (cache[k] for k in ("pose", "rgb", "ids", "ranges", "t_pb",
                                                                            "parts", "tmask"))
     else:
-        parts = pack_particles(w.scene)
         pad = np.zeros((ty * 16, tx * 16), dtype=bool)
         pad[:h, :wd] = valid2
         tmask = pad.reshape(ty, 16, tx, 16).any(axis=(1, 3)).astype(np.uint8)
         t0 = time.perf_counter()
+        parts = cpu_view_rows(w, pose)
         pose_o = oracle.prepare_pose(pose)
         proj, rgb, counts = oracle.project(ocam, pose_o, parts, w.scene.features, w.scene.sh_degree, tmask, d)
         tr = oracle.tile_rays(ocam, pose_o, o, d)
@@ -743,35 +818,34 @@ def cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s: float = 20.0, cache: di
         t_pb = time.perf_counter() - t0
         if cache is not None:
             cache.update(pose=pose_o, rgb=rgb, ids=ids, ranges=ranges, t_pb=t_pb, parts=parts, tmask=tmask)
-    # band of tile rows around the centre, grown until the budget is used
-    rows = 1
-    centre = ty // 2
-    spent = 0.0
-    rendered_tiles = 0
+    order = spread_order(ty)
+    shift = (seed * 7) % ty
+    order = order[shift:] + order[:shift]
     t_render = 0.0
-    while True:
-        r0 = max(0, centre - rows // 2)
-        r1 = min(ty, r0 + rows)
-        tiles = (r0 * tx, r1 * tx)
+    rendered_tiles = 0
+    rows_done = 0
+    take = 4
+    while rows_done < ty and t_render <= budget_s / 2:
+        rows = order[rows_done:rows_done + take]
+        rows_done += len(rows)
+        take *= 2
+        tiles = np.concatenate([np.arange(r * tx, (r + 1) * tx) for r in rows]).astype(np.int32)
         t1 = time.perf_counter()
         rgba, hit_t, _ = oracle.render_forward(ocam, pose_o, parts, rgb, o, d, tmask, ranges, ids, w.k_buffer, tiles)
         grad = np.sign(rgba)
         grad[..., 3] = 0.0
         oracle.render_backward(ocam, pose_o, parts, rgb, o, d, tmask, ranges, ids, w.k_buffer, rgba, hit_t,
                                grad.astype(np.float32), np.zeros_like(hit_t), tiles)
-        t_render = time.perf_counter() - t1
-        rendered_tiles = int(tmask.reshape(-1)[tiles[0]:tiles[1]].sum())
-        spent = t_render if cache is not None else t_pb + t_render
-        if spent > budget_s / 2 or r1 - r0 >= ty:
-            break
-        rows *= 2
+        t_render += time.perf_counter() - t1
+        rendered_tiles += int(tmask.reshape(-1)[tiles].sum())
     retained = int(tmask.sum())
     full = t_pb + t_render * retained / max(1, rendered_tiles)
     pixels = cam.width * cam.height
-    return {"value": round(pixels / full / 1e6, 5), "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-            "sample": (f"projection+sort of all {w.scene.num} Gaussians ({t_pb:.2f} s), fwd+bwd of {rendered_tiles} "
-                       f"of {retained} retained tiles ({t_render:.2f} s), scaled to the full {cam.width}x{cam.height} "
-                       "frame")}
+    return {"value": round(pixels / full / 1e6, 5), "unit": UNIT, "cores": oracle.num_threads(), "cpu": cpu_model(),
+            "kind": "port",
+            "sample": (f"per-view full shape, projection and sort of all {w.scene.num} Gaussians ({t_pb:.2f} s), "
+                       f"fwd+bwd of {rendered_tiles} of {retained} retained tiles in {rows_done} tile rows spread "
+                       f"over the frame ({t_render:.2f} s), scaled to the full {cam.width}x{cam.height} frame")}
 
 
 # ----------------------------------------------------------------------------- inference orbit
@@ -925,7 +999,8 @@ def run_inference(args):
         "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
         "config": inference_config(w, args, world), "e2e": e2e,
-        "roofline": {"kernel": f"k_render_fwd<{w.k_buffer}>", "bound": "hbm", "achieved": round(achieved, 2),
+        "roofline": {"kernel": f"k_render_fwd<{w.k_buffer}>", "bound": "issue", "achieved": round(achieved, 2),
+                     "note": "achieved/peak/frac are the HBM roofline of an instruction-issue-bound kernel",
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "alg_bytes_per_launch": int(alg),
                      "avg_launch_ms": round(avg_s * 1000.0, 4)},
@@ -997,7 +1072,7 @@ def inference_cpu_baseline(w, tracer, batch, ray_o, ray_d, valid, budget_s: floa
         rows *= 2
     retained = int(tmask.sum())
     full = t_shape + t_pb + t_render * retained / max(1, rendered)
-    return {"value": round(1.0 / full, 6), "unit": INF_UNIT, "cores": oracle.num_threads(), "kind": "port",
+    return {"value": round(1.0 / full, 6), "unit": INF_UNIT, "cores": oracle.num_threads(), "cpu": cpu_model(), "kind": "port",
             "sample": (f"full shape of {sample.size} of {w.scene.num} rows ({t_shape:.2f} s scaled), projection+sort "
                        f"of all Gaussians ({t_pb:.2f} s), forward of {rendered} of {retained} retained tiles "
                        f"({t_render:.2f} s), scaled to one {cam.width}x{cam.height} frame")}
@@ -1077,7 +1152,7 @@ def run_reference(args):
     cache: dict = {}
     budget = max(0.4, 60.0 / max(1, args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        base = cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s=budget, cache=cache)
+        base = cpu_baseline(w, pose, ray_o, ray_d, valid, budget_s=budget, cache=cache, seed=i)
         if i >= args.warmup:
             values.append(base["value"])
     value = float(np.median(values))

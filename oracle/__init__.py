@@ -69,6 +69,34 @@ def _po(a):
     return None if a is None else _p(a)
 
 
+def _tiles(tiles, total):
+    """(tile index array or None, (t0, t1)) of a render call's ``tiles``."""
+    if tiles is None:
+        return None, (0, total)
+    if isinstance(tiles, tuple) and len(tiles) == 2:
+        return None, (int(tiles[0]), int(tiles[1]))
+    arr = np.ascontiguousarray(np.asarray(tiles, dtype=np.int32).reshape(-1))
+    if arr.size and (arr.min() < 0 or arr.max() >= total):
+        raise ValueError("tile index out of range")
+    return arr, (0, int(arr.size))
+
+
+class _tile_list:
+    """Context that sets the oracle's tile list for one render call."""
+
+    def __init__(self, lib, arr):
+        self.lib, self.arr = lib, arr
+
+    def __enter__(self):
+        if self.arr is not None:
+            self.lib.oracle_set_tile_list(_p(self.arr), int(self.arr.size))
+
+    def __exit__(self, *exc):
+        if self.arr is not None:
+            self.lib.oracle_set_tile_list(None, 0)
+        return False
+
+
 def load():
     global _lib
     if _lib is not None:
@@ -95,6 +123,7 @@ def load():
         "oracle_mip_best_rate": (i32, [vp, i64, vp, vp, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, i64, vp, vp, vp,
                                        vp]),
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
+        "oracle_set_tile_list": (None, [vp, i32]),
         "oracle_num_threads": (i32, []),
         "oracle_expf": (f32, [f32]),
         "oracle_logf": (f32, [f32]),
@@ -184,24 +213,32 @@ def bin(cam, pose, particles, proj, counts, mask, tile_ray_table, key_mode, ray_
     return keys[:total], ids[:total], ranges
 
 
-def render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, tiles=None):
+def render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, tiles=None, out=None):
+    """Forward compositing of the tiles ``tiles``: a range (t0, t1), an array
+    of tile indices, or None for all tiles.  ``out``: (rgba, hit_t, count)
+    arrays to write instead of new ones (pixels of other tiles keep their
+    contents)."""
     lib = load()
     h, w = cam.height, cam.width
     gx, gy = tile_grid(cam)
-    t0, t1 = (0, gx * gy) if tiles is None else tiles
-    rgba = np.zeros((h, w, 4), dtype=np.float32)
-    hit_t = np.full((h, w), 1e6, dtype=np.float32)
-    count = np.zeros((h, w), dtype=np.float32)
+    tile_list, (t0, t1) = _tiles(tiles, gx * gy)
+    if out is None:
+        rgba = np.zeros((h, w, 4), dtype=np.float32)
+        hit_t = np.full((h, w), 1e6, dtype=np.float32)
+        count = np.zeros((h, w), dtype=np.float32)
+    else:
+        rgba, hit_t, count = out
     particles = np.ascontiguousarray(particles, dtype=np.float32)
     ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
     if ids.size == 0:
         ids = np.zeros(1, dtype=np.uint32)
-    lib.oracle_render_forward(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
-                              _p(np.ascontiguousarray(rgb, dtype=np.float32)),
-                              _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
-                              _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
-                              _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
-                              _p(ids), int(k), int(t0), int(t1), _p(rgba), _p(hit_t), _p(count))
+    with _tile_list(lib, tile_list):
+        lib.oracle_render_forward(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                                  _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                                  _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                                  _p(ids), int(k), int(t0), int(t1), _p(rgba), _p(hit_t), _p(count))
     return rgba, hit_t, count
 
 
@@ -235,25 +272,30 @@ def render_forward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, so
 
 
 def render_backward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, sorted_ids, k, rgba, hit_t, grad_rgba,
-                    grad_hit_t, tiles=None):
+                    grad_hit_t, tiles=None, out=None):
+    """Gradient records [N,16] of the tiles ``tiles`` (a range (t0, t1), an
+    array of tile indices, or None for all tiles); ``out``: an array to
+    overwrite instead of a new one."""
     lib = load()
     gx, gy = tile_grid(cam)
-    t0, t1 = (0, gx * gy) if tiles is None else tiles
+    tile_list, (t0, t1) = _tiles(tiles, gx * gy)
     n = particles.shape[0]
-    grad = np.zeros((n, 16), dtype=np.float32)
+    grad = np.zeros((n, 16), dtype=np.float32) if out is None else out
     ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
     if ids.size == 0:
         ids = np.zeros(1, dtype=np.uint32)
-    lib.oracle_render_backward(ctypes.byref(cam), ctypes.byref(pose), n,
-                               _p(np.ascontiguousarray(particles, dtype=np.float32)),
-                               _p(np.ascontiguousarray(rgb, dtype=np.float32)),
-                               _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
-                               _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
-                               _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
-                               _p(ids), int(k), int(t0), int(t1), _p(np.ascontiguousarray(rgba, dtype=np.float32)),
-                               _p(np.ascontiguousarray(hit_t, dtype=np.float32)),
-                               _p(np.ascontiguousarray(grad_rgba, dtype=np.float32)),
-                               _p(np.ascontiguousarray(grad_hit_t, dtype=np.float32)), _p(grad))
+    with _tile_list(lib, tile_list):
+        lib.oracle_render_backward(ctypes.byref(cam), ctypes.byref(pose), n,
+                                   _p(np.ascontiguousarray(particles, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(rgb, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(mask, dtype=np.uint8)), _p(np.ascontiguousarray(ranges)),
+                                   _p(ids), int(k), int(t0), int(t1),
+                                   _p(np.ascontiguousarray(rgba, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(hit_t, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(grad_rgba, dtype=np.float32)),
+                                   _p(np.ascontiguousarray(grad_hit_t, dtype=np.float32)), _p(grad))
     return grad
 
 

@@ -115,9 +115,29 @@ void parallel_for(int begin, int end, int chunk, Fn&& fn) {
     body(0);
     for (auto& t : pool) t.join();
 }
+// Optional explicit tile list of the render entry points (oracle_set_tile_list):
+// when one is set they visit its tiles instead of the range [tileBegin, tileEnd).
+const int* g_tileList = nullptr;
+int g_tileListCount = 0;
+
+template <typename Fn>
+void parallel_tiles(int tileBegin, int tileEnd, Fn&& fn) {
+    if (g_tileList == nullptr) {
+        parallel_for(tileBegin, tileEnd, 1, fn);
+        return;
+    }
+    parallel_for(0, g_tileListCount, 1, [&](int i, int worker) { fn(g_tileList[i], worker); });
+}
 }  // namespace
 
 extern "C" {
+
+// Sets (tiles != NULL) or clears the tile list of the render entry points;
+// the caller keeps the list alive until it is cleared.
+void oracle_set_tile_list(const int* tiles, int count) {
+    g_tileList = tiles;
+    g_tileListCount = tiles != nullptr ? count : 0;
+}
 
 // Camera model parameters: threedgut_tracer/include/3dgut/sensors/cameraModels.h
 // (OpenCVPinholeProjectionParameters / OpenCVFisheyeProjectionParameters).
@@ -1274,7 +1294,7 @@ int oracle_render_forward(const OracleCamera* cam, const OraclePose* pose, int N
     const int W = cam->width, H = cam->height;
     const int gx = (W + kTile - 1) / kTile;
     Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
-    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int) {
+    parallel_tiles(tileBegin, tileEnd, [&](int tile, int) {
         if (mask[tile] == 0u) return;
         const int tx = tile % gx, ty = tile / gx;
         for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
@@ -1308,7 +1328,7 @@ int oracle_render_forward_geo(const OracleCamera* cam, const OraclePose* pose, i
     const int W = cam->width, H = cam->height;
     const int gx = (W + kTile - 1) / kTile;
     Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
-    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int) {
+    parallel_tiles(tileBegin, tileEnd, [&](int tile, int) {
         if (mask[tile] == 0u) return;
         const int tx = tile % gx, ty = tile / gx;
         for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
@@ -1363,7 +1383,7 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
     const int nthreads = worker_count();
     std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads));
     {
-        parallel_for(tileBegin, tileEnd, 1, [&](int tile, int tid) {
+        parallel_tiles(tileBegin, tileEnd, [&](int tile, int tid) {
             std::vector<float>& acc = partial[size_t(tid)];
             if (acc.empty()) acc.assign(size_t(N) * 16, 0.0f);
             if (mask[tile] == 0u) return;
@@ -1484,7 +1504,7 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
     const int nthreads = worker_count();
     std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads)), partialShape(static_cast<size_t>(nthreads));
     const auto val = [](const float* p, size_t i) { return p != nullptr ? p[i] : 0.0f; };
-    parallel_for(tileBegin, tileEnd, 1, [&](int tile, int tid) {
+    parallel_tiles(tileBegin, tileEnd, [&](int tile, int tid) {
         std::vector<float>& acc = partial[size_t(tid)];
         std::vector<float>& accS = partialShape[size_t(tid)];
         if (acc.empty()) acc.assign(size_t(N) * 16, 0.0f);

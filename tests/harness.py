@@ -181,3 +181,49 @@ def horizon_case(seed: int = 31, n: int = 6000, big: int = 300, size: int = 192)
     scene = dc.replace(scene, positions=positions, scales=sc, rotations=rot, density=dens, features=feats)
     cam = fisheye_camera(size, size, 200.0, random_kb_coefficients(rng, 200.0))
     return make_case(scene, cam, IDENTITY_POSE.copy())
+
+def view_rows(model, batch, gamma: float):
+    """The packed [N,32] rows Tracer.render traces for one view: the per-view
+    full shape (Q_v with pixel variance ``gamma``, C = R S^2 R^T + Q_v, B =
+    C^(1/2) R, B^-1, density m*o) through the product's shape kernels."""
+    import torch
+
+    from gofish_b200.view_observation_filter import build_intrinsic_view_shape
+
+    n = model.num_gaussians
+    shape = build_intrinsic_view_shape(model.get_scale(), model.get_rotation(), model.get_density(), model.positions,
+                                       batch, pixel_footprint_variance=gamma)
+    packed = torch.zeros((n, 32), dtype=torch.float32, device=model.positions.device)
+    packed[:, 0:3] = model.positions
+    packed[:, 3:4] = shape.density.reshape(n, 1)
+    packed[:, 4:8] = model.get_rotation()
+    packed[:, 8:11] = model.get_scale()
+    packed[:, 11:12] = model.get_density()
+    packed[:, 12:21] = shape.factor.reshape(n, 9)
+    packed[:, 21:30] = shape.inverse_factor.reshape(n, 9)
+    return packed
+
+
+def compare_forward(ref, got, image_atol: float = 1e-3, tiles=None):
+    """Bit-exact projected state, counts, keys, ids, ranges and visibility;
+    hit counts bit-exact, images max-abs <= ``image_atol`` with PSNR >= 60
+    dB and hit distance relative <= 1e-3, over the pixels of ``tiles``
+    ([t0, t1) tile range, row-major) or the whole frame."""
+    np.testing.assert_array_equal(got["proj"].view(np.uint32), ref["proj"].view(np.uint32))
+    np.testing.assert_array_equal(got["counts"].astype(np.uint32), ref["counts"])
+    np.testing.assert_array_equal(got["keys"].view(np.uint64), ref["keys"])
+    np.testing.assert_array_equal(got["ids"].view(np.uint32), ref["ids"])
+    np.testing.assert_array_equal(got["ranges"].view(np.uint32), ref["ranges"])
+    np.testing.assert_array_equal(got["visibility"], ref["visibility"])
+    h, w = ref["hit_count"].shape
+    if tiles is None:
+        sel = (slice(None), slice(None))
+    else:
+        tx = (w + 15) // 16
+        r0, r1 = tiles[0] // tx, (tiles[1] + tx - 1) // tx
+        assert tiles[0] % tx == 0 and tiles[1] % tx == 0, "tile bands are whole tile rows"
+        sel = (slice(16 * r0, min(h, 16 * r1)), slice(None))
+    np.testing.assert_array_equal(got["hit_count"][sel], ref["hit_count"][sel])
+    assert np.abs(got["rgba"][sel] - ref["rgba"][sel]).max() <= image_atol
+    assert psnr(got["rgba"][sel], ref["rgba"][sel]) >= 60.0
+    np.testing.assert_allclose(got["hit_t"][sel], ref["hit_t"][sel], rtol=1e-3, atol=1e-4)

@@ -40,10 +40,6 @@ if ROOT not in sys.path:
 
 METRIC = "fisheye Mpix/s fwd+bwd"
 UNIT = "Mpix/s"
-SETTLE_WINDOW = 25     # untimed settling steps per window
-SETTLE_CLEAN = 2       # consecutive settled windows that end the settling
-SETTLE_RATIO = 1.3     # a window is settled when no step exceeds this times its median
-SETTLE_CAP_S = 60.0    # settling ends after this long in any case
 
 
 def parse_args():
@@ -302,8 +298,8 @@ def run_gpu(args):
     tracer = Tracer(conf)
     raster = tracer.tracer_wrapper
     scale = 1.0 / (3.0 * n_valid)
-    view_intersections: list[int] = []
-    view_fallback: list[int] = []
+
+    host_times = {"render": 0.0, "backward": 0.0}
 
     def step(s, want_loss=False):
         """Forward, L1 loss and backward of every local view of input set s
@@ -317,53 +313,30 @@ def run_gpu(args):
                 p.grad = None
         s.loss.zero_()
         for v, batch in enumerate(batches):
+            h0 = time.perf_counter()
             out = tracer.render(s.model, batch, train=True, frame_id=v)
-            st = raster.stats()
-            view_intersections.append(int(st.num_intersections))
-            view_fallback.append(int(st.fallback_particles))
+            host_times["render"] += time.perf_counter() - h0
             loss = ((out["pred_features"][0] - s.target[v]).abs() * valid_f).sum() * scale
             if s.bucket is not None and v == len(batches) - 1:
                 s.bucket.arm()
+            h1 = time.perf_counter()
             loss.backward()
+            host_times["backward"] += time.perf_counter() - h1
             if want_loss:
                 s.loss.add_(loss.detach())
         if s.bucket is not None:
             s.bucket.allreduce()
         return s.loss if want_loss else None
 
-    # Settling (untimed): on a freshly booted box the host pauses for 30-40 ms
-    # now and then during its first minute or two, and a pause drains the one
-    # step of work queued on the GPU.  Steps run, synchronized, in windows of
-    # SETTLE_WINDOW until SETTLE_CLEAN windows in a row have no step (on any
-    # rank) longer than SETTLE_RATIO times the window's median, or
-    # SETTLE_CAP_S have passed.
-    settle_steps = 0
-    clean = 0
-    settle_start = time.perf_counter()
-    while True:
-        times = []
-        for _ in range(SETTLE_WINDOW):
-            t_a = time.perf_counter()
-            step(resident)
-            torch.cuda.synchronize(device)
-            times.append(time.perf_counter() - t_a)
-        settle_steps += SETTLE_WINDOW
-        unsettled = torch.tensor([float(max(times) > SETTLE_RATIO * float(np.median(times)))], device=device)
-        if world > 1:
-            dist.all_reduce(unsettled, op=dist.ReduceOp.MAX)
-        clean = clean + 1 if float(unsettled.item()) == 0.0 else 0
-        if clean >= SETTLE_CLEAN or time.perf_counter() - settle_start > SETTLE_CAP_S:
-            break
     for _ in range(args.warmup):
         step(resident)
     torch.cuda.synchronize(device)
-    intersections = int(raster.stats().num_intersections)
 
     # --- device-timed region: inputs resident in HBM
-    view_intersections.clear()
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
-    launches_before = int(raster.stats().total_kernel_launches)
+    stats_before = raster.stats()
+    launches_before = int(stats_before.total_kernel_launches)
     # the set-up's garbage is collected, and what survives is kept out of later collections
     gc.collect()
     gc.freeze()
@@ -374,18 +347,26 @@ def run_gpu(args):
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
+    host_times["render"] = host_times["backward"] = 0.0
+    host_start = time.perf_counter()
     for _ in range(args.steps):
         step(resident)
     t1.record(stream)
+    host_enqueue_s = time.perf_counter() - host_start
+    host_split = dict(host_times)
     torch.cuda.synchronize(device)
     clock_info = clocks.stop()
     if world > 1:
         dist.barrier()
     elapsed_ms = t0.elapsed_time(t1)
-    timed_intersections = list(view_intersections)
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
-    launches = int(raster.stats().total_kernel_launches) - launches_before
+    stats_after = raster.stats()
+    launches = int(stats_after.total_kernel_launches) - launches_before
+    forwards = max(1, int(stats_after.total_forwards - stats_before.total_forwards))
+    intersections = int(round((stats_after.total_intersections - stats_before.total_intersections) / forwards))
+    fallback_per_view = int(round((stats_after.total_fallback_particles - stats_before.total_fallback_particles)
+                                  / forwards))
     log_overflow = raster.log_overflow_tiles()
     # the full-shape kernels: Q_v, the shape forward and its VJP per view (one chunk each at these sizes)
     free, total = torch.cuda.mem_get_info(device)
@@ -459,7 +440,6 @@ def run_gpu(args):
     dom_ms, dom_launches = stages[dominant]
     avg_s = dom_ms / max(1, dom_launches) / 1000.0
     # per-launch bytes use the mean intersection count of the timed views
-    intersections = int(round(float(np.mean(timed_intersections)))) if timed_intersections else intersections
     if dominant == "render_bwd":
         alg = intersections * BWD_RENDER_BYTES_PER_INTERSECTION + pixels * BWD_RENDER_BYTES_PER_PIXEL
         traffic = alg * BWD_TRAFFIC_PER_ALG_BYTE
@@ -484,10 +464,14 @@ def run_gpu(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
         "config": workload_config(w, args, world, views_per_rank), "e2e": e2e, "roofline": roofline,
         "gpu_launches": int(launches),
-        "settle_steps": settle_steps,
+        "host_enqueue_ms_per_step": round(host_enqueue_s * 1000.0 / args.steps, 4),
+        "host_ms_per_step": {"render": round(host_split["render"] * 1000.0 / args.steps, 4),
+                             "backward": round(host_split["backward"] * 1000.0 / args.steps, 4),
+                             "library_waits": round((stats_after.total_host_wait_us - stats_before.total_host_wait_us)
+                                                    / 1000.0 / args.steps, 4)},
         "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
         "intersections_per_view": intersections,
-        "fallback_particles_per_view": int(round(float(np.mean(view_fallback)))) if view_fallback else 0,
+        "fallback_particles_per_view": fallback_per_view,
         "log_overflow_tiles_last_view": log_overflow,
     }
     if clock_info is not None:
@@ -553,6 +537,7 @@ def run_mesh(args):
     from gofish_b200.mesh import SplatRaster
     from gofish_b200.mesh.bisection import refine_crossings
     from gofish_b200.mesh.field import camera_inputs, evaluate_field, signed_field
+    from gofish_b200.mesh.sharded import gather_shards_tensor, shard_bounds
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -566,7 +551,7 @@ def run_mesh(args):
 
     w, shape, points_all, cameras = mesh_workload(args)
     q_total = points_all.shape[0]
-    lo, hi = q_total * rank // world, q_total * (rank + 1) // world
+    lo, hi = shard_bounds(q_total, rank, world)
     points = np.ascontiguousarray(points_all[lo:hi])
     views = len(cameras)
 
@@ -577,11 +562,16 @@ def run_mesh(args):
     cam_args = [camera_inputs(c, device) for c in cameras]
 
     def field_pass():
+        """One field pass over this rank's points; with N > 1 ranks the
+        [Q] results of all ranks are then all-gathered on the device (the
+        sharded query's only exchange)."""
         token = raster.begin_opacity_field(packed, sigma, query)
         for a in cam_args:
             raster.integrate_opacity_field_camera(token, *a)
         out = raster.finish_opacity_field(token)
         raster.release_opacity_field(token)
+        if world > 1:
+            out = (gather_shards_tensor(out[0], q_total), gather_shards_tensor(out[1], q_total), out[2])
         return out
 
     for _ in range(args.warmup):
@@ -614,6 +604,8 @@ def run_mesh(args):
     elapsed_ms = float(elapsed.item())
     value = q_total * views * args.steps / (elapsed_ms / 1000.0) / 1e6
     minimum, observed = out[0].cpu().numpy(), out[1].cpu().numpy()
+    if world > 1:  # this rank's points (the gathered field holds every rank's)
+        minimum, observed = minimum[lo:hi], observed[lo:hi]
 
     # --- roofline of the ordered-integration kernel
     peak, peak_kind = measured_peaks()
@@ -928,8 +920,8 @@ def run_inference(args):
     torch.cuda.synchronize(device)
     raster.collect_stage_times()
     raster.enable_stage_timing(True)
-    launches_before = int(raster.stats().total_kernel_launches)
-    inter = []
+    stats_before = raster.stats()
+    launches_before = int(stats_before.total_kernel_launches)
     gc.collect()
     gc.freeze()
     clocks.mark()
@@ -941,7 +933,6 @@ def run_inference(args):
     t0.record(stream)
     for s_ in range(args.steps):
         tracer.render(batches[frame_of(args.warmup + s_)])
-        inter.append(int(raster.stats().num_intersections))
     t1.record(stream)
     torch.cuda.synchronize(device)
     clock_info = clocks.stop()
@@ -949,7 +940,10 @@ def run_inference(args):
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
     # the tracer's launches plus the per-frame shape kernels (view Q + full shape, or the fused one)
-    launches = int(raster.stats().total_kernel_launches) - launches_before
+    stats_after = raster.stats()
+    launches = int(stats_after.total_kernel_launches) - launches_before
+    frames_read = max(1, int(stats_after.total_forwards - stats_before.total_forwards))
+    mean_intersections = (stats_after.total_intersections - stats_before.total_intersections) / frames_read
     launches += args.steps * (2 if args.shape == "exact" else 1)
     ms_max = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
     if world > 1:
@@ -990,7 +984,7 @@ def run_inference(args):
     peak, peak_kind = measured_peaks()
     fwd_ms, fwd_launches = stages["render_fwd"]
     avg_s = fwd_ms / max(1, fwd_launches) / 1000.0
-    intersections = int(round(float(np.mean(inter)))) if inter else 0
+    intersections = int(round(mean_intersections))
     pixels = cam.width * cam.height
     alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
     achieved = alg / avg_s / 1e9 if avg_s > 0 else 0.0

@@ -16,6 +16,8 @@ GF_CAMERA_OPENCV_FISHEYE = 1
 GF_KEY_PER_TILE_DEPTH = 0
 GF_KEY_GLOBAL_DEPTH = 1
 GF_FALLBACK_NONE = 0
+GF_CAPACITY_SPECULATIVE = 0
+GF_CAPACITY_EXACT = 1
 GF_FALLBACK_CONE = 1
 STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
 
@@ -44,6 +46,7 @@ class GfTracerConfig(ctypes.Structure):
         ("admission_fallback", ctypes.c_int32),
         ("composite_log_capacity", ctypes.c_int32),
         ("enable_normals", ctypes.c_int32),
+        ("intersection_capacity", ctypes.c_int32),
     ]
 
 
@@ -110,6 +113,10 @@ class GfTraceStats(ctypes.Structure):
         ("kernel_launches", ctypes.c_uint32),
         ("fallback_particles", ctypes.c_uint32),
         ("total_kernel_launches", ctypes.c_uint64),
+        ("total_forwards", ctypes.c_uint64),
+        ("total_intersections", ctypes.c_uint64),
+        ("total_fallback_particles", ctypes.c_uint64),
+        ("total_host_wait_us", ctypes.c_uint64),
     ]
 
 
@@ -209,6 +216,7 @@ _SIGNATURES = [
      [_vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, _vp,
       ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]),
     ("gf_field_collect_times", ctypes.c_int, [_vp, _vp, _vp]),
+    ("gf_mesh_sites", ctypes.c_int, [_vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
 ]
 
 STATIC_SORT_MAX_PAIRS = 262144
@@ -237,7 +245,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 3:
+    if lib.gf_abi_version() != 4:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

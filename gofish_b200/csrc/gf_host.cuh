@@ -128,9 +128,12 @@ int scan_exclusive(DeviceBuffer& tiles, uint32_t& launches, const In* in, uint64
 
 // Stable LSD radix sort of (u64 key, u32 value) pairs held in keys[0]/ids[0]
 // over the key bits [beginBit, endBit), ping-ponging with keys[1]/ids[1];
-// *finalBuf names the buffer that holds the result.
+// *finalBuf names the buffer that holds the result.  With nDev the number of
+// pairs is read on the device (at most n, which sizes the grids), so the host
+// need not know it.
 int sort_pairs(DeviceBuffer& hist, DeviceBuffer& tiles, uint32_t& launches, DeviceBuffer* keys, DeviceBuffer* ids,
-               uint32_t n, int beginBit, int endBit, int* finalBuf, cudaStream_t stream) {
+               uint32_t n, int beginBit, int endBit, int* finalBuf, cudaStream_t stream,
+               const uint32_t* nDev = nullptr) {
     *finalBuf = 0;
     if (n == 0) return GF_OK;
     const uint32_t blocks = (n + gf::kSortTile - 1) / gf::kSortTile;
@@ -140,7 +143,8 @@ int sort_pairs(DeviceBuffer& hist, DeviceBuffer& tiles, uint32_t& launches, Devi
     GF_CUDA(cudaFuncSetAttribute(gf::k_radix_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int src = 0;
     for (int shift = beginBit; shift < endBit; shift += 8) {
-        gf::k_radix_histogram<<<blocks, gf::kSortThreads, 0, stream>>>(keys[src].as<uint64_t>(), n, shift, blocks, h);
+        gf::k_radix_histogram<<<blocks, gf::kSortThreads, 0, stream>>>(keys[src].as<uint64_t>(), n, shift, blocks, h,
+                                                                      nDev);
         launches += 1;
         GF_LAUNCH_CHECK();
         if (int e = scan_exclusive<uint32_t, uint32_t>(tiles, launches, h, uint64_t(blocks) * gf::kRadixBins, h,
@@ -149,7 +153,8 @@ int sort_pairs(DeviceBuffer& hist, DeviceBuffer& tiles, uint32_t& launches, Devi
         gf::k_radix_scatter<<<blocks, gf::kSortThreads, smem, stream>>>(keys[src].as<uint64_t>(),
                                                                         ids[src].as<uint32_t>(),
                                                                         keys[src ^ 1].as<uint64_t>(),
-                                                                        ids[src ^ 1].as<uint32_t>(), n, shift, blocks, h);
+                                                                        ids[src ^ 1].as<uint32_t>(), n, shift, blocks, h,
+                                                                        nDev);
         launches += 1;
         GF_LAUNCH_CHECK();
         src ^= 1;

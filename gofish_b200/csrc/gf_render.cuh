@@ -878,10 +878,11 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     s.depth = s.depth + gdist * weight;
     const bool tail = nextT <= kMinTransmittance;
     const float invNext = tail ? 0.0f : __fdividef(1.0f, nextT);
+    // From here on the values only scale gradients (compared with tolerances,
+    // not bit for bit): products and sums are fused where they pair up.
     const float residualHitT = fmaxf((s.hitTB - s.depth) * invNext, 0.0f);
     const float galphaRayHitGrd = (gdist - residualHitT) * s.T * s.hitTG;
     const float residualTrm = galpha < 0.999999f ? s.TB * __fdividef(1.0f, 1.0f - galpha) : s.T;
-    const float galphaRayDnsGrd = residualTrm * -s.TG;
     const float cr = fmaxf(q.d.y, 0.0f), cg = fmaxf(q.d.z, 0.0f), cb = fmaxf(q.d.w, 0.0f);
     s.r = __fmaf_rn(cr, weight, s.r);
     s.g = __fmaf_rn(cg, weight, s.g);
@@ -889,10 +890,9 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     const float rr = fmaxf((s.featB[0] - s.r) * invNext, 0.0f);
     const float rg = fmaxf((s.featB[1] - s.g) * invNext, 0.0f);
     const float rb = fmaxf((s.featB[2] - s.b) * invNext, 0.0f);
-    float comp = galphaRayHitGrd + galphaRayDnsGrd;
-    comp += s.T * (cr - rr) * s.featG[0];
-    comp += s.T * (cg - rg) * s.featG[1];
-    comp += s.T * (cb - rb) * s.featG[2];
+    float comp = __fmaf_rn(residualTrm, -s.TG, galphaRayHitGrd);
+    const float colourGrad = __fmaf_rn(cb - rb, s.featG[2], __fmaf_rn(cg - rg, s.featG[1], (cr - rr) * s.featG[0]));
+    comp = __fmaf_rn(s.T, colourGrad, comp);
     float tauGrad = weight * s.hitTG;
     // Geometric channels (gaussianParticles.cuh:786-1062): the depth moment
     // and the normal sum reach alpha through their residuals; the depth moment
@@ -956,28 +956,30 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
     const float gresGrd = density * gU;
     const float grayDistGrd = -0.5f * gres * gresGrd;
     // Closest-point VJP (reference gutHalfRayResponse.cuh:39-62).
-    const V3 pointGrad = (2.0f * grayDistGrd) * p;
-    V3 groGrd = pointGrad;
-    V3 grduGrd = tau * pointGrad;
-    const float totalTauGrad = tauGrad + dot3(pointGrad, grdu);
+    const float pg = 2.0f * grayDistGrd;
+    V3 groGrd = v3(pg * p.x, pg * p.y, pg * p.z);
+    V3 grduGrd = v3(tau * groGrd.x, tau * groGrd.y, tau * groGrd.z);
+    const float totalTauGrad = __fmaf_rn(groGrd.z, grdu.z, __fmaf_rn(groGrd.y, grdu.y, __fmaf_rn(groGrd.x, grdu.x, tauGrad)));
     if (interior) {
         const float invDen = __fdividef(1.0f, denom);
-        const float inv = -invDen;
-        const V3 tauOriginGrad = inv * grdu;
-        const V3 tauDirectionGrad = inv * gro + ((2.0f * num) * (invDen * invDen)) * grdu;
-        groGrd = groGrd + totalTauGrad * tauOriginGrad;
-        grduGrd = grduGrd + totalTauGrad * tauDirectionGrad;
+        // tau = -num / denom: dtau/dgro = -grdu / denom, dtau/dgrdu = -gro / denom + 2 num grdu / denom^2
+        const float a = -totalTauGrad * invDen;
+        const float b = (2.0f * num) * (invDen * invDen) * totalTauGrad;
+        groGrd = v3(__fmaf_rn(a, grdu.x, groGrd.x), __fmaf_rn(a, grdu.y, groGrd.y), __fmaf_rn(a, grdu.z, groGrd.z));
+        grduGrd = v3(__fmaf_rn(b, grdu.x, __fmaf_rn(a, gro.x, grduGrd.x)),
+                     __fmaf_rn(b, grdu.y, __fmaf_rn(a, gro.y, grduGrd.y)),
+                     __fmaf_rn(b, grdu.z, __fmaf_rn(a, gro.z, grduGrd.z)));
     }
     // Binv rows: r0 = (b.x b.y b.z), r1 = (b.w c.x c.y), r2 = (c.z c.w d.x).
-    const float gpx = -(groGrd.x * q.b.x + groGrd.y * q.b.w + groGrd.z * q.c.z);
-    const float gpy = -(groGrd.x * q.b.y + groGrd.y * q.c.x + groGrd.z * q.c.w);
-    const float gpz = -(groGrd.x * q.b.z + groGrd.y * q.c.y + groGrd.z * q.d.x);
-    const float m00 = groGrd.x * gp.x + grduGrd.x * ray.d.x, m01 = groGrd.x * gp.y + grduGrd.x * ray.d.y,
-                m02 = groGrd.x * gp.z + grduGrd.x * ray.d.z;
-    const float m10 = groGrd.y * gp.x + grduGrd.y * ray.d.x, m11 = groGrd.y * gp.y + grduGrd.y * ray.d.y,
-                m12 = groGrd.y * gp.z + grduGrd.y * ray.d.z;
-    const float m20 = groGrd.z * gp.x + grduGrd.z * ray.d.x, m21 = groGrd.z * gp.y + grduGrd.z * ray.d.y,
-                m22 = groGrd.z * gp.z + grduGrd.z * ray.d.z;
+    const float gpx = -__fmaf_rn(groGrd.z, q.c.z, __fmaf_rn(groGrd.y, q.b.w, groGrd.x * q.b.x));
+    const float gpy = -__fmaf_rn(groGrd.z, q.c.w, __fmaf_rn(groGrd.y, q.c.x, groGrd.x * q.b.y));
+    const float gpz = -__fmaf_rn(groGrd.z, q.d.x, __fmaf_rn(groGrd.y, q.c.y, groGrd.x * q.b.z));
+    const float m00 = __fmaf_rn(grduGrd.x, ray.d.x, groGrd.x * gp.x), m01 = __fmaf_rn(grduGrd.x, ray.d.y, groGrd.x * gp.y),
+                m02 = __fmaf_rn(grduGrd.x, ray.d.z, groGrd.x * gp.z);
+    const float m10 = __fmaf_rn(grduGrd.y, ray.d.x, groGrd.y * gp.x), m11 = __fmaf_rn(grduGrd.y, ray.d.y, groGrd.y * gp.y),
+                m12 = __fmaf_rn(grduGrd.y, ray.d.z, groGrd.y * gp.z);
+    const float m20 = __fmaf_rn(grduGrd.z, ray.d.x, groGrd.z * gp.x), m21 = __fmaf_rn(grduGrd.z, ray.d.y, groGrd.z * gp.y),
+                m22 = __fmaf_rn(grduGrd.z, ray.d.z, groGrd.z * gp.z);
     g[0] = make_float4(gpx, gpy, gpz, gDensity);
     g[1] = make_float4(m00, m01, m02, m10);
     g[2] = make_float4(m11, m12, m20, m21);
@@ -1030,19 +1032,32 @@ __device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords
     const uint32_t leaderIdx = __shfl_sync(0xffffffffu, idx, leader);
     const bool uniform = __all_sync(0xffffffffu, !have || idx == leaderIdx);
     if (uniform && __popc(hm) > 1) {
-        float4 v[4];
+        // Reduce-scatter over the warp: at each level the lane pair (lane,
+        // lane ^ o) splits the components it still holds, each keeping one
+        // half and adding its partner's copy of that half (16 + 8 + 4 + 2
+        // shuffles), then the last pair adds its one component; lane 2c
+        // ends with component c of the warp's sum and the 16 lanes add their
+        // components with one instruction.
+        float v[16];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = have ? g[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) v[k] = add4(v[k], shfl_down4(v[k], o));
+        for (int k = 0; k < 4; ++k) {
+            v[4 * k] = have ? g[k].x : 0.0f;
+            v[4 * k + 1] = have ? g[k].y : 0.0f;
+            v[4 * k + 2] = have ? g[k].z : 0.0f;
+            v[4 * k + 3] = have ? g[k].w : 0.0f;
         }
-        if (lane == 0) {
-            float4* dst = gradRecords + 4 * size_t(leaderIdx);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) atomicAdd(dst + k, v[k]);
+        for (int half = 8, o = 16; half >= 1; half >>= 1, o >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+                const float keep = upper ? v[i + half] : v[i];
+                const float send = upper ? v[i] : v[i + half];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
         }
+        const float total = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+        if ((lane & 1) == 0) atomicAdd(reinterpret_cast<float*>(gradRecords + 4 * size_t(leaderIdx)) + (lane >> 1), total);
     } else {
         // Merge tree over the 8x4 pixel block: at each level (horizontal pairs,
         // vertical pairs, then pairs of those) two lanes that own sums for the

@@ -123,10 +123,14 @@ constexpr int kRadixBins = 256;
 __device__ __forceinline__ uint32_t digit_of(uint64_t key, int shift) { return uint32_t(key >> shift) & 0xffu; }
 
 // Per-block digit counts, stored digit-major: hist[digit * numBlocks + block].
+// With nDev the item count is read from device memory (at most n, the count
+// the grid was sized for); blocks past it store zero counts.
 __global__ __launch_bounds__(kSortThreads) void k_radix_histogram(const uint64_t* __restrict__ keys, uint32_t n,
                                                                   int shift, uint32_t numBlocks,
-                                                                  uint32_t* __restrict__ hist) {
+                                                                  uint32_t* __restrict__ hist,
+                                                                  const uint32_t* __restrict__ nDev = nullptr) {
     __shared__ uint32_t h[kSortWarps][kRadixBins];
+    if (nDev != nullptr) n = min(n, *nDev);
     for (int i = threadIdx.x; i < kSortWarps * kRadixBins; i += kSortThreads) (&h[0][0])[i] = 0u;
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -173,8 +177,11 @@ __global__ __launch_bounds__(kSortThreads, 2) void k_radix_scatter(const uint64_
                                                                 uint64_t* __restrict__ keysOut,
                                                                 uint32_t* __restrict__ valsOut, uint32_t n,
                                                                 int shift, uint32_t numBlocks,
-                                                                const uint32_t* __restrict__ histScanned) {
+                                                                const uint32_t* __restrict__ histScanned,
+                                                                const uint32_t* __restrict__ nDev = nullptr) {
     extern __shared__ __align__(16) unsigned char smemRaw[];
+    if (nDev != nullptr) n = min(n, *nDev);
+    if (blockIdx.x * uint32_t(kSortTile) >= n) return;  // block-uniform: nothing of this block to move
     SortScatterSmem& sm = *reinterpret_cast<SortScatterSmem*>(smemRaw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < kSortCounters * kRadixBins; i += kSortThreads) (&sm.warpHist[0][0])[i] = 0u;

@@ -7,16 +7,28 @@
 // and the backward gradient records.  Buffers grow geometrically and are
 // stream-ordered (cudaMallocAsync), so steady-state frames allocate nothing.
 //
-// Host synchronization: exactly one per forward pass, to read the number of
-// tile intersections after the count scan (the reference synchronizes about
-// eight times, gutRenderer.cu:843-1599).
+// Host synchronization: none in the steady state.  The number of tile
+// intersections is known only on the device after the count scan; the keys
+// and ids are sized by a speculative capacity (1.5x the largest count of the
+// earlier forwards) and every kernel after the scan reads the count from
+// device memory.  A device-side plan records the count and whether it
+// exceeded the capacity; the host reads the plans of finished forwards
+// without waiting (at most kMaxInFlight forwards are left unread), and
+// reports an overflowed forward -- which emitted, sorted and composited
+// nothing -- as GF_ERR_CAPACITY from the next call, with the capacity grown.
+// The first forward, a forward whose particle count or raster differs from
+// the last one read, and every forward of a tracer configured with
+// GF_CAPACITY_EXACT read the count after the scan with one synchronization
+// (the reference synchronizes about eight times, gutRenderer.cu:843-1599).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <map>
 #include <string>
 #include <vector>
@@ -45,6 +57,18 @@ struct TileMask {
 
 bool valid_k(int k) { return k == 0 || k == 4 || k == 8 || k == 12 || k == 16 || k == 24 || k == 32; }
 
+// Forwards whose intersection plan the host has not read yet, at most (the
+// next forward waits for the oldest beyond this), and the pinned plan slots.
+constexpr size_t kMaxInFlight = 4;
+constexpr int kPlanSlots = 8;
+
+struct InFlight {
+    cudaEvent_t done;   // recorded after the plan's copy to hostPlans[slot]
+    int slot;
+    uint64_t capacity;  // keys reserved for the forward
+    uint32_t N, T;
+};
+
 }  // namespace
 
 struct gf_tracer {
@@ -65,6 +89,18 @@ struct gf_tracer {
     bool frameGeo = false;                                // the last forward wrote the geometric channels
     uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size, [2] log overflow tiles (low 32 bits)
     uint32_t fallbackParticles = 0;
+    // Intersection plans (speculative key capacity).
+    DeviceBuffer plan;                    // gf::FramePlan of the current forward
+    gf::FramePlan* hostPlans = nullptr;   // pinned [kPlanSlots]
+    std::deque<InFlight> inflight;
+    int nextSlot = 0;
+    uint64_t maxIntersections = 0;        // largest count read so far
+    uint64_t forwardsRead = 0, intersectionsRead = 0, fallbackRead = 0;  // sums over the plans read
+    uint64_t hostWaitUs = 0;  // time blocked in synchronizations and plan waits
+    uint32_t lastN = 0, lastT = 0;        // sizes of the last forward read
+    bool haveHistory = false;
+    std::string overflowMessage;          // an overflowed forward, reported by the next call
+    std::vector<cudaEvent_t> planEventPool;
     cudaEvent_t logCopied = nullptr;  // recorded after the copy of the last forward's log overflow count
     bool logCounted = false;
     int finalBuf = 0;
@@ -127,10 +163,61 @@ int bind_device(gf_tracer* t) {
     if (t->device < 0) {
         t->device = dev;
         GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostTotal), 3 * sizeof(uint64_t), cudaHostAllocDefault));
+        GF_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&t->hostPlans), kPlanSlots * sizeof(gf::FramePlan),
+                              cudaHostAllocDefault));
     } else if (t->device != dev) {
         return fail(GF_ERR_STATE, "tracer bound to device %d, called on device %d", t->device, dev);
     }
     return GF_OK;
+}
+
+// Reads the plans of finished forwards in order, waiting only while more
+// than `keep` forwards remain unread.  The last plan read gives the
+// intersection count, the fallback list size and the history of the
+// speculative capacity; an overflowed plan leaves a message for the next call.
+int harvest(gf_tracer* t, size_t keep) {
+    while (!t->inflight.empty()) {
+        const InFlight f = t->inflight.front();
+        if (t->inflight.size() > keep) {
+            const auto w0 = std::chrono::steady_clock::now();
+            GF_CUDA(cudaEventSynchronize(f.done));
+            t->hostWaitUs += uint64_t(std::chrono::duration_cast<std::chrono::microseconds>(
+                std::chrono::steady_clock::now() - w0).count());
+        } else {
+            const cudaError_t q = cudaEventQuery(f.done);
+            if (q == cudaErrorNotReady) break;
+            if (q != cudaSuccess) return fail(GF_ERR_CUDA, "cudaEventQuery failed: %s", cudaGetErrorString(q));
+        }
+        const gf::FramePlan& p = t->hostPlans[f.slot];
+        t->maxIntersections = std::max<uint64_t>(t->maxIntersections, p.intersections);
+        t->forwardsRead += 1;
+        t->intersectionsRead += p.intersections;
+        t->fallbackRead += p.fallback;
+        t->numIntersections = p.count;
+        t->fallbackParticles = p.fallback;
+        t->lastN = f.N;
+        t->lastT = f.T;
+        t->haveHistory = true;
+        if (p.overflow != 0u) {
+            char msg[256];
+            snprintf(msg, sizeof(msg),
+                     "a forward produced %llu tile intersections, more than the %llu its keys were reserved for; "
+                     "it rendered nothing. The capacity has grown: render that frame again",
+                     static_cast<unsigned long long>(p.intersections), static_cast<unsigned long long>(f.capacity));
+            t->overflowMessage = msg;
+        }
+        t->planEventPool.push_back(f.done);
+        t->inflight.pop_front();
+    }
+    return GF_OK;
+}
+
+// GF_ERR_CAPACITY for a forward found overflowed since the last call.
+int report_overflow(gf_tracer* t) {
+    if (t->overflowMessage.empty()) return GF_OK;
+    const std::string m = t->overflowMessage;
+    t->overflowMessage.clear();
+    return fail(GF_ERR_CAPACITY, "%s", m.c_str());
 }
 
 int validate_inputs(const gf_tracer* t, const gf_trace_inputs* in, const TileMask** maskOut) {
@@ -168,8 +255,8 @@ int exclusive_scan(gf_tracer* t, const In* in, uint64_t n, Out* out, Out* grandT
     return scan_exclusive<In, Out>(t->scanTiles, t->launches, in, n, out, grandTotal, stream);
 }
 
-int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream) {
-    return sort_pairs(t->hist, t->scanTiles, t->launches, t->keys, t->ids, n, 0, endBit, &t->finalBuf, stream);
+int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream, const uint32_t* nDev) {
+    return sort_pairs(t->hist, t->scanTiles, t->launches, t->keys, t->ids, n, 0, endBit, &t->finalBuf, stream, nDev);
 }
 
 template <int K, bool kGeo>
@@ -259,6 +346,9 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     const TileMask* mask = nullptr;
     if (int e = validate_inputs(t, in, &mask)) return e;
     if (rgba == nullptr || hd == nullptr) return fail(GF_ERR_BAD_INPUT, "output buffers are NULL");
+    // read what has finished; at most kMaxInFlight - 1 earlier forwards stay unread
+    if (int e = harvest(t, kMaxInFlight - 1)) return e;
+    if (int e = report_overflow(t)) return e;
     t->launches = 0;
     t->haveForward = false;
 
@@ -381,22 +471,51 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
                                                         t->total.as<uint64_t>(), stream))
             return e;
     }
-    GF_CUDA(cudaMemcpyAsync(t->hostTotal, t->total.ptr, sizeof(uint64_t), cudaMemcpyDeviceToHost, stream));
-    t->hostTotal[1] = 0;
-    if (fa.enabled && N > 0)
-        GF_CUDA(cudaMemcpyAsync(t->hostTotal + 1, fa.bigCount, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
-    GF_CUDA(cudaStreamSynchronize(stream));
-    const uint64_t I = *t->hostTotal;
-    t->fallbackParticles = uint32_t(t->hostTotal[1]);
-    if (I > 0xffffffffull - gf::kSortTile)
-        return fail(GF_ERR_CAPACITY, "%llu tile intersections exceed the 32-bit index range",
-                    static_cast<unsigned long long>(I));
-    t->numIntersections = I;
-    for (int b = 0; b < 2; ++b) {
-        if (int e = t->keys[b].ensure(sizeof(uint64_t) * (I + 1), stream)) return e;
-        if (int e = t->ids[b].ensure(sizeof(uint32_t) * (I + 1), stream)) return e;
+    // Key capacity: speculative (no synchronization) when the history covers
+    // this particle count and raster, else the exact count read back now.
+    constexpr uint64_t kMaxKeys = 0xffffffffull - gf::kSortTile;
+    const bool speculative = t->cfg.intersection_capacity == GF_CAPACITY_SPECULATIVE && t->haveHistory &&
+                             N == t->lastN && T == t->lastT;
+    uint64_t capacity = 0;
+    if (speculative) {
+        capacity = std::min<uint64_t>(kMaxKeys, std::max<uint64_t>(t->maxIntersections + t->maxIntersections / 2,
+                                                                   uint64_t(1) << 16));
+    } else {
+        GF_CUDA(cudaMemcpyAsync(t->hostTotal, t->total.ptr, sizeof(uint64_t), cudaMemcpyDeviceToHost, stream));
+        t->hostTotal[1] = 0;
+        if (fa.enabled && N > 0)
+            GF_CUDA(cudaMemcpyAsync(t->hostTotal + 1, fa.bigCount, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream));
+        const auto w0 = std::chrono::steady_clock::now();
+        GF_CUDA(cudaStreamSynchronize(stream));
+        t->hostWaitUs += uint64_t(std::chrono::duration_cast<std::chrono::microseconds>(
+            std::chrono::steady_clock::now() - w0).count());
+        if (int e = harvest(t, 0)) return e;  // earlier forwards on this stream are complete
+        if (int e = report_overflow(t)) return e;
+        const uint64_t I = *t->hostTotal;
+        if (I > kMaxKeys)
+            return fail(GF_ERR_CAPACITY, "%llu tile intersections exceed the 32-bit index range",
+                        static_cast<unsigned long long>(I));
+        capacity = I;
+        t->maxIntersections = std::max<uint64_t>(t->maxIntersections, I);
+        t->numIntersections = I;
+        t->fallbackParticles = uint32_t(t->hostTotal[1]);
+        t->lastN = N;
+        t->lastT = T;
+        t->haveHistory = true;
     }
-    if (I > 0) {
+    for (int b = 0; b < 2; ++b) {
+        if (int e = t->keys[b].ensure(sizeof(uint64_t) * (capacity + 1), stream)) return e;
+        if (int e = t->ids[b].ensure(sizeof(uint32_t) * (capacity + 1), stream)) return e;
+    }
+    if (int e = t->plan.ensure(sizeof(gf::FramePlan), stream)) return e;
+    gf::FramePlan* plan = t->plan.as<gf::FramePlan>();
+    gf::k_plan_intersections<<<1, 32, 0, stream>>>(t->total.as<uint64_t>(), fa.enabled && N > 0 ? fa.bigCount : nullptr,
+                                                   capacity, plan);
+    t->launches += 1;
+    GF_LAUNCH_CHECK();
+    fa.overflow = &plan->overflow;
+    const uint32_t* count = &plan->count;
+    if (capacity > 0 && N > 0) {
         StageTimer st(t, GF_STAGE_EMIT, stream);
         gf::k_emit<<<(N + 255) / 256, 256, 0, stream>>>(f, t->proj.as<float4>(), t->records.as<float4>(),
                                                         mask->buf.as<uint8_t>(), t->tileRays.as<float4>(),
@@ -422,17 +541,32 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     const int endBit = 32 + int(bit_length(T));
     {
         StageTimer st(t, GF_STAGE_SORT, stream);
-        if (int e = radix_sort(t, uint32_t(I), endBit, stream)) return e;
+        if (int e = radix_sort(t, uint32_t(capacity), endBit, stream, count)) return e;
     }
     {
         StageTimer st(t, GF_STAGE_RANGES, stream);
         GF_CUDA(cudaMemsetAsync(t->ranges.ptr, 0, sizeof(uint2) * T, stream));
-        if (I > 0) {
-            gf::k_tile_ranges<<<uint32_t((I + 255) / 256), 256, 0, stream>>>(t->keys[t->finalBuf].as<uint64_t>(),
-                                                                            uint32_t(I), t->ranges.as<uint2>());
+        if (capacity > 0) {
+            gf::k_tile_ranges<<<uint32_t((capacity + 255) / 256), 256, 0, stream>>>(
+                t->keys[t->finalBuf].as<uint64_t>(), uint32_t(capacity), t->ranges.as<uint2>(), count);
             t->launches += 1;
             GF_LAUNCH_CHECK();
         }
+    }
+    // the plan goes to a pinned slot, read by a later call without waiting
+    {
+        const int slot = t->nextSlot;
+        t->nextSlot = (t->nextSlot + 1) % kPlanSlots;
+        GF_CUDA(cudaMemcpyAsync(t->hostPlans + slot, plan, sizeof(gf::FramePlan), cudaMemcpyDeviceToHost, stream));
+        cudaEvent_t done = nullptr;
+        if (!t->planEventPool.empty()) {
+            done = t->planEventPool.back();
+            t->planEventPool.pop_back();
+        } else {
+            GF_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+        }
+        GF_CUDA(cudaEventRecord(done, stream));
+        t->inflight.push_back(InFlight{done, slot, capacity, N, T});
     }
     gf::RenderArgs a;
     a.f = f;
@@ -522,6 +656,11 @@ gf_tracer* gf_tracer_create(const gf_tracer_config* config) {
         fail(GF_ERR_BAD_INPUT, "unknown admission fallback %d", config->admission_fallback);
         return nullptr;
     }
+    if (config->intersection_capacity != GF_CAPACITY_SPECULATIVE &&
+        config->intersection_capacity != GF_CAPACITY_EXACT) {
+        fail(GF_ERR_BAD_INPUT, "unknown intersection capacity mode %d", config->intersection_capacity);
+        return nullptr;
+    }
     gf_tracer* t = new gf_tracer();
     t->cfg = *config;
     return t;
@@ -547,6 +686,10 @@ void gf_tracer_destroy(gf_tracer* t) {
             cudaEventDestroy(ev.end);
         }
         for (cudaEvent_t e : t->eventPool) cudaEventDestroy(e);
+        for (const InFlight& f : t->inflight) cudaEventDestroy(f.done);
+        for (cudaEvent_t e : t->planEventPool) cudaEventDestroy(e);
+        t->plan.release();
+        if (t->hostPlans != nullptr) cudaFreeHost(t->hostPlans);
         if (t->logCopied != nullptr) cudaEventDestroy(t->logCopied);
         if (t->hostTotal != nullptr) cudaFreeHost(t->hostTotal);
         if (prev >= 0) cudaSetDevice(prev);
@@ -585,6 +728,8 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     if (t == nullptr || in == nullptr || g == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
     if (!t->haveForward) return fail(GF_ERR_STATE, "trace_bwd requires a preceding trace");
     if (int e = bind_device(t)) return e;
+    if (int e = harvest(t, kMaxInFlight)) return e;  // without waiting
+    if (int e = report_overflow(t)) return e;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     gf::FrameArgs& f = t->frame;
     if (in->num_particles != f.N || in->camera.width != f.W || in->camera.height != f.H ||
@@ -685,14 +830,23 @@ int gf_tracer_collect_times(gf_tracer* t, float* ms, uint32_t* launches) {
     return GF_OK;
 }
 
-int gf_tracer_stats(const gf_tracer* t, gf_trace_stats* st) {
-    if (t == nullptr || st == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+int gf_tracer_stats(const gf_tracer* tc, gf_trace_stats* st) {
+    if (tc == nullptr || st == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
+    gf_tracer* t = const_cast<gf_tracer*>(tc);  // reading the plans of finished forwards updates the counts
+    if (t->device >= 0) {
+        if (int e = harvest(t, 0)) return e;
+        if (int e = report_overflow(t)) return e;
+    }
     st->num_intersections = t->numIntersections;
     st->num_tiles = uint32_t(t->frame.gx * t->frame.gy);
     st->num_particles = t->frame.N;
     st->kernel_launches = t->launches;
     st->fallback_particles = t->fallbackParticles;
     st->total_kernel_launches = t->totalLaunches;
+    st->total_forwards = t->forwardsRead;
+    st->total_intersections = t->intersectionsRead;
+    st->total_fallback_particles = t->fallbackRead;
+    st->total_host_wait_us = t->hostWaitUs;
     return GF_OK;
 }
 
@@ -711,6 +865,7 @@ int gf_tracer_copy_intermediates(const gf_tracer* t, float* projected, float* ra
                                  void* stream) {
     if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
     if (!t->haveForward) return fail(GF_ERR_STATE, "no forward pass to copy");
+    if (int e = harvest(const_cast<gf_tracer*>(t), 0)) return e;  // the last forward's count
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t N = t->frame.N;
     const size_t T = size_t(t->frame.gx) * t->frame.gy;

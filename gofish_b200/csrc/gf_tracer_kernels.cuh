@@ -637,7 +637,12 @@ struct FallbackArgs {
     uint32_t* bigCursor;  // [2] next list entry of k_fallback_big (count, emit), zeroed per frame
     uint32_t* wide;     // projected particles whose tile box exceeds kWideTiles, left to k_wide
     uint32_t* wideCount;
+    const uint32_t* overflow;  // non-zero: the intersections exceed the key capacity, emit nothing (may be NULL)
 };
+
+__device__ __forceinline__ bool skip_emit(const FallbackArgs& fa) {
+    return fa.overflow != nullptr && *fa.overflow != 0u;
+}
 
 // Projected particles whose tile bounding box holds more tiles than this are
 // counted and emitted by one warp (k_wide) instead of one thread, so that a
@@ -769,6 +774,7 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
     __shared__ uint32_t scratch[8][fb::kWarpScratch];
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* stack = scratch[threadIdx.x >> 5];
+    if (kEmit && skip_emit(fa)) return;  // block-uniform
     const uint32_t total = *fa.bigCount;
     // each warp takes the next listed particle when it is done: the walks
     // differ by orders of magnitude (caps near the camera span most tiles)
@@ -821,6 +827,7 @@ __global__ __launch_bounds__(256) void k_wide(FrameArgs f, FallbackArgs fa, cons
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t below = (1u << lane) - 1u;
     const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    if (kEmit && skip_emit(fa)) return;  // block-uniform
     const uint32_t total = *fa.wideCount;
     for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < total; w += warps) {
         const uint32_t i = fa.wide[w];
@@ -885,7 +892,7 @@ __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restr
                                               const uint32_t* __restrict__ counts, uint64_t* __restrict__ keys,
                                               uint32_t* __restrict__ ids, FallbackArgs fa) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= f.N) return;
+    if (i >= f.N || skip_emit(fa)) return;
     const float4 p0 = proj[2 * i], p1 = proj[2 * i + 1];
     Projected p;
     p.cx = p0.x; p.cy = p0.y; p.conic0 = p0.z; p.conic1 = p0.w;
@@ -916,12 +923,39 @@ __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restr
 }
 
 // Per-tile [begin, end) of the sorted keys (reference gutRenderer.cu:114-144).
-__global__ void k_tile_ranges(const uint64_t* __restrict__ keys, uint32_t n, uint2* __restrict__ ranges) {
+// The number of keys is read on the device (nDev, at most n, which sized the grid).
+__global__ void k_tile_ranges(const uint64_t* __restrict__ keys, uint32_t n, uint2* __restrict__ ranges,
+                              const uint32_t* __restrict__ nDev) {
+    if (nDev != nullptr) n = min(n, *nDev);
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const uint32_t tile = uint32_t(keys[i] >> 32);
     if (i == 0 || uint32_t(keys[i - 1] >> 32) != tile) ranges[tile].x = i;
     if (i == n - 1 || uint32_t(keys[i + 1] >> 32) != tile) ranges[tile].y = i + 1;
+}
+
+// Intersection plan of one forward, written after the count scan: the count,
+// the fallback list size, whether the count exceeds the key capacity the host
+// reserved (then nothing is emitted, sorted or composited, and the host
+// reports the overflow), and the count the later kernels use.
+struct FramePlan {
+    unsigned long long intersections;
+    uint32_t fallback;
+    uint32_t overflow;
+    uint32_t count;  // intersections, or 0 on overflow
+    uint32_t pad;
+};
+
+__global__ void k_plan_intersections(const uint64_t* __restrict__ total, const uint32_t* __restrict__ fallbackCount,
+                                     uint64_t capacity, FramePlan* __restrict__ plan) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const uint64_t I = *total;
+    const bool over = I > capacity;
+    plan->intersections = I;
+    plan->fallback = fallbackCount != nullptr ? *fallbackCount : 0u;
+    plan->overflow = over ? 1u : 0u;
+    plan->count = over ? 0u : uint32_t(I);
+    plan->pad = 0u;
 }
 
 // Projection backward: record gradients to the reference's [N,32] density

@@ -126,6 +126,10 @@ class FullShape:
         the status words of the operator's launches)."""
         _raise_failures(self.pending)
 
+    def ready(self) -> bool:
+        """Whether the status words of every launch are on the host (check() will not wait)."""
+        return all(done.query() for _host, done, _start, _status in self.pending)
+
 
 def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mass_preserving: bool = True,
                      pixel_variance: float = FILTER_VARIANCE_PIXELS, mode: str = "exact",

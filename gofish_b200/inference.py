@@ -38,6 +38,9 @@ from .scene import PACKED_WIDTH, SLOTS
 from .splat_raster import SplatRaster, _select
 from .view_observation_filter import current_view_q6, pixel_footprint_variance, shape_camera
 
+# frames whose full-shape status may still be in flight when render returns
+MAX_UNCHECKED_SHAPES = 4
+
 SHAPE_MODES = ("exact", "fused", "fused32", "fusedmix")
 
 
@@ -98,6 +101,7 @@ class InferenceTracer:
         self._registered: set = set()
         self.cache_static_shape = bool(cache_static_shape)
         self.static_shape = None
+        self._unchecked_shapes: list = []
         self.shape_mode = shape
         self._status = None
         self.freeze(model)
@@ -156,10 +160,27 @@ class InferenceTracer:
             return self.static_shape
         q6, jacobian, observed = current_view_q6(self.positions, gpu_batch, self.gamma, host_sync_free=True)
         shape = build_full_shape(self.physical_scale, self.rotation, self.raw_density, q6, jacobian, observed,
-                                 mass_preserving=True, pixel_variance=self.gamma)
+                                 mass_preserving=True, pixel_variance=self.gamma, defer_check=True)
+        # the status words are checked once they reach the host (at most
+        # MAX_UNCHECKED_SHAPES frames later, or by check_shapes())
+        self._unchecked_shapes.append(shape)
+        self._check_shapes(MAX_UNCHECKED_SHAPES)
         if self.gamma == 0.0 and self.cache_static_shape:
             self.static_shape = shape
         return shape
+
+    def _check_shapes(self, keep: int) -> None:
+        while self._unchecked_shapes:
+            shape = self._unchecked_shapes[0]
+            if len(self._unchecked_shapes) <= keep and not shape.ready():
+                return
+            self._unchecked_shapes.pop(0)
+            shape.check()
+
+    def check_shapes(self) -> None:
+        """Waits for every rendered frame's shape status and raises
+        FootprintNumericalError for the first failed row."""
+        self._check_shapes(0)
 
     def _fused_shape(self, gpu_batch) -> None:
         """Q_v, the Cholesky factor and m of every row written into the packed rows."""

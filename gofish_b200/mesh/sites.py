@@ -71,3 +71,42 @@ def generate_sites(shape: EffectiveShape) -> Sites:
     return Sites(points=np.ascontiguousarray(pts.reshape(-1, 3)),
                  scale=np.repeat(scale.astype("<f4"), SITES_PER_GAUSSIAN).reshape(-1, 1),
                  owner=np.repeat(keep.astype("<i8"), SITES_PER_GAUSSIAN))
+
+
+def generate_sites_cuda(shape: EffectiveShape, device) -> Sites:
+    """generate_sites on the GPU (gf_mesh_sites): the same sites, scales and
+    owners, as CUDA tensors on ``device``.  ``shape`` may hold numpy arrays
+    or tensors; one host read of the kept count sizes the outputs."""
+    import ctypes
+
+    import torch
+
+    from .. import _native
+
+    def dev(a, shape_):
+        t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))
+        return t.to(device=device, dtype=torch.float32).reshape(shape_).contiguous()
+
+    n = int(shape.positions.shape[0])
+    positions = dev(shape.positions, (n, 3))
+    factor = dev(shape.factor, (n, 9))
+    density = dev(shape.density, (n,))
+    sigma = dev(shape.sigma_max, (n,))
+    points = torch.empty((9 * n, 3), dtype=torch.float32, device=device)
+    scale = torch.empty((9 * n,), dtype=torch.float32, device=device)
+    owner = torch.empty((9 * n,), dtype=torch.int64, device=device)
+    count = torch.zeros(1, dtype=torch.int32, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _native.check(_native.load().gf_mesh_sites(positions.data_ptr(), factor.data_ptr(), density.data_ptr(),
+                                                   sigma.data_ptr(), ctypes.c_uint32(n), points.data_ptr(),
+                                                   scale.data_ptr(), owner.data_ptr(), count.data_ptr(),
+                                                   status.data_ptr(), stream), "mesh sites")
+    kept = int(count.item())
+    if int(status.item()) != 0:
+        raise ValueError("support radius is not finite and positive")
+    if kept == 0:
+        raise ValueError("no Gaussian has opacity above 1/255")
+    m = SITES_PER_GAUSSIAN * kept
+    return Sites(points=points[:m], scale=scale[:m].reshape(m, 1), owner=owner[:m])

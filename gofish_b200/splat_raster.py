@@ -66,6 +66,13 @@ class SplatRaster:
         cfg.composite_log_capacity = int(_select(conf, "render.splat.composite_log_capacity", 0))
         # the geometric training channels (normals, depth moments, quantile depths, extent, inverse depth)
         cfg.enable_normals = 1 if bool(_select(conf, "render.enable_normals", False)) else 0
+        # tile-intersection keys: "speculative" (no host synchronization; an overflowed forward renders nothing
+        # and the next call raises) or "exact" (one synchronization per forward reads the count)
+        capacity = str(_select(conf, "render.splat.intersection_capacity", "speculative"))
+        if capacity not in ("speculative", "exact"):
+            raise ValueError(f"render.splat.intersection_capacity must be 'speculative' or 'exact' (got {capacity!r})")
+        cfg.intersection_capacity = (_native.GF_CAPACITY_EXACT if capacity == "exact"
+                                     else _native.GF_CAPACITY_SPECULATIVE)
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())

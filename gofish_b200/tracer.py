@@ -59,6 +59,10 @@ def _conf_value(conf, path: str, default):
     return node
 
 
+# views whose full-shape status may still be in flight when render returns
+MAX_UNCHECKED_SHAPES = 4
+
+
 class Tracer:
     """Differentiable fisheye renderer of a Gaussian scene (reference ``Tracer``)."""
 
@@ -141,6 +145,22 @@ class Tracer:
         self._physical_tile_binding_cache: dict = {}
         self._physical_tile_registration_cache: set = set()
         self._pending_shape = None
+        self._unchecked_shapes: list = []
+
+    def _check_shapes(self, keep: int) -> None:
+        """Checks, in order, the per-view shapes whose status words have reached
+        the host, waiting only for those beyond the newest ``keep``."""
+        while self._unchecked_shapes:
+            shape = self._unchecked_shapes[0]
+            if len(self._unchecked_shapes) <= keep and not shape.ready():
+                return
+            self._unchecked_shapes.pop(0)
+            shape.check()
+
+    def check_shapes(self) -> None:
+        """Waits for every rendered view's shape status and raises
+        FootprintNumericalError for the first failed row."""
+        self._check_shapes(0)
 
     def _physical_tile_token(self, wrapper, gpu_batch, rays) -> str:
         """The tile mask of the batch's calibrated domain, registered once per camera."""
@@ -196,9 +216,13 @@ class Tracer:
             rays_d.contiguous(), gaussians.positions.contiguous(), rot.contiguous(), scale.contiguous(),
             dens.contiguous(), intrinsic_dens.contiguous(), factor.contiguous(), inverse_factor.contiguous(),
             gaussians.get_features().contiguous(), sensor, poses, confidence)
-        # the trace has synchronised its stream, so the shape's status words are on the host
+        # The shape's status words reach the host asynchronously: views are
+        # checked once their copy has landed (without waiting), and only the
+        # MAX_UNCHECKED_SHAPES views before this one may stay unchecked, so a
+        # numerical failure raises within a few calls without a per-view wait.
         shape, self._pending_shape = self._pending_shape, None
-        shape.check()
+        self._unchecked_shapes.append(shape)
+        self._check_shapes(MAX_UNCHECKED_SHAPES)
         f = gaussians.ray_feature_dim
         timings = self.tracer_wrapper.collect_times()
         return {

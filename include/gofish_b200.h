@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 3
+#define GF_ABI_VERSION 4
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -76,7 +76,17 @@ typedef struct gf_tracer_config {
                                        tile through the k-buffer) */
     int32_t enable_normals;         /* render.enable_normals: 1 computes the geometric training channels
                                        (gf_trace_outputs.normal ... inv_depth2) and their gradients */
+    int32_t intersection_capacity;  /* GF_CAPACITY_*: how the tile-intersection keys are sized */
 } gf_tracer_config;
+
+/* Sizing of the tile-intersection keys of a forward.  SPECULATIVE: 1.5x the
+ * largest count of the earlier forwards, with no host synchronization (the
+ * first forward and any forward whose particle count or raster changed read
+ * the exact count); a forward whose count exceeds it renders nothing and the
+ * next call on the tracer returns GF_ERR_CAPACITY, with the capacity grown.
+ * EXACT: every forward reads its count with one synchronization. */
+#define GF_CAPACITY_SPECULATIVE 0
+#define GF_CAPACITY_EXACT 1
 
 /* render.gofish.fast_admission_fallback (setup_3dgut.py:232-239): "none"
  * drops particles whose unscented projection is invalid; "cone" admits them
@@ -153,6 +163,10 @@ typedef struct gf_trace_stats {
     uint32_t kernel_launches;   /* kernels launched by the last trace/trace_bwd call */
     uint32_t fallback_particles; /* particles without a UT footprint handed to the cone admission */
     uint64_t total_kernel_launches; /* kernels launched by this tracer since its creation */
+    uint64_t total_forwards;        /* forwards since the tracer's creation */
+    uint64_t total_intersections;   /* their tile intersections, summed */
+    uint64_t total_fallback_particles; /* their cone-fallback particles, summed */
+    uint64_t total_host_wait_us;    /* microseconds the calling threads spent waiting for the device */
 } gf_trace_stats;
 
 typedef struct gf_tracer gf_tracer;
@@ -440,6 +454,20 @@ int gf_pack_particle_rows(const float* positions, const float* density, const fl
 int gf_unpack_particle_rows(const float* rows, int64_t n, float* positions, float* density, float* rotations,
                             float* scales, float* intrinsic_density, float* factor, float* inverse_factor,
                             void* stream);
+
+/* Tetrahedralization sites of the mesh extraction (gofish/mesh/sites.py:43-83,
+ * generate_sites, host numpy in the reference): for every Gaussian with
+ * density > 1/255, in order, its centre then the eight corners mu + B (r s)
+ * of its support box (s in {-1,+1}^3, x slowest), r = min(sqrt(-2 ln
+ * 0.0113f), sqrt(2 ln(255 o))).  Device inputs: positions [N,3], factor B
+ * [N,3,3] row-major, density [N], sigma_max [N] (float32).  Device outputs,
+ * sized for 9 N sites: points [9N,3] float32, scale [9N] float32 (sigma_max
+ * r), owner [9N] int64, *count = kept Gaussians (sites = 9 * count), *status =
+ * 1 when a kept Gaussian's radius is not finite and positive.  Scratch is
+ * allocated and freed on the stream. */
+int gf_mesh_sites(const float* positions, const float* factor, const float* density, const float* sigma_max,
+                  uint32_t num_gaussians, float* points, float* scale, int64_t* owner, uint32_t* count,
+                  uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

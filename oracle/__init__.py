@@ -124,6 +124,9 @@ def load():
                                        vp]),
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
+        "oracle_field_index_build": (vp, [i32, vp, ctypes.c_double]),
+        "oracle_field_index_free": (None, [vp]),
+        "oracle_field_camera_indexed": (i32, [vp, cam_p, pose_p, vp, vp, i32, vp, vp, vp]),
         "oracle_num_threads": (i32, []),
         "oracle_expf": (f32, [f32]),
         "oracle_logf": (f32, [f32]),
@@ -396,6 +399,63 @@ def evaluate_field(views, particles, points):
     observed = np.zeros(q, dtype=np.uint8)
     for cam, pose7, ray_o, mask in views:
         op, ob = field_camera(cam, pose7, particles, ray_o, points, mask)
+        first = (ob != 0) & (observed == 0)
+        both = (ob != 0) & (observed != 0)
+        minimum[first] = op[first]
+        minimum[both] = np.minimum(minimum[both], op[both])
+        observed |= ob
+    opacity = np.where(observed != 0, minimum, np.float32(0.0)).astype(np.float32)
+    above = ((observed != 0) & (opacity >= np.float32(0.5))).astype(np.uint8)
+    return opacity, observed, above
+
+
+class FieldIndex:
+    """Spatial index of oracle_field_camera_indexed over packed [N,32] rows
+    (the rows are kept alive by this object).  ``scene_bound`` must bound
+    every distance from a camera origin to a particle mean and every query
+    segment's length."""
+
+    def __init__(self, particles, scene_bound: float):
+        self.particles = np.ascontiguousarray(particles, dtype=np.float32)
+        self.handle = load().oracle_field_index_build(self.particles.shape[0], _p(self.particles), float(scene_bound))
+
+    def close(self):
+        if self.handle:
+            load().oracle_field_index_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+    def field_camera(self, cam, pose7, ray_o, points, pixel_mask=None):
+        """oracle field of one camera (field_camera) over the index."""
+        pose = prepare_pose(pose7)
+        points = np.ascontiguousarray(points, dtype=np.float32).reshape(-1, 3)
+        q = points.shape[0]
+        opacity = np.zeros(q, dtype=np.float32)
+        observed = np.zeros(q, dtype=np.uint8)
+        mask = None if pixel_mask is None else np.ascontiguousarray(pixel_mask, dtype=np.uint8)
+        ray_o = np.ascontiguousarray(ray_o, dtype=np.float32)
+        load().oracle_field_camera_indexed(self.handle, ctypes.byref(cam), ctypes.byref(pose), _p(ray_o),
+                                           None if mask is None else _p(mask), q, _p(points), _p(opacity),
+                                           _p(observed))
+        return opacity, observed
+
+    def evaluate_field(self, views, points):
+        """evaluate_field over the index: (opacity, observed, above)."""
+        return _camera_min(views, points, self.field_camera)
+
+
+def _camera_min(views, points, camera_fn):
+    q = np.asarray(points).reshape(-1, 3).shape[0]
+    minimum = np.ones(q, dtype=np.float32)
+    observed = np.zeros(q, dtype=np.uint8)
+    for cam, pose7, ray_o, mask in views:
+        op, ob = camera_fn(cam, pose7, ray_o, points, mask)
         first = (ob != 0) & (observed == 0)
         both = (ob != 0) & (observed != 0)
         minimum[first] = op[first]

@@ -1770,6 +1770,228 @@ int oracle_field_camera(const OracleCamera* cam, const OraclePose* pose, int N, 
     return 0;
 }
 
+// The same field with a conservative spatial index, for point counts the
+// brute force cannot reach (millions of points over millions of particles).
+// A particle can pass the hit test on a segment only if the segment comes
+// within R of its mean: with M = B^-1 (the stored float inverse factor) the
+// world point w of the clamped closest point satisfies w - mu = M^-1 p, and
+// the hit needs |p| < 3 (response above 0.0113 needs |p|^2 < 8.97) for the
+// float p, which differs from the exact one by at most 8u |M|_F (|o - mu| +
+// tmax) (u = 2^-24); so R = (3 + 8u |M|_F 2D) |M^-1|_F (1 + 1e-3) with D
+// bounding |o - mu| and tmax over the scene, |M^-1|_F from the double-precision
+// inverse of M.  Particles with density <= 1/255 never pass and are left out.
+// A bounding volume hierarchy over the spheres (median splits, leaves of at
+// most 4) yields every particle whose sphere meets the segment; they are
+// tested in ascending id, exactly as the brute force multiplies them, and the
+// walk stops once 1 - T rounds to 1 (later factors only shrink T, and the
+// rounding of 1 - T is monotone, so the result is the full product's).
+namespace fieldbvh {
+
+struct Node {
+    double lo[3], hi[3];
+    int32_t left, right;  // children, or -1 for a leaf
+    int32_t begin, end;   // leaf: prims[begin, end)
+};
+
+struct Index {
+    std::vector<Node> nodes;
+    std::vector<int32_t> prims;        // particle ids, permuted by the build
+    std::vector<double> centre, radius;  // [N*3], [N] (radius < 0: never hit)
+    const float* particles = nullptr;
+    int n = 0;
+};
+
+double inverse_frobenius(const float* Mf) {
+    double M[9];
+    for (int i = 0; i < 9; ++i) M[i] = double(Mf[i]);
+    const double c00 = M[4] * M[8] - M[5] * M[7], c01 = M[5] * M[6] - M[3] * M[8], c02 = M[3] * M[7] - M[4] * M[6];
+    const double det = M[0] * c00 + M[1] * c01 + M[2] * c02;
+    if (!(std::fabs(det) > 0.0) || !std::isfinite(det)) return INFINITY;
+    const double inv[9] = {c00, M[2] * M[7] - M[1] * M[8], M[1] * M[5] - M[2] * M[4],
+                           c01, M[0] * M[8] - M[2] * M[6], M[2] * M[3] - M[0] * M[5],
+                           c02, M[1] * M[6] - M[0] * M[7], M[0] * M[4] - M[1] * M[3]};
+    double f = 0.0;
+    for (int i = 0; i < 9; ++i) f += (inv[i] / det) * (inv[i] / det);
+    return std::sqrt(f);
+}
+
+int build_node(Index& ix, int begin, int end) {
+    Node nd;
+    for (int a = 0; a < 3; ++a) {
+        nd.lo[a] = INFINITY;
+        nd.hi[a] = -INFINITY;
+    }
+    double clo[3] = {INFINITY, INFINITY, INFINITY}, chi[3] = {-INFINITY, -INFINITY, -INFINITY};
+    for (int k = begin; k < end; ++k) {
+        const int i = ix.prims[size_t(k)];
+        for (int a = 0; a < 3; ++a) {
+            const double c = ix.centre[3 * size_t(i) + a], r = ix.radius[size_t(i)];
+            nd.lo[a] = std::min(nd.lo[a], c - r);
+            nd.hi[a] = std::max(nd.hi[a], c + r);
+            clo[a] = std::min(clo[a], c);
+            chi[a] = std::max(chi[a], c);
+        }
+    }
+    const int id = int(ix.nodes.size());
+    ix.nodes.push_back(nd);
+    if (end - begin <= 4) {
+        ix.nodes[size_t(id)].left = ix.nodes[size_t(id)].right = -1;
+        ix.nodes[size_t(id)].begin = begin;
+        ix.nodes[size_t(id)].end = end;
+        return id;
+    }
+    int axis = 0;
+    for (int a = 1; a < 3; ++a)
+        if (chi[a] - clo[a] > chi[axis] - clo[axis]) axis = a;
+    const int mid = begin + (end - begin) / 2;
+    std::nth_element(ix.prims.begin() + begin, ix.prims.begin() + mid, ix.prims.begin() + end, [&](int32_t x, int32_t y) {
+        const double cx = ix.centre[3 * size_t(x) + axis], cy = ix.centre[3 * size_t(y) + axis];
+        return cx < cy || (cx == cy && x < y);
+    });
+    const int l = build_node(ix, begin, mid);
+    const int r = build_node(ix, mid, end);
+    ix.nodes[size_t(id)].left = l;
+    ix.nodes[size_t(id)].right = r;
+    ix.nodes[size_t(id)].begin = ix.nodes[size_t(id)].end = 0;
+    return id;
+}
+
+// Segment a + t (b - a), t in [0, 1], against an axis-aligned box (slabs, in double).
+bool segment_meets_box(const double a[3], const double b[3], const double lo[3], const double hi[3]) {
+    double t0 = 0.0, t1 = 1.0;
+    for (int k = 0; k < 3; ++k) {
+        const double d = b[k] - a[k];
+        if (d == 0.0) {
+            if (a[k] < lo[k] || a[k] > hi[k]) return false;
+            continue;
+        }
+        double ta = (lo[k] - a[k]) / d, tb = (hi[k] - a[k]) / d;
+        if (ta > tb) std::swap(ta, tb);
+        t0 = std::max(t0, ta);
+        t1 = std::min(t1, tb);
+        if (t0 > t1) return false;
+    }
+    return true;
+}
+
+bool segment_meets_sphere(const double a[3], const double b[3], const double c[3], double r) {
+    double ab[3], ac[3];
+    double ab2 = 0.0, t = 0.0;
+    for (int k = 0; k < 3; ++k) {
+        ab[k] = b[k] - a[k];
+        ac[k] = c[k] - a[k];
+        ab2 += ab[k] * ab[k];
+        t += ac[k] * ab[k];
+    }
+    t = ab2 > 0.0 ? std::min(1.0, std::max(0.0, t / ab2)) : 0.0;
+    double d2 = 0.0;
+    for (int k = 0; k < 3; ++k) {
+        const double e = a[k] + t * ab[k] - c[k];
+        d2 += e * e;
+    }
+    return d2 <= r * r;
+}
+
+}  // namespace fieldbvh
+
+// Builds the index of oracle_field_camera_indexed over N particles (rows are
+// borrowed: keep them alive and unchanged until oracle_field_index_free).
+// sceneBound bounds every |camera origin - mean| and every segment length.
+void* oracle_field_index_build(int N, const float* particles, double sceneBound) {
+    auto* ix = new fieldbvh::Index();
+    ix->n = N;
+    ix->particles = particles;
+    ix->centre.resize(3 * size_t(N));
+    ix->radius.resize(size_t(N));
+    const double u = std::ldexp(1.0, -24);
+    for (int i = 0; i < N; ++i) {
+        const Particle P = load_particle(particles + 32 * size_t(i));
+        ix->centre[3 * size_t(i)] = P.pos.x;
+        ix->centre[3 * size_t(i) + 1] = P.pos.y;
+        ix->centre[3 * size_t(i) + 2] = P.pos.z;
+        double mf = 0.0;
+        for (int k = 0; k < 9; ++k) mf += double(P.Binv[k]) * double(P.Binv[k]);
+        const double inv = fieldbvh::inverse_frobenius(P.Binv);
+        double r = (3.0 + 8.0 * u * std::sqrt(mf) * 2.0 * sceneBound) * inv * (1.0 + 1e-3);
+        if (!(P.density > kAlphaThreshold) || !std::isfinite(r)) r = -1.0;
+        ix->radius[size_t(i)] = r;
+        if (r >= 0.0) ix->prims.push_back(i);
+    }
+    if (!ix->prims.empty()) fieldbvh::build_node(*ix, 0, int(ix->prims.size()));
+    return ix;
+}
+
+void oracle_field_index_free(void* handle) { delete static_cast<fieldbvh::Index*>(handle); }
+
+// oracle_field_camera over the particles of an index (see above); identical
+// results, with particles whose sphere misses the segment skipped.
+int oracle_field_camera_indexed(void* handle, const OracleCamera* cam, const OraclePose* pose, const float* rayO,
+                                const uint8_t* pixelMask, int Q, const float* points, float* opacity,
+                                uint8_t* observed) {
+    const auto& ix = *static_cast<const fieldbvh::Index*>(handle);
+    const int W = cam->width, H = cam->height;
+    parallel_for(0, Q, 64, [&](int q, int) {
+        opacity[q] = 0.0f;
+        observed[q] = 0u;
+        const float3_ x = f3(points[3 * size_t(q)], points[3 * size_t(q) + 1], points[3 * size_t(q) + 2]);
+        float2_ pr;
+        if (!project_world(*cam, *pose, x, pr)) return;
+        if (!(pr.x >= 0.0f && pr.y >= 0.0f && pr.x < float(W) && pr.y < float(H))) return;
+        const int px = int(floorf(pr.x)), py = int(floorf(pr.y));
+        if (px < 0 || py < 0 || px >= W || py >= H) return;
+        const size_t pix = size_t(px) + size_t(W) * size_t(py);
+        if (pixelMask != nullptr && pixelMask[pix] == 0u) return;
+        const float3_ os = f3(rayO[3 * pix], rayO[3 * pix + 1], rayO[3 * pix + 2]);
+        const float3_ o = add(matvec(pose->Rinv, os), f3(pose->c[0], pose->c[1], pose->c[2]));
+        const float3_ delta = sub(x, o);
+        const float range = sqrtf(dot(delta, delta));
+        if (!(range > 0.0f) || !gf::isfinite_f(range)) return;
+        Ray ray;
+        ray.o = o;
+        ray.d = f3(delta.x / range, delta.y / range, delta.z / range);
+        ray.tmin = 0.0f;
+        ray.tmax = range;
+        ray.valid = true;
+        // the segment from o to o + range d (in double, the float ray's own end)
+        const double a[3] = {o.x, o.y, o.z};
+        const double b[3] = {double(o.x) + double(range) * double(ray.d.x),
+                             double(o.y) + double(range) * double(ray.d.y),
+                             double(o.z) + double(range) * double(ray.d.z)};
+        std::vector<int32_t> cand;
+        if (!ix.nodes.empty()) {
+            int32_t stack[128];
+            int top = 0;
+            stack[top++] = 0;
+            while (top > 0) {
+                const fieldbvh::Node& nd = ix.nodes[size_t(stack[--top])];
+                if (!fieldbvh::segment_meets_box(a, b, nd.lo, nd.hi)) continue;
+                if (nd.left < 0) {
+                    for (int k = nd.begin; k < nd.end; ++k) {
+                        const int32_t i = ix.prims[size_t(k)];
+                        if (fieldbvh::segment_meets_sphere(a, b, &ix.centre[3 * size_t(i)], ix.radius[size_t(i)]))
+                            cand.push_back(i);
+                    }
+                } else {
+                    stack[top++] = nd.left;
+                    stack[top++] = nd.right;
+                }
+            }
+        }
+        std::sort(cand.begin(), cand.end());
+        float T = 1.0f;
+        for (const int32_t i : cand) {
+            const Particle P = load_particle(ix.particles + 32 * size_t(i));
+            float alpha, hitT, resp;
+            HalfRay h;
+            if (hit_test(ray, P, alpha, hitT, resp, h)) T = T * (1.0f - alpha);
+            if (1.0f - T == 1.0f) break;
+        }
+        opacity[q] = 1.0f - T;
+        observed[q] = 1u;
+    });
+    return 0;
+}
+
 // ------------------------------------------------------------------ physical-mip 3-D filter
 // Finest pixel sampling rate of a point over the training frames
 // (threedgrut/physical_mip_csrc/fused_refresh_cuda.cu:40-219,

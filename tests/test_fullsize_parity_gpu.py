@@ -9,6 +9,10 @@
   admitted by the cone fallback.  Image max-abs <= 1e-3 and PSNR >= 60 dB,
   hit distance relative <= 1e-3; particle and SH gradients of a full-frame
   output gradient within 1e-3 relative L2.
+* Mesh opacity query: 1M of the 27M sites of the 3M-Gaussian scene from 4
+  of its 32 views: opacity bits, observed and above flags against the
+  oracle's indexed field (itself equal to its brute force,
+  tests/test_oracle_field_index.py).
 * High-resolution inference orbit frame (6M Gaussians SH3, 5% large beside
   the camera path, equisolid 205 deg 2560x2560, K = 32, physical-mip filter
   from all 240 frames, per-frame full shape): binning bit for bit over the
@@ -185,3 +189,52 @@ def test_orbit_frame_image_band(orbit_frame, band):
     assert harness.psnr(got["rgba"][rows], rgba[rows]) >= 60.0
     np.testing.assert_allclose(got["hit_t"][rows], hit_t[rows], rtol=1e-3, atol=1e-4)
     assert float(rgba[rows][..., 3].max()) > 0.5
+
+
+# ----------------------------------------------------------------------------- mesh opacity query subset
+@pytest.fixture(scope="module")
+def mesh_subset(cuda_device):
+    """The mesh-query scene (3M Gaussians, sites of every kept Gaussian), a
+    seeded subset of 1M sites and 4 of its 32 equidistant 200 deg 800x800
+    views (masked), evaluated by the GPU field and by the oracle's indexed
+    field."""
+    from gofish_b200.mesh import SplatRaster as FieldRaster
+    from gofish_b200.mesh.cameras import fisheye_training_camera
+    from gofish_b200.mesh.field import camera_inputs
+    from gofish_b200.mesh.shape import effective_shape
+    from gofish_b200.mesh.sites import generate_sites
+
+    w = S.workload_mesh_query()
+    shape = effective_shape(w.scene.positions, w.scene.scales, w.scene.rotations, w.scene.density)
+    sites = generate_sites(shape).points
+    rng = np.random.default_rng(1237)
+    points = np.ascontiguousarray(sites[np.sort(rng.choice(sites.shape[0], 1_000_000, replace=False))])
+    chosen = (0, 8, 16, 24)
+    cameras = [fisheye_training_camera(v, w.camera, w.poses[v], masked=True) for v in chosen]
+    raster = FieldRaster()
+    packed = shape.packed_density()
+    token = raster.begin_opacity_field(torch.from_numpy(packed).to(cuda_device),
+                                       torch.from_numpy(np.ascontiguousarray(shape.sigma_max)).to(cuda_device),
+                                       torch.from_numpy(points).to(cuda_device))
+    for cam in cameras:
+        raster.integrate_opacity_field_camera(token, *camera_inputs(cam, cuda_device))
+    opacity, observed, above = (t.cpu().numpy() for t in raster.finish_opacity_field(token))
+    raster.release_opacity_field(token)
+    ocam = harness.oracle_camera(w.camera)
+    ray_o = np.zeros((w.camera.height, w.camera.width, 3), np.float32)
+    views = [(ocam, w.poses[v], ray_o, cam.physical_mask.numpy()) for v, cam in zip(chosen, cameras)]
+    with oracle.FieldIndex(packed, 20.0) as index:
+        ref = index.evaluate_field(views, points)
+    return dict(got=(opacity, observed, above), ref=ref)
+
+
+def test_mesh_query_subset_bit_exact(mesh_subset):
+    (opacity, observed, above), (want_op, want_ob, want_ab) = mesh_subset["got"], mesh_subset["ref"]
+    np.testing.assert_array_equal(observed, want_ob)
+    np.testing.assert_array_equal(opacity.view(np.uint32), want_op.view(np.uint32))
+    np.testing.assert_array_equal(above, want_ab)
+    seen = want_ob != 0
+    assert seen.mean() > 0.5
+    # partial and saturated opacities both occur
+    assert 0.05 < (want_op[seen] == 1.0).mean() < 0.95
+    assert ((want_op[seen] > 0.0) & (want_op[seen] < 0.5)).sum() > 1000

@@ -172,8 +172,9 @@ def test_opacity_field_loss_is_refused():
 
 def test_shape_failure_is_raised_by_render(view, cuda_device):
     """A row whose full shape is not positive definite raises
-    FootprintNumericalError with its global row from the same render call,
-    although the status words are read only after the trace."""
+    FootprintNumericalError with its global row: from the render call once
+    its status words have reached the host, or at the latest from
+    check_shapes() (render does not wait for them)."""
     from gofish_b200.footprint_shape_operator import FootprintNumericalError
 
     scene, cam, batch, valid = view
@@ -181,6 +182,26 @@ def test_shape_failure_is_raised_by_render(view, cuda_device):
     _q6, _jac, obs = current_view_q6(model.positions, batch, GAMMA)
     row = int(torch.nonzero(obs).reshape(-1)[11])
     model.scale[row] = 0.0  # C = Q_v has rank 2
+    tracer = Tracer(_conf())
     with pytest.raises(FootprintNumericalError) as err:
-        Tracer(_conf()).render(model, batch, train=True)
+        tracer.render(model, batch, train=True)
+        tracer.check_shapes()
     assert err.value.global_row == row
+
+
+def test_shape_failure_surfaces_within_the_unchecked_window(view, cuda_device):
+    """Without check_shapes(), the failure raises from one of the next
+    renders: at most MAX_UNCHECKED_SHAPES views stay unchecked."""
+    from gofish_b200.footprint_shape_operator import FootprintNumericalError
+    from gofish_b200.tracer import MAX_UNCHECKED_SHAPES
+
+    scene, cam, batch, valid = view
+    bad = SceneGaussians.from_scene(scene, cuda_device, requires_grad=False)
+    good = SceneGaussians.from_scene(scene, cuda_device, requires_grad=False)
+    _q6, _jac, obs = current_view_q6(bad.positions, batch, GAMMA)
+    bad.scale[int(torch.nonzero(obs).reshape(-1)[5])] = 0.0
+    tracer = Tracer(_conf())
+    with pytest.raises(FootprintNumericalError):
+        tracer.render(bad, batch, train=True)
+        for _ in range(MAX_UNCHECKED_SHAPES + 1):
+            tracer.render(good, batch, train=True)

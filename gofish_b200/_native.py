@@ -217,6 +217,13 @@ _SIGNATURES = [
       ctypes.c_int64, _vp, _vp, _vp, _vp, _vp]),
     ("gf_field_collect_times", ctypes.c_int, [_vp, _vp, _vp]),
     ("gf_mesh_sites", ctypes.c_int, [_vp, _vp, _vp, _vp, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("gf_mesh_mt_create", _vp, []),
+    ("gf_mesh_mt_destroy", None, [_vp]),
+    ("gf_mesh_mt_run", ctypes.c_int, [_vp, _vp, ctypes.c_uint64, _vp, ctypes.c_uint64, _vp, _vp, ctypes.c_uint64,
+                                      ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64), _vp]),
+    ("gf_mesh_mt_outputs", ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("gf_mesh_sof_vertex_filter", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_uint64, _vp, _vp]),
+    ("gf_mesh_gof_cell_filter", ctypes.c_int, [_vp, ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp]),
 ]
 
 STATIC_SORT_MAX_PAIRS = 262144

@@ -16,7 +16,7 @@ PACKAGE_DIR = Path(__file__).resolve().parent
 CSRC = PACKAGE_DIR / "csrc"
 LIBRARY = PACKAGE_DIR / "libgofish_b200.so"
 SOURCES = [CSRC / "gf_tracer.cu", CSRC / "gf_sort_static.cu", CSRC / "gf_field.cu", CSRC / "gf_mip.cu",
-           CSRC / "gf_shape.cu", CSRC / "gf_sites.cu"]
+           CSRC / "gf_shape.cu", CSRC / "gf_sites.cu", CSRC / "gf_mesh.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [PACKAGE_DIR.parent / "include" / "gofish_b200.h"]
 
 NVCC_FLAGS = [

@@ -469,6 +469,37 @@ int gf_mesh_sites(const float* positions, const float* factor, const float* dens
                   uint32_t num_gaussians, float* points, float* scale, int64_t* owner, uint32_t* count,
                   uint32_t* status, void* stream);
 
+/* Marching tetrahedra of the mesh extraction (gofish/mesh/marching_tetrahedra.py:
+ * 47-162, marching_tetrahedra on one grid): the crossing edges of the zero
+ * level set of sdf (inside: sdf > 0) over tetrahedra tets [T,4] (int64 vertex
+ * ids) of vertices [V,3], in the reference's order (distinct edges sorted by
+ * (min, max)), and the faces over them (one-triangle tetrahedra, then
+ * two-triangle ones, per chunk of the reference's chunking; chunk_tets = 0
+ * selects its 32 Mi).  gf_mesh_mt_run classifies, sorts and numbers (two host
+ * reads) and returns the edge and face counts; gf_mesh_mt_outputs writes
+ * endpoints [E,2,3], endpoint fields [E,2], endpoint scales [E,2] (float32),
+ * faces [F,3] and edges [E,2] (int64).  The inputs must stay valid until the
+ * outputs are written. */
+typedef struct gf_mesh_mt gf_mesh_mt;
+gf_mesh_mt* gf_mesh_mt_create(void);
+void gf_mesh_mt_destroy(gf_mesh_mt* mt);
+int gf_mesh_mt_run(gf_mesh_mt* mt, const float* vertices, uint64_t num_vertices, const int64_t* tets,
+                   uint64_t num_tets, const float* sdf, const float* scales, uint64_t chunk_tets,
+                   uint64_t* num_edges, uint64_t* num_faces, void* stream);
+int gf_mesh_mt_outputs(gf_mesh_mt* mt, float* endpoints, float* endpoint_fields, float* endpoint_scales,
+                       int64_t* faces, int64_t* edges, void* stream);
+
+/* SOF's vertex filter (gofish/mesh/filters.py:15-29): keep[e] = 1 when
+ * |p_a - p_b| <= scale_a + scale_b for crossing edge e = (a, b). */
+int gf_mesh_sof_vertex_filter(const float* points, const float* scale, const int64_t* edges, uint64_t num_edges,
+                              uint8_t* keep, void* stream);
+
+/* GOF's cell filter (gofish/mesh/filters.py:42-58): keep[t] = 0 when an edge
+ * of tetrahedron t joins two different owners farther apart than the sum of
+ * their scales. */
+int gf_mesh_gof_cell_filter(const int64_t* cells, uint64_t num_cells, const float* points, const float* scale,
+                            const int64_t* owner, uint8_t* keep, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

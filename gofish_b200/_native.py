@@ -18,6 +18,8 @@ GF_KEY_GLOBAL_DEPTH = 1
 GF_FALLBACK_NONE = 0
 GF_CAPACITY_SPECULATIVE = 0
 GF_CAPACITY_EXACT = 1
+GF_COMPOSITOR_KBUFFER = 0
+GF_COMPOSITOR_SOF = 1
 GF_FALLBACK_CONE = 1
 STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
 
@@ -47,6 +49,7 @@ class GfTracerConfig(ctypes.Structure):
         ("composite_log_capacity", ctypes.c_int32),
         ("enable_normals", ctypes.c_int32),
         ("intersection_capacity", ctypes.c_int32),
+        ("compositor", ctypes.c_int32),
     ]
 
 
@@ -252,7 +255,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 4:
+    if lib.gf_abi_version() != 5:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

@@ -36,6 +36,7 @@
 #include "../../include/gofish_b200.h"
 #include "gf_host.cuh"
 #include "gf_render.cuh"
+#include "gf_render_sof.cuh"
 #include "gf_tracer_kernels.cuh"
 
 namespace {
@@ -609,7 +610,20 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     t->frameGeo = geoOut != nullptr;
     {
         StageTimer st(t, GF_STAGE_RENDER_FWD, stream);
-        if (int e = dispatch_fwd(t->cfg.k_buffer_size, a, T, rgba, hd, hc, stream)) return e;
+        if (t->cfg.compositor == GF_COMPOSITOR_SOF) {
+            const int smem = int(gf::sof_smem_bytes());
+            if (a.geo.particles != nullptr) {
+                GF_CUDA(cudaFuncSetAttribute(gf::k_render_fwd_sof<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem));
+                gf::k_render_fwd_sof<true><<<T, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
+            } else {
+                GF_CUDA(cudaFuncSetAttribute(gf::k_render_fwd_sof<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem));
+                gf::k_render_fwd_sof<false><<<T, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
+            }
+        } else if (int e = dispatch_fwd(t->cfg.k_buffer_size, a, T, rgba, hd, hc, stream)) {
+            return e;
+        }
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();
@@ -654,6 +668,10 @@ gf_tracer* gf_tracer_create(const gf_tracer_config* config) {
     }
     if (config->admission_fallback != GF_FALLBACK_NONE && config->admission_fallback != GF_FALLBACK_CONE) {
         fail(GF_ERR_BAD_INPUT, "unknown admission fallback %d", config->admission_fallback);
+        return nullptr;
+    }
+    if (config->compositor != GF_COMPOSITOR_KBUFFER && config->compositor != GF_COMPOSITOR_SOF) {
+        fail(GF_ERR_BAD_INPUT, "unknown compositor %d", config->compositor);
         return nullptr;
     }
     if (config->intersection_capacity != GF_CAPACITY_SPECULATIVE &&
@@ -786,7 +804,20 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
         }
         if (t->residentBlocks == 0) t->residentBlocks = int(resident_blocks());
         const uint32_t grid = a.r.log.ids != nullptr ? std::min<uint32_t>(T, uint32_t(t->residentBlocks)) : T;
-        if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, grid, s)) return e;
+        if (t->cfg.compositor == GF_COMPOSITOR_SOF) {
+            const int smem = int(gf::sof_smem_bytes());
+            if (a.geo.gradShape != nullptr) {
+                GF_CUDA(cudaFuncSetAttribute(gf::k_render_bwd_sof<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem));
+                gf::k_render_bwd_sof<true><<<grid, gf::kTileThreads, smem, s>>>(a);
+            } else {
+                GF_CUDA(cudaFuncSetAttribute(gf::k_render_bwd_sof<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             smem));
+                gf::k_render_bwd_sof<false><<<grid, gf::kTileThreads, smem, s>>>(a);
+            }
+        } else if (int e = dispatch_bwd(t->cfg.k_buffer_size, a, grid, s)) {
+            return e;
+        }
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();

@@ -73,6 +73,15 @@ class SplatRaster:
             raise ValueError(f"render.splat.intersection_capacity must be 'speculative' or 'exact' (got {capacity!r})")
         cfg.intersection_capacity = (_native.GF_CAPACITY_EXACT if capacity == "exact"
                                      else _native.GF_CAPACITY_SPECULATIVE)
+        # SOF's HEAD4 / MID8 / TAIL64 hierarchy instead of the flat k-buffer
+        hierarchical = bool(_select(conf, "render.splat.hierarchical_sort", False))
+        if hierarchical and not bool(_select(conf, "render.splat.sof_mid8_hierarchy", True)):
+            raise NotImplementedError("render.splat.hierarchical_sort renders with SOF's MID8 hierarchy only")
+        if hierarchical and (int(_select(conf, "render.splat.head_size", 4)) != 4
+                             or int(_select(conf, "render.splat.mid_size", 8)) != 8
+                             or int(_select(conf, "render.splat.tail_size", 64)) != 64):
+            raise ValueError("SOF's hierarchy uses HEAD4, MID8 and TAIL64")
+        cfg.compositor = _native.GF_COMPOSITOR_SOF if hierarchical else _native.GF_COMPOSITOR_KBUFFER
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())

@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 4
+#define GF_ABI_VERSION 5
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -77,7 +77,17 @@ typedef struct gf_tracer_config {
     int32_t enable_normals;         /* render.enable_normals: 1 computes the geometric training channels
                                        (gf_trace_outputs.normal ... inv_depth2) and their gradients */
     int32_t intersection_capacity;  /* GF_CAPACITY_*: how the tile-intersection keys are sized */
+    int32_t compositor;             /* GF_COMPOSITOR_*: render.splat.hierarchical_sort */
 } gf_tracer_config;
+
+/* Compositing order of a pixel's hits.  KBUFFER: the tile's depth-sorted
+ * candidates through a per-pixel k-buffer of k_buffer_size
+ * (gutKBufferRenderer.cuh:614-700).  SOF: SOF's hierarchy, a per-pixel HEAD
+ * of 4 fed by per-2x2 MID8 and per-4x4 TAIL64 windows ordered by
+ * representative depth (sofMid8Hierarchy.inl:161-598); k_buffer_size is not
+ * used. */
+#define GF_COMPOSITOR_KBUFFER 0
+#define GF_COMPOSITOR_SOF 1
 
 /* Sizing of the tile-intersection keys of a forward.  SPECULATIVE: 1.5x the
  * largest count of the earlier forwards, with no host synchronization (the

@@ -124,6 +124,7 @@ def load():
                                        vp]),
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
+        "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
         "oracle_field_index_build": (vp, [i32, vp, ctypes.c_double]),
         "oracle_field_index_free": (None, [vp]),
         "oracle_field_camera_indexed": (i32, [vp, cam_p, pose_p, vp, vp, i32, vp, vp, vp]),
@@ -370,6 +371,30 @@ def trace_backward(cam, fwd, particles, sh, sh_degree, ray_o, ray_d, mask, k, gr
                           fwd["rgba"], fwd["hit_t"], grad_rgba, grad_hit_t, tiles)
     gp, gs = project_backward(fwd["pose"], particles, sh, sh_degree, fwd["counts"], rec)
     return gp, gs, rec
+
+
+SOF_HIERARCHY = -1  # the k argument of the render calls that selects SOF's HEAD4 / MID8 / TAIL64 hierarchy
+
+
+def sof_feeds(cam, pose, particles, ray_o, ray_d, ranges, sorted_ids, tile):
+    """The SOF hierarchy's feed sequence (sorted positions, in order) of every
+    pixel of one tile: a list of 256 arrays, row-major within the tile."""
+    lib = load()
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    r = np.ascontiguousarray(ranges, dtype=np.uint32)
+    count = int(r.reshape(-1, 2)[tile, 1] - r.reshape(-1, 2)[tile, 0])
+    offset = np.zeros(257, dtype=np.uint32)
+    feed = np.zeros(max(1, 256 * count), dtype=np.uint32)
+    total = lib.oracle_sof_feeds(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                                 _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                 _p(np.ascontiguousarray(ray_d, dtype=np.float32)), _p(r), _p(ids), int(tile),
+                                 _p(offset), _p(feed), feed.size)
+    if total < 0:
+        raise RuntimeError("oracle_sof_feeds capacity")
+    return [feed[offset[p]:offset[p + 1]].copy() for p in range(256)]
 
 
 def field_camera(cam, pose7, particles, ray_o, points, pixel_mask=None):

@@ -788,6 +788,7 @@ struct Ray {
     float3_ o, d;
     float tmin, tmax;
     bool valid;
+    int local = 0;  // pixel index within its 16x16 tile (row-major), for the SOF feed
 };
 
 // bounding_box.h:89-133 ray_intersect against the +-1e6 box; rayPayload.cuh:113-162.
@@ -928,13 +929,218 @@ struct Scene {
     const uint8_t* mask;
     const uint32_t* ranges;
     const uint32_t* sortedIds;
-    int K;
+    int K;  // k-buffer size; kSofHierarchy: SOF's HEAD4 / MID8 / TAIL64 hierarchy
 };
 
+// ------------------------------------------------------------------ SOF hierarchy
+// The SOF compositor (sofMid8Hierarchy.inl:161-598, gutRenderer training
+// default): per 4x4 pixel group a TAIL window of up to 64 candidates, per 2x2
+// group a MID window of up to 8, per pixel a HEAD k-buffer of 4 by exact hit
+// distance.  TAIL and MID order candidates by (representative depth, position
+// in the tile's sorted list), the representative depth being the
+// maximum-response depth of the particle along the group's representative
+// ray (mean of the group's in-raster world rays: the central 2x2 pixels of a
+// 4x4 group, else all of them; the four pixels of a 2x2 group).  The tile's
+// candidates stream in chunks of 32 into every TAIL; a TAIL holding more than
+// 32 emits its 16 nearest (twice per chunk); an emission reaches the four MID
+// windows under it in batches of 4; a MID holding more than 4 emits its 4
+// nearest, which every pixel of the 2x2 group feeds through its HEAD.  At the
+// end the TAILs drain in two emissions of up to 16, then the MIDs and the
+// HEADs.  The cascade does not depend on the pixels' state, so it is
+// computed once per tile as each pixel's feed sequence (sorted positions).
+constexpr int kSofHierarchy = -1;
+constexpr int kSofHead = 4;
+
+struct SofItem {
+    float key;
+    uint32_t pos;  // position in the tile's sorted list (unique: the tie-break)
+};
+inline bool sof_less(const SofItem& a, const SofItem& b) { return a.key < b.key || (a.key == b.key && a.pos < b.pos); }
+
+// Merge of two windows by rank counting: item order is (key, position), and
+// each item's place is the number of items below it (as the GPU writes by rank).
+std::vector<SofItem> sof_merge(const std::vector<SofItem>& a, const std::vector<SofItem>& b) {
+    std::vector<SofItem> all(a);
+    all.insert(all.end(), b.begin(), b.end());
+    std::vector<SofItem> out(all.size());
+    for (size_t i = 0; i < all.size(); ++i) {
+        size_t rank = 0;
+        for (size_t j = 0; j < all.size(); ++j) rank += sof_less(all[j], all[i]) ? 1 : 0;
+        out[rank] = all[i];
+    }
+    return out;
+}
+
+struct SofRay {
+    float3_ o, d;
+};
+
+// Mean of the listed world rays: origin sum x (1 / count), direction
+// d / sqrt(|d|^2) of the summed directions ((0,0,1) when degenerate).
+SofRay sof_mean_ray(const std::vector<const Ray*>& rays) {
+    float3_ o = f3(0.0f, 0.0f, 0.0f), d = f3(0.0f, 0.0f, 0.0f);
+    for (const Ray* r : rays) {
+        o = add(o, r->o);
+        d = add(d, r->d);
+    }
+    SofRay out;
+    const float inv = rays.empty() ? 0.0f : 1.0f / float(rays.size());
+    out.o = rays.empty() ? f3(0.0f, 0.0f, 0.0f) : f3(o.x * inv, o.y * inv, o.z * inv);
+    const float n2 = fdot(d, d);
+    if (!(n2 > 0.0f) || !gf::isfinite_f(n2)) {
+        out.d = f3(0.0f, 0.0f, 1.0f);
+    } else {
+        const float inorm = 1.0f / sqrtf(n2);
+        out.d = f3(d.x * inorm, d.y * inorm, d.z * inorm);
+    }
+    return out;
+}
+
+// Maximum-response depth of a particle along a representative ray
+// (sofMid8Hierarchy.inl:95-129): max(0, -(B^-1 (o - mu)) . (B^-1 d) / |B^-1 d|^2),
+// the radial distance |mu - o| when that is not defined.
+float sof_depth(const Particle& P, const SofRay& r) {
+    const float3_ co = fmatvec(P.Binv, sub(r.o, P.pos));
+    const float3_ cd = fmatvec(P.Binv, r.d);
+    const float den = fdot(cd, cd);
+    const float3_ delta = sub(P.pos, r.o);
+    const float radial = sqrtf(fdot(delta, delta));
+    if (!(den > 0.0f) || !gf::isfinite_f(den)) return radial;
+    const float depth = -fdot(co, cd) / den;
+    return gf::isfinite_f(depth) ? gf::max_f(0.0f, depth) : radial;
+}
+
+// Feed sequences (sorted positions) of the 256 pixels of a tile.
+std::vector<std::vector<uint32_t>> sof_feeds(const Scene& sc, uint32_t tile) {
+    const int W = sc.cam->width, H = sc.cam->height;
+    const int gx = (W + kTile - 1) / kTile;
+    const int tx = int(tile) % gx, ty = int(tile) / gx;
+    std::vector<Ray> rays(256);
+    std::vector<bool> inb(256, false);
+    for (int ly = 0; ly < 16; ++ly)
+        for (int lx = 0; lx < 16; ++lx) {
+            const int px = tx * kTile + lx, py = ty * kTile + ly;
+            if (px < W && py < H) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                rays[size_t(ly * 16 + lx)] = make_ray(*sc.pose, sc.rayO + 3 * pix, sc.rayD + 3 * pix);
+                inb[size_t(ly * 16 + lx)] = true;
+            }
+        }
+    SofRay tailRay[16], midRay[64];
+    for (int g = 0; g < 16; ++g) {
+        const int bx = (g & 3) * 4, by = (g >> 2) * 4;
+        std::vector<const Ray*> sel;
+        for (int oy = 1; oy <= 2; ++oy)
+            for (int ox = 1; ox <= 2; ++ox)
+                if (inb[size_t((by + oy) * 16 + bx + ox)]) sel.push_back(&rays[size_t((by + oy) * 16 + bx + ox)]);
+        if (sel.empty())
+            for (int oy = 0; oy < 4; ++oy)
+                for (int ox = 0; ox < 4; ++ox)
+                    if (inb[size_t((by + oy) * 16 + bx + ox)]) sel.push_back(&rays[size_t((by + oy) * 16 + bx + ox)]);
+        tailRay[g] = sof_mean_ray(sel);
+    }
+    for (int m = 0; m < 64; ++m) {
+        const int bx = (m & 7) * 2, by = (m >> 3) * 2;
+        std::vector<const Ray*> sel;
+        for (int oy = 0; oy < 2; ++oy)
+            for (int ox = 0; ox < 2; ++ox)
+                if (inb[size_t((by + oy) * 16 + bx + ox)]) sel.push_back(&rays[size_t((by + oy) * 16 + bx + ox)]);
+        midRay[m] = sof_mean_ray(sel);
+    }
+    std::vector<std::vector<uint32_t>> feeds(256);
+    std::vector<SofItem> tail[16], mid[64];
+    auto key_of = [&](uint32_t pos, const SofRay& r) {
+        const Particle P = load_particle(sc.particles + 32 * size_t(sc.sortedIds[pos]));
+        return SofItem{sof_depth(P, r), pos};
+    };
+    // MID windows of one tail emission per tail group, in batches of four
+    auto route = [&](std::vector<SofItem> (&emitted)[16]) {
+        for (int batch = 0; batch < 4; ++batch) {
+            for (int m = 0; m < 64; ++m) {
+                const int parent = ((m >> 3) >> 1) * 4 + ((m & 7) >> 1);
+                std::vector<SofItem> fresh;
+                for (int k = 4 * batch; k < 4 * batch + 4 && k < int(emitted[parent].size()); ++k)
+                    fresh.push_back(key_of(emitted[parent][size_t(k)].pos, midRay[m]));
+                mid[m] = sof_merge(mid[m], fresh);
+                if (mid[m].size() > 4) {
+                    const int bx = (m & 7) * 2, by = (m >> 3) * 2;
+                    for (int i = 0; i < 4; ++i)
+                        for (int oy = 0; oy < 2; ++oy)
+                            for (int ox = 0; ox < 2; ++ox) feeds[size_t((by + oy) * 16 + bx + ox)].push_back(mid[m][size_t(i)].pos);
+                    mid[m].erase(mid[m].begin(), mid[m].begin() + 4);
+                }
+            }
+        }
+    };
+    auto emit_tails = [&](bool drain) {
+        std::vector<SofItem> emitted[16];
+        for (int g = 0; g < 16; ++g) {
+            const size_t count = drain ? std::min<size_t>(16, tail[g].size()) : (tail[g].size() > 32 ? 16 : 0);
+            emitted[g].assign(tail[g].begin(), tail[g].begin() + long(count));
+            tail[g].erase(tail[g].begin(), tail[g].begin() + long(count));
+        }
+        route(emitted);
+    };
+    const uint32_t b = sc.ranges[2 * tile], e = sc.ranges[2 * tile + 1];
+    for (uint32_t chunk = b; chunk < e; chunk += 32) {
+        const uint32_t stop = std::min(chunk + 32u, e);
+        for (int g = 0; g < 16; ++g) {
+            std::vector<SofItem> fresh;
+            for (uint32_t pos = chunk; pos < stop; ++pos) fresh.push_back(key_of(pos, tailRay[g]));
+            tail[g] = sof_merge(tail[g], fresh);
+        }
+        emit_tails(false);
+        emit_tails(false);
+    }
+    emit_tails(true);
+    emit_tails(true);
+    for (int m = 0; m < 64; ++m) {
+        const int bx = (m & 7) * 2, by = (m >> 3) * 2;
+        for (const SofItem& it : mid[m])
+            for (int oy = 0; oy < 2; ++oy)
+                for (int ox = 0; ox < 2; ++ox) feeds[size_t((by + oy) * 16 + bx + ox)].push_back(it.pos);
+        mid[m].clear();
+    }
+    return feeds;
+}
+
+// The feed sequence of one pixel, computed once per tile and worker thread.
+const std::vector<uint32_t>& sof_pixel_feed(const Scene& sc, uint32_t tile, const Ray& ray) {
+    thread_local const Scene* cachedScene = nullptr;
+    thread_local uint32_t cachedTile = 0xffffffffu;
+    thread_local std::vector<std::vector<uint32_t>> cached;
+    if (cachedScene != &sc || cachedTile != tile) {
+        cached = sof_feeds(sc, tile);
+        cachedScene = &sc;
+        cachedTile = tile;
+    }
+    return cached[size_t(ray.local)];
+}
+
 // Walk one pixel's tile list in the order of gutKBufferRenderer.cuh:614-700,
-// calling `hitFn(Hit, state)` for each composited hit.
+// calling `hitFn(Hit, state)` for each composited hit; with the SOF
+// hierarchy, walk its feed sequence through a HEAD of 4.
 template <typename HitFn>
 void traverse(const Scene& sc, uint32_t tile, const Ray& ray, bool& alive, HitFn&& hitFn) {
+    if (sc.K == kSofHierarchy) {
+        const std::vector<uint32_t>& feed = sof_pixel_feed(sc, tile, ray);
+        KBuffer kb;
+        kb.init(kSofHead);
+        for (size_t f = 0; f < feed.size() && alive; ++f) {
+            const uint32_t idx = sc.sortedIds[feed[f]];
+            const Particle P = load_particle(sc.particles + 32 * size_t(idx));
+            Hit h;
+            h.idx = idx;
+            float resp;
+            HalfRay hr;
+            if (hit_test(ray, P, h.alpha, h.hitT, resp, hr) && h.hitT >= ray.tmin && h.hitT <= ray.tmax) {
+                if (kb.full()) hitFn(kb.e[0]);
+                kb.insert(h);
+            }
+        }
+        for (uint32_t i = 0; alive && i < kb.n; ++i) hitFn(kb.e[kSofHead - kb.n + i]);
+        return;
+    }
     const uint32_t b = sc.ranges[2 * tile], e = sc.ranges[2 * tile + 1];
     KBuffer kb;
     kb.init(sc.K);
@@ -1300,7 +1506,8 @@ int oracle_render_forward(const OracleCamera* cam, const OraclePose* pose, int N
         for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
             for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
                 const size_t pix = size_t(px) + size_t(W) * py;
-                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                ray.local = (py - ty * kTile) * kTile + (px - tx * kTile);
                 if (!ray.valid) continue;
                 PixelState s{1.0f, {0.0f, 0.0f, 0.0f}, 0.0f, 0u, true};
                 traverse(sc, uint32_t(tile), ray, s.alive, [&](const Hit& h) { composite(s, h, rgb); });
@@ -1334,7 +1541,8 @@ int oracle_render_forward_geo(const OracleCamera* cam, const OraclePose* pose, i
         for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
             for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
                 const size_t pix = size_t(px) + size_t(W) * py;
-                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                ray.local = (py - ty * kTile) * kTile + (px - tx * kTile);
                 if (!ray.valid) continue;
                 PixelState s{1.0f, {0.0f, 0.0f, 0.0f}, 0.0f, 0u, true};
                 GeoState g{};
@@ -1391,7 +1599,8 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
             for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
                 for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
                     const size_t pix = size_t(px) + size_t(W) * py;
-                    const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                    Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                    ray.local = (py - ty * kTile) * kTile + (px - tx * kTile);
                     if (!ray.valid) continue;
                     // initializeBackwardRay, rayPayloadBackward.cuh:59-120
                     const float featB[3] = {rgba[4 * pix], rgba[4 * pix + 1], rgba[4 * pix + 2]};
@@ -1514,7 +1723,8 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
         for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py) {
             for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
                 const size_t pix = size_t(px) + size_t(W) * py;
-                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                ray.local = (py - ty * kTile) * kTile + (px - tx * kTile);
                 if (!ray.valid) continue;
                 const float featB[3] = {rgba[4 * pix], rgba[4 * pix + 1], rgba[4 * pix + 2]};
                 const float featG[3] = {gradRgba[4 * pix], gradRgba[4 * pix + 1], gradRgba[4 * pix + 2]};
@@ -1709,6 +1919,28 @@ int oracle_project_backward(const OraclePose* pose, int N, const float* particle
         gp[2] += (dirGrad.z - dir.z * ndg) / dist;
     });
     return 0;
+}
+
+// The SOF hierarchy's feed sequences of one tile: for local pixel p,
+// feed[offset[p] .. offset[p+1]) are the sorted positions fed to its HEAD in
+// order (offset has 257 entries).  Returns the total, or -1 when it exceeds
+// capacity.
+int64_t oracle_sof_feeds(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                         const float* rayO, const float* rayD, const uint32_t* ranges, const uint32_t* sortedIds,
+                         int tile, uint32_t* offset, uint32_t* feed, int64_t capacity) {
+    Scene sc{cam, pose, N, particles, nullptr, rayO, rayD, nullptr, ranges, sortedIds, kSofHierarchy};
+    const auto feeds = sof_feeds(sc, uint32_t(tile));
+    int64_t total = 0;
+    for (int p = 0; p < 256; ++p) {
+        offset[p] = uint32_t(total);
+        total += int64_t(feeds[size_t(p)].size());
+    }
+    offset[256] = uint32_t(total);
+    if (total > capacity) return -1;
+    int64_t k = 0;
+    for (int p = 0; p < 256; ++p)
+        for (const uint32_t v : feeds[size_t(p)]) feed[k++] = v;
+    return total;
 }
 
 // Visibility of gutRenderer.cu:204-209: 1 (as an int bit pattern) when the

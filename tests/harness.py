@@ -82,6 +82,7 @@ class GpuTracer:
 
     def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0,
                  enable_normals: bool = False):
+        """k: k-buffer size, or oracle.SOF_HIERARCHY for SOF's hierarchy."""
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -89,7 +90,9 @@ class GpuTracer:
         self.torch = torch
         self.case = case
         self.device = device
-        conf = {"render": {"splat": {"k_buffer_size": k, "composite_log_capacity": log_capacity},
+        sof = k == oracle.SOF_HIERARCHY
+        conf = {"render": {"splat": {"k_buffer_size": 16 if sof else k, "composite_log_capacity": log_capacity,
+                                     "hierarchical_sort": sof},
                            "gofish": {"fast_global_depth_key": key_mode == 1,
                                       "fast_admission_fallback": "cone" if fallback else "none"},
                            "enable_hitcounts": True, "enable_normals": enable_normals}}

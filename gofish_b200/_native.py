@@ -69,6 +69,7 @@ class GfTraceInputs(ctypes.Structure):
         ("timestamp_start", ctypes.c_int64),
         ("timestamp_end", ctypes.c_int64),
         ("tile_token", ctypes.c_char_p),
+        ("sof_opacity_active", ctypes.c_int32),
     ]
 
 
@@ -84,6 +85,7 @@ class GfTraceOutputs(ctypes.Structure):
         ("extent", ctypes.c_void_p),
         ("inv_depth", ctypes.c_void_p),
         ("inv_depth2", ctypes.c_void_p),
+        ("opacity_field", ctypes.c_void_p),
     ]
 
 
@@ -105,6 +107,9 @@ class GfTraceGrads(ctypes.Structure):
         ("grad_inv_depth", ctypes.c_void_p),
         ("inv_depth2", ctypes.c_void_p),
         ("grad_inv_depth2", ctypes.c_void_p),
+        ("quant", ctypes.c_void_p),
+        ("opacity_field", ctypes.c_void_p),
+        ("grad_opacity_field", ctypes.c_void_p),
     ]
 
 

@@ -37,6 +37,7 @@
 #include "gf_host.cuh"
 #include "gf_render.cuh"
 #include "gf_render_sof.cuh"
+#include "gf_sof_opacity.cuh"
 #include "gf_tracer_kernels.cuh"
 
 namespace {
@@ -88,6 +89,8 @@ struct gf_tracer {
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
     gf::CompositeLog frameLog{};
     bool frameGeo = false;                                // the last forward wrote the geometric channels
+    bool frameSof = false;                                // the last forward wrote the SOF opacity field
+    DeviceBuffer gradIntrinsic;                           // SOF opacity field gradient [N,4] float4
     uint64_t* hostTotal = nullptr;  // [0] intersections, [1] fallback list size, [2] log overflow tiles (low 32 bits)
     uint32_t fallbackParticles = 0;
     // Intersection plans (speculative key capacity).
@@ -627,6 +630,25 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();
+    t->frameSof = false;
+    if (in->sof_opacity_active != 0) {
+        if (geoOut == nullptr || geoOut->quant == nullptr || geoOut->opacity_field == nullptr)
+            return fail(GF_ERR_BAD_INPUT, "the SOF opacity field needs enable_normals (its exact crossing depth)");
+        gf::SofOpacityArgs so{};
+        so.f = f;
+        so.mask = a.mask;
+        so.ranges = a.ranges;
+        so.sortedIds = a.sortedIds;
+        so.particles = in->particles;
+        so.rayO = in->ray_origin;
+        so.rayD = in->ray_direction;
+        so.quant = geoOut->quant;
+        so.opacity = geoOut->opacity_field;
+        gf::k_sof_opacity<false><<<T, gf::kTileThreads, 0, stream>>>(so);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+        t->frameSof = true;
+    }
     // the overflow count for gf_tracer_stats, read without a synchronization here
     t->logCounted = false;
     if (a.log.ids != nullptr) {
@@ -696,7 +718,7 @@ void gf_tracer_destroy(gf_tracer* t) {
         for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow, &t->logList}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,
                                 &t->tileRays, &t->ranges,  &t->keys[0], &t->keys[1], &t->ids[0],   &t->ids[1],
-                                &t->hist,    &t->gradRecords, &t->gradShape};
+                                &t->hist,    &t->gradRecords, &t->gradShape, &t->gradIntrinsic};
         for (DeviceBuffer* b : bufs) b->release();
         for (auto& kv : t->masks) kv.second.buf.release();
         for (auto& ev : t->pending) {
@@ -821,12 +843,35 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     }
     t->launches += 1;
     GF_LAUNCH_CHECK();
+    float4* gradIntrinsic = nullptr;
+    if (g->grad_opacity_field != nullptr) {
+        if (!t->frameSof || g->opacity_field == nullptr || g->quant == nullptr)
+            return fail(GF_ERR_STATE, "an opacity-field gradient needs a forward with the SOF opacity field");
+        if (int e = t->gradIntrinsic.ensure(sizeof(float4) * 4 * size_t(N) + 16, s)) return e;
+        GF_CUDA(cudaMemsetAsync(t->gradIntrinsic.ptr, 0, sizeof(float4) * 4 * size_t(N), s));
+        gradIntrinsic = t->gradIntrinsic.as<float4>();
+        gf::SofOpacityArgs so{};
+        so.f = f;
+        so.mask = t->frameMask;
+        so.ranges = t->ranges.as<uint2>();
+        so.sortedIds = t->ids[t->finalBuf].as<uint32_t>();
+        so.particles = in->particles;
+        so.rayO = t->frameRayO;
+        so.rayD = t->frameRayD;
+        so.quant = g->quant;
+        so.opacityIn = g->opacity_field;
+        so.gradOpacity = g->grad_opacity_field;
+        so.gradIntrinsic = gradIntrinsic;
+        gf::k_sof_opacity<true><<<T, gf::kTileThreads, 0, s>>>(so);
+        t->launches += 1;
+        GF_LAUNCH_CHECK();
+    }
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT_BWD, s);
         gf::k_project_bwd<<<(N + gf::kProjectBwdThreads - 1) / gf::kProjectBwdThreads, gf::kProjectBwdThreads,
                              gf::project_bwd_smem_bytes(f.shCoeffs), s>>>(
             f, in->particles, in->features, t->counts.as<uint32_t>(), t->gradRecords.as<float4>(), a.geo.gradShape,
-            g->grad_particles, g->grad_features);
+            gradIntrinsic, g->grad_particles, g->grad_features);
         t->launches += 1;
         GF_LAUNCH_CHECK();
     }

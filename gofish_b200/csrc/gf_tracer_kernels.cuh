@@ -976,6 +976,7 @@ __global__ __launch_bounds__(kProjectBwdThreads) void k_project_bwd(FrameArgs f,
                                                                     const uint32_t* __restrict__ counts,
                                                                     const float4* __restrict__ gradRecords,
                                                                     const float4* __restrict__ gradShape,
+                                                                    const float4* __restrict__ gradIntrinsic,
                                                                     float* __restrict__ gradParticles,
                                                                     float* __restrict__ gradFeatures) {
     extern __shared__ float shRows[];  // [kProjectBwdThreads][3 * shCoeffs + 1]
@@ -1044,11 +1045,23 @@ __global__ __launch_bounds__(kProjectBwdThreads) void k_project_bwd(FrameArgs f,
         }
         float4* out = reinterpret_cast<float4*>(gradParticles + 32 * size_t(i));
         // rotation and intrinsic scale receive the extent channel's gradient (enable_normals)
-        const float4 gq = gradShape != nullptr ? gradShape[2 * size_t(i)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        const float4 gsc = gradShape != nullptr ? gradShape[2 * size_t(i) + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 gq = gradShape != nullptr ? gradShape[2 * size_t(i)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 gsc = gradShape != nullptr ? gradShape[2 * size_t(i) + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float gIntrinsicDensity = 0.0f;
+        if (gradIntrinsic != nullptr) {
+            // the SOF opacity field's gradient of the intrinsic Gaussian
+            const float4 i0 = gradIntrinsic[4 * size_t(i)], i1 = gradIntrinsic[4 * size_t(i) + 1],
+                         i2 = gradIntrinsic[4 * size_t(i) + 2];
+            gp0 += i0.x;
+            gp1 += i0.y;
+            gp2 += i0.z;
+            gIntrinsicDensity = i0.w;
+            gq = make_float4(gq.x + i1.x, gq.y + i1.y, gq.z + i1.z, gq.w + i1.w);
+            gsc = make_float4(gsc.x + i2.x, gsc.y + i2.y, gsc.z + i2.z, 0.0f);
+        }
         out[0] = make_float4(gp0, gp1, gp2, g0.w);                      // pos, density
         out[1] = gq;                                                    // rotation
-        out[2] = make_float4(gsc.x, gsc.y, gsc.z, 0.0f);                // scale, intrinsic density
+        out[2] = make_float4(gsc.x, gsc.y, gsc.z, gIntrinsicDensity);   // scale, intrinsic density
         out[3] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 0..3
         out[4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);                   // factor 4..7
         out[5] = make_float4(0.0f, g1.x, g1.y, g1.z);                   // factor 8 | Binv 0..2

@@ -156,8 +156,8 @@ class SplatRaster:
         """splatRaster.cpp:259-380.  Returns the reference's 11 tensors:
         radiance+opacity [H,W,4], hit distance [H,W,1], hit count [H,W,1],
         visibility [N,1], and the seven training geometric channels."""
-        if sof_exact_opacity_active:
-            raise NotImplementedError("the SOF opacity-field channel is not implemented by this tracer")
+        if sof_exact_opacity_active and not self.config.enable_normals:
+            raise ValueError("the SOF opacity field needs render.enable_normals (its exact crossing depth)")
         device = ray_ori.device
         height, width = int(ray_ori.shape[1]), int(ray_ori.shape[2])
         n = particle_density.shape[0]
@@ -179,6 +179,9 @@ class SplatRaster:
         if self.config.enable_normals:
             out.normal, out.depth_var, out.quant, out.extent = (t.data_ptr() for t in geo[:4])
             out.inv_depth, out.inv_depth2 = geo[5].data_ptr(), geo[6].data_ptr()
+        if sof_exact_opacity_active:
+            inp.sof_opacity_active = 1
+            out.opacity_field = geo[4].data_ptr()
         with torch.cuda.device(device):
             end = self._timed("forward_render", device)
             check(self._lib.gf_tracer_trace(self._handle, ctypes.byref(inp), ctypes.byref(out), _stream(device)),
@@ -239,7 +242,8 @@ class SplatRaster:
         return grad_particles, grad_features
 
     # (value, gradient) pairs of trace_bwd in the reference's order (splatRaster.cpp:469-500) and their
-    # channel widths; the opacity field and the quantile/crossing channel have no gradient path here
+    # channel widths; the quantile/crossing channel has no gradient path here (its value feeds the
+    # opacity field's gradient)
     GEOMETRY_PAIRS = (("depth_var", 1), ("extent", 1), ("opacity_field", 1), ("quant", QUANT_CHANNELS),
                       ("normal", 3), ("inv_depth", 1), ("inv_depth2", 1))
 
@@ -251,11 +255,21 @@ class SplatRaster:
             return keep
         for i, (name, channels) in enumerate(self.GEOMETRY_PAIRS):
             value, grad = geometry[2 * i], geometry[2 * i + 1]
+            if name == "quant":
+                # the forward's crossing depths, read by the opacity field's gradient
+                if value is not None and value.numel() == height * width * channels:
+                    q = value.float().contiguous()
+                    keep.append(q)
+                    g.quant = q.data_ptr()
+                if grad is not None and bool(torch.count_nonzero(grad)):
+                    raise NotImplementedError("the gradient of the quantile channel is not propagated by this tracer")
+                continue
             if grad is None or value is None or grad.numel() != height * width * channels:
                 continue
-            if name in ("opacity_field", "quant"):
-                if bool(torch.count_nonzero(grad)):
-                    raise NotImplementedError(f"the gradient of the {name} channel is not propagated by this tracer")
+            if name == "opacity_field":
+                v, gv = value.float().contiguous(), grad.float().contiguous()
+                keep += [v, gv]
+                g.opacity_field, g.grad_opacity_field = v.data_ptr(), gv.data_ptr()
                 continue
             v = value.float().contiguous()
             d = grad.float().contiguous()

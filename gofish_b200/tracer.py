@@ -45,7 +45,7 @@ PACKED_SPLIT = (3, 1, 4, 3, 1, 9, 9, 2)
 # Losses on the geometric training channels (they need render.enable_normals),
 # and the one whose channel (the SOF opacity field) is not rendered here.
 GEOMETRIC_LOSSES = ("lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_extent", "lambda_normal_variance")
-UNSUPPORTED_LOSSES = ("lambda_opa",)
+UNSUPPORTED_LOSSES: tuple = ()
 
 
 def _conf_value(conf, path: str, default):
@@ -133,9 +133,10 @@ class Tracer:
             return [name for name in names if float(_conf_value(conf, f"loss.{name}", 0.0) or 0.0) > 0.0]
 
         if active(UNSUPPORTED_LOSSES):
-            raise NotImplementedError("the SOF opacity-field loss (loss.lambda_opa) is not supported by this tracer")
-        if active(GEOMETRIC_LOSSES) and not bool(_conf_value(conf, "render.enable_normals", False)):
-            raise ValueError("losses on the geometric channels (" + ", ".join(active(GEOMETRIC_LOSSES)) +
+            raise NotImplementedError("unsupported losses: " + ", ".join(active(UNSUPPORTED_LOSSES)))
+        geometric = active(GEOMETRIC_LOSSES + ("lambda_opa",))
+        if geometric and not bool(_conf_value(conf, "render.enable_normals", False)):
+            raise ValueError("losses on the geometric channels (" + ", ".join(geometric) +
                              ") need render.enable_normals")
         if bool(_conf_value(conf, "loss.color_confidence", False)):
             raise NotImplementedError("CoMe colour confidence (loss.color_confidence) is not rendered by this tracer")
@@ -202,17 +203,30 @@ class Tracer:
     def build_acc(self, gaussians, rebuild=True):
         """No acceleration structure for a rasterised tracer (tracer.py:443-444)."""
 
+    def _sof_opacity_active(self, train: bool, frame_id: int) -> bool:
+        """tracer.py:433-448: the SOF opacity field is traced for training
+        frames with loss.lambda_opa > 0 from loss.opa_warmup (default
+        loss.geom_warmup, 15,000) until the distillation steps."""
+        lam = float(_conf_value(self.conf, "loss.lambda_opa", 0.0) or 0.0)
+        warm = _conf_value(self.conf, "loss.opa_warmup", None)
+        if warm is None:
+            warm = _conf_value(self.conf, "loss.geom_warmup", 15_000)
+        total = int(_conf_value(self.conf, "n_iterations", 0) or 0)
+        distill = int(_conf_value(self.conf, "post_processing.n_distillation_steps", 0) or 0)
+        return bool(train and lam > 0.0 and int(warm or 0) <= int(frame_id) < total - distill)
+
     def render(self, gaussians, gpu_batch, train=False, frame_id=0) -> dict[str, Any]:
         rays_o = gpu_batch.rays_ori
         rays_d = gpu_batch.rays_dir
         token = self._physical_tile_token(self.tracer_wrapper, gpu_batch, rays_d)
         sensor, poses = create_camera_parameters(gpu_batch)
+        sof_active = self._sof_opacity_active(train, frame_id)
         rot, scale, dens, intrinsic_dens, factor, inverse_factor = self._density_shape_inputs(
             gaussians, gpu_batch, detach=False, frame_id=frame_id)
         confidence = gaussians.positions.new_empty((0, 1))
         (features_alpha, pred_dist, hits_count, visibility, normal, depth_var, quant, extent, opacity_field, invd,
          invd2) = Tracer._Autograd.apply(
-            self.tracer_wrapper, token, frame_id, False, gaussians.n_active_features, rays_o.contiguous(),
+            self.tracer_wrapper, token, frame_id, sof_active, gaussians.n_active_features, rays_o.contiguous(),
             rays_d.contiguous(), gaussians.positions.contiguous(), rot.contiguous(), scale.contiguous(),
             dens.contiguous(), intrinsic_dens.contiguous(), factor.contiguous(), inverse_factor.contiguous(),
             gaussians.get_features().contiguous(), sensor, poses, confidence)

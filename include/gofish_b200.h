@@ -121,6 +121,8 @@ typedef struct gf_trace_inputs {
     int64_t timestamp_start;
     int64_t timestamp_end;
     const char* tile_token;     /* token of a registered physical tile mask */
+    int32_t sof_opacity_active; /* sof_exact_opacity_active: trace writes the SOF opacity field (needs
+                                   enable_normals, for the exact 0.5-crossing depth) */
 } gf_trace_inputs;
 
 /* Forward outputs (caller-allocated device buffers, initialized by the call
@@ -140,6 +142,10 @@ typedef struct gf_trace_outputs {
     float* extent;        /* [H,W,1] sum_i w_i sigma_i, sigma_i = |s_i * (R_i^T d)| of the intrinsic shape */
     float* inv_depth;     /* [H,W,1] sum_i w_i / max(d_i, 0.2) */
     float* inv_depth2;    /* [H,W,1] sum_i w_i / max(d_i, 0.2)^2 */
+    float* opacity_field; /* [H,W,1] SOF opacity field (gutRenderer.cuh:297-346): 1 - prod(1 - alpha_i) over the
+                             tile's candidates, alpha_i of the intrinsic Gaussian (rotation, scale and density of
+                             slots 4-11) on the ray up to the exact 0.5 crossing (the whole ray without one);
+                             written when sof_opacity_active */
 } gf_trace_outputs;
 
 /* Backward inputs/outputs (splatRaster.cpp:469-640). */
@@ -163,6 +169,12 @@ typedef struct gf_trace_grads {
     const float* grad_inv_depth;
     const float* inv_depth2;
     const float* grad_inv_depth2;
+    /* SOF opacity field and its gradient (gutRenderer.cuh:351-430), with the
+     * forward's quantile channel (its exact crossing depth); the gradient
+     * reaches the position, rotation, scale and intrinsic density slots. */
+    const float* quant;
+    const float* opacity_field;
+    const float* grad_opacity_field;
 } gf_trace_grads;
 
 /* Counters of the last forward pass. */

@@ -125,6 +125,8 @@ def load():
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
+        "oracle_sof_opacity_forward": (i32, [cam_p, pose_p, vp, vp, vp, vp, vp, vp, vp, vp]),
+        "oracle_sof_opacity_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_field_index_build": (vp, [i32, vp, ctypes.c_double]),
         "oracle_field_index_free": (None, [vp]),
         "oracle_field_camera_indexed": (i32, [vp, cam_p, pose_p, vp, vp, i32, vp, vp, vp]),
@@ -395,6 +397,36 @@ def sof_feeds(cam, pose, particles, ray_o, ray_d, ranges, sorted_ids, tile):
     if total < 0:
         raise RuntimeError("oracle_sof_feeds capacity")
     return [feed[offset[p]:offset[p + 1]].copy() for p in range(256)]
+
+
+def sof_opacity(cam, pose, particles, ray_o, ray_d, mask, ranges, sorted_ids, quant):
+    """SOF opacity field [H,W] (zero for invalid rays and dropped tiles) from
+    the forward's quantile channel [H,W,10]."""
+    c = lambda a, dt: np.ascontiguousarray(a, dtype=dt)  # noqa: E731
+    ids = c(sorted_ids, np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    out = np.zeros((cam.height, cam.width), np.float32)
+    load().oracle_sof_opacity_forward(ctypes.byref(cam), ctypes.byref(pose), _p(c(particles, np.float32)),
+                                      _p(c(ray_o, np.float32)), _p(c(ray_d, np.float32)), _p(c(mask, np.uint8)),
+                                      _p(c(ranges, np.uint32)), _p(ids), _p(c(quant, np.float32)), _p(out))
+    return out
+
+
+def sof_opacity_backward(cam, pose, particles, ray_o, ray_d, mask, ranges, sorted_ids, quant, opacity, grad):
+    """Gradient [N,16] of the SOF opacity field: position xyz, intrinsic
+    density | quaternion wxyz | scale xyz, 0 | 0."""
+    c = lambda a, dt: np.ascontiguousarray(a, dtype=dt)  # noqa: E731
+    particles = c(particles, np.float32)
+    ids = c(sorted_ids, np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    out = np.zeros((particles.shape[0], 16), np.float32)
+    load().oracle_sof_opacity_backward(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                                       _p(c(ray_o, np.float32)), _p(c(ray_d, np.float32)), _p(c(mask, np.uint8)),
+                                       _p(c(ranges, np.uint32)), _p(ids), _p(c(quant, np.float32)),
+                                       _p(c(opacity, np.float32)), _p(c(grad, np.float32)), _p(out))
+    return out
 
 
 def field_camera(cam, pose7, particles, ray_o, points, pixel_mask=None):

@@ -1921,6 +1921,168 @@ int oracle_project_backward(const OraclePose* pose, int N, const float* particle
     return 0;
 }
 
+// ------------------------------------------------------------------ SOF opacity field
+// gutRenderer.cuh:297-430 with gaussianParticles.cuh:496-588: the opacity of
+// the intrinsic Gaussians (slots 4-11: rotation, physical scale, peak
+// opacity) replayed over every candidate of the tile, in list order, on
+// [tmin, min(rho*, tmax)] (rho*: the exact 0.5-crossing depth of the
+// quantile channel; the whole ray without one).
+namespace sofop {
+
+struct Intrinsic {
+    float3_ mu;
+    float rho;
+    float3_ r0, r1, r2;  // rows of R^T
+    float is[3];         // 1 / s
+};
+
+Intrinsic intrinsic(const float* row) {
+    Intrinsic g;
+    g.mu = f3(row[0], row[1], row[2]);
+    g.rho = row[11];
+    const float r = row[4], x = row[5], y = row[6], z = row[7];
+    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z, rx = r * x, ry = r * y,
+                rz = r * z;
+    g.r0 = f3(1.0f - 2.0f * (yy + zz), 2.0f * (xy + rz), 2.0f * (xz - ry));
+    g.r1 = f3(2.0f * (xy - rz), 1.0f - 2.0f * (xx + zz), 2.0f * (yz + rx));
+    g.r2 = f3(2.0f * (xz + ry), 2.0f * (yz - rx), 1.0f - 2.0f * (xx + yy));
+    for (int k = 0; k < 3; ++k) g.is[k] = 1.0f / row[8 + k];
+    return g;
+}
+
+float3_ local(const Intrinsic& g, float3_ v) {
+    return f3(fdot(g.r0, v) * g.is[0], fdot(g.r1, v) * g.is[1], fdot(g.r2, v) * g.is[2]);
+}
+
+struct Sample {
+    bool accepted = false;
+    float alpha = 0.0f, response = 0.0f, depth = 0.0f;
+    float3_ p{};
+};
+
+Sample sample(const Intrinsic& g, const Ray& ray, float tmin, float tmax) {
+    Sample s;
+    if (!(tmax >= tmin)) return s;
+    const float3_ gro = local(g, sub(ray.o, g.mu));
+    const float3_ grdu = local(g, ray.d);
+    float tau;
+    if (tmax == tmin) {
+        tau = tmin;
+    } else {
+        const float denom = fdot(grdu, grdu);
+        if (!(denom > 0.0f && gf::isfinite_f(denom) && gf::isfinite_f(tmin))) return s;
+        const float tauLine = -fdot(gro, grdu) / denom;
+        tau = gf::min_f(gf::max_f(tauLine, tmin), tmax);
+    }
+    s.depth = tau;
+    s.p = f3(fmaf_rn(tau, grdu.x, gro.x), fmaf_rn(tau, grdu.y, gro.y), fmaf_rn(tau, grdu.z, gro.z));
+    const float arg = gf::max_f(fdot(s.p, s.p), 0.0f);
+    s.response = gf::gf_expf(-0.5f * arg);
+    s.alpha = gf::min_f(kMaxAlpha, s.response * g.rho);
+    s.accepted = s.response > kMinKernelResponse && s.alpha > kAlphaThreshold;
+    return s;
+}
+
+float replay_end(const float* quant, size_t pix, const Ray& ray) {
+    const float rho = quant[10 * pix + 8];
+    return (rho > 0.0f && gf::isfinite_f(rho)) ? gf::min_f(rho, ray.tmax) : ray.tmax;
+}
+
+}  // namespace sofop
+
+// opacity[P] (zero for invalid rays and pixels of dropped tiles).
+int oracle_sof_opacity_forward(const OracleCamera* cam, const OraclePose* pose, const float* particles,
+                               const float* rayO, const float* rayD, const uint8_t* mask, const uint32_t* ranges,
+                               const uint32_t* sortedIds, const float* quant, float* opacity) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
+    parallel_for(0, gx * gy, 1, [&](int tile, int) {
+        if (mask[tile] == 0u) return;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py)
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                const float end = sofop::replay_end(quant, pix, ray);
+                if (!(end >= ray.tmin)) {
+                    opacity[pix] = 0.0f;
+                    continue;
+                }
+                float product = 1.0f;
+                for (uint32_t s = ranges[2 * tile]; s < ranges[2 * tile + 1]; ++s) {
+                    const sofop::Sample smp =
+                        sofop::sample(sofop::intrinsic(particles + 32 * size_t(sortedIds[s])), ray, ray.tmin, end);
+                    if (smp.accepted) product = product * (1.0f - smp.alpha);
+                }
+                opacity[pix] = 1.0f - product;
+            }
+    });
+    return 0;
+}
+
+// Gradient of the opacity field: grad[N*16] = position xyz, intrinsic
+// density | quaternion w x y z | scale xyz, 0 | 0 (accumulated in double).
+int oracle_sof_opacity_backward(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                                const float* rayO, const float* rayD, const uint8_t* mask, const uint32_t* ranges,
+                                const uint32_t* sortedIds, const float* quant, const float* opacity,
+                                const float* gradOpacity, float* grad) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
+    std::vector<std::vector<double>> partial(static_cast<size_t>(worker_count()));
+    parallel_for(0, gx * gy, 1, [&](int tile, int worker) {
+        std::vector<double>& acc = partial[size_t(worker)];
+        if (acc.empty()) acc.assign(size_t(N) * 16, 0.0);
+        if (mask[tile] == 0u) return;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py)
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                const float end = sofop::replay_end(quant, pix, ray);
+                const float upstream = gradOpacity[pix];
+                if (!(end >= ray.tmin) || upstream == 0.0f) continue;
+                const float full = gf::min_f(gf::max_f(1.0f - opacity[pix], 0.0f), 1.0f);
+                for (uint32_t s = ranges[2 * tile]; s < ranges[2 * tile + 1]; ++s) {
+                    const uint32_t idx = sortedIds[s];
+                    const float* row = particles + 32 * size_t(idx);
+                    const sofop::Intrinsic g = sofop::intrinsic(row);
+                    const sofop::Sample smp = sofop::sample(g, ray, ray.tmin, end);
+                    if (!smp.accepted) continue;
+                    const float exclusive =
+                        gf::min_f(gf::max_f(full / gf::max_f(1.0f - smp.alpha, 1.0f - kMaxAlpha), 0.0f), 1.0f);
+                    const float dAlpha = upstream * exclusive;
+                    const float cap = smp.response * g.rho < kMaxAlpha ? 1.0f : 0.0f;
+                    const float gDensity = cap * dAlpha * smp.response;
+                    const float dArg = cap * dAlpha * g.rho * (-0.5f * smp.response);
+                    const float lpg[3] = {2.0f * dArg * smp.p.x, 2.0f * dArg * smp.p.y, 2.0f * dArg * smp.p.z};
+                    const float rpg[3] = {g.is[0] * lpg[0], g.is[1] * lpg[1], g.is[2] * lpg[2]};
+                    const float3_ w = f3(fmaf_rn(smp.depth, ray.d.x, ray.o.x) - g.mu.x,
+                                         fmaf_rn(smp.depth, ray.d.y, ray.o.y) - g.mu.y,
+                                         fmaf_rn(smp.depth, ray.d.z, ray.o.z) - g.mu.z);
+                    const float rot[3] = {fdot(g.r0, w), fdot(g.r1, w), fdot(g.r2, w)};
+                    double* a = acc.data() + 16 * size_t(idx);
+                    a[0] += -(double(g.r0.x) * rpg[0] + double(g.r1.x) * rpg[1] + double(g.r2.x) * rpg[2]);
+                    a[1] += -(double(g.r0.y) * rpg[0] + double(g.r1.y) * rpg[1] + double(g.r2.y) * rpg[2]);
+                    a[2] += -(double(g.r0.z) * rpg[0] + double(g.r1.z) * rpg[1] + double(g.r2.z) * rpg[2]);
+                    a[3] += gDensity;
+                    float gq[4];
+                    rotate_transpose_vjp(row + 4, w, f3(rpg[0], rpg[1], rpg[2]), gq);
+                    for (int k = 0; k < 4; ++k) a[4 + k] += gq[k];
+                    for (int k = 0; k < 3; ++k) a[8 + k] += -double(rot[k]) * g.is[k] * g.is[k] * lpg[k];
+                }
+            }
+    });
+    for (size_t i = 0; i < size_t(N) * 16; ++i) {
+        double v = 0.0;
+        for (const auto& part : partial)
+            if (!part.empty()) v += part[i];
+        grad[i] = float(v);
+    }
+    return 0;
+}
+
 // The SOF hierarchy's feed sequences of one tile: for local pixel p,
 // feed[offset[p] .. offset[p+1]) are the sorted positions fed to its HEAD in
 // order (offset has 257 entries).  Returns the total, or -1 when it exceeds

@@ -99,3 +99,43 @@ def test_training_entry_point_renders_the_hierarchy(cuda_device):
     loss = out["pred_features"].sum()
     loss.backward()
     assert model.positions.grad is not None and bool(torch.isfinite(model.positions.grad).all())
+
+
+def test_sof_opacity_field_matches_oracle(cuda_device):
+    """The SOF exact-crossing opacity field (gutRenderer.cuh:297-430) and its
+    gradient to the intrinsic Gaussian against the oracle."""
+    import torch
+
+    case = _dense(seed=21, size=96)
+    gpu = harness.GpuTracer(case, 16, 0, cuda_device, enable_normals=True)
+    r = gpu.raster
+    out = r.trace(0, True, case.scene.sh_degree, gpu.particles, gpu.features, gpu.ray_o, gpu.ray_d, None, gpu.sensor,
+                  0, 1, gpu.pose, gpu.pose, gpu.token)
+    field = out[8][..., 0].cpu().numpy()
+    quant = out[6].cpu().numpy()
+    pose = oracle.prepare_pose(case.pose)
+    ref = harness.oracle_forward(case, 16, 0)
+    geo = oracle.render_forward_geo(case.ocam, pose, case.particles, ref["rgb"], case.ray_o, case.ray_d, case.tmask,
+                                    ref["ranges"], ref["ids"], 16)
+    np.testing.assert_array_equal(quant.view(np.uint32), geo["quant"].view(np.uint32))
+    want = oracle.sof_opacity(case.ocam, pose, case.particles, case.ray_o, case.ray_d, case.tmask, ref["ranges"],
+                              ref["ids"], geo["quant"])
+    np.testing.assert_array_equal(field.view(np.uint32), want.view(np.uint32))
+    assert (want > 0.1).sum() > 500
+    # gradient of sum(w * O) alone
+    rng = np.random.default_rng(6)
+    w = rng.uniform(-1, 1, field.shape).astype(np.float32)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(cuda_device)  # noqa: E731
+    zeros = torch.zeros_like
+    pairs = [out[5], None, out[7], None, out[8], dev(w)[..., None], out[6], None, out[4], None, out[9], None,
+             out[10], None]
+    gp, _gs = r.trace_bwd(0, True, case.scene.sh_degree, gpu.particles, gpu.features, gpu.ray_o, gpu.ray_d, None,
+                          gpu.sensor, 0, 1, gpu.pose, gpu.pose, out[0], zeros(out[0]), out[1], zeros(out[1]), *pairs,
+                          gpu.token)
+    gp = gp.cpu().numpy()
+    ref_g = oracle.sof_opacity_backward(case.ocam, pose, case.particles, case.ray_o, case.ray_d, case.tmask,
+                                        ref["ranges"], ref["ids"], geo["quant"], want, w)
+    for got, exp in ((gp[:, 0:3], ref_g[:, 0:3]), (gp[:, 4:8], ref_g[:, 4:8]), (gp[:, 8:11], ref_g[:, 8:11]),
+                     (gp[:, 11], ref_g[:, 3])):
+        assert harness.rel_l2(got, exp) <= 1e-3
+    assert np.abs(ref_g[:, 3]).max() > 0

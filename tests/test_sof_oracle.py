@@ -77,3 +77,54 @@ def test_hierarchy_reorders_a_dense_scene():
     err_flat = np.abs(flat["rgba"] - full["rgba"]).mean()
     assert err_sof < err_flat
     np.testing.assert_allclose(sof["rgba"][..., 3], flat["rgba"][..., 3], atol=0.02)
+
+
+def _opacity_case():
+    case = _dense_case()
+    pose = oracle.prepare_pose(case.pose)
+    ref = harness.oracle_forward(case, 16, 0)
+    geo = oracle.render_forward_geo(case.ocam, pose, case.particles, ref["rgb"], case.ray_o, case.ray_d, case.tmask,
+                                    ref["ranges"], ref["ids"], 16)
+    return case, pose, ref, geo["quant"]
+
+
+def test_sof_opacity_field_bounds_and_crossings():
+    """The field lies in [0, 1); rays with a crossing replay only up to it, so
+    their field is at most the full-ray replay's."""
+    case, pose, ref, quant = _opacity_case()
+    args = (case.ocam, pose, case.particles, case.ray_o, case.ray_d, case.tmask, ref["ranges"], ref["ids"])
+    field = oracle.sof_opacity(*args, quant)
+    whole = oracle.sof_opacity(*args, np.zeros_like(quant))
+    crossing = quant[..., 8] > 0
+    assert crossing.sum() > 100 and (~crossing & (whole > 0)).sum() > 100
+    assert field.min() >= 0.0 and field.max() < 1.0
+    assert np.all(field[crossing] <= whole[crossing] + 1e-6)
+    np.testing.assert_array_equal(field[~crossing], whole[~crossing])
+
+
+def test_sof_opacity_gradient_matches_finite_differences():
+    case, pose, ref, quant = _opacity_case()
+    args = (case.ocam, pose)
+    rest = (case.ray_o, case.ray_d, case.tmask, ref["ranges"], ref["ids"], quant)
+    rng = np.random.default_rng(8)
+    weights = rng.uniform(-1, 1, (case.camera.height, case.camera.width)).astype(np.float32)
+    field = oracle.sof_opacity(*args, case.particles, *rest)
+    grad = oracle.sof_opacity_backward(*args, case.particles, *rest, field, weights)
+    # particles with the largest gradient magnitude; slots: position 0-2, intrinsic density 11, scale 8-10
+    order = np.argsort(-np.abs(grad[:, 0:4]).sum(axis=1))[:6]
+    checks = [(0, 0), (1, 1), (2, 2), (11, 3), (8, 8), (9, 9), (10, 10)]
+    for i in order:
+        for slot, gi in checks:
+            # small steps: an acceptance threshold crossed inside the step (response 0.0113, alpha 1/255)
+            # adds a jump of about 1/255 to the difference
+            h = 2e-5 * max(1.0, abs(float(case.particles[i, slot])))
+            if slot >= 8:
+                h = 2e-4 * float(case.particles[i, slot])
+            plus, minus = case.particles.copy(), case.particles.copy()
+            plus[i, slot] += h
+            minus[i, slot] -= h
+            fp = float((oracle.sof_opacity(*args, plus, *rest) * weights).astype(np.float64).sum())
+            fm = float((oracle.sof_opacity(*args, minus, *rest) * weights).astype(np.float64).sum())
+            fd = (fp - fm) / (2 * h)
+            an = float(grad[i, gi])
+            assert abs(fd - an) <= 0.05 * max(abs(fd), abs(an)) + 2e-3, (i, slot, fd, an)

@@ -126,9 +126,25 @@ def test_confidence_is_refused():
                                x["idns"], x["fac"], x["inv"], x["sph"], None, poses, torch.ones((n, 1)))
 
 
-def test_opacity_field_loss_is_refused():
-    with pytest.raises(NotImplementedError, match="lambda_opa"):
-        Tracer({"render": {"enable_normals": True}, "loss": {"lambda_opa": 0.004}})
+def test_opacity_field_loss_needs_the_geometric_channels():
+    with pytest.raises(ValueError, match="lambda_opa"):
+        Tracer({"render": {"enable_normals": False}, "loss": {"lambda_opa": 0.004}})
+
+
+def test_opacity_field_activation_follows_the_reference():
+    """tracer.py:433-448: active for training frames from opa_warmup (default
+    geom_warmup) until the distillation steps, with lambda_opa > 0."""
+    conf = {"render": {"enable_normals": True}, "loss": {"lambda_opa": 0.004, "geom_warmup": 100},
+            "n_iterations": 1000, "post_processing": {"n_distillation_steps": 200}}
+    t = Tracer(conf)
+    assert not t._sof_opacity_active(True, 99)
+    assert t._sof_opacity_active(True, 100) and t._sof_opacity_active(True, 799)
+    assert not t._sof_opacity_active(True, 800)
+    assert not t._sof_opacity_active(False, 500)
+    conf["loss"]["opa_warmup"] = 10
+    assert Tracer(conf)._sof_opacity_active(True, 10)
+    conf["loss"]["lambda_opa"] = 0.0
+    assert not Tracer(conf)._sof_opacity_active(True, 500)
 
 
 @pytest.mark.parametrize("loss", ["lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_extent",

@@ -165,9 +165,9 @@ def test_gradients_match_the_oracle_chain(view, cuda_device, geometry):
         assert harness.rel_l2(got.cpu().numpy(), w) <= 1e-3, name
 
 
-def test_opacity_field_loss_is_refused():
-    with pytest.raises(NotImplementedError, match="lambda_opa"):
-        Tracer({"render": {"enable_normals": True}, "loss": {"lambda_opa": 0.004}})
+def test_opacity_field_loss_needs_the_geometric_channels():
+    with pytest.raises(ValueError, match="lambda_opa"):
+        Tracer({"render": {"enable_normals": False}, "loss": {"lambda_opa": 0.004}})
 
 
 def test_shape_failure_is_raised_by_render(view, cuda_device):

@@ -50,6 +50,7 @@ class GfTracerConfig(ctypes.Structure):
         ("enable_normals", ctypes.c_int32),
         ("intersection_capacity", ctypes.c_int32),
         ("compositor", ctypes.c_int32),
+        ("complete_admission", ctypes.c_int32),
     ]
 
 

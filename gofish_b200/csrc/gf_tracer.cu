@@ -380,7 +380,8 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     if (int e = t->ranges.ensure(sizeof(uint2) * size_t(T), stream)) return e;
 
     gf::FallbackArgs fa{};
-    fa.enabled = t->cfg.admission_fallback == GF_FALLBACK_CONE ? 1 : 0;
+    fa.complete = t->cfg.complete_admission != 0 ? 1 : 0;
+    fa.enabled = (t->cfg.admission_fallback == GF_FALLBACK_CONE || fa.complete) ? 1 : 0;
     if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
     if (int e = t->bigCount.ensure(sizeof(uint32_t) * 4, stream)) return e;

@@ -638,6 +638,7 @@ struct FallbackArgs {
     uint32_t* wide;     // projected particles whose tile box exceeds kWideTiles, left to k_wide
     uint32_t* wideCount;
     const uint32_t* overflow;  // non-zero: the intersections exceed the key capacity, emit nothing (may be NULL)
+    int complete;              // every particle takes the cone route (complete admission)
 };
 
 __device__ __forceinline__ bool skip_emit(const FallbackArgs& fa) {
@@ -709,11 +710,13 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
     rec[2] = make_float4(r6.y, r6.z, r6.w, r7.x);
     rec[3] = make_float4(r7.y, rgb[0], rgb[1], rgb[2]);
 
+    // complete admission: every particle takes the cone route, none its footprint
+    const bool footprint = !fa.complete && fast_ut_valid(p);
     bool wide = false;
-    if (fast_ut_valid(p)) wide = wide_box(tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey));
-    const uint32_t n = wide ? 0u : for_admitted_tiles(f, mask, p, [](int, int, uint32_t) {});
+    if (footprint) wide = wide_box(tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey));
+    const uint32_t n = (wide || !footprint) ? 0u : for_admitted_tiles(f, mask, p, [](int, int, uint32_t) {});
     bool deferred = false;
-    if (!fast_ut_valid(p)) {
+    if (!footprint) {
         // Without a valid projection: the cone fallback, left to the warp
         // kernel once the cap meets the root cone.
         fb::Cap c{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, fb::kNone};
@@ -897,7 +900,7 @@ __global__ __launch_bounds__(256) void k_emit(FrameArgs f, const float4* __restr
     Projected p;
     p.cx = p0.x; p.cy = p0.y; p.conic0 = p0.z; p.conic1 = p0.w;
     p.conic2 = p1.x; p.opacity = p1.y; p.ex = p1.z; p.ey = p1.w;
-    if (!fast_ut_valid(p)) return;  // cone-fallback particles: k_fallback_big<true>
+    if (fa.complete || !fast_ut_valid(p)) return;  // cone-route particles: k_fallback_big<true>
     if (wide_box(tile_bbox(f.gx, f.gy, p.cx, p.cy, p.ex, p.ey))) return;  // k_wide<true>
     const float4 a = records[4 * size_t(i)], b = records[4 * size_t(i) + 1], c = records[4 * size_t(i) + 2],
                  d = records[4 * size_t(i) + 3];

@@ -82,6 +82,8 @@ class SplatRaster:
                              or int(_select(conf, "render.splat.tail_size", 64)) != 64):
             raise ValueError("SOF's hierarchy uses HEAD4, MID8 and TAIL64")
         cfg.compositor = _native.GF_COMPOSITOR_SOF if hierarchical else _native.GF_COMPOSITOR_KBUFFER
+        # every particle admitted by the conservative cone test (complete: no pixel's hit is missed)
+        cfg.complete_admission = 1 if bool(_select(conf, "render.gofish.complete_admission", False)) else 0
         handle = self._lib.gf_tracer_create(ctypes.byref(cfg))
         if not handle:
             raise _native.NativeError("gf_tracer_create failed: " + self._lib.gf_last_error().decode())

@@ -78,6 +78,10 @@ typedef struct gf_tracer_config {
                                        (gf_trace_outputs.normal ... inv_depth2) and their gradients */
     int32_t intersection_capacity;  /* GF_CAPACITY_*: how the tile-intersection keys are sized */
     int32_t compositor;             /* GF_COMPOSITOR_*: render.splat.hierarchical_sort */
+    int32_t complete_admission;     /* render.gofish.complete_admission: 1 admits every particle (density >= 1/255)
+                                       by the conservative cone test of its support sphere, whose tiles hold every
+                                       pixel its hit test can pass on; 0 admits particles with a valid unscented
+                                       projection by their footprint (admission_fallback for the others) */
 } gf_tracer_config;
 
 /* Compositing order of a pixel's hits.  KBUFFER: the tile's depth-sorted

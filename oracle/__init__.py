@@ -124,6 +124,8 @@ def load():
                                        vp]),
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
+        "oracle_set_complete_admission": (None, [i32]),
+        "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
         "oracle_sof_opacity_forward": (i32, [cam_p, pose_p, vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_sof_opacity_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
@@ -353,15 +355,54 @@ def project_backward(pose, particles, sh, sh_degree, counts, grad_record):
     return gp, gs
 
 
-def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None, fallback=True):
+class complete_admission:
+    """Context in which project / bin admit every particle (density >= 1/255)
+    by the conservative cone test of its support sphere (the tracer's
+    render.gofish.complete_admission)."""
+
+    def __init__(self, on: bool = True):
+        self.on = bool(on)
+
+    def __enter__(self):
+        load().oracle_set_complete_admission(1 if self.on else 0)
+
+    def __exit__(self, *exc):
+        load().oracle_set_complete_admission(0)
+        return False
+
+
+def admission_misses(cam, pose, particles, ray_o, ray_d, mask, ranges, sorted_ids, max_misses=64):
+    """(count, [(pixel, particle)...]) of brute-force hits on valid rays of
+    retained tiles whose particle is missing from the tile's candidate list."""
+    lib = load()
+    ids = np.ascontiguousarray(sorted_ids, dtype=np.uint32)
+    if ids.size == 0:
+        ids = np.zeros(1, dtype=np.uint32)
+    pix = np.zeros(max_misses, np.int64)
+    part = np.zeros(max_misses, np.uint32)
+    particles = np.ascontiguousarray(particles, dtype=np.float32)
+    n = lib.oracle_admission_misses(ctypes.byref(cam), ctypes.byref(pose), particles.shape[0], _p(particles),
+                                    _p(np.ascontiguousarray(ray_o, dtype=np.float32)),
+                                    _p(np.ascontiguousarray(ray_d, dtype=np.float32)),
+                                    _p(np.ascontiguousarray(mask, dtype=np.uint8)),
+                                    _p(np.ascontiguousarray(ranges, dtype=np.uint32)), _p(ids), max_misses, _p(pix),
+                                    _p(part))
+    k = min(int(n), max_misses)
+    return int(n), list(zip(pix[:k].tolist(), part[:k].tolist()))
+
+
+def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None, fallback=True,
+          complete=False):
     """Full forward pass; returns a dict of every intermediate and output.
     ``fallback`` admits particles without a valid projection by the cone test
-    (render.gofish.fast_admission_fallback = "cone")."""
+    (render.gofish.fast_admission_fallback = "cone"); ``complete`` admits every
+    particle that way (render.gofish.complete_admission)."""
     pose = prepare_pose(pose7)
-    rd = ray_d if fallback else None
-    proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask, rd)
-    tr = tile_rays(cam, pose, ray_o, ray_d)
-    keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode, rd)
+    rd = ray_d if (fallback or complete) else None
+    with complete_admission(complete):
+        proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask, rd)
+        tr = tile_rays(cam, pose, ray_o, ray_d)
+        keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode, rd)
     rgba, hit_t, count = render_forward(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, ids, k, tiles)
     vis = (counts > 0).astype(np.uint32)
     return dict(pose=pose, proj=proj, rgb=rgb, counts=counts, tile_rays=tr, keys=keys, ids=ids, ranges=ranges,

@@ -115,6 +115,11 @@ void parallel_for(int begin, int end, int chunk, Fn&& fn) {
     body(0);
     for (auto& t : pool) t.join();
 }
+// Complete admission (oracle_set_complete_admission): every particle of
+// density >= 1/255 is admitted by the conservative cone test of its support
+// sphere, none by its projected footprint.
+bool g_completeAdmission = false;
+
 // Optional explicit tile list of the render entry points (oracle_set_tile_list):
 // when one is set they visit its tiles instead of the range [tileBegin, tileEnd).
 const int* g_tileList = nullptr;
@@ -131,6 +136,9 @@ void parallel_tiles(int tileBegin, int tileEnd, Fn&& fn) {
 }  // namespace
 
 extern "C" {
+
+// Selects (1) or clears (0) complete admission for oracle_project / oracle_bin.
+void oracle_set_complete_admission(int complete) { g_completeAdmission = complete != 0; }
 
 // Sets (tiles != NULL) or clears the tile list of the render entry points;
 // the caller keeps the list alive until it is cleared.
@@ -1345,8 +1353,8 @@ int oracle_project(const OracleCamera* cam, const OraclePose* pose, int N, const
             const float v = acc + 0.5f;
             rgb[3 * size_t(i) + ch] = gf::max_f(v, 0.0f);
         }
-        counts[i] = admitted_tiles(gx, gy, mask, pr, [](int, int) {});
-        if (rayD != nullptr && !fast_ut_valid(pr) && P.density >= kAlphaThreshold)
+        counts[i] = g_completeAdmission ? 0u : admitted_tiles(gx, gy, mask, pr, [](int, int) {});
+        if (rayD != nullptr && (g_completeAdmission || !fast_ut_valid(pr)) && P.density >= kAlphaThreshold)
             counts[i] = fallback::tiles(tree, mask, fallback::cap_of(P, *pose), [](int, int) {});
     });
     return 0;
@@ -1463,8 +1471,8 @@ int64_t oracle_bin(const OracleCamera* cam, const OraclePose* pose, int N, const
             }
             ++k;
         };
-        admitted_tiles(gx, gy, mask, pr, emit);
-        if (rayD != nullptr && !fast_ut_valid(pr) && P.density >= kAlphaThreshold)
+        if (!g_completeAdmission) admitted_tiles(gx, gy, mask, pr, emit);
+        if (rayD != nullptr && (g_completeAdmission || !fast_ut_valid(pr)) && P.density >= kAlphaThreshold)
             fallback::tiles(tree, mask, fallback::cap_of(P, *pose), emit);
     });
     // Stable sort of (key, id) pairs by key.
@@ -2081,6 +2089,45 @@ int oracle_sof_opacity_backward(const OracleCamera* cam, const OraclePose* pose,
         grad[i] = float(v);
     }
     return 0;
+}
+
+// Completeness of a binning: for every valid ray of a retained tile, the
+// particles whose hit test passes on that ray (by brute force over all N)
+// but that are not in the tile's candidate list.  Returns their number; the
+// first misses go to missPixel / missParticle (up to maxMisses).
+int64_t oracle_admission_misses(const OracleCamera* cam, const OraclePose* pose, int N, const float* particles,
+                                const float* rayO, const float* rayD, const uint8_t* mask, const uint32_t* ranges,
+                                const uint32_t* sortedIds, int64_t maxMisses, int64_t* missPixel,
+                                uint32_t* missParticle) {
+    const int W = cam->width, H = cam->height;
+    const int gx = (W + kTile - 1) / kTile, gy = (H + kTile - 1) / kTile;
+    std::atomic<int64_t> misses(0);
+    parallel_for(0, gx * gy, 1, [&](int tile, int) {
+        if (mask[tile] == 0u) return;
+        std::vector<uint8_t> listed(size_t(N), 0u);
+        for (uint32_t s = ranges[2 * tile]; s < ranges[2 * tile + 1]; ++s) listed[sortedIds[s]] = 1u;
+        const int tx = tile % gx, ty = tile / gx;
+        for (int py = ty * kTile; py < std::min(H, (ty + 1) * kTile); ++py)
+            for (int px = tx * kTile; px < std::min(W, (tx + 1) * kTile); ++px) {
+                const size_t pix = size_t(px) + size_t(W) * py;
+                const Ray ray = make_ray(*pose, rayO + 3 * pix, rayD + 3 * pix);
+                if (!ray.valid) continue;
+                for (int i = 0; i < N; ++i) {
+                    if (listed[size_t(i)]) continue;
+                    const Particle P = load_particle(particles + 32 * size_t(i));
+                    float alpha, hitT, resp;
+                    HalfRay hr;
+                    if (hit_test(ray, P, alpha, hitT, resp, hr) && hitT >= ray.tmin && hitT <= ray.tmax) {
+                        const int64_t k = misses.fetch_add(1);
+                        if (k < maxMisses) {
+                            missPixel[k] = int64_t(pix);
+                            missParticle[k] = uint32_t(i);
+                        }
+                    }
+                }
+            }
+    });
+    return misses.load();
 }
 
 // The SOF hierarchy's feed sequences of one tile: for local pixel p,

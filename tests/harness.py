@@ -67,9 +67,9 @@ def small_case(seed: int = 7, n: int = 20_000, size: int = 256, sh_degree: int =
     return make_case(scene, cam, pose)
 
 
-def oracle_forward(case: Case, k: int, key_mode: int, tiles=None, fallback: bool = True):
+def oracle_forward(case: Case, k: int, key_mode: int, tiles=None, fallback: bool = True, complete: bool = False):
     return oracle.trace(case.ocam, case.pose, case.particles, case.features, case.scene.sh_degree, case.ray_o,
-                        case.ray_d, case.tmask, k, key_mode, tiles, fallback)
+                        case.ray_d, case.tmask, k, key_mode, tiles, fallback, complete)
 
 
 def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
@@ -81,7 +81,7 @@ class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
     def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0,
-                 enable_normals: bool = False):
+                 enable_normals: bool = False, complete: bool = False):
         """k: k-buffer size, or oracle.SOF_HIERARCHY for SOF's hierarchy."""
         import torch
 
@@ -94,7 +94,8 @@ class GpuTracer:
         conf = {"render": {"splat": {"k_buffer_size": 16 if sof else k, "composite_log_capacity": log_capacity,
                                      "hierarchical_sort": sof},
                            "gofish": {"fast_global_depth_key": key_mode == 1,
-                                      "fast_admission_fallback": "cone" if fallback else "none"},
+                                      "fast_admission_fallback": "cone" if fallback else "none",
+                                      "complete_admission": complete},
                            "enable_hitcounts": True, "enable_normals": enable_normals}}
         self.raster = SplatRaster(conf)
         self.token = "test-token"
@@ -122,6 +123,11 @@ class GpuTracer:
                            out[4:]):
             res[name] = t.cpu().numpy()
         return res
+
+    def backward_after_forward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray):
+        """forward() then backward()."""
+        self.forward()
+        return self.backward(grad_rgba, grad_hit)
 
     def backward(self, grad_rgba: np.ndarray, grad_hit: np.ndarray, geometry: dict | None = None):
         """geometry: output gradients of the geometric channels by name (normal,

@@ -275,12 +275,13 @@ def run_gpu(args):
 
     def input_set():
         """A model, its gradient bucket (the [N,59] gradients in one buffer;
-        the SH part, 48 floats per Gaussian, is all-reduced as soon as the
-        last view's render backward has produced it, overlapping the
-        full-shape VJP; the rest after), a target and a loss accumulator."""
+        the SH and position parts, 51 floats per Gaussian, are all-reduced as
+        soon as the last view's render backward has produced them,
+        overlapping the full-shape VJP; the rotation, scale and opacity after),
+        a target and a loss accumulator."""
         model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in param_keys), scene.sh_degree)
         params = model.parameters()
-        bucket = GradientBucket(params, early=[model.features]) if world > 1 else None
+        bucket = GradientBucket(params, early=[model.positions, model.features]) if world > 1 else None
         return SimpleNamespace(model=model, params=params, bucket=bucket, target=target_host.to(device),
                                loss=torch.zeros((), device=device))
 

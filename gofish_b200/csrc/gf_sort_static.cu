@@ -1,10 +1,10 @@
 // Tile-key sort that allocates no device memory.
 //
 // Some callers of this library cannot allocate device memory while they
-// render: code that runs between the begin and end of a CUDA stream capture
-// (cudaMalloc is not allowed there), renderers embedded in a host application
-// that hands the library a fixed device budget and forbids allocation on its
-// frame path, and allocator-less tools that only pass preallocated buffers.
+// render: renderers embedded in a host application that hands the library a
+// fixed device budget and forbids allocation on its frame path, real-time
+// loops in which a cudaMalloc (which can synchronize the device) would stall
+// a frame, and allocator-less tools that only pass preallocated buffers.
 // gf_sort_tile_keys_static gives them the tracer's (tile | depth) key sort
 // with all of its scratch in one file-scope device array of fixed size.
 //
@@ -13,7 +13,9 @@
 // GPU that loads the library holds it until the process exits.  Host code
 // cannot use the array's name as a device address, so the first call on each
 // device looks the address up with cudaGetSymbolAddress while that device is
-// current; make that first call before any stream capture.  Every call on a
+// current; make that first call before any stream capture.  The address is
+// kept for the life of the process, so cudaDeviceReset is not supported while
+// the library is loaded (the array would move).  Every call on a
 // device shares the one array: calls whose GPU work overlaps (on different
 // streams, or from different threads) race on it and must be serialized by
 // the caller.  Nothing in the array needs to start at zero: each pass
@@ -70,8 +72,11 @@ extern "C" int gf_sort_tile_keys_static(const uint64_t* keys_in, const uint32_t*
         return gf_record_error(GF_ERR_BAD_INPUT, "gf_sort_tile_keys_static: NULL buffer");
     if (n > 0 && (static_cast<const void*>(keys_in) == keys_out || static_cast<const void*>(ids_in) == ids_out))
         return gf_record_error(GF_ERR_BAD_INPUT, "gf_sort_tile_keys_static: inputs must not alias the outputs");
+    // an error left by earlier work is reported as such, not as this sort's launch failure
+    cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) return fail_cuda("a CUDA call made before this sort", e);
     int device = -1;
-    cudaError_t e = cudaGetDevice(&device);
+    e = cudaGetDevice(&device);
     if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
     if (device < 0 || device >= kMaxDevices) return gf_record_error(GF_ERR_STATE, "gf_sort_tile_keys_static: device index out of range");
     StaticSortScratch* scratch = nullptr;

@@ -40,7 +40,12 @@ class GradientBucket:
     step, the accumulation of the last of them starts an asynchronous
     all-reduce of that tail, which overlaps the rest of the backward;
     ``allreduce()`` then reduces the head and orders the stream after both.
-    Every rank must arm before the same backward."""
+    Every rank must arm before the same backward.  An early parameter must
+    receive exactly one gradient in the armed backward (one producer): the
+    all-reduce starts at its first accumulation, so a second contribution
+    would arrive after the reduction had read the buffer.  For the tracer
+    the SH coefficients and the positions qualify: both come only out of the
+    render's backward (the per-view footprint reads the positions detached)."""
 
     def __init__(self, params: Sequence[torch.Tensor], early: Sequence[torch.Tensor] = ()):
         params = list(params)

@@ -277,15 +277,18 @@ int gf_tracer_copy_intermediates(const gf_tracer* tracer, float* projected, floa
 /* Stable sort of (tile << 32 | depth bits) keys and their particle ids by the
  * key bits [0, end_bit), the same order as the sort inside gf_tracer_trace.
  * No counterpart in the reference: it exists for callers that cannot allocate
- * device memory while they render -- code running inside a CUDA stream
- * capture (where cudaMalloc is not allowed), hosts that give the library a
- * fixed device budget and forbid allocation on the frame path, tools that only
- * pass preallocated buffers.  It allocates nothing: its scratch is a fixed
+ * device memory while they render -- hosts that give the library a fixed
+ * device budget and forbid allocation on the frame path, real-time loops in
+ * which a cudaMalloc (which can synchronize the device) would stall a frame,
+ * tools that only pass preallocated buffers.  It allocates nothing: its scratch is a fixed
  * file-scope device array sized for GF_STATIC_SORT_MAX_PAIRS pairs (about
  * 3.1 MiB, held by every GPU that loads the library until exit).  Larger
  * inputs are rejected with GF_ERR_CAPACITY.  The first call on a device
  * resolves the array's device address and must come before any stream
- * capture.  All calls on a device share the array: calls whose GPU work
+ * capture; the address is kept for the life of the process, so
+ * cudaDeviceReset is not supported while the library is loaded.  A CUDA error
+ * left by earlier work is returned as GF_ERR_CUDA before anything is launched.
+ * All calls on a device share the array: calls whose GPU work
  * overlaps race and must be serialized by the caller.  Inputs are read only
  * and must not alias the outputs. */
 int gf_sort_tile_keys_static(const uint64_t* keys_in, const uint32_t* ids_in, uint64_t* keys_out, uint32_t* ids_out,

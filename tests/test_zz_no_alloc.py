@@ -1,6 +1,6 @@
 """gf_sort_tile_keys_static: the tile-key sort for callers that cannot allocate
-device memory while they render (inside a CUDA stream capture, or under a host
-that forbids allocation on its frame path).  It must return exactly the order
+device memory while they render (under a host that gives the library a fixed
+device budget and forbids allocation on its frame path).  It must return exactly the order
 of the sort inside gf_tracer_trace, using only its fixed static scratch.
 
 Collected last on purpose: a failure here leaves every other test already run.
@@ -67,3 +67,37 @@ def test_static_sort_rejects_more_pairs_than_its_scratch(cuda_device):
     code = lib.gf_sort_tile_keys_static(None, None, None, None, _native.STATIC_SORT_MAX_PAIRS + 1, 46, None)
     assert code == -5  # GF_ERR_CAPACITY
     assert b"exceed the fixed scratch" in lib.gf_last_error()
+
+
+def test_static_sort_at_its_limits(cuda_device):
+    """MAX_PAIRS random keys (the whole histogram table, the grand total in its
+    last slot) against a stable argsort; n = 0 and end_bit = 0 (nothing to
+    sort: the pairs are copied)."""
+    import torch
+
+    from gofish_b200 import _native
+
+    lib = _native.load()
+    n = _native.STATIC_SORT_MAX_PAIRS
+    rng = np.random.default_rng(17)
+    keys = ((rng.integers(0, 4096, n, dtype=np.uint64) << np.uint64(32))
+            | rng.integers(0, 1 << 20, n, dtype=np.uint64))  # repeated keys: stability matters
+    ids = np.arange(n, dtype=np.uint32)
+    order = np.argsort(keys, kind="stable")
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    k_in = torch.from_numpy(keys.view(np.int64)).to(cuda_device)
+    i_in = torch.from_numpy(ids.view(np.int32)).to(cuda_device)
+    k_out = torch.empty_like(k_in)
+    i_out = torch.empty_like(i_in)
+    assert lib.gf_sort_tile_keys_static(k_in.data_ptr(), i_in.data_ptr(), k_out.data_ptr(), i_out.data_ptr(), n, 44,
+                                        stream) == 0, lib.gf_last_error()
+    torch.cuda.synchronize(cuda_device)
+    np.testing.assert_array_equal(k_out.cpu().numpy().view(np.uint64), keys[order])
+    np.testing.assert_array_equal(i_out.cpu().numpy().view(np.uint32), ids[order])
+    # end_bit 0: the pairs are copied in input order
+    assert lib.gf_sort_tile_keys_static(k_in.data_ptr(), i_in.data_ptr(), k_out.data_ptr(), i_out.data_ptr(), 1000, 0,
+                                        stream) == 0, lib.gf_last_error()
+    torch.cuda.synchronize(cuda_device)
+    np.testing.assert_array_equal(k_out.cpu().numpy()[:1000].view(np.uint64), keys[:1000])
+    # n = 0: nothing is touched
+    assert lib.gf_sort_tile_keys_static(None, None, None, None, 0, 44, stream) == 0, lib.gf_last_error()

@@ -858,7 +858,10 @@ def inference_config(w, args, world: int) -> dict:
     cam = w.camera
     return {
         "workload": w.name, "gaussians": w.scene.num, "large_gaussians": int(len(w.big_rows)),
-        "large_gaussian_sigma_m": [0.05, 0.2], "sh_degree": w.scene.sh_degree,
+        "large_gaussian_sigma_m": [0.05, 0.2],
+        "variant": "C4 with sigma_big reduced x10 (0.05-0.2 m, not 0.5-2 m: a camera inside most support spheres "
+                   "bins ~6e9 intersections per frame in any tile renderer)",
+        "sh_degree": w.scene.sh_degree,
         "camera": f"OPENCV_FISHEYE equisolid (KB 4-term Taylor) 205deg {cam.width}x{cam.height}",
         "k_buffer": w.k_buffer, "frames": len(w.poses), "frames_per_step": world, "orbit": "2 m ring, outward",
         "shape": args.shape, "pixel_footprint_variance": INF_GAMMA,

@@ -117,6 +117,37 @@ def workload_config(w, args, world: int, views_per_rank: int = 1) -> dict:
     }
 
 
+def exchange_timing(bucket, events, device, repeats: int = 10) -> dict:
+    """The gradient exchange of the timed steps: the compute stream's wait in
+    the bucket's all-reduce per step (the part the full-shape VJP did not
+    hide; max over ranks), and the same [N,59] all-reduce timed alone
+    (mean of ``repeats`` after 3 warm-up, max over ranks), with its bus
+    bandwidth 2 (n-1)/n * bytes / time."""
+    import torch
+    import torch.distributed as dist
+
+    exposed = sum(a.elapsed_time(b) for a, b in events) / max(1, len(events))
+    scratch = torch.zeros_like(bucket.flat)
+    for _ in range(3):
+        dist.all_reduce(scratch)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(repeats):
+        dist.all_reduce(scratch)
+    b.record()
+    torch.cuda.synchronize(device)
+    both = torch.tensor([exposed, a.elapsed_time(b) / repeats], device=device, dtype=torch.float64)
+    dist.all_reduce(both, op=dist.ReduceOp.MAX)
+    exposed, alone = (float(x) for x in both.tolist())
+    n = dist.get_world_size()
+    nbytes = bucket.flat.numel() * bucket.flat.element_size()
+    return {"bytes": int(nbytes), "early_bytes": int((bucket.flat.numel() - bucket.head_numel) * 4),
+            "exposed_ms_per_step": round(exposed, 4), "allreduce_alone_ms": round(alone, 4),
+            "allreduce_alone_bus_gbs": round(2.0 * (n - 1) / n * nbytes / (alone / 1000.0) / 1e9, 1)}
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -301,6 +332,8 @@ def run_gpu(args):
     scale = 1.0 / (3.0 * n_valid)
 
     host_times = {"render": 0.0, "backward": 0.0}
+    exchange_events = []  # (before, after) the bucket's all-reduce wait, per timed step
+    timing_exchange = [False]
 
     def step(s, want_loss=False):
         """Forward, L1 loss and backward of every local view of input set s
@@ -326,7 +359,14 @@ def run_gpu(args):
             if want_loss:
                 s.loss.add_(loss.detach())
         if s.bucket is not None:
-            s.bucket.allreduce()
+            if timing_exchange[0]:
+                pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                pair[0].record()
+                s.bucket.allreduce()
+                pair[1].record()
+                exchange_events.append(pair)
+            else:
+                s.bucket.allreduce()
         return s.loss if want_loss else None
 
     for _ in range(args.warmup):
@@ -350,9 +390,11 @@ def run_gpu(args):
     t0.record(stream)
     host_times["render"] = host_times["backward"] = 0.0
     host_start = time.perf_counter()
+    timing_exchange[0] = world > 1
     for _ in range(args.steps):
         step(resident)
     t1.record(stream)
+    timing_exchange[0] = False
     host_enqueue_s = time.perf_counter() - host_start
     host_split = dict(host_times)
     torch.cuda.synchronize(device)
@@ -382,6 +424,7 @@ def run_gpu(args):
     pixels = cam.width * cam.height
     views_per_rank = len(poses)
     value = world * views_per_rank * pixels * args.steps / (elapsed_ms / 1000.0) / 1e6
+    exchange = exchange_timing(resident.bucket, exchange_events, device) if world > 1 else None
 
     # --- end to end through the public API with host buffers
     e2e = None
@@ -475,6 +518,8 @@ def run_gpu(args):
         "fallback_particles_per_view": fallback_per_view,
         "log_overflow_tiles_last_view": log_overflow,
     }
+    if exchange is not None:
+        result["exchange"] = exchange
     if clock_info is not None:
         result["clocks"] = clock_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

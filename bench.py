@@ -60,6 +60,13 @@ def parse_args():
     p.add_argument("--size", type=int, default=None, help="override the raster size")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--exchange", choices=["overlap", "after"], default="overlap",
+                   help="N>1 training: all-reduce the SH and position gradients while the full-shape VJP runs "
+                        "(overlap), or the whole [N,59] bucket in one all-reduce after the backward (after)")
+    p.add_argument("--nccl-stream-priority", choices=["normal", "high"], default="normal",
+                   help="N>1: priority of the process group's NCCL streams")
+    p.add_argument("--no-mesh-query", action="store_true",
+                   help="single GPU, training workloads: skip the mesh opacity query sub-measurement")
     return p.parse_args()
 
 
@@ -111,9 +118,11 @@ def workload_config(w, args, world: int, views_per_rank: int = 1) -> dict:
         "entry_point": "Tracer.render (per-view full shape, trace, trace_bwd, full-shape VJP)",
         "pixel_footprint_variance": BENCH_GAMMA,
         "l2_policy": "inputs larger than L2 (model 236 B/Gaussian + packed rows + rays > 126 MB)",
-        "parallelism": (f"dp{world} (views sharded, NCCL all-reduce of the [N,59] model gradients, the SH part "
-                        "overlapping the full-shape VJP)" if world > 1
-                        else "single GPU"),
+        "parallelism": (f"dp{world} (views sharded, NCCL all-reduce of the [N,59] model gradients, "
+                        + ("the SH and position part overlapping the full-shape VJP"
+                           if args.exchange == "overlap" else "one all-reduce after the backward")
+                        + (", high-priority NCCL streams" if args.nccl_stream_priority == "high" else "") + ")"
+                        if world > 1 else "single GPU"),
     }
 
 
@@ -287,7 +296,12 @@ def run_gpu(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        pg_options = None
+        if args.nccl_stream_priority == "high":
+            pg_options = dist.ProcessGroupNCCL.Options()
+            pg_options.is_high_priority_stream = True
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device,
+                                pg_options=pg_options)
     clocks = ClockSampler(local)
     clocks.start()
 
@@ -312,7 +326,8 @@ def run_gpu(args):
         a target and a loss accumulator."""
         model = SceneGaussians(*(host[k].to(device).requires_grad_(True) for k in param_keys), scene.sh_degree)
         params = model.parameters()
-        bucket = GradientBucket(params, early=[model.positions, model.features]) if world > 1 else None
+        early = [model.positions, model.features] if args.exchange == "overlap" else []
+        bucket = GradientBucket(params, early=early) if world > 1 else None
         return SimpleNamespace(model=model, params=params, bucket=bucket, target=target_host.to(device),
                                loss=torch.zeros((), device=device))
 
@@ -524,6 +539,18 @@ def run_gpu(args):
         result["clocks"] = clock_info
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(w, poses[0], ray_o_np, ray_d_np, valid_np, budget_s=20.0)
+    if world == 1 and not args.no_mesh_query and args.workload in ("single_view", "multi_view"):
+        # The second metric of the benchmark: the mesh opacity query (3M
+        # Gaussians, 27M sites, 32 views) on this GPU, 2 timed field passes.
+        mesh_args = argparse.Namespace(**{**vars(args), "num_gaussians": None, "size": None, "views": None})
+        mesh_clocks = ClockSampler(local)
+        mesh_clocks.start()
+        try:
+            result["mesh_query"] = measure_mesh(mesh_args, rank, world, device, steps=2, warmup=1, clocks=mesh_clocks,
+                                                e2e=not args.no_e2e, cpu=not args.no_cpu_baseline)
+        except Exception as exc:  # one GPU, no collective in flight: report and keep the main line
+            mesh_clocks.stop()
+            result["mesh_query"] = {"error": f"{type(exc).__name__}: {exc}"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -545,11 +572,14 @@ FIELD_BYTES_PER_POINT = 4 + 16 + 8 + 2
 FIELD_TRAFFIC_PER_ALG_BYTE = 67.37 / 136.68
 
 
-def mesh_workload(args):
+def mesh_workload(args, device=None):
+    """The mesh query's scene, effective shape, sites (on the GPU when
+    ``device`` is given: gf_mesh_sites, bit-equal to the host generator) and
+    its 32 cameras (one shared ray table)."""
     from gofish_b200 import scene as sc
     from gofish_b200.mesh.cameras import fisheye_training_camera
     from gofish_b200.mesh.shape import effective_shape
-    from gofish_b200.mesh.sites import generate_sites
+    from gofish_b200.mesh.sites import generate_sites, generate_sites_cuda
 
     kw = {}
     if args.num_gaussians:
@@ -560,8 +590,12 @@ def mesh_workload(args):
         kw["views"] = args.views
     w = sc.workload_mesh_query(**kw)
     shape = effective_shape(w.scene.positions, w.scene.scales, w.scene.rotations, w.scene.density)
-    points = generate_sites(shape).points
-    cameras = [fisheye_training_camera(v, w.camera, pose, masked=True) for v, pose in enumerate(w.poses)]
+    if device is None:
+        points = generate_sites(shape).points
+    else:
+        points = np.ascontiguousarray(generate_sites_cuda(shape, device).points.cpu().numpy())
+    rays = w.camera.rays()
+    cameras = [fisheye_training_camera(v, w.camera, pose, masked=True, rays=rays) for v, pose in enumerate(w.poses)]
     return w, shape, points, cameras
 
 
@@ -580,11 +614,6 @@ def run_mesh(args):
     import torch
     import torch.distributed as dist
 
-    from gofish_b200.mesh import SplatRaster
-    from gofish_b200.mesh.bisection import refine_crossings
-    from gofish_b200.mesh.field import camera_inputs, evaluate_field, signed_field
-    from gofish_b200.mesh.sharded import gather_shards_tensor, shard_bounds
-
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -594,8 +623,30 @@ def run_mesh(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     clocks = ClockSampler(local)
     clocks.start()
+    result = measure_mesh(args, rank, world, device, args.steps, args.warmup, clocks,
+                          e2e=not args.no_e2e, cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
 
-    w, shape, points_all, cameras = mesh_workload(args)
+
+def measure_mesh(args, rank: int, world: int, device, steps: int, warmup: int, clocks=None, e2e: bool = True,
+                 cpu: bool = False) -> dict:
+    """The mesh opacity query on this rank's shard of the sites: ``steps``
+    timed field passes (max over ranks), its roofline, optionally the end to
+    end pass through evaluate_field, the bisection of ``args.edges`` edges and
+    the oracle's CPU rate."""
+    import torch
+    import torch.distributed as dist
+
+    from gofish_b200.mesh import SplatRaster
+    from gofish_b200.mesh.bisection import refine_crossings
+    from gofish_b200.mesh.field import camera_inputs, evaluate_field, signed_field
+    from gofish_b200.mesh.sharded import gather_shards_tensor, shard_bounds
+
+    w, shape, points_all, cameras = mesh_workload(args, device)
     q_total = points_all.shape[0]
     lo, hi = shard_bounds(q_total, rank, world)
     points = np.ascontiguousarray(points_all[lo:hi])
@@ -620,7 +671,7 @@ def run_mesh(args):
             out = (gather_shards_tensor(out[0], q_total), gather_shards_tensor(out[1], q_total), out[2])
         return out
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         field_pass()
     torch.cuda.synchronize(device)
 
@@ -629,18 +680,19 @@ def run_mesh(args):
     raster.enable_stage_timing(True)
     gc.collect()
     gc.freeze()
-    clocks.mark()
+    if clocks is not None:
+        clocks.mark()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         out = field_pass()
     t1.record(stream)
     torch.cuda.synchronize(device)
-    clock_info = clocks.stop()
+    clock_info = clocks.stop() if clocks is not None else None
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
     stats1 = raster.stats()
@@ -648,7 +700,7 @@ def run_mesh(args):
     if world > 1:
         dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
     elapsed_ms = float(elapsed.item())
-    value = q_total * views * args.steps / (elapsed_ms / 1000.0) / 1e6
+    value = q_total * views * steps / (elapsed_ms / 1000.0) / 1e6
     minimum, observed = out[0].cpu().numpy(), out[1].cpu().numpy()
     if world > 1:  # this rank's points (the gathered field holds every rank's)
         minimum, observed = minimum[lo:hi], observed[lo:hi]
@@ -678,15 +730,15 @@ def run_mesh(args):
                 "hit_tests_per_s": round(tests / (integ_ms / 1000.0), 1) if integ_ms > 0 else None}
 
     # --- end to end through evaluate_field with host inputs and host results
-    e2e = None
-    if not args.no_e2e:
+    e2e_line = None
+    if e2e:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         evaluate_field(raster, shape, cameras, points, device)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(device)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             evaluate_field(raster, shape, cameras, points, device)
         e1.record(stream)
         torch.cuda.synchronize(device)
@@ -696,7 +748,7 @@ def run_mesh(args):
         h2d = packed.numel() * 4 + sigma.numel() * 4 + points.nbytes
         for c in cameras:
             h2d += c.ray_direction.numel() * 4 + 12 + (0 if c.physical_mask is None else c.physical_mask.numel())
-        e2e = {"value": round(q_total * views * args.steps / (float(ems.item()) / 1000.0) / 1e6, 3),
+        e2e_line = {"value": round(q_total * views * steps / (float(ems.item()) / 1000.0) / 1e6, 3),
                "unit": MESH_UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(points.shape[0] * 5)}
 
     # --- bisection of crossing edges (pairs of this rank's solid and free sites)
@@ -727,25 +779,21 @@ def run_mesh(args):
                          "note": "refine_crossings end to end (host endpoints in, host vertices out)"}
 
     result = {
-        "metric": MESH_METRIC, "value": round(value, 3), "unit": MESH_UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
+        "metric": MESH_METRIC, "value": round(value, 3), "unit": MESH_UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(elapsed_ms / steps, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
-        "config": mesh_config(w, q_total, world, args.edges), "e2e": e2e, "roofline": roofline,
+        "config": mesh_config(w, q_total, world, args.edges), "e2e": e2e_line, "roofline": roofline,
         "gpu_launches": int((stats1.kernel_launches - stats0.kernel_launches)),
-        "points_per_s": round(q_total * args.steps / (elapsed_ms / 1000.0), 1),
-        "stage_ms_per_step": {k: round(v[0] / args.steps, 3) for k, v in stages.items()},
-        "candidate_pairs_per_view": int((stats1.pairs - stats0.pairs) / max(1, args.steps * views)),
+        "points_per_s": round(q_total * steps / (elapsed_ms / 1000.0), 1),
+        "stage_ms_per_step": {k: round(v[0] / steps, 3) for k, v in stages.items()},
+        "candidate_pairs_per_view": int((stats1.pairs - stats0.pairs) / max(1, steps * views)),
         "observed_fraction": round(float(observed.mean()), 4), "bisection": bisection,
     }
     if clock_info is not None:
         result["clocks"] = clock_info
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if cpu:
         result["cpu_baseline"] = mesh_cpu_baseline(w, shape, points_all, cameras)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+    return result
 
 
 def mesh_cpu_baseline(w, shape, points, cameras, budget_s: float = 15.0) -> dict:

@@ -31,10 +31,12 @@ class TrainingCamera:
 
 
 def fisheye_training_camera(frame_number: int, camera: FisheyeCamera, pose7, masked: bool = True,
-                            timestamp_us: int = 0) -> TrainingCamera:
+                            timestamp_us: int = 0, rays=None) -> TrainingCamera:
     """Global-shutter camera at ``pose7`` with its first-branch rays and, when
-    ``masked``, the physical mask of pixels whose ray lies inside max_angle."""
-    _origin, direction, valid = camera.rays()
+    ``masked``, the physical mask of pixels whose ray lies inside max_angle.
+    ``rays`` (the ``camera.rays()`` triple) lets views of one camera share a
+    ray table computed once."""
+    _origin, direction, valid = camera.rays() if rays is None else rays
     pose = torch.as_tensor(np.asarray(pose7, dtype=np.float32).reshape(7))
     mask = torch.from_numpy(valid.reshape(camera.height, camera.width).astype(np.uint8)) if masked else None
     return TrainingCamera(

@@ -335,7 +335,6 @@ def run_gpu(args):
     ray_o = torch.from_numpy(ray_o_np).to(device)
     ray_d = torch.from_numpy(ray_d_np).to(device)
     mask = torch.from_numpy(valid_np).to(device)            # [1,H,W,1] bool
-    valid_f = mask[0].float()
     n_valid = max(1.0, float(valid_np.sum()))
     batches = [Batch(ray_o, ray_d, torch.from_numpy(pose_to_c2w(p)[None]).float(),
                      intrinsics_OpenCVFisheyeCameraModelParameters=cam.intrinsics(), physical_fov_mask=mask,
@@ -345,6 +344,10 @@ def run_gpu(args):
     tracer = Tracer(conf)
     raster = tracer.tracer_wrapper
     scale = 1.0 / (3.0 * n_valid)
+    # L1 weights per colour channel: the pixel mask over the 3 channels times
+    # 1 / (3 valid pixels), contiguous so the loss and its backward run as
+    # vectorised elementwise kernels
+    weights = (mask[0].float() * scale).expand(cam.height, cam.width, 3).contiguous()
 
     host_times = {"render": 0.0, "backward": 0.0}
     exchange_events = []  # (before, after) the bucket's all-reduce wait, per timed step
@@ -365,7 +368,7 @@ def run_gpu(args):
             h0 = time.perf_counter()
             out = tracer.render(s.model, batch, train=True, frame_id=v)
             host_times["render"] += time.perf_counter() - h0
-            loss = ((out["pred_features"][0] - s.target[v]).abs() * valid_f).sum() * scale
+            loss = ((out["pred_features"][0] - s.target[v]).abs() * weights).sum()
             if s.bucket is not None and v == len(batches) - 1:
                 s.bucket.arm()
             h1 = time.perf_counter()

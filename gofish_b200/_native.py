@@ -21,6 +21,7 @@ GF_CAPACITY_EXACT = 1
 GF_COMPOSITOR_KBUFFER = 0
 GF_COMPOSITOR_SOF = 1
 GF_FALLBACK_CONE = 1
+GF_FALLBACK_CONE_BIG = 5
 STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
 
 
@@ -51,6 +52,9 @@ class GfTracerConfig(ctypes.Structure):
         ("intersection_capacity", ctypes.c_int32),
         ("compositor", ctypes.c_int32),
         ("complete_admission", ctypes.c_int32),
+        ("fallback_min_angle", ctypes.c_float),
+        ("fallback_max_angle", ctypes.c_float),
+        ("partial_ut_scale", ctypes.c_float),
     ]
 
 
@@ -261,7 +265,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 5:
+    if lib.gf_abi_version() != 6:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

@@ -129,8 +129,14 @@ struct Projected {
     float ex, ey;
 };
 
+// partialScale2 > 0 enables the partial UT (gutProjector.cuh:470-499): with
+// the mean projected and, on every axis, one of its two sigma points valid,
+// each invalid point becomes the reflection 2 p0 - p of its mirror, the mean
+// is re-accumulated over the repaired points in index order and the
+// covariance is scaled by partialScale2.
 __device__ __forceinline__ bool unscented_projection(const gf_camera& cam, const Pose& pose, V3 mu, float density,
-                                                     const float* B, float& cx, float& cy, float cov[3]) {
+                                                     const float* B, float& cx, float& cy, float cov[3],
+                                                     float partialScale2 = 0.0f) {
     if (density < kAlphaThreshold) return false;
     const bool fisheye = cam.model == GF_CAMERA_OPENCV_FISHEYE;
     if (fisheye) {
@@ -142,6 +148,7 @@ __device__ __forceinline__ bool unscented_projection(const gf_camera& cam, const
         if (z < kParticleMinSensorZ) return false;
     }
     float su[7], sv[7];
+    bool ok[7];
     int numValid = 0;
     const bool c0 = project_world(cam, pose, mu, su[0], sv[0]);
     if (fisheye && !c0) return false;
@@ -151,14 +158,41 @@ __device__ __forceinline__ bool unscented_projection(const gf_camera& cam, const
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         const V3 delta = kUtDelta * v3(B[i], B[3 + i], B[6 + i]);
-        numValid += project_world(cam, pose, mu + delta, su[i + 1], sv[i + 1]) ? 1 : 0;
+        ok[i + 1] = project_world(cam, pose, mu + delta, su[i + 1], sv[i + 1]);
+        numValid += ok[i + 1] ? 1 : 0;
         cx = cx + kUtWeightI * su[i + 1];
         cy = cy + kUtWeightI * sv[i + 1];
-        numValid += project_world(cam, pose, mu - delta, su[i + 4], sv[i + 4]) ? 1 : 0;
+        ok[i + 4] = project_world(cam, pose, mu - delta, su[i + 4], sv[i + 4]);
+        numValid += ok[i + 4] ? 1 : 0;
         cx = cx + kUtWeightI * su[i + 4];
         cy = cy + kUtWeightI * sv[i + 4];
     }
-    if (numValid != 7) return false;
+    float covScale = 1.0f;
+    if (numValid != 7) {
+        if (!(partialScale2 > 0.0f) || !c0) return false;
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            if (!ok[i + 1] && !ok[i + 4]) return false;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            if (!ok[i + 1]) {
+                su[i + 1] = 2.0f * su[0] - su[i + 4];
+                sv[i + 1] = 2.0f * sv[0] - sv[i + 4];
+            }
+            if (!ok[i + 4]) {
+                su[i + 4] = 2.0f * su[0] - su[i + 1];
+                sv[i + 4] = 2.0f * sv[0] - sv[i + 1];
+            }
+        }
+        cx = su[0] * 0.0f;
+        cy = sv[0] * 0.0f;
+#pragma unroll
+        for (int k = 1; k < 7; ++k) {
+            cx = cx + kUtWeightI * su[k];
+            cy = cy + kUtWeightI * sv[k];
+        }
+        covScale = partialScale2;
+    }
     {
         const float dx = su[0] - cx, dy = sv[0] - cy;
         cov[0] = kUtWeight0 * (dx * dx);
@@ -171,6 +205,11 @@ __device__ __forceinline__ bool unscented_projection(const gf_camera& cam, const
         cov[0] = cov[0] + kUtWeightI * (dx * dx);
         cov[1] = cov[1] + kUtWeightI * (dx * dy);
         cov[2] = cov[2] + kUtWeightI * (dy * dy);
+    }
+    if (covScale != 1.0f) {
+        cov[0] = cov[0] * covScale;
+        cov[1] = cov[1] * covScale;
+        cov[2] = cov[2] * covScale;
     }
     return true;
 }

@@ -41,6 +41,14 @@
 #include "gf_tracer_kernels.cuh"
 
 namespace {
+
+// Sine of a cap half-angle bound of the cone_big window: the half-angle lies
+// in [0, pi/2], where the sine is increasing, so the window is tested on the
+// caps' sines (1 for bounds of pi/2 and above).
+float cap_sine(float angle) {
+    if (!(angle < 1.5707963267948966f)) return 1.0f;
+    return static_cast<float>(std::sin(static_cast<double>(angle > 0.0f ? angle : 0.0f)));
+}
 thread_local std::string g_lastError;
 }  // namespace
 
@@ -367,6 +375,7 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     f.shDegree = in->sh_degree;
     f.shCoeffs = in->sh_coeffs;
     f.keyMode = t->cfg.sort_key;
+    f.utPartialScale2 = t->cfg.partial_ut_scale > 0.0f ? t->cfg.partial_ut_scale * t->cfg.partial_ut_scale : 0.0f;
     const uint32_t T = uint32_t(f.gx * f.gy);
     const uint32_t N = f.N;
 
@@ -381,7 +390,13 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
 
     gf::FallbackArgs fa{};
     fa.complete = t->cfg.complete_admission != 0 ? 1 : 0;
-    fa.enabled = (t->cfg.admission_fallback == GF_FALLBACK_CONE || fa.complete) ? 1 : 0;
+    fa.enabled = (t->cfg.admission_fallback == GF_FALLBACK_CONE || t->cfg.admission_fallback == GF_FALLBACK_CONE_BIG ||
+                  fa.complete)
+                     ? 1
+                     : 0;
+    fa.coneBig = t->cfg.admission_fallback == GF_FALLBACK_CONE_BIG ? 1 : 0;
+    fa.sinMin = cap_sine(t->cfg.fallback_min_angle);
+    fa.sinMax = cap_sine(t->cfg.fallback_max_angle);
     if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
     if (int e = t->bigCount.ensure(sizeof(uint32_t) * 4, stream)) return e;
@@ -689,8 +704,20 @@ gf_tracer* gf_tracer_create(const gf_tracer_config* config) {
         fail(GF_ERR_BAD_INPUT, "unknown sort key %d", config->sort_key);
         return nullptr;
     }
-    if (config->admission_fallback != GF_FALLBACK_NONE && config->admission_fallback != GF_FALLBACK_CONE) {
+    if (config->admission_fallback != GF_FALLBACK_NONE && config->admission_fallback != GF_FALLBACK_CONE &&
+        config->admission_fallback != GF_FALLBACK_CONE_BIG) {
         fail(GF_ERR_BAD_INPUT, "unknown admission fallback %d", config->admission_fallback);
+        return nullptr;
+    }
+    if (config->admission_fallback == GF_FALLBACK_CONE_BIG &&
+        !(std::isfinite(config->fallback_min_angle) && std::isfinite(config->fallback_max_angle) &&
+          config->fallback_min_angle >= 0.0f && config->fallback_min_angle <= config->fallback_max_angle)) {
+        fail(GF_ERR_BAD_INPUT, "cone_big needs finite fallback angles with 0 <= min <= max (got %g, %g)",
+             double(config->fallback_min_angle), double(config->fallback_max_angle));
+        return nullptr;
+    }
+    if (!(std::isfinite(config->partial_ut_scale) && config->partial_ut_scale >= 0.0f)) {
+        fail(GF_ERR_BAD_INPUT, "partial_ut_scale must be finite and >= 0 (got %g)", double(config->partial_ut_scale));
         return nullptr;
     }
     if (config->compositor != GF_COMPOSITOR_KBUFFER && config->compositor != GF_COMPOSITOR_SOF) {

@@ -14,6 +14,7 @@ struct FrameArgs {
     int shDegree;
     uint32_t shCoeffs;
     int keyMode;
+    float utPartialScale2;  // partial UT covariance scale (0: off)
 };
 
 // ------------------------------------------------------------ per-tile rays
@@ -639,6 +640,8 @@ struct FallbackArgs {
     uint32_t* wideCount;
     const uint32_t* overflow;  // non-zero: the intersections exceed the key capacity, emit nothing (may be NULL)
     int complete;              // every particle takes the cone route (complete admission)
+    int coneBig;               // "cone_big": no sphere holding the camera, cap sine in [sinMin, sinMax]
+    float sinMin, sinMax;
 };
 
 __device__ __forceinline__ bool skip_emit(const FallbackArgs& fa) {
@@ -675,7 +678,7 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
 
     Projected p{};
     float cx = 0.0f, cy = 0.0f, cov[3] = {0.0f, 0.0f, 0.0f};
-    bool valid = unscented_projection(f.cam, f.pose, mu, density, B, cx, cy, cov);
+    bool valid = unscented_projection(f.cam, f.pose, mu, density, B, cx, cy, cov, f.utPartialScale2);
     if (valid) {
         p.cx = cx;
         p.cy = cy;
@@ -722,6 +725,11 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
         fb::Cap c{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, fb::kNone};
         if (fa.enabled && density >= kAlphaThreshold) {
             c = fb::fallback_cap(B, mu, density, v3(f.pose.c[0], f.pose.c[1], f.pose.c[2]));
+            // "cone_big" (gutProjector.cuh:145-154): only caps whose half-angle lies in the window, never a
+            // sphere around the camera (the window compares sines: the half-angle is at most pi/2)
+            if (fa.coneBig && !fa.complete &&
+                (c.mode == fb::kAll || (c.mode == fb::kCone && (c.sinA < fa.sinMin || c.sinA > fa.sinMax))))
+                c.mode = fb::kNone;
             if (c.mode == fb::kCone && !fb::node_pass(fa.tree, fa.tree.n - 1, 0u, c)) c.mode = fb::kNone;
             deferred = c.mode != fb::kNone;
         }

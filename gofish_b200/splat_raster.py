@@ -10,6 +10,7 @@ enqueued on the current CUDA stream of that device.
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Any, Mapping
 
 import torch
@@ -58,10 +59,24 @@ class SplatRaster:
         cfg.sort_key = (_native.GF_KEY_GLOBAL_DEPTH if bool(_select(conf, "render.gofish.fast_global_depth_key", False))
                         else _native.GF_KEY_PER_TILE_DEPTH)
         cfg.enable_hit_counts = 1 if bool(_select(conf, "render.enable_hitcounts", True)) else 0
+        # particles without a valid projection (setup_3dgut.py:232-239): dropped, the cone test, or the cone
+        # test restricted to spheres away from the camera whose cap half-angle lies in a window (degrees)
         fallback = str(_select(conf, "render.gofish.fast_admission_fallback", "cone"))
-        if fallback not in ("none", "cone"):
-            raise ValueError(f"render.gofish.fast_admission_fallback must be 'none' or 'cone' (got {fallback!r})")
-        cfg.admission_fallback = _native.GF_FALLBACK_CONE if fallback == "cone" else _native.GF_FALLBACK_NONE
+        modes = {"none": _native.GF_FALLBACK_NONE, "cone": _native.GF_FALLBACK_CONE,
+                 "cone_big": _native.GF_FALLBACK_CONE_BIG}
+        if fallback not in modes:
+            raise ValueError("render.gofish.fast_admission_fallback must be 'none', 'cone' or 'cone_big' "
+                             f"(got {fallback!r})")
+        cfg.admission_fallback = modes[fallback]
+        cfg.fallback_min_angle = math.radians(float(_select(conf, "render.gofish.fast_admission_fallback_min_angle_deg",
+                                                            0.0)))
+        cfg.fallback_max_angle = math.radians(float(_select(conf, "render.gofish.fast_admission_fallback_max_angle_deg",
+                                                            90.0)))
+        # partial UT (gutProjector.cuh:53-62): None = off, else the covariance scale of repaired projections
+        partial = _select(conf, "render.gofish.fast_partial_ut_scale", None)
+        cfg.partial_ut_scale = 0.0 if partial is None else float(partial)
+        if partial is not None and not cfg.partial_ut_scale > 0.0:
+            raise ValueError(f"render.gofish.fast_partial_ut_scale must be positive (got {partial!r})")
         # entries per pixel of the composite log the backward reads (0: default, < 0: replay every tile)
         cfg.composite_log_capacity = int(_select(conf, "render.splat.composite_log_capacity", 0))
         # the geometric training channels (normals, depth moments, quantile depths, extent, inverse depth)

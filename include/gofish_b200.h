@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 5
+#define GF_ABI_VERSION 6
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -82,6 +82,15 @@ typedef struct gf_tracer_config {
                                        by the conservative cone test of its support sphere, whose tiles hold every
                                        pixel its hit test can pass on; 0 admits particles with a valid unscented
                                        projection by their footprint (admission_fallback for the others) */
+    float fallback_min_angle;       /* GF_FALLBACK_CONE_BIG: half-angle window [min, max] (radians, 0 <= min <= max)
+                                       of the caps the fallback admits (render.gofish.fast_admission_fallback_
+                                       {min,max}_angle_deg, setup_3dgut.py:235-239) */
+    float fallback_max_angle;
+    float partial_ut_scale;         /* render.gofish.fast_partial_ut_scale (gutProjector.cuh:53-62, :470-499): > 0
+                                       repairs a projection whose mean is valid and whose every axis keeps one
+                                       valid sigma point (each invalid point replaced by the reflection of its
+                                       mirror about the projected mean, the covariance scaled by its square);
+                                       0 = off (every sigma point must project) */
 } gf_tracer_config;
 
 /* Compositing order of a pixel's hits.  KBUFFER: the tile's depth-sorted
@@ -104,9 +113,14 @@ typedef struct gf_tracer_config {
 
 /* render.gofish.fast_admission_fallback (setup_3dgut.py:232-239): "none"
  * drops particles whose unscented projection is invalid; "cone" admits them
- * by their bounding sphere against the tile ray cones. */
+ * by their bounding sphere against the tile ray cones; "cone_big" does so
+ * only for spheres that leave the camera centre outside and whose cap
+ * half-angle lies in [fallback_min_angle, fallback_max_angle]
+ * (gutProjector.cuh:44-50, :145-154): large UT-invalid particles near the
+ * camera, not the many small ones beyond a wide-angle rim. */
 #define GF_FALLBACK_NONE 0
 #define GF_FALLBACK_CONE 1
+#define GF_FALLBACK_CONE_BIG 5
 
 /* Per-call inputs of trace / trace_bwd / trace_inference
  * (splatRaster.cpp:259-273, :383-393, :469-500). */

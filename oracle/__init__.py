@@ -16,6 +16,7 @@ against the reference binary itself is unpinned.
 from __future__ import annotations
 
 import ctypes
+import math
 import subprocess
 from pathlib import Path
 
@@ -125,6 +126,7 @@ def load():
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
         "oracle_set_complete_admission": (None, [i32]),
+        "oracle_set_admission_variants": (None, [ctypes.c_float, i32, ctypes.c_float, ctypes.c_float]),
         "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
         "oracle_sof_opacity_forward": (i32, [cam_p, pose_p, vp, vp, vp, vp, vp, vp, vp, vp]),
@@ -371,6 +373,35 @@ class complete_admission:
         return False
 
 
+def cap_sine(angle: float) -> np.float32:
+    """Sine bound of a cone_big half-angle bound (the tracer's cap_sine): 1
+    from pi/2 up, else sin(max(angle, 0)) in double rounded to float32."""
+    a = np.float32(angle)
+    if not a < np.float32(math.pi / 2):
+        return np.float32(1.0)
+    return np.float32(math.sin(float(max(a, np.float32(0.0)))))
+
+
+class admission_variants:
+    """Context of project / bin with the reference's fast-admission variants:
+    the partial UT (render.gofish.fast_partial_ut_scale; 0 = off) and the
+    "cone_big" fallback window (min, max) half-angle in radians (None: the
+    plain cone fallback)."""
+
+    def __init__(self, partial_ut_scale: float = 0.0, cone_big=None):
+        s = np.float32(partial_ut_scale)
+        self.scale2 = float(s * s) if s > 0 else 0.0
+        self.cone_big = cone_big
+
+    def __enter__(self):
+        lo, hi = (cap_sine(self.cone_big[0]), cap_sine(self.cone_big[1])) if self.cone_big is not None else (0.0, 1.0)
+        load().oracle_set_admission_variants(self.scale2, 1 if self.cone_big is not None else 0, float(lo), float(hi))
+
+    def __exit__(self, *exc):
+        load().oracle_set_admission_variants(0.0, 0, 0.0, 1.0)
+        return False
+
+
 def admission_misses(cam, pose, particles, ray_o, ray_d, mask, ranges, sorted_ids, max_misses=64):
     """(count, [(pixel, particle)...]) of brute-force hits on valid rays of
     retained tiles whose particle is missing from the tile's candidate list."""
@@ -392,14 +423,16 @@ def admission_misses(cam, pose, particles, ray_o, ray_d, mask, ranges, sorted_id
 
 
 def trace(cam, pose7, particles, sh, sh_degree, ray_o, ray_d, mask, k, key_mode, tiles=None, fallback=True,
-          complete=False):
+          complete=False, partial_ut_scale=0.0, cone_big=None):
     """Full forward pass; returns a dict of every intermediate and output.
     ``fallback`` admits particles without a valid projection by the cone test
-    (render.gofish.fast_admission_fallback = "cone"); ``complete`` admits every
-    particle that way (render.gofish.complete_admission)."""
+    (render.gofish.fast_admission_fallback = "cone"; ``cone_big`` = (min, max)
+    radians restricts it to that cap window); ``complete`` admits every
+    particle that way (render.gofish.complete_admission);
+    ``partial_ut_scale`` > 0 repairs partially valid projections."""
     pose = prepare_pose(pose7)
     rd = ray_d if (fallback or complete) else None
-    with complete_admission(complete):
+    with complete_admission(complete), admission_variants(partial_ut_scale, cone_big):
         proj, rgb, counts = project(cam, pose, particles, sh, sh_degree, mask, rd)
         tr = tile_rays(cam, pose, ray_o, ray_d)
         keys, ids, ranges = bin(cam, pose, particles, proj, counts, mask, tr, key_mode, rd)

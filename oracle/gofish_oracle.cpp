@@ -119,6 +119,11 @@ void parallel_for(int begin, int end, int chunk, Fn&& fn) {
 // density >= 1/255 is admitted by the conservative cone test of its support
 // sphere, none by its projected footprint.
 bool g_completeAdmission = false;
+// Partial UT covariance scale (oracle_set_admission_variants; 0 = off) and
+// the cone_big fallback window on the caps' sines.
+float g_partialUtScale2 = 0.0f;
+bool g_coneBig = false;
+float g_coneSinMin = 0.0f, g_coneSinMax = 1.0f;
 
 // Optional explicit tile list of the render entry points (oracle_set_tile_list):
 // when one is set they visit its tiles instead of the range [tileBegin, tileEnd).
@@ -139,6 +144,15 @@ extern "C" {
 
 // Selects (1) or clears (0) complete admission for oracle_project / oracle_bin.
 void oracle_set_complete_admission(int complete) { g_completeAdmission = complete != 0; }
+
+// Partial UT (partialScale2 = scale^2 > 0, 0 = off) and the cone_big window
+// (coneBig != 0; the caps' sine bounds) of oracle_project / oracle_bin.
+void oracle_set_admission_variants(float partialScale2, int coneBig, float sinMin, float sinMax) {
+    g_partialUtScale2 = partialScale2;
+    g_coneBig = coneBig != 0;
+    g_coneSinMin = sinMin;
+    g_coneSinMax = sinMax;
+}
 
 // Sets (tiles != NULL) or clears the tile list of the render entry points;
 // the caller keeps the list alive until it is cleared.
@@ -298,7 +312,11 @@ struct Projection {
     bool valid;
 };
 
-// gutProjector.cuh:359-518, unscentedParticleProjection (no partial UT).
+// gutProjector.cuh:359-518, unscentedParticleProjection; with
+// g_partialUtScale2 > 0 the partial UT of :470-499 (each invalid sigma point
+// replaced by the reflection of its mirror about the projected mean when the
+// mean and one point per axis project; mean re-accumulated over points 1..6
+// in order; covariance scaled).
 bool unscented_projection(const OracleCamera& cam, const OraclePose& pose, const Particle& P,
                           float2_& center, float cov[3]) {
     if (P.density < kAlphaThreshold) return false;  // :375-378
@@ -315,6 +333,7 @@ bool unscented_projection(const OracleCamera& cam, const OraclePose& pose, const
         if (z < kParticleMinSensorZ) return false;
     }
     float2_ s[7];
+    bool ok[7];
     int numValid = 0;
     const bool c0 = project_world(cam, pose, P.pos, s[0]);  // :413-420
     if (fisheye && !c0) return false;                         // :421-428
@@ -323,14 +342,31 @@ bool unscented_projection(const OracleCamera& cam, const OraclePose& pose, const
     for (int i = 0; i < 3; ++i) {                             // :434-462
         const float3_ col = f3(P.B[0 * 3 + i], P.B[1 * 3 + i], P.B[2 * 3 + i]);
         const float3_ delta = scale(kUtDelta, col);
-        if (project_world(cam, pose, add(P.pos, delta), s[i + 1])) numValid++;
+        ok[i + 1] = project_world(cam, pose, add(P.pos, delta), s[i + 1]);
+        if (ok[i + 1]) numValid++;
         center.x = center.x + kUtWeightI * s[i + 1].x;
         center.y = center.y + kUtWeightI * s[i + 1].y;
-        if (project_world(cam, pose, sub(P.pos, delta), s[i + 4])) numValid++;
+        ok[i + 4] = project_world(cam, pose, sub(P.pos, delta), s[i + 4]);
+        if (ok[i + 4]) numValid++;
         center.x = center.x + kUtWeightI * s[i + 4].x;
         center.y = center.y + kUtWeightI * s[i + 4].y;
     }
-    if (numValid != 7) return false;  // :467-499 (partial UT off)
+    float covScale = 1.0f;
+    if (numValid != 7) {  // :466-499
+        if (!(g_partialUtScale2 > 0.0f) || !c0) return false;
+        for (int i = 0; i < 3; ++i)
+            if (!ok[i + 1] && !ok[i + 4]) return false;  // both points of an axis invalid: no footprint
+        for (int i = 0; i < 3; ++i) {
+            if (!ok[i + 1]) s[i + 1] = {2.0f * s[0].x - s[i + 4].x, 2.0f * s[0].y - s[i + 4].y};
+            if (!ok[i + 4]) s[i + 4] = {2.0f * s[0].x - s[i + 1].x, 2.0f * s[0].y - s[i + 1].y};
+        }
+        center = {s[0].x * 0.0f, s[0].y * 0.0f};
+        for (int k = 1; k < 7; ++k) {
+            center.x = center.x + kUtWeightI * s[k].x;
+            center.y = center.y + kUtWeightI * s[k].y;
+        }
+        covScale = g_partialUtScale2;
+    }
     {
         const float cx = s[0].x - center.x, cy = s[0].y - center.y;  // :501-506
         cov[0] = kUtWeight0 * (cx * cx);
@@ -342,6 +378,11 @@ bool unscented_projection(const OracleCamera& cam, const OraclePose& pose, const
         cov[0] = cov[0] + kUtWeightI * (cx * cx);
         cov[1] = cov[1] + kUtWeightI * (cx * cy);
         cov[2] = cov[2] + kUtWeightI * (cy * cy);
+    }
+    if (covScale != 1.0f) {  // :514
+        cov[0] = cov[0] * covScale;
+        cov[1] = cov[1] * covScale;
+        cov[2] = cov[2] * covScale;
     }
     return true;
 }
@@ -681,6 +722,18 @@ Cap cap_of(const Particle& P, const OraclePose& pose) {
     c.sinA = gf::min_f(1.0f, (r / D) * 1.0001f);
     c.cosA = sqrtf(gf::max_f(0.0f, 1.0f - c.sinA * c.sinA));
     c.mode = 1;
+    return c;
+}
+
+// The cap the fallback admits by: cap_of, except that "cone_big"
+// (gutProjector.cuh:145-154) admits no sphere holding the camera and no cap
+// whose half-angle (its sine here) lies outside the window; complete
+// admission ignores the window.
+Cap admitted_cap(const Particle& P, const OraclePose& pose) {
+    Cap c = cap_of(P, pose);
+    if (g_coneBig && !g_completeAdmission &&
+        (c.mode == 2 || (c.mode == 1 && (c.sinA < g_coneSinMin || c.sinA > g_coneSinMax))))
+        c.mode = 0;
     return c;
 }
 
@@ -1355,7 +1408,7 @@ int oracle_project(const OracleCamera* cam, const OraclePose* pose, int N, const
         }
         counts[i] = g_completeAdmission ? 0u : admitted_tiles(gx, gy, mask, pr, [](int, int) {});
         if (rayD != nullptr && (g_completeAdmission || !fast_ut_valid(pr)) && P.density >= kAlphaThreshold)
-            counts[i] = fallback::tiles(tree, mask, fallback::cap_of(P, *pose), [](int, int) {});
+            counts[i] = fallback::tiles(tree, mask, fallback::admitted_cap(P, *pose), [](int, int) {});
     });
     return 0;
 }
@@ -1473,7 +1526,7 @@ int64_t oracle_bin(const OracleCamera* cam, const OraclePose* pose, int N, const
         };
         if (!g_completeAdmission) admitted_tiles(gx, gy, mask, pr, emit);
         if (rayD != nullptr && (g_completeAdmission || !fast_ut_valid(pr)) && P.density >= kAlphaThreshold)
-            fallback::tiles(tree, mask, fallback::cap_of(P, *pose), emit);
+            fallback::tiles(tree, mask, fallback::admitted_cap(P, *pose), emit);
     });
     // Stable sort of (key, id) pairs by key.
     std::vector<uint64_t> order(static_cast<size_t>(total));

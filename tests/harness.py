@@ -67,9 +67,10 @@ def small_case(seed: int = 7, n: int = 20_000, size: int = 256, sh_degree: int =
     return make_case(scene, cam, pose)
 
 
-def oracle_forward(case: Case, k: int, key_mode: int, tiles=None, fallback: bool = True, complete: bool = False):
+def oracle_forward(case: Case, k: int, key_mode: int, tiles=None, fallback: bool = True, complete: bool = False,
+                   partial_ut_scale: float = 0.0, cone_big=None):
     return oracle.trace(case.ocam, case.pose, case.particles, case.features, case.scene.sh_degree, case.ray_o,
-                        case.ray_d, case.tmask, k, key_mode, tiles, fallback, complete)
+                        case.ray_d, case.tmask, k, key_mode, tiles, fallback, complete, partial_ut_scale, cone_big)
 
 
 def oracle_backward(case: Case, fwd, k: int, grad_rgba, grad_hit, tiles=None):
@@ -81,8 +82,9 @@ class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
     def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0,
-                 enable_normals: bool = False, complete: bool = False):
-        """k: k-buffer size, or oracle.SOF_HIERARCHY for SOF's hierarchy."""
+                 enable_normals: bool = False, complete: bool = False, gofish: dict | None = None):
+        """k: k-buffer size, or oracle.SOF_HIERARCHY for SOF's hierarchy;
+        ``gofish``: further render.gofish keys."""
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -95,7 +97,7 @@ class GpuTracer:
                                      "hierarchical_sort": sof},
                            "gofish": {"fast_global_depth_key": key_mode == 1,
                                       "fast_admission_fallback": "cone" if fallback else "none",
-                                      "complete_admission": complete},
+                                      "complete_admission": complete, **(gofish or {})},
                            "enable_hitcounts": True, "enable_normals": enable_normals}}
         self.raster = SplatRaster(conf)
         self.token = "test-token"

@@ -33,7 +33,7 @@ def test_ctypes_binding_covers_the_header():
 
 def test_library_loads_and_reports_abi_version():
     lib = _native.load()
-    assert lib.gf_abi_version() == 5
+    assert lib.gf_abi_version() == 6
 
 
 def test_create_rejects_bad_configuration():

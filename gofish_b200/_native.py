@@ -115,6 +115,7 @@ class GfTraceGrads(ctypes.Structure):
         ("quant", ctypes.c_void_p),
         ("opacity_field", ctypes.c_void_p),
         ("grad_opacity_field", ctypes.c_void_p),
+        ("grad_quant", ctypes.c_void_p),
     ]
 
 

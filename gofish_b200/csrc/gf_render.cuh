@@ -84,6 +84,8 @@ struct GeoBwd {
     const float* gradInvD2;
     const float* particles;    // packed [N,32] rows: quaternion (slots 4-7), intrinsic scale (8-10)
     float4* gradShape;         // [N,2] float4: quaternion (w, x, y, z) | scale.xyz, 0  (extent gradient)
+    const float* quant;        // forward quantile channels [H*W, 10] (crossing depth 8, crossing rate 9)
+    const float* gradQuant;    // dL/d quant (channel 8 read) or NULL
 };
 
 struct RenderBwdArgs {
@@ -795,6 +797,7 @@ struct PixelGeoBwd {
     float nB[3], wd2B;                        // forward outputs
     float nG[3], wd2G, extG, invDG, invD2G;   // output gradients
     float dscale;
+    float crossG, crossT;                     // -(dL/dt*) / (dO/dt at t*) and the crossing depth t* (0: none)
 };
 
 __device__ __forceinline__ void geo_bwd_init(PixelGeoBwd& g, const GeoBwd& a, size_t pix, float dscale) {
@@ -812,6 +815,18 @@ __device__ __forceinline__ void geo_bwd_init(PixelGeoBwd& g, const GeoBwd& a, si
     g.invDG = val(a.gradInvD, pix);
     g.invD2G = val(a.gradInvD2, pix);
     g.dscale = dscale;
+    // the crossing depth's gradient scale (rayPayloadBackward.cuh:122-128)
+    g.crossG = 0.0f;
+    g.crossT = 0.0f;
+    if (a.quant != nullptr && a.gradQuant != nullptr) {
+        const float t = a.quant[size_t(kQuantStride) * pix + kQuantiles + 1];
+        const float rate = a.quant[size_t(kQuantStride) * pix + kQuantiles + 2];
+        const float dLdt = a.gradQuant[size_t(kQuantStride) * pix + kQuantiles + 1];
+        if (fabsf(rate) > 1e-8f && t > 0.0f) {
+            g.crossG = -dLdt / rate;
+            g.crossT = t;
+        }
+    }
 }
 
 // d/dv of v / |v| applied to the output gradient go (safe_normalize_bw,
@@ -951,8 +966,40 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
         gShape[0] = rotate_transpose_vjp(quat, ray.d, rdGrd);
         gShape[1] = make_float4(nG * (sc.x * rd.x * rd.x), nG * (sc.y * rd.y * rd.y), nG * (sc.z * rd.z * rd.z), 0.0f);
     }
+    // The exact 0.5-crossing depth t* by the implicit function theorem
+    // (gaussianParticles.cuh:934-986): F = T_before (1 - alpha_k(t)) - 1/2 in
+    // the crossing Gaussian k, so dL/dtheta = g dO/dtheta at t*, g = -(dL/dt*)
+    // / Odot*.  Hits before the crossing add g * 0.5 / (1 - alpha_i) to their
+    // alpha gradient; the crossing hit differentiates its alpha at t* (its
+    // canonical point gro + t* grdu, with its own cap mask); later hits add
+    // nothing.
+    float crossDensity = 0.0f;
+    V3 groCross = v3(0.0f, 0.0f, 0.0f), grduCross = v3(0.0f, 0.0f, 0.0f);
+    if constexpr (kGeo) {
+        const PixelGeoBwd& G = *geo;
+        if (G.crossG != 0.0f && s.T > 0.5f) {
+            if (nextT > 0.5f) {
+                comp += G.crossG * fminf(0.5f / fmaxf(1.0f - galpha, 1.0f - kMaxAlpha), 1.0f);
+            } else {
+                const float ts = G.crossT;
+                const float AA = fdot3(grdu, grdu), BB = 2.0f * fdot3(gro, grdu), CC = fdot3(gro, gro);
+                const float gd = fmaxf(AA * ts * ts + BB * ts + CC, 0.0f);
+                const float gr = gf_expf(-0.5f * gd);
+                const float aU = gr * density;
+                const float aC = fminf(kMaxAlpha, aU);
+                const float dLda = G.crossG * fminf(0.5f / fmaxf(1.0f - aC, 1.0f - kMaxAlpha), 1.0f);
+                const float capC = aU < kMaxAlpha ? 1.0f : 0.0f;
+                crossDensity = capC * dLda * gr;
+                const float dgd = capC * dLda * density * (-0.5f * gr);
+                grduCross = v3(dgd * 2.0f * (ts * ts * grdu.x + ts * gro.x), dgd * 2.0f * (ts * ts * grdu.y + ts * gro.y),
+                               dgd * 2.0f * (ts * ts * grdu.z + ts * gro.z));
+                groCross = v3(dgd * 2.0f * (ts * grdu.x + gro.x), dgd * 2.0f * (ts * grdu.y + gro.y),
+                              dgd * 2.0f * (ts * grdu.z + gro.z));
+            }
+        }
+    }
     const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
-    const float gDensity = gres * gU;
+    const float gDensity = gres * gU + crossDensity;
     const float gresGrd = density * gU;
     const float grayDistGrd = -0.5f * gres * gresGrd;
     // Closest-point VJP (reference gutHalfRayResponse.cuh:39-62).
@@ -969,6 +1016,10 @@ __device__ __forceinline__ bool hit_vjp(PixelBwd& s, const Ray& ray, const Recor
         grduGrd = v3(__fmaf_rn(b, grdu.x, __fmaf_rn(a, gro.x, grduGrd.x)),
                      __fmaf_rn(b, grdu.y, __fmaf_rn(a, gro.y, grduGrd.y)),
                      __fmaf_rn(b, grdu.z, __fmaf_rn(a, gro.z, grduGrd.z)));
+    }
+    if constexpr (kGeo) {
+        groGrd = v3(groGrd.x + groCross.x, groGrd.y + groCross.y, groGrd.z + groCross.z);
+        grduGrd = v3(grduGrd.x + grduCross.x, grduGrd.y + grduCross.y, grduGrd.z + grduCross.z);
     }
     // Binv rows: r0 = (b.x b.y b.z), r1 = (b.w c.x c.y), r2 = (c.z c.w d.x).
     const float gpx = -__fmaf_rn(groGrd.z, q.c.z, __fmaf_rn(groGrd.y, q.b.w, groGrd.x * q.b.x));

@@ -839,6 +839,11 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
         a.geo.invD2 = g->inv_depth2;
         a.geo.gradInvD2 = g->grad_inv_depth2;
         a.geo.particles = in->particles;
+        if (g->grad_quant != nullptr) {
+            if (g->quant == nullptr) return fail(GF_ERR_BAD_INPUT, "a quantile-channel gradient needs the forward quant");
+            a.geo.quant = g->quant;
+            a.geo.gradQuant = g->grad_quant;
+        }
         if (int e = t->gradShape.ensure(sizeof(float4) * 2 * size_t(N) + 16, s)) return e;
         GF_CUDA(cudaMemsetAsync(t->gradShape.ptr, 0, sizeof(float4) * 2 * size_t(N), s));
         a.geo.gradShape = t->gradShape.as<float4>();

@@ -259,8 +259,8 @@ class SplatRaster:
         return grad_particles, grad_features
 
     # (value, gradient) pairs of trace_bwd in the reference's order (splatRaster.cpp:469-500) and their
-    # channel widths; the quantile/crossing channel has no gradient path here (its value feeds the
-    # opacity field's gradient)
+    # channel widths; of the quantile channels only the exact crossing depth (channel 8) carries a
+    # gradient, and the forward values also feed the opacity field's gradient
     GEOMETRY_PAIRS = (("depth_var", 1), ("extent", 1), ("opacity_field", 1), ("quant", QUANT_CHANNELS),
                       ("normal", 3), ("inv_depth", 1), ("inv_depth2", 1))
 
@@ -273,13 +273,16 @@ class SplatRaster:
         for i, (name, channels) in enumerate(self.GEOMETRY_PAIRS):
             value, grad = geometry[2 * i], geometry[2 * i + 1]
             if name == "quant":
-                # the forward's crossing depths, read by the opacity field's gradient
+                # the forward's crossing depths (read by the opacity field's gradient) and the crossing
+                # depth's gradient (implicit-function backward through the hits up to the crossing)
                 if value is not None and value.numel() == height * width * channels:
                     q = value.float().contiguous()
                     keep.append(q)
                     g.quant = q.data_ptr()
-                if grad is not None and bool(torch.count_nonzero(grad)):
-                    raise NotImplementedError("the gradient of the quantile channel is not propagated by this tracer")
+                    if grad is not None and grad.numel() == height * width * channels:
+                        gq = grad.float().contiguous()
+                        keep.append(gq)
+                        g.grad_quant = gq.data_ptr()
                 continue
             if grad is None or value is None or grad.numel() != height * width * channels:
                 continue

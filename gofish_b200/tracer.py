@@ -17,12 +17,11 @@ One render of one view:
 
 With ``render.enable_normals`` the geometric training channels are rendered
 (normal sum, sum w t^2, quantile and exact 0.5-crossing depths, intrinsic
-extent, inverse-depth moments) and the normal, depth-moment, extent and
-inverse-depth channels carry gradients; without it they are zeros, as the
-reference's buffers are with its normal channel compiled out.  The SOF
-opacity field (``loss.lambda_opa``) and the CoMe colour confidence
-(``loss.color_confidence``) are refused when the tracer is built; a gradient
-on the quantile/crossing channel raises.
+extent, inverse-depth moments) and the normal, depth-moment, extent,
+inverse-depth and exact-crossing-depth channels carry gradients (the
+crossing depth by the implicit function theorem); without it they are zeros,
+as the reference's buffers are with its normal channel compiled out.  The
+CoMe colour confidence (``loss.color_confidence``) is refused.
 """
 
 from __future__ import annotations
@@ -42,8 +41,9 @@ from .view_observation_filter import build_intrinsic_view_shape, pixel_footprint
 # gradient split of tracer.py:334-343.
 PACKED_SPLIT = (3, 1, 4, 3, 1, 9, 9, 2)
 
-# Losses on the geometric training channels (they need render.enable_normals),
-# and the one whose channel (the SOF opacity field) is not rendered here.
+# Losses on the geometric training channels (they need render.enable_normals;
+# loss.lambda_opa, on the SOF opacity field, as well), and those refused here
+# (none).
 GEOMETRIC_LOSSES = ("lambda_distortion", "lambda_dnc", "lambda_esmooth", "lambda_extent", "lambda_normal_variance")
 UNSUPPORTED_LOSSES: tuple = ()
 

@@ -193,6 +193,12 @@ typedef struct gf_trace_grads {
     const float* quant;
     const float* opacity_field;
     const float* grad_opacity_field;
+    /* dL/d quant [H,W,10] (with quant): the exact 0.5-crossing depth's channel
+     * (8) back-propagates by the implicit function theorem through the hits
+     * before the crossing and the crossing Gaussian evaluated at that depth
+     * (gaussianParticles.cuh:934-986, rayPayloadBackward.cuh:122-128); the other
+     * channels carry no gradient.  NULL: no crossing gradient. */
+    const float* grad_quant;
 } gf_trace_grads;
 
 /* Counters of the last forward pass. */

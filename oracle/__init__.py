@@ -115,7 +115,7 @@ def load():
         "oracle_render_forward_geo": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
                                             vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_render_backward_geo": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
-                                             vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+                                             vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
         "oracle_render_backward": (i32, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp,
                                          vp]),
         "oracle_project_backward": (i32, [pose_p, i32, vp, vp, i32, i32, vp, vp, vp, vp]),
@@ -313,7 +313,8 @@ def render_backward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, s
                         tiles=None, pinhole=False):
     """render_backward with the geometric channels.  fwd: render_forward_geo's
     dict; grads: dict of output gradients (rgba, hit_t, and any of normal,
-    depth_var, extent, inv_depth, inv_depth2).  Returns (grad record [N,16],
+    depth_var, extent, inv_depth, inv_depth2, and quant: only its crossing
+    depth channel 8 is read).  Returns (grad record [N,16],
     shape gradient [N,8]: quaternion w,x,y,z | scale xyz, 0)."""
     lib = load()
     gx, gy = tile_grid(cam)
@@ -329,6 +330,8 @@ def render_backward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, s
         return None if d.get(key) is None else _p(np.ascontiguousarray(d[key], dtype=np.float32))
 
     keep = {key: np.ascontiguousarray(fwd[key], dtype=np.float32) for key in ("rgba", "hit_t", "normal", "depth_var")}
+    if grads.get("quant") is not None:
+        keep["quant"] = np.ascontiguousarray(fwd["quant"], dtype=np.float32)
     lib.oracle_render_backward_geo(ctypes.byref(cam), ctypes.byref(pose), n,
                                    _p(np.ascontiguousarray(particles, dtype=np.float32)),
                                    _p(np.ascontiguousarray(rgb, dtype=np.float32)),
@@ -341,7 +344,9 @@ def render_backward_geo(cam, pose, particles, rgb, ray_o, ray_d, mask, ranges, s
                                    opt(grads, "normal"),
                                    _p(keep["depth_var"]) if grads.get("depth_var") is not None else None,
                                    opt(grads, "depth_var"), opt(grads, "extent"), opt(grads, "inv_depth"),
-                                   opt(grads, "inv_depth2"), _p(grad), _p(gshape))
+                                   opt(grads, "inv_depth2"),
+                                   _p(keep["quant"]) if grads.get("quant") is not None else None,
+                                   opt(grads, "quant"), _p(grad), _p(gshape))
     return grad, gshape
 
 

@@ -1767,7 +1767,8 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
                                int pinhole, const float* rgba, const float* hitT, const float* gradRgba,
                                const float* gradHitT, const float* normal, const float* gradNormal,
                                const float* depthVar, const float* gradDepthVar, const float* gradExtent,
-                               const float* gradInvD, const float* gradInvD2, float* gradRecord, float* gradShape) {
+                               const float* gradInvD, const float* gradInvD2, const float* quant,
+                               const float* gradQuant, float* gradRecord, float* gradShape) {
     const int W = cam->width, H = cam->height;
     const int gx = (W + kTile - 1) / kTile;
     Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
@@ -1802,6 +1803,16 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
                 const float wd2G = depthVar != nullptr ? val(gradDepthVar, pix) : 0.0f;
                 const float extG = val(gradExtent, pix), invDG = val(gradInvD, pix), invD2G = val(gradInvD2, pix);
                 const float dscale = pinhole ? rayD[3 * pix + 2] : 1.0f;
+                // exact 0.5-crossing depth t* and its gradient scale g = -(dL/dt*) / Odot*
+                // (rayPayloadBackward.cuh:122-128)
+                float crossG = 0.0f, crossT = 0.0f;
+                if (quant != nullptr && gradQuant != nullptr) {
+                    const float t = quant[10 * pix + 8], rate = quant[10 * pix + 9], dLdt = gradQuant[10 * pix + 8];
+                    if (std::fabs(rate) > 1e-8f && t > 0.0f) {
+                        crossG = -dLdt / rate;
+                        crossT = t;
+                    }
+                }
                 float T = 1.0f, depth = 0.0f, wd2 = 0.0f;
                 float nRun[3] = {0.0f, 0.0f, 0.0f};
                 float radiance[3] = {0.0f, 0.0f, 0.0f};
@@ -1883,10 +1894,39 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
                             gs[4] += nGe * (P.scale[0] * rd.x * rd.x);
                             gs[5] += nGe * (P.scale[1] * rd.y * rd.y);
                             gs[6] += nGe * (P.scale[2] * rd.z * rd.z);
+                            // the crossing depth by the implicit function theorem
+                            // (gaussianParticles.cuh:934-986): earlier hits through their
+                            // peak alpha, the crossing hit through its alpha at t*
+                            float crossDensity = 0.0f;
+                            float3_ groCross = f3(0.0f, 0.0f, 0.0f), grduCross = f3(0.0f, 0.0f, 0.0f);
+                            if (crossG != 0.0f && T > 0.5f) {
+                                if (nextT > 0.5f) {
+                                    comp += crossG * gf::min_f(0.5f / gf::max_f(1.0f - galpha, 1.0f - kMaxAlpha), 1.0f);
+                                } else {
+                                    const float ts = crossT;
+                                    const float AA = fdot(h.grdu, h.grdu), BB = 2.0f * fdot(h.gro, h.grdu),
+                                                CC = fdot(h.gro, h.gro);
+                                    const float gdc = gf::max_f(AA * ts * ts + BB * ts + CC, 0.0f);
+                                    const float grc = gf::gf_expf(-0.5f * gdc);
+                                    const float aU = grc * P.density;
+                                    const float aC = gf::min_f(kMaxAlpha, aU);
+                                    const float dLda =
+                                        crossG * gf::min_f(0.5f / gf::max_f(1.0f - aC, 1.0f - kMaxAlpha), 1.0f);
+                                    const float capC = aU < kMaxAlpha ? 1.0f : 0.0f;
+                                    crossDensity = capC * dLda * grc;
+                                    const float dgd = capC * dLda * P.density * (-0.5f * grc);
+                                    grduCross = f3(dgd * 2.0f * (ts * ts * h.grdu.x + ts * h.gro.x),
+                                                   dgd * 2.0f * (ts * ts * h.grdu.y + ts * h.gro.y),
+                                                   dgd * 2.0f * (ts * ts * h.grdu.z + ts * h.gro.z));
+                                    groCross = f3(dgd * 2.0f * (ts * h.grdu.x + h.gro.x),
+                                                  dgd * 2.0f * (ts * h.grdu.y + h.gro.y),
+                                                  dgd * 2.0f * (ts * h.grdu.z + h.gro.z));
+                                }
+                            }
                             // alpha, response, closest point
                             const float gU = (galphaU < kMaxAlpha ? 1.0f : 0.0f) * comp;
                             float* g = acc.data() + 16 * size_t(hh.idx);
-                            g[3] += gres * gU;
+                            g[3] += gres * gU + crossDensity;
                             const float gresGrd = P.density * gU;
                             const float grayDistGrd = -0.5f * gres * gresGrd;
                             const float3_ pointGrad = scale(2.0f * grayDistGrd, h.p);
@@ -1900,6 +1940,8 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
                                 groGrd = add(groGrd, scale(totalTauGrad, tauOriginGrad));
                                 grduGrd = add(grduGrd, scale(totalTauGrad, tauDirectionGrad));
                             }
+                            groGrd = add(groGrd, groCross);
+                            grduGrd = add(grduGrd, grduCross);
                             g[0] -= groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6];
                             g[1] -= groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7];
                             g[2] -= groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8];

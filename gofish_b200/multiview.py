@@ -43,7 +43,7 @@ class GradientBucket:
     Every rank must arm before the same backward.  An early parameter must
     receive exactly one gradient in the armed backward (one producer): the
     all-reduce starts at its first accumulation, so a second contribution
-    would arrive after the reduction had read the buffer.  For the tracer
+    would arrive after the reduction had read the buffer, and raises.  For the tracer
     the SH coefficients and the positions qualify: both come only out of the
     render's backward (the per-view footprint reads the positions detached)."""
 
@@ -91,6 +91,9 @@ class GradientBucket:
     def _on_accumulated(self, param: torch.Tensor) -> None:
         if not self._armed:
             return
+        if self._work is not None:
+            raise RuntimeError("an early parameter received another gradient after its all-reduce started: early "
+                               "parameters must have one gradient producer in the armed backward")
         self._pending.discard(id(param))
         if not self._pending and self._work is None:
             self._work = dist.all_reduce(self.flat[self.head_numel:], op=dist.ReduceOp.SUM, group=self._group,

@@ -133,3 +133,43 @@ def test_gradient_bucket_early_is_a_no_op_on_one_process():
     assert torch.equal(pos.grad, torch.full((4, 3), 2.0)) and torch.equal(sh.grad, torch.full((4, 48), 3.0))
     with pytest.raises(ValueError):
         GradientBucket([pos], early=[sh])
+
+
+def _second_producer_worker(rank, world, port, out):
+    from gofish_b200.multiview import GradientBucket
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pos = torch.ones(5, 3, requires_grad=True)
+        sh = torch.ones(5, 48, requires_grad=True)
+        bucket = GradientBucket([pos, sh], early=[sh])
+        bucket.attach()
+        bucket.arm()
+        (pos.sum() + sh.sum()).backward()  # starts the tail's all-reduce
+        raised = False
+        try:
+            (2.0 * sh.sum()).backward()  # a second producer of the early gradient
+        except RuntimeError as exc:
+            raised = "one gradient producer" in str(exc)
+        bucket._work.wait()
+        out[rank] = raised
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_bucket_rejects_a_second_early_producer():
+    """A gradient reaching an early parameter after its all-reduce started
+    would be left out of the sum: the bucket raises instead."""
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    procs = [ctx.Process(target=_second_producer_worker, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert out[0] and out[1]

@@ -69,8 +69,8 @@ bool valid_k(int k) { return k == 0 || k == 4 || k == 8 || k == 12 || k == 16 ||
 
 // Forwards whose intersection plan the host has not read yet, at most (the
 // next forward waits for the oldest beyond this), and the pinned plan slots.
-constexpr size_t kMaxInFlight = 4;
-constexpr int kPlanSlots = 8;
+constexpr size_t kMaxInFlight = 8;
+constexpr int kPlanSlots = 16;
 
 struct InFlight {
     cudaEvent_t done;   // recorded after the plan's copy to hostPlans[slot]

@@ -39,7 +39,7 @@ from .splat_raster import SplatRaster, _select
 from .view_observation_filter import current_view_q6, pixel_footprint_variance, shape_camera
 
 # frames whose full-shape status may still be in flight when render returns
-MAX_UNCHECKED_SHAPES = 4
+MAX_UNCHECKED_SHAPES = 8
 
 SHAPE_MODES = ("exact", "fused", "fused32", "fusedmix")
 

@@ -60,7 +60,7 @@ def _conf_value(conf, path: str, default):
 
 
 # views whose full-shape status may still be in flight when render returns
-MAX_UNCHECKED_SHAPES = 4
+MAX_UNCHECKED_SHAPES = 8
 
 
 class Tracer:

@@ -1287,10 +1287,7 @@ __global__ __launch_bounds__(kTileThreads, 3) void k_render_bwd(RenderBwdArgs a)
 // same step, and shared-memory atomics on one address serialise.  Tiles whose
 // log overflowed are left to k_render_bwd.  The loop runs to the warp's
 // longest log so that the gradient reduction can use full-warp shuffles.
-#ifndef GF_BWD_SLOTS
-#define GF_BWD_SLOTS 512
-#endif
-constexpr int kBwdSlots = GF_BWD_SLOTS;
+constexpr int kBwdSlots = 512;
 
 __host__ __device__ constexpr size_t bwd_log_smem_bytes() {
     return size_t(kBwdSlots) * (4 * sizeof(float4) + sizeof(uint32_t));
@@ -1363,37 +1360,25 @@ __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_
     for (int o = 16; o > 0; o >>= 1) warpN = max(warpN, __shfl_xor_sync(0xffffffffu, warpN, o));
     const uint32_t* entries = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
     const size_t stride = size_t(lg.tiles) * kTileThreads;
-    // Two-deep prefetch: the log entry of step i + 2 and the particle id of
-    // step i + 1 are loaded ahead, so a record read from global memory (a
-    // candidate beyond the staged ones) waits for one load, not three.
-    const auto idOf = [&](uint32_t local) {
-        return local < staged ? sIds[local] : __ldg(a.r.sortedIds + range.x + local);
-    };
     uint32_t next = n > 0 ? __ldg(entries) : 0u;
-    uint32_t next2 = n > 1 ? __ldg(entries + stride) : 0u;
-    uint32_t nextId = n > 0 ? idOf(next) : kInvalidParticle;
 #pragma unroll 1
     for (uint32_t i = 0; i < warpN; ++i) {
         const bool active = i < n && s.alive;
         const uint32_t local = next;
-        const uint32_t localId = nextId;
-        if (i + 1 < n) {
-            next = next2;
-            nextId = idOf(next);
-        }
-        if (i + 2 < n) next2 = __ldg(entries + (i + 2) * stride);
+        if (i + 1 < n) next = __ldg(entries + (i + 1) * stride);
         bool have = false;
         uint32_t cid = kInvalidParticle;
         float4 g[4] = {};
         if (active) {
             Record q;
-            cid = localId;
             if (local < staged) {
+                cid = sIds[local];
                 q.a = sRec[local];
                 q.b = sRec[kBwdSlots + local];
                 q.c = sRec[2 * kBwdSlots + local];
                 q.d = sRec[3 * kBwdSlots + local];
             } else {
+                cid = __ldg(a.r.sortedIds + range.x + local);
                 q = load_record(a.r.records, cid);
             }
             if constexpr (kGeo) {

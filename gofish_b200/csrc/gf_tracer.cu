@@ -70,6 +70,8 @@ bool valid_k(int k) { return k == 0 || k == 4 || k == 8 || k == 12 || k == 16 ||
 // Forwards whose intersection plan the host has not read yet, at most (the
 // next forward waits for the oldest beyond this), and the pinned plan slots.
 constexpr size_t kMaxInFlight = 8;
+// Tiles of the fallback walks kept for the emit pass (16 MB); walks beyond it are repeated.
+constexpr uint32_t kFallbackCacheTiles = 1u << 22;
 constexpr int kPlanSlots = 16;
 
 struct InFlight {
@@ -92,6 +94,7 @@ struct gf_tracer {
     DeviceBuffer gradRecords;
     DeviceBuffer gradShape;  // extent gradient: quaternion, intrinsic scale [N,2] float4 (enable_normals)
     DeviceBuffer coneA, coneS, caps, bigList, bigCount;  // cone-fallback admission
+    DeviceBuffer tileCache, cacheStart;                    // the fallback walks' tile lists
     DeviceBuffer wideList;                                // projected particles with a large tile box
     DeviceBuffer logIds, logCount, logOverflow, logList;  // composite log of the last training forward
     int residentBlocks = 0;                               // SMs x 3: the replay grid when a log exists
@@ -399,7 +402,9 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     fa.sinMax = cap_sine(t->cfg.fallback_max_angle);
     if (int e = t->caps.ensure(sizeof(float4) * 2 * size_t(N) + 16, stream)) return e;
     if (int e = t->bigList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
-    if (int e = t->bigCount.ensure(sizeof(uint32_t) * 4, stream)) return e;
+    if (int e = t->bigCount.ensure(sizeof(uint32_t) * 5, stream)) return e;
+    if (int e = t->cacheStart.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
+    if (int e = t->tileCache.ensure(sizeof(uint32_t) * size_t(kFallbackCacheTiles), stream)) return e;
     if (int e = t->wideList.ensure(sizeof(uint32_t) * size_t(N) + 16, stream)) return e;
     fa.caps = t->caps.as<float4>();
     fa.big = t->bigList.as<uint32_t>();
@@ -407,6 +412,10 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     fa.wide = t->wideList.as<uint32_t>();
     fa.wideCount = t->bigCount.as<uint32_t>() + 1;
     fa.bigCursor = t->bigCount.as<uint32_t>() + 2;
+    fa.cacheCursor = t->bigCount.as<uint32_t>() + 4;
+    fa.cacheStart = t->cacheStart.as<uint32_t>();
+    fa.tileCache = t->tileCache.as<uint32_t>();
+    fa.cacheCapacity = kFallbackCacheTiles;
     {
         StageTimer st(t, GF_STAGE_TILE_RAYS, stream);
         if (f.keyMode == GF_KEY_PER_TILE_DEPTH) {
@@ -464,7 +473,7 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     if (N > 0) {
         StageTimer st(t, GF_STAGE_PROJECT, stream);
         // fallback and wide lists, and the fallback kernels' cursors
-        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, 4 * sizeof(uint32_t), stream));
+        GF_CUDA(cudaMemsetAsync(fa.bigCount, 0, 5 * sizeof(uint32_t), stream));
         gf::k_project<<<(N + 255) / 256, 256, 0, stream>>>(f, in->particles, in->features, mask->buf.as<uint8_t>(),
                                                           t->proj.as<float4>(), t->records.as<float4>(),
                                                           t->counts.as<uint32_t>(), reinterpret_cast<uint32_t*>(vis),
@@ -741,7 +750,8 @@ void gf_tracer_destroy(gf_tracer* t) {
         cudaGetDevice(&prev);
         cudaSetDevice(t->device);
         cudaDeviceSynchronize();
-        for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount, &t->wideList})
+        for (DeviceBuffer* b : {&t->coneA, &t->coneS, &t->caps, &t->bigList, &t->bigCount, &t->wideList,
+                                &t->tileCache, &t->cacheStart})
             b->release();
         for (DeviceBuffer* b : {&t->logIds, &t->logCount, &t->logOverflow, &t->logList}) b->release();
         DeviceBuffer* bufs[] = {&t->proj,    &t->records, &t->bounds, &t->counts, &t->offsets, &t->scanTiles, &t->total,

@@ -642,7 +642,17 @@ struct FallbackArgs {
     int complete;              // every particle takes the cone route (complete admission)
     int coneBig;               // "cone_big": no sphere holding the camera, cap sine in [sinMin, sinMax]
     float sinMin, sinMax;
+    // Tile lists of the count pass's walks, read back by the emit pass: a
+    // particle's admitted tiles (at most kCachedTiles, in walk order) at
+    // cacheStart[i] of tileCache, kNotCached when they did not fit.
+    uint32_t* tileCache;
+    uint32_t cacheCapacity;
+    uint32_t* cacheCursor;  // zeroed per frame
+    uint32_t* cacheStart;   // [N], written for listed particles
 };
+
+constexpr uint32_t kCachedTiles = 256;
+constexpr uint32_t kNotCached = 0xffffffffu;
 
 __device__ __forceinline__ bool skip_emit(const FallbackArgs& fa) {
     return fa.overflow != nullptr && *fa.overflow != 0u;
@@ -783,6 +793,7 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
                                                       const uint64_t* __restrict__ offsets,
                                                       uint64_t* __restrict__ keys, uint32_t* __restrict__ ids) {
     __shared__ uint32_t scratch[8][fb::kWarpScratch];
+    __shared__ uint32_t walked[kEmit ? 1 : 8][kEmit ? 1 : kCachedTiles];
     const uint32_t lane = threadIdx.x & 31u;
     uint32_t* stack = scratch[threadIdx.x >> 5];
     if (kEmit && skip_emit(fa)) return;  // block-uniform
@@ -799,10 +810,27 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
         const uint32_t i = fa.big[w];
         const float4 c0 = fa.caps[2 * size_t(i)], c1 = fa.caps[2 * size_t(i) + 1];
         const fb::Cap c{c0.x, c0.y, c0.z, c0.w, c1.x, int(c1.y)};
-        if (!kEmit) {
-            const uint32_t n = fb::warp_tiles(fa.tree, mask, c, lane, stack, [](uint32_t, uint32_t) {});
+        if constexpr (!kEmit) {
+            uint32_t* list = walked[threadIdx.x >> 5];
+            const uint32_t n = fb::warp_tiles(fa.tree, mask, c, lane, stack, [&](uint32_t k, uint32_t tile) {
+                if (k < kCachedTiles) list[k] = tile;
+            });
+            __syncwarp();
+            // keep the walk for the emit pass when it fits
+            uint32_t start = kNotCached;
+            if (n > 0u && n <= kCachedTiles) {
+                if (lane == 0) start = atomicAdd(fa.cacheCursor, n);
+                start = __shfl_sync(0xffffffffu, start, 0);
+                if (start <= fa.cacheCapacity && n <= fa.cacheCapacity - start) {
+                    for (uint32_t j = lane; j < n; j += 32u) fa.tileCache[start + j] = list[j];
+                } else {
+                    start = kNotCached;
+                }
+            }
+            __syncwarp();
             if (lane == 0) {
                 counts[i] = n;
+                fa.cacheStart[i] = start;
                 if (visibility != nullptr) visibility[i] = n ? 1u : 0u;
             }
         } else {
@@ -814,11 +842,17 @@ __global__ __launch_bounds__(256) void k_fallback_big(FrameArgs f, FallbackArgs 
             const float camRadial = finite_nonneg(__fsqrt_rn(dot3(cv, cv)), kMaxDepthValue);
             const uint64_t begin = offsets[i];
             const uint32_t reserved = counts[i];
-            fb::warp_tiles(fa.tree, mask, c, lane, stack, [&](uint32_t k, uint32_t tile) {
+            const auto put = [&](uint32_t k, uint32_t tile) {
                 if (k >= reserved) return;
                 keys[begin + k] = (uint64_t(tile) << 32) | tile_depth_key(f.keyMode, mu, Binv, camRadial, tileRays, tile);
                 ids[begin + k] = i;
-            });
+            };
+            const uint32_t start = fa.cacheStart[i];
+            if (start != kNotCached) {
+                for (uint32_t k = lane; k < reserved; k += 32u) put(k, fa.tileCache[start + k]);
+            } else {
+                fb::warp_tiles(fa.tree, mask, c, lane, stack, put);
+            }
         }
     }
 }

@@ -660,8 +660,14 @@ __device__ __forceinline__ bool skip_emit(const FallbackArgs& fa) {
 
 // Projected particles whose tile bounding box holds more tiles than this are
 // counted and emitted by one warp (k_wide) instead of one thread, so that a
-// large Gaussian near the camera does not serialise thousands of tile tests.
-constexpr int kWideTiles = 64;
+// large Gaussian near the camera does not serialise thousands of tile tests
+// and one thread's long box walk does not hold its warp's 31 others (on the
+// 1M-Gaussian bench view: count + emit 0.84 ms at 64 tiles, 0.76 at 32,
+// 0.69 at 16).
+#ifndef GF_WIDE_TILES
+#define GF_WIDE_TILES 16
+#endif
+constexpr int kWideTiles = GF_WIDE_TILES;
 
 __device__ __forceinline__ bool wide_box(const TileBox& b) {
     return (b.x1 - b.x0) * (b.y1 - b.y0) > kWideTiles;
@@ -709,13 +715,34 @@ __global__ __launch_bounds__(256) void k_project(FrameArgs f, const float* __res
     float rgb[3];
     // loops unrolled over all 16 coefficients with a predicate, so that the
     // basis stays in registers (a runtime bound would put it in local memory)
+    if ((3u * f.shCoeffs) % 4u == 0u && (reinterpret_cast<uintptr_t>(features) & 15u) == 0u) {
+        // rows of whole float4s: coefficient (k, channel) is float 3k + channel
+        // of the row, read 4 at a time; each channel still sums in k order
+        float acc[3] = {0.0f, 0.0f, 0.0f};
+        const float4* c4 = reinterpret_cast<const float4*>(c);
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) {
-        float acc = basis[0] * __ldg(c + ch);
+        for (int q = 0; q < 12; ++q) {
+            if (4 * q < 3 * nb) {
+                const float4 v = __ldg(c4 + q);
+                const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int k = 1; k < 16; ++k)
-            if (k < nb) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
-        rgb[ch] = fmaxf(acc + 0.5f, 0.0f);
+                for (int r = 0; r < 4; ++r) {
+                    const int k = (4 * q + r) / 3, ch = (4 * q + r) % 3;
+                    if (k < nb) acc[ch] = k == 0 ? basis[0] * e[r] : __fmaf_rn(basis[k], e[r], acc[ch]);
+                }
+            }
+        }
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) rgb[ch] = fmaxf(acc[ch] + 0.5f, 0.0f);
+    } else {
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            float acc = basis[0] * __ldg(c + ch);
+#pragma unroll
+            for (int k = 1; k < 16; ++k)
+                if (k < nb) acc = __fmaf_rn(basis[k], __ldg(c + 3 * k + ch), acc);
+            rgb[ch] = fmaxf(acc + 0.5f, 0.0f);
+        }
     }
     float4* rec = records + 4 * size_t(i);
     rec[0] = r0;

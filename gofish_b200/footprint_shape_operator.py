@@ -37,6 +37,37 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+# Chunk plans by device: (rows, allocator reserved bytes, plan, calls since the
+# device's free memory was last read).
+_PLANS: dict = {}
+PLAN_REFRESH_CALLS = 64
+
+
+def _chunk_plan(n: int, device: torch.device):
+    """plan_footprint_chunks for n rows on ``device``, fed as the reference
+    feeds it (threedgut_tracer/footprint_shape_operator.py:305-315): the
+    driver's free and total memory and the caching allocator's reserved and
+    allocated bytes.  The free-memory query (cudaMemGetInfo) costs tens of
+    microseconds to milliseconds of host time per call, so a plan is kept while
+    the row count and the allocator's reserved bytes stay the same (the free
+    memory this process sees changes only with them, unless another process
+    allocates on the device) and is re-derived at least every
+    PLAN_REFRESH_CALLS calls."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    stats = torch.cuda.memory_stats_as_nested_dict(index)
+    reserved = int(stats.get("reserved_bytes", {}).get("all", {}).get("current", 0))
+    allocated = int(stats.get("allocated_bytes", {}).get("all", {}).get("current", 0))
+    cached = _PLANS.get(index)
+    if cached is not None and cached[0] == n and cached[1] == reserved and cached[3] < PLAN_REFRESH_CALLS:
+        _PLANS[index] = (n, reserved, cached[2], cached[3] + 1)
+        return cached[2]
+    free, total = torch.cuda.mem_get_info(index)
+    plan = plan_footprint_chunks(n, driver_free_bytes=int(free), device_total_bytes=int(total),
+                                 allocator_reserved_bytes=reserved, allocator_allocated_bytes=allocated)
+    _PLANS[index] = (n, reserved, plan, 1)
+    return plan
+
+
 def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preserving, gamma, mode, pending, start):
     n = scales.shape[0]
     dev = scales.device
@@ -149,11 +180,7 @@ def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mas
         raise ValueError("observed must be a detached bool tensor")
     if mode not in MODES:
         raise ValueError(f"unknown full-shape mode {mode!r}")
-    free, total = torch.cuda.mem_get_info(scales.device)
-    plan = plan_footprint_chunks(n, driver_free_bytes=int(free), device_total_bytes=int(total),
-                                 allocator_reserved_bytes=int(torch.cuda.memory_reserved(scales.device)),
-                                 allocator_allocated_bytes=int(torch.cuda.memory_allocated(scales.device)))
-    rows = plan.chunk_rows if n else 0
+    rows = _chunk_plan(n, scales.device).chunk_rows if n else 0
     parts = []
     pending: list = []
     for start in range(0, n, max(1, rows)) if n else []:

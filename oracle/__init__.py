@@ -6,11 +6,17 @@ tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as
 the checker or as the timed CPU baseline; the product never imports it.
 
 Parity status: the reference's CUDA extension cannot be built or run in this
-environment (empty tiny-cuda-nn submodule, no slangc) and the reference ships
-no tests or golden vectors for this path, so the restatement is pinned by
-analytic known-answer tests and finite-difference gradient checks
-(tests/test_oracle_kat.py, tests/test_oracle_gradcheck.py) -- parity
-against the reference binary itself is unpinned.
+environment as a whole (empty tiny-cuda-nn submodule, no slangc) and the
+reference ships no tests or golden vectors for this path.  Its header-only
+per-hit device code is compiled for the host from the reference checkout
+(oracle/ref_device, ``make -C oracle ref REF=...``), and the hit test,
+compositing, training channels, backward and SH radiance of this oracle are
+checked against its outputs (tests/test_hit_golden.py); the camera rays are
+checked against the reference's Python domain module
+(tests/test_domain_golden.py).  The projection, admission, binning, sort and
+k-buffer order are pinned by analytic known-answer tests and
+finite-difference gradient checks (tests/test_oracle_kat.py,
+tests/test_oracle_gradcheck.py).
 """
 
 from __future__ import annotations

@@ -6,11 +6,18 @@
 // checker or the timed CPU baseline, never as the product path.
 //
 // Parity pinning: the reference CUDA extension cannot be built or run here
-// (its tiny-cuda-nn submodule is empty and slangc is absent), and the
-// reference has no tests or golden vectors for this path.  The restatement is
-// therefore pinned by analytic known-answer tests in tests/test_oracle_kat.py
-// (on-axis Gaussian, equidistant projection identities, ...), and by the
-// finite-difference gradient checks of tests/test_oracle_gradcheck.py.
+// as a whole (its tiny-cuda-nn submodule is empty and slangc is absent), and
+// the reference has no tests or golden vectors for this path.  Its
+// header-only per-hit device code (gaussianParticles.cuh processHitFwd,
+// processHitBwd, particleExactDepthCrossingRaw, radianceFromSpH) is compiled
+// for the host from the reference checkout (oracle/ref_device, `make ref`),
+// and tests/test_hit_golden.py checks this file's hit test, compositing,
+// training channels, backward and SH radiance against its outputs
+// (tests/golden/hit_golden.npz).  The projection, admission, binning, sort
+// and k-buffer order are pinned by analytic known-answer tests in
+// tests/test_oracle_kat.py (on-axis Gaussian, equidistant projection
+// identities, ...), and the backward passes also by the finite-difference
+// gradient checks of tests/test_oracle_gradcheck.py.
 //
 // Floating-point contract (shared with the sm_100a kernels): IEEE single
 // precision, no implicit contraction (-ffp-contract=off), fmaf only where

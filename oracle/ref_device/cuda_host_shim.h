@@ -1,0 +1,96 @@
+// Host stand-ins for the CUDA built-ins used by the reference's per-hit
+// device headers (threedgut_tracer/include/3dgut/kernels/cuda/models and
+// common), so that those headers compile with g++ and run on the host cores.
+// Test infrastructure only: it builds the golden-vector generator that pins
+// the oracle's per-hit forward and backward to the reference's own code.
+//
+// Semantics: IEEE float arithmetic with no contraction (built with
+// -ffp-contract=off), the C library's expf/logf/sqrtf, plain (non-atomic)
+// read-modify-write for the atomics, which is exact for a single host thread.
+#pragma once
+
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <limits>
+
+#define __device__
+#define __host__
+#define __global__
+#define __forceinline__ inline
+#define __inline__ inline
+#define __restrict__
+// mathUtils.cuh includes its float2/float3 operator header only under nvcc.
+#ifndef __CUDACC__
+#define __CUDACC__ 1
+#endif
+
+struct float2 { float x, y; };
+struct float3 { float x, y, z; };
+struct float4 { float x, y, z, w; };
+struct int2 { int x, y; };
+struct int3 { int x, y, z; };
+struct uint2 { unsigned x, y; };
+struct uint3 { unsigned x, y, z; };
+
+inline float2 make_float2(float x, float y) { return {x, y}; }
+inline float3 make_float3(float x, float y, float z) { return {x, y, z}; }
+inline float4 make_float4(float x, float y, float z, float w) { return {x, y, z, w}; }
+inline float2 make_float2(float s) { return {s, s}; }
+inline float3 make_float3(float s) { return {s, s, s}; }
+inline float4 make_float4(float s) { return {s, s, s, s}; }
+inline int2 make_int2(int x, int y) { return {x, y}; }
+inline uint2 make_uint2(unsigned x, unsigned y) { return {x, y}; }
+
+// Component-wise vector-vector arithmetic, negation and the scalar
+// broadcasting constructors, which the reference headers take from the
+// vector helper header of their CUDA build; the scalar and compound forms and
+// float4 addition come from the reference's own mathUtils.cuh / cudaMath.cuh.
+#define GF_SHIM_BINARY(T, OP)                                                     \
+    inline T operator OP(const T& a, const T& b) {                               \
+        T r;                                                                      \
+        float* rp = &r.x;                                                         \
+        const float* ap = &a.x;                                                   \
+        const float* bp = &b.x;                                                   \
+        for (unsigned i = 0; i < sizeof(T) / sizeof(float); ++i) rp[i] = ap[i] OP bp[i]; \
+        return r;                                                                 \
+    }
+#define GF_SHIM_VECTOR(T)                                                         \
+    GF_SHIM_BINARY(T, +)                                                          \
+    GF_SHIM_BINARY(T, -)                                                          \
+    GF_SHIM_BINARY(T, *)                                                          \
+    GF_SHIM_BINARY(T, /)                                                          \
+    inline T operator-(const T& a) {                                              \
+        T r;                                                                      \
+        float* rp = &r.x;                                                         \
+        const float* ap = &a.x;                                                   \
+        for (unsigned i = 0; i < sizeof(T) / sizeof(float); ++i) rp[i] = -ap[i];  \
+        return r;                                                                 \
+    }
+GF_SHIM_VECTOR(float2)
+GF_SHIM_VECTOR(float3)
+GF_SHIM_BINARY(float4, -)
+GF_SHIM_BINARY(float4, *)
+GF_SHIM_BINARY(float4, /)
+#undef GF_SHIM_VECTOR
+#undef GF_SHIM_BINARY
+
+// __saturatef: clamp to [0, 1]; NaN maps to 0.
+inline float __saturatef(float x) { return (x > 0.0f) ? (x < 1.0f ? x : 1.0f) : 0.0f; }
+inline float rsqrtf(float x) { return 1.0f / sqrtf(x); }
+
+inline int __float_as_int(float f) { int i; memcpy(&i, &f, 4); return i; }
+inline unsigned __float_as_uint(float f) { unsigned i; memcpy(&i, &f, 4); return i; }
+inline float __int_as_float(int i) { float f; memcpy(&f, &i, 4); return f; }
+inline float __uint_as_float(unsigned i) { float f; memcpy(&f, &i, 4); return f; }
+
+template <typename T>
+inline T atomicAdd(T* address, T value) { const T old = *address; *address = old + value; return old; }
+template <typename T>
+inline T atomicMax(T* address, T value) { const T old = *address; *address = std::max(old, value); return old; }
+template <typename T>
+inline T atomicMin(T* address, T value) { const T old = *address; *address = std::min(old, value); return old; }

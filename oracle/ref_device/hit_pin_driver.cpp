@@ -1,0 +1,232 @@
+// Golden-vector generator for the per-hit forward and backward of the
+// tracer: runs the reference's own device functions on the host cores.
+// Test infrastructure only (built by `make -C oracle ref REF=<reference
+// checkout>` into oracle/_ref/, run by tests/golden/make_hit_golden.py).
+//
+// It includes, unmodified, the reference headers
+//   threedgut_tracer/include/3dgut/kernels/cuda/models/gaussianParticles.cuh
+//   (processHitFwd :611-686, processHitBwd :736-1155,
+//    particleExactDepthCrossingRaw :592-609,
+//    particleAlongRaySigmaIntrinsicPhysicalMip :175-179)
+// and the headers they include, compiled with g++ against
+// cuda_host_shim.h, with the reference build's defines for the default
+// training configuration (configs/render/3dgut.yaml: kernel degree 2,
+// min response 0.0113, min alpha 1/255, max alpha 0.99, min transmittance
+// 1e-4; setup_3dgut.py:183-191).
+//
+// Each ray composites one tile's particle list in list order (the K = 0
+// order of gutKBufferRenderer.cuh, one candidate after another, stopping
+// once the transmittance falls below the minimum), as the renderer's
+// per-hit calls do:
+//  * forward A: processHitFwd with per-particle (non per-ray) radiance, the
+//    colour clamped at zero as the renderer passes it
+//    (gutKBufferRenderer.cuh:264-268, :404-405);
+//  * forward B: the training channels, accumulated by a walk of
+//    processHitBwd with zero output gradients (that walk maintains the same
+//    front-to-back sums as the forward: radiance, transmittance, hit
+//    distance, sum w t^2, the GOF normal, the intrinsic extent and the
+//    clipped inverse-depth moments), plus, from the hit distance of
+//    gutHalfRayClosestPoint and the transmittance after each hit, the first
+//    depths where the opacity reaches 0.05 ... 0.50 and the exact 0.5
+//    crossing with its rate (gutKBufferRenderer.cuh:361-390);
+//  * backward: a second walk of processHitBwd with the integrated values of
+//    forward B and the given output gradients, the per-hit particle and
+//    colour gradients summed per particle
+//    (initializeBackwardRay, rayPayloadBackward.cuh:55-139:
+//    transmittance gradient = -dL/d(opacity), crossing gradient =
+//    -dL/dt* / rate when |rate| > 1e-8 and t* > 0).
+//
+// Per-hit mode input file (little-endian): int32 tiles, int32 rays_per_tile; per tile
+// int32 count then count x float32[32] packed rows and count x float32[3]
+// colours; per ray float32[8] (origin, unit direction, t_min, t_max) and
+// float32[12] output gradients (rgb, opacity, hit distance, normal xyz,
+// sum w t^2, extent, inverse depth, inverse depth squared) and float32 dL/dt*.
+// Output file: per ray float32[6] forward A (rgb, opacity, hit distance,
+// hit count), float32[19] forward B (rgb, opacity, hit distance, normal xyz,
+// sum w t^2, extent, inverse depth, inverse depth squared, seven quantile
+// depths) + float32[2] (exact crossing depth, its rate); per tile and
+// particle float32[32] particle gradient (ParticleDensity layout) and
+// float32[3] colour gradient.
+
+#include "cuda_host_shim.h"
+
+#include <3dgut/kernels/cuda/models/gaussianParticles.cuh>
+
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
+namespace {
+
+constexpr float kMinResponse = GAUSSIAN_PARTICLE_MIN_KERNEL_DENSITY;
+constexpr float kMinAlpha = GAUSSIAN_PARTICLE_MIN_ALPHA;
+constexpr float kMinTransmittance = GAUSSIAN_MIN_TRANSMITTANCE_THRESHOLD;
+constexpr int kKernelDegree = GAUSSIAN_PARTICLE_KERNEL_DEGREE;
+constexpr int kQuantiles = 7;
+constexpr float kQuantileLevels[kQuantiles] = {0.05f, 0.10f, 0.15f, 0.20f, 0.30f, 0.40f, 0.50f};
+
+static_assert(sizeof(threedgut::ParticleDensity) == 32 * sizeof(float), "packed particle row is 32 floats");
+
+struct Ray {
+    float3 o, d;
+    float tmin, tmax;
+};
+
+struct Accum {
+    float T = 1.0f;
+    float3 rgb = make_float3(0.0f, 0.0f, 0.0f);
+    float depth = 0.0f;
+    float sumWD2 = 0.0f;
+    float3 normal = make_float3(0.0f, 0.0f, 0.0f);
+    float sumExt = 0.0f;
+    float sumWinvD = 0.0f;
+    float sumWinvD2 = 0.0f;
+};
+
+bool read_all(FILE* f, void* p, size_t bytes) { return fread(p, 1, bytes, f) == bytes; }
+
+}  // namespace
+
+// `sh` mode: the particle radiance of the projector,
+// radianceFromSpH(degree, coefficients, incident direction, unclamped)
+// (gaussianParticles.cuh:188-220 as gutProjector.cuh:903 calls it).  Input:
+// int32 count, int32 degree, then per item float32[3] unit direction and
+// float32[48] coefficients (16 x rgb); output per item float32[3].
+int run_sh(const char* inPath, const char* outPath) {
+    FILE* in = fopen(inPath, "rb");
+    if (in == nullptr) return 3;
+    int32_t count = 0, degree = 0;
+    if (!read_all(in, &count, 4) || !read_all(in, &degree, 4)) return 4;
+    FILE* out = fopen(outPath, "wb");
+    if (out == nullptr) return 5;
+    for (int i = 0; i < count; ++i) {
+        float3 dir;
+        float3 coeffs[16];
+        if (!read_all(in, &dir, sizeof(dir)) || !read_all(in, coeffs, sizeof(coeffs))) return 6;
+        const float3 rgb = threedgut::radianceFromSpH(degree, coeffs, dir, false);
+        fwrite(&rgb, sizeof(float3), 1, out);
+    }
+    fclose(out);
+    fclose(in);
+    return 0;
+}
+
+int main(int argc, char** argv) {
+    if (argc == 4 && strcmp(argv[1], "sh") == 0) return run_sh(argv[2], argv[3]);
+    if (argc != 3) {
+        fprintf(stderr, "usage: %s input.bin output.bin | %s sh input.bin output.bin\n", argv[0], argv[0]);
+        return 2;
+    }
+    FILE* in = fopen(argv[1], "rb");
+    if (in == nullptr) return 3;
+    int32_t tiles = 0, raysPerTile = 0;
+    if (!read_all(in, &tiles, 4) || !read_all(in, &raysPerTile, 4)) return 4;
+    FILE* out = fopen(argv[2], "wb");
+    if (out == nullptr) return 5;
+
+    for (int tile = 0; tile < tiles; ++tile) {
+        int32_t count = 0;
+        if (!read_all(in, &count, 4)) return 6;
+        std::vector<threedgut::ParticleDensity> particles(static_cast<size_t>(count));
+        std::vector<float3> colours(static_cast<size_t>(count));
+        if (!read_all(in, particles.data(), sizeof(threedgut::ParticleDensity) * size_t(count))) return 7;
+        if (!read_all(in, colours.data(), sizeof(float3) * size_t(count))) return 8;
+        for (auto& c : colours) c = make_float3(fmaxf(c.x, 0.0f), fmaxf(c.y, 0.0f), fmaxf(c.z, 0.0f));
+        std::vector<threedgut::ParticleDensity> gradSum(static_cast<size_t>(count));
+        std::vector<float3> colourGradSum(size_t(count), make_float3(0.0f, 0.0f, 0.0f));
+        memset(gradSum.data(), 0, sizeof(threedgut::ParticleDensity) * size_t(count));
+
+        for (int r = 0; r < raysPerTile; ++r) {
+            float rayIn[8], gradIn[12], dLdtStar = 0.0f;
+            if (!read_all(in, rayIn, sizeof(rayIn)) || !read_all(in, gradIn, sizeof(gradIn)) ||
+                !read_all(in, &dLdtStar, 4))
+                return 9;
+            const Ray ray{make_float3(rayIn[0], rayIn[1], rayIn[2]), make_float3(rayIn[3], rayIn[4], rayIn[5]),
+                          rayIn[6], rayIn[7]};
+
+            // forward A: processHitFwd
+            float fT = 1.0f, fDepth = 0.0f;
+            float3 fRgb = make_float3(0.0f, 0.0f, 0.0f);
+            float hits = 0.0f;
+            for (int i = 0; i < count && fT >= kMinTransmittance; ++i) {
+                const bool hit = threedgut::processHitFwd<kKernelDegree, false, false>(
+                    ray.o, ray.d, i, particles.data(), reinterpret_cast<const float*>(colours.data()), kMinResponse,
+                    kMinAlpha, 0, &fT, &fRgb, &fDepth, nullptr, ray.tmin, ray.tmax);
+                if (hit) hits += 1.0f;
+            }
+
+            // forward B: processHitBwd walk with zero output gradients
+            Accum acc;
+            float quant[kQuantiles] = {};
+            float exactDepth = 0.0f, exactRate = 0.0f;
+            for (int i = 0; i < count && acc.T >= kMinTransmittance; ++i) {
+                threedgut::ParticleDensity scratch;
+                memset(&scratch, 0, sizeof(scratch));
+                float colourGrad[3] = {};
+                const float before = acc.T;
+                threedgut::processHitBwd<kKernelDegree, false, false>(
+                    ray.o, ray.d, uint32_t(i), particles[size_t(i)], &scratch,
+                    reinterpret_cast<const float*>(&colours[size_t(i)]), colourGrad, kMinResponse, kMinAlpha,
+                    kMinTransmittance, 0, 0.0f, acc.T, 0.0f, make_float3(0.0f, 0.0f, 0.0f), acc.rgb,
+                    make_float3(0.0f, 0.0f, 0.0f), 0.0f, acc.depth, 0.0f, 0.0f, &acc.sumWD2, 0.0f, &acc.normal,
+                    make_float3(0.0f, 0.0f, 0.0f), make_float3(0.0f, 0.0f, 0.0f), 0.0f, &acc.sumExt, 0.0f, 0.0f,
+                    0.0f, 0.0f, 0.0f, &acc.sumWinvD, 0.0f, 0.0f, &acc.sumWinvD2, 0.0f, 0.0f, 0.0f, ray.tmin,
+                    ray.tmax, 1.0f);
+                if (acc.T != before) {
+                    // the hit distance of the accepted hit (gutHalfRayResponse.cuh:17-37)
+                    float hitT = 0.0f;
+                    threedgut::intersectCustomParticle(ray.o, ray.d, i, particles.data(), ray.tmin, ray.tmax,
+                                                       1e30f, hitT);
+                    const float opacity = 1.0f - acc.T;
+                    for (int q = 0; q < kQuantiles; ++q)
+                        if (quant[q] == 0.0f && opacity >= kQuantileLevels[q]) quant[q] = hitT;
+                    if (exactDepth == 0.0f && before > 0.5f && acc.T <= 0.5f) {
+                        const threedgut::FiniteIntervalCrossingResult c = threedgut::particleExactDepthCrossingRaw(
+                            particles[size_t(i)], ray.o, ray.d, before, ray.tmin, ray.tmax);
+                        exactDepth = c.valid ? c.depth : hitT;
+                        exactRate = c.valid ? c.rate : 0.0f;
+                    }
+                }
+            }
+
+            // backward: processHitBwd walk with the integrated values of forward B
+            const float3 gRgb = make_float3(gradIn[0], gradIn[1], gradIn[2]);
+            const float gT = -1.0f * gradIn[3];
+            const float3 gNormal = make_float3(gradIn[5], gradIn[6], gradIn[7]);
+            const float crossingGrad = (fabsf(exactRate) > 1e-8f && exactDepth > 0.0f) ? (-dLdtStar / exactRate)
+                                                                                       : 0.0f;
+            Accum run;
+            for (int i = 0; i < count && run.T >= kMinTransmittance; ++i) {
+                threedgut::ParticleDensity g;
+                memset(&g, 0, sizeof(g));
+                float colourGrad[3] = {};
+                threedgut::processHitBwd<kKernelDegree, false, false>(
+                    ray.o, ray.d, uint32_t(i), particles[size_t(i)], &g,
+                    reinterpret_cast<const float*>(&colours[size_t(i)]), colourGrad, kMinResponse, kMinAlpha,
+                    kMinTransmittance, 0, acc.T, run.T, gT, acc.rgb, run.rgb, gRgb, acc.depth, run.depth, gradIn[4],
+                    acc.sumWD2, &run.sumWD2, gradIn[8], &run.normal, acc.normal, gNormal, acc.sumExt, &run.sumExt,
+                    gradIn[9], 0.0f, 0.0f, 0.0f, acc.sumWinvD, &run.sumWinvD, gradIn[10], acc.sumWinvD2,
+                    &run.sumWinvD2, gradIn[11], crossingGrad, exactDepth, ray.tmin, ray.tmax, 1.0f);
+                float* dst = reinterpret_cast<float*>(&gradSum[size_t(i)]);
+                const float* src = reinterpret_cast<const float*>(&g);
+                for (int k = 0; k < 32; ++k) dst[k] += src[k];
+                colourGradSum[size_t(i)].x += colourGrad[0];
+                colourGradSum[size_t(i)].y += colourGrad[1];
+                colourGradSum[size_t(i)].z += colourGrad[2];
+            }
+
+            const float fwdA[6] = {fRgb.x, fRgb.y, fRgb.z, 1.0f - fT, fDepth, hits};
+            const float fwdB[21] = {acc.rgb.x, acc.rgb.y, acc.rgb.z, 1.0f - acc.T, acc.depth, acc.normal.x,
+                                    acc.normal.y, acc.normal.z, acc.sumWD2, acc.sumExt, acc.sumWinvD, acc.sumWinvD2,
+                                    quant[0], quant[1], quant[2], quant[3], quant[4], quant[5], quant[6],
+                                    exactDepth, exactRate};
+            fwrite(fwdA, sizeof(float), 6, out);
+            fwrite(fwdB, sizeof(float), 21, out);
+        }
+        fwrite(gradSum.data(), sizeof(threedgut::ParticleDensity), size_t(count), out);
+        fwrite(colourGradSum.data(), sizeof(float3), size_t(count), out);
+    }
+    fclose(out);
+    fclose(in);
+    return 0;
+}

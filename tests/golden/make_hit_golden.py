@@ -1,0 +1,245 @@
+"""Generates tests/golden/hit_golden.npz from the reference's own per-hit
+device functions, compiled for the host cores and run in a container where
+the reference checkout is present.
+
+The reference's header-only per-hit code
+(threedgut_tracer/include/3dgut/kernels/cuda/models/gaussianParticles.cuh:
+processHitFwd :611-686, processHitBwd :736-1155,
+particleExactDepthCrossingRaw :592-609, with gutHalfRayResponse.cuh,
+finiteIntervalExactCrossing.cuh, alphaCapBackward.cuh, mathUtils.cuh,
+cudaMath.cuh and sensorConstants.cuh) is built unmodified with g++ by
+``make -C oracle ref REF=<reference>`` against oracle/ref_device/cuda_host_shim.h
+into oracle/_ref/hit_pin_driver (see the driver's header for what it runs).
+
+It also records the projector's particle radiance, radianceFromSpH
+(gaussianParticles.cuh:188-220, unclamped as gutProjector.cuh:903 calls it),
+at SH degrees 0 to 3.
+
+Inputs (seeded): tiles of 16x16 rays, each tile with its own ordered list
+of 6 to 48 Gaussians (random rotation, log-normal scales, opacities up to 1
+so the 0.99 alpha cap is reached, a few Gaussians behind the ray origins or
+within the 0.2 m inverse-depth clip, colours in [-0.2, 1.2] so the zero clamp
+is exercised) and per-ray output gradients.  Rays whose float64 evaluation
+puts a hit, the minimum transmittance or an opacity threshold within a
+relative 2e-3 of its decision boundary are redrawn, so that the float32
+evaluations of the reference and of this library take the same branches.
+
+    python tests/golden/make_hit_golden.py /path/to/reference
+"""
+
+from __future__ import annotations
+
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+DRIVER = REPO / "oracle" / "_ref" / "hit_pin_driver"
+
+TILES = 24
+RAYS = 256
+MIN_RESPONSE = 0.0113
+MIN_ALPHA = 1.0 / 255.0
+MAX_ALPHA = 0.99
+MIN_TRANSMITTANCE = 1e-4
+QUANTILES = (0.05, 0.10, 0.15, 0.20, 0.30, 0.40, 0.50)
+MARGIN = 2e-3
+
+
+def quaternion_matrix(q: np.ndarray) -> np.ndarray:
+    """Rotation matrices of unit quaternions (w, x, y, z)."""
+    w, x, y, z = q[:, 0], q[:, 1], q[:, 2], q[:, 3]
+    return np.stack([
+        np.stack([1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)], -1),
+        np.stack([2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)], -1),
+        np.stack([2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1),
+    ], -2)
+
+
+def packed_rows(pos, quat, scale, density) -> np.ndarray:
+    """[M,32] rows: position, density, quaternion (w,x,y,z), scale, intrinsic
+    density, B = R diag(s) and B^-1 = diag(1/s) R^T row-major, two zeros."""
+    m = pos.shape[0]
+    R = quaternion_matrix(quat.astype(np.float64))
+    s = scale.astype(np.float64)
+    rows = np.zeros((m, 32), np.float32)
+    rows[:, 0:3] = pos
+    rows[:, 3] = density
+    rows[:, 4:8] = quat
+    rows[:, 8:11] = scale
+    rows[:, 11] = density
+    rows[:, 12:21] = (R * s[:, None, :]).reshape(m, 9)
+    rows[:, 21:30] = (np.transpose(R, (0, 2, 1)) / s[:, :, None]).reshape(m, 9)
+    return rows
+
+
+def draw_tile(rng: np.random.Generator):
+    m = int(rng.integers(6, 49))
+    axis = rng.standard_normal(3)
+    axis /= np.linalg.norm(axis)
+    helper = np.array([1.0, 0.0, 0.0]) if abs(axis[0]) < 0.9 else np.array([0.0, 1.0, 0.0])
+    u = np.cross(axis, helper)
+    u /= np.linalg.norm(u)
+    v = np.cross(axis, u)
+    origin = rng.uniform(-0.5, 0.5, 3)
+    depth = np.sort(rng.uniform(0.4, 6.0, m))
+    depth[rng.random(m) < 0.08] = rng.uniform(-0.6, 0.15)          # behind the origins / inside the clip
+    lateral = rng.uniform(-0.35, 0.35, (m, 2)) * np.maximum(depth, 0.3)[:, None]
+    pos = origin + depth[:, None] * axis + lateral[:, :1] * u + lateral[:, 1:] * v
+    q = rng.standard_normal((m, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    scale = np.exp(rng.normal(np.log(0.12), 0.6, (m, 3)))
+    density = np.where(rng.random(m) < 0.25, rng.uniform(0.9, 1.0, m), rng.uniform(0.02, 0.9, m))
+    order = np.arange(m)
+    swaps = rng.integers(0, max(1, m - 1), size=m // 4)               # the list need not be depth sorted
+    for a in swaps:
+        order[[a, a + 1]] = order[[a + 1, a]]
+    rows = packed_rows(pos[order].astype(np.float32), q[order].astype(np.float32),
+                       scale[order].astype(np.float32), density[order].astype(np.float32))
+    colours = rng.uniform(-0.2, 1.2, (m, 3)).astype(np.float32)
+    return rows, colours, origin, axis, u, v
+
+
+def ray_is_clear(rows, o, d) -> bool:
+    """No decision of the K = 0 walk lies near its boundary (float64)."""
+    T = 1.0
+    for r in rows.astype(np.float64):
+        binv = r[21:30].reshape(3, 3)
+        gro = binv @ (o - r[0:3])
+        grdu = binv @ d
+        den = grdu @ grdu
+        tau_line = -(gro @ grdu) / den
+        if abs(tau_line) < 1e-3:            # the closest point's interior flag flips at t_min = 0
+            return False
+        tau = max(tau_line, 0.0)
+        p = gro + tau * grdu
+        resp = np.exp(-0.5 * (p @ p))
+        a_u = resp * r[3]
+        for value, edge in ((resp, MIN_RESPONSE), (a_u, MIN_ALPHA), (a_u, MAX_ALPHA)):
+            if abs(value - edge) <= MARGIN * edge:
+                return False
+        if resp > MIN_RESPONSE and min(a_u, MAX_ALPHA) > MIN_ALPHA:
+            T_next = T * (1.0 - min(a_u, MAX_ALPHA))
+            for level in QUANTILES:
+                if abs((1.0 - T_next) - level) <= MARGIN * level:
+                    return False
+            if abs(T_next - MIN_TRANSMITTANCE) <= 0.05 * MIN_TRANSMITTANCE:
+                return False
+            T = T_next
+            if T < MIN_TRANSMITTANCE:
+                break
+    return True
+
+
+def aabb_exit(o: np.ndarray, d: np.ndarray) -> np.float32:
+    """Far end of the +-1e6 scene box along the ray (float32 slab test of the
+    renderer's ray set-up, bounding_box.h:89-133) for an origin inside it."""
+    o32, d32 = o.astype(np.float32), d.astype(np.float32)
+    far = np.float32(np.inf)
+    for k in range(3):
+        a = (np.float32(-1e6) - o32[k]) / d32[k]
+        b = (np.float32(1e6) - o32[k]) / d32[k]
+        far = min(far, max(a, b))
+    return np.float32(far)
+
+
+def sh_goldens(rng: np.random.Generator, items: int = 512):
+    """The reference's unclamped particle radiance at SH degrees 0-3 for unit
+    directions (seeded, plus the six axis directions) and N(0, 0.6)
+    coefficients: arrays [4, items, 3], [4, items, 48], [4, items, 3]."""
+    dirs = rng.standard_normal((4, items, 3))
+    dirs[:, :6] = np.array([[1, 0, 0], [-1, 0, 0], [0, 1, 0], [0, -1, 0], [0, 0, 1], [0, 0, -1]], np.float64)
+    dirs = (dirs / np.linalg.norm(dirs, axis=-1, keepdims=True)).astype(np.float32)
+    coeffs = rng.normal(0.0, 0.6, (4, items, 48)).astype(np.float32)
+    rgb = np.zeros((4, items, 3), np.float32)
+    with tempfile.TemporaryDirectory() as tmp:
+        for degree in range(4):
+            src, dst = Path(tmp) / "sh.bin", Path(tmp) / "sh.out"
+            with open(src, "wb") as f:
+                f.write(np.array([items, degree], np.int32).tobytes())
+                f.write(np.concatenate([dirs[degree], coeffs[degree]], axis=1).tobytes())
+            subprocess.run([str(DRIVER), "sh", str(src), str(dst)], check=True)
+            rgb[degree] = np.fromfile(dst, dtype=np.float32).reshape(items, 3)
+    return dirs, coeffs, rgb
+
+
+def main(reference: Path) -> None:
+    subprocess.run(["make", "-C", str(REPO / "oracle"), "ref", f"REF={reference}"], check=True)
+    rng = np.random.default_rng(20261202)
+    tiles = []
+    for _ in range(TILES):
+        rows, colours, origin, axis, u, v = draw_tile(rng)
+        rays = np.zeros((RAYS, 8), np.float32)
+        for i in range(RAYS):
+            while True:
+                o = origin + rng.uniform(-0.02, 0.02, 3)
+                a, b = rng.uniform(-0.33, 0.33, 2)
+                d = axis + a * u + b * v
+                d /= np.linalg.norm(d)
+                d32 = d.astype(np.float32)
+                o32 = o.astype(np.float32)
+                if ray_is_clear(rows, o32.astype(np.float64), d32.astype(np.float64)):
+                    break
+            rays[i, 0:3], rays[i, 3:6] = o32, d32
+            rays[i, 6], rays[i, 7] = 0.0, aabb_exit(o32, d32)
+        grads = rng.normal(0.0, 1.0, (RAYS, 13)).astype(np.float32)
+        grads[:, 4] *= 0.2                       # hit distance
+        grads[:, 8] *= 0.05                      # sum w t^2
+        grads[:, 10:12] *= 0.1                   # inverse-depth moments
+        grads[:, 12] *= 0.2                      # dL/dt*
+        tiles.append((rows, colours, rays, grads))
+
+    with tempfile.TemporaryDirectory() as tmp:
+        src, dst = Path(tmp) / "in.bin", Path(tmp) / "out.bin"
+        with open(src, "wb") as f:
+            f.write(np.array([TILES, RAYS], np.int32).tobytes())
+            for rows, colours, rays, grads in tiles:
+                f.write(np.array([rows.shape[0]], np.int32).tobytes())
+                f.write(rows.tobytes())
+                f.write(colours.tobytes())
+                f.write(np.concatenate([rays, grads], axis=1).astype(np.float32).tobytes())
+        subprocess.run([str(DRIVER), str(src), str(dst)], check=True)
+        out = np.fromfile(dst, dtype=np.float32)
+
+    sh_dirs, sh_coeffs, sh_rgb = sh_goldens(rng)
+    counts = np.array([t[0].shape[0] for t in tiles], np.int32)
+    fwd_a, fwd_b, grad, grad_rgb = [], [], [], []
+    at = 0
+    for (rows, _c, _r, _g), m in zip(tiles, counts):
+        per_ray = out[at:at + RAYS * 27].reshape(RAYS, 27)
+        at += RAYS * 27
+        fwd_a.append(per_ray[:, :6])
+        fwd_b.append(per_ray[:, 6:])
+        grad.append(out[at:at + m * 32].reshape(m, 32))
+        at += m * 32
+        grad_rgb.append(out[at:at + m * 3].reshape(m, 3))
+        at += m * 3
+    assert at == out.size, (at, out.size)
+    np.savez_compressed(
+        HERE / "hit_golden.npz",
+        counts=counts,
+        rows=np.concatenate([t[0] for t in tiles]),
+        colours=np.concatenate([t[1] for t in tiles]),
+        rays=np.stack([t[2] for t in tiles]),
+        grads=np.stack([t[3] for t in tiles]),
+        fwd_a=np.stack(fwd_a),
+        fwd_b=np.stack(fwd_b),
+        grad=np.concatenate(grad),
+        grad_rgb=np.concatenate(grad_rgb),
+        sh_dirs=sh_dirs,
+        sh_coeffs=sh_coeffs,
+        sh_rgb=sh_rgb,
+    )
+    print(f"{TILES} tiles x {RAYS} rays, {int(counts.sum())} Gaussians; "
+          f"hits per ray {float(np.stack(fwd_a)[..., 5].mean()):.2f}, "
+          f"crossings {int((np.stack(fwd_b)[..., 19] > 0).sum())}")
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_hit_golden.py REFERENCE_CHECKOUT")
+    main(Path(sys.argv[1]).resolve())

@@ -99,6 +99,10 @@ struct RenderBwdArgs {
 };
 
 constexpr int kBatch = kTileThreads;
+// The forward stages 64 candidates at a time: with the K = 16 ring (48 KiB)
+// its block then needs 54 KiB of shared memory, so four blocks (32 warps)
+// fit on an SM instead of three with a 256-candidate batch.
+constexpr int kFwdBatch = 64;
 
 // A staged candidate: the 64-byte render record, its canonical ray origin for
 // the tile's common ray origin, and the cone from that origin that contains
@@ -127,8 +131,8 @@ struct WarpCone {
 
 // Shared memory of a render CTA: the staged batch, its particle ids, and the
 // per-pixel rings (hit distance + alpha, sorted candidate position).
-__host__ __device__ constexpr size_t render_smem_bytes(int K) {
-    return sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch +
+__host__ __device__ constexpr size_t render_smem_bytes(int K, int batch = kBatch) {
+    return sizeof(Staged) * batch + sizeof(uint32_t) * batch +
            size_t(K > 0 ? K : 1) * kTileThreads * (sizeof(float2) + sizeof(uint32_t));
 }
 
@@ -666,28 +670,36 @@ __device__ __forceinline__ uint32_t id_at(const RenderArgs& a, const Batch& b, u
     return __ldg(a.sortedIds + sp);
 }
 
+template <int B>
 __device__ __forceinline__ float2* ring_ta(unsigned char* smem) {
-    return reinterpret_cast<float2*>(smem + sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch);
+    return reinterpret_cast<float2*>(smem + sizeof(Staged) * B + sizeof(uint32_t) * B);
 }
-template <int K>
+template <int K, int B>
 __device__ __forceinline__ uint32_t* ring_id(unsigned char* smem) {
-    return reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch + sizeof(uint32_t) * kBatch +
+    return reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * B + sizeof(uint32_t) * B +
                                        sizeof(float2) * K * kTileThreads);
 }
 
+// Blocks per SM the forward is built for: four (64 registers a thread) when
+// its shared memory allows them (K <= 16) and it carries no geometric
+// channels, which would spill at 64 registers; else two.
+__host__ __device__ constexpr int fwd_min_blocks(int K, bool geo) {
+    return (!geo && render_smem_bytes(K, kFwdBatch) <= 55u * 1024u) ? 4 : 2;
+}
+
 template <int K, bool kGeo>
-__global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float* __restrict__ rgba,
-                                                             float* __restrict__ hitDistance,
-                                                             float* __restrict__ hitCount) {
+__global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_render_fwd(RenderArgs a, float* __restrict__ rgba,
+                                                                                 float* __restrict__ hitDistance,
+                                                                                 float* __restrict__ hitCount) {
     constexpr int KR = K > 0 ? K : 1;
     extern __shared__ __align__(16) unsigned char smem[];
     Staged* sRec = reinterpret_cast<Staged*>(smem);
-    uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kBatch);
+    uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kFwdBatch);
     const bool retained = a.mask[blockIdx.x] != 0u;
     const TileSetup ts = tile_setup(a, retained, int(blockIdx.x));
     PixelFwd s{1.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0u, ts.ray.valid};
     RingKBuffer<KR> kb;
-    kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
+    kb.init(ring_ta<kFwdBatch>(smem), ring_id<KR, kFwdBatch>(smem), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
     uint32_t nlog = 0;
     PixelGeo geo;
@@ -704,15 +716,15 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd(RenderArgs a, float
     };
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
-        for (uint32_t base = range.x; base < range.y; base += kBatch) {
+        for (uint32_t base = range.x; base < range.y; base += kFwdBatch) {
             if (__syncthreads_and(!s.alive)) break;
             const uint32_t sIdx = base + threadIdx.x;
-            if (sIdx < range.y) {
+            if (threadIdx.x < kFwdBatch && sIdx < range.y) {
                 sId[threadIdx.x] = __ldg(a.sortedIds + sIdx);
                 stage<true>(a, ts, sIdx, sRec[threadIdx.x]);
             }
             __syncthreads();
-            const int cnt = min(uint32_t(kBatch), range.y - base);
+            const int cnt = min(uint32_t(kFwdBatch), range.y - base);
             bt.base = base;
             bt.cnt = uint32_t(cnt);
             const int words = (cnt + 31) >> 5;
@@ -1187,7 +1199,7 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
         }
     };
     RingKBuffer<KR> kb;
-    kb.init(ring_ta(smem), ring_id<KR>(smem), threadIdx.x);
+    kb.init(ring_ta<kBatch>(smem), ring_id<KR, kBatch>(smem), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
     const uint2 range = a.r.ranges[ts.tile];
     for (uint32_t base = range.x; base < range.y; base += kBatch) {

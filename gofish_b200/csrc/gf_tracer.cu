@@ -277,8 +277,10 @@ int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream, const 
 template <int K, bool kGeo>
 void launch_render_fwd_geo(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
                            cudaStream_t stream) {
-    const size_t smem = gf::render_smem_bytes(K);
+    const size_t smem = gf::render_smem_bytes(K, gf::kFwdBatch);
     cudaFuncSetAttribute(gf::k_render_fwd<K, kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaFuncSetAttribute(gf::k_render_fwd<K, kGeo>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         int(cudaSharedmemCarveoutMaxShared));
     gf::k_render_fwd<K, kGeo><<<tiles, gf::kTileThreads, smem, stream>>>(a, rgba, hd, hc);
 }
 

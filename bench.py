@@ -14,6 +14,11 @@ its own views of the same scene (weak scaling).
 (oracle/) on the host cores: the reference renders only on the GPU and its
 extension cannot be built here, so the scalar C++ port is the reference arm.
 
+The default single-GPU run also measures the benchmark's other workloads and
+adds them to its line: ``mesh_query`` (the mesh opacity query, 3M Gaussians,
+27M sites, 32 views) and ``inference`` (the forward-only orbit renderer, 6M
+Gaussians, equisolid 205 deg 2560x2560, K = 32).
+
 Prints one JSON line (rank 0).
 """
 
@@ -65,6 +70,8 @@ def parse_args():
                         "(overlap), or the whole [N,59] bucket in one all-reduce after the backward (after)")
     p.add_argument("--nccl-stream-priority", choices=["normal", "high"], default="normal",
                    help="N>1: priority of the process group's NCCL streams")
+    p.add_argument("--no-inference", action="store_true",
+                   help="skip the inference orbit sub-measurement of the default single-GPU run")
     p.add_argument("--no-mesh-query", action="store_true",
                    help="single GPU, training workloads: skip the mesh opacity query sub-measurement")
     return p.parse_args()
@@ -555,6 +562,20 @@ def run_gpu(args):
         except Exception as exc:  # one GPU, no collective in flight: report and keep the main line
             mesh_clocks.stop()
             result["mesh_query"] = {"error": f"{type(exc).__name__}: {exc}"}
+    if world == 1 and not args.no_inference and args.workload in ("single_view", "multi_view"):
+        # The inference renderer over the orbit (6M Gaussians, equisolid 205
+        # deg 2560x2560, K = 32, physical-mip filter), 10 timed frames.
+        inf_args = argparse.Namespace(**{**vars(args), "num_gaussians": None, "size": None})
+        inf_clocks = ClockSampler(local)
+        inf_clocks.start()
+        try:
+            # (its CPU baseline, about two minutes of oracle work on the 6M
+            # Gaussians, is reported by `--workload inference` alone)
+            result["inference"] = measure_inference(inf_args, rank, world, device, steps=10, warmup=3,
+                                                    clocks=inf_clocks, e2e=not args.no_e2e, cpu=False)
+        except Exception as exc:  # one GPU, no collective in flight: report and keep the main line
+            inf_clocks.stop()
+            result["inference"] = {"error": f"{type(exc).__name__}: {exc}"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -977,11 +998,6 @@ def run_inference(args):
     import torch
     import torch.distributed as dist
 
-    from gofish_b200 import scene as sc
-    from gofish_b200.batch import Batch
-    from gofish_b200.inference import FrozenGaussians, InferenceTracer
-    from gofish_b200.physical_mip import compute_filter, pack_camera_table
-
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -991,6 +1007,27 @@ def run_inference(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     clocks = ClockSampler(local)
     clocks.start()
+    result = measure_inference(args, rank, world, device, args.steps, args.warmup, clocks, e2e=not args.no_e2e,
+                               cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def measure_inference(args, rank: int, world: int, device, steps: int, warmup: int, clocks=None, e2e: bool = True,
+                      cpu: bool = False) -> dict:
+    """The inference measurement (run_inference) with the process group, if
+    any, already set up: `steps` timed frames per rank after `warmup`."""
+    import torch
+    import torch.distributed as dist
+
+    from gofish_b200 import scene as sc
+    from gofish_b200.batch import Batch
+    from gofish_b200.inference import FrozenGaussians, InferenceTracer
+    from gofish_b200.physical_mip import compute_filter, pack_camera_table
+
     w = inference_workload(args)
     cam = w.camera
     ray_o_np, ray_d_np, valid_np = cam.rays()
@@ -1016,7 +1053,7 @@ def run_inference(args):
         return (step * world + rank) % len(batches)
 
     raster = tracer.wrapper
-    for s_ in range(args.warmup):
+    for s_ in range(warmup):
         tracer.render(batches[frame_of(s_)])
     torch.cuda.synchronize(device)
     raster.collect_stage_times()
@@ -1025,18 +1062,19 @@ def run_inference(args):
     launches_before = int(stats_before.total_kernel_launches)
     gc.collect()
     gc.freeze()
-    clocks.mark()
+    if clocks is not None:
+        clocks.mark()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     stream = torch.cuda.current_stream(device)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for s_ in range(args.steps):
-        tracer.render(batches[frame_of(args.warmup + s_)])
+    for s_ in range(steps):
+        tracer.render(batches[frame_of(warmup + s_)])
     t1.record(stream)
     torch.cuda.synchronize(device)
-    clock_info = clocks.stop()
+    clock_info = clocks.stop() if clocks is not None else None
     elapsed_ms = t0.elapsed_time(t1)
     raster.enable_stage_timing(False)
     stages = raster.collect_stage_times()
@@ -1045,15 +1083,15 @@ def run_inference(args):
     launches = int(stats_after.total_kernel_launches) - launches_before
     frames_read = max(1, int(stats_after.total_forwards - stats_before.total_forwards))
     mean_intersections = (stats_after.total_intersections - stats_before.total_intersections) / frames_read
-    launches += args.steps * (2 if args.shape == "exact" else 1)
+    launches += steps * (2 if args.shape == "exact" else 1)
     ms_max = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(ms_max, op=dist.ReduceOp.MAX)
     elapsed_ms = float(ms_max.item())
-    value = world * args.steps / (elapsed_ms / 1000.0)
+    value = world * steps / (elapsed_ms / 1000.0)
 
-    e2e = None
-    if not args.no_e2e:
+    e2e_line = None
+    if e2e:
         h, wd = cam.height, cam.width
         rgb_host = torch.empty((1, h, wd, 3), dtype=torch.float32).pin_memory()
         alpha_host = torch.empty((1, h, wd, 1), dtype=torch.float32).pin_memory()
@@ -1065,21 +1103,21 @@ def run_inference(args):
             alpha_host.copy_(out["pred_opacity"], non_blocking=True)
             dist_host.copy_(out["pred_dist"], non_blocking=True)
 
-        for s_ in range(max(1, args.warmup // 2)):
+        for s_ in range(max(1, warmup // 2)):
             e2e_frame(s_)
         torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for s_ in range(args.steps):
-            e2e_frame(args.warmup + s_)
+        for s_ in range(steps):
+            e2e_frame(warmup + s_)
         e1.record(stream)
         torch.cuda.synchronize(device)
         ems = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(world * args.steps / (float(ems.item()) / 1000.0), 4), "unit": INF_UNIT,
+        e2e_line = {"value": round(world * steps / (float(ems.item()) / 1000.0), 4), "unit": INF_UNIT,
                "h2d_bytes_per_step": 64, "d2h_bytes_per_step": int(h * wd * 5 * 4)}
 
     peak, peak_kind = measured_peaks()
@@ -1090,28 +1128,24 @@ def run_inference(args):
     alg = intersections * FWD_RENDER_BYTES_PER_INTERSECTION + pixels * FWD_RENDER_BYTES_PER_PIXEL
     achieved = alg / avg_s / 1e9 if avg_s > 0 else 0.0
     result = {
-        "metric": INF_METRIC, "value": round(value, 4), "unit": INF_UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+        "metric": INF_METRIC, "value": round(value, 4), "unit": INF_UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(elapsed_ms / steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene, see config)",
-        "config": inference_config(w, args, world), "e2e": e2e,
+        "config": inference_config(w, args, world), "e2e": e2e_line,
         "roofline": {"kernel": f"k_render_fwd<{w.k_buffer}>", "bound": "issue", "achieved": round(achieved, 2),
                      "note": "achieved/peak/frac are the HBM roofline of an instruction-issue-bound kernel",
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "alg_bytes_per_launch": int(alg),
                      "avg_launch_ms": round(avg_s * 1000.0, 4)},
         "gpu_launches": int(launches),
-        "stage_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in stages.items()},
+        "stage_ms_per_step": {k: round(v[0] / steps, 4) for k, v in stages.items()},
         "intersections_per_frame": intersections, "filter_3d_ms_once": round(filter_ms, 2),
     }
     if clock_info is not None:
         result["clocks"] = clock_info
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if cpu:
         result["cpu_baseline"] = inference_cpu_baseline(w, tracer, batches[0], ray_o_np, ray_d_np, valid_np)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+    return result
 
 
 def inference_cpu_baseline(w, tracer, batch, ray_o, ray_d, valid, budget_s: float = 20.0) -> dict:

@@ -99,10 +99,14 @@ struct RenderBwdArgs {
 };
 
 constexpr int kBatch = kTileThreads;
-// The forward stages 64 candidates at a time: with the K = 16 ring (48 KiB)
-// its block then needs 54 KiB of shared memory, so four blocks (32 warps)
-// fit on an SM instead of three with a 256-candidate batch.
-constexpr int kFwdBatch = 64;
+// The forward stages 32 candidates at a time into one of two buffers: the
+// records of the next batch are copied asynchronously (cp.async) by the
+// block's first warp while every warp composites the current one, so no warp
+// waits out a global-memory latency at the batch barrier.  With the K = 16
+// ring (48 KiB) its block needs 54.5 KiB of shared memory, so four blocks
+// (32 warps) fit on an SM.
+constexpr int kFwdBatch = 32;
+constexpr int kFwdBuffers = 2;
 
 // A staged candidate: the 64-byte render record, its canonical ray origin for
 // the tile's common ray origin, and the cone from that origin that contains
@@ -132,7 +136,7 @@ struct WarpCone {
 // Shared memory of a render CTA: the staged batch, its particle ids, and the
 // per-pixel rings (hit distance + alpha, sorted candidate position).
 __host__ __device__ constexpr size_t render_smem_bytes(int K, int batch = kBatch) {
-    return sizeof(Staged) * batch + sizeof(uint32_t) * batch +
+    return (sizeof(Staged) + sizeof(uint32_t)) * batch +
            size_t(K > 0 ? K : 1) * kTileThreads * (sizeof(float2) + sizeof(uint32_t));
 }
 
@@ -423,6 +427,50 @@ __device__ __forceinline__ void stage(const RenderArgs& a, const TileSetup& ts, 
     }
 }
 
+// The forward's staging, in two halves: the raw record of candidate sIdx is
+// copied asynchronously into `out.a..d` (and its id and support radius into
+// `id`, `bound`), then, once the copies have landed, derive() adds the
+// fields that stage<true>() computes from them.
+__device__ __forceinline__ void cp_async16(void* smemDst, const void* gmemSrc) {
+    const uint32_t dst = uint32_t(__cvta_generic_to_shared(smemDst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmemSrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smemDst, const void* gmemSrc) {
+    const uint32_t dst = uint32_t(__cvta_generic_to_shared(smemDst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(gmemSrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+__device__ __forceinline__ void fetch_async(const RenderArgs& a, uint32_t id, Staged& out, float& bound) {
+    const float4* r = a.records + 4 * size_t(id);
+    cp_async16(&out.a, r);
+    cp_async16(&out.b, r + 1);
+    cp_async16(&out.c, r + 2);
+    cp_async16(&out.d, r + 3);
+    cp_async4(&bound, a.bounds + id);
+}
+
+// The fields stage<true>() derives for a central tile, from the landed record.
+__device__ __forceinline__ void derive(const TileSetup& ts, Staged& out, float radius) {
+    if (!ts.central) return;
+    const float4 qa = out.a;
+    const V3 gro = binv_times(out.b, out.c, out.d, v3(ts.origin.x - qa.x, ts.origin.y - qa.y, ts.origin.z - qa.z));
+    const float A = fdot3(gro, gro);
+    out.a.x = __fsub_rn(A, __fadd_rn(miss_distance2(qa.w), __fmul_rn(1e-5f, A)));
+    const V3 v = v3(qa.x - ts.origin.x, qa.y - ts.origin.y, qa.z - ts.origin.z);
+    const float dist = sqrtf(dot3(v, v));
+    float sinB = 0.0f, cosB = -3.0f;
+    float4 u = make_float4(0.0f, 0.0f, 0.0f, cosB);
+    if (dist > radius && isfinite_f(dist) && isfinite_f(radius)) {
+        sinB = radius / dist;
+        cosB = sqrtf(fmaxf(0.0f, 1.0f - sinB * sinB));
+        u = make_float4(v.x / dist, v.y / dist, v.z / dist, cosB);
+    }
+    out.g = make_float4(gro.x, gro.y, gro.z, sinB);
+    out.u = u;
+}
+
 template <bool kFwd = false>
 __device__ __forceinline__ bool hit_staged(const TileSetup& ts, const Staged& q, float& alpha, float& ht) {
     if (ts.central) {
@@ -670,21 +718,27 @@ __device__ __forceinline__ uint32_t id_at(const RenderArgs& a, const Batch& b, u
     return __ldg(a.sortedIds + sp);
 }
 
-template <int B>
-__device__ __forceinline__ float2* ring_ta(unsigned char* smem) {
-    return reinterpret_cast<float2*>(smem + sizeof(Staged) * B + sizeof(uint32_t) * B);
+// The per-pixel rings follow `offset` bytes of staging.
+__device__ __forceinline__ float2* ring_ta(unsigned char* smem, size_t offset) {
+    return reinterpret_cast<float2*>(smem + offset);
 }
-template <int K, int B>
-__device__ __forceinline__ uint32_t* ring_id(unsigned char* smem) {
-    return reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * B + sizeof(uint32_t) * B +
-                                       sizeof(float2) * K * kTileThreads);
+template <int K>
+__device__ __forceinline__ uint32_t* ring_id(unsigned char* smem, size_t offset) {
+    return reinterpret_cast<uint32_t*>(smem + offset + sizeof(float2) * K * kTileThreads);
+}
+
+// Forward shared memory: two staging buffers of kFwdBatch records, ids and
+// support radii, then the rings.
+constexpr size_t kFwdStagingBytes = (sizeof(Staged) + 2 * sizeof(uint32_t)) * kFwdBatch * kFwdBuffers;
+__host__ __device__ constexpr size_t fwd_smem_bytes(int K) {
+    return kFwdStagingBytes + size_t(K > 0 ? K : 1) * kTileThreads * (sizeof(float2) + sizeof(uint32_t));
 }
 
 // Blocks per SM the forward is built for: four (64 registers a thread) when
 // its shared memory allows them (K <= 16) and it carries no geometric
 // channels, which would spill at 64 registers; else two.
 __host__ __device__ constexpr int fwd_min_blocks(int K, bool geo) {
-    return (!geo && render_smem_bytes(K, kFwdBatch) <= 55u * 1024u) ? 4 : 2;
+    return (!geo && fwd_smem_bytes(K) <= 55u * 1024u) ? 4 : 2;
 }
 
 template <int K, bool kGeo>
@@ -693,14 +747,16 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
                                                                                  float* __restrict__ hitCount) {
     constexpr int KR = K > 0 ? K : 1;
     extern __shared__ __align__(16) unsigned char smem[];
+    // staging buffer b: sRec[b * kFwdBatch + j], sIdB[b * kFwdBatch + j], sBound[b * kFwdBatch + j]
     Staged* sRec = reinterpret_cast<Staged*>(smem);
-    uint32_t* sId = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kFwdBatch);
+    uint32_t* sIdB = reinterpret_cast<uint32_t*>(smem + sizeof(Staged) * kFwdBatch * kFwdBuffers);
+    float* sBound = reinterpret_cast<float*>(sIdB + kFwdBatch * kFwdBuffers);
     const bool retained = a.mask[blockIdx.x] != 0u;
     const TileSetup ts = tile_setup(a, retained, int(blockIdx.x));
     PixelFwd s{1.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0u, ts.ray.valid};
     RingKBuffer<KR> kb;
-    kb.init(ring_ta<kFwdBatch>(smem), ring_id<KR, kFwdBatch>(smem), threadIdx.x);
-    Batch bt{sRec, sId, 0u, 0u};
+    kb.init(ring_ta(smem, kFwdStagingBytes), ring_id<KR>(smem, kFwdStagingBytes), threadIdx.x);
+    Batch bt{sRec, sIdB, 0u, 0u};
     uint32_t nlog = 0;
     PixelGeo geo;
     if constexpr (kGeo) {
@@ -716,31 +772,61 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
     };
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
-        for (uint32_t base = range.x; base < range.y; base += kFwdBatch) {
-            if (__syncthreads_and(!s.alive)) break;
-            const uint32_t sIdx = base + threadIdx.x;
-            if (threadIdx.x < kFwdBatch && sIdx < range.y) {
-                sId[threadIdx.x] = __ldg(a.sortedIds + sIdx);
-                stage<true>(a, ts, sIdx, sRec[threadIdx.x]);
+        // The first warp stages: candidate base + lane of each batch.  It
+        // holds the id of the batch after the one in flight in a register.
+        const bool stager = threadIdx.x < kFwdBatch;
+        uint32_t nextId = 0u;
+        if (stager) {
+            const uint32_t i0 = range.x + threadIdx.x;
+            if (i0 < range.y) {
+                const uint32_t id = __ldg(a.sortedIds + i0);
+                sIdB[threadIdx.x] = id;
+                fetch_async(a, id, sRec[threadIdx.x], sBound[threadIdx.x]);
             }
-            __syncthreads();
+            cp_async_commit();
+            const uint32_t i1 = i0 + kFwdBatch;
+            if (i1 < range.y) nextId = __ldg(a.sortedIds + i1);
+        }
+        int buf = 0;
+        for (uint32_t base = range.x; base < range.y; base += kFwdBatch, buf ^= 1) {
+            Staged* cur = sRec + buf * kFwdBatch;
+            if (stager) {
+                // this batch's copies have landed: add the derived fields
+                cp_async_wait_all();
+                if (base + threadIdx.x < range.y) derive(ts, cur[threadIdx.x], sBound[buf * kFwdBatch + threadIdx.x]);
+            }
+            // publishes the batch; every warp is done with the other buffer
+            if (__syncthreads_and(!s.alive)) break;
+            if (stager) {
+                const int nb = buf ^ 1;
+                const uint32_t i1 = base + kFwdBatch + threadIdx.x;
+                if (i1 < range.y) {
+                    sIdB[nb * kFwdBatch + threadIdx.x] = nextId;
+                    fetch_async(a, nextId, sRec[nb * kFwdBatch + threadIdx.x], sBound[nb * kFwdBatch + threadIdx.x]);
+                }
+                cp_async_commit();
+                const uint32_t i2 = i1 + kFwdBatch;
+                nextId = i2 < range.y ? __ldg(a.sortedIds + i2) : 0u;
+            }
             const int cnt = min(uint32_t(kFwdBatch), range.y - base);
+            bt.rec = cur;
+            bt.ids = sIdB + buf * kFwdBatch;
             bt.base = base;
             bt.cnt = uint32_t(cnt);
             const int words = (cnt + 31) >> 5;
 #pragma unroll 1
             for (int k = 0; k < words && __any_sync(0xffffffffu, s.alive); ++k) {
-                uint32_t m = warp_mask(ts, sRec, cnt, k);
+                uint32_t m = warp_mask(ts, cur, cnt, k);
                 while (m != 0u && s.alive) {
                     const int j = k * 32 + __ffs(m) - 1;
                     m &= m - 1u;
                     float alpha, ht;
-                    if (hit_staged<true>(ts, sRec[j], alpha, ht)) {
+                    if (hit_staged<true>(ts, cur[j], alpha, ht)) {
                         if constexpr (K == 0) {
                             log_composite(a.log, uint32_t(ts.tile), nlog, base + uint32_t(j) - range.x);
                             const float tBefore = s.T;
-                            composite_fwd(s, ht, alpha, sRec[j].d);
-                            geoHit(sId[j], ht, alpha, tBefore);
+                            composite_fwd(s, ht, alpha, cur[j].d);
+                            geoHit(bt.ids[j], ht, alpha, tBefore);
                         } else {
                             if (kb.full()) {
                                 float t0, a0;
@@ -757,6 +843,7 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
                 }
             }
         }
+        if (stager) cp_async_wait_all();  // no copy outlives the block
         if constexpr (K > 0) {
             for (int i = 0; s.alive && i < kb.n; ++i) {
                 float ht, ha;
@@ -1199,7 +1286,8 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
         }
     };
     RingKBuffer<KR> kb;
-    kb.init(ring_ta<kBatch>(smem), ring_id<KR, kBatch>(smem), threadIdx.x);
+    constexpr size_t kRingOffset = (sizeof(Staged) + sizeof(uint32_t)) * kBatch;
+    kb.init(ring_ta(smem, kRingOffset), ring_id<KR>(smem, kRingOffset), threadIdx.x);
     Batch bt{sRec, sId, 0u, 0u};
     const uint2 range = a.r.ranges[ts.tile];
     for (uint32_t base = range.x; base < range.y; base += kBatch) {

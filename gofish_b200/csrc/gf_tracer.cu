@@ -277,7 +277,7 @@ int radix_sort(gf_tracer* t, uint32_t n, int endBit, cudaStream_t stream, const 
 template <int K, bool kGeo>
 void launch_render_fwd_geo(const gf::RenderArgs& a, uint32_t tiles, float* rgba, float* hd, float* hc,
                            cudaStream_t stream) {
-    const size_t smem = gf::render_smem_bytes(K, gf::kFwdBatch);
+    const size_t smem = gf::fwd_smem_bytes(K);
     cudaFuncSetAttribute(gf::k_render_fwd<K, kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     cudaFuncSetAttribute(gf::k_render_fwd<K, kGeo>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          int(cudaSharedmemCarveoutMaxShared));
@@ -927,6 +927,18 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
 int gf_tracer_enable_timing(gf_tracer* t, int enable) {
     if (t == nullptr) return fail(GF_ERR_BAD_INPUT, "NULL argument");
     t->timing = enable != 0;
+    if (t->timing) {
+        // Events for a few hundred traces, created now so that creating them
+        // (a driver call of several microseconds each) adds no host time to
+        // the timed calls; collect_times returns them to the pool.
+        constexpr size_t kPoolEvents = 4096;
+        while (t->eventPool.size() + 2 * t->pending.size() < kPoolEvents) {
+            cudaEvent_t e = nullptr;
+            GF_CUDA(cudaEventCreate(&e));
+            t->eventPool.push_back(e);
+        }
+        t->pending.reserve(kPoolEvents / 2);
+    }
     return GF_OK;
 }
 

@@ -11,7 +11,7 @@ chunks the footprint planner gives.
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 
@@ -85,12 +85,42 @@ def _forward(scales, quaternion, density, q6, jacobian, observed, mass_preservin
                   "full shape")
     # the status words reach pinned host memory without a host synchronization;
     # FullShape.check() reads them once the copy's event has completed
-    host = torch.empty(4, dtype=torch.int32, pin_memory=True)
-    host.copy_(status, non_blocking=True)
-    done = torch.cuda.Event()
-    done.record(torch.cuda.current_stream(dev))
-    pending.append((host, done, start, status))
+    _status_copy(dev, status, start, pending)
     return cov, factor, inverse, comp, dens
+
+
+# Pinned host words and events for the status copies, per device: allocated
+# once and reused round-robin, so a call allocates no pinned memory and
+# creates no event (a fresh pinned block costs a cudaHostAlloc, up to
+# milliseconds, whenever more calls are in flight than the caching host
+# allocator has blocks for).  A slot comes round again STATUS_SLOTS calls
+# later: its last copy is waited for and, if its FullShape has not been
+# checked yet, the words are moved into ordinary host memory first.
+STATUS_SLOTS = 64
+_SLOTS: dict = {}
+
+
+def _status_copy(device: torch.device, status: torch.Tensor, start: int, pending: list) -> None:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    ring = _SLOTS.get(index)
+    if ring is None:
+        ring = {"host": torch.zeros((STATUS_SLOTS, 4), dtype=torch.int32, pin_memory=True),
+                "events": [torch.cuda.Event() for _ in range(STATUS_SLOTS)], "owner": [None] * STATUS_SLOTS,
+                "next": 0}
+        _SLOTS[index] = ring
+    i = ring["next"]
+    ring["next"] = (i + 1) % STATUS_SLOTS
+    host, done = ring["host"][i], ring["events"][i]
+    owner = ring["owner"][i]
+    if owner is not None:
+        done.synchronize()
+        lst, at = owner
+        if at < len(lst) and lst[at][0].data_ptr() == host.data_ptr():
+            lst[at] = (host.clone(),) + tuple(lst[at][1:])
+    host.copy_(status, non_blocking=True)
+    done.record(torch.cuda.current_stream(device))
+    pending.append((host, done, start, status))
+    ring["owner"][i] = (pending, len(pending) - 1)
 
 
 def _raise_failures(pending) -> None:
@@ -150,7 +180,7 @@ class FullShape:
     compensation: torch.Tensor
     density: torch.Tensor
     observed: torch.Tensor
-    pending: tuple = ()
+    pending: list = field(default_factory=list)  # (host words, event, first row, device words) per launch
 
     def check(self) -> None:
         """Raises FootprintNumericalError for the first failed row (waits for
@@ -194,7 +224,7 @@ def build_full_shape(scales, quaternion, density, q6, jacobian, observed, *, mas
         empty = scales.new_zeros((0, 3, 3))
         return FullShape(empty, empty, empty, scales.new_zeros(0), density[:0], observed)
     outs = parts[0] if len(parts) == 1 else tuple(torch.cat([p[i] for p in parts], 0) for i in range(5))
-    return FullShape(*outs, observed=observed, pending=tuple(pending))
+    return FullShape(*outs, observed=observed, pending=pending)
 
 
 __all__ = ["FootprintNumericalError", "FullShape", "build_full_shape"]

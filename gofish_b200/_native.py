@@ -22,6 +22,9 @@ GF_COMPOSITOR_KBUFFER = 0
 GF_COMPOSITOR_SOF = 1
 GF_FALLBACK_CONE = 1
 GF_FALLBACK_CONE_BIG = 5
+GF_ABS_GRAD_SCREEN = 1
+GF_ABS_GRAD_WORLD = 2
+ABI_VERSION = 7  # GF_ABI_VERSION of include/gofish_b200.h
 STAGES = ("tile_rays", "project", "scan", "emit", "sort", "ranges", "render_fwd", "render_bwd", "project_bwd")
 
 
@@ -116,6 +119,8 @@ class GfTraceGrads(ctypes.Structure):
         ("opacity_field", ctypes.c_void_p),
         ("grad_opacity_field", ctypes.c_void_p),
         ("grad_quant", ctypes.c_void_p),
+        ("position_abs_grad", ctypes.c_void_p),
+        ("position_abs_grad_mode", ctypes.c_int32),
     ]
 
 
@@ -266,7 +271,7 @@ def load(path: Path | None = None):
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.gf_abi_version() != 6:
+    if lib.gf_abi_version() != ABI_VERSION:
         raise RuntimeError("gofish_b200 native library ABI version mismatch")
     if path is None:
         _lib = lib

@@ -96,6 +96,8 @@ struct RenderBwdArgs {
     const float* gradHitDistance;
     float4* gradRecords;  // [N,4] float4: pos.xyz+density | Binv row0 + row1.x | row1.yz + row2.xy | row2.z + rgb
     GeoBwd geo;
+    float* absGrad;       // densification statistic (gf_trace_grads.position_abs_grad) or NULL
+    int absMode;          // GF_ABS_GRAD_SCREEN ([N,8]: map 0-5, sums 6-7) or GF_ABS_GRAD_WORLD ([N,3])
 };
 
 constexpr int kBatch = kTileThreads;
@@ -1241,6 +1243,53 @@ __device__ __forceinline__ void accumulate_grad(float4* __restrict__ gradRecords
     }
 }
 
+// The densification statistic of one composited hit per lane
+// (gutKBufferRenderer.cuh:283-296): the absolute values of the hit's position
+// gradient `gp` (screen mode: of the two rows of the particle's map times it),
+// added to the particle's sums; a warp whose lanes all hold one particle adds
+// its warp sums once.  Sums of absolute values are additive, so the warp sum
+// gives the same statistic as per-lane additions.  The composite-log backward
+// is instantiated with kAbs = false for backwards without the statistic, so
+// their inner loop carries none of it.
+template <bool kAbs = true>
+__device__ __forceinline__ void accumulate_abs_grad(float* __restrict__ absGrad, int mode, bool have, uint32_t idx,
+                                                    float4 gp) {
+    if constexpr (!kAbs) return;
+    if (absGrad == nullptr) return;  // kernel-uniform
+    float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f;
+    if (have) {
+        if (mode == GF_ABS_GRAD_SCREEN) {
+            const float* row = absGrad + 8 * size_t(idx);
+            v0 = fabsf(row[0] * gp.x + row[1] * gp.y + row[2] * gp.z);
+            v1 = fabsf(row[3] * gp.x + row[4] * gp.y + row[5] * gp.z);
+        } else {
+            v0 = fabsf(gp.x);
+            v1 = fabsf(gp.y);
+            v2 = fabsf(gp.z);
+        }
+    }
+    const uint32_t hm = __ballot_sync(0xffffffffu, have);
+    if (hm == 0u) return;
+    const int leader = __ffs(hm) - 1;
+    const uint32_t leaderIdx = __shfl_sync(0xffffffffu, idx, leader);
+    if (__all_sync(0xffffffffu, !have || idx == leaderIdx)) {
+        v0 = warp_sum(v0);
+        v1 = warp_sum(v1);
+        v2 = warp_sum(v2);
+        if ((threadIdx.x & 31) != leader) return;
+    } else if (!have) {
+        return;
+    }
+    if (mode == GF_ABS_GRAD_SCREEN) {
+        atomicAdd(absGrad + 8 * size_t(idx) + 6, v0);
+        atomicAdd(absGrad + 8 * size_t(idx) + 7, v1);
+    } else {
+        atomicAdd(absGrad + 3 * size_t(idx), v0);
+        atomicAdd(absGrad + 3 * size_t(idx) + 1, v1);
+        atomicAdd(absGrad + 3 * size_t(idx) + 2, v2);
+    }
+}
+
 // Backward replay: the identical traversal and k-buffer, each composited hit
 // back-propagated from the final pixel values.  Loops are warp-uniform so
 // the gradient reduction can use full-warp shuffles.
@@ -1333,6 +1382,7 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
                         if (s.T < kMinTransmittance) s.alive = false;
                     }
                 }
+                accumulate_abs_grad(a.absGrad, a.absMode, have, cid, g[0]);
                 accumulate_grad(a.gradRecords, have, cid, g);
             }
         }
@@ -1351,6 +1401,7 @@ __device__ __forceinline__ void replay_tile(const RenderBwdArgs& a, unsigned cha
                 have = vjp(q, cid, g);
                 if (s.T < kMinTransmittance) s.alive = false;
             }
+            accumulate_abs_grad(a.absGrad, a.absMode, have, cid, g[0]);
             accumulate_grad(a.gradRecords, have, cid, g);
         }
     }
@@ -1396,7 +1447,7 @@ __host__ __device__ constexpr size_t bwd_log_smem_bytes() {
 #ifndef GF_BWD_LOG_MIN_BLOCKS
 #define GF_BWD_LOG_MIN_BLOCKS 3
 #endif
-template <bool kGeo>
+template <bool kGeo, bool kAbs>
 __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_bwd_log(RenderBwdArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     float4* sRec = reinterpret_cast<float4*>(smem);                                      // [4][kBwdSlots]
@@ -1493,6 +1544,7 @@ __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_
             }
             if (s.T < kMinTransmittance) s.alive = false;
         }
+        accumulate_abs_grad<kAbs>(a.absGrad, a.absMode, have, cid, g[0]);
         accumulate_grad(a.gradRecords, have, cid, g);
     }
 }

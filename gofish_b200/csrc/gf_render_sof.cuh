@@ -482,6 +482,7 @@ __device__ __forceinline__ void replay_tile_sof(const RenderBwdArgs& a, unsigned
                 if (s.T < kMinTransmittance) s.alive = false;
             }
         }
+        accumulate_abs_grad(a.absGrad, a.absMode, have, cid, g[0]);
         accumulate_grad(a.gradRecords, have, cid, g);
     };
     auto done = [&]() { return __syncthreads_and(!s.alive) != 0; };
@@ -498,6 +499,7 @@ __device__ __forceinline__ void replay_tile_sof(const RenderBwdArgs& a, unsigned
             have = vjp(sp, cid, g);
             if (s.T < kMinTransmittance) s.alive = false;
         }
+        accumulate_abs_grad(a.absGrad, a.absMode, have, cid, g[0]);
         accumulate_grad(a.gradRecords, have, cid, g);
     }
 }

@@ -304,11 +304,17 @@ void launch_render_bwd(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t 
     else launch_render_bwd_geo<K, false>(a, tiles, stream);
 }
 
+template <bool kGeo, bool kAbs>
+void launch_render_bwd_log_abs(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
+    const size_t smem = gf::bwd_log_smem_bytes();
+    cudaFuncSetAttribute(gf::k_render_bwd_log<kGeo, kAbs>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    gf::k_render_bwd_log<kGeo, kAbs><<<tiles, gf::kTileThreads, smem, stream>>>(a);
+}
+
 template <bool kGeo>
 void launch_render_bwd_log(const gf::RenderBwdArgs& a, uint32_t tiles, cudaStream_t stream) {
-    const size_t smem = gf::bwd_log_smem_bytes();
-    cudaFuncSetAttribute(gf::k_render_bwd_log<kGeo>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    gf::k_render_bwd_log<kGeo><<<tiles, gf::kTileThreads, smem, stream>>>(a);
+    if (a.absGrad != nullptr) launch_render_bwd_log_abs<kGeo, true>(a, tiles, stream);
+    else launch_render_bwd_log_abs<kGeo, false>(a, tiles, stream);
 }
 
 // Blocks of the replay grid that walks the overflowed tiles: 3 per SM.
@@ -838,6 +844,10 @@ int gf_tracer_trace_bwd(gf_tracer* t, const gf_trace_inputs* in, const gf_trace_
     a.gradRgba = g->grad_rgba;
     a.gradHitDistance = g->grad_hit_distance;
     a.gradRecords = t->gradRecords.as<float4>();
+    a.absGrad = g->position_abs_grad;
+    a.absMode = g->position_abs_grad_mode;
+    if (a.absGrad != nullptr && a.absMode != GF_ABS_GRAD_SCREEN && a.absMode != GF_ABS_GRAD_WORLD)
+        return fail(GF_ERR_BAD_INPUT, "unknown position_abs_grad_mode %d", int(a.absMode));
     a.geo = gf::GeoBwd{};
     if (t->cfg.enable_normals && t->frameGeo) {
         a.geo.normal = g->normal;

@@ -2,8 +2,9 @@
 
 Method names, argument order and outputs follow the reference's pybind module
 (threedgut_tracer/bindings.cpp:106-124, src/splatRaster.cpp): ``trace``,
-``trace_bwd``, ``trace_inference``, ``register_physical_tile_mask`` and
-``collect_times``.  Tensors stay on the device of the rays; every call is
+``trace_bwd``, ``trace_inference``, ``register_physical_tile_mask``,
+``collect_times``, and the densification statistic's
+``set_exact_screen_absgrad_map`` and ``collect_abs_grad``.  Tensors stay on the device of the rays; every call is
 enqueued on the current CUDA stream of that device.
 """
 
@@ -108,6 +109,11 @@ class SplatRaster:
         self._times: dict[str, float] = {}
         self._events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
         self.enable_kernel_timings = bool(_select(conf, "render.enable_kernel_timings", False))
+        # densification statistic (setup_3dgut.py:135,182): per-hit |map g| with a caller-armed map, or per-hit
+        # |g| in world space
+        self._abs_grad_screen = bool(_select(conf, "strategy.densify.generic_camera_absgrad", True))
+        self._abs_workspace: torch.Tensor | None = None
+        self._last_abs_grad: torch.Tensor | None = None
 
     def __del__(self):
         handle = getattr(self, "_handle", None)
@@ -250,13 +256,62 @@ class SplatRaster:
         g.grad_particles = grad_particles.data_ptr()
         g.grad_features = grad_features.data_ptr()
         keep = self._geometry_grads(g, geometry, int(ray_ori.shape[1]), int(ray_ori.shape[2]))
+        abs_grad = self._abs_grad_buffer(n, device)
+        if abs_grad is not None:
+            g.position_abs_grad = abs_grad.data_ptr()
+            g.position_abs_grad_mode = _native.GF_ABS_GRAD_SCREEN if self._abs_grad_screen else _native.GF_ABS_GRAD_WORLD
         with torch.cuda.device(device):
             end = self._timed("backward_render", device)
             check(self._lib.gf_tracer_trace_bwd(self._handle, ctypes.byref(inp), ctypes.byref(g), _stream(device)),
                   "trace_bwd")
             if end is not None:
                 end.record(torch.cuda.current_stream(device))
+        # splatRaster.cpp:628-637: the statistic of this backward
+        if self._abs_grad_screen:
+            self._last_abs_grad = None if abs_grad is None else abs_grad[:, 6:8].contiguous()
+            self._abs_workspace = None
+        else:
+            self._last_abs_grad = abs_grad
         return grad_particles, grad_features
+
+    # ------------------------------------------------------------------ densification statistic
+    def _abs_grad_buffer(self, n: int, device) -> torch.Tensor | None:
+        """The statistic's buffer for a backward over n particles
+        (splatRaster.cpp:515-531): the armed [N,8] map workspace in screen
+        mode (None when unarmed), a zeroed [N,3] in world mode."""
+        if not self._abs_grad_screen:
+            return torch.zeros((n, 3), dtype=torch.float32, device=device)
+        w = self._abs_workspace
+        if w is None:
+            return None
+        if w.device != device or w.dim() != 2 or w.shape[0] != n or w.shape[1] != 8:
+            raise RuntimeError("exact screen AbsGrad workspace differs")
+        return w
+
+    def set_exact_screen_absgrad_map(self, mapping: torch.Tensor) -> None:
+        """splatRaster.cpp:688-698: arms the next backward with the per-particle
+        2x3 map M (float32 [N,2,3] on the device); that backward adds, for every
+        composited hit, |M g| of the hit's position gradient g to the
+        particle's two sums, which collect_abs_grad() then returns."""
+        if not self._abs_grad_screen:
+            raise RuntimeError("set_exact_screen_absgrad_map needs strategy.densify.generic_camera_absgrad")
+        if not (torch.is_tensor(mapping) and mapping.is_cuda and mapping.dtype == torch.float32
+                and mapping.is_contiguous() and mapping.dim() == 3 and mapping.shape[1] == 2 and mapping.shape[2] == 3):
+            raise RuntimeError("exact screen AbsGrad map must be contiguous CUDA float32 [N,2,3]")
+        if self._abs_workspace is not None:
+            raise RuntimeError("exact screen AbsGrad map was armed twice before backward")
+        w = torch.zeros((mapping.shape[0], 8), dtype=torch.float32, device=mapping.device)
+        w[:, 0:6].copy_(mapping.reshape(mapping.shape[0], 6))
+        self._abs_workspace = w
+
+    def collect_abs_grad(self) -> torch.Tensor | None:
+        """splatRaster.cpp:642-650: the statistic of the last backward, [N,2]
+        in screen mode (raises if that backward was not armed), [N,3] in
+        world mode."""
+        last = self._last_abs_grad
+        if self._abs_grad_screen and (last is None or last.dim() != 2 or last.shape[1] != 2):
+            raise RuntimeError("exact screen AbsGrad was not armed for the last backward")
+        return last
 
     # (value, gradient) pairs of trace_bwd in the reference's order (splatRaster.cpp:469-500) and their
     # channel widths; of the quantile channels only the exact crossing depth (channel 8) carries a

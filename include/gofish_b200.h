@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define GF_ABI_VERSION 6
+#define GF_ABI_VERSION 7
 
 #define GF_OK 0
 #define GF_ERR_BAD_INPUT (-1)
@@ -199,7 +199,19 @@ typedef struct gf_trace_grads {
      * (gaussianParticles.cuh:934-986, rayPayloadBackward.cuh:122-128); the other
      * channels carry no gradient.  NULL: no crossing gradient. */
     const float* grad_quant;
+    /* Densification statistic (splatRaster.cpp:515-531,628-649 with
+     * gutKBufferRenderer.cuh:283-296; read by threedgrut/strategy/gs.py:88-96,
+     * 306-313): for every composited hit, the absolute value of that hit's
+     * position gradient, summed per particle.  NULL: not accumulated.
+     * GF_ABS_GRAD_SCREEN: [N,8] floats, slots 0-5 the caller's map M (2x3
+     * row-major) of the particle, slots 6 and 7 += |M[0,:] g| and |M[1,:] g|.
+     * GF_ABS_GRAD_WORLD: [N,3] floats += |g_x|, |g_y|, |g_z|. */
+    float* position_abs_grad;
+    int32_t position_abs_grad_mode;
 } gf_trace_grads;
+
+#define GF_ABS_GRAD_SCREEN 1
+#define GF_ABS_GRAD_WORLD 2
 
 /* Counters of the last forward pass. */
 typedef struct gf_trace_stats {

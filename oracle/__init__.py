@@ -132,6 +132,7 @@ def load():
         "oracle_atan2d": (ctypes.c_double, [ctypes.c_double, ctypes.c_double]),
         "oracle_set_tile_list": (None, [vp, i32]),
         "oracle_set_complete_admission": (None, [i32]),
+        "oracle_set_abs_grad": (None, [vp, vp, i32]),
         "oracle_set_admission_variants": (None, [ctypes.c_float, i32, ctypes.c_float, ctypes.c_float]),
         "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
@@ -381,6 +382,31 @@ class complete_admission:
 
     def __exit__(self, *exc):
         load().oracle_set_complete_admission(0)
+        return False
+
+
+class abs_grad:
+    """Context in which render_backward / render_backward_geo accumulate the
+    densification statistic (gutKBufferRenderer.cuh:54-60,283-296): for every
+    composited hit, |M g| of its position gradient g with the per-particle
+    map M ([N,2,3], mode "screen", sums [N,2]) or |g| (mode "world", [N,3]).
+    The sums are in ``.out`` after the block."""
+
+    def __init__(self, n: int, mode: str, mapping=None):
+        if mode not in ("screen", "world"):
+            raise ValueError("abs_grad mode must be 'screen' or 'world'")
+        self.mode = 1 if mode == "screen" else 2
+        self.map = None if mapping is None else np.ascontiguousarray(np.asarray(mapping, np.float32).reshape(n, 6))
+        if self.mode == 1 and self.map is None:
+            raise ValueError("screen mode needs the [N,2,3] map")
+        self.out = np.zeros((n, 2 if self.mode == 1 else 3), np.float32)
+
+    def __enter__(self):
+        load().oracle_set_abs_grad(_po(self.map), _p(self.out), self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        load().oracle_set_abs_grad(None, None, 0)
         return False
 
 

@@ -126,6 +126,37 @@ void parallel_for(int begin, int end, int chunk, Fn&& fn) {
 // density >= 1/255 is admitted by the conservative cone test of its support
 // sphere, none by its projected footprint.
 bool g_completeAdmission = false;
+// Densification statistic of oracle_render_backward(_geo) (oracle_set_abs_grad):
+// map [N,6] (screen mode) or NULL, sums [N,2] / [N,3], mode 1 screen, 2 world, 0 off.
+const float* g_absMap = nullptr;
+float* g_absOut = nullptr;
+int g_absMode = 0;
+
+// Adds |M g| (screen) or |g| (world) of one hit's position gradient g to the
+// worker's partial sums (gutKBufferRenderer.cuh:54-60,283-296).
+inline void abs_grad_hit(std::vector<float>& partial, int N, uint32_t idx, float gx, float gy, float gz) {
+    if (g_absMode == 0) return;
+    const int width = g_absMode == 1 ? 2 : 3;
+    if (partial.empty()) partial.assign(size_t(N) * width, 0.0f);
+    float* o = partial.data() + size_t(idx) * width;
+    if (g_absMode == 1) {
+        const float* row = g_absMap + size_t(idx) * 6;
+        o[0] += std::fabs(row[0] * gx + row[1] * gy + row[2] * gz);
+        o[1] += std::fabs(row[3] * gx + row[4] * gy + row[5] * gz);
+    } else {
+        o[0] += std::fabs(gx);
+        o[1] += std::fabs(gy);
+        o[2] += std::fabs(gz);
+    }
+}
+
+void abs_grad_reduce(const std::vector<std::vector<float>>& partial, int N) {
+    if (g_absMode == 0) return;
+    const size_t count = size_t(N) * (g_absMode == 1 ? 2 : 3);
+    for (const auto& p : partial)
+        if (!p.empty())
+            for (size_t i = 0; i < count; ++i) g_absOut[i] += p[i];
+}
 // Partial UT covariance scale (oracle_set_admission_variants; 0 = off) and
 // the cone_big fallback window on the caps' sines.
 float g_partialUtScale2 = 0.0f;
@@ -151,6 +182,15 @@ extern "C" {
 
 // Selects (1) or clears (0) complete admission for oracle_project / oracle_bin.
 void oracle_set_complete_admission(int complete) { g_completeAdmission = complete != 0; }
+
+// Arms (mode 1: screen, map [N,6]; mode 2: world) or clears (0) the
+// densification statistic of oracle_render_backward(_geo): each composited
+// hit adds |M g| or |g| of its position gradient g to out ([N,2] / [N,3]).
+void oracle_set_abs_grad(const float* map, float* out, int mode) {
+    g_absMap = map;
+    g_absOut = out;
+    g_absMode = (out != nullptr && (mode == 2 || (mode == 1 && map != nullptr))) ? mode : 0;
+}
 
 // Partial UT (partialScale2 = scale^2 > 0, 0 = off) and the cone_big window
 // (coneBig != 0; the caps' sine bounds) of oracle_project / oracle_bin.
@@ -1658,6 +1698,7 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
     Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
     const int nthreads = worker_count();
     std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads));
+    std::vector<std::vector<float>> absPartial(static_cast<size_t>(nthreads));
     {
         parallel_tiles(tileBegin, tileEnd, [&](int tile, int tid) {
             std::vector<float>& acc = partial[size_t(tid)];
@@ -1731,9 +1772,13 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
                                 }
                                 // position: -(Binv^T groGrd); Binv rows: += groGrd[i] gposc + grduGrd[i] d
                                 const float* M = P.Binv;
-                                g[0] -= groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6];
-                                g[1] -= groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7];
-                                g[2] -= groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8];
+                                const float px = -(groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6]);
+                                const float py = -(groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7]);
+                                const float pz = -(groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8]);
+                                g[0] += px;
+                                g[1] += py;
+                                g[2] += pz;
+                                abs_grad_hit(absPartial[size_t(tid)], N, hh.idx, px, py, pz);
                                 const float3_ gposc = sub(ray.o, P.pos);
                                 const float gr[3] = {groGrd.x, groGrd.y, groGrd.z};
                                 const float gd[3] = {grduGrd.x, grduGrd.y, grduGrd.z};
@@ -1758,6 +1803,7 @@ int oracle_render_backward(const OracleCamera* cam, const OraclePose* pose, int 
         const float* a = partial[size_t(t)].data();
         for (size_t i = 0; i < size_t(N) * 16; ++i) gradRecord[i] += a[i];
     }
+    abs_grad_reduce(absPartial, N);
     return 0;
 }
 
@@ -1781,6 +1827,7 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
     Scene sc{cam, pose, N, particles, rgb, rayO, rayD, mask, ranges, sortedIds, K};
     const int nthreads = worker_count();
     std::vector<std::vector<float>> partial(static_cast<size_t>(nthreads)), partialShape(static_cast<size_t>(nthreads));
+    std::vector<std::vector<float>> absPartial(static_cast<size_t>(nthreads));
     const auto val = [](const float* p, size_t i) { return p != nullptr ? p[i] : 0.0f; };
     parallel_tiles(tileBegin, tileEnd, [&](int tile, int tid) {
         std::vector<float>& acc = partial[size_t(tid)];
@@ -1949,9 +1996,13 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
                             }
                             groGrd = add(groGrd, groCross);
                             grduGrd = add(grduGrd, grduCross);
-                            g[0] -= groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6];
-                            g[1] -= groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7];
-                            g[2] -= groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8];
+                            const float px = -(groGrd.x * M[0] + groGrd.y * M[3] + groGrd.z * M[6]);
+                            const float py = -(groGrd.x * M[1] + groGrd.y * M[4] + groGrd.z * M[7]);
+                            const float pz = -(groGrd.x * M[2] + groGrd.y * M[5] + groGrd.z * M[8]);
+                            g[0] += px;
+                            g[1] += py;
+                            g[2] += pz;
+                            abs_grad_hit(absPartial[size_t(tid)], N, hh.idx, px, py, pz);
                             const float3_ gposc = sub(ray.o, P.pos);
                             const float gr[3] = {groGrd.x, groGrd.y, groGrd.z};
                             const float gd[3] = {grduGrd.x, grduGrd.y, grduGrd.z};
@@ -1982,6 +2033,7 @@ int oracle_render_backward_geo(const OracleCamera* cam, const OraclePose* pose, 
             for (size_t i = 0; i < size_t(N) * 8; ++i) gradShape[i] += a[i];
         }
     }
+    abs_grad_reduce(absPartial, N);
     return 0;
 }
 

@@ -45,8 +45,10 @@
 // hit count), float32[19] forward B (rgb, opacity, hit distance, normal xyz,
 // sum w t^2, extent, inverse depth, inverse depth squared, seven quantile
 // depths) + float32[2] (exact crossing depth, its rate); per tile and
-// particle float32[32] particle gradient (ParticleDensity layout) and
-// float32[3] colour gradient.
+// particle float32[32] particle gradient (ParticleDensity layout),
+// float32[3] colour gradient and float32[3] sum over its hits of the absolute
+// values of the hit's position gradient (the world-space densification
+// statistic).
 
 #include "cuda_host_shim.h"
 
@@ -134,6 +136,7 @@ int main(int argc, char** argv) {
         for (auto& c : colours) c = make_float3(fmaxf(c.x, 0.0f), fmaxf(c.y, 0.0f), fmaxf(c.z, 0.0f));
         std::vector<threedgut::ParticleDensity> gradSum(static_cast<size_t>(count));
         std::vector<float3> colourGradSum(size_t(count), make_float3(0.0f, 0.0f, 0.0f));
+        std::vector<float3> absSum(size_t(count), make_float3(0.0f, 0.0f, 0.0f));
         memset(gradSum.data(), 0, sizeof(threedgut::ParticleDensity) * size_t(count));
 
         for (int r = 0; r < raysPerTile; ++r) {
@@ -210,6 +213,10 @@ int main(int argc, char** argv) {
                 float* dst = reinterpret_cast<float*>(&gradSum[size_t(i)]);
                 const float* src = reinterpret_cast<const float*>(&g);
                 for (int k = 0; k < 32; ++k) dst[k] += src[k];
+                // the world-space densification statistic (gutKBufferRenderer.cuh:290-294)
+                absSum[size_t(i)].x += fabsf(g.position.x);
+                absSum[size_t(i)].y += fabsf(g.position.y);
+                absSum[size_t(i)].z += fabsf(g.position.z);
                 colourGradSum[size_t(i)].x += colourGrad[0];
                 colourGradSum[size_t(i)].y += colourGrad[1];
                 colourGradSum[size_t(i)].z += colourGrad[2];
@@ -225,6 +232,7 @@ int main(int argc, char** argv) {
         }
         fwrite(gradSum.data(), sizeof(threedgut::ParticleDensity), size_t(count), out);
         fwrite(colourGradSum.data(), sizeof(float3), size_t(count), out);
+        fwrite(absSum.data(), sizeof(float3), size_t(count), out);
     }
     fclose(out);
     fclose(in);

@@ -207,7 +207,7 @@ def main(reference: Path) -> None:
 
     sh_dirs, sh_coeffs, sh_rgb = sh_goldens(rng)
     counts = np.array([t[0].shape[0] for t in tiles], np.int32)
-    fwd_a, fwd_b, grad, grad_rgb = [], [], [], []
+    fwd_a, fwd_b, grad, grad_rgb, abs_world = [], [], [], [], []
     at = 0
     for (rows, _c, _r, _g), m in zip(tiles, counts):
         per_ray = out[at:at + RAYS * 27].reshape(RAYS, 27)
@@ -217,6 +217,8 @@ def main(reference: Path) -> None:
         grad.append(out[at:at + m * 32].reshape(m, 32))
         at += m * 32
         grad_rgb.append(out[at:at + m * 3].reshape(m, 3))
+        at += m * 3
+        abs_world.append(out[at:at + m * 3].reshape(m, 3))
         at += m * 3
     assert at == out.size, (at, out.size)
     np.savez_compressed(
@@ -230,6 +232,7 @@ def main(reference: Path) -> None:
         fwd_b=np.stack(fwd_b),
         grad=np.concatenate(grad),
         grad_rgb=np.concatenate(grad_rgb),
+        abs_world=np.concatenate(abs_world),
         sh_dirs=sh_dirs,
         sh_coeffs=sh_coeffs,
         sh_rgb=sh_rgb,

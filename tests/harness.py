@@ -82,9 +82,11 @@ class GpuTracer:
     """The product path: SplatRaster over the C ABI on one CUDA device."""
 
     def __init__(self, case: Case, k: int, key_mode: int, device, fallback: bool = True, log_capacity: int = 0,
-                 enable_normals: bool = False, complete: bool = False, gofish: dict | None = None):
+                 enable_normals: bool = False, complete: bool = False, gofish: dict | None = None,
+                 strategy: dict | None = None):
         """k: k-buffer size, or oracle.SOF_HIERARCHY for SOF's hierarchy;
-        ``gofish``: further render.gofish keys."""
+        ``gofish``: further render.gofish keys; ``strategy``: the configuration's
+        strategy section."""
         import torch
 
         from gofish_b200.splat_raster import SplatRaster
@@ -98,7 +100,8 @@ class GpuTracer:
                            "gofish": {"fast_global_depth_key": key_mode == 1,
                                       "fast_admission_fallback": "cone" if fallback else "none",
                                       "complete_admission": complete, **(gofish or {})},
-                           "enable_hitcounts": True, "enable_normals": enable_normals}}
+                           "enable_hitcounts": True, "enable_normals": enable_normals},
+                "strategy": strategy or {}}
         self.raster = SplatRaster(conf)
         self.token = "test-token"
         self.raster.register_physical_tile_mask(torch.from_numpy(case.tmask).to(device), self.token)

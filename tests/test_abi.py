@@ -33,7 +33,7 @@ def test_ctypes_binding_covers_the_header():
 
 def test_library_loads_and_reports_abi_version():
     lib = _native.load()
-    assert lib.gf_abi_version() == 6
+    assert lib.gf_abi_version() == _native.ABI_VERSION == 7
 
 
 def test_create_rejects_bad_configuration():
@@ -51,3 +51,34 @@ def test_create_rejects_bad_configuration():
     handle = lib.gf_tracer_create(ctypes.byref(cfg))
     assert handle
     lib.gf_tracer_destroy(handle)
+
+
+def test_ctypes_structures_match_the_header_layout(tmp_path):
+    """Size and field offsets of every ctypes mirror equal those of the C
+    struct in include/gofish_b200.h (compiled here with gcc)."""
+    import ctypes
+    import subprocess
+    from pathlib import Path
+
+    mirrors = {"gf_camera": _native.GfCamera, "gf_tracer_config": _native.GfTracerConfig,
+               "gf_trace_inputs": _native.GfTraceInputs, "gf_trace_outputs": _native.GfTraceOutputs,
+               "gf_trace_grads": _native.GfTraceGrads, "gf_trace_stats": _native.GfTraceStats,
+               "gf_field_camera": _native.GfFieldCamera, "gf_field_stats": _native.GfFieldStats,
+               "gf_shape_camera": _native.GfShapeCamera}
+    header = Path(__file__).resolve().parents[1] / "include" / "gofish_b200.h"
+    lines = ['#include <stddef.h>', '#include <stdio.h>', f'#include "{header}"', "int main(void) {"]
+    for cname, mirror in mirrors.items():
+        lines.append(f'    printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, *_ in mirror._fields_:
+            lines.append(f'    printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["    return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(line.split()[:2]): int(line.split()[2]) for line in out if line}
+    for cname, mirror in mirrors.items():
+        assert got[(cname, "size")] == ctypes.sizeof(mirror), cname
+        for field, *_ in mirror._fields_:
+            assert got[(cname, field)] == getattr(mirror, field).offset, (cname, field)

@@ -165,3 +165,32 @@ def test_sh_radiance_matches_the_reference(golden):
         _proj, rgb, _counts = oracle.project(cam, pose, rows, golden["sh_coeffs"][degree], degree, mask)
         ref = np.maximum(golden["sh_rgb"][degree], 0.0)
         np.testing.assert_allclose(rgb, ref, rtol=1e-5, atol=2e-6, err_msg=f"SH degree {degree}")
+
+
+def test_world_abs_grad_matches_the_reference(golden):
+    """The densification statistic (gutKBufferRenderer.cuh:290-294): per
+    composited hit |g| of the hit's position gradient, summed per particle,
+    against the reference's processHitBwd per hit; and the screen form with
+    the map [[1,0,0],[0,1,0]] equals its first two components."""
+    for t, start, m, rows, colours in tiles(golden):
+        cam, pose, ray_o, ray_d, mask, ranges, ids = render_tile(golden, t, m, rows, colours)
+        fwd = golden_forward(golden, t)
+        gi = golden["grads"][t]
+        quant_grad = np.zeros((256, 10), np.float32)
+        quant_grad[:, 8] = gi[:, 12]
+        grads = dict(rgba=gi[:, 0:4].reshape(16, 16, 4), hit_t=gi[:, 4].reshape(16, 16),
+                     normal=gi[:, 5:8].reshape(16, 16, 3), depth_var=gi[:, 8].reshape(16, 16),
+                     extent=gi[:, 9].reshape(16, 16), inv_depth=gi[:, 10].reshape(16, 16),
+                     inv_depth2=gi[:, 11].reshape(16, 16), quant=quant_grad.reshape(16, 16, 10))
+        with oracle.abs_grad(m, "world") as world:
+            oracle.render_backward_geo(cam, pose, rows, colours, ray_o, ray_d, mask, ranges, ids, 0, fwd, grads)
+        ref = golden["abs_world"][start:start + m]
+        assert (ref >= 0).all()
+        err = rel_l2(world.out, ref)
+        assert err < REL_L2_GRAD, f"tile {t}: world abs-grad rel L2 {err:.2e}"
+        mapping = np.zeros((m, 2, 3), np.float32)
+        mapping[:, 0, 0] = 1.0
+        mapping[:, 1, 1] = 1.0
+        with oracle.abs_grad(m, "screen", mapping) as screen:
+            oracle.render_backward_geo(cam, pose, rows, colours, ray_o, ray_d, mask, ranges, ids, 0, fwd, grads)
+        np.testing.assert_array_equal(screen.out, world.out[:, 0:2])

@@ -178,8 +178,11 @@ class ClockSampler:
 
     def start(self):
         try:
+            # every 200 ms: sampling every 50 ms stretched some timed regions (host stalls of
+            # tens of milliseconds inside CUDA calls while the query ran; 305-313 against 312-313
+            # Mpix/s over four runs each)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None

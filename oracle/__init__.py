@@ -133,6 +133,7 @@ def load():
         "oracle_set_tile_list": (None, [vp, i32]),
         "oracle_set_complete_admission": (None, [i32]),
         "oracle_set_abs_grad": (None, [vp, vp, i32]),
+        "oracle_project_points": (i32, [cam_p, i32, vp, vp, vp]),
         "oracle_set_admission_variants": (None, [ctypes.c_float, i32, ctypes.c_float, ctypes.c_float]),
         "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
@@ -201,6 +202,16 @@ def project(cam, pose, particles, sh, sh_degree, mask, ray_d=None):
     lib.oracle_project(ctypes.byref(cam), ctypes.byref(pose), n, _p(particles), _p(sh), sh.shape[1] // 3,
                        int(sh_degree), _p(mask), _po(ray_d), _p(proj), _p(rgb), _p(counts))
     return proj, rgb, counts
+
+
+def project_points(cam, points):
+    """Sensor-space projection of [n,3] points without raster bounds:
+    (uv [n,2] float32, valid [n] bool)."""
+    pts = np.ascontiguousarray(points, dtype=np.float32).reshape(-1, 3)
+    uv = np.zeros((pts.shape[0], 2), np.float32)
+    valid = np.zeros(pts.shape[0], np.uint8)
+    load().oracle_project_points(ctypes.byref(cam), pts.shape[0], _p(pts), _p(uv), _p(valid))
+    return uv, valid.astype(bool)
 
 
 def tile_rays(cam, pose, ray_o, ray_d):

@@ -331,6 +331,28 @@ bool project_world(const OracleCamera& cam, const OraclePose& pose, float3_ pw, 
     return project_pinhole(cam, ps, out);
 }
 
+}  // namespace
+
+extern "C" {
+
+// Sensor-space point projection of the camera (pinhole or fisheye, without
+// raster bounds, as the UT uses it): uv[n*2], valid[n].
+int oracle_project_points(const OracleCamera* cam, int n, const float* pts, float* uv, uint8_t* valid) {
+    for (int i = 0; i < n; ++i) {
+        const float3_ p = f3(pts[3 * i], pts[3 * i + 1], pts[3 * i + 2]);
+        float2_ o{0.0f, 0.0f};
+        const bool ok = cam->model == 1 ? project_fisheye(*cam, p, o) : project_pinhole(*cam, p, o);
+        uv[2 * i] = o.x;
+        uv[2 * i + 1] = o.y;
+        valid[i] = ok ? 1u : 0u;
+    }
+    return 0;
+}
+
+}  // extern "C"
+
+namespace {
+
 // Packed particle row accessors, tracer.py:171-179 / inference.py:43-47.
 struct Particle {
     float3_ pos;

@@ -4,6 +4,9 @@
 // checkout>` into oracle/_ref/, run by tests/golden/make_hit_golden.py).
 //
 // It includes, unmodified, the reference headers
+//   threedgut_tracer/include/3dgut/kernels/cuda/sensors/cameraProjections.cuh
+//   (projectPoint, with sensors.h and cameraModels.h over the vector types of
+//   tiny-cuda-nn/vec.h here)
 //   threedgut_tracer/include/3dgut/kernels/cuda/models/gaussianParticles.cuh
 //   (processHitFwd :611-686, processHitBwd :736-1155,
 //    particleExactDepthCrossingRaw :592-609,
@@ -53,6 +56,7 @@
 #include "cuda_host_shim.h"
 
 #include <3dgut/kernels/cuda/models/gaussianParticles.cuh>
+#include <3dgut/kernels/cuda/sensors/cameraProjections.cuh>
 
 #include <cstdio>
 #include <cstdlib>
@@ -113,8 +117,51 @@ int run_sh(const char* inPath, const char* outPath) {
     return 0;
 }
 
+// `project` mode: the sensor-space point projection of the UT sigma points,
+// projectPoint of cameraProjections.cuh:75-122 (OpenCV pinhole) and :124-152
+// (OpenCV fisheye / Kannala-Brandt) with requireRasterBounds = false, as
+// gutProjector.cuh calls it.  Input: int32 count, int32 model (0 pinhole, 1
+// fisheye), int32 width, int32 height, float32 principal[2], focal[2],
+// radial[6], tangential[2], thin_prism[4], max_angle, tolerance, then per point
+// float32[3]; output per point float32 u, v, valid (0 or 1).
+int run_project(const char* inPath, const char* outPath) {
+    FILE* in = fopen(inPath, "rb");
+    if (in == nullptr) return 3;
+    int32_t head[4];
+    float cam[18];
+    if (!read_all(in, head, sizeof(head)) || !read_all(in, cam, sizeof(cam))) return 4;
+    FILE* out = fopen(outPath, "wb");
+    if (out == nullptr) return 5;
+    threedgut::OpenCVPinholeProjectionParameters pin{};
+    threedgut::OpenCVFisheyeProjectionParameters fish{};
+    pin.principalPoint = tcnn::vec2(cam[0], cam[1]);
+    pin.focalLength = tcnn::vec2(cam[2], cam[3]);
+    for (int i = 0; i < 6; ++i) pin.radialCoeffs[i] = cam[4 + i];
+    pin.tangentialCoeffs = tcnn::vec2(cam[10], cam[11]);
+    pin.thinPrismCoeffs = tcnn::vec4(cam[12], cam[13], cam[14], cam[15]);
+    fish.principalPoint = pin.principalPoint;
+    fish.focalLength = pin.focalLength;
+    for (int i = 0; i < 4; ++i) fish.radialCoeffs[i] = cam[4 + i];
+    fish.maxAngle = cam[16];
+    const tcnn::ivec2 resolution(head[2], head[3]);
+    for (int i = 0; i < head[0]; ++i) {
+        float p[3];
+        if (!read_all(in, p, sizeof(p))) return 6;
+        tcnn::vec2 uv;
+        const tcnn::vec3 position(p[0], p[1], p[2]);
+        const bool valid = head[1] == 1 ? threedgut::projectPoint(fish, resolution, position, cam[17], uv, false)
+                                        : threedgut::projectPoint(pin, resolution, position, cam[17], uv, false);
+        const float rec[3] = {uv.x, uv.y, valid ? 1.0f : 0.0f};
+        fwrite(rec, sizeof(float), 3, out);
+    }
+    fclose(out);
+    fclose(in);
+    return 0;
+}
+
 int main(int argc, char** argv) {
     if (argc == 4 && strcmp(argv[1], "sh") == 0) return run_sh(argv[2], argv[3]);
+    if (argc == 4 && strcmp(argv[1], "project") == 0) return run_project(argv[2], argv[3]);
     if (argc != 3) {
         fprintf(stderr, "usage: %s input.bin output.bin | %s sh input.bin output.bin\n", argv[0], argv[0]);
         return 2;

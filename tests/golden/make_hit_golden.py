@@ -13,7 +13,9 @@ into oracle/_ref/hit_pin_driver (see the driver's header for what it runs).
 
 It also records the projector's particle radiance, radianceFromSpH
 (gaussianParticles.cuh:188-220, unclamped as gutProjector.cuh:903 calls it),
-at SH degrees 0 to 3.
+at SH degrees 0 to 3, and the sensor-space point projection projectPoint
+(cameraProjections.cuh:75-152, without raster bounds as the UT calls it) of
+three fisheye cameras and a distorted pinhole.
 
 Inputs (seeded): tiles of 16x16 rays, each tile with its own ordered list
 of 6 to 48 Gaussians (random rotation, log-normal scales, opacities up to 1
@@ -29,6 +31,7 @@ evaluations of the reference and of this library take the same branches.
 
 from __future__ import annotations
 
+import math
 import subprocess
 import sys
 import tempfile
@@ -167,6 +170,56 @@ def sh_goldens(rng: np.random.Generator, items: int = 512):
     return dirs, coeffs, rgb
 
 
+# Cameras of the projection goldens: model, width, height, principal, focal,
+# radial[6], tangential[2], thin prism[4], max angle (rad): an equidistant and
+# a Kannala-Brandt 200 deg fisheye, the equisolid 205 deg one (its 4-term
+# Taylor series), and a distorted pinhole.
+PROJECTION_CAMERAS = (
+    (1, 320, 320, (160.0, 160.0), (91.67, 91.67), (0.0, 0.0, 0.0, 0.0, 0.0, 0.0), (0.0, 0.0), (0.0,) * 4,
+     1.7453293),
+    (1, 1600, 1600, (799.5, 800.5), (452.0, 455.0), (0.021, -0.012, 0.0031, -0.0004, 0.0, 0.0), (0.0, 0.0),
+     (0.0,) * 4, 1.7453293),
+    (1, 2560, 2560, (1280.0, 1280.0), (716.0, 716.0),
+     (-1.0 / 24.0, 1.0 / 1920.0, -1.0 / 322560.0, 1.0 / 92897280.0, 0.0, 0.0), (0.0, 0.0), (0.0,) * 4, 1.7889625),
+    (0, 640, 480, (321.5, 239.0), (500.0, 498.0), (0.11, -0.05, 0.012, 0.021, -0.011, 0.004), (0.0012, -0.0021),
+     (1e-4, -2e-4, 3e-4, -1e-4), 3.1415927),
+)
+
+
+def projection_goldens(rng: np.random.Generator, points: int = 4096):
+    """The reference's projectPoint for each camera of PROJECTION_CAMERAS at
+    seeded points: directions over the whole sphere at 0.05-50 m, points on
+    and near the optical axis and behind the camera; directions within 1e-4
+    rad of the maximum angle are redrawn (the validity there depends on the
+    last bit of atan2).  Returns ([C, P, 3] points, [C, P, 3] u, v, valid)."""
+    all_pts, all_out = [], []
+    with tempfile.TemporaryDirectory() as tmp:
+        for model, w, h, pp, f, k, tg, tp, max_angle in PROJECTION_CAMERAS:
+            pts = np.zeros((points, 3), np.float64)
+            i = 0
+            while i < points:
+                d = rng.standard_normal(3)
+                d /= np.linalg.norm(d)
+                theta = math.atan2(math.hypot(d[0], d[1]), d[2])
+                if abs(theta - max_angle) < 1e-4:
+                    continue
+                pts[i] = d * math.exp(rng.uniform(math.log(0.05), math.log(50.0)))
+                i += 1
+            pts[:8] = [[0, 0, 1], [0, 0, 3.5], [0, 0, -2], [1e-20, 0, 1], [0, -1e-20, 2], [1e-3, 2e-3, 1],
+                       [0.5, -0.25, 1e-7], [3.0, 4.0, 0.0]]
+            pts = pts.astype(np.float32)
+            src, dst = Path(tmp) / "pr.bin", Path(tmp) / "pr.out"
+            cam = np.array([*pp, *f, *k, *tg, *tp, max_angle, 0.1], np.float32)
+            with open(src, "wb") as fh:
+                fh.write(np.array([points, model, w, h], np.int32).tobytes())
+                fh.write(cam.tobytes())
+                fh.write(pts.tobytes())
+            subprocess.run([str(DRIVER), "project", str(src), str(dst)], check=True)
+            all_pts.append(pts)
+            all_out.append(np.fromfile(dst, dtype=np.float32).reshape(points, 3))
+    return np.stack(all_pts), np.stack(all_out)
+
+
 def main(reference: Path) -> None:
     subprocess.run(["make", "-C", str(REPO / "oracle"), "ref", f"REF={reference}"], check=True)
     rng = np.random.default_rng(20261202)
@@ -206,6 +259,7 @@ def main(reference: Path) -> None:
         out = np.fromfile(dst, dtype=np.float32)
 
     sh_dirs, sh_coeffs, sh_rgb = sh_goldens(rng)
+    proj_points, proj_out = projection_goldens(rng)
     counts = np.array([t[0].shape[0] for t in tiles], np.int32)
     fwd_a, fwd_b, grad, grad_rgb, abs_world = [], [], [], [], []
     at = 0
@@ -236,6 +290,8 @@ def main(reference: Path) -> None:
         sh_dirs=sh_dirs,
         sh_coeffs=sh_coeffs,
         sh_rgb=sh_rgb,
+        proj_points=proj_points,
+        proj_out=proj_out,
     )
     print(f"{TILES} tiles x {RAYS} rays, {int(counts.sum())} Gaussians; "
           f"hits per ray {float(np.stack(fwd_a)[..., 5].mean()):.2f}, "

@@ -194,3 +194,24 @@ def test_world_abs_grad_matches_the_reference(golden):
         with oracle.abs_grad(m, "screen", mapping) as screen:
             oracle.render_backward_geo(cam, pose, rows, colours, ray_o, ray_d, mask, ranges, ids, 0, fwd, grads)
         np.testing.assert_array_equal(screen.out, world.out[:, 0:2])
+
+
+def test_point_projection_matches_the_reference(golden):
+    """The sensor-space projection of the UT's sigma points (projectPoint,
+    cameraProjections.cuh:75-152, without raster bounds) against the oracle's,
+    for three fisheye cameras (equidistant, Kannala-Brandt, equisolid 205 deg)
+    and a distorted pinhole, over the whole sphere: validity exactly, pixel
+    coordinates within 1e-5 relative + 1e-3 px (the oracle's atan2 is within
+    2.5 ulp of the C library's)."""
+    from tests.golden.make_hit_golden import PROJECTION_CAMERAS
+
+    for c, (model, w, h, pp, f, k, tg, tp, max_angle) in enumerate(PROJECTION_CAMERAS):
+        cam = oracle.camera(model, w, h, pp, f, k, max_angle, tangential=tg, thin_prism=tp)
+        pts = golden["proj_points"][c]
+        ref = golden["proj_out"][c]
+        uv, valid = oracle.project_points(cam, pts)
+        assert np.array_equal(valid, ref[:, 2] == 1.0), f"camera {c}: validity differs"
+        assert valid.sum() > 1000 and (~valid).sum() > 100
+        finite = np.isfinite(ref[:, :2]).all(axis=1)
+        assert np.array_equal(finite, np.isfinite(uv).all(axis=1)), f"camera {c}"
+        np.testing.assert_allclose(uv[finite], ref[finite, :2], rtol=1e-5, atol=1e-3, err_msg=f"camera {c}")

@@ -134,6 +134,7 @@ def load():
         "oracle_set_complete_admission": (None, [i32]),
         "oracle_set_abs_grad": (None, [vp, vp, i32]),
         "oracle_project_points": (i32, [cam_p, i32, vp, vp, vp]),
+        "oracle_kbuffer_order": (i32, [i32, i32, vp, vp]),
         "oracle_set_admission_variants": (None, [ctypes.c_float, i32, ctypes.c_float, ctypes.c_float]),
         "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
@@ -202,6 +203,16 @@ def project(cam, pose, particles, sh, sh_degree, mask, ray_d=None):
     lib.oracle_project(ctypes.byref(cam), ctypes.byref(pose), n, _p(particles), _p(sh), sh.shape[1] // 3,
                        int(sh_degree), _p(mask), _po(ray_d), _p(proj), _p(rgb), _p(counts))
     return proj, rgb, counts
+
+
+def kbuffer_order(k: int, hit_t) -> np.ndarray:
+    """Composite order (hit indices) of a K-entry k-buffer fed the hit
+    distances ``hit_t`` in sequence."""
+    t = np.ascontiguousarray(hit_t, dtype=np.float32)
+    order = np.zeros(t.size, np.uint32)
+    if load().oracle_kbuffer_order(int(k), int(t.size), _p(t), _p(order)) != 0:
+        raise ValueError("k-buffer size must be 1..64")
+    return order
 
 
 def project_points(cam, points):

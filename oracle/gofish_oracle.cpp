@@ -335,6 +335,10 @@ bool project_world(const OracleCamera& cam, const OraclePose& pose, float3_ pw, 
 
 extern "C" {
 
+// Composite order of the k-buffer (KBuffer, fed as traverse() feeds it) for
+// hits i = 0..n-1 with distances hitT[i]: order[n] of hit indices.
+int oracle_kbuffer_order(int K, int n, const float* hitT, uint32_t* order);
+
 // Sensor-space point projection of the camera (pinhole or fisheye, without
 // raster bounds, as the UT uses it): uv[n*2], valid[n].
 int oracle_project_points(const OracleCamera* cam, int n, const float* pts, float* uv, uint8_t* valid) {
@@ -2800,3 +2804,17 @@ float oracle_atan2f(float y, float x) { return gf::gf_atan2f(y, x); }
 double oracle_atan2d(double y, double x) { return gf::gf_atan2d(y, x); }
 
 }  // extern "C"
+
+extern "C" int oracle_kbuffer_order(int K, int n, const float* hitT, uint32_t* order) {
+    if (K <= 0 || K > 64) return -1;
+    KBuffer kb;
+    kb.init(K);
+    int at = 0;
+    for (int i = 0; i < n; ++i) {
+        const Hit h{uint32_t(i), hitT[i], 0.5f};
+        if (kb.full()) order[at++] = kb.e[0].idx;
+        kb.insert(h);
+    }
+    for (uint32_t i = 0; i < kb.n; ++i) order[at++] = kb.e[K - kb.n + i].idx;
+    return 0;
+}

@@ -37,6 +37,39 @@ struct int3 { int x, y, z; };
 struct uint2 { unsigned x, y; };
 struct uint3 { unsigned x, y, z; };
 
+// The launch built-ins, as host variables a driver sets before calling
+// device code that reads them (one thread at a time).
+struct dim3 {
+    unsigned x = 0, y = 0, z = 0;
+};
+inline dim3 threadIdx, blockIdx, blockDim, gridDim;
+constexpr int warpSize = 32;
+#define __shared__ static
+#define __constant__ static
+
+// Block and warp intrinsics: declared only, so that the reference's kernel
+// templates parse; none is instantiated by the host drivers (a call would
+// fail to link).
+void __syncthreads();
+int __syncthreads_and(int);
+int __syncthreads_or(int);
+int __syncthreads_count(int);
+void __syncwarp(unsigned = 0xffffffffu);
+int __all_sync(unsigned, int);
+int __any_sync(unsigned, int);
+unsigned __ballot_sync(unsigned, int);
+unsigned __activemask();
+template <typename T> T __shfl_sync(unsigned, T, int, int = 32);
+template <typename T> T __shfl_up_sync(unsigned, T, unsigned, int = 32);
+template <typename T> T __shfl_down_sync(unsigned, T, unsigned, int = 32);
+template <typename T> T __shfl_xor_sync(unsigned, T, int, int = 32);
+template <typename T> unsigned __match_any_sync(unsigned, T);
+int __ffs(int);
+int __popc(unsigned);
+int __clz(int);
+using std::max;
+using std::min;
+
 inline float2 make_float2(float x, float y) { return {x, y}; }
 inline float3 make_float3(float x, float y, float z) { return {x, y, z}; }
 inline float4 make_float4(float x, float y, float z, float w) { return {x, y, z, w}; }

@@ -7,6 +7,8 @@
 //   threedgut_tracer/include/3dgut/kernels/cuda/sensors/cameraProjections.cuh
 //   (projectPoint, with sensors.h and cameraModels.h over the vector types of
 //   tiny-cuda-nn/vec.h here)
+//   threedgut_tracer/include/3dgut/kernels/cuda/renderers/gutKBufferRenderer.cuh
+//   (HitParticleKBufferT :118-166; its kernel templates are parsed, not used)
 //   threedgut_tracer/include/3dgut/kernels/cuda/models/gaussianParticles.cuh
 //   (processHitFwd :611-686, processHitBwd :736-1155,
 //    particleExactDepthCrossingRaw :592-609,
@@ -57,6 +59,7 @@
 
 #include <3dgut/kernels/cuda/models/gaussianParticles.cuh>
 #include <3dgut/kernels/cuda/sensors/cameraProjections.cuh>
+#include <3dgut/kernels/cuda/renderers/gutKBufferRenderer.cuh>
 
 #include <cstdio>
 #include <cstdlib>
@@ -159,7 +162,58 @@ int run_project(const char* inPath, const char* outPath) {
     return 0;
 }
 
+// `kbuffer` mode: the composite order of the k-buffer, the reference's
+// HitParticleKBufferT<K>::insert (gutKBufferRenderer.cuh:118-166) fed as
+// evalKBuffer feeds it (:676-699: when full, composite the closest entry,
+// then insert; at the end composite the held entries from the closest).
+// Input: int32 sequences, then per sequence int32 K, int32 n and n float32 hit
+// distances (hit i has id i); output per sequence the n ids in composite order.
+template <int K>
+void kbuffer_order(const float* hitT, int n, int32_t* order) {
+    ::HitParticleKBufferT<K, false> kb;
+    int at = 0;
+    for (int i = 0; i < n; ++i) {
+        ::HitParticleT<false> h;
+        h.idx = i;
+        h.hitT = hitT[i];
+        h.alpha = 0.5f;
+        if (kb.full()) order[at++] = kb.closestHit(h).idx;
+        kb.insert(h);
+    }
+    for (uint32_t i = 0; i < kb.numHits(); ++i) order[at++] = kb[K - kb.numHits() + i].idx;
+}
+
+int run_kbuffer(const char* inPath, const char* outPath) {
+    FILE* in = fopen(inPath, "rb");
+    if (in == nullptr) return 3;
+    int32_t sequences = 0;
+    if (!read_all(in, &sequences, 4)) return 4;
+    FILE* out = fopen(outPath, "wb");
+    if (out == nullptr) return 5;
+    for (int sq = 0; sq < sequences; ++sq) {
+        int32_t head[2];
+        if (!read_all(in, head, sizeof(head))) return 6;
+        std::vector<float> hitT(static_cast<size_t>(head[1]));
+        std::vector<int32_t> order(static_cast<size_t>(head[1]), -1);
+        if (!read_all(in, hitT.data(), sizeof(float) * hitT.size())) return 7;
+        switch (head[0]) {
+            case 4: kbuffer_order<4>(hitT.data(), head[1], order.data()); break;
+            case 8: kbuffer_order<8>(hitT.data(), head[1], order.data()); break;
+            case 12: kbuffer_order<12>(hitT.data(), head[1], order.data()); break;
+            case 16: kbuffer_order<16>(hitT.data(), head[1], order.data()); break;
+            case 24: kbuffer_order<24>(hitT.data(), head[1], order.data()); break;
+            case 32: kbuffer_order<32>(hitT.data(), head[1], order.data()); break;
+            default: return 8;
+        }
+        fwrite(order.data(), sizeof(int32_t), order.size(), out);
+    }
+    fclose(out);
+    fclose(in);
+    return 0;
+}
+
 int main(int argc, char** argv) {
+    if (argc == 4 && strcmp(argv[1], "kbuffer") == 0) return run_kbuffer(argv[2], argv[3]);
     if (argc == 4 && strcmp(argv[1], "sh") == 0) return run_sh(argv[2], argv[3]);
     if (argc == 4 && strcmp(argv[1], "project") == 0) return run_project(argv[2], argv[3]);
     if (argc != 3) {

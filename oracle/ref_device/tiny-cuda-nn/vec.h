@@ -84,6 +84,10 @@ struct tvec : tvec_storage<T, N> {
         for (uint32_t i = 0; i < N; ++i) (*this)[i] += s;
         return *this;
     }
+    tvec& operator-=(const tvec& o) {
+        for (uint32_t i = 0; i < N; ++i) (*this)[i] -= o[i];
+        return *this;
+    }
     tvec& operator*=(T s) {
         for (uint32_t i = 0; i < N; ++i) (*this)[i] *= s;
         return *this;
@@ -122,12 +126,77 @@ tvec<T, N, A> operator-(const tvec<T, N, A>& a) {
     return r;
 }
 
+// Component-wise min, max, abs, sqrt; Euclidean length; swap.
+template <typename T>
+T min(T a, T b) { return b < a ? b : a; }
+template <typename T>
+T max(T a, T b) { return a < b ? b : a; }
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> min(const tvec<T, N, A>& a, const tvec<T, N, A>& b) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = b[i] < a[i] ? b[i] : a[i];
+    return r;
+}
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> max(const tvec<T, N, A>& a, const tvec<T, N, A>& b) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = a[i] < b[i] ? b[i] : a[i];
+    return r;
+}
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> abs(const tvec<T, N, A>& a) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = a[i] < T(0) ? -a[i] : a[i];
+    return r;
+}
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> sqrt(const tvec<T, N, A>& a) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = ::sqrt(a[i]);
+    return r;
+}
+inline float sqrt(float x) { return ::sqrtf(x); }
+template <typename T, uint32_t N, size_t A>
+T length2(const tvec<T, N, A>& a) {
+    T s = T(0);
+    for (uint32_t i = 0; i < N; ++i) s += a[i] * a[i];
+    return s;
+}
+template <typename T, uint32_t N, size_t A>
+T length(const tvec<T, N, A>& a) {
+    return ::sqrt(length2(a));
+}
+template <typename T>
+void host_device_swap(T& a, T& b) {
+    T t = a;
+    a = b;
+    b = t;
+}
+
 template <uint32_t N>
 using vec = tvec<float, N>;
 using vec2 = tvec<float, 2>;
 using vec3 = tvec<float, 3>;
 using vec4 = tvec<float, 4>;
 using ivec2 = tvec<int, 2>;
+using uvec2 = tvec<uint32_t, 2>;
+using uvec3 = tvec<uint32_t, 3>;
+
+// largest component
+template <typename T, uint32_t N, size_t A>
+T max(const tvec<T, N, A>& a) {
+    T m = a[0];
+    for (uint32_t i = 1; i < N; ++i) m = a[i] > m ? a[i] : m;
+    return m;
+}
+template <typename T, uint32_t N, size_t A>
+T min(const tvec<T, N, A>& a) {
+    T m = a[0];
+    for (uint32_t i = 1; i < N; ++i) m = a[i] < m ? a[i] : m;
+    return m;
+}
+template <typename T>
+T div_round_up(T a, T b) { return (a + b - 1) / b; }
 
 template <typename T, uint32_t N, size_t A>
 tvec<T, N, A> mix(const tvec<T, N, A>& a, const tvec<T, N, A>& b, T t) {

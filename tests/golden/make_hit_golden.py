@@ -15,7 +15,9 @@ It also records the projector's particle radiance, radianceFromSpH
 (gaussianParticles.cuh:188-220, unclamped as gutProjector.cuh:903 calls it),
 at SH degrees 0 to 3, and the sensor-space point projection projectPoint
 (cameraProjections.cuh:75-152, without raster bounds as the UT calls it) of
-three fisheye cameras and a distorted pinhole.
+three fisheye cameras and a distorted pinhole, and the k-buffer's composite
+order (HitParticleKBufferT, gutKBufferRenderer.cuh:118-166, compiled with its
+renderer header) for every K the tracer supports.
 
 Inputs (seeded): tiles of 16x16 rays, each tile with its own ordered list
 of 6 to 48 Gaussians (random rotation, log-normal scales, opacities up to 1
@@ -220,6 +222,46 @@ def projection_goldens(rng: np.random.Generator, points: int = 4096):
     return np.stack(all_pts), np.stack(all_out)
 
 
+KBUFFER_SIZES = (4, 8, 12, 16, 24, 32)
+
+
+def kbuffer_goldens(rng: np.random.Generator, per_k: int = 64):
+    """The reference k-buffer's composite order (HitParticleKBufferT::insert
+    as evalKBuffer feeds it) for seeded hit-distance sequences of 1-300 hits
+    per K of KBUFFER_SIZES: distances drawn from a few values (many ties, the
+    case the compare-and-swap network orders by position), from a
+    continuous range, and ascending, descending and constant runs.  Returns
+    (k [S], offsets [S+1], hit distances [total], orders [total])."""
+    ks, seqs = [], []
+    for k in KBUFFER_SIZES:
+        for j in range(per_k):
+            n = int(rng.integers(1, 301))
+            kind = j % 5
+            if kind == 0:
+                t = rng.integers(0, 4, n).astype(np.float32)
+            elif kind == 1:
+                t = rng.uniform(0.1, 10.0, n).astype(np.float32)
+            elif kind == 2:
+                t = np.sort(rng.uniform(0.1, 10.0, n)).astype(np.float32)
+            elif kind == 3:
+                t = np.sort(rng.uniform(0.1, 10.0, n))[::-1].astype(np.float32)
+            else:
+                t = np.full(n, 2.5, np.float32)
+            ks.append(k)
+            seqs.append(np.ascontiguousarray(t))
+    with tempfile.TemporaryDirectory() as tmp:
+        src, dst = Path(tmp) / "kb.bin", Path(tmp) / "kb.out"
+        with open(src, "wb") as fh:
+            fh.write(np.array([len(seqs)], np.int32).tobytes())
+            for k, t in zip(ks, seqs):
+                fh.write(np.array([k, t.size], np.int32).tobytes())
+                fh.write(t.tobytes())
+        subprocess.run([str(DRIVER), "kbuffer", str(src), str(dst)], check=True)
+        orders = np.fromfile(dst, dtype=np.int32)
+    offsets = np.concatenate([[0], np.cumsum([t.size for t in seqs])]).astype(np.int64)
+    return np.array(ks, np.int32), offsets, np.concatenate(seqs), orders
+
+
 def main(reference: Path) -> None:
     subprocess.run(["make", "-C", str(REPO / "oracle"), "ref", f"REF={reference}"], check=True)
     rng = np.random.default_rng(20261202)
@@ -260,6 +302,7 @@ def main(reference: Path) -> None:
 
     sh_dirs, sh_coeffs, sh_rgb = sh_goldens(rng)
     proj_points, proj_out = projection_goldens(rng)
+    kb_k, kb_offsets, kb_hit_t, kb_order = kbuffer_goldens(rng)
     counts = np.array([t[0].shape[0] for t in tiles], np.int32)
     fwd_a, fwd_b, grad, grad_rgb, abs_world = [], [], [], [], []
     at = 0
@@ -292,6 +335,10 @@ def main(reference: Path) -> None:
         sh_rgb=sh_rgb,
         proj_points=proj_points,
         proj_out=proj_out,
+        kb_k=kb_k,
+        kb_offsets=kb_offsets,
+        kb_hit_t=kb_hit_t,
+        kb_order=kb_order,
     )
     print(f"{TILES} tiles x {RAYS} rays, {int(counts.sum())} Gaussians; "
           f"hits per ray {float(np.stack(fwd_a)[..., 5].mean()):.2f}, "

@@ -215,3 +215,18 @@ def test_point_projection_matches_the_reference(golden):
         finite = np.isfinite(ref[:, :2]).all(axis=1)
         assert np.array_equal(finite, np.isfinite(uv).all(axis=1)), f"camera {c}"
         np.testing.assert_allclose(uv[finite], ref[finite, :2], rtol=1e-5, atol=1e-3, err_msg=f"camera {c}")
+
+
+def test_kbuffer_order_matches_the_reference(golden):
+    """The k-buffer's composite order (HitParticleKBufferT::insert fed as
+    evalKBuffer feeds it, gutKBufferRenderer.cuh:118-166,676-699) against the
+    oracle's KBuffer, exactly, for K = 4 ... 32 over sequences with ties,
+    continuous, ascending, descending and constant distances.  The tracer's
+    shared-memory ring is held to the same order by tests/test_kbuffer_model.py
+    and the GPU parity tests."""
+    off = golden["kb_offsets"]
+    for s, k in enumerate(golden["kb_k"]):
+        t = golden["kb_hit_t"][off[s]:off[s + 1]]
+        ref = golden["kb_order"][off[s]:off[s + 1]]
+        np.testing.assert_array_equal(oracle.kbuffer_order(int(k), t), ref.astype(np.uint32),
+                                      err_msg=f"sequence {s}, K={k}")

@@ -77,3 +77,19 @@ def test_ring_matches_network(k, levels):
         dist = np.clip(base + noise, 0, None) / 4.0
         hits = [(float(d), i) for i, d in enumerate(dist)]
         assert ring_stream(hits, k) == network_stream(hits, k), (k, levels, trial)
+
+
+def test_ring_matches_the_reference_kbuffer():
+    """The ring model against the reference's own HitParticleKBufferT
+    (gutKBufferRenderer.cuh:118-166, compiled for the host:
+    tests/golden/hit_golden.npz, made by tests/golden/make_hit_golden.py) on
+    its recorded composite orders."""
+    from pathlib import Path
+
+    golden = np.load(Path(__file__).resolve().parent / "golden" / "hit_golden.npz")
+    off = golden["kb_offsets"]
+    for s, k in enumerate(golden["kb_k"]):
+        t = golden["kb_hit_t"][off[s]:off[s + 1]]
+        hits = [(float(d), i) for i, d in enumerate(t)]
+        order = [i for _, i in ring_stream(hits, int(k))]
+        assert order == golden["kb_order"][off[s]:off[s + 1]].tolist(), (s, int(k))

@@ -135,6 +135,7 @@ def load():
         "oracle_set_abs_grad": (None, [vp, vp, i32]),
         "oracle_project_points": (i32, [cam_p, i32, vp, vp, vp]),
         "oracle_kbuffer_order": (i32, [i32, i32, vp, vp]),
+        "oracle_ut_project": (i32, [cam_p, pose_p, i32, vp, vp]),
         "oracle_set_admission_variants": (None, [ctypes.c_float, i32, ctypes.c_float, ctypes.c_float]),
         "oracle_admission_misses": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, vp, i64, vp, vp]),
         "oracle_sof_feeds": (i64, [cam_p, pose_p, i32, vp, vp, vp, vp, vp, i32, vp, vp, i64]),
@@ -203,6 +204,15 @@ def project(cam, pose, particles, sh, sh_degree, mask, ray_d=None):
     lib.oracle_project(ctypes.byref(cam), ctypes.byref(pose), n, _p(particles), _p(sh), sh.shape[1] // 3,
                        int(sh_degree), _p(mask), _po(ray_d), _p(proj), _p(rgb), _p(counts))
     return proj, rgb, counts
+
+
+def ut_project(cam, pose, particles) -> np.ndarray:
+    """The UT projection of packed rows alone: [n,6] = centre u, v,
+    covariance xx, xy, yy, valid (0/1)."""
+    rows = np.ascontiguousarray(particles, dtype=np.float32)
+    out = np.zeros((rows.shape[0], 6), np.float32)
+    load().oracle_ut_project(ctypes.byref(cam), ctypes.byref(pose), rows.shape[0], _p(rows), _p(out))
+    return out
 
 
 def kbuffer_order(k: int, hit_t) -> np.ndarray:

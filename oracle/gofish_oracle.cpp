@@ -335,6 +335,10 @@ bool project_world(const OracleCamera& cam, const OraclePose& pose, float3_ pw, 
 
 extern "C" {
 
+// The UT projection alone (unscented_projection) of n packed rows:
+// out[n*6] = centre u, v, covariance xx, xy, yy, valid (0 or 1).
+int oracle_ut_project(const OracleCamera* cam, const OraclePose* pose, int n, const float* particles, float* out);
+
 // Composite order of the k-buffer (KBuffer, fed as traverse() feeds it) for
 // hits i = 0..n-1 with distances hitT[i]: order[n] of hit indices.
 int oracle_kbuffer_order(int K, int n, const float* hitT, uint32_t* order);
@@ -2816,5 +2820,23 @@ extern "C" int oracle_kbuffer_order(int K, int n, const float* hitT, uint32_t* o
         kb.insert(h);
     }
     for (uint32_t i = 0; i < kb.n; ++i) order[at++] = kb.e[K - kb.n + i].idx;
+    return 0;
+}
+
+extern "C" int oracle_ut_project(const OracleCamera* cam, const OraclePose* pose, int n, const float* particles,
+                                 float* out) {
+    for (int i = 0; i < n; ++i) {
+        const Particle P = load_particle(particles + 32 * size_t(i));
+        float2_ center{0.0f, 0.0f};
+        float cov[3] = {0.0f, 0.0f, 0.0f};
+        const bool valid = unscented_projection(*cam, *pose, P, center, cov);
+        float* o = out + 6 * size_t(i);
+        o[0] = center.x;
+        o[1] = center.y;
+        o[2] = cov[0];
+        o[3] = cov[1];
+        o[4] = cov[2];
+        o[5] = valid ? 1.0f : 0.0f;
+    }
     return 0;
 }

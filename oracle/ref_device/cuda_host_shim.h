@@ -15,8 +15,11 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cfenv>
 #include <cmath>
 #include <limits>
+
+#include "math_constants.h"
 
 #define __device__
 #define __host__
@@ -47,10 +50,10 @@ constexpr int warpSize = 32;
 #define __shared__ static
 #define __constant__ static
 
-// Block and warp intrinsics: declared only, so that the reference's kernel
-// templates parse; none is instantiated by the host drivers (a call would
-// fail to link).
-void __syncthreads();
+// Block and warp intrinsics: declared only (a call would fail to link), so
+// that the reference's kernel templates parse; the block barrier is a no-op
+// for the one host thread.
+inline void __syncthreads() {}  // one host thread: nothing to wait for
 int __syncthreads_and(int);
 int __syncthreads_or(int);
 int __syncthreads_count(int);
@@ -69,6 +72,63 @@ int __popc(unsigned);
 int __clz(int);
 using std::max;
 using std::min;
+// the mixed-sign integer overloads of the CUDA math header
+inline unsigned min(unsigned a, int b) { return a < unsigned(b) ? a : unsigned(b); }
+inline unsigned min(int a, unsigned b) { return unsigned(a) < b ? unsigned(a) : b; }
+inline unsigned max(unsigned a, int b) { return a > unsigned(b) ? a : unsigned(b); }
+inline unsigned max(int a, unsigned b) { return unsigned(a) > b ? unsigned(a) : b; }
+
+// Directed-rounding arithmetic (the certified-admission headers' interval
+// bounds): the operation evaluated under the requested rounding mode of the
+// host FPU (built with -frounding-math).  The host drivers do not call the
+// certified paths; their kernels, which the host build compiles as ordinary
+// functions, reference these.
+#define GF_SHIM_DIRECTED2(T, NAME, MODE, OP)                 \
+    inline T NAME(T a, T b) {                                 \
+        const int saved = std::fegetround();                  \
+        std::fesetround(MODE);                                \
+        volatile T r = a OP b;                                \
+        std::fesetround(saved);                               \
+        return r;                                             \
+    }
+#define GF_SHIM_DIRECTED_SET(SUFFIX, MODE)                    \
+    GF_SHIM_DIRECTED2(double, __dadd_##SUFFIX, MODE, +)       \
+    GF_SHIM_DIRECTED2(double, __dsub_##SUFFIX, MODE, -)       \
+    GF_SHIM_DIRECTED2(double, __dmul_##SUFFIX, MODE, *)       \
+    GF_SHIM_DIRECTED2(double, __ddiv_##SUFFIX, MODE, /)       \
+    GF_SHIM_DIRECTED2(float, __fadd_##SUFFIX, MODE, +)        \
+    GF_SHIM_DIRECTED2(float, __fsub_##SUFFIX, MODE, -)        \
+    GF_SHIM_DIRECTED2(float, __fmul_##SUFFIX, MODE, *)        \
+    GF_SHIM_DIRECTED2(float, __fdiv_##SUFFIX, MODE, /)        \
+    inline double __dsqrt_##SUFFIX(double a) {               \
+        const int saved = std::fegetround();                  \
+        std::fesetround(MODE);                                \
+        volatile double r = std::sqrt(a);                     \
+        std::fesetround(saved);                               \
+        return r;                                             \
+    }                                                         \
+    inline float __fsqrt_##SUFFIX(float a) {                  \
+        const int saved = std::fegetround();                  \
+        std::fesetround(MODE);                                \
+        volatile float r = std::sqrt(a);                      \
+        std::fesetround(saved);                               \
+        return r;                                             \
+    }                                                         \
+    inline float __double2float_##SUFFIX(double a) {          \
+        const int saved = std::fegetround();                  \
+        std::fesetround(MODE);                                \
+        volatile float r = float(a);                          \
+        std::fesetround(saved);                               \
+        return r;                                             \
+    }                                                         \
+    inline float __frcp_##SUFFIX(float a) { return __fdiv_##SUFFIX(1.0f, a); }
+GF_SHIM_DIRECTED_SET(rd, FE_DOWNWARD)
+GF_SHIM_DIRECTED_SET(ru, FE_UPWARD)
+GF_SHIM_DIRECTED_SET(rz, FE_TOWARDZERO)
+GF_SHIM_DIRECTED_SET(rn, FE_TONEAREST)
+#undef GF_SHIM_DIRECTED_SET
+#undef GF_SHIM_DIRECTED2
+
 
 inline float2 make_float2(float x, float y) { return {x, y}; }
 inline float3 make_float3(float x, float y, float z) { return {x, y, z}; }
@@ -123,6 +183,12 @@ inline float __uint_as_float(unsigned i) { float f; memcpy(&f, &i, 4); return f;
 
 template <typename T>
 inline T atomicAdd(T* address, T value) { const T old = *address; *address = old + value; return old; }
+template <typename T>
+inline T atomicAnd(T* address, T value) { const T old = *address; *address = old & value; return old; }
+template <typename T>
+inline T atomicOr(T* address, T value) { const T old = *address; *address = old | value; return old; }
+template <typename T>
+inline T atomicExch(T* address, T value) { const T old = *address; *address = value; return old; }
 template <typename T>
 inline T atomicMax(T* address, T value) { const T old = *address; *address = std::max(old, value); return old; }
 template <typename T>

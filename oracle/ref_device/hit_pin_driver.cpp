@@ -61,6 +61,26 @@
 #include <3dgut/kernels/cuda/sensors/cameraProjections.cuh>
 #include <3dgut/kernels/cuda/renderers/gutKBufferRenderer.cuh>
 
+// The projector's compile-time configuration, which the reference's
+// threedgut.cuh:56-69 builds from the build defines before it includes
+// gutProjector.cuh; the UT projection reads ParticleMinSensorZ and
+// AlphaThreshold, the other members only have to exist.
+struct TGUTProjectorParams {
+    static constexpr float ParticleMinSensorZ = threedgut::kParticleMinSensorZ;
+    static constexpr float CovarianceDilation = 0.3f;
+    static constexpr float AlphaThreshold = GAUSSIAN_PARTICLE_MIN_ALPHA;
+    static constexpr bool TightOpacityBounding = true;
+    static constexpr bool RectBounding = true;
+    static constexpr bool TileCulling = true;
+    static constexpr bool PerRayParticleFeatures = false;
+    static constexpr float MaxDepthValue = 3.4028235e+38f;
+    static constexpr bool GlobalZOrder = false;
+    static constexpr bool PerTileDepth = true;
+    static constexpr bool BackwardProjection = false;
+    static constexpr bool MipSplattingScaling = true;
+};
+#include <3dgut/kernels/cuda/renderers/gutProjector.cuh>
+
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -212,7 +232,99 @@ int run_kbuffer(const char* inPath, const char* outPath) {
     return 0;
 }
 
+// `ut` mode: GUTProjector::unscentedParticleProjection (gutProjector.cuh:359-518),
+// the 7-point unscented transform of a particle through a global-shutter
+// camera, with the reference's default UT parameters
+// (threedgut.cuh:72-81 with configs/render/3dgut.yaml: alpha 1, beta 2,
+// kappa 0, delta sqrt(3), 10% image margin, not every sigma point required).
+// The particle model is reached through three accessors, restated here as
+// the reference's shRadiativeGaussianParticles.cuh:89-123 defines them (the
+// model class itself is built from Slang-generated code): position = slots
+// 0-2, opacity = slot 3, factorColumn(i) = column i of the row-major B in
+// slots 12-20.
+struct UtParams {
+    static constexpr int NRollingShutterIterations = 1;
+    static constexpr int D = 3;
+    static constexpr float Alpha = 1.0f;
+    static constexpr float Beta = 2.0f;
+    static constexpr float Kappa = 0.0f;
+    static constexpr float Delta = 1.7320508075688772f;
+    static constexpr float ImageMarginFactor = 0.1f;
+    static constexpr bool RequireAllSigmaPoints = false;
+};
+
+struct PackedRowParticles {
+    using DensityParameters = threedgut::ParticleDensity;
+    using TFeaturesVec = tcnn::vec3;  // named by the projector's declarations only
+    const tcnn::vec3& position(const DensityParameters& p) const {
+        return *reinterpret_cast<const tcnn::vec3*>(&p.position);
+    }
+    const float& opacity(const DensityParameters& p) const { return p.density; }
+    tcnn::vec3 factorColumn(const DensityParameters& p, int axis) const {
+        const float* b = &p.factor[0].x;
+        return tcnn::vec3(b[axis], b[3 + axis], b[6 + axis]);
+    }
+};
+
+// Input: int32 count, int32 model, int32 width, int32 height, float32
+// camera[18] (as `project`), float32 pose[7] (world->sensor t, q xyzw),
+// float32 centre[3] (the sensor position in the world), then count packed
+// rows; output per particle float32 centre u, v, covariance xx, xy, yy, valid.
+int run_ut(const char* inPath, const char* outPath) {
+    using Projector = GUTProjector<PackedRowParticles, TGUTProjectorParams, UtParams>;
+    FILE* in = fopen(inPath, "rb");
+    if (in == nullptr) return 3;
+    int32_t head[4];
+    float cam[18], pose[7], centre[3];
+    if (!read_all(in, head, sizeof(head)) || !read_all(in, cam, sizeof(cam)) || !read_all(in, pose, sizeof(pose)) ||
+        !read_all(in, centre, sizeof(centre)))
+        return 4;
+    FILE* out = fopen(outPath, "wb");
+    if (out == nullptr) return 5;
+    threedgut::TSensorModel model{};
+    model.shutterType = threedgut::TSensorModel::GlobalShutter;
+    if (head[1] == 1) {
+        model.modelType = threedgut::TSensorModel::OpenCVFisheyeModel;
+        model.ocvFisheyeParams.principalPoint = tcnn::vec2(cam[0], cam[1]);
+        model.ocvFisheyeParams.focalLength = tcnn::vec2(cam[2], cam[3]);
+        for (int i = 0; i < 4; ++i) model.ocvFisheyeParams.radialCoeffs[i] = cam[4 + i];
+        model.ocvFisheyeParams.maxAngle = cam[16];
+    } else {
+        model.modelType = threedgut::TSensorModel::OpenCVPinholeModel;
+        model.ocvPinholeParams.principalPoint = tcnn::vec2(cam[0], cam[1]);
+        model.ocvPinholeParams.focalLength = tcnn::vec2(cam[2], cam[3]);
+        for (int i = 0; i < 6; ++i) model.ocvPinholeParams.radialCoeffs[i] = cam[4 + i];
+        model.ocvPinholeParams.tangentialCoeffs = tcnn::vec2(cam[10], cam[11]);
+        model.ocvPinholeParams.thinPrismCoeffs = tcnn::vec4(cam[12], cam[13], cam[14], cam[15]);
+    }
+    threedgut::TSensorState state{};
+    for (int i = 0; i < 7; ++i) state.startPose[i] = state.endPose[i] = pose[i];
+    state.startTimestamp = 0;
+    state.endTimestamp = 1;
+    const tcnn::mat4x3 sensorMatrix = threedgut::sensorPoseToMat(state.startPose);
+    const tcnn::vec3 sensorPosition(centre[0], centre[1], centre[2]);
+    const tcnn::ivec2 resolution(head[2], head[3]);
+    PackedRowParticles particles;
+    for (int i = 0; i < head[0]; ++i) {
+        threedgut::ParticleDensity row;
+        if (!read_all(in, &row, sizeof(row))) return 6;
+        tcnn::vec3 sensorRay, cov(0.0f);
+        tcnn::vec2 centreUv(0.0f);
+        float opacity = 0.0f;
+        bool capEligible = false;
+        const bool valid = Projector::unscentedParticleProjection(resolution, model, sensorPosition, sensorMatrix, state,
+                                                                  particles, row, sensorRay, opacity, centreUv, cov,
+                                                                  capEligible);
+        const float rec[6] = {centreUv.x, centreUv.y, cov.x, cov.y, cov.z, valid ? 1.0f : 0.0f};
+        fwrite(rec, sizeof(float), 6, out);
+    }
+    fclose(out);
+    fclose(in);
+    return 0;
+}
+
 int main(int argc, char** argv) {
+    if (argc == 4 && strcmp(argv[1], "ut") == 0) return run_ut(argv[2], argv[3]);
     if (argc == 4 && strcmp(argv[1], "kbuffer") == 0) return run_kbuffer(argv[2], argv[3]);
     if (argc == 4 && strcmp(argv[1], "sh") == 0) return run_sh(argv[2], argv[3]);
     if (argc == 4 && strcmp(argv[1], "project") == 0) return run_project(argv[2], argv[3]);

@@ -157,6 +157,12 @@ tvec<T, N, A> sqrt(const tvec<T, N, A>& a) {
 }
 inline float sqrt(float x) { return ::sqrtf(x); }
 template <typename T, uint32_t N, size_t A>
+T dot(const tvec<T, N, A>& a, const tvec<T, N, A>& b) {
+    T s = a[0] * b[0];
+    for (uint32_t i = 1; i < N; ++i) s += a[i] * b[i];
+    return s;
+}
+template <typename T, uint32_t N, size_t A>
 T length2(const tvec<T, N, A>& a) {
     T s = T(0);
     for (uint32_t i = 0; i < N; ++i) s += a[i] * a[i];
@@ -165,6 +171,10 @@ T length2(const tvec<T, N, A>& a) {
 template <typename T, uint32_t N, size_t A>
 T length(const tvec<T, N, A>& a) {
     return ::sqrt(length2(a));
+}
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> normalize(const tvec<T, N, A>& a) {
+    return a / length(a);
 }
 template <typename T>
 void host_device_swap(T& a, T& b) {
@@ -202,6 +212,18 @@ template <typename T, uint32_t N, size_t A>
 tvec<T, N, A> mix(const tvec<T, N, A>& a, const tvec<T, N, A>& b, T t) {
     return a * (T(1) - t) + b * t;
 }
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> mix(const tvec<T, N, A>& a, const tvec<T, N, A>& b, const tvec<T, N, A>& t) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = a[i] * (T(1) - t[i]) + b[i] * t[i];
+    return r;
+}
+template <typename T, uint32_t N, size_t A>
+tvec<T, N, A> copysign(const tvec<T, N, A>& a, const tvec<T, N, A>& b) {
+    tvec<T, N, A> r;
+    for (uint32_t i = 0; i < N; ++i) r[i] = ::copysign(a[i], b[i]);
+    return r;
+}
 
 // Column-major R x C matrix: m[c] is column c.
 template <typename T, uint32_t C, uint32_t R>
@@ -210,6 +232,11 @@ struct tmat {
     tmat() = default;
     template <typename... Cs, typename = typename std::enable_if<sizeof...(Cs) == C>::type>
     tmat(const Cs&... cs) : col{cs...} {}
+    // the leading C columns of a wider matrix (a 4x3 pose's rotation part)
+    template <uint32_t C2, typename = typename std::enable_if<(C2 > C)>::type>
+    explicit tmat(const tmat<T, C2, R>& o) {
+        for (uint32_t c = 0; c < C; ++c) col[c] = o[c];
+    }
     tvec<T, R>& operator[](uint32_t c) { return col[c]; }
     const tvec<T, R>& operator[](uint32_t c) const { return col[c]; }
 };

@@ -17,7 +17,9 @@ at SH degrees 0 to 3, and the sensor-space point projection projectPoint
 (cameraProjections.cuh:75-152, without raster bounds as the UT calls it) of
 three fisheye cameras and a distorted pinhole, and the k-buffer's composite
 order (HitParticleKBufferT, gutKBufferRenderer.cuh:118-166, compiled with its
-renderer header) for every K the tracer supports.
+renderer header) for every K the tracer supports, and the UT projection
+(GUTProjector::unscentedParticleProjection, gutProjector.cuh:359-518) of
+particles around each camera.
 
 Inputs (seeded): tiles of 16x16 rays, each tile with its own ordered list
 of 6 to 48 Gaussians (random rotation, log-normal scales, opacities up to 1
@@ -222,6 +224,77 @@ def projection_goldens(rng: np.random.Generator, points: int = 4096):
     return np.stack(all_pts), np.stack(all_out)
 
 
+def quaternion_xyzw_matrix(q) -> np.ndarray:
+    """Rotation matrix of a unit quaternion (x, y, z, w), float64."""
+    x, y, z, w = (float(v) for v in q)
+    return np.array([[1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)],
+                     [2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)],
+                     [2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)]])
+
+
+def ut_goldens(rng: np.random.Generator, count: int = 3000):
+    """The reference's UT projection (GUTProjector::unscentedParticleProjection)
+    of seeded particles around a random global-shutter pose of each camera of
+    PROJECTION_CAMERAS: means over the whole sphere at 0.1-20 m, log-normal
+    scales up to metres (sigma points beyond the fisheye's limit angle), some
+    opacities below 1/255.  Particles with the mean within 1e-3 m of the 0.2 m
+    near radius, or a sigma point within 1e-4 rad of the limit angle or of the
+    pinhole's z = 0, are redrawn.  Returns ([C,7] poses, [C,3] centres,
+    [C,count,32] rows, [C,count,6] centre u, v, covariance xx, xy, yy, valid)."""
+    poses, centres, all_rows, outs = [], [], [], []
+    with tempfile.TemporaryDirectory() as tmp:
+        for model, w, h, pp, f, k, tg, tp, max_angle in PROJECTION_CAMERAS:
+            q = rng.standard_normal(4)
+            q /= np.linalg.norm(q)
+            pose = np.array([*rng.uniform(-1, 1, 3), *q], np.float32)
+            R = quaternion_xyzw_matrix(pose[3:7].astype(np.float64))
+            t = pose[0:3].astype(np.float64)
+            centre = (-(R.T @ t)).astype(np.float32)
+            rows = np.zeros((count, 32), np.float32)
+            i = 0
+            while i < count:
+                d = rng.standard_normal(3)
+                d /= np.linalg.norm(d)
+                dist = math.exp(rng.uniform(math.log(0.1), math.log(20.0)))
+                mean = centre.astype(np.float64) + d * dist
+                if abs(dist - 0.2) < 1e-3:
+                    continue
+                qq = rng.standard_normal(4)
+                qq /= np.linalg.norm(qq)
+                scale = np.exp(rng.normal(math.log(0.05), 1.2, 3))
+                opacity = rng.uniform(0.001, 1.0)
+                row = packed_rows(mean[None].astype(np.float32), qq[None].astype(np.float32),
+                                  scale[None].astype(np.float32), np.array([opacity], np.float32))[0]
+                B = row[12:21].astype(np.float64).reshape(3, 3)
+                near_edge = False
+                for sgn in (1.0, -1.0):
+                    for a in range(3):
+                        p = R @ (row[0:3].astype(np.float64) + sgn * math.sqrt(3.0) * B[:, a]) + t
+                        if model == 1:
+                            th = math.atan2(math.hypot(p[0], p[1]), p[2])
+                            near_edge |= abs(th - max_angle) < 1e-4
+                        else:
+                            near_edge |= abs(p[2]) < 1e-4
+                if near_edge:
+                    continue
+                rows[i] = row
+                i += 1
+            src, dst = Path(tmp) / "ut.bin", Path(tmp) / "ut.out"
+            cam = np.array([*pp, *f, *k, *tg, *tp, max_angle, 0.1], np.float32)
+            with open(src, "wb") as fh:
+                fh.write(np.array([count, model, w, h], np.int32).tobytes())
+                fh.write(cam.tobytes())
+                fh.write(pose.tobytes())
+                fh.write(centre.tobytes())
+                fh.write(rows.tobytes())
+            subprocess.run([str(DRIVER), "ut", str(src), str(dst)], check=True)
+            poses.append(pose)
+            centres.append(centre)
+            all_rows.append(rows)
+            outs.append(np.fromfile(dst, dtype=np.float32).reshape(count, 6))
+    return np.stack(poses), np.stack(centres), np.stack(all_rows), np.stack(outs)
+
+
 KBUFFER_SIZES = (4, 8, 12, 16, 24, 32)
 
 
@@ -303,6 +376,7 @@ def main(reference: Path) -> None:
     sh_dirs, sh_coeffs, sh_rgb = sh_goldens(rng)
     proj_points, proj_out = projection_goldens(rng)
     kb_k, kb_offsets, kb_hit_t, kb_order = kbuffer_goldens(rng)
+    ut_poses, ut_centres, ut_rows, ut_out = ut_goldens(rng)
     counts = np.array([t[0].shape[0] for t in tiles], np.int32)
     fwd_a, fwd_b, grad, grad_rgb, abs_world = [], [], [], [], []
     at = 0
@@ -339,6 +413,10 @@ def main(reference: Path) -> None:
         kb_offsets=kb_offsets,
         kb_hit_t=kb_hit_t,
         kb_order=kb_order,
+        ut_poses=ut_poses,
+        ut_centres=ut_centres,
+        ut_rows=ut_rows,
+        ut_out=ut_out,
     )
     print(f"{TILES} tiles x {RAYS} rays, {int(counts.sum())} Gaussians; "
           f"hits per ray {float(np.stack(fwd_a)[..., 5].mean()):.2f}, "

@@ -50,7 +50,9 @@ UNIT = "Mpix/s"
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default 200 for the training workloads, whose 8 ms steps would let one "
+                        "host pause of a few tens of milliseconds weigh on a short region; 50 otherwise)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["gofish", "reference"], default="gofish")
     p.add_argument("--workload", choices=["single_view", "multi_view", "cpu_scale", "mesh_query", "inference"],
@@ -1301,6 +1303,8 @@ def run_reference(args):
 
 def main():
     args = parse_args()
+    if args.steps is None:
+        args.steps = 200 if args.workload in ("single_view", "multi_view") else 50
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "mesh_query":

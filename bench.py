@@ -259,11 +259,11 @@ BWD_RENDER_BYTES_PER_INTERSECTION = 144             # id 4 + particle record 128
 BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output gradients
 # DRAM bytes per algorithmic byte of the render kernels in a one-pass ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch
-# of this workload (k_render_fwd<16>: 865.9 MB for 473.7 MB, the excess being
-# the composite-log write; k_render_bwd_log: 864.5 MB for 649.7 MB, the log
+# of this workload (k_render_fwd<16>: 904.6 MB for 473.7 MB, the excess being
+# the composite-log write; k_render_bwd_log: 864.6 MB for 649.7 MB, the log
 # read); the bench line's traffic is the live algorithmic bytes scaled by them.
-FWD_TRAFFIC_PER_ALG_BYTE = 865.9 / 473.7
-BWD_TRAFFIC_PER_ALG_BYTE = 864.5 / 649.7
+FWD_TRAFFIC_PER_ALG_BYTE = 904.6 / 473.7
+BWD_TRAFFIC_PER_ALG_BYTE = 864.6 / 649.7
 TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio to the algorithmic bytes"
 # Warp instructions per tile intersection of the render kernels: ncu
 # smsp__inst_executed.sum of one full-size launch of this workload divided by
@@ -271,7 +271,7 @@ TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio
 # the bench line's issue fraction is the instructions of the average launch
 # over the SMs' issue slots in its duration (148 SMs x 4 schedulers x one warp
 # instruction per cycle at the median SM clock sampled during the region).
-FWD_INST_PER_INTERSECTION = 2.2215e9 / 3_373_688
+FWD_INST_PER_INTERSECTION = 2.2415e9 / 3_373_688
 BWD_INST_PER_INTERSECTION = 1.8804e9 / 3_373_688
 INST_SOURCE = "ncu smsp__inst_executed.sum of one full-size launch, per intersection"
 SM_COUNT = 148

@@ -33,9 +33,11 @@ namespace gf {
 // through the k-buffer.  Entry i of the pixel at thread p of tile t is
 // ids[(i * tiles + t) * kTileThreads + p] (coalesced across a warp).  A pixel
 // that composites more than `capacity` hits marks its tile in `overflow`; the
-// backward replays such tiles.  ids == nullptr: no log (inference).
+// backward replays such tiles.  Entries are 16-bit, so a tile of more than
+// kLogTileCandidates candidates is marked the same way.  ids == nullptr: no
+// log (inference).
 struct CompositeLog {
-    uint32_t* ids;       // [capacity][tiles][kTileThreads] candidate positions within the tile
+    uint16_t* ids;       // [capacity][tiles][kTileThreads] candidate positions within the tile
     uint32_t* count;     // [tiles][kTileThreads] entries logged, at most capacity
     uint32_t* overflow;  // [tiles] 1 when a pixel of the tile exceeded the capacity
     uint32_t* overflowList;   // the flagged tiles, in no particular order
@@ -522,12 +524,27 @@ __device__ __forceinline__ float4 color_at(const RenderArgs& a, const Batch& b, 
     return __ldg(a.records + 4 * size_t(__ldg(a.sortedIds + sp)) + 3);
 }
 
+// Candidates a logged tile may hold: log entries are 16-bit positions.
+constexpr uint32_t kLogTileCandidates = 65536u;
+
 // Appends one composited candidate (its position in the tile's list) to the
 // pixel's log; entries past the capacity are counted, not stored.
 __device__ __forceinline__ void log_composite(const CompositeLog& lg, uint32_t tile, uint32_t& n, uint32_t local) {
     if (lg.ids == nullptr) return;
-    if (n < lg.capacity) lg.ids[(size_t(n) * lg.tiles + tile) * kTileThreads + threadIdx.x] = local;
+    if (n < lg.capacity) lg.ids[(size_t(n) * lg.tiles + tile) * kTileThreads + threadIdx.x] = uint16_t(local);
     ++n;
+}
+
+// Ends the pixel's log: stores its entry count and marks the tile for the
+// backward's replay when a pixel composited more hits than the log holds or
+// the tile holds more candidates (`candidates`) than a 16-bit entry can name.
+__device__ __forceinline__ void log_finish(const CompositeLog& lg, uint32_t tile, uint32_t nlog, uint32_t candidates) {
+    lg.count[size_t(tile) * kTileThreads + threadIdx.x] = min(nlog, lg.capacity);
+    const int over = __syncthreads_or(nlog > lg.capacity || candidates > kLogTileCandidates);
+    if (threadIdx.x == 0) {
+        lg.overflow[tile] = over ? 1u : 0u;
+        if (over) lg.overflowList[atomicAdd(lg.overflowCount, 1u)] = tile;
+    }
 }
 
 // Front-to-back composite of one hit (reference gutKBufferRenderer.cuh:307-416);
@@ -759,7 +776,7 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
     RingKBuffer<KR> kb;
     kb.init(ring_ta(smem, kFwdStagingBytes), ring_id<KR>(smem, kFwdStagingBytes), threadIdx.x);
     Batch bt{sRec, sIdB, 0u, 0u};
-    uint32_t nlog = 0;
+    uint32_t nlog = 0, candidates = 0;
     PixelGeo geo;
     if constexpr (kGeo) {
         const bool pinhole = a.f.cam.model == GF_CAMERA_OPENCV_PINHOLE;
@@ -774,6 +791,7 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
     };
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
+        candidates = range.y - range.x;
         // The first warp stages: candidate base + lane of each batch.  It
         // holds the id of the batch after the one in flight in a register.
         const bool stager = threadIdx.x < kFwdBatch;
@@ -858,15 +876,7 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
             }
         }
     }
-    if (a.log.ids != nullptr) {
-        const CompositeLog& lg = a.log;
-        lg.count[size_t(ts.tile) * kTileThreads + threadIdx.x] = min(nlog, lg.capacity);
-        const int over = __syncthreads_or(nlog > lg.capacity);
-        if (threadIdx.x == 0) {
-            lg.overflow[ts.tile] = over ? 1u : 0u;
-            if (over) lg.overflowList[atomicAdd(lg.overflowCount, 1u)] = uint32_t(ts.tile);
-        }
-    }
+    if (a.log.ids != nullptr) log_finish(a.log, uint32_t(ts.tile), nlog, candidates);
     if (!ts.inImage) return;
     float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float hd = 1e06f, hc = 0.0f;
@@ -1509,7 +1519,7 @@ __global__ __launch_bounds__(kTileThreads, GF_BWD_LOG_MIN_BLOCKS) void k_render_
     uint32_t warpN = n;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) warpN = max(warpN, __shfl_xor_sync(0xffffffffu, warpN, o));
-    const uint32_t* entries = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
+    const uint16_t* entries = lg.ids + size_t(tile) * kTileThreads + threadIdx.x;
     const size_t stride = size_t(lg.tiles) * kTileThreads;
     uint32_t next = n > 0 ? __ldg(entries) : 0u;
 #pragma unroll 1

@@ -389,15 +389,7 @@ __global__ __launch_bounds__(kTileThreads) void k_render_fwd_sof(RenderArgs a, f
             composite(ht, ha, sp);
         }
     }
-    if (a.log.ids != nullptr) {
-        const CompositeLog& lg = a.log;
-        lg.count[size_t(ts.tile) * kTileThreads + threadIdx.x] = min(nlog, lg.capacity);
-        const int over = __syncthreads_or(nlog > lg.capacity);
-        if (threadIdx.x == 0) {
-            lg.overflow[ts.tile] = over ? 1u : 0u;
-            if (over) lg.overflowList[atomicAdd(lg.overflowCount, 1u)] = uint32_t(ts.tile);
-        }
-    }
+    if (a.log.ids != nullptr) log_finish(a.log, uint32_t(ts.tile), nlog, range.y - range.x);
     if (!ts.inImage) return;
     float4 out = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float hd = 1e06f, hc = 0.0f;

@@ -616,14 +616,14 @@ int forward(gf_tracer* t, const gf_trace_inputs* in, float* rgba, float* hd, flo
     a.rayD = in->ray_direction;
     a.log = gf::CompositeLog{};
     if (logComposites && T > 0 && t->cfg.composite_log_capacity >= 0) {
-        const size_t perEntry = size_t(T) * gf::kTileThreads * sizeof(uint32_t);
+        const size_t perEntry = size_t(T) * gf::kTileThreads * sizeof(uint16_t);
         const size_t want = t->cfg.composite_log_capacity > 0 ? size_t(t->cfg.composite_log_capacity) : kLogCapacity;
         const uint32_t cap = uint32_t(std::min<size_t>(want, std::max<size_t>(1, kLogBudgetBytes / perEntry)));
         if (int e = t->logIds.ensure(perEntry * cap, stream)) return e;
-        if (int e = t->logCount.ensure(perEntry, stream)) return e;
+        if (int e = t->logCount.ensure(size_t(T) * gf::kTileThreads * sizeof(uint32_t), stream)) return e;
         if (int e = t->logOverflow.ensure(sizeof(uint32_t) * size_t(T), stream)) return e;
         if (int e = t->logList.ensure(sizeof(uint32_t) * (size_t(T) + 1), stream)) return e;
-        a.log.ids = t->logIds.as<uint32_t>();
+        a.log.ids = t->logIds.as<uint16_t>();
         a.log.count = t->logCount.as<uint32_t>();
         a.log.overflow = t->logOverflow.as<uint32_t>();
         a.log.overflowCount = t->logList.as<uint32_t>();

@@ -259,11 +259,12 @@ BWD_RENDER_BYTES_PER_INTERSECTION = 144             # id 4 + particle record 128
 BWD_RENDER_BYTES_PER_PIXEL = 64                     # rays, outputs, output gradients
 # DRAM bytes per algorithmic byte of the render kernels in a one-pass ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch
-# of this workload (k_render_fwd<16>: 904.6 MB for 473.7 MB, the excess being
-# the composite-log write; k_render_bwd_log: 864.6 MB for 649.7 MB, the log
-# read); the bench line's traffic is the live algorithmic bytes scaled by them.
-FWD_TRAFFIC_PER_ALG_BYTE = 904.6 / 473.7
-BWD_TRAFFIC_PER_ALG_BYTE = 864.6 / 649.7
+# of this workload (k_render_fwd<16>: 527.7 MB for 473.7 MB, the excess being
+# the 16-bit composite-log write; k_render_bwd_log: 577.9 MB for 649.7 MB, the
+# log read outweighed by particle records that neighbouring tiles find in L2);
+# the bench line's traffic is the live algorithmic bytes scaled by them.
+FWD_TRAFFIC_PER_ALG_BYTE = 527.7 / 473.7
+BWD_TRAFFIC_PER_ALG_BYTE = 577.9 / 649.7
 TRAFFIC_SOURCE = "ncu dram__bytes_read+write of one full-size launch, as a ratio to the algorithmic bytes"
 # Warp instructions per tile intersection of the render kernels: ncu
 # smsp__inst_executed.sum of one full-size launch of this workload divided by

@@ -365,3 +365,46 @@ def test_geometric_channels_backward(cuda_device, k, log_capacity):
         assert float(np.linalg.norm(gp_ref[:, cols])) > 0.0, name
         assert harness.rel_l2(gp[:, cols], gp_ref[:, cols]) <= GRAD_RTOL_L2, name
     assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2
+
+
+def _crowded_tile_case(n: int = 70_000, size: int = 32, seed: int = 23):
+    """Opaque Gaussians clustered on the optical axis of a 32x32 fisheye, so
+    that each of its four tiles holds more candidates than a 16-bit composite
+    log entry can name; no pixel composites 1024 hits."""
+    import dataclasses as dc
+
+    from gofish_b200.camera import fisheye_camera, random_kb_coefficients
+    from gofish_b200.scene import IDENTITY_POSE, random_scene
+
+    rng = np.random.default_rng(seed)
+    scene = random_scene(n, 1, seed)
+    pos = np.stack([rng.uniform(-0.2, 0.2, n), rng.uniform(-0.2, 0.2, n), rng.uniform(2.5, 3.5, n)], 1)
+    scene = dc.replace(scene, positions=pos.astype(np.float32),
+                       scales=rng.uniform(0.25, 0.4, (n, 3)).astype(np.float32),
+                       density=rng.uniform(0.9, 0.99, (n, 1)).astype(np.float32))
+    cam = fisheye_camera(size, size, 200.0, random_kb_coefficients(rng, 200.0))
+    return harness.make_case(scene, cam, IDENTITY_POSE.copy())
+
+
+@pytest.mark.parametrize("k", [0, 16])
+def test_tile_beyond_16bit_log_is_replayed(cuda_device, k):
+    """A tile with more than 65,536 candidates cannot be named by the 16-bit
+    composite log: the forward flags it for replay even though no pixel
+    composited more hits than the (1024-entry) log holds, and the gradients
+    are the oracle's."""
+    case = _crowded_tile_case()
+    ref = harness.oracle_forward(case, k, 0)
+    per_tile = np.diff(ref["ranges"].reshape(-1, 2).astype(np.int64), axis=1)[:, 0]
+    crowded = int((per_tile > 65_536).sum())
+    assert crowded > 0 and int(ref["hit_count"].max()) <= 1024
+    gpu = harness.GpuTracer(case, k, 0, cuda_device, log_capacity=1024)
+    got = gpu.forward()
+    _compare_forward(ref, got)
+    assert gpu.raster.log_overflow_tiles() == crowded
+    rng = np.random.default_rng(29)
+    g_rgba = rng.standard_normal(ref["rgba"].shape).astype(np.float32)
+    g_hit = (0.1 * rng.standard_normal(ref["hit_t"].shape)).astype(np.float32)
+    gp_ref, gs_ref, _ = harness.oracle_backward(case, ref, k, g_rgba, g_hit)
+    gp, gs = gpu.backward(g_rgba, g_hit)
+    assert harness.rel_l2(gp, gp_ref) <= GRAD_RTOL_L2
+    assert harness.rel_l2(gs, gs_ref) <= GRAD_RTOL_L2

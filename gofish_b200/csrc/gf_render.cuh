@@ -108,7 +108,8 @@ constexpr int kBatch = kTileThreads;
 // block's first warp while every warp composites the current one, so no warp
 // waits out a global-memory latency at the batch barrier.  With the K = 16
 // ring (48 KiB) its block needs 54.5 KiB of shared memory, so four blocks
-// (32 warps) fit on an SM.
+// (32 warps) fit on an SM.  The two-block kernels use the same room as one
+// batch of 64, staged synchronously.
 constexpr int kFwdBatch = 32;
 constexpr int kFwdBuffers = 2;
 
@@ -792,45 +793,10 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
     if (retained) {
         const uint2 range = a.ranges[ts.tile];
         candidates = range.y - range.x;
-        // The first warp stages: candidate base + lane of each batch.  It
-        // holds the id of the batch after the one in flight in a register.
-        const bool stager = threadIdx.x < kFwdBatch;
-        uint32_t nextId = 0u;
-        if (stager) {
-            const uint32_t i0 = range.x + threadIdx.x;
-            if (i0 < range.y) {
-                const uint32_t id = __ldg(a.sortedIds + i0);
-                sIdB[threadIdx.x] = id;
-                fetch_async(a, id, sRec[threadIdx.x], sBound[threadIdx.x]);
-            }
-            cp_async_commit();
-            const uint32_t i1 = i0 + kFwdBatch;
-            if (i1 < range.y) nextId = __ldg(a.sortedIds + i1);
-        }
-        int buf = 0;
-        for (uint32_t base = range.x; base < range.y; base += kFwdBatch, buf ^= 1) {
-            Staged* cur = sRec + buf * kFwdBatch;
-            if (stager) {
-                // this batch's copies have landed: add the derived fields
-                cp_async_wait_all();
-                if (base + threadIdx.x < range.y) derive(ts, cur[threadIdx.x], sBound[buf * kFwdBatch + threadIdx.x]);
-            }
-            // publishes the batch; every warp is done with the other buffer
-            if (__syncthreads_and(!s.alive)) break;
-            if (stager) {
-                const int nb = buf ^ 1;
-                const uint32_t i1 = base + kFwdBatch + threadIdx.x;
-                if (i1 < range.y) {
-                    sIdB[nb * kFwdBatch + threadIdx.x] = nextId;
-                    fetch_async(a, nextId, sRec[nb * kFwdBatch + threadIdx.x], sBound[nb * kFwdBatch + threadIdx.x]);
-                }
-                cp_async_commit();
-                const uint32_t i2 = i1 + kFwdBatch;
-                nextId = i2 < range.y ? __ldg(a.sortedIds + i2) : 0u;
-            }
-            const int cnt = min(uint32_t(kFwdBatch), range.y - base);
+        // composites one staged batch: `cnt` candidates from sorted position `base`
+        auto runBatch = [&](const Staged* cur, const uint32_t* ids, uint32_t base, int cnt) {
             bt.rec = cur;
-            bt.ids = sIdB + buf * kFwdBatch;
+            bt.ids = ids;
             bt.base = base;
             bt.cnt = uint32_t(cnt);
             const int words = (cnt + 31) >> 5;
@@ -862,8 +828,64 @@ __global__ __launch_bounds__(kTileThreads, fwd_min_blocks(K, kGeo)) void k_rende
                     }
                 }
             }
+        };
+        if constexpr (fwd_min_blocks(K, kGeo) == 2) {
+            // Two-block kernels (K > 16 or the geometric channels) stage
+            // both buffers' room as one batch of 64, synchronously: at 16
+            // warps per SM the asynchronous double buffer was slower (K = 32:
+            // 17.24 ms per 2560^2 inference frame against 16.64 ms).
+            constexpr int kBatch64 = kFwdBatch * kFwdBuffers;
+            for (uint32_t base = range.x; base < range.y; base += kBatch64) {
+                if (__syncthreads_and(!s.alive)) break;
+                const uint32_t sIdx = base + threadIdx.x;
+                if (threadIdx.x < kBatch64 && sIdx < range.y) {
+                    sIdB[threadIdx.x] = __ldg(a.sortedIds + sIdx);
+                    stage<true>(a, ts, sIdx, sRec[threadIdx.x]);
+                }
+                __syncthreads();
+                runBatch(sRec, sIdB, base, int(min(uint32_t(kBatch64), range.y - base)));
+            }
+        } else {
+            // The first warp stages: candidate base + lane of each batch.  It
+            // holds the id of the batch after the one in flight in a register.
+            const bool stager = threadIdx.x < kFwdBatch;
+            uint32_t nextId = 0u;
+            if (stager) {
+                const uint32_t i0 = range.x + threadIdx.x;
+                if (i0 < range.y) {
+                    const uint32_t id = __ldg(a.sortedIds + i0);
+                    sIdB[threadIdx.x] = id;
+                    fetch_async(a, id, sRec[threadIdx.x], sBound[threadIdx.x]);
+                }
+                cp_async_commit();
+                const uint32_t i1 = i0 + kFwdBatch;
+                if (i1 < range.y) nextId = __ldg(a.sortedIds + i1);
+            }
+            int buf = 0;
+            for (uint32_t base = range.x; base < range.y; base += kFwdBatch, buf ^= 1) {
+                Staged* cur = sRec + buf * kFwdBatch;
+                if (stager) {
+                    // this batch's copies have landed: add the derived fields
+                    cp_async_wait_all();
+                    if (base + threadIdx.x < range.y) derive(ts, cur[threadIdx.x], sBound[buf * kFwdBatch + threadIdx.x]);
+                }
+                // publishes the batch; every warp is done with the other buffer
+                if (__syncthreads_and(!s.alive)) break;
+                if (stager) {
+                    const int nb = buf ^ 1;
+                    const uint32_t i1 = base + kFwdBatch + threadIdx.x;
+                    if (i1 < range.y) {
+                        sIdB[nb * kFwdBatch + threadIdx.x] = nextId;
+                        fetch_async(a, nextId, sRec[nb * kFwdBatch + threadIdx.x], sBound[nb * kFwdBatch + threadIdx.x]);
+                    }
+                    cp_async_commit();
+                    const uint32_t i2 = i1 + kFwdBatch;
+                    nextId = i2 < range.y ? __ldg(a.sortedIds + i2) : 0u;
+                }
+                runBatch(cur, sIdB + buf * kFwdBatch, base, int(min(uint32_t(kFwdBatch), range.y - base)));
+            }
+            if (stager) cp_async_wait_all();  // no copy outlives the block
         }
-        if (stager) cp_async_wait_all();  // no copy outlives the block
         if constexpr (K > 0) {
             for (int i = 0; s.alive && i < kb.n; ++i) {
                 float ht, ha;

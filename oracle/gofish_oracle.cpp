@@ -1056,6 +1056,11 @@ struct KBuffer {
     }
 };
 
+uint64_t next_scene_serial() {
+    static std::atomic<uint64_t> counter{0};
+    return counter.fetch_add(1) + 1;
+}
+
 struct Scene {
     const OracleCamera* cam;
     const OraclePose* pose;
@@ -1068,6 +1073,10 @@ struct Scene {
     const uint32_t* ranges;
     const uint32_t* sortedIds;
     int K;  // k-buffer size; kSofHierarchy: SOF's HEAD4 / MID8 / TAIL64 hierarchy
+    // Distinct for every Scene built in this process: the per-thread SOF feed
+    // cache is keyed on it, not on the Scene's address, which a later call's
+    // Scene may reuse (the calling thread keeps its cache between calls).
+    uint64_t serial = next_scene_serial();
 };
 
 // ------------------------------------------------------------------ SOF hierarchy
@@ -1244,12 +1253,12 @@ std::vector<std::vector<uint32_t>> sof_feeds(const Scene& sc, uint32_t tile) {
 
 // The feed sequence of one pixel, computed once per tile and worker thread.
 const std::vector<uint32_t>& sof_pixel_feed(const Scene& sc, uint32_t tile, const Ray& ray) {
-    thread_local const Scene* cachedScene = nullptr;
+    thread_local uint64_t cachedScene = 0;
     thread_local uint32_t cachedTile = 0xffffffffu;
     thread_local std::vector<std::vector<uint32_t>> cached;
-    if (cachedScene != &sc || cachedTile != tile) {
+    if (cachedScene != sc.serial || cachedTile != tile) {
         cached = sof_feeds(sc, tile);
-        cachedScene = &sc;
+        cachedScene = sc.serial;
         cachedTile = tile;
     }
     return cached[size_t(ray.local)];
